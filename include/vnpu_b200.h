@@ -1,0 +1,74 @@
+/*
+ * vnpu_b200.h - B200 extensions to the vnpu v1 ABI.
+ *
+ * Everything here is additive, in the way the reference's ABI rules allow
+ * (reference include/vnpu.h:14: "new capabilities are added via opcodes/flags,
+ * not by changing v1 structs").  An engine that only knows vnpu.h never needs
+ * this header.
+ */
+#ifndef VNPU_B200_H
+#define VNPU_B200_H
+
+#include "vnpu.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/*
+ * Dequant epilogue form for MATMUL_I8 (command flags; no reference
+ * counterpart - the reference has no switch, its form follows from how GCC
+ * compiled each of its kernels).  With a bias and/or an activation, the
+ * reference's outputs differ in the last bits between its own code paths:
+ *
+ *   block  (default)  out = fmaf(float(acc)*sa, sb, bias), activation
+ *                     polynomial evaluated with FMAs.  The reference's
+ *                     register-block AVX2 kernels (2x32 block, packed panel;
+ *                     src/kernels/kernels.cpp:634-701,779-869).
+ *   stream            out = (float(acc)*sa)*sb + bias (two roundings), FMA
+ *                     polynomial.  The reference's AVX2 rank-1 / rank-R decode
+ *                     streams (kernels.cpp:581-632,702-767): M=1 always, M=2/3
+ *                     when a thread's column slice is >= 1024.
+ *   scalar            no fused operation anywhere: VNPU_FORCE_ISA=scalar and
+ *                     VNPU_MODE=reference (kernels.cpp:537-550).
+ *
+ * Without bias and with epilogue NONE or RELU all three forms are the same
+ * bits.  VNPU_B200_EPILOGUE=block|stream|scalar in the environment sets the
+ * default of devices created afterwards.
+ */
+#define VNPU_CMD_FLAG_EPI_STREAM   (1u << 8)
+#define VNPU_CMD_FLAG_EPI_SCALAR   (1u << 9)
+
+/* The cudaStream_t behind a vnpu stream (as void*), so callers can order
+ * their own CUDA work and timing events against it. */
+VNPU_API void * VNPU_CALL vnpu_b200_stream_handle(vnpu_stream_t *stream);
+
+/* CUDA device ordinal of a vnpu device. */
+VNPU_API int VNPU_CALL vnpu_b200_device_ordinal(const vnpu_device_t *device);
+
+/* Number of kernels this library has launched on the device so far. */
+VNPU_API uint64_t VNPU_CALL vnpu_b200_kernel_launches(const vnpu_device_t *device);
+
+/* Device address of the packed K-major weight matrix ([N][k_stride] int8)
+ * and of its scales, for callers that fuse their own kernels around it. */
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_packed_weights_device(
+    const vnpu_packed_weights_t *weights, const int8_t **bt, uint32_t *k_stride,
+    const float **scales);
+
+/* Which MATMUL_I8 kernel the dispatcher picks for a shape, by name
+ * ("tcgen05", "gemv", "simt"); for tests and the bench. */
+VNPU_API const char * VNPU_CALL vnpu_b200_matmul_i8_kernel(uint32_t M, uint32_t K, uint32_t N,
+                                                          uint32_t lda, const void *A);
+
+/* Device-side wait self-test: launches a kernel that waits on a flag nothing
+ * sets, bounded by timeout_us, and returns VNPU_ERR_TIMEOUT when the bound is
+ * hit (VNPU_OK would mean the flag was seen).  It exercises the same bounded
+ * wait and error-word path the GEMM pipeline uses, without faulting the GPU. */
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_selftest_wait_timeout(vnpu_stream_t *stream,
+                                                                uint32_t timeout_us);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* VNPU_B200_H */

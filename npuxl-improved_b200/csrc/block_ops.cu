@@ -1,0 +1,434 @@
+// block_ops.cu - decoder-block operators on sm_100a: RMSNORM_F32, ROPE_F32,
+// SWIGLU_F32, ADD_F32, ATTENTION_F32 (src/kernels/llm.cpp).
+//
+// Each restates the arithmetic of the reference's AVX2 build in the same
+// order of operations where the order is cheap to keep (RMSNorm's 8-lane
+// sum, SwiGLU's exp256, ADD's FMA, attention's 16x64 blocking with its
+// 8-lane dot products and in-order probability sums), so on identical inputs
+// they reproduce the reference bit for bit; RoPE uses the device sinf/cosf
+// (<= 2 ulp from glibc) with the reference's inverse frequencies computed on
+// the host with the same libm powf.
+#include <cmath>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace vnpu_b200 {
+namespace {
+
+inline void count_launch(const LaunchCtx &ctx, uint64_t n = 1) {
+    if (ctx.launch_counter) *ctx.launch_counter += n;
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm (llm.cpp:80-106, AVX2): ss = 8-lane FMA partial sums over full
+// 8-element groups, hsum256 order, scalar FMA tail; inv = 1/sqrt(ss/cols+eps);
+// y = (x*w)*inv on the vector part, x*inv*w on the tail.
+// One warp per row; lanes 0..7 run the eight partial-sum chains.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ X,
+                                                      const float *__restrict__ W,
+                                                      float *__restrict__ Y, uint32_t rows,
+                                                      uint32_t cols, float eps) {
+    const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint32_t lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    const float *x = X + static_cast<uint64_t>(warp) * cols;
+    float *y = Y + static_cast<uint64_t>(warp) * cols;
+    const uint32_t full = cols & ~7u;
+    float part = 0.0f;
+    if (lane < 8)
+        for (uint32_t j = lane; j < full; j += 8) part = __fmaf_rn(x[j], x[j], part);
+    // hsum256: ((v0+v4)+(v1+v5)) + ((v2+v6)+(v3+v7))
+    const float hi = __shfl_down_sync(0xffffffffu, part, 4);
+    const float s = __fadd_rn(part, hi);             // lane i<4: v_i + v_{i+4}
+    const float s1 = __shfl_down_sync(0xffffffffu, s, 1);
+    const float s01 = __fadd_rn(s, s1);              // lane 0: s0+s1, lane 2: s2+s3
+    const float s23 = __shfl_down_sync(0xffffffffu, s01, 2);
+    float sum = __fadd_rn(s01, s23);                 // lane 0
+    if (lane == 0)
+        for (uint32_t j = full; j < cols; ++j) sum = __fmaf_rn(x[j], x[j], sum);
+    sum = __shfl_sync(0xffffffffu, sum, 0);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(cols)), eps)));
+    for (uint32_t j = lane; j < cols; j += 32) {
+        const float w = W ? W[j] : 1.0f;
+        y[j] = j < full ? __fmul_rn(__fmul_rn(x[j], w), inv) : __fmul_rn(__fmul_rn(x[j], inv), w);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// RoPE (llm.cpp:188-217, :576-602): one thread per (batch*head, token, pair).
+// ---------------------------------------------------------------------------
+constexpr uint32_t kRopeMaxPairs = 256;
+struct RopeFreq {
+    float inv[kRopeMaxPairs];
+};
+
+__device__ __forceinline__ void rotate_pair(float *x, uint32_t i0, uint32_t i1, float angle) {
+    float s, c;
+    sincosf(angle, &s, &c);
+    const float x0 = x[i0], x1 = x[i1];
+    x[i0] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+    x[i1] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+}
+
+__global__ void rope_kernel(float *__restrict__ Q, float *__restrict__ K,
+                            const int32_t *__restrict__ positions, uint32_t bh_count,
+                            uint32_t q_seq, uint32_t k_seq, uint32_t head_dim,
+                            uint32_t position_offset, uint32_t interleaved, float scaling,
+                            const RopeFreq freq) {
+    const uint32_t pairs = head_dim / 2;
+    const uint32_t seq = max(q_seq, k_seq);
+    const uint64_t total = static_cast<uint64_t>(bh_count) * seq * pairs;
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t j = static_cast<uint32_t>(i % pairs);
+        const uint64_t tok = i / pairs;
+        const uint32_t t = static_cast<uint32_t>(tok % seq);
+        const uint64_t bh = tok / seq;
+        const float position = __fmul_rn(
+            static_cast<float>(positions ? positions[t] : static_cast<int32_t>(t + position_offset)),
+            scaling);
+        const float angle = __fmul_rn(position, freq.inv[j]);
+        const uint32_t i0 = interleaved ? 2 * j : j;
+        const uint32_t i1 = interleaved ? 2 * j + 1 : j + pairs;
+        if (Q && t < q_seq) rotate_pair(Q + (bh * q_seq + t) * head_dim, i0, i1, angle);
+        if (K && t < k_seq) rotate_pair(K + (bh * k_seq + t) * head_dim, i0, i1, angle);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// SwiGLU (llm.cpp:289-306, AVX2): s = g / (1 + exp256(-g)); y = (s*u)*alpha.
+// ADD (llm.cpp:256-271, AVX2): y = fma(a, alpha, b*beta).
+// ---------------------------------------------------------------------------
+__global__ void swiglu_kernel(const float *__restrict__ G, const float *__restrict__ U,
+                              float *__restrict__ Y, uint64_t n, float alpha) {
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const float g = G[i];
+        const float s = __fdiv_rn(g, __fadd_rn(1.0f, ref_exp256_lane(-g)));
+        Y[i] = __fmul_rn(__fmul_rn(s, U[i]), alpha);
+    }
+}
+
+__global__ void swiglu_vec_kernel(const float4 *__restrict__ G, const float4 *__restrict__ U,
+                                  float4 *__restrict__ Y, uint64_t n4, float alpha) {
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const float4 g = G[i], u = U[i];
+        float4 y;
+        y.x = __fmul_rn(__fmul_rn(__fdiv_rn(g.x, __fadd_rn(1.0f, ref_exp256_lane(-g.x))), u.x), alpha);
+        y.y = __fmul_rn(__fmul_rn(__fdiv_rn(g.y, __fadd_rn(1.0f, ref_exp256_lane(-g.y))), u.y), alpha);
+        y.z = __fmul_rn(__fmul_rn(__fdiv_rn(g.z, __fadd_rn(1.0f, ref_exp256_lane(-g.z))), u.z), alpha);
+        y.w = __fmul_rn(__fmul_rn(__fdiv_rn(g.w, __fadd_rn(1.0f, ref_exp256_lane(-g.w))), u.w), alpha);
+        Y[i] = y;
+    }
+}
+
+__global__ void add_kernel(const float *__restrict__ A, const float *__restrict__ B,
+                           float *__restrict__ Y, uint64_t n, float alpha, float beta) {
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+        Y[i] = __fmaf_rn(A[i], alpha, __fmul_rn(B[i], beta));
+}
+
+__global__ void add_vec_kernel(const float4 *__restrict__ A, const float4 *__restrict__ B,
+                               float4 *__restrict__ Y, uint64_t n4, float alpha, float beta) {
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const float4 a = A[i], b = B[i];
+        Y[i] = make_float4(__fmaf_rn(a.x, alpha, __fmul_rn(b.x, beta)),
+                           __fmaf_rn(a.y, alpha, __fmul_rn(b.y, beta)),
+                           __fmaf_rn(a.z, alpha, __fmul_rn(b.z, beta)),
+                           __fmaf_rn(a.w, alpha, __fmul_rn(b.w, beta)));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Attention (llm.cpp:442-546).  One CTA (16 warps) per (batch*head, block of
+// 16 queries); keys in blocks of 64 as in the reference.
+//   scores : thread (key, chain) holds chain c of K[key] (elements 8t+c) in
+//            registers and runs the FMA chain against each query;
+//            the eight chains are combined in hsum256 order, the D%8 tail is
+//            FMA'd after, then *scale (+mask); causal keys are -inf.
+//   softmax: warp q: block max; skip the block if it is not finite;
+//            alpha = fast_expf(m - new_m), p = fast_expf(s - new_m) (the
+//            reference's attention is compiled without FMA: unfused
+//            polynomial); l = l*alpha + (in-order sum of p).
+//   values : thread (q, d): acc = acc*alpha, then acc = fma(V[j][d], p_j, acc)
+//            for j in order, skipping p == 0.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kAttBQ = 16;
+constexpr uint32_t kAttBK = 64;
+constexpr uint32_t kAttThreads = 512;
+constexpr uint32_t kAttMaxD = 256;
+constexpr uint32_t kAttMaxChain = kAttMaxD / 8;
+constexpr uint32_t kAttMaxAcc = kAttBQ * kAttMaxD / kAttThreads;  // 8
+
+struct AttParams {
+    const float *Q, *K, *V, *mask;
+    float *O;
+    uint32_t heads, seq_q, seq_k, D, causal;
+    float scale;
+};
+
+__global__ void __launch_bounds__(kAttThreads) attention_kernel(const AttParams p) {
+    extern __shared__ float att_smem[];
+    const uint32_t D = p.D;
+    float *Qs = att_smem;                                   // [16][D]
+    float *Vs = Qs + kAttBQ * D;                            // [64][D]
+    float *S = Vs + kAttBK * D;                             // [16][64] scores, then probs
+    float *alpha_s = S + kAttBQ * kAttBK;                   // [16]
+    float *m_s = alpha_s + kAttBQ;                          // [16]
+    float *l_s = m_s + kAttBQ;                              // [16]
+    int *active = reinterpret_cast<int *>(l_s + kAttBQ);    // [16]
+
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t bh = blockIdx.y;
+    const uint32_t q0 = blockIdx.x * kAttBQ;
+    const uint32_t qc = min(kAttBQ, p.seq_q - q0);
+    const uint64_t head_q = static_cast<uint64_t>(bh) * p.seq_q * D;
+    const uint64_t head_k = static_cast<uint64_t>(bh) * p.seq_k * D;
+    const float *Qh = p.Q + head_q;
+    const float *Kh = p.K + head_k;
+    const float *Vh = p.V + head_k;
+    const float *Mh = p.mask ? p.mask + static_cast<uint64_t>(bh) * p.seq_q * p.seq_k : nullptr;
+    const uint32_t causal_offset = p.seq_k > p.seq_q ? p.seq_k - p.seq_q : 0;
+
+    for (uint32_t i = tid; i < kAttBQ * D; i += kAttThreads) {
+        const uint32_t q = i / D;
+        Qs[i] = q < qc ? Qh[static_cast<uint64_t>(q0 + q) * D + (i % D)] : 0.0f;
+    }
+    if (tid < kAttBQ) {
+        m_s[tid] = -__int_as_float(0x7f800000);
+        l_s[tid] = 0.0f;
+    }
+    float acc[kAttMaxAcc];
+#pragma unroll
+    for (uint32_t r = 0; r < kAttMaxAcc; ++r) acc[r] = 0.0f;
+
+    const uint32_t chains = D / 8;
+    const uint32_t full = chains * 8;
+    // Blocks whose first key is past every query's causal limit are fully
+    // masked: the reference skips them (non-finite block max); so do we.
+    uint32_t k_end = p.seq_k;
+    if (p.causal) k_end = min(p.seq_k, q0 + qc - 1 + causal_offset + 1);
+
+    const uint32_t my_key = tid >> 3, my_chain = tid & 7;
+    for (uint32_t k0 = 0; k0 < k_end; k0 += kAttBK) {
+        const uint32_t kc = min(kAttBK, p.seq_k - k0);
+        __syncthreads();  // previous block's V / probabilities fully consumed
+        for (uint32_t i = tid; i < kc * D; i += kAttThreads)
+            Vs[i] = Vh[static_cast<uint64_t>(k0) * D + i];
+        // ---- scores
+        float kreg[kAttMaxChain];
+        const bool key_ok = my_key < kc;
+        const float *krow = Kh + static_cast<uint64_t>(k0 + (key_ok ? my_key : 0)) * D;
+#pragma unroll
+        for (uint32_t t = 0; t < kAttMaxChain; ++t)
+            kreg[t] = (key_ok && t < chains) ? __ldg(krow + 8 * t + my_chain) : 0.0f;
+        __syncthreads();  // Qs, Vs visible
+        for (uint32_t q = 0; q < qc; ++q) {
+            const float *qrow = Qs + q * D;
+            float part = 0.0f;
+#pragma unroll
+            for (uint32_t t = 0; t < kAttMaxChain; ++t)
+                if (t < chains) part = __fmaf_rn(qrow[8 * t + my_chain], kreg[t], part);
+            // hsum256 within the 8-lane group
+            const float hi = __shfl_down_sync(0xffffffffu, part, 4, 8);
+            const float s = __fadd_rn(part, hi);
+            const float s1 = __shfl_down_sync(0xffffffffu, s, 1, 8);
+            const float s01 = __fadd_rn(s, s1);
+            const float s23 = __shfl_down_sync(0xffffffffu, s01, 2, 8);
+            if (my_chain == 0 && key_ok) {
+                float dot = __fadd_rn(s01, s23);
+                for (uint32_t i = full; i < D; ++i) dot = __fmaf_rn(qrow[i], krow[i], dot);
+                const uint32_t qi = q0 + q, ki = k0 + my_key;
+                float sc;
+                if (p.causal && ki > qi + causal_offset) {
+                    sc = -__int_as_float(0x7f800000);
+                } else {
+                    sc = __fmul_rn(dot, p.scale);
+                    if (Mh) sc = __fadd_rn(sc, Mh[static_cast<uint64_t>(qi) * p.seq_k + ki]);
+                }
+                S[q * kAttBK + my_key] = sc;
+            }
+        }
+        __syncthreads();
+        // ---- online softmax, one warp per query
+        if (warp < qc) {
+            float* srow = S + warp * kAttBK;
+            float bmax = -__int_as_float(0x7f800000);
+            for (uint32_t j = lane; j < kc; j += 32) bmax = fmaxf(bmax, srow[j]);
+            for (int o = 16; o > 0; o >>= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
+            const bool act = isfinite(bmax);
+            if (act) {
+                const float m_old = m_s[warp];
+                const float nm = fmaxf(m_old, bmax);
+                for (uint32_t j = lane; j < kc; j += 32)
+                    srow[j] = ref_fast_expf(__fsub_rn(srow[j], nm), false);
+                __syncwarp();
+                if (lane == 0) {
+                    const float alpha = ref_fast_expf(__fsub_rn(m_old, nm), false);
+                    float sum_p = 0.0f;
+                    for (uint32_t j = 0; j < kc; ++j) sum_p = __fadd_rn(sum_p, srow[j]);
+                    l_s[warp] = __fadd_rn(__fmul_rn(l_s[warp], alpha), sum_p);
+                    m_s[warp] = nm;
+                    alpha_s[warp] = alpha;
+                }
+            }
+            if (lane == 0) active[warp] = act ? 1 : 0;
+        }
+        __syncthreads();
+        // ---- value accumulation
+#pragma unroll
+        for (uint32_t r = 0; r < kAttMaxAcc; ++r) {
+            const uint32_t idx = tid + r * kAttThreads;
+            if (idx >= qc * D) break;
+            const uint32_t q = idx / D, d = idx % D;
+            if (!active[q]) continue;
+            float a = __fmul_rn(acc[r], alpha_s[q]);
+            const float *prow = S + q * kAttBK;
+            for (uint32_t j = 0; j < kc; ++j) {
+                const float pj = prow[j];
+                if (pj == 0.0f) continue;
+                a = __fmaf_rn(Vs[j * D + d], pj, a);
+            }
+            acc[r] = a;
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (uint32_t r = 0; r < kAttMaxAcc; ++r) {
+        const uint32_t idx = tid + r * kAttThreads;
+        if (idx >= qc * D) break;
+        const uint32_t q = idx / D, d = idx % D;
+        const float l = l_s[q];
+        const float inv = l > 0.0f ? __fdiv_rn(1.0f, l) : 0.0f;
+        p.O[head_q + static_cast<uint64_t>(q0 + q) * D + d] = __fmul_rn(acc[r], inv);
+    }
+}
+
+// Spins on a flag nothing sets, bounded by limit_ns: the device-side wait
+// pattern of the GEMM pipeline, exercised on its own.
+__global__ void wait_probe_kernel(const uint32_t *flag, uint64_t limit_ns, uint32_t *err) {
+    const uint64_t start = global_timer_ns();
+    while (true) {
+        if (*reinterpret_cast<const volatile uint32_t *>(flag) != 0u) return;
+        if (global_timer_ns() - start > limit_ns) {
+            record_error(err, kErrWaitTimeout);
+            return;
+        }
+        __nanosleep(1000);
+    }
+}
+
+unsigned grid_for(uint64_t n, int num_sms, unsigned threads) {
+    const uint64_t want = (n + threads - 1) / threads;
+    const uint64_t cap = static_cast<uint64_t>(num_sms) * 16;
+    return static_cast<unsigned>(want < cap ? (want ? want : 1) : cap);
+}
+
+}  // namespace
+
+cudaError_t rmsnorm(const LaunchCtx &ctx, const float *X, const float *W, float *Y,
+                    uint32_t rows, uint32_t cols, float eps) {
+    const unsigned blocks = (rows + 7) / 8;
+    rmsnorm_kernel<<<blocks, 256, 0, ctx.stream>>>(X, W, Y, rows, cols, eps);
+    count_launch(ctx);
+    return cudaGetLastError();
+}
+
+cudaError_t rope(const LaunchCtx &ctx, float *Q, float *K, const int32_t *positions,
+                 uint32_t batch, uint32_t heads, uint32_t q_seq, uint32_t k_seq,
+                 uint32_t head_dim, uint32_t position_offset, uint32_t interleaved,
+                 float scaling, const float *inv_freq_host) {
+    if (head_dim / 2 > kRopeMaxPairs) return cudaErrorInvalidValue;
+    RopeFreq f;
+    for (uint32_t j = 0; j < head_dim / 2; ++j) f.inv[j] = inv_freq_host[j];
+    const uint64_t total = static_cast<uint64_t>(batch) * heads * (q_seq > k_seq ? q_seq : k_seq) *
+                           (head_dim / 2);
+    rope_kernel<<<grid_for(total, ctx.num_sms, 256), 256, 0, ctx.stream>>>(
+        Q, K, positions, batch * heads, q_seq, k_seq, head_dim, position_offset, interleaved,
+        scaling, f);
+    count_launch(ctx);
+    return cudaGetLastError();
+}
+
+cudaError_t swiglu(const LaunchCtx &ctx, const float *gate, const float *up, float *Y,
+                   uint64_t count, float alpha) {
+    const bool vec = count % 4 == 0 && (reinterpret_cast<uintptr_t>(gate) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(up) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(Y) & 15) == 0;
+    if (vec)
+        swiglu_vec_kernel<<<grid_for(count / 4, ctx.num_sms, 256), 256, 0, ctx.stream>>>(
+            reinterpret_cast<const float4 *>(gate), reinterpret_cast<const float4 *>(up),
+            reinterpret_cast<float4 *>(Y), count / 4, alpha);
+    else
+        swiglu_kernel<<<grid_for(count, ctx.num_sms, 256), 256, 0, ctx.stream>>>(gate, up, Y,
+                                                                                 count, alpha);
+    count_launch(ctx);
+    return cudaGetLastError();
+}
+
+cudaError_t add(const LaunchCtx &ctx, const float *A, const float *B, float *Y, uint64_t count,
+                float alpha, float beta) {
+    const bool vec = count % 4 == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(B) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(Y) & 15) == 0;
+    if (vec)
+        add_vec_kernel<<<grid_for(count / 4, ctx.num_sms, 256), 256, 0, ctx.stream>>>(
+            reinterpret_cast<const float4 *>(A), reinterpret_cast<const float4 *>(B),
+            reinterpret_cast<float4 *>(Y), count / 4, alpha, beta);
+    else
+        add_kernel<<<grid_for(count, ctx.num_sms, 256), 256, 0, ctx.stream>>>(A, B, Y, count,
+                                                                              alpha, beta);
+    count_launch(ctx);
+    return cudaGetLastError();
+}
+
+cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, const float *V,
+                      const float *mask, float *O, uint32_t batch, uint32_t heads,
+                      uint32_t seq_q, uint32_t seq_k, uint32_t head_dim, uint32_t causal,
+                      float scale) {
+    if (head_dim > kAttMaxD || head_dim == 0) return cudaErrorInvalidValue;
+    const size_t smem = sizeof(float) * (kAttBQ * head_dim + kAttBK * head_dim +
+                                         kAttBQ * kAttBK + 3 * kAttBQ) +
+                        sizeof(int) * kAttBQ;
+    static int configured_for = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_for != dev) {
+        cudaError_t e = cudaFuncSetAttribute(attention_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(sizeof(float) *
+                                                              (kAttBQ + kAttBK) * kAttMaxD +
+                                                              8192));
+        if (e != cudaSuccess) return e;
+        configured_for = dev;
+    }
+    AttParams ap;
+    ap.Q = Q;
+    ap.K = K;
+    ap.V = V;
+    ap.mask = mask;
+    ap.O = O;
+    ap.heads = heads;
+    ap.seq_q = seq_q;
+    ap.seq_k = seq_k;
+    ap.D = head_dim;
+    ap.causal = causal;
+    ap.scale = scale;
+    dim3 grid((seq_q + kAttBQ - 1) / kAttBQ, batch * heads);
+    attention_kernel<<<grid, kAttThreads, smem, ctx.stream>>>(ap);
+    count_launch(ctx);
+    return cudaGetLastError();
+}
+
+cudaError_t wait_timeout_probe(const LaunchCtx &ctx, const uint32_t *flag, uint64_t limit_ns) {
+    wait_probe_kernel<<<1, 1, 0, ctx.stream>>>(flag, limit_ns, ctx.err);
+    count_launch(ctx);
+    return cudaGetLastError();
+}
+
+}  // namespace vnpu_b200

@@ -1,0 +1,292 @@
+// common.cuh - device helpers shared by the sm_100a kernels.
+//
+// * the reference's float arithmetic, restated with explicit rounding
+//   intrinsics so nvcc's contraction never changes a result: every fused
+//   multiply-add is a __fmaf_rn that mirrors a fusion GCC performs in the
+//   reference's AVX2 kernels, every other product/sum is __fmul_rn/__fadd_rn;
+// * inline-PTX wrappers for mbarrier, TMA (cp.async.bulk.tensor), and the
+//   5th-generation tensor core (tcgen05 alloc/mma/commit/ld);
+// * bounded waits: every spin on an mbarrier gives up after a wall-clock
+//   limit, records an error code in the stream's device error word, and lets
+//   the kernel wind down instead of hanging the GPU.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "kernels.h"
+
+namespace vnpu_b200 {
+
+// DeviceError and EpiForm come from kernels.h.
+
+// ---------------------------------------------------------------------------
+// Reference arithmetic (src/internal.h:87-136, src/kernels/kernels.cpp:526-535)
+// ---------------------------------------------------------------------------
+
+// 2^f on [0,1): the reference's degree-5 polynomial (internal.h:97-101).
+__device__ __forceinline__ float exp2_poly(float f, bool fused) {
+    const float c1 = 0.6931471805599453f, c2 = 0.2402265069591007f,
+                c3 = 0.05550410866482158f, c4 = 0.009618129107628477f,
+                c5 = 0.0013333558146428443f;
+    if (fused) {
+        float p = __fmaf_rn(f, c5, c4);
+        p = __fmaf_rn(f, p, c3);
+        p = __fmaf_rn(f, p, c2);
+        p = __fmaf_rn(f, p, c1);
+        return __fmaf_rn(f, p, 1.0f);
+    }
+    float p = __fadd_rn(c4, __fmul_rn(f, c5));
+    p = __fadd_rn(c3, __fmul_rn(f, p));
+    p = __fadd_rn(c2, __fmul_rn(f, p));
+    p = __fadd_rn(c1, __fmul_rn(f, p));
+    return __fadd_rn(1.0f, __fmul_rn(f, p));
+}
+
+// fast_expf (internal.h:87-108): cut-offs at +-80, z = x*log2e, split into
+// floor and fraction, polynomial, exact scaling by 2^floor.
+__device__ __forceinline__ float ref_fast_expf(float x, bool fused) {
+    if (x < -80.0f) return 0.0f;
+    if (x > 80.0f) return __int_as_float(0x7f800000);
+    const float z = __fmul_rn(x, 1.4426950408889634f);
+    const float zi = floorf(z);
+    const float f = __fsub_rn(z, zi);
+    return ldexpf(exp2_poly(f, fused), __float2int_rz(zi));
+}
+
+// exp256_ps (src/kernels/llm.cpp:32-56): clamps to [-80,80] instead; for the
+// clamped range 2^n built from exponent bits equals ldexpf exactly.
+__device__ __forceinline__ float ref_exp256_lane(float x) {
+    x = fmaxf(-80.0f, fminf(x, 80.0f));
+    const float z = __fmul_rn(x, 1.4426950408889634f);
+    const float zi = floorf(z);
+    const float f = __fsub_rn(z, zi);
+    return ldexpf(exp2_poly(f, true), __float2int_rz(zi));
+}
+
+__device__ __forceinline__ float ref_silu(float x, bool fused) {
+    return __fdiv_rn(x, __fadd_rn(1.0f, ref_fast_expf(-x, fused)));
+}
+
+__device__ __forceinline__ float ref_gelu_tanh(float x, bool fused) {
+    const float k0 = 0.7978845608028654f, k1 = 0.035677408136300125f;
+    const float x3 = __fmul_rn(__fmul_rn(x, x), x);
+    const float inner = fused ? __fmul_rn(k0, __fmaf_rn(k1, x3, x))
+                              : __fmul_rn(k0, __fadd_rn(x, __fmul_rn(k1, x3)));
+    const float e = ref_fast_expf(__fmul_rn(-2.0f, inner), fused);
+    const float t = __fsub_rn(__fdiv_rn(2.0f, __fadd_rn(1.0f, e)), 1.0f);
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, t));
+}
+
+__device__ __forceinline__ float ref_activation(float v, uint32_t epilogue, bool fused) {
+    switch (epilogue) {
+    case 1: return v > 0.0f ? v : 0.0f;
+    case 2: return ref_silu(v, fused);
+    case 3:
+    case 4: return ref_gelu_tanh(v, fused);
+    default: return v;
+    }
+}
+
+// store_i8_c (kernels.cpp:526-535) for one accumulator.
+__device__ __forceinline__ float ref_dequant(int32_t acc, float sa, float sb, bool has_bias,
+                                             float bias, uint32_t epilogue, uint32_t form) {
+    const float t = __fmul_rn(__int2float_rn(acc), sa);
+    float out;
+    if (!has_bias) {
+        out = __fmul_rn(t, sb);
+    } else if (form == kFormBlock) {
+        out = __fmaf_rn(t, sb, bias);
+    } else {
+        out = __fadd_rn(__fmul_rn(t, sb), bias);
+    }
+    return ref_activation(out, epilogue, form != kFormScalar);
+}
+
+// ---------------------------------------------------------------------------
+// Time and errors
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void record_error(uint32_t *err, uint32_t code) {
+    if (err) atomicOr(err, code);
+}
+
+// ---------------------------------------------------------------------------
+// Shared memory, mbarriers
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+                 : "memory");
+}
+
+// Make barrier initialisation visible to the async proxy (TMA, tcgen05).
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
+                     smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Wait for the phase with the given parity to complete.  Gives up when the
+// wall-clock deadline passes (or when another thread of the CTA has already
+// given up, *abort != 0): records kErrWaitTimeout and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64_t limit_ns,
+                                          uint32_t *err, volatile int *abort) {
+    const uint32_t a = smem_addr(bar);
+    if (mbar_try_wait(a, parity)) return true;
+    const uint64_t start = global_timer_ns();
+    for (uint32_t spin = 1;; ++spin) {
+        if (mbar_try_wait(a, parity)) return true;
+        if ((spin & 63u) == 0) {
+            if (abort && *abort) return false;
+            if (global_timer_ns() - start > limit_ns) {
+                record_error(err, kErrWaitTimeout);
+                if (abort) *abort = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// TMA
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
+// 2-D tiled load into this CTA's shared memory, completing on `bar`.
+// x is the innermost (contiguous) coordinate in elements; the caller keeps
+// x * elem_bytes a multiple of 16.
+__device__ __forceinline__ void tma_load_2d(void *smem_dst, const void *tmap, uint64_t *bar,
+                                            int32_t x, int32_t y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_addr(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 (5th-generation tensor core, tensor memory)
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *smem_result, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(smem_result)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] x B[smem desc], int8 x int8 -> int32.
+__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive (once) on `bar` when every tcgen05.mma issued so far by this thread
+// has completed.
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 32 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major operand tile written by TMA
+// with 128-byte swizzle: rows of 128 bytes, 8-row swizzle atoms 1024 bytes
+// apart (SBO), leading offset unused for this layout (encoded 1), version 1,
+// layout type 2 = SWIZZLE_128B.  The tile base must be 1024-byte aligned;
+// stepping K inside the atom adds the byte offset to the start address.
+__device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>(1u) << 16;
+    d |= static_cast<uint64_t>(1024u >> 4) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(2u) << 61;
+    return d;
+}
+
+// Instruction descriptor for kind::i8: D s32, A s8, B s8, both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_i8(uint32_t m, uint32_t n) {
+    return (2u << 4)            // D format: s32
+           | (1u << 7)          // A format: signed 8-bit
+           | (1u << 10)         // B format: signed 8-bit
+           | ((n >> 3) << 17)   // N / 8
+           | ((m >> 4) << 24);  // M / 16
+}
+
+}  // namespace vnpu_b200

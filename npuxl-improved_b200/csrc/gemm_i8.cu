@@ -1,0 +1,610 @@
+// gemm_i8.cu - MATMUL_I8 on sm_100a.
+//
+// C[m][n] = epilogue(dequant(sum_k A[m][k] * B[k][n]))   (int8 x int8 -> int32)
+//
+// Restates the reference's int8 GEMM (src/kernels/kernels.cpp:526-978,
+// dispatch :922-978): int32 accumulation over all of K is exact, so any tiling
+// gives the reference's integers; the dequant epilogue (store_i8_c,
+// kernels.cpp:526-535) is reproduced operation for operation in
+// ref_dequant() (common.cuh).
+//
+// Three kernels:
+//  * tcgen05  - persistent warp-specialised tensor-core GEMM.  One CTA per SM,
+//               128x256 output tile, K in 128-byte steps.  Warp 0 issues TMA
+//               loads (128B swizzle) into a 4-stage shared-memory ring; warp 1
+//               (one elected thread) issues tcgen05.mma kind::i8 into one of
+//               two 128x256 int32 accumulators in tensor memory (all 512
+//               columns); warps 2-5 drain the other accumulator with
+//               tcgen05.ld, apply the dequant epilogue and store f32 C.
+//  * gemv     - M <= 8 decode: HBM-bound stream of the K-major weights with
+//               16-byte loads, __dp4a, warp-shuffle reduction.
+//  * simt     - any stride / alignment the TMA path cannot take: 64x64 tiles
+//               through shared memory with __dp4a.  Also the GPU-side
+//               cross-check of the other two.
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace vnpu_b200 {
+namespace {
+
+inline void count_launch(const LaunchCtx &ctx) {
+    if (ctx.launch_counter) *ctx.launch_counter += 1;
+}
+
+// ===========================================================================
+// tcgen05 tensor-core GEMM
+// ===========================================================================
+
+constexpr uint32_t kBM = 128;                 // rows per tile (UMMA M)
+constexpr uint32_t kBN = 256;                 // columns per tile (UMMA N)
+constexpr uint32_t kBK = 128;                 // K bytes per stage (one 128B swizzle atom)
+constexpr uint32_t kUmmaK = 32;               // K per tcgen05.mma kind::i8
+constexpr uint32_t kStages = 4;
+constexpr uint32_t kABytes = kBM * kBK;       // 16 KiB
+constexpr uint32_t kBBytes = kBN * kBK;       // 32 KiB
+constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kTmemCols = 2 * kBN;       // two accumulators
+constexpr uint32_t kThreads = 192;            // 6 warps
+constexpr uint32_t kEpiWarps = 4;
+constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024;  // + alignment slack
+constexpr uint32_t kGroupM = 8;               // raster: 8 m-tiles per band
+
+struct TcParams {
+    const float *scale_a;
+    const float *scale_b;
+    const float *bias;
+    float *C;
+    uint32_t ldc;
+    uint32_t M, N, K;
+    uint32_t tiles_m, tiles_n, num_kb;
+    uint32_t epilogue, form;
+    uint32_t *err;
+    uint64_t limit_ns;
+};
+
+__device__ __forceinline__ void tile_coords(uint32_t t, uint32_t tiles_m, uint32_t tiles_n,
+                                            uint32_t &mb, uint32_t &nb) {
+    // Grouped raster: bands of kGroupM m-tiles walk all n-tiles, so a wave of
+    // CTAs shares a few A row-panels and a contiguous run of B panels in L2.
+    const uint32_t per_band = kGroupM * tiles_n;
+    const uint32_t band = t / per_band;
+    const uint32_t first_m = band * kGroupM;
+    const uint32_t rows = min(kGroupM, tiles_m - first_m);
+    const uint32_t r = t - band * per_band;
+    mb = first_m + r % rows;
+    nb = r / rows;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_i8_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                           const __grid_constant__ CUtensorMap tmap_b, const TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[kStages];
+    __shared__ __align__(8) uint64_t empty_bar[kStages];
+    __shared__ __align__(8) uint64_t tmem_full_bar[2];
+    __shared__ __align__(8) uint64_t tmem_empty_bar[2];
+    __shared__ __align__(8) uint64_t drain_bar;
+    __shared__ uint32_t tmem_base_slot;
+    __shared__ volatile int abort_flag;
+
+    // 1024-byte aligned tile ring (128B swizzle atoms are 1024 bytes).
+    const uint32_t raw_addr = smem_addr(smem_raw);
+    uint8_t *ring = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+
+    const uint32_t warp = threadIdx.x >> 5;
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t total_tiles = p.tiles_m * p.tiles_n;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < kStages; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (uint32_t a = 0; a < 2; ++a) {
+            mbar_init(&tmem_full_bar[a], 1);
+            mbar_init(&tmem_empty_bar[a], kEpiWarps);
+        }
+        mbar_init(&drain_bar, 1);
+        abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmap_a);
+        tma_prefetch_desc(&tmap_b);
+    }
+    if (warp == 1) {
+        tmem_alloc(&tmem_base_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_base_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (uint32_t t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+                uint32_t mb, nb;
+                tile_coords(t, p.tiles_m, p.tiles_n, mb, nb);
+                for (uint32_t kb = 0; kb < p.num_kb; ++kb, ++it) {
+                    const uint32_t s = it % kStages;
+                    const uint32_t ph = (it / kStages) & 1u;
+                    if (!mbar_wait(&empty_bar[s], ph ^ 1u, p.limit_ns, p.err, &abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *sa = ring + s * kStageBytes;
+                    uint8_t *sb = sa + kABytes;
+                    mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+                    tma_load_2d(sa, &tmap_a, &full_bar[s], static_cast<int32_t>(kb * kBK),
+                                static_cast<int32_t>(mb * kBM));
+                    tma_load_2d(sb, &tmap_b, &full_bar[s], static_cast<int32_t>(kb * kBK),
+                                static_cast<int32_t>(nb * kBN));
+                }
+            }
+            // Never leave with copies in flight: wait for the last loads issued.
+            const uint32_t tail = it < kStages ? it : kStages;
+            for (uint32_t i = it - tail; i < it; ++i)
+                mbar_wait(&full_bar[i % kStages], (i / kStages) & 1u, p.limit_ns, p.err,
+                          nullptr);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_i8(kBM, kBN);
+            uint32_t it = 0, tcount = 0;
+            bool ok = true;
+            for (uint32_t t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++tcount) {
+                const uint32_t acc = tcount & 1u;
+                const uint32_t use = tcount >> 1;
+                if (!mbar_wait(&tmem_empty_bar[acc], (use & 1u) ^ 1u, p.limit_ns, p.err,
+                               &abort_flag))
+                    break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * kBN;
+                for (uint32_t kb = 0; kb < p.num_kb; ++kb, ++it) {
+                    const uint32_t s = it % kStages;
+                    const uint32_t ph = (it / kStages) & 1u;
+                    if (!mbar_wait(&full_bar[s], ph, p.limit_ns, p.err, &abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_addr(ring + s * kStageBytes);
+                    const uint64_t adesc = umma_desc_k_sw128(sa);
+                    const uint64_t bdesc = umma_desc_k_sw128(sa + kABytes);
+#pragma unroll
+                    for (uint32_t kk = 0; kk < kBK / kUmmaK; ++kk) {
+                        // +32 bytes of K inside the swizzle atom = +2 in the
+                        // 16-byte-granular start address field.
+                        umma_i8(d_tmem, adesc + 2u * kk, bdesc + 2u * kk, idesc,
+                                (kb | kk) != 0u);
+                    }
+                    umma_commit(&empty_bar[s]);
+                }
+                if (!ok) break;
+                umma_commit(&tmem_full_bar[acc]);
+            }
+            // All issued MMAs complete before tensor memory is released.
+            umma_commit(&drain_bar);
+            mbar_wait(&drain_bar, 0, p.limit_ns, p.err, nullptr);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        // Warp w may only touch TMEM lanes 32*(w%4) .. +31.
+        const uint32_t lane_base = (warp & 3u) * 32u;
+        const uint32_t row = lane_base + lane;
+        const bool has_bias = p.bias != nullptr;
+        const bool vec_ok = (p.ldc % 4u == 0u) &&
+                            ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0u);
+        uint32_t tcount = 0;
+        for (uint32_t t = blockIdx.x; t < total_tiles; t += gridDim.x, ++tcount) {
+            uint32_t mb, nb;
+            tile_coords(t, p.tiles_m, p.tiles_n, mb, nb);
+            const uint32_t acc = tcount & 1u;
+            const uint32_t use = tcount >> 1;
+            // Lane 0 waits, the warp follows its verdict: the tcgen05.ld below
+            // is .sync.aligned and needs all 32 lanes together.
+            uint32_t ok = 0;
+            if (lane == 0)
+                ok = mbar_wait(&tmem_full_bar[acc], use & 1u, p.limit_ns, p.err, &abort_flag);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t m = mb * kBM + row;
+            const bool row_ok = m < p.M;
+            const float sa = row_ok ? (p.scale_a ? __ldg(p.scale_a + m) : 1.0f) : 0.0f;
+            float *crow = p.C + static_cast<uint64_t>(row_ok ? m : 0) * p.ldc;
+#pragma unroll 1
+            for (uint32_t c = 0; c < kBN / 32u; ++c) {
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld_32cols(tmem_base + (lane_base << 16) + acc * kBN + c * 32u, r);
+                tmem_wait_ld();
+                const uint32_t n0 = nb * kBN + c * 32u;
+                if (!row_ok || n0 >= p.N) continue;
+                if (vec_ok && n0 + 32u <= p.N) {
+#pragma unroll
+                    for (uint32_t j = 0; j < 32u; j += 4u) {
+                        float4 o;
+                        o.x = ref_dequant(static_cast<int32_t>(r[j + 0]), sa,
+                                          __ldg(p.scale_b + n0 + j + 0), has_bias,
+                                          has_bias ? __ldg(p.bias + n0 + j + 0) : 0.0f,
+                                          p.epilogue, p.form);
+                        o.y = ref_dequant(static_cast<int32_t>(r[j + 1]), sa,
+                                          __ldg(p.scale_b + n0 + j + 1), has_bias,
+                                          has_bias ? __ldg(p.bias + n0 + j + 1) : 0.0f,
+                                          p.epilogue, p.form);
+                        o.z = ref_dequant(static_cast<int32_t>(r[j + 2]), sa,
+                                          __ldg(p.scale_b + n0 + j + 2), has_bias,
+                                          has_bias ? __ldg(p.bias + n0 + j + 2) : 0.0f,
+                                          p.epilogue, p.form);
+                        o.w = ref_dequant(static_cast<int32_t>(r[j + 3]), sa,
+                                          __ldg(p.scale_b + n0 + j + 3), has_bias,
+                                          has_bias ? __ldg(p.bias + n0 + j + 3) : 0.0f,
+                                          p.epilogue, p.form);
+                        *reinterpret_cast<float4 *>(crow + n0 + j) = o;
+                    }
+                } else {
+#pragma unroll
+                    for (uint32_t j = 0; j < 32u; ++j) {
+                        const uint32_t n = n0 + j;
+                        if (n < p.N)
+                            crow[n] = ref_dequant(static_cast<int32_t>(r[j]), sa,
+                                                  __ldg(p.scale_b + n), has_bias,
+                                                  has_bias ? __ldg(p.bias + n) : 0.0f,
+                                                  p.epilogue, p.form);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_empty_bar[acc]);
+        }
+    }
+
+    // ---------------------------------------------------------------- teardown
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ===========================================================================
+// M <= 8 decode GEMV
+// ===========================================================================
+
+constexpr int kGvThreads = 256;
+constexpr int kGvColsPerWarp = 2;
+constexpr int kGvColsPerCta = (kGvThreads / 32) * kGvColsPerWarp;
+
+struct GvParams {
+    const int8_t *A;
+    uint32_t lda;
+    const int8_t *Bt;
+    uint32_t k_stride;
+    const float *scale_a;
+    const float *scale_b;
+    const float *bias;
+    float *C;
+    uint32_t ldc;
+    uint32_t M, K, N;
+    uint32_t epilogue, form;
+};
+
+// 16 bytes of row m of A starting at k (zeros past K; B is zero there too).
+template <bool kAligned>
+__device__ __forceinline__ int4 load_a16(const GvParams &p, uint32_t m, uint32_t k) {
+    const int8_t *row = p.A + static_cast<uint64_t>(m) * p.lda;
+    if (kAligned && k + 16u <= p.K) return __ldg(reinterpret_cast<const int4 *>(row + k));
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (uint32_t b = 0; b < 16u; ++b)
+        if (k + b < p.K)
+            w[b >> 2] |= static_cast<uint32_t>(static_cast<uint8_t>(row[k + b])) << (8u * (b & 3u));
+    return make_int4(static_cast<int>(w[0]), static_cast<int>(w[1]), static_cast<int>(w[2]),
+                     static_cast<int>(w[3]));
+}
+
+template <int kM, bool kAligned>
+__global__ void __launch_bounds__(kGvThreads) gemv_i8_kernel(const GvParams p) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t n_first = blockIdx.x * kGvColsPerCta + warp * kGvColsPerWarp;
+    int32_t acc[kGvColsPerWarp][kM];
+#pragma unroll
+    for (int c = 0; c < kGvColsPerWarp; ++c)
+#pragma unroll
+        for (int m = 0; m < kM; ++m) acc[c][m] = 0;
+
+    const int4 *bcol[kGvColsPerWarp];
+#pragma unroll
+    for (int c = 0; c < kGvColsPerWarp; ++c) {
+        const uint32_t n = min(n_first + c, p.N - 1);
+        bcol[c] = reinterpret_cast<const int4 *>(p.Bt + static_cast<uint64_t>(n) * p.k_stride);
+    }
+    // Each lane owns 16 bytes of every 512-byte K chunk; 4 chunks in flight.
+    constexpr uint32_t kUnroll = 4;
+    const uint32_t k_end = p.K;
+    for (uint32_t k0 = lane * 16u; k0 < k_end; k0 += 512u * kUnroll) {
+        int4 b[kUnroll][kGvColsPerWarp];
+#pragma unroll
+        for (uint32_t u = 0; u < kUnroll; ++u) {
+            const uint32_t k = k0 + u * 512u;
+#pragma unroll
+            for (int c = 0; c < kGvColsPerWarp; ++c)
+                b[u][c] = k < k_end ? __ldcs(bcol[c] + (k >> 4)) : make_int4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < kUnroll; ++u) {
+            const uint32_t k = k0 + u * 512u;
+            if (k >= k_end) break;
+#pragma unroll
+            for (int m = 0; m < kM; ++m) {
+                if (m >= static_cast<int>(p.M)) break;
+                const int4 a = load_a16<kAligned>(p, m, k);
+#pragma unroll
+                for (int c = 0; c < kGvColsPerWarp; ++c) {
+                    int s = acc[c][m];
+                    s = __dp4a(a.x, b[u][c].x, s);
+                    s = __dp4a(a.y, b[u][c].y, s);
+                    s = __dp4a(a.z, b[u][c].z, s);
+                    s = __dp4a(a.w, b[u][c].w, s);
+                    acc[c][m] = s;
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < kGvColsPerWarp; ++c)
+#pragma unroll
+        for (int m = 0; m < kM; ++m)
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+                acc[c][m] += __shfl_xor_sync(0xffffffffu, acc[c][m], o);
+
+    const bool has_bias = p.bias != nullptr;
+#pragma unroll
+    for (int c = 0; c < kGvColsPerWarp; ++c) {
+        const uint32_t n = n_first + c;
+        if (n >= p.N) continue;
+#pragma unroll
+        for (int m = 0; m < kM; ++m) {
+            if (static_cast<uint32_t>(m) == lane && static_cast<uint32_t>(m) < p.M) {
+                const float sa = p.scale_a ? __ldg(p.scale_a + m) : 1.0f;
+                p.C[static_cast<uint64_t>(m) * p.ldc + n] =
+                    ref_dequant(acc[c][m], sa, __ldg(p.scale_b + n), has_bias,
+                                has_bias ? __ldg(p.bias + n) : 0.0f, p.epilogue, p.form);
+            }
+        }
+    }
+}
+
+// ===========================================================================
+// SIMT fallback: 64x64 tiles, 256 threads, 4x4 outputs per thread.
+// ===========================================================================
+
+__global__ void __launch_bounds__(256) gemm_i8_simt_kernel(const GvParams p) {
+    __shared__ int32_t As[64][9];   // 64 rows x 32 K bytes (8 words), padded
+    __shared__ int32_t Bs[64][9];   // 64 columns x 32 K bytes
+    const uint32_t tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const uint32_t m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+    int32_t acc[4][4] = {};
+    for (uint32_t k0 = 0; k0 < p.K; k0 += 32) {
+        for (uint32_t i = threadIdx.x; i < 64 * 8; i += 256) {
+            const uint32_t r = i >> 3, w = i & 7;
+            uint32_t av = 0, bv = 0;
+            const uint32_t m = m0 + r, n = n0 + r;
+#pragma unroll
+            for (uint32_t b = 0; b < 4; ++b) {
+                const uint32_t k = k0 + w * 4 + b;
+                if (m < p.M && k < p.K)
+                    av |= static_cast<uint32_t>(static_cast<uint8_t>(
+                              p.A[static_cast<uint64_t>(m) * p.lda + k]))
+                          << (8 * b);
+                if (n < p.N && k < p.K)
+                    bv |= static_cast<uint32_t>(static_cast<uint8_t>(
+                              p.Bt[static_cast<uint64_t>(n) * p.k_stride + k]))
+                          << (8 * b);
+            }
+            As[r][w] = static_cast<int32_t>(av);
+            Bs[r][w] = static_cast<int32_t>(bv);
+        }
+        __syncthreads();
+#pragma unroll
+        for (uint32_t w = 0; w < 8; ++w) {
+            int32_t a[4], b[4];
+#pragma unroll
+            for (uint32_t i = 0; i < 4; ++i) {
+                a[i] = As[ty * 4 + i][w];
+                b[i] = Bs[tx * 4 + i][w];
+            }
+#pragma unroll
+            for (uint32_t i = 0; i < 4; ++i)
+#pragma unroll
+                for (uint32_t j = 0; j < 4; ++j) acc[i][j] = __dp4a(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+    const bool has_bias = p.bias != nullptr;
+#pragma unroll
+    for (uint32_t i = 0; i < 4; ++i) {
+        const uint32_t m = m0 + ty * 4 + i;
+        if (m >= p.M) continue;
+        const float sa = p.scale_a ? p.scale_a[m] : 1.0f;
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+            const uint32_t n = n0 + tx * 4 + j;
+            if (n >= p.N) continue;
+            p.C[static_cast<uint64_t>(m) * p.ldc + n] =
+                ref_dequant(acc[i][j], sa, p.scale_b[n], has_bias, has_bias ? p.bias[n] : 0.0f,
+                            p.epilogue, p.form);
+        }
+    }
+}
+
+GvParams gv_params(const MatmulI8 &p) {
+    GvParams g;
+    g.A = p.A;
+    g.lda = p.lda;
+    g.Bt = p.Bt;
+    g.k_stride = p.k_stride;
+    g.scale_a = p.scale_a;
+    g.scale_b = p.scale_b;
+    g.bias = p.bias;
+    g.C = p.C;
+    g.ldc = p.ldc;
+    g.M = p.M;
+    g.K = p.K;
+    g.N = p.N;
+    g.epilogue = p.epilogue;
+    g.form = p.form;
+    return g;
+}
+
+template <int kM>
+cudaError_t launch_gemv_m(const LaunchCtx &ctx, const GvParams &g, bool aligned) {
+    const unsigned grid = (g.N + kGvColsPerCta - 1) / kGvColsPerCta;
+    if (aligned)
+        gemv_i8_kernel<kM, true><<<grid, kGvThreads, 0, ctx.stream>>>(g);
+    else
+        gemv_i8_kernel<kM, false><<<grid, kGvThreads, 0, ctx.stream>>>(g);
+    return cudaGetLastError();
+}
+
+// Driver entry point for cuTensorMapEncodeTiled, resolved once.
+PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, []() {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+}  // namespace
+
+bool encode_tmap_kmajor_i8(CUtensorMap *map, const void *base, uint64_t k_extent, uint64_t rows,
+                           uint64_t row_stride_bytes, uint32_t box_k, uint32_t box_rows) {
+    auto fn = tmap_encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {k_extent, rows};
+    const cuuint64_t strides[1] = {row_stride_bytes};
+    const cuuint32_t box[2] = {box_k, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+MatmulKernel choose_matmul_kernel(uint32_t M, uint32_t K, uint32_t N, uint32_t lda,
+                                  const void *A) {
+    (void)N;
+    // TMA needs a 16-byte aligned base and a row stride that is a multiple of
+    // 16 bytes; anything else takes the SIMT kernel (still on the GPU).
+    const bool tma_ok = (reinterpret_cast<uintptr_t>(A) % 16u == 0u) && (lda % 16u == 0u) &&
+                        K >= 16u;
+    // VNPU_B200_FORCE_KERNEL=tcgen05|gemv|simt pins the choice where the kernel
+    // can take the shape (tests use it to compare kernels on equal inputs).
+    if (const char *f = std::getenv("VNPU_B200_FORCE_KERNEL")) {
+        if (!std::strcmp(f, "simt")) return MatmulKernel::kSimt;
+        if (!std::strcmp(f, "gemv") && M <= 8) return MatmulKernel::kGemv;
+        if (!std::strcmp(f, "tcgen05") && tma_ok) return MatmulKernel::kTcgen05;
+    }
+    if (M <= 8) return MatmulKernel::kGemv;
+    return tma_ok ? MatmulKernel::kTcgen05 : MatmulKernel::kSimt;
+}
+
+const char *matmul_kernel_name(MatmulKernel k) {
+    switch (k) {
+    case MatmulKernel::kTcgen05: return "tcgen05";
+    case MatmulKernel::kGemv: return "gemv";
+    default: return "simt";
+    }
+}
+
+cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_i8_tcgen05_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kSmemBytes));
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    if (!p.tmap_b) return cudaErrorInvalidValue;
+    CUtensorMap tmap_a;
+    if (!encode_tmap_kmajor_i8(&tmap_a, p.A, p.K, p.M, p.lda, kBK, kBM))
+        return cudaErrorInvalidValue;
+    TcParams tp;
+    tp.scale_a = p.scale_a;
+    tp.scale_b = p.scale_b;
+    tp.bias = p.bias;
+    tp.C = p.C;
+    tp.ldc = p.ldc;
+    tp.M = p.M;
+    tp.N = p.N;
+    tp.K = p.K;
+    tp.tiles_m = (p.M + kBM - 1) / kBM;
+    tp.tiles_n = (p.N + kBN - 1) / kBN;
+    tp.num_kb = (p.K + kBK - 1) / kBK;
+    tp.epilogue = p.epilogue;
+    tp.form = p.form;
+    tp.err = ctx.err;
+    tp.limit_ns = ctx.wait_limit_ns;
+    const uint32_t tiles = tp.tiles_m * tp.tiles_n;
+    const uint32_t grid = tiles < static_cast<uint32_t>(ctx.num_sms) ? tiles
+                                                                     : static_cast<uint32_t>(ctx.num_sms);
+    gemm_i8_tcgen05_kernel<<<grid, kThreads, kSmemBytes, ctx.stream>>>(tmap_a, *p.tmap_b, tp);
+    count_launch(ctx);
+    return cudaGetLastError();
+}
+
+cudaError_t matmul_i8_gemv(const LaunchCtx &ctx, const MatmulI8 &p) {
+    const GvParams g = gv_params(p);
+    const bool aligned = (reinterpret_cast<uintptr_t>(p.A) % 16u == 0u) && (p.lda % 16u == 0u);
+    cudaError_t e;
+    switch (p.M) {
+    case 1: e = launch_gemv_m<1>(ctx, g, aligned); break;
+    case 2: e = launch_gemv_m<2>(ctx, g, aligned); break;
+    case 3: e = launch_gemv_m<3>(ctx, g, aligned); break;
+    case 4: e = launch_gemv_m<4>(ctx, g, aligned); break;
+    default: e = launch_gemv_m<8>(ctx, g, aligned); break;
+    }
+    count_launch(ctx);
+    return e;
+}
+
+cudaError_t matmul_i8_simt(const LaunchCtx &ctx, const MatmulI8 &p) {
+    const GvParams g = gv_params(p);
+    dim3 grid((p.N + 63) / 64, (p.M + 63) / 64);
+    gemm_i8_simt_kernel<<<grid, 256, 0, ctx.stream>>>(g);
+    count_launch(ctx);
+    return cudaGetLastError();
+}
+
+cudaError_t matmul_i8(const LaunchCtx &ctx, const MatmulI8 &p) {
+    switch (choose_matmul_kernel(p.M, p.K, p.N, p.lda, p.A)) {
+    case MatmulKernel::kTcgen05: return matmul_i8_tcgen05(ctx, p);
+    case MatmulKernel::kGemv: return matmul_i8_gemv(ctx, p);
+    default: return matmul_i8_simt(ctx, p);
+    }
+}
+
+}  // namespace vnpu_b200

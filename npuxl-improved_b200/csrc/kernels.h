@@ -1,0 +1,105 @@
+// kernels.h - host-side launch interface of the sm_100a kernels.
+//
+// The runtime (runtime.cpp) validates a command, resolves its pointers to
+// device memory and calls one of these; each enqueues its kernel(s) on
+// ctx.stream and returns the launch status.  Nothing here synchronises.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace vnpu_b200 {
+
+// Error codes written (atomicOr) into the per-stream device error word.
+enum DeviceError : uint32_t {
+    kErrNone = 0,
+    kErrWaitTimeout = 1u << 0,   // an mbarrier / flag wait ran out of time
+    kErrBadConfig = 1u << 1,     // a kernel saw a launch shape it cannot run
+    kErrTmemAlloc = 1u << 2,     // tensor memory allocation returned nonsense
+};
+
+// Dequant epilogue forms (vnpu_b200.h: block / stream / scalar).
+enum EpiForm : uint32_t { kFormBlock = 0, kFormStream = 1, kFormScalar = 2 };
+
+struct LaunchCtx {
+    cudaStream_t stream = nullptr;
+    uint32_t *err = nullptr;        // per-stream device error word
+    int num_sms = 148;
+    uint64_t wait_limit_ns = 2000000000ull;  // bound of every device-side wait
+    uint64_t *launch_counter = nullptr;      // host counter, +1 per kernel launch
+};
+
+// ---- QUANTIZE_I8 (src/kernels/llm.cpp:387-436) ------------------------------
+cudaError_t quantize_rows(const LaunchCtx &ctx, const float *X, int8_t *Y, float *scales,
+                          uint64_t rows, uint64_t cols);
+cudaError_t quantize_columns(const LaunchCtx &ctx, const float *X, int8_t *Y, float *scales,
+                             uint64_t rows, uint64_t cols);
+// Per tensor needs a device scratch word for the running absmax (4 bytes).
+cudaError_t quantize_tensor(const LaunchCtx &ctx, const float *X, int8_t *Y, float *scales,
+                            uint64_t rows, uint64_t cols, uint32_t *absmax_scratch);
+
+// ---- PACK_WEIGHTS_I8 (src/core/scheduler.cpp:763-836) -------------------------
+// B (K x N, or N x K when trans_b) with row stride ldb -> Bt[N][k_stride]
+// (K-major, zero padded to k_stride) and column_sums[N].
+cudaError_t pack_weights(const LaunchCtx &ctx, const int8_t *B, uint32_t K, uint32_t N,
+                         uint32_t ldb, uint32_t trans_b, int8_t *Bt, uint32_t k_stride,
+                         int32_t *column_sums);
+
+// ---- MATMUL_I8 ----------------------------------------------------------------
+struct MatmulI8 {
+    const int8_t *A = nullptr;      // M x K, row stride lda (bytes)
+    uint32_t lda = 0;
+    const int8_t *Bt = nullptr;     // N x k_stride, K-major packed weights
+    uint32_t k_stride = 0;
+    const float *scale_a = nullptr; // M or NULL (1.0)
+    const float *scale_b = nullptr; // N (device copy in the packed handle)
+    const float *bias = nullptr;    // N or NULL
+    float *C = nullptr;             // M x N, row stride ldc (floats)
+    uint32_t ldc = 0;
+    uint32_t M = 0, K = 0, N = 0;
+    uint32_t epilogue = 0;
+    uint32_t form = 0;              // EpiForm
+    const CUtensorMap *tmap_b = nullptr;  // TMA map of Bt (box 128 x 256, SW128)
+};
+
+enum class MatmulKernel { kTcgen05, kGemv, kSimt };
+
+// Which kernel a shape goes to (pure function of the arguments).
+MatmulKernel choose_matmul_kernel(uint32_t M, uint32_t K, uint32_t N, uint32_t lda,
+                                  const void *A);
+const char *matmul_kernel_name(MatmulKernel k);
+
+cudaError_t matmul_i8(const LaunchCtx &ctx, const MatmulI8 &p);
+// Individual kernels (tests pin each against the oracle).
+cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p);
+cudaError_t matmul_i8_gemv(const LaunchCtx &ctx, const MatmulI8 &p);
+cudaError_t matmul_i8_simt(const LaunchCtx &ctx, const MatmulI8 &p);
+
+// TMA tensor maps (driver entry point resolved once through the runtime).
+bool encode_tmap_kmajor_i8(CUtensorMap *map, const void *base, uint64_t k_extent,
+                           uint64_t rows, uint64_t row_stride_bytes, uint32_t box_k,
+                           uint32_t box_rows);
+
+// ---- decoder-block ops (src/kernels/llm.cpp) -----------------------------------
+cudaError_t rmsnorm(const LaunchCtx &ctx, const float *X, const float *W, float *Y,
+                    uint32_t rows, uint32_t cols, float eps);
+// inv_freq: host-computed 1/theta^(2j/dim) (or j/dim interleaved), head_dim/2 entries.
+cudaError_t rope(const LaunchCtx &ctx, float *Q, float *K, const int32_t *positions,
+                 uint32_t batch, uint32_t heads, uint32_t q_seq, uint32_t k_seq,
+                 uint32_t head_dim, uint32_t position_offset, uint32_t interleaved,
+                 float scaling, const float *inv_freq_host);
+cudaError_t swiglu(const LaunchCtx &ctx, const float *gate, const float *up, float *Y,
+                   uint64_t count, float alpha);
+cudaError_t add(const LaunchCtx &ctx, const float *A, const float *B, float *Y, uint64_t count,
+                float alpha, float beta);
+cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, const float *V,
+                      const float *mask, float *O, uint32_t batch, uint32_t heads,
+                      uint32_t seq_q, uint32_t seq_k, uint32_t head_dim, uint32_t causal,
+                      float scale);
+
+// ---- device-wait self test -------------------------------------------------------
+cudaError_t wait_timeout_probe(const LaunchCtx &ctx, const uint32_t *flag, uint64_t limit_ns);
+
+}  // namespace vnpu_b200

@@ -1,0 +1,481 @@
+"""ctypes binding of the vnpu v1 C ABI.
+
+The same binding drives both libraries that export this ABI:
+
+* ``libvnpu.so`` built from ``csrc/`` - the B200 backend (device memory,
+  CUDA streams, sm_100a kernels);
+* the reference library built from its own sources into ``oracle/_ref`` -
+  used only by tests and by ``bench.py``'s reference arm.
+
+The struct layouts follow the reference header ``include/vnpu.h:186-468``
+field for field; ``include/vnpu.h`` in this repository is the C statement of
+the same ABI.  Pointer arguments are plain integers: a numpy array's
+``ctypes.data`` (host memory) or a device address (``torch.Tensor.data_ptr()``).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from typing import Optional
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libvnpu.so")
+
+# Status codes (include/vnpu.h:103-118)
+OK = 0
+ERR_INVALID_ARGUMENT = -1
+ERR_OUT_OF_MEMORY = -2
+ERR_UNSUPPORTED = -3
+ERR_INVALID_COMMAND = -4
+ERR_DEVICE_BUSY = -5
+ERR_DEVICE_ERROR = -6
+ERR_TIMEOUT = -7
+ERR_INTERNAL = -100
+
+# Opcodes (include/vnpu.h:165-184)
+OP_NOP, OP_MATMUL_F32, OP_MATMUL_I8, OP_RMSNORM_F32, OP_SOFTMAX_F32 = 0, 1, 2, 3, 4
+OP_ROPE_F32, OP_SWIGLU_F32, OP_GELU_F32, OP_ADD_F32, OP_MUL_F32 = 5, 6, 7, 8, 9
+OP_ATTENTION_F32, OP_QUANTIZE_I8, OP_PACK_WEIGHTS_I8, OP_MTP_HEAD_F32 = 10, 11, 12, 13
+OP_COPY, OP_MEMSET, OP_BARRIER = 14, 15, 16
+
+UNIT_AUTO, UNIT_VOODOO, UNIT_WILDCAT, UNIT_CELL, UNIT_GPU = 0, 1, 2, 3, 16
+EPI_NONE, EPI_RELU, EPI_SILU, EPI_GELU_TANH, EPI_GELU_ERF = 0, 1, 2, 3, 4
+QUANT_PER_ROW, QUANT_PER_COLUMN, QUANT_PER_TENSOR = 0, 1, 2
+COPY_H2H, COPY_H2D, COPY_D2H, COPY_D2D = 0, 1, 2, 3
+
+FEATURE_GPU_FUTURE = 1 << 31
+
+# B200 extensions (include/vnpu_b200.h)
+CMD_FLAG_EPI_STREAM = 1 << 8
+CMD_FLAG_EPI_SCALAR = 1 << 9
+# oracle form index (oracle/oracle.h) -> command flags of the B200 library
+FORM_FLAGS = {0: 0, 1: CMD_FLAG_EPI_SCALAR, 2: CMD_FLAG_EPI_STREAM}
+
+vp = C.c_void_p
+u32 = C.c_uint32
+u64 = C.c_uint64
+f32 = C.c_float
+
+
+class Config(C.Structure):
+    _fields_ = [("abi_version", u32), ("num_threads", u32), ("num_compute_units", u32),
+                ("tile_m", u32), ("tile_k", u32), ("tile_n", u32), ("flags", u32),
+                ("reserved0", u32), ("trace_file", C.c_char_p), ("node_name", C.c_char_p)]
+
+
+class DeviceInfo(C.Structure):
+    _fields_ = [("abi_version", u32), ("name", C.c_char * 64), ("vendor", C.c_char * 64),
+                ("cpu_arch", C.c_char * 32), ("backend", C.c_char * 64), ("simd_bits", u32),
+                ("num_threads", u32), ("num_compute_units", u32), ("local_store_bytes", u32),
+                ("tile_m", u32), ("tile_k", u32), ("tile_n", u32), ("physical_cores", u32),
+                ("features", u64), ("l1d_bytes", u64), ("l2_bytes", u64), ("l3_bytes", u64),
+                ("total_memory_bytes", u64)]
+
+
+class DeviceStatus(C.Structure):
+    _fields_ = [(n, u64) for n in ("commands_submitted", "commands_completed", "kernel_time_ns",
+                                   "dispatch_time_ns", "memory_time_ns", "sync_time_ns",
+                                   "bytes_read", "bytes_written", "flops", "tiles_dispatched",
+                                   "tiles_culled", "dma_bytes", "interrupts")] + \
+              [("busy", u32), ("error", u32), ("last_opcode", u32), ("active_workers", u32),
+               ("reserved", u64 * 4)]
+
+
+class TraceSummary(C.Structure):
+    _fields_ = [(n, u64) for n in ("events", "total_time_ns", "dispatch_time_ns", "memory_time_ns",
+                                   "compute_time_ns", "sync_time_ns", "bytes_read",
+                                   "bytes_written", "flops")] + \
+              [("achieved_gflops", C.c_double), ("achieved_gbytes_s", C.c_double),
+               ("hot_opcode", u32), ("hot_time_ns", u64), ("trace_overhead_ns", C.c_double)]
+
+
+class MatmulF32Args(C.Structure):
+    _fields_ = [("A", vp), ("B", vp), ("bias", vp), ("C", vp), ("M", u32), ("K", u32), ("N", u32),
+                ("lda", u32), ("ldb", u32), ("ldc", u32), ("trans_a", u32), ("trans_b", u32),
+                ("alpha", f32), ("beta", f32), ("epilogue", u32), ("unit", u32),
+                ("reserved0", u32), ("tile_mask", vp), ("mask_tile_m", u32), ("mask_tile_n", u32)]
+
+
+class MatmulI8Args(C.Structure):
+    _fields_ = [("A", vp), ("B", vp), ("scale_a", vp), ("bias", vp), ("C", vp),
+                ("M", u32), ("K", u32), ("N", u32), ("lda", u32), ("ldc", u32),
+                ("epilogue", u32), ("unit", u32)]
+
+
+class RmsnormArgs(C.Structure):
+    _fields_ = [("X", vp), ("W", vp), ("Y", vp), ("rows", u32), ("cols", u32), ("eps", f32),
+                ("unit", u32)]
+
+
+class SoftmaxArgs(C.Structure):
+    _fields_ = [("X", vp), ("Y", vp), ("rows", u32), ("cols", u32), ("temperature", f32),
+                ("unit", u32)]
+
+
+class RopeArgs(C.Structure):
+    _fields_ = [("Q", vp), ("K", vp), ("positions", vp), ("batch", u32), ("heads", u32),
+                ("q_seq", u32), ("k_seq", u32), ("head_dim", u32), ("position_offset", u32),
+                ("interleaved", u32), ("theta_base", f32), ("scaling", f32)]
+
+
+class BinaryArgs(C.Structure):
+    _fields_ = [("A", vp), ("B", vp), ("Y", vp), ("count", u64), ("alpha", f32), ("beta", f32),
+                ("unit", u32), ("reserved0", u32)]
+
+
+class UnaryArgs(C.Structure):
+    _fields_ = [("X", vp), ("Y", vp), ("count", u64), ("param", f32), ("unit", u32),
+                ("reserved0", u32)]
+
+
+class SwigluArgs(C.Structure):
+    _fields_ = [("gate", vp), ("up", vp), ("Y", vp), ("count", u64), ("alpha", f32),
+                ("unit", u32), ("reserved0", u32)]
+
+
+class AttentionArgs(C.Structure):
+    _fields_ = [("Q", vp), ("K", vp), ("V", vp), ("mask", vp), ("O", vp), ("workspace", vp),
+                ("workspace_bytes", u64), ("batch", u32), ("heads", u32), ("seq_q", u32),
+                ("seq_k", u32), ("head_dim", u32), ("causal", u32), ("scale", f32),
+                ("unit", u32)]
+
+
+class QuantizeI8Args(C.Structure):
+    _fields_ = [("X", vp), ("Y", vp), ("scales", vp), ("rows", u64), ("cols", u64),
+                ("axis", u32), ("unit", u32)]
+
+
+class PackWeightsI8Args(C.Structure):
+    _fields_ = [("B", vp), ("scales", vp), ("out", vp), ("K", u32), ("N", u32), ("ldb", u32),
+                ("trans_b", u32), ("unit", u32), ("reserved0", u32)]
+
+
+class MtpHeadArgs(C.Structure):
+    _fields_ = [("hidden", vp), ("W", vp), ("bias", vp), ("logits", vp), ("gamma", u32),
+                ("hidden_dim", u32), ("vocab", u32), ("trans_w", u32), ("unit", u32),
+                ("reserved0", u32)]
+
+
+class CopyArgs(C.Structure):
+    _fields_ = [("dst", vp), ("src", vp), ("bytes", u64), ("direction", u32), ("reserved0", u32)]
+
+
+class MemsetArgs(C.Structure):
+    _fields_ = [("dst", vp), ("bytes", u64), ("value", u32), ("reserved0", u32)]
+
+
+class CommandArgs(C.Union):
+    _fields_ = [("matmul_f32", MatmulF32Args), ("matmul_i8", MatmulI8Args),
+                ("rmsnorm", RmsnormArgs), ("softmax", SoftmaxArgs), ("rope", RopeArgs),
+                ("binary", BinaryArgs), ("unary", UnaryArgs), ("swiglu", SwigluArgs),
+                ("attention", AttentionArgs), ("quantize_i8", QuantizeI8Args),
+                ("pack_weights_i8", PackWeightsI8Args), ("mtp_head", MtpHeadArgs),
+                ("copy", CopyArgs), ("memset", MemsetArgs), ("raw", C.c_uint8 * 192)]
+
+
+class Command(C.Structure):
+    _fields_ = [("opcode", u32), ("flags", u32), ("id", u64), ("args", CommandArgs)]
+
+
+assert C.sizeof(Command) == 208, C.sizeof(Command)
+
+_ST = C.c_int  # vnpu_status_t
+
+
+def _sig(lib, name, res, *args):
+    fn = getattr(lib, name)
+    fn.restype = res
+    fn.argtypes = list(args)
+    return fn
+
+
+class VnpuError(RuntimeError):
+    def __init__(self, what: str, status: int):
+        super().__init__(f"{what}: status {status}")
+        self.status = status
+
+
+def ptr(x) -> Optional[int]:
+    """Address of a numpy array / torch tensor / int (None stays None)."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if isinstance(x, np.ndarray):
+        return x.ctypes.data
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    raise TypeError(type(x))
+
+
+class Lib:
+    """One loaded vnpu ABI library (the B200 backend or the reference)."""
+
+    def __init__(self, path: str = LIB_PATH):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} is not built (run __graft_entry__.build())")
+        self.path = path
+        self.h = C.CDLL(path)
+        h = self.h
+        self.config_init = _sig(h, "vnpu_config_init", None, C.POINTER(Config))
+        self.status_string = _sig(h, "vnpu_status_string", C.c_char_p, _ST)
+        self.version_string = _sig(h, "vnpu_version_string", C.c_char_p)
+        self.device_create = _sig(h, "vnpu_device_create", _ST, C.POINTER(Config), C.POINTER(vp))
+        self.device_destroy = _sig(h, "vnpu_device_destroy", None, vp)
+        self.device_get_info = _sig(h, "vnpu_device_get_info", _ST, vp, C.POINTER(DeviceInfo))
+        self.device_get_status = _sig(h, "vnpu_device_get_status", _ST, vp, C.POINTER(DeviceStatus))
+        self.stream_create = _sig(h, "vnpu_stream_create", _ST, vp, C.c_int, C.POINTER(vp))
+        self.stream_destroy = _sig(h, "vnpu_stream_destroy", None, vp)
+        self.stream_sync = _sig(h, "vnpu_stream_sync", _ST, vp)
+        self.stream_submit = _sig(h, "vnpu_stream_submit", _ST, vp, C.POINTER(Command), u64, vp)
+        self.event_create = _sig(h, "vnpu_event_create", _ST, C.POINTER(vp))
+        self.event_destroy = _sig(h, "vnpu_event_destroy", None, vp)
+        self.event_wait = _sig(h, "vnpu_event_wait", _ST, vp, u32)
+        self.event_query = _sig(h, "vnpu_event_query", _ST, vp)
+        self.buffer_alloc = _sig(h, "vnpu_buffer_alloc", _ST, vp, u64, C.POINTER(vp))
+        self.buffer_free = _sig(h, "vnpu_buffer_free", None, vp)
+        self.buffer_host_ptr = _sig(h, "vnpu_buffer_host_ptr", vp, vp)
+        self.buffer_size = _sig(h, "vnpu_buffer_size", u64, vp)
+        self.buffer_copy = _sig(h, "vnpu_buffer_copy", _ST, vp, vp, vp, u64, u32)
+        self.buffer_memset = _sig(h, "vnpu_buffer_memset", _ST, vp, vp, u32, u64)
+        self.pack_weights_i8 = _sig(h, "vnpu_pack_weights_i8", _ST, vp, vp, vp, u32, u32, u32,
+                                    u32, C.POINTER(vp))
+        self.packed_weights_destroy = _sig(h, "vnpu_packed_weights_destroy", None, vp)
+        self.packed_weights_info = _sig(h, "vnpu_packed_weights_info", _ST, vp, C.POINTER(u32),
+                                        C.POINTER(u32), C.POINTER(u64), C.POINTER(vp),
+                                        C.POINTER(vp))
+        self.matmul_i8 = _sig(h, "vnpu_matmul_i8", _ST, vp, C.POINTER(MatmulI8Args))
+        self.quantize_i8 = _sig(h, "vnpu_quantize_i8", _ST, vp, C.POINTER(QuantizeI8Args))
+        self.rmsnorm_f32 = _sig(h, "vnpu_rmsnorm_f32", _ST, vp, C.POINTER(RmsnormArgs))
+        self.rope_f32 = _sig(h, "vnpu_rope_f32", _ST, vp, C.POINTER(RopeArgs))
+        self.swiglu_f32 = _sig(h, "vnpu_swiglu_f32", _ST, vp, C.POINTER(SwigluArgs))
+        self.add_f32 = _sig(h, "vnpu_add_f32", _ST, vp, C.POINTER(BinaryArgs))
+        self.attention_f32 = _sig(h, "vnpu_attention_f32", _ST, vp, C.POINTER(AttentionArgs))
+        self.get_backend_v1 = _sig(h, "vnpu_get_backend_v1", vp)
+        self.is_b200 = hasattr(h, "vnpu_b200_stream_handle")
+        if self.is_b200:
+            self.b200_stream_handle = _sig(h, "vnpu_b200_stream_handle", vp, vp)
+            self.b200_kernel_launches = _sig(h, "vnpu_b200_kernel_launches", u64, vp)
+            self.b200_matmul_kernel = _sig(h, "vnpu_b200_matmul_i8_kernel", C.c_char_p, u32, u32,
+                                           u32, u32, vp)
+            self.b200_selftest_wait = _sig(h, "vnpu_b200_selftest_wait_timeout", _ST, vp, u32)
+            self.b200_packed_device = _sig(h, "vnpu_b200_packed_weights_device", _ST, vp,
+                                           C.POINTER(vp), C.POINTER(u32), C.POINTER(vp))
+
+    def check(self, rc: int, what: str):
+        if rc != OK:
+            msg = self.status_string(rc)
+            raise VnpuError(f"{what} failed ({msg.decode() if msg else rc})", rc)
+
+
+class Device:
+    """A vnpu device plus one stream: the unit the tests and the bench drive."""
+
+    def __init__(self, lib: Lib, num_threads: int = 0, ordinal: int = 0):
+        self.lib = lib
+        cfg = Config()
+        lib.config_init(C.byref(cfg))
+        if num_threads:
+            cfg.num_threads = num_threads
+        cfg.reserved0 = ordinal
+        dev = vp()
+        lib.check(lib.device_create(C.byref(cfg), C.byref(dev)), "device_create")
+        self.dev = dev
+        st = vp()
+        lib.check(lib.stream_create(dev, 0, C.byref(st)), "stream_create")
+        self.stream = st
+
+    def close(self):
+        if self.dev:
+            self.lib.device_destroy(self.dev)
+            self.dev = None
+            self.stream = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def info(self) -> DeviceInfo:
+        inf = DeviceInfo()
+        self.lib.check(self.lib.device_get_info(self.dev, C.byref(inf)), "device_get_info")
+        return inf
+
+    def status(self) -> DeviceStatus:
+        s = DeviceStatus()
+        self.lib.check(self.lib.device_get_status(self.dev, C.byref(s)), "device_get_status")
+        return s
+
+    def sync(self) -> int:
+        return self.lib.stream_sync(self.stream)
+
+    # -- packed weights ------------------------------------------------------
+    def pack(self, B, scales, K: int, N: int, ldb: int = 0, trans_b: int = 0) -> int:
+        w = vp()
+        self.lib.check(self.lib.pack_weights_i8(self.dev, ptr(B), ptr(scales), K, N, ldb, trans_b,
+                                                C.byref(w)), "pack_weights_i8")
+        return w.value
+
+    def packed_info(self, w: int):
+        K, N, nbytes = u32(), u32(), u64()
+        sc, cs = vp(), vp()
+        self.lib.check(self.lib.packed_weights_info(w, C.byref(K), C.byref(N), C.byref(nbytes),
+                                                    C.byref(sc), C.byref(cs)),
+                       "packed_weights_info")
+        return K.value, N.value, nbytes.value, sc.value, cs.value
+
+    def unpack(self, w: int):
+        self.lib.packed_weights_destroy(w)
+
+    # -- synchronous ops -----------------------------------------------------
+    def matmul_i8(self, A, w, scale_a, bias, Cout, M, K, N, lda=0, ldc=0, epilogue=0,
+                  unit=UNIT_AUTO, flags=0, check=True) -> int:
+        a = MatmulI8Args(ptr(A), w, ptr(scale_a), ptr(bias), ptr(Cout), M, K, N, lda, ldc,
+                         epilogue, unit)
+        if flags:
+            cmd = Command()
+            cmd.opcode = OP_MATMUL_I8
+            cmd.flags = flags
+            cmd.args.matmul_i8 = a
+            rc = self.lib.stream_submit(self.stream, C.byref(cmd), 1, None)
+            if rc == OK:
+                rc = self.lib.stream_sync(self.stream)
+        else:
+            rc = self.lib.matmul_i8(self.stream, C.byref(a))
+        if check:
+            self.lib.check(rc, "matmul_i8")
+        return rc
+
+    def quantize_i8(self, X, Y, scales, rows, cols, axis=QUANT_PER_ROW, check=True) -> int:
+        a = QuantizeI8Args(ptr(X), ptr(Y), ptr(scales), rows, cols, axis, 0)
+        rc = self.lib.quantize_i8(self.stream, C.byref(a))
+        if check:
+            self.lib.check(rc, "quantize_i8")
+        return rc
+
+    def rmsnorm(self, X, W, Y, rows, cols, eps) -> None:
+        a = RmsnormArgs(ptr(X), ptr(W), ptr(Y), rows, cols, eps, 0)
+        self.lib.check(self.lib.rmsnorm_f32(self.stream, C.byref(a)), "rmsnorm_f32")
+
+    def rope(self, Q, K, positions, batch, heads, q_seq, k_seq, head_dim, position_offset=0,
+             interleaved=0, theta=10000.0, scaling=1.0) -> None:
+        a = RopeArgs(ptr(Q), ptr(K), ptr(positions), batch, heads, q_seq, k_seq, head_dim,
+                     position_offset, interleaved, theta, scaling)
+        self.lib.check(self.lib.rope_f32(self.stream, C.byref(a)), "rope_f32")
+
+    def swiglu(self, g, u, Y, count, alpha=1.0) -> None:
+        a = SwigluArgs(ptr(g), ptr(u), ptr(Y), count, alpha, 0, 0)
+        self.lib.check(self.lib.swiglu_f32(self.stream, C.byref(a)), "swiglu_f32")
+
+    def add(self, A, B, Y, count, alpha=1.0, beta=1.0) -> None:
+        a = BinaryArgs(ptr(A), ptr(B), ptr(Y), count, alpha, beta, 0, 0)
+        self.lib.check(self.lib.add_f32(self.stream, C.byref(a)), "add_f32")
+
+    def attention(self, Q, K, V, mask, O, batch, heads, seq_q, seq_k, head_dim, causal=1,
+                  scale=0.0) -> None:
+        a = AttentionArgs(ptr(Q), ptr(K), ptr(V), ptr(mask), ptr(O), None, 0, batch, heads, seq_q,
+                          seq_k, head_dim, causal, scale, 0)
+        self.lib.check(self.lib.attention_f32(self.stream, C.byref(a)), "attention_f32")
+
+    def submit(self, cmds, event=None) -> int:
+        arr = (Command * len(cmds))(*cmds)
+        return self.lib.stream_submit(self.stream, arr, len(cmds), event)
+
+
+# ---------------------------------------------------------------------------
+# The C restatement oracle (oracle/liboracle.so) - test infrastructure only.
+# ---------------------------------------------------------------------------
+
+class Oracle:
+    FORM_AVX2 = 0
+    FORM_SCALAR = 1
+
+    def __init__(self, path: str):
+        self.h = C.CDLL(path)
+        h = self.h
+        i8p = C.c_void_p
+        self._matmul = _sig(h, "oracle_matmul_i8", None, i8p, u32, i8p, vp, vp, vp, vp, u32, u32,
+                            u32, u32, u32, C.c_int)
+        self._acc = _sig(h, "oracle_gemm_i8_acc", None, i8p, u32, i8p, u32, vp, u32, u32, u32)
+        self._quant = _sig(h, "oracle_quantize_i8", C.c_int, vp, vp, vp, u64, u64, u32)
+        self._colsums = _sig(h, "oracle_column_sums", None, vp, u32, u32, u32, u32, vp, vp)
+        self._rms = _sig(h, "oracle_rmsnorm", None, vp, vp, vp, u32, u32, f32, C.c_int)
+        self._rope = _sig(h, "oracle_rope", None, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32,
+                          f32, f32)
+        self._swiglu = _sig(h, "oracle_swiglu", None, vp, vp, vp, u64, f32, C.c_int)
+        self._add = _sig(h, "oracle_add", None, vp, vp, vp, u64, f32, f32, C.c_int)
+        self._attn = _sig(h, "oracle_attention", None, vp, vp, vp, vp, vp, u32, u32, u32, u32,
+                          u32, u32, f32)
+        self.fast_expf = _sig(h, "oracle_fast_expf", f32, f32, C.c_int)
+        self.dequant = _sig(h, "oracle_dequant", f32, C.c_int32, f32, f32, C.POINTER(f32), u32,
+                            C.c_int)
+
+    def quantize(self, X: np.ndarray, axis: int = QUANT_PER_ROW):
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        rows, cols = X.shape
+        Y = np.empty((rows, cols), np.int8)
+        n = rows if axis == QUANT_PER_ROW else (cols if axis == QUANT_PER_COLUMN else 1)
+        s = np.empty(n, np.float32)
+        rc = self._quant(ptr(X), ptr(Y), ptr(s), rows, cols, axis)
+        assert rc == 0
+        return Y, s
+
+    def gemm_acc(self, A: np.ndarray, B: np.ndarray) -> np.ndarray:
+        A = np.ascontiguousarray(A, np.int8)
+        B = np.ascontiguousarray(B, np.int8)
+        M, K = A.shape
+        N = B.shape[1]
+        acc = np.empty((M, N), np.int32)
+        self._acc(ptr(A), K, ptr(B), N, ptr(acc), M, K, N)
+        return acc
+
+    def matmul_i8(self, A, B, scale_a, scale_b, bias=None, epilogue=0, form=0) -> np.ndarray:
+        A = np.ascontiguousarray(A, np.int8)
+        B = np.ascontiguousarray(B, np.int8)
+        M, K = A.shape
+        N = B.shape[1]
+        Cm = np.empty((M, N), np.float32)
+        self._matmul(ptr(A), K, ptr(B), ptr(scale_a), ptr(scale_b), ptr(bias), ptr(Cm), N, M, K,
+                     N, epilogue, form)
+        return Cm
+
+    def column_sums(self, B: np.ndarray, trans_b: int = 0):
+        B = np.ascontiguousarray(B, np.int8)
+        K, N = (B.shape[1], B.shape[0]) if trans_b else B.shape
+        sums = np.empty(N, np.int32)
+        canon = np.empty((K, N), np.int8)
+        self._colsums(ptr(B), K, N, 0, trans_b, ptr(sums), ptr(canon))
+        return sums, canon
+
+    def rmsnorm(self, X, W, eps, form=0):
+        X = np.ascontiguousarray(X, np.float32)
+        Y = np.empty_like(X)
+        self._rms(ptr(X), ptr(W), ptr(Y), X.shape[0], X.shape[1], eps, form)
+        return Y
+
+    def rope(self, Q, K, positions, batch, heads, q_seq, k_seq, head_dim, position_offset=0,
+             interleaved=0, theta=10000.0, scaling=1.0):
+        Q = None if Q is None else np.array(Q, np.float32, copy=True)
+        K = None if K is None else np.array(K, np.float32, copy=True)
+        self._rope(ptr(Q), ptr(K), ptr(positions), batch, heads, q_seq, k_seq, head_dim,
+                   position_offset, interleaved, theta, scaling)
+        return Q, K
+
+    def swiglu(self, g, u, alpha=1.0, form=0):
+        Y = np.empty_like(g)
+        self._swiglu(ptr(g), ptr(u), ptr(Y), g.size, alpha, form)
+        return Y
+
+    def add(self, A, B, alpha=1.0, beta=1.0, form=0):
+        Y = np.empty_like(A)
+        self._add(ptr(A), ptr(B), ptr(Y), A.size, alpha, beta, form)
+        return Y
+
+    def attention(self, Q, K, V, mask, batch, heads, seq_q, seq_k, head_dim, causal=1, scale=0.0):
+        O = np.empty((batch, heads, seq_q, head_dim), np.float32)
+        self._attn(ptr(Q), ptr(K), ptr(V), ptr(mask), ptr(O), batch, heads, seq_q, seq_k,
+                   head_dim, causal, scale)
+        return O

@@ -1,0 +1,445 @@
+/*
+ * oracle.c - CPU restatement of the reference's int8 GEMM path and decoder
+ * block ops.  TEST INFRASTRUCTURE ONLY (see oracle.h): the B200 library never
+ * links or calls this file.
+ *
+ * Built with -ffp-contract=off: every fused multiply-add is an explicit
+ * fmaf() that mirrors a fusion GCC performs in the reference's
+ * target("avx2,fma") kernels (the reference builds with -ffp-contract=fast,
+ * Makefile CXXFLAGS).  Those fusions were confirmed bit-for-bit against the
+ * reference library compiled from source (tests/test_oracle.py).
+ */
+#include "oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------------- */
+/* Epilogue math (src/internal.h:87-136)                                      */
+/* ------------------------------------------------------------------------- */
+
+static const float kLog2e = 1.4426950408889634f;
+static const float kC1 = 0.6931471805599453f;
+static const float kC2 = 0.2402265069591007f;
+static const float kC3 = 0.05550410866482158f;
+static const float kC4 = 0.009618129107628477f;
+static const float kC5 = 0.0013333558146428443f;
+
+/* 2^f for f in [0,1): the reference's degree-5 polynomial.  In the AVX2
+ * kernels every "c + f*(...)" step of the Horner chain becomes one FMA. */
+static float exp2_poly(float f, int form)
+{
+    if (form != ORACLE_FORM_SCALAR) {
+        float p = fmaf(f, kC5, kC4);
+        p = fmaf(f, p, kC3);
+        p = fmaf(f, p, kC2);
+        p = fmaf(f, p, kC1);
+        return fmaf(f, p, 1.0f);
+    }
+    return 1.0f + f * (kC1 + f * (kC2 + f * (kC3 + f * (kC4 + f * kC5))));
+}
+
+/* fast_expf, src/internal.h:87-108. */
+float oracle_fast_expf(float x, int form)
+{
+    if (x < -80.0f) return 0.0f;
+    if (x > 80.0f) return INFINITY;
+    float z = x * kLog2e;
+    float zi = floorf(z);
+    float f = z - zi;
+    return ldexpf(exp2_poly(f, form), (int)zi);
+}
+
+/* exp256_ps, src/kernels/llm.cpp:32-56: clamps to [-80,80] instead of the
+ * scalar cut-offs, FMA Horner, 2^n from exponent bits (exact for the clamped
+ * range, n in [-116,116]). */
+static float exp256_lane(float x)
+{
+    if (x < -80.0f) x = -80.0f;
+    if (x > 80.0f) x = 80.0f;
+    float z = x * kLog2e;
+    float zi = floorf(z);
+    float f = z - zi;
+    return ldexpf(exp2_poly(f, ORACLE_FORM_AVX2), (int)zi);
+}
+
+static float silu_f(float x, int form)
+{
+    return x / (1.0f + oracle_fast_expf(-x, form));
+}
+
+/* gelu_tanh, src/internal.h:113-120.  In the AVX2 kernels x + k1*x3 fuses. */
+static float gelu_tanh_f(float x, int form)
+{
+    const float k0 = 0.7978845608028654f;
+    const float k1 = 0.035677408136300125f;
+    float x3 = x * x * x;
+    float inner = form != ORACLE_FORM_SCALAR ? k0 * fmaf(k1, x3, x)
+                                             : k0 * (x + k1 * x3);
+    float t = 2.0f / (1.0f + oracle_fast_expf(-2.0f * inner, form)) - 1.0f;
+    return 0.5f * x * (1.0f + t);
+}
+
+float oracle_epilogue(float v, uint32_t epilogue, int form)
+{
+    switch (epilogue) {
+    case 1: return v > 0.0f ? v : 0.0f;              /* RELU */
+    case 2: return silu_f(v, form);                  /* SILU */
+    case 3:                                          /* GELU_TANH */
+    case 4: return gelu_tanh_f(v, form);             /* GELU_ERF aliases tanh */
+    default: return v;
+    }
+}
+
+/* ------------------------------------------------------------------------- */
+/* MATMUL_I8 (src/kernels/kernels.cpp:526-550)                                */
+/* ------------------------------------------------------------------------- */
+
+void oracle_gemm_i8_acc(const int8_t *A, uint32_t lda, const int8_t *B,
+                        uint32_t ldb, int32_t *acc, uint32_t M, uint32_t K,
+                        uint32_t N)
+{
+    /* int32 accumulation over all of K is exact and order-free, so a rank-1
+     * update order (vectorisable) gives the same integers as the reference's
+     * dot-product order. */
+    for (uint32_t m = 0; m < M; ++m) {
+        int32_t *row = acc + (size_t)m * N;
+        memset(row, 0, sizeof(int32_t) * N);
+        const int8_t *a = A + (size_t)m * lda;
+        for (uint32_t k = 0; k < K; ++k) {
+            const int32_t av = a[k];
+            if (!av) continue;
+            const int8_t *b = B + (size_t)k * ldb;
+            for (uint32_t n = 0; n < N; ++n) row[n] += av * (int32_t)b[n];
+        }
+    }
+}
+
+/* store_i8_c, src/kernels/kernels.cpp:526-535.
+ *   out = (float)dot * sa * sb      (left to right, IEEE)
+ *   out += bias                     (AVX2 register-block kernels: fused,
+ *                                    fmaf(t, sb, bias); decode streams and
+ *                                    scalar: two roundings)
+ *   out = apply_epilogue(out)       (polynomial fused except in scalar) */
+float oracle_dequant(int32_t acc, float sa, float sb, const float *bias_n,
+                     uint32_t epilogue, int form)
+{
+    float t = (float)acc * sa;
+    float out;
+    if (bias_n)
+        out = form == ORACLE_FORM_AVX2 ? fmaf(t, sb, *bias_n) : t * sb + *bias_n;
+    else
+        out = t * sb;
+    return oracle_epilogue(out, epilogue, form);
+}
+
+void oracle_matmul_i8(const int8_t *A, uint32_t lda, const int8_t *B,
+                      const float *scale_a, const float *scale_b,
+                      const float *bias, float *C, uint32_t ldc, uint32_t M,
+                      uint32_t K, uint32_t N, uint32_t epilogue, int form)
+{
+    int32_t *row = (int32_t *)malloc(sizeof(int32_t) * (N ? N : 1));
+    if (!row) return;
+    for (uint32_t m = 0; m < M; ++m) {
+        oracle_gemm_i8_acc(A + (size_t)m * lda, lda, B, N, row, 1, K, N);
+        const float sa = scale_a ? scale_a[m] : 1.0f;
+        for (uint32_t n = 0; n < N; ++n) {
+            const float sb = scale_b ? scale_b[n] : 1.0f;
+            C[(size_t)m * ldc + n] = oracle_dequant(row[n], sa, sb,
+                                                    bias ? bias + n : NULL,
+                                                    epilogue, form);
+        }
+    }
+    free(row);
+}
+
+/* ------------------------------------------------------------------------- */
+/* QUANTIZE_I8 (src/kernels/llm.cpp:387-436)                                  */
+/* ------------------------------------------------------------------------- */
+
+/* quantize_value, src/kernels/llm.cpp:387-393: std::round is half away from
+ * zero (roundf), clamp to [-128, 127]. */
+static int8_t quantize_value(float x, float inv)
+{
+    float q = roundf(x * inv);
+    if (q > 127.0f) q = 127.0f;
+    if (q < -128.0f) q = -128.0f;
+    return (int8_t)(int)q;
+}
+
+/* scale = maxabs/127 with the reference's guard (llm.cpp:403-404).  NaN
+ * elements never win std::max(maxabs, |x|), so they are skipped. */
+static float scale_of(float maxabs)
+{
+    float scale = maxabs / 127.0f;
+    if (scale <= 0.0f || !isfinite(scale)) scale = 1.0f;
+    return scale;
+}
+
+static float absmax_step(float m, float x)
+{
+    float a = fabsf(x);
+    return m < a ? a : m;   /* std::max(m, a) */
+}
+
+int oracle_quantize_i8(const float *X, int8_t *Y, float *scales, uint64_t rows,
+                       uint64_t cols, uint32_t axis)
+{
+    if (!X || !Y || !scales || !rows || !cols || axis > 2) return -1;
+    if (axis == 0) {
+        for (uint64_t r = 0; r < rows; ++r) {
+            const float *x = X + r * cols;
+            float m = 0.0f;
+            for (uint64_t j = 0; j < cols; ++j) m = absmax_step(m, x[j]);
+            float scale = scale_of(m);
+            float inv = 1.0f / scale;
+            scales[r] = scale;
+            for (uint64_t j = 0; j < cols; ++j) Y[r * cols + j] = quantize_value(x[j], inv);
+        }
+    } else if (axis == 1) {
+        float *m = (float *)calloc(cols, sizeof(float));
+        if (!m) return -2;
+        for (uint64_t r = 0; r < rows; ++r)
+            for (uint64_t c = 0; c < cols; ++c) m[c] = absmax_step(m[c], X[r * cols + c]);
+        for (uint64_t c = 0; c < cols; ++c) scales[c] = scale_of(m[c]);
+        for (uint64_t r = 0; r < rows; ++r)
+            for (uint64_t c = 0; c < cols; ++c)
+                Y[r * cols + c] = quantize_value(X[r * cols + c], 1.0f / scales[c]);
+        free(m);
+    } else {
+        /* Per tensor (src/core/scheduler.cpp:441-460, llm.cpp:430-436):
+         * scales[0] = maxabs/127, then inv = 1/(scales[0] > 0 ? scales[0] : 1). */
+        uint64_t n = rows * cols;
+        float m = 0.0f;
+        for (uint64_t i = 0; i < n; ++i) m = absmax_step(m, X[i]);
+        scales[0] = scale_of(m);
+        float inv = 1.0f / (scales[0] > 0.0f ? scales[0] : 1.0f);
+        for (uint64_t i = 0; i < n; ++i) Y[i] = quantize_value(X[i], inv);
+    }
+    return 0;
+}
+
+/* vnpu_pack_weights_i8, src/core/scheduler.cpp:783-805: canonical KxN copy
+ * and int32 column sums. */
+void oracle_column_sums(const int8_t *B, uint32_t K, uint32_t N, uint32_t ldb,
+                        uint32_t trans_b, int32_t *sums, int8_t *canonical)
+{
+    uint32_t ld = ldb ? ldb : (trans_b ? K : N);
+    for (uint32_t n = 0; n < N; ++n) sums[n] = 0;
+    for (uint32_t k = 0; k < K; ++k)
+        for (uint32_t n = 0; n < N; ++n) {
+            int8_t v = trans_b ? B[(size_t)n * ld + k] : B[(size_t)k * ld + n];
+            if (canonical) canonical[(size_t)k * N + n] = v;
+            sums[n] += v;
+        }
+}
+
+/* ------------------------------------------------------------------------- */
+/* Block ops (src/kernels/llm.cpp)                                            */
+/* ------------------------------------------------------------------------- */
+
+/* hsum256, src/kernels/llm.cpp:19-28: (lo+hi), then two horizontal adds. */
+static float hsum8(const float v[8])
+{
+    float s0 = v[0] + v[4], s1 = v[1] + v[5], s2 = v[2] + v[6], s3 = v[3] + v[7];
+    return (s0 + s1) + (s2 + s3);
+}
+
+/* dot_avx2, src/kernels/llm.cpp:332-343. */
+static float dot_avx2(const float *a, const float *b, uint32_t n)
+{
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    uint32_t i = 0;
+    for (; i + 8 <= n; i += 8)
+        for (int l = 0; l < 8; ++l) acc[l] = fmaf(a[i + l], b[i + l], acc[l]);
+    float sum = hsum8(acc);
+    for (; i < n; ++i) sum = fmaf(a[i], b[i], sum);
+    return sum;
+}
+
+/* RMSNorm: scalar src/kernels/llm.cpp:64-77; AVX2 :80-106. */
+void oracle_rmsnorm(const float *X, const float *W, float *Y, uint32_t rows,
+                    uint32_t cols, float eps, int form)
+{
+    float e = eps > 0.0f ? eps : 1e-5f;
+    for (uint32_t r = 0; r < rows; ++r) {
+        const float *x = X + (size_t)r * cols;
+        float *y = Y + (size_t)r * cols;
+        float ss;
+        if (form == ORACLE_FORM_AVX2) {
+            ss = dot_avx2(x, x, cols);
+        } else {
+            ss = 0.0f;
+            for (uint32_t j = 0; j < cols; ++j) ss += x[j] * x[j];
+        }
+        float inv = 1.0f / sqrtf(ss / (float)cols + e);
+        uint32_t vec_end = form == ORACLE_FORM_AVX2 ? (cols / 8u) * 8u : 0u;
+        for (uint32_t j = 0; j < cols; ++j) {
+            float w = W ? W[j] : 1.0f;
+            y[j] = j < vec_end ? (x[j] * w) * inv : x[j] * inv * w;
+        }
+    }
+}
+
+/* rotate_vector, src/kernels/llm.cpp:188-217. */
+static void rotate_vector(float *x, uint32_t dim, float position,
+                          float theta_base, float scaling, int interleaved)
+{
+    if (!x || dim < 2) return;
+    position *= scaling;
+    if (interleaved) {
+        for (uint32_t j = 0; j + 1 < dim; j += 2) {
+            float inv = 1.0f / powf(theta_base, (float)j / (float)dim);
+            float angle = position * inv;
+            float c = cosf(angle), s = sinf(angle);
+            float x0 = x[j], x1 = x[j + 1];
+            x[j] = x0 * c - x1 * s;
+            x[j + 1] = x0 * s + x1 * c;
+        }
+    } else {
+        uint32_t half = dim / 2;
+        for (uint32_t j = 0; j < half; ++j) {
+            float inv = 1.0f / powf(theta_base, 2.0f * (float)j / (float)dim);
+            float angle = position * inv;
+            float c = cosf(angle), s = sinf(angle);
+            float x0 = x[j], x1 = x[j + half];
+            x[j] = x0 * c - x1 * s;
+            x[j + half] = x0 * s + x1 * c;
+        }
+    }
+}
+
+/* kernel_rope_tokens, src/kernels/llm.cpp:576-602. */
+void oracle_rope(float *Q, float *K, const int32_t *positions, uint32_t batch,
+                 uint32_t heads, uint32_t q_seq, uint32_t k_seq,
+                 uint32_t head_dim, uint32_t position_offset,
+                 uint32_t interleaved, float theta_base, float scaling)
+{
+    if (!Q && !K) return;
+    uint32_t seq = q_seq > k_seq ? q_seq : k_seq;
+    uint64_t total = (uint64_t)batch * heads * seq;
+    float theta = theta_base > 0.0f ? theta_base : 10000.0f;
+    float sc = scaling > 0.0f ? scaling : 1.0f;
+    for (uint64_t idx = 0; idx < total; ++idx) {
+        uint64_t bh = idx / seq;
+        uint32_t t = (uint32_t)(idx % seq);
+        float position = (float)(positions ? positions[t]
+                                           : (int32_t)(t + position_offset));
+        if (Q && t < q_seq)
+            rotate_vector(Q + (bh * q_seq + t) * head_dim, head_dim, position,
+                          theta, sc, interleaved != 0);
+        if (K && t < k_seq)
+            rotate_vector(K + (bh * k_seq + t) * head_dim, head_dim, position,
+                          theta, sc, interleaved != 0);
+    }
+}
+
+/* SwiGLU: AVX2 src/kernels/llm.cpp:289-306 (exp256 lanes), scalar :240-246. */
+void oracle_swiglu(const float *gate, const float *up, float *Y,
+                   uint64_t count, float alpha, int form)
+{
+    float a = alpha == 0.0f ? 1.0f : alpha;
+    for (uint64_t i = 0; i < count; ++i) {
+        float g = gate[i];
+        if (form == ORACLE_FORM_AVX2) {
+            float s = g / (1.0f + exp256_lane(-g));
+            Y[i] = (s * up[i]) * a;
+        } else {
+            Y[i] = silu_f(g, ORACLE_FORM_SCALAR) * up[i] * a;
+        }
+    }
+}
+
+/* ADD: AVX2 src/kernels/llm.cpp:256-271 fma(x, alpha, y*beta); scalar :223-230. */
+void oracle_add(const float *A, const float *B, float *Y, uint64_t count,
+                float alpha, float beta, int form)
+{
+    int dflt = alpha == 0.0f && beta == 0.0f;
+    float al = dflt ? 1.0f : alpha;
+    float be = dflt ? 1.0f : beta;
+    for (uint64_t i = 0; i < count; ++i)
+        Y[i] = form == ORACLE_FORM_AVX2 ? fmaf(A[i], al, B[i] * be)
+                                        : al * A[i] + be * B[i];
+}
+
+/* attention_range, src/kernels/llm.cpp:442-546: 16-query x 64-key blocks,
+ * online softmax with fast_expf (the function is compiled without FMA, so the
+ * scalar form), dot products and V accumulation through the AVX2 helpers. */
+void oracle_attention(const float *Q, const float *K, const float *V,
+                      const float *mask, float *O, uint32_t batch,
+                      uint32_t heads, uint32_t seq_q, uint32_t seq_k,
+                      uint32_t head_dim, uint32_t causal, float scale_in)
+{
+    enum { BQ = 16, BK = 64 };
+    const uint32_t D = head_dim;
+    const float scale = scale_in > 0.0f ? scale_in : 1.0f / sqrtf((float)D);
+    const uint32_t causal_offset = seq_k > seq_q ? seq_k - seq_q : 0;
+    float *scores = (float *)malloc(sizeof(float) * BQ * BK);
+    float *acc = (float *)malloc(sizeof(float) * BQ * D);
+    float m[BQ], l[BQ];
+    if (!scores || !acc) { free(scores); free(acc); return; }
+    for (uint64_t bh = 0; bh < (uint64_t)batch * heads; ++bh) {
+        const float *Qh = Q + bh * seq_q * D;
+        const float *Kh = K + bh * seq_k * D;
+        const float *Vh = V + bh * seq_k * D;
+        const float *Mh = mask ? mask + bh * seq_q * seq_k : NULL;
+        float *Oh = O + bh * seq_q * D;
+        for (uint32_t q0 = 0; q0 < seq_q; q0 += BQ) {
+            uint32_t qc = seq_q - q0 < BQ ? seq_q - q0 : BQ;
+            for (uint32_t i = 0; i < qc; ++i) {
+                m[i] = -INFINITY;
+                l[i] = 0.0f;
+                memset(acc + (size_t)i * D, 0, sizeof(float) * D);
+            }
+            for (uint32_t k0 = 0; k0 < seq_k; k0 += BK) {
+                uint32_t kc = seq_k - k0 < BK ? seq_k - k0 : BK;
+                for (uint32_t i = 0; i < qc; ++i) {
+                    uint32_t qi = q0 + i;
+                    for (uint32_t j = 0; j < kc; ++j) {
+                        uint32_t ki = k0 + j;
+                        float s;
+                        if (causal && ki > qi + causal_offset) {
+                            s = -INFINITY;
+                        } else {
+                            s = dot_avx2(Qh + (size_t)qi * D, Kh + (size_t)ki * D, D) * scale;
+                            if (Mh) s += Mh[(size_t)qi * seq_k + ki];
+                        }
+                        scores[i * BK + j] = s;
+                    }
+                }
+                for (uint32_t i = 0; i < qc; ++i) {
+                    float bmax = -INFINITY;
+                    for (uint32_t j = 0; j < kc; ++j)
+                        bmax = bmax < scores[i * BK + j] ? scores[i * BK + j] : bmax;
+                    if (!isfinite(bmax)) continue;
+                    float nm = m[i] < bmax ? bmax : m[i];
+                    float alpha = oracle_fast_expf(m[i] - nm, ORACLE_FORM_SCALAR);
+                    float sum_p = 0.0f;
+                    for (uint32_t j = 0; j < kc; ++j) {
+                        float p = oracle_fast_expf(scores[i * BK + j] - nm, ORACLE_FORM_SCALAR);
+                        scores[i * BK + j] = p;
+                        sum_p += p;
+                    }
+                    l[i] = l[i] * alpha + sum_p;
+                    float *row = acc + (size_t)i * D;
+                    for (uint32_t d = 0; d < D; ++d) row[d] *= alpha;
+                    for (uint32_t j = 0; j < kc; ++j) {
+                        float p = scores[i * BK + j];
+                        if (p == 0.0f) continue;
+                        const float *v = Vh + (size_t)(k0 + j) * D;
+                        for (uint32_t d = 0; d < D; ++d) row[d] = fmaf(v[d], p, row[d]);
+                    }
+                    m[i] = nm;
+                }
+            }
+            for (uint32_t i = 0; i < qc; ++i) {
+                float inv = l[i] > 0.0f ? 1.0f / l[i] : 0.0f;
+                for (uint32_t d = 0; d < D; ++d)
+                    Oh[(size_t)(q0 + i) * D + d] = acc[(size_t)i * D + d] * inv;
+            }
+        }
+    }
+    free(scores);
+    free(acc);
+}

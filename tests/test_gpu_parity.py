@@ -1,0 +1,326 @@
+"""Parity of the B200 kernels with the reference, through the C ABI.
+
+Bar (north star): int32 accumulators and QUANTIZE_I8 codes bit-exact; the
+dequantised f32 GEMM output bit-exact for the same epilogue form (tolerance
+0 ulp, which is inside the stated 1 ulp); f32 block ops within 1e-4 relative /
+1e-5 absolute (the kernels restate the reference's operation order, so most
+are checked at 0 ulp, RoPE within 4 ulp because it uses the device sinf/cosf).
+
+Checked against the committed golden vectors (produced by the reference
+library itself) and against the C restatement in oracle/ on fresh seeded
+inputs, including ragged shapes, strides and the three GEMM kernels.
+"""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+
+import vnpu
+from conftest import bits_equal, ulp_diff
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-4, 1e-5
+
+
+@pytest.fixture
+def force_kernel():
+    """Pin the MATMUL_I8 kernel choice for one test."""
+    def _set(name):
+        if name:
+            os.environ["VNPU_B200_FORCE_KERNEL"] = name
+        else:
+            os.environ.pop("VNPU_B200_FORCE_KERNEL", None)
+    yield _set
+    os.environ.pop("VNPU_B200_FORCE_KERNEL", None)
+
+
+def run_matmul(dev, A, B, sa, sb, bias, epi, form=0, lda=0, ldc=0, Cbuf=None, M=None, K=None,
+               N=None):
+    K = K if K is not None else B.shape[0]
+    N = N if N is not None else B.shape[1]
+    M = M if M is not None else A.shape[0]
+    w = dev.pack(B, sb, K, N)
+    try:
+        C = Cbuf if Cbuf is not None else np.full((M, N), np.nan, np.float32)
+        dev.matmul_i8(A, w, sa, bias, C, M, K, N, lda=lda, ldc=ldc, epilogue=epi,
+                      flags=vnpu.FORM_FLAGS[form])
+    finally:
+        dev.unpack(w)
+    return C
+
+
+# --------------------------------------------------------------------------- QUANTIZE_I8
+@pytest.mark.parametrize("name,axis", [("row", 0), ("col", 1), ("tensor", 2)])
+def test_quantize_golden(gpu, golden, name, axis):
+    X = golden[f"quant_{name}_X"]
+    r, c = X.shape
+    Y = np.empty((r, c), np.int8)
+    s = np.empty(golden[f"quant_{name}_s"].shape, np.float32)
+    gpu.quantize_i8(X, Y, s, r, c, axis)
+    assert bits_equal(Y, golden[f"quant_{name}_Y"])
+    assert bits_equal(s, golden[f"quant_{name}_s"])
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 4097), (64, 4096), (7, 12000), (512, 4096),
+                                       (33, 8192)])
+@pytest.mark.parametrize("axis", [0, 1, 2])
+def test_quantize_vs_oracle(gpu, oracle, rows, cols, axis):
+    rng = np.random.default_rng(rows * 7919 + cols + axis)
+    X = rng.uniform(-1, 1, (rows, cols)).astype(np.float32)
+    if rows > 1 and cols > 8:
+        X[0, :4] = [np.nan, np.inf if axis != 0 else 2.0, -0.0, 1e-30]
+        X[-1, :] = 0.0  # all-zero row: scale 1.0
+    Yo, so = oracle.quantize(X, axis)
+    Y = np.empty_like(Yo)
+    s = np.empty_like(so)
+    gpu.quantize_i8(X, Y, s, rows, cols, axis)
+    assert bits_equal(Y, Yo)
+    assert bits_equal(s, so)
+
+
+def test_quantize_device_pointers(gpu, oracle):
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(5)
+    X = rng.normal(0, 1, (256, 4096)).astype(np.float32)
+    Yo, so = oracle.quantize(X, 0)
+    dX = torch.from_numpy(X).cuda()
+    dY = torch.empty((256, 4096), dtype=torch.int8, device="cuda")
+    ds = torch.empty(256, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    gpu.quantize_i8(dX.data_ptr(), dY.data_ptr(), ds.data_ptr(), 256, 4096, 0)
+    assert bits_equal(dY.cpu().numpy(), Yo)
+    assert bits_equal(ds.cpu().numpy(), so)
+
+
+# --------------------------------------------------------------------------- MATMUL_I8
+def _golden_case(golden, i):
+    M, K, N, has_bias, epi = (int(v) for v in golden["mm_cases"][i])
+    A, B = golden[f"mm{i}_A"], golden[f"mm{i}_B"]
+    sa, sb = golden[f"mm{i}_sa"], golden[f"mm{i}_sb"]
+    bias = golden.get(f"mm{i}_bias")
+    return M, K, N, epi, A, B, sa, sb, bias, golden[f"mm{i}_C"], int(golden["mm_forms"][i])
+
+
+@pytest.mark.parametrize("i", range(11))
+@pytest.mark.parametrize("kernel", [None, "simt"])
+def test_matmul_golden(gpu, golden, force_kernel, i, kernel):
+    M, K, N, epi, A, B, sa, sb, bias, Cref, form = _golden_case(golden, i)
+    force_kernel(kernel)
+    C = run_matmul(gpu, A, B, sa, sb, bias, epi, form)
+    assert bits_equal(C, Cref), f"case {i}: max ulp {ulp_diff(C, Cref)}"
+
+
+@pytest.mark.parametrize("kernel", ["tcgen05", "gemv", "simt"])
+@pytest.mark.parametrize("M,K,N", [(1, 4096, 4096), (4, 4096, 512), (8, 4096, 384),
+                                   (9, 1000, 257), (128, 128, 256), (200, 1024, 1000),
+                                   (257, 777, 513), (512, 512, 512)])
+def test_matmul_int32_exact(gpu, oracle, force_kernel, kernel, M, K, N):
+    """scale 1, no bias, |acc| < 2^24: C == float(acc) exactly."""
+    if kernel == "gemv" and M > 8:
+        pytest.skip("gemv takes M <= 8")
+    rng = np.random.default_rng(M * 131 + K * 7 + N)
+    A = rng.integers(-128, 128, (M, K), dtype=np.int8)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    acc = oracle.gemm_acc(A, B)
+    assert np.abs(acc).max() < 2 ** 24
+    force_kernel(kernel)
+    C = run_matmul(gpu, A, B, None, None, None, 0)
+    assert bits_equal(C, acc.astype(np.float32))
+
+
+@pytest.mark.parametrize("form", [0, 1, 2])
+@pytest.mark.parametrize("epi", [0, 1, 2, 3, 4])
+@pytest.mark.parametrize("M,K,N", [(1, 300, 200), (6, 129, 77), (130, 200, 300),
+                                   (256, 1024, 512)])
+def test_matmul_epilogue_forms(gpu, oracle, form, epi, M, K, N):
+    rng = np.random.default_rng(epi * 1000 + form * 100 + M)
+    Af = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    Bf = rng.normal(0, 0.02, (K, N)).astype(np.float32)
+    A, sa = oracle.quantize(Af, 0)
+    B, sb = oracle.quantize(Bf, 1)
+    bias = rng.normal(0, 0.5, N).astype(np.float32)
+    Co = oracle.matmul_i8(A, B, sa, sb, bias, epi, form)
+    C = run_matmul(gpu, A, B, sa, sb, bias, epi, form)
+    assert bits_equal(C, Co), f"max ulp {ulp_diff(C, Co)}"
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8, 9, 17, 127, 128, 129, 255, 257])
+@pytest.mark.parametrize("N", [1, 7, 255, 256, 257])
+@pytest.mark.parametrize("K", [1, 15, 16, 17, 127, 128, 129, 1000])
+def test_matmul_ragged_shapes(gpu, oracle, M, N, K):
+    rng = np.random.default_rng(M * 100003 + N * 101 + K)
+    A = rng.integers(-128, 128, (M, K), dtype=np.int8)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    sa = rng.uniform(1e-3, 2e-2, M).astype(np.float32)
+    sb = rng.uniform(1e-4, 2e-3, N).astype(np.float32)
+    bias = rng.normal(0, 0.1, N).astype(np.float32)
+    Co = oracle.matmul_i8(A, B, sa, sb, bias, 2, 0)
+    C = run_matmul(gpu, A, B, sa, sb, bias, 2, 0)
+    assert bits_equal(C, Co), f"max ulp {ulp_diff(C, Co)}"
+
+
+@pytest.mark.parametrize("lda_pad,ldc_pad", [(0, 0), (16, 0), (5, 3), (48, 64)])
+def test_matmul_strides(gpu, oracle, lda_pad, ldc_pad):
+    """lda > K (aligned and not), ldc > N: gaps in C must be left untouched."""
+    M, K, N = 150, 320, 300
+    lda, ldc = K + lda_pad, N + ldc_pad
+    rng = np.random.default_rng(lda * 3 + ldc)
+    Abuf = rng.integers(-128, 128, (M, lda), dtype=np.int8)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    sa = rng.uniform(1e-3, 2e-2, M).astype(np.float32)
+    sb = rng.uniform(1e-4, 2e-3, N).astype(np.float32)
+    Co = oracle.matmul_i8(Abuf[:, :K], B, sa, sb, None, 0, 0)
+    Cbuf = np.full((M, ldc), 7.25, np.float32)
+    run_matmul(gpu, Abuf, B, sa, sb, None, 0, 0, lda=lda, ldc=ldc, Cbuf=Cbuf, M=M, K=K, N=N)
+    assert bits_equal(Cbuf[:, :N], Co)
+    assert np.all(Cbuf[:, N:] == 7.25)
+
+
+def test_matmul_device_pointers_and_kernels_agree(gpu, oracle, force_kernel):
+    """Device-resident operands; tcgen05 and simt give the same bits."""
+    torch = pytest.importorskip("torch")
+    M, K, N = 1024, 2048, 1536
+    rng = np.random.default_rng(11)
+    Af = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    Bf = rng.normal(0, 0.02, (K, N)).astype(np.float32)
+    A, sa = oracle.quantize(Af, 0)
+    B, sb = oracle.quantize(Bf, 1)
+    bias = rng.normal(0, 0.01, N).astype(np.float32)
+    dA = torch.from_numpy(A).cuda()
+    dsa = torch.from_numpy(sa).cuda()
+    dbias = torch.from_numpy(bias).cuda()
+    w = gpu.pack(torch.from_numpy(B).cuda().data_ptr(), torch.from_numpy(sb).cuda().data_ptr(),
+                 K, N)
+    outs = {}
+    try:
+        for kern in ("tcgen05", "simt"):
+            force_kernel(kern)
+            dC = torch.full((M, N), float("nan"), device="cuda")
+            torch.cuda.synchronize()
+            gpu.matmul_i8(dA.data_ptr(), w, dsa.data_ptr(), dbias.data_ptr(), dC.data_ptr(),
+                          M, K, N, epilogue=2)
+            outs[kern] = dC.cpu().numpy()
+    finally:
+        gpu.unpack(w)
+    assert bits_equal(outs["tcgen05"], outs["simt"])
+    rows = np.arange(0, M, 37)
+    Co = oracle.matmul_i8(A[rows], B, sa[rows], sb, bias, 2, 0)
+    assert bits_equal(outs["tcgen05"][rows], Co)
+
+
+@pytest.mark.parametrize("M,K,N", [(8192, 8192, 8192), (4096, 4096, 14336)])
+def test_matmul_full_size_sampled(gpu, oracle, M, K, N):
+    """Headline sizes: every 97th row against the oracle, plus a row-sum
+    checksum of all rows against the oracle's int32 arithmetic."""
+    torch = pytest.importorskip("torch")
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    dA = torch.randint(-128, 128, (M, K), dtype=torch.int8, device="cuda", generator=g)
+    dB = torch.randint(-128, 128, (K, N), dtype=torch.int8, device="cuda", generator=g)
+    ones_a = torch.ones(M, device="cuda")
+    ones_b = torch.ones(N, device="cuda")
+    w = gpu.pack(dB.data_ptr(), ones_b.data_ptr(), K, N)
+    try:
+        dC = torch.empty((M, N), device="cuda")
+        torch.cuda.synchronize()
+        gpu.matmul_i8(dA.data_ptr(), w, ones_a.data_ptr(), None, dC.data_ptr(), M, K, N)
+        torch.cuda.synchronize()
+    finally:
+        gpu.unpack(w)
+    A = dA.cpu().numpy()
+    B = dB.cpu().numpy()
+    rows = np.arange(0, M, 97)
+    acc = oracle.gemm_acc(A[rows], B)
+    C_rows = dC[torch.from_numpy(rows).cuda()].cpu().numpy()
+    # |acc| may exceed 2^24 at K=8192: compare with float(acc), the exact
+    # int32->f32 rounding the epilogue performs (scale 1.0).
+    assert bits_equal(C_rows, acc.astype(np.float32))
+    # every row: sum over n of float(acc) in float64 equals A . (B summed over n)
+    colsum = B.astype(np.int64).sum(axis=1)
+    exact = A.astype(np.int64) @ colsum
+    got = dC.double().sum(dim=1).cpu().numpy()
+    # float(acc) rounds each |acc| <= 2^14 * K by at most 2^-24 relative
+    bound = N * (128.0 * 128.0 * K) * 2.0 ** -24 + 1.0
+    assert np.abs(got - exact).max() <= bound
+
+
+# --------------------------------------------------------------------------- block ops
+def test_rmsnorm_golden(gpu, golden):
+    X, W = golden["rms_X"], golden["rms_W"]
+    Y = np.empty_like(X)
+    gpu.rmsnorm(X, W, Y, X.shape[0], X.shape[1], 1e-6)
+    assert bits_equal(Y, golden["rms_Y"])
+    X2 = golden["rms2_X"]
+    Y2 = np.empty_like(X2)
+    gpu.rmsnorm(X2, None, Y2, X2.shape[0], X2.shape[1], 0.0)
+    assert bits_equal(Y2, golden["rms2_Y"])
+
+
+def test_rmsnorm_block_sizes(gpu, oracle):
+    rng = np.random.default_rng(3)
+    for rows, cols in ((512, 4096), (1, 4096), (7, 11008), (3, 13)):
+        X = rng.normal(0, 1, (rows, cols)).astype(np.float32)
+        W = rng.normal(1, 0.1, cols).astype(np.float32)
+        Y = np.empty_like(X)
+        gpu.rmsnorm(X, W, Y, rows, cols, 1e-6)
+        assert bits_equal(Y, oracle.rmsnorm(X, W, 1e-6, 0))
+
+
+def test_rope_golden(gpu, golden):
+    Q, K = golden["rope_Q"].copy(), golden["rope_K"].copy()
+    _, H, T, D = Q.shape
+    gpu.rope(Q, K, None, 1, H, T, T, D, position_offset=5)
+    for got, ref in ((Q, golden["rope_Qr"]), (K, golden["rope_Kr"])):
+        np.testing.assert_allclose(got, ref, rtol=RTOL, atol=ATOL)
+        assert ulp_diff(got, ref) <= 4 or np.abs(got - ref).max() <= ATOL
+    Qi = golden["ropei_Q"].copy()
+    gpu.rope(Qi, None, golden["ropei_pos"], 1, 2, 9, 0, 64, interleaved=1, theta=500000.0,
+             scaling=0.5)
+    np.testing.assert_allclose(Qi, golden["ropei_Qr"], rtol=RTOL, atol=ATOL)
+
+
+def test_rope_decode_positions(gpu, oracle):
+    rng = np.random.default_rng(9)
+    for pos in (0, 511, 639):
+        Q = rng.normal(0, 1, (1, 32, 1, 128)).astype(np.float32)
+        K = rng.normal(0, 1, (1, 32, 1, 128)).astype(np.float32)
+        Qg, Kg = Q.copy(), K.copy()
+        gpu.rope(Qg, Kg, None, 1, 32, 1, 1, 128, position_offset=pos)
+        Qo, Ko = oracle.rope(Q, K, None, 1, 32, 1, 1, 128, position_offset=pos)
+        np.testing.assert_allclose(Qg, Qo, rtol=RTOL, atol=ATOL)
+        np.testing.assert_allclose(Kg, Ko, rtol=RTOL, atol=ATOL)
+
+
+def test_swiglu_add_golden(gpu, golden):
+    g, u = golden["swiglu_g"], golden["swiglu_u"]
+    Y = np.empty_like(g)
+    gpu.swiglu(g, u, Y, g.size, 0.0)
+    assert bits_equal(Y, golden["swiglu_Y"])
+    a, b = golden["add_A"], golden["add_B"]
+    Y = np.empty_like(a)
+    gpu.add(a, b, Y, a.size, 0.7, 1.3)
+    assert bits_equal(Y, golden["add_Y"])
+
+
+@pytest.mark.parametrize("name", ["attn", "attnd", "attnm"])
+def test_attention_golden(gpu, golden, name):
+    h, sq, sk, d, causal = (int(v) for v in golden[f"{name}_shape"])
+    O = np.empty((1, h, sq, d), np.float32)
+    gpu.attention(golden[f"{name}_Q"], golden[f"{name}_K"], golden[f"{name}_V"],
+                  golden.get(f"{name}_M"), O, 1, h, sq, sk, d, causal, 0.0)
+    assert bits_equal(O, golden[f"{name}_O"]), f"max ulp {ulp_diff(O, golden[f'{name}_O'])}"
+
+
+@pytest.mark.parametrize("sq,sk", [(512, 512), (1, 513), (1, 640), (16, 16), (17, 100)])
+def test_attention_block_shapes(gpu, oracle, sq, sk):
+    H, D = 32 if sq <= 16 else 8, 128
+    rng = np.random.default_rng(sq * 1000 + sk)
+    Q = rng.normal(0, 1, (1, H, sq, D)).astype(np.float32)
+    K = rng.normal(0, 1, (1, H, sk, D)).astype(np.float32)
+    V = rng.normal(0, 1, (1, H, sk, D)).astype(np.float32)
+    O = np.empty((1, H, sq, D), np.float32)
+    gpu.attention(Q, K, V, None, O, 1, H, sq, sk, D, 1, 0.0)
+    Oo = oracle.attention(Q, K, V, None, 1, H, sq, sk, D, 1, 0.0)
+    assert bits_equal(O, Oo), f"max ulp {ulp_diff(O, Oo)}"
