@@ -1,0 +1,562 @@
+"""Benchmark of the B200 MATMUL_I8 hot path (one JSON line on rank 0).
+
+Workload: column-sharded MATMUL_I8, M=8192, K=8192,
+N=28672, split evenly over the N GPUs (strong scaling); activations f32
+U[-1,1] quantized per row by QUANTIZE_I8 every step, weights f32 N(0,0.02)
+quantized per column and packed once (resident).  One step = QUANTIZE_I8 of
+A + MATMUL_I8 on this rank's column shard.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+value   - whole-job int8 TOPS with inputs resident in HBM, device-timed with
+          CUDA events on the library's stream, max over ranks.
+e2e     - the same step through the C ABI with HOST buffers: A f32 from pinned
+          host memory in, C f32 shard to pinned host memory out, copies inside
+          the timed region.
+roofline- the tcgen05 GEMM kernel alone, algorithmic int8 ops / event time,
+          against 2x the measured dense bf16 rate (int8 runs at twice bf16 on
+          B200; nominal 4.5 POPS).
+--impl reference times the reference's own CPU implementation (built from
+its sources into oracle/_ref) on this host's cores, on a row sample of the
+same workload, through the same ABI calls.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "npuxl-improved_b200"))
+
+import numpy as np  # noqa: E402
+
+import vnpu  # noqa: E402
+from shard import column_shard  # noqa: E402
+
+M_TOTAL, K_TOTAL, N_TOTAL = 8192, 8192, 28672
+REF_LIB = os.path.join(ROOT, "oracle", "_ref", "libvnpu_ref.so")
+ORACLE_LIB = os.path.join(ROOT, "oracle", "liboracle.so")
+WORKLOAD = ("MATMUL_I8 column-sharded M=8192 K=8192 N=28672 (QUANTIZE_I8 per row of A "
+            "each step; weights per-column quantized, packed, resident)")
+METRIC = "int8 GEMM TOPS (MATMUL_I8 8192x8192x28672 column-sharded)"
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        p = json.load(open(path))
+        return {"hbm_gbs": p["hbm_gbs"], "bf16": p["bf16_tflops"],
+                "bf16_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]),
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+def profile_traffic(key: str):
+    """DRAM bytes per launch recorded from an ncu capture (profiles/*.md)."""
+    pdir = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(pdir):
+        return None
+    for f in sorted(os.listdir(pdir)):
+        if not f.endswith(".md"):
+            continue
+        for line in open(os.path.join(pdir, f)):
+            if line.startswith(f"dram_bytes_per_launch[{key}]:"):
+                try:
+                    return int(line.split(":", 1)[1].strip().split()[0])
+                except ValueError:
+                    return None
+    return None
+
+
+class ClockSampler:
+    """NVML SM clock / throttle reasons sampled during the timed region."""
+
+    def __init__(self, index: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nvml = None
+        self.names = {
+            0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+            0x80: "hw_power_brake_slowdown", 0x4: "sw_power_cap", 0x2: "applications_clocks_setting",
+            0x100: "sync_boost",
+        }
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.h, self.nvml.NVML_CLOCK_SM))
+                r = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.names.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.05)
+
+    def __enter__(self):
+        if self.nvml:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self.nvml:
+            self.t.join()
+
+    def report(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"]}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ===========================================================================
+# CPU reference arm / baseline
+# ===========================================================================
+def reference_sample(rows: int, steps: int, warmup: int, threads: int):
+    """Time QUANTIZE_I8 + MATMUL_I8 of `rows` rows of the workload on the
+    reference's CPU implementation (host buffers, its own thread pool)."""
+    if os.path.exists(REF_LIB):
+        lib, kind = vnpu.Lib(REF_LIB), "reference"
+        os.environ.setdefault("VNPU_FORCE_ISA", "avx2")
+    else:
+        lib, kind = None, "port"
+    rng = np.random.default_rng(1)
+    n = N_TOTAL
+    Bf = rng.normal(0, 0.02, (K_TOTAL, n)).astype(np.float32)
+    A = rng.uniform(-1, 1, (rows, K_TOTAL)).astype(np.float32)
+    if lib is None:
+        orc = vnpu.Oracle(ORACLE_LIB)
+        B8, sb = orc.quantize(Bf, 1)
+        del Bf
+        times = []
+        for i in range(warmup + steps):
+            t0 = time.perf_counter()
+            A8, sa = orc.quantize(A, 0)
+            orc.matmul_i8(A8, B8, sa, sb, None, 0, 0)
+            if i >= warmup:
+                times.append(time.perf_counter() - t0)
+        cores = 1
+    else:
+        dev = vnpu.Device(lib, num_threads=threads)
+        B8 = np.empty((K_TOTAL, n), np.int8)
+        sb = np.empty(n, np.float32)
+        dev.quantize_i8(Bf, B8, sb, K_TOTAL, n, vnpu.QUANT_PER_COLUMN)
+        del Bf
+        w = dev.pack(B8, sb, K_TOTAL, n)
+        A8 = np.empty((rows, K_TOTAL), np.int8)
+        sa = np.empty(rows, np.float32)
+        Cout = np.empty((rows, n), np.float32)
+        times = []
+        for i in range(warmup + steps):
+            t0 = time.perf_counter()
+            dev.quantize_i8(A, A8, sa, rows, K_TOTAL, vnpu.QUANT_PER_ROW)
+            dev.matmul_i8(A8, w, sa, None, Cout, rows, K_TOTAL, n, unit=vnpu.UNIT_VOODOO)
+            if i >= warmup:
+                times.append(time.perf_counter() - t0)
+        cores = dev.info().num_threads
+        dev.unpack(w)
+        dev.close()
+    t = statistics.median(times)
+    ops = 2.0 * rows * K_TOTAL * n
+    return {"value": ops / t / 1e12, "unit": "TOPS", "cores": cores, "kind": kind,
+            "sample": f"{rows} rows of A ({rows}x{K_TOTAL}x{n}, quantize+matmul, host buffers), "
+                      f"median of {len(times)} steps, {t:.3f} s/step",
+            "seconds_per_step": t}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    # about 1 s of work per step on a many-core host
+    rows = int(os.environ.get("VNPU_BENCH_REF_ROWS", "32"))
+    r = reference_sample(rows, max(1, args.steps), max(0, min(args.warmup, 2)), threads)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": r["value"], "unit": "TOPS",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": r["seconds_per_step"] * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample_rows": rows, "M": M_TOTAL, "K": K_TOTAL,
+                   "N": N_TOTAL, "isa": os.environ.get("VNPU_FORCE_ISA", "port")},
+        "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": r["value"], "unit": "TOPS", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ===========================================================================
+# B200 arm
+# ===========================================================================
+class Stream:
+    """The library's CUDA stream seen from torch, for events."""
+
+    def __init__(self, lib, dev):
+        import torch
+        self.torch = torch
+        self.cs = torch.cuda.ExternalStream(lib.b200_stream_handle(dev.stream))
+
+    def event(self):
+        e = self.torch.cuda.Event(enable_timing=True)
+        e.record(self.cs)
+        return e
+
+
+def cmd_quantize(X, Y, s, rows, cols):
+    c = vnpu.Command()
+    c.opcode = vnpu.OP_QUANTIZE_I8
+    c.args.quantize_i8 = vnpu.QuantizeI8Args(X, Y, s, rows, cols, vnpu.QUANT_PER_ROW, 0)
+    return c
+
+
+def cmd_matmul(A, w, sa, bias, Cp, M, K, N, epi=0, ldc=0):
+    c = vnpu.Command()
+    c.opcode = vnpu.OP_MATMUL_I8
+    c.args.matmul_i8 = vnpu.MatmulI8Args(A, w, sa, bias, Cp, M, K, N, 0, ldc, epi,
+                                         vnpu.UNIT_GPU)
+    return c
+
+
+def submit(lib, dev, cmds):
+    arr = (vnpu.Command * len(cmds))(*cmds)
+    rc = lib.stream_submit(dev.stream, arr, len(cmds), None)
+    if rc != vnpu.OK:
+        raise RuntimeError(f"submit failed: {rc}")
+
+
+def time_loop(lib, dev, st, cmds, iters):
+    """Average ms of one iteration of `cmds`, device-timed on the library stream."""
+    e0 = st.event()
+    for _ in range(iters):
+        submit(lib, dev, cmds)
+    e1 = st.event()
+    if dev.sync() != vnpu.OK:
+        raise RuntimeError("stream error")
+    e1.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def make_weights(lib, dev, torch, K, N, seed, shard=None):
+    """f32 N(0,0.02) weights -> QUANTIZE_I8 per column on the GPU -> pack."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    n0, n1 = shard if shard else (0, N)
+    Bf = torch.empty((K, N), device="cuda").normal_(0, 0.02, generator=g)[:, n0:n1].contiguous()
+    n = n1 - n0
+    B8 = torch.empty((K, n), dtype=torch.int8, device="cuda")
+    sb = torch.empty(n, device="cuda")
+    torch.cuda.synchronize()
+    dev.quantize_i8(Bf.data_ptr(), B8.data_ptr(), sb.data_ptr(), K, n, vnpu.QUANT_PER_COLUMN)
+    w = dev.pack(B8.data_ptr(), sb.data_ptr(), K, n)
+    del Bf, B8
+    return w, sb, n
+
+
+def gemm_secondary(lib, dev, st, torch, M, K, N, epi, with_bias, iters=20):
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    Af = torch.empty((M, K), device="cuda").uniform_(-1, 1, generator=g)
+    A8 = torch.empty((M, K), dtype=torch.int8, device="cuda")
+    sa = torch.empty(M, device="cuda")
+    w, sb, n = make_weights(lib, dev, torch, K, N, seed=7)
+    bias = torch.empty(N, device="cuda").normal_(0, 0.01, generator=g) if with_bias else None
+    Cm = torch.empty((M, N), device="cuda")
+    torch.cuda.synchronize()
+    q = cmd_quantize(Af.data_ptr(), A8.data_ptr(), sa.data_ptr(), M, K)
+    mm = cmd_matmul(A8.data_ptr(), w, sa.data_ptr(), bias.data_ptr() if bias is not None else None,
+                    Cm.data_ptr(), M, K, N, epi)
+    time_loop(lib, dev, st, [q, mm], 3)
+    ms = time_loop(lib, dev, st, [mm], iters)
+    dev.unpack(w)
+    return {"shape": f"{M}x{K}x{N}", "epilogue": ["none", "relu", "silu", "gelu"][epi],
+            "bias": with_bias, "ms": ms, "tops": 2.0 * M * K * N / ms / 1e9,
+            "kernel": lib.b200_matmul_kernel(M, K, N, 0, A8.data_ptr()).decode()}
+
+
+def gemv_secondary(lib, dev, st, torch, M, K=4096, N=4096, copies=32, rounds=8):
+    """Decode GEMV with bias; rotates `copies` weight sets (> 4x L2) so the
+    16 MiB matrix is read from HBM each launch."""
+    g = torch.Generator(device="cuda").manual_seed(M)
+    Af = torch.empty((M, K), device="cuda").uniform_(-1, 1, generator=g)
+    A8 = torch.empty((M, K), dtype=torch.int8, device="cuda")
+    sa = torch.empty(M, device="cuda")
+    bias = torch.empty(N, device="cuda").normal_(0, 0.01, generator=g)
+    Cm = torch.empty((M, N), device="cuda")
+    torch.cuda.synchronize()
+    dev.quantize_i8(Af.data_ptr(), A8.data_ptr(), sa.data_ptr(), M, K, vnpu.QUANT_PER_ROW)
+    ws = [make_weights(lib, dev, torch, K, N, seed=100 + i)[0] for i in range(copies)]
+    cmds = [cmd_matmul(A8.data_ptr(), w, sa.data_ptr(), bias.data_ptr(), Cm.data_ptr(), M, K, N)
+            for w in ws]
+    time_loop(lib, dev, st, cmds, 2)
+    ms = time_loop(lib, dev, st, cmds, rounds) / copies
+    for w in ws:
+        dev.unpack(w)
+    nbytes = K * N + K * M + 4 * M + 4 * N + 4 * N + 4 * M * N
+    return {"M": M, "K": K, "N": N, "us": ms * 1e3, "gbs": nbytes / ms / 1e6,
+            "bytes_per_launch": nbytes,
+            "weight_copies": copies, "kernel": lib.b200_matmul_kernel(M, K, N, 0, A8.data_ptr()).decode()}
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    lib = vnpu.Lib(vnpu.LIB_PATH)
+    dev = vnpu.Device(lib, ordinal=local)
+    st = Stream(lib, dev)
+    pk = peaks()
+
+    M, K = M_TOTAL, K_TOTAL
+    n0, n1 = column_shard(N_TOTAL, world, rank)
+    w, sb, n = make_weights(lib, dev, torch, K, N_TOTAL, seed=1, shard=(n0, n1))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    Af = torch.empty((M, K), device="cuda").uniform_(-1, 1, generator=g)
+    A8 = torch.empty((M, K), dtype=torch.int8, device="cuda")
+    sa = torch.empty(M, device="cuda")
+    Cm = torch.empty((M, n), device="cuda")
+    torch.cuda.synchronize()
+    q = cmd_quantize(Af.data_ptr(), A8.data_ptr(), sa.data_ptr(), M, K)
+    mm = cmd_matmul(A8.data_ptr(), w, sa.data_ptr(), None, Cm.data_ptr(), M, K, n)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- warm-up, then the timed steps (device-resident inputs)
+    for _ in range(args.warmup):
+        submit(lib, dev, [q, mm])
+    dev.sync()
+    barrier()
+    launches0 = lib.b200_kernel_launches(dev.dev)
+    with ClockSampler(local) as clocks:
+        e0 = st.event()
+        for _ in range(args.steps):
+            submit(lib, dev, [q, mm])
+        e1 = st.event()
+        rc = dev.sync()
+        e1.synchronize()
+    launches = lib.b200_kernel_launches(dev.dev) - launches0
+    if rc != vnpu.OK:
+        raise RuntimeError(f"stream error {rc}")
+    ms_step = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    barrier()
+
+    # ---- the GEMM kernel alone (roofline)
+    ms_gemm = max_over_ranks(time_loop(lib, dev, st, [mm], max(3, args.steps)))
+    ops_rank = 2.0 * M * K * n
+    int8_peak = 2.0 * pk["bf16"]
+    achieved = ops_rank / ms_gemm / 1e9
+    traffic = profile_traffic(f"gemm_i8_tcgen05:{M}x{K}x{n}")
+
+    # ---- e2e through the C ABI with host buffers (pinned)
+    hA = torch.empty((M, K), dtype=torch.float32).uniform_(-1, 1).pin_memory()
+    hC = torch.empty((M, n), dtype=torch.float32).pin_memory()
+    qe = cmd_quantize(hA.data_ptr(), A8.data_ptr(), sa.data_ptr(), M, K)
+    me = cmd_matmul(A8.data_ptr(), w, sa.data_ptr(), None, hC.data_ptr(), M, K, n)
+    submit(lib, dev, [qe, me])
+    dev.sync()
+    barrier()
+    e_steps = max(2, min(args.steps, 5))
+    t0 = time.perf_counter()
+    ms_e2e_dev = time_loop(lib, dev, st, [qe, me], e_steps)
+    ms_e2e_wall = (time.perf_counter() - t0) * 1e3 / e_steps
+    ms_e2e = max_over_ranks(max(ms_e2e_dev, ms_e2e_wall))
+
+    # ---- all-gather of the shards over NCCL (config 5's collective)
+    allgather = None
+    if world > 1:
+        shard_pad = torch.zeros((M, -(-N_TOTAL // world // 256) * 256 + 256), device="cuda")
+        width = shard_pad.shape[1]
+        shard_pad[:, :n] = Cm
+        gathered = torch.empty((world, M, width), device="cuda")
+        dist.all_gather_into_tensor(gathered, shard_pad)
+        torch.cuda.synchronize()
+        barrier()
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        a0.record()
+        reps = 3
+        for _ in range(reps):
+            dist.all_gather_into_tensor(gathered, shard_pad)
+        a1.record()
+        torch.cuda.synchronize()
+        ms_ag = max_over_ranks(a0.elapsed_time(a1) / reps)
+        recv = (world - 1) * M * width * 4
+        allgather = {"ms": ms_ag, "bytes_received_per_rank": recv,
+                     "gbs_per_rank": recv / ms_ag / 1e6, "layout": "shard-major [P][M][N/P]",
+                     "ms_step_plus_gather": ms_step + ms_ag}
+        del gathered, shard_pad
+
+    out = None
+    if rank == 0:
+        secondary = {}
+        cpu = None
+        if world == 1 and not args.no_secondary:
+            secondary["gemm_8192_cube"] = gemm_secondary(lib, dev, st, torch, 8192, 8192, 8192, 0, False)
+            secondary["ffn_4096x4096x14336_silu"] = gemm_secondary(lib, dev, st, torch, 4096, 4096,
+                                                                   14336, 2, False)
+            secondary["gemm_512_cube"] = gemm_secondary(lib, dev, st, torch, 512, 512, 512, 0, False,
+                                                        iters=200)
+            for m in (1, 4, 8):
+                gv = gemv_secondary(lib, dev, st, torch, m)
+                gv["frac_of_hbm"] = gv["gbs"] / pk["hbm_gbs"]
+                secondary[f"gemv_m{m}"] = gv
+            try:
+                A_ = torch.randint(-128, 128, (8192, 8192), dtype=torch.int8, device="cuda")
+                B_ = torch.randint(-128, 128, (8192, 8192), dtype=torch.int8, device="cuda").t()
+                torch._int_mm(A_, B_)
+                torch.cuda.synchronize()
+                c0 = torch.cuda.Event(enable_timing=True)
+                c1 = torch.cuda.Event(enable_timing=True)
+                c0.record()
+                for _ in range(10):
+                    torch._int_mm(A_, B_)
+                c1.record()
+                torch.cuda.synchronize()
+                secondary["cublas_int8_8192_cube_tops"] = 2.0 * 8192 ** 3 / (c0.elapsed_time(c1) / 10) / 1e9
+                del A_, B_
+            except Exception as exc:  # library comparator only
+                secondary["cublas_int8_8192_cube_tops"] = f"unavailable: {exc}"
+        if world == 1 and not args.no_cpu_baseline:
+            r = reference_sample(int(os.environ.get("VNPU_BENCH_REF_ROWS", "32")), 3, 1,
+                                 os.cpu_count() or 1)
+            cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        total_ops = 2.0 * M * K * N_TOTAL
+        out = {
+            "metric": METRIC, "value": total_ops / ms_step / 1e9, "unit": "TOPS",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "M": M, "K": K, "N": N_TOTAL, "n_per_gpu": n,
+                       "epilogue": "none", "bias": False, "parallelism": f"column shard x{world}",
+                       "l2": "inputs larger than L2 (A f32 256 MiB, B int8 224 MiB/P, C f32 896 MiB/P)",
+                       "step": "QUANTIZE_I8(A) + MATMUL_I8"},
+            "roofline": {"bound": "tensor", "kernel": "gemm_i8_tcgen05_kernel",
+                         "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
+                         "frac": achieved / int8_peak, "traffic": traffic,
+                         "peak_source": f"2 x {pk['source']} bf16 dense ({pk['bf16']} TFLOP/s); "
+                                        f"nominal int8 dense 4500 TOPS",
+                         "frac_of_nominal": achieved / 4500.0, "ms_per_launch": ms_gemm},
+            "e2e": {"value": total_ops / ms_e2e / 1e9, "unit": "TOPS",
+                    "h2d_bytes_per_step": M * K * 4, "d2h_bytes_per_step": M * n * 4,
+                    "ms_per_step": ms_e2e, "path": "vnpu_stream_submit(QUANTIZE_I8, MATMUL_I8), host X and C"},
+            "gpu_launches": int(launches),
+            "clocks": clocks.report(),
+            "cpu_baseline": cpu,
+            "secondary": secondary,
+        }
+        if allgather:
+            out["allgather"] = allgather
+    dev.unpack(w)
+    dev.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if out is not None:
+        print(json.dumps(out), flush=True)
+    return 0
+
+
+def run_kernel_case(spec: str):
+    """One small case of one kernel, launched twice (for ncu captures):
+    gemm:MxKxN[:silu], gemv:MxKxN, quantize:RxC, attention:HxSQxSKxD."""
+    import torch
+
+    lib = vnpu.Lib(vnpu.LIB_PATH)
+    dev = vnpu.Device(lib, ordinal=0)
+    kind, dims = spec.split(":", 1)
+    parts = dims.split(":")
+    shape = [int(x) for x in parts[0].split("x")]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    if kind in ("gemm", "gemv"):
+        M, K, N = shape
+        epi = 2 if len(parts) > 1 and parts[1] == "silu" else 0
+        Af = torch.empty((M, K), device="cuda").uniform_(-1, 1, generator=g)
+        A8 = torch.empty((M, K), dtype=torch.int8, device="cuda")
+        sa = torch.empty(M, device="cuda")
+        Cm = torch.empty((M, N), device="cuda")
+        torch.cuda.synchronize()
+        dev.quantize_i8(Af.data_ptr(), A8.data_ptr(), sa.data_ptr(), M, K, vnpu.QUANT_PER_ROW)
+        w, sb, n = make_weights(lib, dev, torch, K, N, seed=3)
+        for _ in range(2):
+            dev.matmul_i8(A8.data_ptr(), w, sa.data_ptr(), None, Cm.data_ptr(), M, K, N,
+                          epilogue=epi)
+        dev.unpack(w)
+    elif kind == "quantize":
+        R, Cc = shape
+        X = torch.empty((R, Cc), device="cuda").uniform_(-1, 1, generator=g)
+        Y = torch.empty((R, Cc), dtype=torch.int8, device="cuda")
+        s = torch.empty(R, device="cuda")
+        torch.cuda.synchronize()
+        for _ in range(2):
+            dev.quantize_i8(X.data_ptr(), Y.data_ptr(), s.data_ptr(), R, Cc, vnpu.QUANT_PER_ROW)
+    elif kind == "attention":
+        H, SQ, SK, D = shape
+        Q = torch.randn((1, H, SQ, D), device="cuda", generator=g)
+        Kt = torch.randn((1, H, SK, D), device="cuda", generator=g)
+        V = torch.randn((1, H, SK, D), device="cuda", generator=g)
+        O = torch.empty((1, H, SQ, D), device="cuda")
+        torch.cuda.synchronize()
+        for _ in range(2):
+            dev.attention(Q.data_ptr(), Kt.data_ptr(), V.data_ptr(), None, O.data_ptr(), 1, H,
+                          SQ, SK, D, 1, 0.0)
+    else:
+        raise SystemExit(f"unknown kernel case {spec}")
+    rc = dev.sync()
+    dev.close()
+    print(f"kernel case {spec}: rc={rc}")
+    return 0 if rc == vnpu.OK else 1
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-case", default=None,
+                    help="run one small kernel case twice and exit (ncu captures)")
+    args = ap.parse_args()
+    if args.kernel_case:
+        return run_kernel_case(args.kernel_case)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,176 @@
+"""The C restatement (oracle/) pinned to the reference.
+
+1. Against the committed golden vectors, which the reference library itself
+   produced (tests/golden/make_golden.py): every value bit-exact.
+2. Against the reference library built from its own sources, when it is
+   present (oracle/_ref): fresh seeded inputs, every value bit-exact, for
+   both of the reference's ISAs (VNPU_FORCE_ISA=avx2 and scalar) and the
+   kernels each shape selects.
+"""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+
+import vnpu
+from conftest import bits_equal
+
+
+# ---------------------------------------------------------------- golden vectors
+@pytest.mark.parametrize("name,axis", [("row", 0), ("col", 1), ("tensor", 2)])
+def test_quantize_golden(oracle, golden, name, axis):
+    Y, s = oracle.quantize(golden[f"quant_{name}_X"], axis)
+    assert bits_equal(Y, golden[f"quant_{name}_Y"])
+    assert bits_equal(s, golden[f"quant_{name}_s"])
+
+
+def test_quantize_golden_has_ties(golden):
+    """The fixture exercises round-half-away-from-zero: 2.5 -> 3, -2.5 -> -3."""
+    Y = golden["quant_row_Y"]
+    assert Y[0, 3] == 3 and Y[0, 4] == -3 and Y[0, 1] == 1 and Y[0, 2] == -1
+
+
+@pytest.mark.parametrize("i", range(11))
+def test_matmul_golden(oracle, golden, i):
+    M, K, N, has_bias, epi = (int(v) for v in golden["mm_cases"][i])
+    bias = golden.get(f"mm{i}_bias")
+    C = oracle.matmul_i8(golden[f"mm{i}_A"], golden[f"mm{i}_B"], golden[f"mm{i}_sa"],
+                         golden[f"mm{i}_sb"], bias, epi, int(golden["mm_forms"][i]))
+    assert bits_equal(C, golden[f"mm{i}_C"])
+
+
+def test_matmul_golden_forms_cover_reference_paths(golden):
+    """Bias cases exist for all three forms the reference produces."""
+    forms = {int(f) for f, c in zip(golden["mm_forms"], golden["mm_cases"]) if c[3]}
+    assert forms == {0, 1, 2}
+
+
+def test_block_ops_golden(oracle, golden):
+    assert bits_equal(oracle.rmsnorm(golden["rms_X"], golden["rms_W"], 1e-6, 0), golden["rms_Y"])
+    assert bits_equal(oracle.rmsnorm(golden["rms2_X"], None, 0.0, 0), golden["rms2_Y"])
+    Q, K = golden["rope_Q"], golden["rope_K"]
+    _, H, T, D = Q.shape
+    Qr, Kr = oracle.rope(Q, K, None, 1, H, T, T, D, position_offset=5)
+    assert bits_equal(Qr, golden["rope_Qr"]) and bits_equal(Kr, golden["rope_Kr"])
+    Qi, _ = oracle.rope(golden["ropei_Q"], None, golden["ropei_pos"], 1, 2, 9, 0, 64,
+                        interleaved=1, theta=500000.0, scaling=0.5)
+    assert bits_equal(Qi, golden["ropei_Qr"])
+    assert bits_equal(oracle.swiglu(golden["swiglu_g"], golden["swiglu_u"], 0.0, 0),
+                      golden["swiglu_Y"])
+    assert bits_equal(oracle.add(golden["add_A"], golden["add_B"], 0.7, 1.3, 0), golden["add_Y"])
+
+
+@pytest.mark.parametrize("name", ["attn", "attnd", "attnm"])
+def test_attention_golden(oracle, golden, name):
+    h, sq, sk, d, causal = (int(v) for v in golden[f"{name}_shape"])
+    O = oracle.attention(golden[f"{name}_Q"], golden[f"{name}_K"], golden[f"{name}_V"],
+                         golden.get(f"{name}_M"), 1, h, sq, sk, d, causal, 0.0)
+    assert bits_equal(O, golden[f"{name}_O"])
+
+
+def test_fast_expf_properties(oracle):
+    """fast_expf (src/internal.h:87-108): cut-offs and 2^n scaling exact."""
+    assert oracle.fast_expf(-80.5, 0) == 0.0
+    assert oracle.fast_expf(80.5, 0) == float("inf")
+    for n in range(-10, 11):
+        assert oracle.fast_expf(n * 0.6931471805599453, 0) == pytest.approx(2.0 ** n, rel=2e-4)
+
+
+# ---------------------------------------------------------------- live reference
+def _ref_device(ref_lib, isa, threads):
+    os.environ["VNPU_FORCE_ISA"] = isa
+    try:
+        return vnpu.Device(ref_lib, num_threads=threads)
+    finally:
+        os.environ.pop("VNPU_FORCE_ISA", None)
+
+
+@pytest.mark.parametrize("isa", ["avx2", "scalar"])
+def test_quantize_vs_reference(ref_lib, oracle, isa):
+    rng = np.random.default_rng(17)
+    with _ref_device(ref_lib, isa, 4) as d:
+        for rows, cols in ((1, 1), (5, 333), (64, 4096), (300, 17)):
+            X = rng.normal(0, 2, (rows, cols)).astype(np.float32)
+            X.flat[: min(4, X.size)] = [0.5, -1.5, np.nan, -0.0][: min(4, X.size)]
+            for axis in (0, 1, 2):
+                Yo, so = oracle.quantize(X, axis)
+                Y = np.empty_like(Yo)
+                s = np.empty_like(so)
+                d.quantize_i8(X, Y, s, rows, cols, axis)
+                assert bits_equal(Y, Yo) and bits_equal(s, so), (rows, cols, axis)
+
+
+@pytest.mark.parametrize("isa,threads,M,K,N,epi,form", [
+    ("avx2", 8, 64, 512, 512, 2, 0),     # packed panel, 2x32 blocks: block form
+    ("avx2", 8, 4, 1024, 256, 3, 0),     # decode 64-column packed tiles
+    ("avx2", 8, 1, 1024, 512, 2, 2),     # rank-1 stream
+    ("avx2", 1, 2, 256, 2048, 1, 2),     # rank-2 stream (column slice >= 1024)
+    ("scalar", 4, 37, 129, 70, 2, 1),
+    ("scalar", 4, 3, 64, 2048, 4, 1),
+])
+def test_matmul_vs_reference(ref_lib, oracle, isa, threads, M, K, N, epi, form):
+    rng = np.random.default_rng(M * 7 + N)
+    A, sa = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
+    B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
+    bias = rng.normal(0, 0.5, N).astype(np.float32)
+    with _ref_device(ref_lib, isa, threads) as d:
+        w = d.pack(B, sb, K, N)
+        C = np.empty((M, N), np.float32)
+        d.matmul_i8(A, w, sa, bias, C, M, K, N, epilogue=epi, unit=vnpu.UNIT_VOODOO)
+        d.unpack(w)
+    assert bits_equal(C, oracle.matmul_i8(A, B, sa, sb, bias, epi, form))
+
+
+def test_no_bias_is_form_free(ref_lib, oracle):
+    """Without bias and with NONE/RELU every reference path gives one answer."""
+    rng = np.random.default_rng(99)
+    M, K, N = 19, 47, 31
+    A, sa = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
+    B, sb = oracle.quantize(rng.uniform(-1, 1, (K, N)).astype(np.float32), 1)
+    ref = oracle.matmul_i8(A, B, sa, sb, None, 0, 0)
+    for form in (1, 2):
+        assert bits_equal(oracle.matmul_i8(A, B, sa, sb, None, 0, form), ref)
+    for isa in ("avx2", "scalar"):
+        for threads in (1, 2):
+            with _ref_device(ref_lib, isa, threads) as d:
+                w = d.pack(B, sb, K, N)
+                for unit in (vnpu.UNIT_AUTO, vnpu.UNIT_VOODOO, vnpu.UNIT_WILDCAT, vnpu.UNIT_CELL):
+                    C = np.empty((M, N), np.float32)
+                    d.matmul_i8(A, w, sa, None, C, M, K, N, unit=unit)
+                    assert bits_equal(C, ref), (isa, threads, unit)
+                d.unpack(w)
+
+
+def test_column_sums_vs_reference(ref_lib, oracle):
+    rng = np.random.default_rng(4)
+    K, N = 77, 45
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    sums, _ = oracle.column_sums(B)
+    with _ref_device(ref_lib, "avx2", 2) as d:
+        w = d.pack(B, None, K, N)
+        Kr, Nr, _, sc_ptr, cs_ptr = d.packed_info(w)
+        import ctypes as C
+        cs = np.ctypeslib.as_array(C.cast(cs_ptr, C.POINTER(C.c_int32)), (N,)).copy()
+        sc = np.ctypeslib.as_array(C.cast(sc_ptr, C.POINTER(C.c_float)), (N,)).copy()
+        d.unpack(w)
+    assert (Kr, Nr) == (K, N)
+    assert np.array_equal(cs, sums)
+    assert np.all(sc == 1.0)  # scales NULL -> 1.0 (src/core/scheduler.cpp:795)
+
+
+@pytest.mark.parametrize("H,sq,sk,D", [(2, 40, 40, 128), (4, 1, 200, 64), (1, 33, 70, 24)])
+def test_block_ops_vs_reference(ref_lib, oracle, H, sq, sk, D):
+    rng = np.random.default_rng(H * 1000 + sq + sk)
+    with _ref_device(ref_lib, "avx2", 4) as d:
+        Q = rng.normal(0, 1, (1, H, sq, D)).astype(np.float32)
+        K = rng.normal(0, 1, (1, H, sk, D)).astype(np.float32)
+        V = rng.normal(0, 1, (1, H, sk, D)).astype(np.float32)
+        O = np.empty((1, H, sq, D), np.float32)
+        d.attention(Q, K, V, None, O, 1, H, sq, sk, D, 1, 0.0)
+        assert bits_equal(O, oracle.attention(Q, K, V, None, 1, H, sq, sk, D, 1, 0.0))
+        X = rng.normal(0, 1, (sq, D * 8 + 3)).astype(np.float32)
+        Y = np.empty_like(X)
+        d.rmsnorm(X, None, Y, X.shape[0], X.shape[1], 1e-6)
+        assert bits_equal(Y, oracle.rmsnorm(X, None, 1e-6, 0))
