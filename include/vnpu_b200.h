@@ -67,6 +67,24 @@ VNPU_API const char * VNPU_CALL vnpu_b200_matmul_i8_kernel(uint32_t M, uint32_t 
 VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_selftest_wait_timeout(vnpu_stream_t *stream,
                                                                 uint32_t timeout_us);
 
+/*
+ * CUDA-graph capture of a command stream (no reference counterpart: the
+ * reference's stream worker has no launch cost to amortise).  Commands
+ * submitted between capture_begin and capture_end are recorded, not run;
+ * graph_launch replays them on any stream of the same device with one launch.
+ * While capturing, every operand must already be in device memory (host
+ * operands would need a host copy at replay time): such commands, and
+ * PACK_WEIGHTS_I8, fail with VNPU_ERR_INVALID_ARGUMENT, and vnpu_stream_sync
+ * returns VNPU_ERR_DEVICE_BUSY.  Packed weights used by a graph must outlive it.
+ */
+typedef struct vnpu_b200_graph vnpu_b200_graph_t;
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_capture_begin(vnpu_stream_t *stream);
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_capture_end(vnpu_stream_t *stream,
+                                                      vnpu_b200_graph_t **out_graph);
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_graph_launch(vnpu_b200_graph_t *graph,
+                                                       vnpu_stream_t *stream);
+VNPU_API void VNPU_CALL vnpu_b200_graph_destroy(vnpu_b200_graph_t *graph);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

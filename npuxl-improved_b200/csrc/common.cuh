@@ -45,13 +45,20 @@ __device__ __forceinline__ float exp2_poly(float f, bool fused) {
 
 // fast_expf (internal.h:87-108): cut-offs at +-80, z = x*log2e, split into
 // floor and fraction, polynomial, exact scaling by 2^floor.
+// p * 2^n for n in [-126, 127] and p in [1, 2): one exact multiply (the
+// power of two is a normal float, the product neither overflows nor goes
+// subnormal), the same value ldexp gives.
+__device__ __forceinline__ float scale_pow2(float p, int n) {
+    return __fmul_rn(p, __int_as_float((n + 127) << 23));
+}
+
 __device__ __forceinline__ float ref_fast_expf(float x, bool fused) {
     if (x < -80.0f) return 0.0f;
     if (x > 80.0f) return __int_as_float(0x7f800000);
     const float z = __fmul_rn(x, 1.4426950408889634f);
-    const float zi = floorf(z);
+    const float zi = floorf(z);  // in [-116, 115] here
     const float f = __fsub_rn(z, zi);
-    return ldexpf(exp2_poly(f, fused), __float2int_rz(zi));
+    return scale_pow2(exp2_poly(f, fused), __float2int_rz(zi));
 }
 
 // exp256_ps (src/kernels/llm.cpp:32-56): clamps to [-80,80] instead; for the
@@ -61,7 +68,7 @@ __device__ __forceinline__ float ref_exp256_lane(float x) {
     const float z = __fmul_rn(x, 1.4426950408889634f);
     const float zi = floorf(z);
     const float f = __fsub_rn(z, zi);
-    return ldexpf(exp2_poly(f, true), __float2int_rz(zi));
+    return scale_pow2(exp2_poly(f, true), __float2int_rz(zi));
 }
 
 __device__ __forceinline__ float ref_silu(float x, bool fused) {
@@ -287,6 +294,86 @@ __host__ __device__ constexpr uint32_t umma_idesc_i8(uint32_t m, uint32_t n) {
            | (1u << 10)         // B format: signed 8-bit
            | ((n >> 3) << 17)   // N / 8
            | ((m >> 4) << 24);  // M / 16
+}
+
+// ---------------------------------------------------------------------------
+// Clusters and cta_group::2 (a pair of CTAs on two SMs sharing one MMA)
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Address of the same shared variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t local_addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+    return r;
+}
+
+// Arrive on an mbarrier of another CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+                 : "memory");
+}
+
+// All threads of all CTAs of the cluster.  Only used where every thread of
+// the pair is guaranteed to arrive (kernel start, and the end after every
+// bounded wait has returned).
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// 2-D tiled load into this CTA's shared memory whose completion is counted
+// on the leader CTA's mbarrier (cluster address), for cta_group::2 MMAs.
+// No multicast: each CTA loads its own tile.
+__device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const void *tmap,
+                                                 uint32_t leader_bar, int32_t x, int32_t y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(leader_bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *smem_result, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(smem_result)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+
+// Pair MMA: issued by the leader CTA only; A rows and B columns come half
+// from each CTA's shared memory at the same offsets; each CTA's tensor memory
+// receives its 128 rows of D.
+__device__ __forceinline__ void umma_i8_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive on `bar` in every CTA of `cta_mask` when the pair MMAs issued so far
+// complete.
+__device__ __forceinline__ void umma_commit_pair_mc(uint64_t *bar, uint16_t cta_mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+        " [%0], %1;" ::"r"(smem_addr(bar)),
+        "h"(cta_mask)
+        : "memory");
 }
 
 }  // namespace vnpu_b200

@@ -82,6 +82,37 @@ __device__ __forceinline__ void tile_coords(uint32_t t, uint32_t tiles_m, uint32
     nb = r / rows;
 }
 
+// Dequantise 32 accumulators (columns n0..n0+31 of one row) and store them.
+// vec: C row 16-byte aligned, ldc % 4 == 0, bias NULL or 16-byte aligned.
+__device__ __forceinline__ void store_chunk32(const uint32_t (&r)[32], float *crow, uint32_t n0,
+                                              uint32_t N, float sa, const float *scale_b,
+                                              const float *bias, uint32_t epilogue,
+                                              uint32_t form, bool vec) {
+    const bool has_bias = bias != nullptr;
+    if (vec && n0 + 32u <= N) {
+#pragma unroll
+        for (uint32_t j = 0; j < 32u; j += 4u) {
+            const float4 sb = __ldg(reinterpret_cast<const float4 *>(scale_b + n0 + j));
+            const float4 bb = has_bias ? __ldg(reinterpret_cast<const float4 *>(bias + n0 + j))
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 o;
+            o.x = ref_dequant(static_cast<int32_t>(r[j + 0]), sa, sb.x, has_bias, bb.x, epilogue, form);
+            o.y = ref_dequant(static_cast<int32_t>(r[j + 1]), sa, sb.y, has_bias, bb.y, epilogue, form);
+            o.z = ref_dequant(static_cast<int32_t>(r[j + 2]), sa, sb.z, has_bias, bb.z, epilogue, form);
+            o.w = ref_dequant(static_cast<int32_t>(r[j + 3]), sa, sb.w, has_bias, bb.w, epilogue, form);
+            *reinterpret_cast<float4 *>(crow + n0 + j) = o;
+        }
+        return;
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < 32u; ++j) {
+        const uint32_t n = n0 + j;
+        if (n < N)
+            crow[n] = ref_dequant(static_cast<int32_t>(r[j]), sa, __ldg(scale_b + n), has_bias,
+                                  has_bias ? __ldg(bias + n) : 0.0f, epilogue, form);
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a,
                            const __grid_constant__ CUtensorMap tmap_b, const TcParams p) {
@@ -202,9 +233,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Warp w may only touch TMEM lanes 32*(w%4) .. +31.
         const uint32_t lane_base = (warp & 3u) * 32u;
         const uint32_t row = lane_base + lane;
-        const bool has_bias = p.bias != nullptr;
         const bool vec_ok = (p.ldc % 4u == 0u) &&
-                            ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0u);
+                            ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0u) &&
+                            ((reinterpret_cast<uintptr_t>(p.bias) & 15u) == 0u);
         uint32_t tcount = 0;
         for (uint32_t t = blockIdx.x; t < total_tiles; t += gridDim.x, ++tcount) {
             uint32_t mb, nb;
@@ -231,39 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_wait_ld();
                 const uint32_t n0 = nb * kBN + c * 32u;
                 if (!row_ok || n0 >= p.N) continue;
-                if (vec_ok && n0 + 32u <= p.N) {
-#pragma unroll
-                    for (uint32_t j = 0; j < 32u; j += 4u) {
-                        float4 o;
-                        o.x = ref_dequant(static_cast<int32_t>(r[j + 0]), sa,
-                                          __ldg(p.scale_b + n0 + j + 0), has_bias,
-                                          has_bias ? __ldg(p.bias + n0 + j + 0) : 0.0f,
-                                          p.epilogue, p.form);
-                        o.y = ref_dequant(static_cast<int32_t>(r[j + 1]), sa,
-                                          __ldg(p.scale_b + n0 + j + 1), has_bias,
-                                          has_bias ? __ldg(p.bias + n0 + j + 1) : 0.0f,
-                                          p.epilogue, p.form);
-                        o.z = ref_dequant(static_cast<int32_t>(r[j + 2]), sa,
-                                          __ldg(p.scale_b + n0 + j + 2), has_bias,
-                                          has_bias ? __ldg(p.bias + n0 + j + 2) : 0.0f,
-                                          p.epilogue, p.form);
-                        o.w = ref_dequant(static_cast<int32_t>(r[j + 3]), sa,
-                                          __ldg(p.scale_b + n0 + j + 3), has_bias,
-                                          has_bias ? __ldg(p.bias + n0 + j + 3) : 0.0f,
-                                          p.epilogue, p.form);
-                        *reinterpret_cast<float4 *>(crow + n0 + j) = o;
-                    }
-                } else {
-#pragma unroll
-                    for (uint32_t j = 0; j < 32u; ++j) {
-                        const uint32_t n = n0 + j;
-                        if (n < p.N)
-                            crow[n] = ref_dequant(static_cast<int32_t>(r[j]), sa,
-                                                  __ldg(p.scale_b + n), has_bias,
-                                                  has_bias ? __ldg(p.bias + n) : 0.0f,
-                                                  p.epilogue, p.form);
-                    }
-                }
+                store_chunk32(r, crow, n0, p.N, sa, p.scale_b, p.bias, p.epilogue, p.form, vec_ok);
             }
             tc_fence_before();
             __syncwarp();
@@ -277,6 +276,204 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ===========================================================================
+// tcgen05 pair GEMM (cta_group::2): a cluster of two CTAs on two SMs computes
+// one 256x256 output tile.  CTA r holds rows [128r, 128r+128) of the A tile
+// and columns [128r, 128r+128) of the B tile in its own shared memory; the
+// leader (r = 0) issues tcgen05.mma.cta_group::2 with M=256, N=256, which
+// reads both halves and writes each CTA's 128 rows of D into that CTA's
+// tensor memory.  Per SM that is 32 KiB of operands per 128-deep K step
+// instead of 48 KiB for the 128x256 single-CTA tile.
+//   barriers: full[s] (leader only) counts both CTAs' TMA bytes;
+//             empty[s] (both) is arrived by the leader's commit, multicast;
+//             tmem_full[a] (both) likewise; tmem_empty[a] (leader) gets one
+//             arrival from each of the 16 epilogue warps of the pair.
+// No TMA multicast anywhere: each CTA loads only its own tiles.
+// ===========================================================================
+
+constexpr uint32_t kPStages = 6;
+constexpr uint32_t kPTileM = 256;                 // per pair
+constexpr uint32_t kPTileN = 256;                 // per pair
+constexpr uint32_t kPABytes = 128 * kBK;          // 16 KiB per CTA
+constexpr uint32_t kPBBytes = 128 * kBK;          // 16 KiB per CTA
+constexpr uint32_t kPStageBytes = kPABytes + kPBBytes;
+constexpr uint32_t kPEpiWarps = 8;                // per CTA
+constexpr uint32_t kPThreads = (2 + kPEpiWarps) * 32;
+constexpr uint32_t kPSmemBytes = kPStages * kPStageBytes + 1024;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
+    gemm_i8_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                const __grid_constant__ CUtensorMap tmap_b, const TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[kPStages];
+    __shared__ __align__(8) uint64_t empty_bar[kPStages];
+    __shared__ __align__(8) uint64_t tmem_full_bar[2];
+    __shared__ __align__(8) uint64_t tmem_empty_bar[2];
+    __shared__ __align__(8) uint64_t drain_bar;
+    __shared__ uint32_t tmem_base_slot;
+    __shared__ volatile int abort_flag;
+
+    const uint32_t raw_addr = smem_addr(smem_raw);
+    uint8_t *ring = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+
+    const uint32_t warp = threadIdx.x >> 5;
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const uint32_t pair = blockIdx.x >> 1;
+    const uint32_t npairs = gridDim.x >> 1;
+    const uint32_t total_tiles = p.tiles_m * p.tiles_n;   // 256x256 tiles
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < kPStages; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (uint32_t a = 0; a < 2; ++a) {
+            mbar_init(&tmem_full_bar[a], 1);
+            mbar_init(&tmem_empty_bar[a], 2 * kPEpiWarps);
+        }
+        mbar_init(&drain_bar, 1);
+        abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmap_a);
+        tma_prefetch_desc(&tmap_b);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(&tmem_base_slot, kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();   // both CTAs' barriers initialised, tensor memory allocated
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_base_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer (both CTAs)
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (uint32_t t = pair; t < total_tiles && ok; t += npairs) {
+                uint32_t mb, nb;
+                tile_coords(t, p.tiles_m, p.tiles_n, mb, nb);
+                for (uint32_t kb = 0; kb < p.num_kb; ++kb, ++it) {
+                    const uint32_t s = it % kPStages;
+                    const uint32_t ph = (it / kPStages) & 1u;
+                    if (!mbar_wait(&empty_bar[s], ph ^ 1u, p.limit_ns, p.err, &abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    // The leader's full barrier counts both CTAs' bytes.
+                    if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * kPStageBytes);
+                    const uint32_t leader_full = mapa_shared(smem_addr(&full_bar[s]), 0);
+                    uint8_t *sa = ring + s * kPStageBytes;
+                    uint8_t *sb = sa + kPABytes;
+                    tma_load_2d_pair(sa, &tmap_a, leader_full, static_cast<int32_t>(kb * kBK),
+                                     static_cast<int32_t>(mb * kPTileM + rank * 128u));
+                    tma_load_2d_pair(sb, &tmap_b, leader_full, static_cast<int32_t>(kb * kBK),
+                                     static_cast<int32_t>(nb * kPTileN + rank * 128u));
+                }
+            }
+            // The leader never leaves with copies in flight (its full barriers
+            // count the peer's bytes too).
+            if (rank == 0) {
+                const uint32_t tail = it < kPStages ? it : kPStages;
+                for (uint32_t i = it - tail; i < it; ++i)
+                    mbar_wait(&full_bar[i % kPStages], (i / kPStages) & 1u, p.limit_ns, p.err,
+                              nullptr);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer (leader)
+        if (rank == 0 && lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_i8(kPTileM, kPTileN);
+            uint32_t it = 0, tcount = 0;
+            bool ok = true;
+            for (uint32_t t = pair; t < total_tiles && ok; t += npairs, ++tcount) {
+                const uint32_t acc = tcount & 1u;
+                const uint32_t use = tcount >> 1;
+                if (!mbar_wait(&tmem_empty_bar[acc], (use & 1u) ^ 1u, p.limit_ns, p.err,
+                               &abort_flag))
+                    break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * kPTileN;
+                for (uint32_t kb = 0; kb < p.num_kb; ++kb, ++it) {
+                    const uint32_t s = it % kPStages;
+                    const uint32_t ph = (it / kPStages) & 1u;
+                    if (!mbar_wait(&full_bar[s], ph, p.limit_ns, p.err, &abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_addr(ring + s * kPStageBytes);
+                    const uint64_t adesc = umma_desc_k_sw128(sa);
+                    const uint64_t bdesc = umma_desc_k_sw128(sa + kPABytes);
+#pragma unroll
+                    for (uint32_t kk = 0; kk < kBK / kUmmaK; ++kk)
+                        umma_i8_pair(d_tmem, adesc + 2u * kk, bdesc + 2u * kk, idesc,
+                                     (kb | kk) != 0u);
+                    umma_commit_pair_mc(&empty_bar[s], 0x3);
+                }
+                if (!ok) break;
+                umma_commit_pair_mc(&tmem_full_bar[acc], 0x3);
+            }
+            umma_commit_pair_mc(&drain_bar, 0x1);
+            mbar_wait(&drain_bar, 0, p.limit_ns, p.err, nullptr);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue (both CTAs)
+        // Warp w reads TMEM lanes 32*(w%4)..+31; warps 2-5 take columns
+        // 0-127 of the tile, warps 6-9 columns 128-255.
+        const uint32_t lane_base = (warp & 3u) * 32u;
+        const uint32_t col_base = ((warp - 2u) >> 2) * 128u;
+        const uint32_t row = rank * 128u + lane_base + lane;
+        const bool vec_ok = (p.ldc % 4u == 0u) &&
+                            ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0u) &&
+                            ((reinterpret_cast<uintptr_t>(p.bias) & 15u) == 0u);
+        const uint32_t leader_empty0 = mapa_shared(smem_addr(&tmem_empty_bar[0]), 0);
+        const uint32_t leader_empty1 = mapa_shared(smem_addr(&tmem_empty_bar[1]), 0);
+        uint32_t tcount = 0;
+        for (uint32_t t = pair; t < total_tiles; t += npairs, ++tcount) {
+            uint32_t mb, nb;
+            tile_coords(t, p.tiles_m, p.tiles_n, mb, nb);
+            const uint32_t acc = tcount & 1u;
+            const uint32_t use = tcount >> 1;
+            uint32_t ok = 0;
+            if (lane == 0)
+                ok = mbar_wait(&tmem_full_bar[acc], use & 1u, p.limit_ns, p.err, &abort_flag);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t m = mb * kPTileM + row;
+            const bool row_ok = m < p.M;
+            const float sa = row_ok ? (p.scale_a ? __ldg(p.scale_a + m) : 1.0f) : 0.0f;
+            float *crow = p.C + static_cast<uint64_t>(row_ok ? m : 0) * p.ldc;
+#pragma unroll 1
+            for (uint32_t c = 0; c < 4u; ++c) {
+                uint32_t r[32];
+                const uint32_t col = col_base + c * 32u;
+                __syncwarp();
+                tmem_ld_32cols(tmem_base + (lane_base << 16) + acc * kPTileN + col, r);
+                tmem_wait_ld();
+                const uint32_t n0 = nb * kPTileN + col;
+                if (!row_ok || n0 >= p.N) continue;
+                store_chunk32(r, crow, n0, p.N, sa, p.scale_b, p.bias, p.epilogue, p.form, vec_ok);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc ? leader_empty1 : leader_empty0);
+        }
+    }
+
+    // ---------------------------------------------------------------- teardown
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();   // the peer's smem / TMEM are no longer in use by the pair MMA
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, kTmemCols);
     }
 }
 
@@ -539,16 +736,86 @@ const char *matmul_kernel_name(MatmulKernel k) {
     }
 }
 
-cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_i8_tcgen05_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kSmemBytes));
-        if (e != cudaSuccess) return e;
-        attr_set = true;
+namespace {
+
+// Per-device one-time kernel set-up: shared-memory opt-in and the number of
+// co-resident CTA pairs.
+struct DeviceSetup {
+    bool done = false;
+    int max_pairs = 0;
+};
+DeviceSetup g_setup[64];
+std::mutex g_setup_mutex;
+
+cudaError_t device_setup(int &max_pairs) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64) return e != cudaSuccess ? e : cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> l(g_setup_mutex);
+    DeviceSetup &d = g_setup[dev];
+    if (!d.done) {
+        if ((e = cudaFuncSetAttribute(gemm_i8_tcgen05_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(kSmemBytes))) != cudaSuccess)
+            return e;
+        if ((e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(kPSmemBytes))) != cudaSuccess)
+            return e;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2, 1, 1);
+        cfg.blockDim = dim3(kPThreads, 1, 1);
+        cfg.dynamicSmemBytes = kPSmemBytes;
+        int clusters = 0;
+        if ((e = cudaOccupancyMaxActiveClusters(&clusters, gemm_i8_tcgen05_pair_kernel, &cfg)) !=
+            cudaSuccess)
+            return e;
+        d.max_pairs = clusters;
+        d.done = true;
     }
+    max_pairs = d.max_pairs;
+    return cudaSuccess;
+}
+
+}  // namespace
+
+cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
+    int max_pairs = 0;
+    cudaError_t se = device_setup(max_pairs);
+    if (se != cudaSuccess) return se;
     if (!p.tmap_b) return cudaErrorInvalidValue;
+    // Pairs of CTAs (256x256 tiles) whenever M fills more than one 128-row
+    // tile; the single-CTA 128x256 kernel otherwise.
+    const bool use_pair = p.M > kBM && p.tmap_b128 && max_pairs > 0 &&
+                          std::getenv("VNPU_B200_NO_PAIR") == nullptr;
+    if (use_pair) {
+        CUtensorMap tmap_a;
+        if (!encode_tmap_kmajor_i8(&tmap_a, p.A, p.K, p.M, p.lda, kBK, 128))
+            return cudaErrorInvalidValue;
+        TcParams tp;
+        tp.scale_a = p.scale_a;
+        tp.scale_b = p.scale_b;
+        tp.bias = p.bias;
+        tp.C = p.C;
+        tp.ldc = p.ldc;
+        tp.M = p.M;
+        tp.N = p.N;
+        tp.K = p.K;
+        tp.tiles_m = (p.M + kPTileM - 1) / kPTileM;
+        tp.tiles_n = (p.N + kPTileN - 1) / kPTileN;
+        tp.num_kb = (p.K + kBK - 1) / kBK;
+        tp.epilogue = p.epilogue;
+        tp.form = p.form;
+        tp.err = ctx.err;
+        tp.limit_ns = ctx.wait_limit_ns;
+        const uint32_t tiles = tp.tiles_m * tp.tiles_n;
+        const uint32_t pairs = tiles < static_cast<uint32_t>(max_pairs) ? tiles
+                                                                         : static_cast<uint32_t>(max_pairs);
+        gemm_i8_tcgen05_pair_kernel<<<2 * pairs, kPThreads, kPSmemBytes, ctx.stream>>>(
+            tmap_a, *p.tmap_b128, tp);
+        count_launch(ctx);
+        return cudaGetLastError();
+    }
     CUtensorMap tmap_a;
     if (!encode_tmap_kmajor_i8(&tmap_a, p.A, p.K, p.M, p.lda, kBK, kBM))
         return cudaErrorInvalidValue;

@@ -61,7 +61,8 @@ struct MatmulI8 {
     uint32_t M = 0, K = 0, N = 0;
     uint32_t epilogue = 0;
     uint32_t form = 0;              // EpiForm
-    const CUtensorMap *tmap_b = nullptr;  // TMA map of Bt (box 128 x 256, SW128)
+    const CUtensorMap *tmap_b = nullptr;     // TMA map of Bt (box 128 x 256, SW128)
+    const CUtensorMap *tmap_b128 = nullptr;  // same, box 128 x 128 (CTA-pair kernel)
 };
 
 enum class MatmulKernel { kTcgen05, kGemv, kSimt };

@@ -105,7 +105,8 @@ Mem classify(const void *p, int device) {
 
 class Staging {
 public:
-    Staging(cudaStream_t s, int device) : s_(s), device_(device) {}
+    Staging(cudaStream_t s, int device, bool capturing = false)
+        : s_(s), device_(device), capturing_(capturing) {}
     ~Staging() {
         for (auto &a : allocs_) cudaFreeAsync(a, s_);
     }
@@ -136,6 +137,8 @@ private:
         if (m == Mem::kDevice) return p;
         if (m == Mem::kForeign)
             throw CommandError("operand lives on another GPU", VNPU_ERR_INVALID_ARGUMENT);
+        if (capturing_)
+            throw CommandError("host operand inside a graph capture", VNPU_ERR_INVALID_ARGUMENT);
         auto it = map_.find(p);
         if (it != map_.end()) {
             if (copy_out) outs_.push_back({p, it->second, bytes});
@@ -157,6 +160,7 @@ private:
     };
     cudaStream_t s_;
     int device_;
+    bool capturing_;
     std::vector<void *> allocs_;
     std::vector<Out> outs_;
     std::unordered_map<void *, void *> map_;
@@ -208,7 +212,7 @@ void exec_matmul_i8(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags,
     const uint32_t lda = in.lda ? in.lda : in.K;
     const uint32_t ldc = in.ldc ? in.ldc : in.N;
     if (lda < in.K || ldc < in.N) throw CommandError("invalid int8 leading dimensions");
-    Staging st(s->cs, s->device->ordinal);
+    Staging st(s->cs, s->device->ordinal, s->capturing);
     MatmulI8 p;
     p.A = st.in(in.A, static_cast<uint64_t>(in.M - 1) * lda + in.K);
     p.lda = lda;
@@ -226,6 +230,7 @@ void exec_matmul_i8(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags,
     p.epilogue = in.epilogue;
     p.form = epi_form_for(s->device, flags);
     p.tmap_b = w->tmap_ok ? &w->tmap : nullptr;
+    p.tmap_b128 = w->tmap128_ok ? &w->tmap128 : nullptr;
     cuda_check(matmul_i8(ctx, p), "matmul_i8 launch");
     st.finish();
     const uint64_t a_bytes = static_cast<uint64_t>(in.M) * in.K;
@@ -249,7 +254,7 @@ void exec_quantize_i8(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchC
     const uint64_t nscales = a.axis == VNPU_QUANT_PER_ROW      ? a.rows
                              : a.axis == VNPU_QUANT_PER_COLUMN ? a.cols
                                                                : 1;
-    Staging st(s->cs, s->device->ordinal);
+    Staging st(s->cs, s->device->ordinal, s->capturing);
     const float *X = st.in(a.X, total * sizeof(float));
     int8_t *Y = st.out(a.Y, total, false);
     float *sc = st.out(a.scales, nscales * sizeof(float), false);
@@ -274,7 +279,7 @@ void exec_rmsnorm(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &
     const auto &a = cmd.args.rmsnorm;
     if (!a.X || !a.Y || !a.rows || !a.cols) throw CommandError("invalid rmsnorm arguments");
     const uint64_t n = static_cast<uint64_t>(a.rows) * a.cols;
-    Staging st(s->cs, s->device->ordinal);
+    Staging st(s->cs, s->device->ordinal, s->capturing);
     float *Y = st.out(a.Y, n * sizeof(float), a.Y == a.X);
     const float *X = st.in(a.X, n * sizeof(float));
     const float *W = st.in(a.W, sizeof(float) * a.cols);
@@ -309,7 +314,7 @@ void exec_rope(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &ctx
     const uint64_t qn = static_cast<uint64_t>(a.batch) * a.heads * a.q_seq * a.head_dim;
     const uint64_t kn = static_cast<uint64_t>(a.batch) * a.heads * a.k_seq * a.head_dim;
     const uint32_t seq = std::max(a.q_seq, a.k_seq);
-    Staging st(s->cs, s->device->ordinal);
+    Staging st(s->cs, s->device->ordinal, s->capturing);
     float *Q = st.out(a.Q, qn * sizeof(float), true);
     float *K = st.out(a.K, kn * sizeof(float), true);
     const int32_t *pos = st.in(a.positions, sizeof(int32_t) * seq);
@@ -330,7 +335,7 @@ void exec_swiglu(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &c
     const auto &a = cmd.args.swiglu;
     if (!a.gate || !a.up || !a.Y || !a.count) throw CommandError("invalid swiglu arguments");
     const uint64_t bytes = a.count * sizeof(float);
-    Staging st(s->cs, s->device->ordinal);
+    Staging st(s->cs, s->device->ordinal, s->capturing);
     float *Y = st.out(a.Y, bytes, a.Y == a.gate || a.Y == a.up);
     const float *G = st.in(a.gate, bytes);
     const float *U = st.in(a.up, bytes);
@@ -349,7 +354,7 @@ void exec_add(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &ctx,
     if (!a.A || !a.B || !a.Y || !a.count) throw CommandError("invalid binary arguments");
     const bool dflt = a.alpha == 0.0f && a.beta == 0.0f;
     const uint64_t bytes = a.count * sizeof(float);
-    Staging st(s->cs, s->device->ordinal);
+    Staging st(s->cs, s->device->ordinal, s->capturing);
     float *Y = st.out(a.Y, bytes, a.Y == a.A || a.Y == a.B);
     const float *A = st.in(a.A, bytes);
     const float *B = st.in(a.B, bytes);
@@ -377,7 +382,7 @@ void exec_attention(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx
     const uint64_t mn = a.mask ? bh * a.seq_q * a.seq_k : 0;
     const float scale =
         a.scale > 0.0f ? a.scale : 1.0f / std::sqrt(static_cast<float>(a.head_dim));
-    Staging st(s->cs, s->device->ordinal);
+    Staging st(s->cs, s->device->ordinal, s->capturing);
     float *O = st.out(a.O, qn * sizeof(float), false);
     const float *Q = st.in(a.Q, qn * sizeof(float));
     const float *K = st.in(a.K, kn * sizeof(float));
@@ -406,6 +411,8 @@ void exec_copy(vnpu_stream_t *s, const vnpu_command_t &cmd, Accounting &acc) {
 void exec_memset(vnpu_stream_t *s, const vnpu_command_t &cmd, Accounting &acc) {
     const auto &a = cmd.args.memset;
     if (!a.dst || !a.bytes) throw CommandError("invalid memset arguments");
+    if (s->capturing && classify(a.dst, s->device->ordinal) != Mem::kDevice)
+        throw CommandError("host memset inside a graph capture", VNPU_ERR_INVALID_ARGUMENT);
     if (classify(a.dst, s->device->ordinal) == Mem::kDevice) {
         cuda_check(cudaMemsetAsync(a.dst, static_cast<int>(a.value & 0xffu), a.bytes, s->cs),
                    "memset");
@@ -421,6 +428,8 @@ void exec_memset(vnpu_stream_t *s, const vnpu_command_t &cmd, Accounting &acc) {
 void exec_pack(vnpu_stream_t *s, const vnpu_command_t &cmd, Accounting &acc) {
     const auto &a = cmd.args.pack_weights_i8;
     if (!a.B || !a.out || !a.K || !a.N) throw CommandError("invalid pack_weights arguments");
+    if (s->capturing)
+        throw CommandError("PACK_WEIGHTS_I8 inside a graph capture", VNPU_ERR_INVALID_ARGUMENT);
     // Stream order: everything before this command must have produced B.
     cuda_check(cudaStreamSynchronize(s->cs), "pack order");
     vnpu_packed_weights_t *w = nullptr;
@@ -447,7 +456,7 @@ vnpu_status_t execute_command(vnpu_stream_t *s, const vnpu_command_t &cmd, uint3
         category = 1;
     else if (cmd.opcode == VNPU_OP_BARRIER || cmd.opcode == VNPU_OP_NOP)
         category = 2;
-    if (tracing) {
+    if (tracing && !s->capturing) {
         pt.ev.name = std::string(opcode_name(cmd.opcode)) + "#" + std::to_string(cmd.id);
         pt.ev.opcode = cmd.opcode;
         pt.ev.unit = cmd.opcode == VNPU_OP_MATMUL_I8 ? VNPU_UNIT_GPU : VNPU_UNIT_GPU;
@@ -483,7 +492,10 @@ vnpu_status_t execute_command(vnpu_stream_t *s, const vnpu_command_t &cmd, uint3
         return VNPU_OK;
     });
     const uint64_t host_ns = now_ns() - t0;
-    dev->launches.fetch_add(launched);
+    if (s->capturing)
+        s->captured_launches += launched;  // counted when the graph is replayed
+    else
+        dev->launches.fetch_add(launched);
     dev->dispatch_ns.fetch_add(host_ns);
     if (category == 1) dev->memory_ns.fetch_add(host_ns);
     dev->bytes_read.fetch_add(acc.bytes_read);
@@ -491,7 +503,7 @@ vnpu_status_t execute_command(vnpu_stream_t *s, const vnpu_command_t &cmd, uint3
     dev->flops.fetch_add(acc.flops);
     dev->tiles_dispatched.fetch_add(acc.tiles);
     dev->dma_bytes.fetch_add(acc.dma);
-    if (tracing) {
+    if (tracing && !s->capturing) {
         cudaEventRecord(pt.end, s->cs);
         pt.ev.bytes_read = acc.bytes_read;
         pt.ev.bytes_written = acc.bytes_written;
@@ -984,6 +996,7 @@ VNPU_API void VNPU_CALL vnpu_stream_destroy(vnpu_stream_t *stream) {
 VNPU_API vnpu_status_t VNPU_CALL vnpu_stream_sync(vnpu_stream_t *stream) {
     if (!stream) return VNPU_ERR_INVALID_ARGUMENT;
     std::lock_guard<std::mutex> l(stream->mutex);
+    if (stream->capturing) return VNPU_ERR_DEVICE_BUSY;
     return stream_sync_impl(stream);
 }
 
@@ -1245,6 +1258,8 @@ VNPU_API vnpu_status_t VNPU_CALL vnpu_pack_weights_i8(vnpu_device_t *device, con
         if ((e = cudaStreamSynchronize(device->aux)) != cudaSuccess) return fail(e);
         device->launches.fetch_add(launched);
         w->tmap_ok = encode_tmap_kmajor_i8(&w->tmap, w->bt, w->k_stride, N, w->k_stride, 128, 256);
+        w->tmap128_ok =
+            encode_tmap_kmajor_i8(&w->tmap128, w->bt, w->k_stride, N, w->k_stride, 128, 128);
         device->dma_bytes.fetch_add(static_cast<uint64_t>(K) * N * 2);
         *out_weights = w.release();
         return VNPU_OK;
@@ -1373,6 +1388,79 @@ VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_selftest_wait_timeout(vnpu_stream_t *
     if (cudaStreamSynchronize(stream->cs) != cudaSuccess) return VNPU_ERR_DEVICE_ERROR;
     const uint32_t err = take_device_error(stream);
     return (err & kErrWaitTimeout) ? VNPU_ERR_TIMEOUT : (err ? VNPU_ERR_DEVICE_ERROR : VNPU_OK);
+}
+
+// ---------------------------------------------------------------- graph capture
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_capture_begin(vnpu_stream_t *stream) {
+    if (!stream) return VNPU_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> l(stream->mutex);
+    if (stream->capturing) return VNPU_ERR_DEVICE_BUSY;
+    cudaSetDevice(stream->device->ordinal);
+    // Work already queued must not be captured: let it finish first.
+    const vnpu_status_t rc = stream_sync_impl(stream);
+    if (rc != VNPU_OK) return rc;
+    if (cudaStreamBeginCapture(stream->cs, cudaStreamCaptureModeRelaxed) != cudaSuccess) {
+        cudaGetLastError();
+        return VNPU_ERR_DEVICE_ERROR;
+    }
+    stream->capturing = true;
+    stream->captured_launches = 0;
+    return VNPU_OK;
+}
+
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_capture_end(vnpu_stream_t *stream,
+                                                      vnpu_b200_graph_t **out_graph) {
+    if (!stream || !out_graph) return VNPU_ERR_INVALID_ARGUMENT;
+    *out_graph = nullptr;
+    std::lock_guard<std::mutex> l(stream->mutex);
+    if (!stream->capturing) return VNPU_ERR_INVALID_ARGUMENT;
+    cudaSetDevice(stream->device->ordinal);
+    stream->capturing = false;
+    cudaGraph_t g = nullptr;
+    if (cudaStreamEndCapture(stream->cs, &g) != cudaSuccess || !g) {
+        cudaGetLastError();
+        return VNPU_ERR_DEVICE_ERROR;
+    }
+    // Commands that failed validation while capturing left a sticky error.
+    if (stream->last_error.load()) {
+        cudaGraphDestroy(g);
+        return VNPU_ERR_DEVICE_ERROR;
+    }
+    cudaGraphExec_t exec = nullptr;
+    if (cudaGraphInstantiate(&exec, g, 0) != cudaSuccess) {
+        cudaGetLastError();
+        cudaGraphDestroy(g);
+        return VNPU_ERR_DEVICE_ERROR;
+    }
+    auto *graph = new vnpu_b200_graph_t();
+    graph->device = stream->device;
+    graph->graph = g;
+    graph->exec = exec;
+    graph->kernels = stream->captured_launches;
+    *out_graph = graph;
+    return VNPU_OK;
+}
+
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_graph_launch(vnpu_b200_graph_t *graph,
+                                                       vnpu_stream_t *stream) {
+    if (!graph || !stream || graph->device != stream->device) return VNPU_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> l(stream->mutex);
+    if (stream->capturing) return VNPU_ERR_DEVICE_BUSY;
+    cudaSetDevice(stream->device->ordinal);
+    if (cudaGraphLaunch(graph->exec, stream->cs) != cudaSuccess) {
+        cudaGetLastError();
+        return VNPU_ERR_DEVICE_ERROR;
+    }
+    stream->device->launches.fetch_add(graph->kernels);
+    return VNPU_OK;
+}
+
+VNPU_API void VNPU_CALL vnpu_b200_graph_destroy(vnpu_b200_graph_t *graph) {
+    if (!graph) return;
+    cudaSetDevice(graph->device->ordinal);
+    cudaGraphExecDestroy(graph->exec);
+    cudaGraphDestroy(graph->graph);
+    delete graph;
 }
 
 }  // extern "C"

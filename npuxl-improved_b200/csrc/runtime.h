@@ -92,7 +92,9 @@ struct vnpu_packed_weights {
     std::vector<int32_t> host_column_sums;
     uint32_t K = 0, N = 0, k_stride = 0;
     CUtensorMap tmap{};              // box 128 (K) x 256 (N), 128B swizzle
+    CUtensorMap tmap128{};           // box 128 (K) x 128 (N), for the CTA-pair kernel
     bool tmap_ok = false;
+    bool tmap128_ok = false;
 };
 
 struct vnpu_stream {
@@ -106,6 +108,15 @@ struct vnpu_stream {
     std::atomic<uint32_t> last_error{0};
     std::atomic<uint64_t> pending{0};
     std::vector<vnpu_b200::PendingTrace> traces;
+    bool capturing = false;          // inside vnpu_b200_capture_begin/end
+    uint64_t captured_launches = 0;  // kernels recorded by the capture
+};
+
+struct vnpu_b200_graph {
+    vnpu_device_t *device = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    uint64_t kernels = 0;  // kernel launches per replay
 };
 
 struct vnpu_device {

@@ -263,6 +263,10 @@ class Lib:
             self.b200_selftest_wait = _sig(h, "vnpu_b200_selftest_wait_timeout", _ST, vp, u32)
             self.b200_packed_device = _sig(h, "vnpu_b200_packed_weights_device", _ST, vp,
                                            C.POINTER(vp), C.POINTER(u32), C.POINTER(vp))
+            self.b200_capture_begin = _sig(h, "vnpu_b200_capture_begin", _ST, vp)
+            self.b200_capture_end = _sig(h, "vnpu_b200_capture_end", _ST, vp, C.POINTER(vp))
+            self.b200_graph_launch = _sig(h, "vnpu_b200_graph_launch", _ST, vp, vp)
+            self.b200_graph_destroy = _sig(h, "vnpu_b200_graph_destroy", None, vp)
 
     def check(self, rc: int, what: str):
         if rc != OK:
@@ -383,6 +387,19 @@ class Device:
     def submit(self, cmds, event=None) -> int:
         arr = (Command * len(cmds))(*cmds)
         return self.lib.stream_submit(self.stream, arr, len(cmds), event)
+
+    def capture(self, cmds) -> int:
+        """Record `cmds` (device operands only) as a CUDA graph; returns the handle."""
+        self.lib.check(self.lib.b200_capture_begin(self.stream), "capture_begin")
+        rc = self.submit(cmds)
+        g = vp()
+        rc2 = self.lib.b200_capture_end(self.stream, C.byref(g))
+        self.lib.check(rc, "submit while capturing")
+        self.lib.check(rc2, "capture_end")
+        return g.value
+
+    def replay(self, graph: int) -> None:
+        self.lib.check(self.lib.b200_graph_launch(graph, self.stream), "graph_launch")
 
 
 # ---------------------------------------------------------------------------

@@ -265,3 +265,51 @@ def test_mmio_window(gpu, b200_lib):
     assert h.vnpu_mmio_read32(gpu.dev, 0x00) == 0x56504E55
     assert h.vnpu_mmio_read32(gpu.dev, 0x04) == 1
     assert h.vnpu_mmio_read32(gpu.dev, 0x03) == 0xFFFFFFFF
+
+
+def test_graph_capture_replay(gpu, b200_lib, oracle):
+    """Commands captured into a CUDA graph replay to the same bits; host
+    operands and syncs are refused while capturing."""
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(21)
+    M, K, N = 300, 512, 384
+    Xf = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
+    A, sa = oracle.quantize(Xf, 0)
+    ref = oracle.matmul_i8(A, B, sa, sb, None, 2, 0)
+    dX = torch.from_numpy(Xf).cuda()
+    dA = torch.empty((M, K), dtype=torch.int8, device="cuda")
+    dsa = torch.empty(M, device="cuda")
+    dC = torch.zeros((M, N), device="cuda")
+    torch.cuda.synchronize()
+    w = gpu.pack(B, sb, K, N)
+    q = vnpu.Command()
+    q.opcode = vnpu.OP_QUANTIZE_I8
+    q.args.quantize_i8 = vnpu.QuantizeI8Args(dX.data_ptr(), dA.data_ptr(), dsa.data_ptr(), M, K, 0, 0)
+    mm = vnpu.Command()
+    mm.opcode = vnpu.OP_MATMUL_I8
+    mm.args.matmul_i8 = vnpu.MatmulI8Args(dA.data_ptr(), w, dsa.data_ptr(), None, dC.data_ptr(),
+                                          M, K, N, 0, 0, 2, 0)
+    launches0 = b200_lib.b200_kernel_launches(gpu.dev)
+    g = gpu.capture([q, mm])
+    assert b200_lib.b200_kernel_launches(gpu.dev) == launches0  # recorded, not run
+    assert not dC.any().item()
+    for _ in range(3):
+        gpu.replay(g)
+    assert gpu.sync() == vnpu.OK
+    assert b200_lib.b200_kernel_launches(gpu.dev) >= launches0 + 6
+    assert bits_equal(dC.cpu().numpy(), ref)
+    b200_lib.b200_graph_destroy(g)
+    # host operand while capturing -> refused; sync while capturing -> busy
+    with vnpu.Device(b200_lib) as dev2:
+        assert b200_lib.b200_capture_begin(dev2.stream) == vnpu.OK
+        assert dev2.sync() == vnpu.ERR_DEVICE_BUSY
+        hq = vnpu.Command()
+        hq.opcode = vnpu.OP_QUANTIZE_I8
+        hq.args.quantize_i8 = vnpu.QuantizeI8Args(Xf.ctypes.data, dA.data_ptr(), dsa.data_ptr(),
+                                                  M, K, 0, 0)
+        assert dev2.submit([hq]) == vnpu.OK
+        out = vnpu.vp()
+        assert b200_lib.b200_capture_end(dev2.stream, C.byref(out)) == vnpu.ERR_DEVICE_ERROR
+        assert not out.value
+    gpu.unpack(w)
