@@ -324,3 +324,23 @@ def test_attention_block_shapes(gpu, oracle, sq, sk):
     gpu.attention(Q, K, V, None, O, 1, H, sq, sk, D, 1, 0.0)
     Oo = oracle.attention(Q, K, V, None, 1, H, sq, sk, D, 1, 0.0)
     assert bits_equal(O, Oo), f"max ulp {ulp_diff(O, Oo)}"
+
+
+@pytest.mark.parametrize("M,K,N", [(129, 256, 256), (300, 1000, 700), (1024, 2048, 1536),
+                                   (2000, 640, 2056)])
+def test_pair_and_single_cta_kernels_agree(gpu, oracle, monkeypatch, M, K, N):
+    """The CTA-pair (256x256) and single-CTA (128x256) tcgen05 kernels give
+    the same bits, equal to the oracle on sampled rows."""
+    rng = np.random.default_rng(M + K + N)
+    A, sa = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
+    B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
+    bias = rng.normal(0, 0.01, N).astype(np.float32)
+    outs = []
+    for no_pair in (False, True):
+        if no_pair:
+            monkeypatch.setenv("VNPU_B200_NO_PAIR", "1")
+        outs.append(run_matmul(gpu, A, B, sa, sb, bias, 3, 0))
+    monkeypatch.delenv("VNPU_B200_NO_PAIR", raising=False)
+    assert bits_equal(outs[0], outs[1])
+    rows = np.arange(0, M, 13)
+    assert bits_equal(outs[0][rows], oracle.matmul_i8(A[rows], B, sa[rows], sb, bias, 3, 0))
