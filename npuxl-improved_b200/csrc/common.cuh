@@ -95,6 +95,61 @@ __device__ __forceinline__ float ref_activation(float v, uint32_t epilogue, bool
     }
 }
 
+// ---- branch-free variants, selected once per launch ------------------------
+// Same arithmetic as above; out-of-range and NaN inputs handled with selects
+// so a warp can interleave independent elements.  fast_expf: NaN propagates
+// (as in the reference: z, floor and the polynomial all become NaN).
+template <bool FUSED>
+__device__ __forceinline__ float ref_fast_expf_sel(float x) {
+    const float xc = x < -80.0f ? -80.0f : (x > 80.0f ? 80.0f : x);
+    const float z = __fmul_rn(xc, 1.4426950408889634f);
+    const float zi = floorf(z);
+    const float f = __fsub_rn(z, zi);
+    const int n = __float2int_rz(zi);
+    const float r = scale_pow2(exp2_poly(f, FUSED), n);
+    return x < -80.0f ? 0.0f : (x > 80.0f ? __int_as_float(0x7f800000) : r);
+}
+
+// Activation variants: 0 none, 1 relu, 2 silu, 3 gelu (tanh; GELU_ERF aliases it).
+template <uint32_t ACT, bool FUSED>
+__device__ __forceinline__ float ref_activation_t(float v) {
+    if constexpr (ACT == 1) {
+        return v > 0.0f ? v : 0.0f;
+    } else if constexpr (ACT == 2) {
+        return __fdiv_rn(v, __fadd_rn(1.0f, ref_fast_expf_sel<FUSED>(-v)));
+    } else if constexpr (ACT == 3) {
+        const float k0 = 0.7978845608028654f, k1 = 0.035677408136300125f;
+        const float x3 = __fmul_rn(__fmul_rn(v, v), v);
+        const float inner = FUSED ? __fmul_rn(k0, __fmaf_rn(k1, x3, v))
+                                  : __fmul_rn(k0, __fadd_rn(v, __fmul_rn(k1, x3)));
+        const float e = ref_fast_expf_sel<FUSED>(__fmul_rn(-2.0f, inner));
+        const float t = __fsub_rn(__fdiv_rn(2.0f, __fadd_rn(1.0f, e)), 1.0f);
+        return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, t));
+    } else {
+        return v;
+    }
+}
+
+// BIAS: 0 none, 1 fused (fmaf), 2 two roundings.
+template <uint32_t ACT, uint32_t BIAS, bool FUSED>
+__device__ __forceinline__ float ref_dequant_t(int32_t acc, float sa, float sb, float bias) {
+    const float t = __fmul_rn(__int2float_rn(acc), sa);
+    float out;
+    if constexpr (BIAS == 0) out = __fmul_rn(t, sb);
+    else if constexpr (BIAS == 1) out = __fmaf_rn(t, sb, bias);
+    else out = __fadd_rn(__fmul_rn(t, sb), bias);
+    return ref_activation_t<ACT, FUSED>(out);
+}
+
+// Launch-constant epilogue variant: act | bias << 2 | fused << 4.
+__host__ __device__ constexpr uint32_t epi_variant(uint32_t epilogue, bool has_bias,
+                                                   uint32_t form) {
+    const uint32_t act = epilogue == 1 ? 1u : epilogue == 2 ? 2u : (epilogue == 3 || epilogue == 4) ? 3u : 0u;
+    const uint32_t bias = !has_bias ? 0u : (form == kFormBlock ? 1u : 2u);
+    const uint32_t fused = (act >= 2 && form == kFormScalar) ? 0u : 1u;
+    return act | (bias << 2) | (fused << 4);
+}
+
 // store_i8_c (kernels.cpp:526-535) for one accumulator.
 __device__ __forceinline__ float ref_dequant(int32_t acc, float sa, float sb, bool has_bias,
                                              float bias, uint32_t epilogue, uint32_t form) {
@@ -206,6 +261,31 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const void *tmap, ui
         " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(smem_dst)),
         "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_addr(bar)), "r"(x), "r"(y)
         : "memory");
+}
+
+// 2-D tiled store from this CTA's shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const void *tmap, const void *smem_src, int32_t x,
+                                             int32_t y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(tmap)),
+        "r"(smem_addr(smem_src)), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Shared-memory sources of committed bulk stores may be reused.
+__device__ __forceinline__ void bulk_wait_read0() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Committed bulk stores are complete.
+__device__ __forceinline__ void bulk_wait0() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Generic-proxy shared-memory writes become visible to the async proxy (TMA).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------

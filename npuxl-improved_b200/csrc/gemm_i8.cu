@@ -65,6 +65,8 @@ struct TcParams {
     uint32_t M, N, K;
     uint32_t tiles_m, tiles_n, num_kb;
     uint32_t epilogue, form;
+    uint32_t variant;      // epi_variant(epilogue, bias != NULL, form)
+    uint32_t tma_store;    // 1: C written by TMA from shared memory
     uint32_t *err;
     uint64_t limit_ns;
 };
@@ -110,6 +112,72 @@ __device__ __forceinline__ void store_chunk32(const uint32_t (&r)[32], float *cr
         if (n < N)
             crow[n] = ref_dequant(static_cast<int32_t>(r[j]), sa, __ldg(scale_b + n), has_bias,
                                   has_bias ? __ldg(bias + n) : 0.0f, epilogue, form);
+    }
+}
+
+// Store 32 finished values of one row (vec: 16-byte aligned row, ldc % 4 == 0).
+__device__ __forceinline__ void store_row32(const float (&v)[32], float *crow, uint32_t n0,
+                                            uint32_t N, bool vec) {
+    if (vec && n0 + 32u <= N) {
+#pragma unroll
+        for (uint32_t j = 0; j < 32u; j += 4u)
+            *reinterpret_cast<float4 *>(crow + n0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        return;
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < 32u; ++j)
+        if (n0 + j < N) crow[n0 + j] = v[j];
+}
+
+// Launch-constant dequant of 32 accumulators of one row into v[] (variant V
+// = epi_variant(); scale_b is padded to a multiple of 256 so the vector
+// loads never leave its allocation; bias is read guarded past N).
+template <uint32_t V>
+__device__ __forceinline__ void dequant32(const uint32_t (&r)[32], float (&v)[32], float sa,
+                                          const float *scale_b, const float *bias, uint32_t n0,
+                                          uint32_t N, bool bias_vec) {
+    constexpr uint32_t ACT = V & 3u, BIAS = (V >> 2) & 3u;
+    constexpr bool FUSED = ((V >> 4) & 1u) != 0u;
+    const bool full = n0 + 32u <= N;
+#pragma unroll
+    for (uint32_t j = 0; j < 32u; j += 4u) {
+        const float4 sb = __ldg(reinterpret_cast<const float4 *>(scale_b + n0 + j));
+        float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+        if constexpr (BIAS != 0) {
+            if (bias_vec && full) {
+                bb = __ldg(reinterpret_cast<const float4 *>(bias + n0 + j));
+            } else {
+                bb.x = n0 + j + 0 < N ? __ldg(bias + n0 + j + 0) : 0.0f;
+                bb.y = n0 + j + 1 < N ? __ldg(bias + n0 + j + 1) : 0.0f;
+                bb.z = n0 + j + 2 < N ? __ldg(bias + n0 + j + 2) : 0.0f;
+                bb.w = n0 + j + 3 < N ? __ldg(bias + n0 + j + 3) : 0.0f;
+            }
+        }
+        v[j + 0] = ref_dequant_t<ACT, BIAS, FUSED>(static_cast<int32_t>(r[j + 0]), sa, sb.x, bb.x);
+        v[j + 1] = ref_dequant_t<ACT, BIAS, FUSED>(static_cast<int32_t>(r[j + 1]), sa, sb.y, bb.y);
+        v[j + 2] = ref_dequant_t<ACT, BIAS, FUSED>(static_cast<int32_t>(r[j + 2]), sa, sb.z, bb.z);
+        v[j + 3] = ref_dequant_t<ACT, BIAS, FUSED>(static_cast<int32_t>(r[j + 3]), sa, sb.w, bb.w);
+    }
+}
+
+// The 16 variants epi_variant() can produce.
+#define VNPU_B200_EPI_VARIANTS(X)                                                             \
+    X(0x10) X(0x11) X(0x12) X(0x13) X(0x14) X(0x15) X(0x16) X(0x17) X(0x18) X(0x19) X(0x1a) \
+    X(0x1b) X(0x02) X(0x03) X(0x0a) X(0x0b)
+
+__device__ __forceinline__ void dequant32_any(uint32_t variant, const uint32_t (&r)[32],
+                                              float (&v)[32], float sa, const float *scale_b,
+                                              const float *bias, uint32_t n0, uint32_t N,
+                                              bool bias_vec) {
+    switch (variant) {
+#define VNPU_B200_CASE(V)                                                 \
+    case V:                                                               \
+        dequant32<V>(r, v, sa, scale_b, bias, n0, N, bias_vec);           \
+        break;
+        VNPU_B200_EPI_VARIANTS(VNPU_B200_CASE)
+#undef VNPU_B200_CASE
+    default:
+        break;
     }
 }
 
@@ -234,8 +302,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_base = (warp & 3u) * 32u;
         const uint32_t row = lane_base + lane;
         const bool vec_ok = (p.ldc % 4u == 0u) &&
-                            ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0u) &&
-                            ((reinterpret_cast<uintptr_t>(p.bias) & 15u) == 0u);
+                            ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0u);
+        const bool bias_vec = (reinterpret_cast<uintptr_t>(p.bias) & 15u) == 0u;
         uint32_t tcount = 0;
         for (uint32_t t = blockIdx.x; t < total_tiles; t += gridDim.x, ++tcount) {
             uint32_t mb, nb;
@@ -262,7 +330,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_wait_ld();
                 const uint32_t n0 = nb * kBN + c * 32u;
                 if (!row_ok || n0 >= p.N) continue;
-                store_chunk32(r, crow, n0, p.N, sa, p.scale_b, p.bias, p.epilogue, p.form, vec_ok);
+                float v[32];
+                dequant32_any(p.variant, r, v, sa, p.scale_b, p.bias, n0, p.N, bias_vec);
+                store_row32(v, crow, n0, p.N, vec_ok);
             }
             tc_fence_before();
             __syncwarp();
@@ -302,11 +372,13 @@ constexpr uint32_t kPBBytes = 128 * kBK;          // 16 KiB per CTA
 constexpr uint32_t kPStageBytes = kPABytes + kPBBytes;
 constexpr uint32_t kPEpiWarps = 8;                // per CTA
 constexpr uint32_t kPThreads = (2 + kPEpiWarps) * 32;
-constexpr uint32_t kPSmemBytes = kPStages * kPStageBytes + 1024;
+constexpr uint32_t kPStageOutBytes = 32 * 32 * 4;  // per epilogue warp: 32 rows x 32 floats
+constexpr uint32_t kPSmemBytes = kPStages * kPStageBytes + kPEpiWarps * kPStageOutBytes + 1024;
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     gemm_i8_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                                const __grid_constant__ CUtensorMap tmap_b, const TcParams p) {
+                                const __grid_constant__ CUtensorMap tmap_b,
+                                const __grid_constant__ CUtensorMap tmap_c, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[kPStages];
     __shared__ __align__(8) uint64_t empty_bar[kPStages];
@@ -340,6 +412,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         fence_barrier_init();
         tma_prefetch_desc(&tmap_a);
         tma_prefetch_desc(&tmap_b);
+        if (p.tma_store) tma_prefetch_desc(&tmap_c);
     }
     if (warp == 1) {
         tmem_alloc_pair(&tmem_base_slot, kTmemCols);
@@ -425,13 +498,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     } else {
         // ------------------------------------------------------------ epilogue (both CTAs)
         // Warp w reads TMEM lanes 32*(w%4)..+31; warps 2-5 take columns
-        // 0-127 of the tile, warps 6-9 columns 128-255.
+        // 0-127 of the tile, warps 6-9 columns 128-255.  Each 32x32 chunk is
+        // dequantised in registers, written 128B-swizzled into this warp's
+        // 4 KiB staging buffer and stored to C by TMA (rows >= M and columns
+        // >= N are clipped by the tensor map); without a C tensor map the
+        // rows are stored directly.
         const uint32_t lane_base = (warp & 3u) * 32u;
         const uint32_t col_base = ((warp - 2u) >> 2) * 128u;
         const uint32_t row = rank * 128u + lane_base + lane;
         const bool vec_ok = (p.ldc % 4u == 0u) &&
-                            ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0u) &&
-                            ((reinterpret_cast<uintptr_t>(p.bias) & 15u) == 0u);
+                            ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0u);
+        const bool bias_vec = (reinterpret_cast<uintptr_t>(p.bias) & 15u) == 0u;
+        uint8_t *stage_out = ring + kPStages * kPStageBytes + (warp - 2u) * kPStageOutBytes;
+        float *my_row = reinterpret_cast<float *>(stage_out + lane * 128u);
         const uint32_t leader_empty0 = mapa_shared(smem_addr(&tmem_empty_bar[0]), 0);
         const uint32_t leader_empty1 = mapa_shared(smem_addr(&tmem_empty_bar[1]), 0);
         uint32_t tcount = 0;
@@ -446,7 +525,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
-            const uint32_t m = mb * kPTileM + row;
+            const uint32_t m_first = mb * kPTileM + rank * 128u + lane_base;  // warp's first row
+            const uint32_t m = m_first + lane;
             const bool row_ok = m < p.M;
             const float sa = row_ok ? (p.scale_a ? __ldg(p.scale_a + m) : 1.0f) : 0.0f;
             float *crow = p.C + static_cast<uint64_t>(row_ok ? m : 0) * p.ldc;
@@ -458,13 +538,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                 tmem_ld_32cols(tmem_base + (lane_base << 16) + acc * kPTileN + col, r);
                 tmem_wait_ld();
                 const uint32_t n0 = nb * kPTileN + col;
-                if (!row_ok || n0 >= p.N) continue;
-                store_chunk32(r, crow, n0, p.N, sa, p.scale_b, p.bias, p.epilogue, p.form, vec_ok);
+                if (n0 >= p.N || m_first >= p.M) continue;  // warp-uniform
+                float v[32];
+                dequant32_any(p.variant, r, v, sa, p.scale_b, p.bias, n0, p.N, bias_vec);
+                if (p.tma_store) {
+                    if (lane == 0) bulk_wait_read0();  // previous store has read the buffer
+                    __syncwarp();
+#pragma unroll
+                    for (uint32_t j = 0; j < 8u; ++j)
+                        *reinterpret_cast<float4 *>(my_row + 4u * (j ^ (lane & 7u))) =
+                            make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmap_c, stage_out, static_cast<int32_t>(n0),
+                                     static_cast<int32_t>(m_first));
+                        bulk_commit();
+                    }
+                } else if (row_ok) {
+                    store_row32(v, crow, n0, p.N, vec_ok);
+                }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc ? leader_empty1 : leader_empty0);
         }
+        if (lane == 0) bulk_wait0();  // C written before the CTA retires
     }
 
     // ---------------------------------------------------------------- teardown
@@ -710,6 +809,20 @@ bool encode_tmap_kmajor_i8(CUtensorMap *map, const void *base, uint64_t k_extent
     return r == CUDA_SUCCESS;
 }
 
+bool encode_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t dim0,
+                    uint64_t dim1, uint64_t stride1_bytes, uint32_t box0, uint32_t box1,
+                    CUtensorMapSwizzle swizzle) {
+    auto fn = tmap_encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {dim0, dim1};
+    const cuuint64_t strides[1] = {stride1_bytes};
+    const cuuint32_t box[2] = {box0, box1};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 MatmulKernel choose_matmul_kernel(uint32_t M, uint32_t K, uint32_t N, uint32_t lda,
                                   const void *A) {
     (void)N;
@@ -806,13 +919,20 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         tp.num_kb = (p.K + kBK - 1) / kBK;
         tp.epilogue = p.epilogue;
         tp.form = p.form;
+        tp.variant = epi_variant(p.epilogue, p.bias != nullptr, p.form);
         tp.err = ctx.err;
         tp.limit_ns = ctx.wait_limit_ns;
+        CUtensorMap tmap_c;
+        tp.tma_store = (reinterpret_cast<uintptr_t>(p.C) % 16u == 0u) && (p.ldc % 4u == 0u) &&
+                       encode_tmap_2d(&tmap_c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.C, p.N, p.M,
+                                      static_cast<uint64_t>(p.ldc) * 4u, 32, 32,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!tp.tma_store) std::memset(&tmap_c, 0, sizeof(tmap_c));
         const uint32_t tiles = tp.tiles_m * tp.tiles_n;
         const uint32_t pairs = tiles < static_cast<uint32_t>(max_pairs) ? tiles
                                                                          : static_cast<uint32_t>(max_pairs);
         gemm_i8_tcgen05_pair_kernel<<<2 * pairs, kPThreads, kPSmemBytes, ctx.stream>>>(
-            tmap_a, *p.tmap_b128, tp);
+            tmap_a, *p.tmap_b128, tmap_c, tp);
         count_launch(ctx);
         return cudaGetLastError();
     }
@@ -833,6 +953,8 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
     tp.num_kb = (p.K + kBK - 1) / kBK;
     tp.epilogue = p.epilogue;
     tp.form = p.form;
+    tp.variant = epi_variant(p.epilogue, p.bias != nullptr, p.form);
+    tp.tma_store = 0;
     tp.err = ctx.err;
     tp.limit_ns = ctx.wait_limit_ns;
     const uint32_t tiles = tp.tiles_m * tp.tiles_n;

@@ -82,6 +82,9 @@ cudaError_t matmul_i8_simt(const LaunchCtx &ctx, const MatmulI8 &p);
 bool encode_tmap_kmajor_i8(CUtensorMap *map, const void *base, uint64_t k_extent,
                            uint64_t rows, uint64_t row_stride_bytes, uint32_t box_k,
                            uint32_t box_rows);
+bool encode_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t dim0,
+                    uint64_t dim1, uint64_t stride1_bytes, uint32_t box0, uint32_t box1,
+                    CUtensorMapSwizzle swizzle);
 
 // ---- decoder-block ops (src/kernels/llm.cpp) -----------------------------------
 cudaError_t rmsnorm(const LaunchCtx &ctx, const float *X, const float *W, float *Y,

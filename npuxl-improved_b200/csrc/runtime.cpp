@@ -1219,7 +1219,7 @@ VNPU_API vnpu_status_t VNPU_CALL vnpu_pack_weights_i8(vnpu_device_t *device, con
         };
         cudaError_t e;
         if ((e = cudaMalloc(&w->bt, bt_bytes)) != cudaSuccess ||
-            (e = cudaMalloc(&w->scales, sizeof(float) * N)) != cudaSuccess ||
+            (e = cudaMalloc(&w->scales, sizeof(float) * ((N + 255u) & ~255u))) != cudaSuccess ||
             (e = cudaMalloc(&w->column_sums, sizeof(int32_t) * N)) != cudaSuccess)
             return fail(e);
         uint64_t launched = 0;
@@ -1246,9 +1246,14 @@ VNPU_API vnpu_status_t VNPU_CALL vnpu_pack_weights_i8(vnpu_device_t *device, con
                 }
                 if (e != cudaSuccess) return fail(e);
             }
-            if ((e = cudaMemcpyAsync(w->scales, w->host_scales.data(), sizeof(float) * N,
+            // Scales are padded with 1.0 to a multiple of 256 so the epilogue's
+            // 16-byte loads of a ragged last tile stay inside the allocation.
+            std::vector<float> padded(w->host_scales);
+            padded.resize((N + 255u) & ~255u, 1.0f);
+            if ((e = cudaMemcpyAsync(w->scales, padded.data(), sizeof(float) * padded.size(),
                                      cudaMemcpyHostToDevice, device->aux)) != cudaSuccess)
                 return fail(e);
+            if ((e = cudaStreamSynchronize(device->aux)) != cudaSuccess) return fail(e);
             w->host_column_sums.resize(N);
             if ((e = cudaMemcpyAsync(w->host_column_sums.data(), w->column_sums,
                                      sizeof(int32_t) * N, cudaMemcpyDeviceToHost,
