@@ -577,6 +577,157 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 }
 
 // ===========================================================================
+// M <= 8 decode on the tensor core ("swap AB"): D[n][m] = sum_k Bt[n][k] A[m][k].
+// The packed weights are the 128-row UMMA operand and the (at most 8)
+// activation rows the N=8 operand, so the kernel is a pure TMA stream of the
+// weight matrix.  One cluster of S CTAs owns 128 weight rows (output
+// columns); its CTAs split K, each accumulates its slice in tensor memory,
+// and the leader CTA adds the S partial int32 tiles through distributed
+// shared memory (exact, fixed order) and applies the dequant epilogue.
+// ===========================================================================
+
+constexpr uint32_t kSkStages = 6;
+constexpr uint32_t kSkWBytes = 128 * kBK;   // 16 KiB of weight rows per stage
+constexpr uint32_t kSkXBytes = 8 * kBK;     // 1 KiB of activations per stage
+constexpr uint32_t kSkThreads = 128;
+constexpr uint32_t kSkSmemBytes = kSkStages * (kSkWBytes + kSkXBytes) + 1024;
+
+struct SkParams {
+    const float *scale_a;
+    const float *scale_b;
+    const float *bias;
+    float *C;
+    uint32_t ldc;
+    uint32_t M, N, K;
+    uint32_t num_kb, kb_per_rank;
+    uint32_t epilogue, form;
+    uint32_t *err;
+    uint64_t limit_ns;
+};
+
+__global__ void __launch_bounds__(kSkThreads, 2)
+    gemv_i8_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                           const __grid_constant__ CUtensorMap tmap_x, const SkParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[kSkStages];
+    __shared__ __align__(8) uint64_t empty_bar[kSkStages];
+    __shared__ __align__(8) uint64_t mma_done_bar;
+    __shared__ uint32_t tmem_base_slot;
+    __shared__ volatile int abort_flag;
+    __shared__ int32_t part[128][9];   // this CTA's partial sums [row n][m]
+
+    const uint32_t raw_addr = smem_addr(smem_raw);
+    uint8_t *ring = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+    uint8_t *wtiles = ring;                              // [stage][16 KiB]
+    uint8_t *xtiles = ring + kSkStages * kSkWBytes;      // [stage][1 KiB]
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const uint32_t csize = cluster_nctarank();
+    const uint32_t n0 = (blockIdx.x / csize) * 128u;
+    const uint32_t kb0 = rank * p.kb_per_rank;
+    const uint32_t kb1 = min(p.num_kb, kb0 + p.kb_per_rank);
+    const uint32_t nkb = kb1 > kb0 ? kb1 - kb0 : 0u;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < kSkStages; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        mbar_init(&mma_done_bar, 1);
+        abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmap_w);
+        tma_prefetch_desc(&tmap_x);
+    }
+    if (warp == 1) {
+        tmem_alloc(&tmem_base_slot, 32);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_base_slot;
+
+    if (warp == 0 && lane == 0) {
+        uint32_t issued = 0;
+        for (uint32_t i = 0; i < nkb; ++i, ++issued) {
+            const uint32_t s = i % kSkStages, ph = (i / kSkStages) & 1u;
+            if (!mbar_wait(&empty_bar[s], ph ^ 1u, p.limit_ns, p.err, &abort_flag)) break;
+            mbar_arrive_expect_tx(&full_bar[s], kSkWBytes + kSkXBytes);
+            const int32_t k = static_cast<int32_t>((kb0 + i) * kBK);
+            tma_load_2d(wtiles + s * kSkWBytes, &tmap_w, &full_bar[s], k, static_cast<int32_t>(n0));
+            tma_load_2d(xtiles + s * kSkXBytes, &tmap_x, &full_bar[s], k, 0);
+        }
+        // Never leave with copies in flight.
+        const uint32_t tail = issued < kSkStages ? issued : kSkStages;
+        for (uint32_t i = issued - tail; i < issued; ++i)
+            mbar_wait(&full_bar[i % kSkStages], (i / kSkStages) & 1u, p.limit_ns, p.err, nullptr);
+    } else if (warp == 1 && lane == 0 && nkb > 0) {
+        constexpr uint32_t idesc = umma_idesc_i8(128, 8);
+        bool ok = true;
+        for (uint32_t i = 0; i < nkb; ++i) {
+            const uint32_t s = i % kSkStages, ph = (i / kSkStages) & 1u;
+            if (!mbar_wait(&full_bar[s], ph, p.limit_ns, p.err, &abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint64_t adesc = umma_desc_k_sw128(smem_addr(wtiles + s * kSkWBytes));
+            const uint64_t bdesc = umma_desc_k_sw128(smem_addr(xtiles + s * kSkXBytes));
+#pragma unroll
+            for (uint32_t kk = 0; kk < kBK / kUmmaK; ++kk)
+                umma_i8(tmem_base, adesc + 2u * kk, bdesc + 2u * kk, idesc, (i | kk) != 0u);
+            umma_commit(&empty_bar[s]);
+        }
+        (void)ok;
+        umma_commit(&mma_done_bar);  // also covers an early exit: all issued MMAs done
+    }
+
+    // ---- partial sums: TMEM lane = weight row n0 + 32*warp + lane, column = m
+    uint32_t ok = 1;
+    if (nkb > 0) {
+        if (lane == 0) ok = mbar_wait(&mma_done_bar, 0, p.limit_ns, p.err, &abort_flag);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+    __syncwarp();
+    uint32_t r[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+    if (nkb > 0 && ok) {
+        tc_fence_after();
+        tmem_ld_8cols(tmem_base + ((warp * 32u) << 16), r);
+        tmem_wait_ld();
+    }
+    const uint32_t row = warp * 32u + lane;
+#pragma unroll
+    for (uint32_t m = 0; m < 8; ++m) part[row][m] = static_cast<int32_t>(r[m]);
+
+    tc_fence_before();
+    cluster_sync_all();   // every CTA's partials are in its shared memory
+
+    if (rank == 0) {
+        const uint32_t n = n0 + row;
+        if (n < p.N) {
+            const bool has_bias = p.bias != nullptr;
+            const float sb = __ldg(p.scale_b + n);
+            const float bv = has_bias ? __ldg(p.bias + n) : 0.0f;
+            for (uint32_t m = 0; m < p.M; ++m) {
+                int32_t acc = part[row][m];
+                for (uint32_t q = 1; q < csize; ++q)
+                    acc += ld_shared_cluster_s32(mapa_shared(smem_addr(&part[row][m]), q));
+                const float sa = p.scale_a ? __ldg(p.scale_a + m) : 1.0f;
+                p.C[static_cast<uint64_t>(m) * p.ldc + n] =
+                    ref_dequant(acc, sa, sb, has_bias, bv, p.epilogue, p.form);
+            }
+        }
+    }
+    cluster_sync_all();   // peers keep their shared memory until the leader is done
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 32);
+    }
+}
+
+// ===========================================================================
 // M <= 8 decode GEMV
 // ===========================================================================
 
@@ -965,9 +1116,69 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
     return cudaGetLastError();
 }
 
+namespace {
+
+cudaError_t gemv_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemv_i8_tcgen05_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kSkSmemBytes));
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(gemv_i8_tcgen05_kernel,
+                                 cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+        attr[dev] = true;
+    }
+    CUtensorMap tmap_x;
+    if (!encode_tmap_kmajor_i8(&tmap_x, p.A, p.K, p.M, p.lda, kBK, 8)) return cudaErrorInvalidValue;
+    SkParams sp;
+    sp.scale_a = p.scale_a;
+    sp.scale_b = p.scale_b;
+    sp.bias = p.bias;
+    sp.C = p.C;
+    sp.ldc = p.ldc;
+    sp.M = p.M;
+    sp.N = p.N;
+    sp.K = p.K;
+    sp.num_kb = (p.K + kBK - 1) / kBK;
+    sp.epilogue = p.epilogue;
+    sp.form = p.form;
+    sp.err = ctx.err;
+    sp.limit_ns = ctx.wait_limit_ns;
+    // Split K over a cluster so that about two CTAs per SM stream weights.
+    const uint32_t blocks = (p.N + 127u) / 128u;
+    uint32_t csize = 1;
+    while (csize < 8u && blocks * csize * 2u <= 2u * static_cast<uint32_t>(ctx.num_sms) &&
+           csize * 2u <= sp.num_kb)
+        csize *= 2u;
+    sp.kb_per_rank = (sp.num_kb + csize - 1) / csize;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks * csize, 1, 1);
+    cfg.blockDim = dim3(kSkThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSkSmemBytes;
+    cfg.stream = ctx.stream;
+    cudaLaunchAttribute attrs[1];
+    attrs[0].id = cudaLaunchAttributeClusterDimension;
+    attrs[0].val.clusterDim.x = csize;
+    attrs[0].val.clusterDim.y = 1;
+    attrs[0].val.clusterDim.z = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemv_i8_tcgen05_kernel, *p.tmap_b128, tmap_x, sp);
+}
+
+}  // namespace
+
 cudaError_t matmul_i8_gemv(const LaunchCtx &ctx, const MatmulI8 &p) {
     const GvParams g = gv_params(p);
     const bool aligned = (reinterpret_cast<uintptr_t>(p.A) % 16u == 0u) && (p.lda % 16u == 0u);
+    if (aligned && p.K >= 16u && p.tmap_b128 && std::getenv("VNPU_B200_SIMT_GEMV") == nullptr) {
+        const cudaError_t e = gemv_tcgen05(ctx, p);
+        count_launch(ctx);
+        return e;
+    }
     cudaError_t e;
     switch (p.M) {
     case 1: e = launch_gemv_m<1>(ctx, g, aligned); break;

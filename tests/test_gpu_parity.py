@@ -344,3 +344,24 @@ def test_pair_and_single_cta_kernels_agree(gpu, oracle, monkeypatch, M, K, N):
     assert bits_equal(outs[0], outs[1])
     rows = np.arange(0, M, 13)
     assert bits_equal(outs[0][rows], oracle.matmul_i8(A[rows], B, sa[rows], sb, bias, 3, 0))
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8])
+@pytest.mark.parametrize("K,N", [(4096, 4096), (11008, 4096), (4096, 11008), (100, 300),
+                                 (16, 128), (1000, 1000), (130, 12288)])
+def test_decode_tensor_core_vs_simt(gpu, oracle, monkeypatch, M, K, N):
+    """The M<=8 decode kernel on the tensor core (cluster split-K, partials
+    summed through distributed shared memory) equals the SIMT GEMV and the
+    oracle bit for bit, with bias (the decode shape of configs[1])."""
+    rng = np.random.default_rng(M * 1000 + K + N)
+    A, sa = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
+    B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
+    bias = rng.normal(0, 0.01, N).astype(np.float32)
+    outs = []
+    for simt in (False, True):
+        if simt:
+            monkeypatch.setenv("VNPU_B200_SIMT_GEMV", "1")
+        outs.append(run_matmul(gpu, A, B, sa, sb, bias, 0, 2))
+    monkeypatch.delenv("VNPU_B200_SIMT_GEMV", raising=False)
+    assert bits_equal(outs[0], outs[1])
+    assert bits_equal(outs[0], oracle.matmul_i8(A, B, sa, sb, bias, 0, 2))
