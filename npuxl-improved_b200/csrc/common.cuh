@@ -415,6 +415,23 @@ __device__ __forceinline__ int32_t ld_shared_cluster_s32(uint32_t cluster_addr) 
     return v;
 }
 
+__device__ __forceinline__ void st_shared_cluster_v4(uint32_t cluster_addr, int32_t a, int32_t b,
+                                                     int32_t c, int32_t d) {
+    asm volatile("st.shared::cluster.v4.s32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(a),
+                 "r"(b), "r"(c), "r"(d)
+                 : "memory");
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue now / wait until the previous kernel has completed and its memory
+// is visible.  Both are no-ops for launches without the PDL attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait_previous() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // Arrive on an mbarrier of another CTA of the cluster.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)

@@ -586,11 +586,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 // shared memory (exact, fixed order) and applies the dequant epilogue.
 // ===========================================================================
 
-constexpr uint32_t kSkStages = 6;
+constexpr uint32_t kSkStages = 4;
 constexpr uint32_t kSkWBytes = 128 * kBK;   // 16 KiB of weight rows per stage
 constexpr uint32_t kSkXBytes = 8 * kBK;     // 1 KiB of activations per stage
 constexpr uint32_t kSkThreads = 128;
-constexpr uint32_t kSkSmemBytes = kSkStages * (kSkWBytes + kSkXBytes) + 1024;
+constexpr uint32_t kSkMaxCluster = 8;
+constexpr uint32_t kSkPartBytes = 128 * 8 * 4;  // one CTA's partial tile [128][8] int32
+constexpr uint32_t kSkSmemBytes =
+    kSkStages * (kSkWBytes + kSkXBytes) + kSkMaxCluster * kSkPartBytes + 1024;
 
 struct SkParams {
     const float *scale_a;
@@ -614,12 +617,18 @@ __global__ void __launch_bounds__(kSkThreads, 2)
     __shared__ __align__(8) uint64_t mma_done_bar;
     __shared__ uint32_t tmem_base_slot;
     __shared__ volatile int abort_flag;
-    __shared__ int32_t part[128][9];   // this CTA's partial sums [row n][m]
 
     const uint32_t raw_addr = smem_addr(smem_raw);
     uint8_t *ring = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
     uint8_t *wtiles = ring;                              // [stage][16 KiB]
     uint8_t *xtiles = ring + kSkStages * kSkWBytes;      // [stage][1 KiB]
+    // [rank][128 rows][8 m] int32: each CTA of the cluster stores its partial
+    // tile into its own slot of the leader's copy.
+    int32_t *parts = reinterpret_cast<int32_t *>(xtiles + kSkStages * kSkXBytes);
+
+    // The next kernel of the stream may start its prologue (and its own
+    // weight stream) while this one runs.
+    pdl_launch_dependents();
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
@@ -650,8 +659,21 @@ __global__ void __launch_bounds__(kSkThreads, 2)
     const uint32_t tmem_base = tmem_base_slot;
 
     if (warp == 0 && lane == 0) {
-        uint32_t issued = 0;
-        for (uint32_t i = 0; i < nkb; ++i, ++issued) {
+        // Weights (resident, written by no earlier kernel) for the first
+        // stages go out before waiting on the previous kernel; activations,
+        // which the previous kernel may have produced, only after it.
+        const uint32_t first = nkb < kSkStages ? nkb : kSkStages;
+        for (uint32_t i = 0; i < first; ++i) {
+            mbar_arrive_expect_tx(&full_bar[i], kSkWBytes + kSkXBytes);
+            tma_load_2d(wtiles + i * kSkWBytes, &tmap_w, &full_bar[i],
+                        static_cast<int32_t>((kb0 + i) * kBK), static_cast<int32_t>(n0));
+        }
+        pdl_wait_previous();
+        for (uint32_t i = 0; i < first; ++i)
+            tma_load_2d(xtiles + i * kSkXBytes, &tmap_x, &full_bar[i],
+                        static_cast<int32_t>((kb0 + i) * kBK), 0);
+        uint32_t issued = first;
+        for (uint32_t i = first; i < nkb; ++i, ++issued) {
             const uint32_t s = i % kSkStages, ph = (i / kSkStages) & 1u;
             if (!mbar_wait(&empty_bar[s], ph ^ 1u, p.limit_ns, p.err, &abort_flag)) break;
             mbar_arrive_expect_tx(&full_bar[s], kSkWBytes + kSkXBytes);
@@ -665,13 +687,9 @@ __global__ void __launch_bounds__(kSkThreads, 2)
             mbar_wait(&full_bar[i % kSkStages], (i / kSkStages) & 1u, p.limit_ns, p.err, nullptr);
     } else if (warp == 1 && lane == 0 && nkb > 0) {
         constexpr uint32_t idesc = umma_idesc_i8(128, 8);
-        bool ok = true;
         for (uint32_t i = 0; i < nkb; ++i) {
             const uint32_t s = i % kSkStages, ph = (i / kSkStages) & 1u;
-            if (!mbar_wait(&full_bar[s], ph, p.limit_ns, p.err, &abort_flag)) {
-                ok = false;
-                break;
-            }
+            if (!mbar_wait(&full_bar[s], ph, p.limit_ns, p.err, &abort_flag)) break;
             tc_fence_after();
             const uint64_t adesc = umma_desc_k_sw128(smem_addr(wtiles + s * kSkWBytes));
             const uint64_t bdesc = umma_desc_k_sw128(smem_addr(xtiles + s * kSkXBytes));
@@ -680,8 +698,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
                 umma_i8(tmem_base, adesc + 2u * kk, bdesc + 2u * kk, idesc, (i | kk) != 0u);
             umma_commit(&empty_bar[s]);
         }
-        (void)ok;
-        umma_commit(&mma_done_bar);  // also covers an early exit: all issued MMAs done
+        umma_commit(&mma_done_bar);  // also after an early exit: all issued MMAs done
     }
 
     // ---- partial sums: TMEM lane = weight row n0 + 32*warp + lane, column = m
@@ -698,29 +715,44 @@ __global__ void __launch_bounds__(kSkThreads, 2)
         tmem_wait_ld();
     }
     const uint32_t row = warp * 32u + lane;
-#pragma unroll
-    for (uint32_t m = 0; m < 8; ++m) part[row][m] = static_cast<int32_t>(r[m]);
+    // Push this CTA's partial row into its slot of the leader's buffer
+    // (fire-and-forget stores; the cluster barrier below orders them).
+    const uint32_t slot = mapa_shared(smem_addr(parts + (rank * 128u + row) * 8u), 0);
+    st_shared_cluster_v4(slot, static_cast<int32_t>(r[0]), static_cast<int32_t>(r[1]),
+                         static_cast<int32_t>(r[2]), static_cast<int32_t>(r[3]));
+    st_shared_cluster_v4(slot + 16u, static_cast<int32_t>(r[4]), static_cast<int32_t>(r[5]),
+                         static_cast<int32_t>(r[6]), static_cast<int32_t>(r[7]));
 
     tc_fence_before();
-    cluster_sync_all();   // every CTA's partials are in its shared memory
+    cluster_sync_all();   // all partial tiles have landed in the leader
 
     if (rank == 0) {
+        // C may still be read or written by the previous kernel until it ends.
+        pdl_wait_previous();
         const uint32_t n = n0 + row;
         if (n < p.N) {
             const bool has_bias = p.bias != nullptr;
             const float sb = __ldg(p.scale_b + n);
             const float bv = has_bias ? __ldg(p.bias + n) : 0.0f;
-            for (uint32_t m = 0; m < p.M; ++m) {
-                int32_t acc = part[row][m];
-                for (uint32_t q = 1; q < csize; ++q)
-                    acc += ld_shared_cluster_s32(mapa_shared(smem_addr(&part[row][m]), q));
-                const float sa = p.scale_a ? __ldg(p.scale_a + m) : 1.0f;
-                p.C[static_cast<uint64_t>(m) * p.ldc + n] =
-                    ref_dequant(acc, sa, sb, has_bias, bv, p.epilogue, p.form);
+            int32_t acc[8];
+#pragma unroll
+            for (uint32_t m = 0; m < 8; ++m) acc[m] = 0;
+            for (uint32_t q = 0; q < csize; ++q) {
+                const int4 lo = *reinterpret_cast<const int4 *>(parts + (q * 128u + row) * 8u);
+                const int4 hi = *reinterpret_cast<const int4 *>(parts + (q * 128u + row) * 8u + 4u);
+                acc[0] += lo.x; acc[1] += lo.y; acc[2] += lo.z; acc[3] += lo.w;
+                acc[4] += hi.x; acc[5] += hi.y; acc[6] += hi.z; acc[7] += hi.w;
+            }
+#pragma unroll
+            for (uint32_t m = 0; m < 8; ++m) {
+                if (m < p.M) {
+                    const float sa = p.scale_a ? __ldg(p.scale_a + m) : 1.0f;
+                    p.C[static_cast<uint64_t>(m) * p.ldc + n] =
+                        ref_dequant(acc[m], sa, sb, has_bias, bv, p.epilogue, p.form);
+                }
             }
         }
     }
-    cluster_sync_all();   // peers keep their shared memory until the leader is done
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, 32);
@@ -1159,13 +1191,15 @@ cudaError_t gemv_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
     cfg.blockDim = dim3(kSkThreads, 1, 1);
     cfg.dynamicSmemBytes = kSkSmemBytes;
     cfg.stream = ctx.stream;
-    cudaLaunchAttribute attrs[1];
+    cudaLaunchAttribute attrs[2];
     attrs[0].id = cudaLaunchAttributeClusterDimension;
     attrs[0].val.clusterDim.x = csize;
     attrs[0].val.clusterDim.y = 1;
     attrs[0].val.clusterDim.z = 1;
+    attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attrs;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = std::getenv("VNPU_B200_NO_PDL") ? 1 : 2;
     return cudaLaunchKernelEx(&cfg, gemv_i8_tcgen05_kernel, *p.tmap_b128, tmap_x, sp);
 }
 
