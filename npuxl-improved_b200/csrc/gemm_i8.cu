@@ -23,6 +23,7 @@
 //               cross-check of the other two.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -811,8 +812,9 @@ __global__ void __launch_bounds__(kGvThreads) gemv_i8_kernel(const GvParams p) {
         const uint32_t n = min(n_first + c, p.N - 1);
         bcol[c] = reinterpret_cast<const int4 *>(p.Bt + static_cast<uint64_t>(n) * p.k_stride);
     }
-    // Each lane owns 16 bytes of every 512-byte K chunk; 4 chunks in flight.
-    constexpr uint32_t kUnroll = 4;
+    // Each lane owns 16 bytes of every 512-byte K chunk; 8 chunks (4 KiB of
+    // each column) in flight, so K <= 4096 is a single DRAM round trip.
+    constexpr uint32_t kUnroll = 8;
     const uint32_t k_end = p.K;
     for (uint32_t k0 = lane * 16u; k0 < k_end; k0 += 512u * kUnroll) {
         int4 b[kUnroll][kGvColsPerWarp];
@@ -1181,8 +1183,10 @@ cudaError_t gemv_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
     sp.limit_ns = ctx.wait_limit_ns;
     // Split K over a cluster so that about two CTAs per SM stream weights.
     const uint32_t blocks = (p.N + 127u) / 128u;
+    uint32_t max_c = 8u;
+    if (const char *e = std::getenv("VNPU_B200_DECODE_CLUSTER")) max_c = std::max(1, std::atoi(e));
     uint32_t csize = 1;
-    while (csize < 8u && blocks * csize * 2u <= 2u * static_cast<uint32_t>(ctx.num_sms) &&
+    while (csize < max_c && blocks * csize * 2u <= 2u * static_cast<uint32_t>(ctx.num_sms) &&
            csize * 2u <= sp.num_kb)
         csize *= 2u;
     sp.kb_per_rank = (sp.num_kb + csize - 1) / csize;
@@ -1208,7 +1212,10 @@ cudaError_t gemv_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
 cudaError_t matmul_i8_gemv(const LaunchCtx &ctx, const MatmulI8 &p) {
     const GvParams g = gv_params(p);
     const bool aligned = (reinterpret_cast<uintptr_t>(p.A) % 16u == 0u) && (p.lda % 16u == 0u);
-    if (aligned && p.K >= 16u && p.tmap_b128 && std::getenv("VNPU_B200_SIMT_GEMV") == nullptr) {
+    bool use_tc = p.M > 1;
+    if (const char *e = std::getenv("VNPU_B200_DECODE")) use_tc = std::strcmp(e, "tc") == 0;
+    if (std::getenv("VNPU_B200_SIMT_GEMV")) use_tc = false;
+    if (use_tc && aligned && p.K >= 16u && p.tmap_b128) {
         const cudaError_t e = gemv_tcgen05(ctx, p);
         count_launch(ctx);
         return e;
