@@ -816,6 +816,8 @@ __global__ void __launch_bounds__(kGvThreads) gemv_i8_kernel(const GvParams p) {
     // each column) in flight, so K <= 4096 is a single DRAM round trip.
     constexpr uint32_t kUnroll = 8;
     const uint32_t k_end = p.K;
+    pdl_launch_dependents();
+    bool waited = false;
     for (uint32_t k0 = lane * 16u; k0 < k_end; k0 += 512u * kUnroll) {
         int4 b[kUnroll][kGvColsPerWarp];
 #pragma unroll
@@ -824,6 +826,12 @@ __global__ void __launch_bounds__(kGvThreads) gemv_i8_kernel(const GvParams p) {
 #pragma unroll
             for (int c = 0; c < kGvColsPerWarp; ++c)
                 b[u][c] = k < k_end ? __ldcs(bcol[c] + (k >> 4)) : make_int4(0, 0, 0, 0);
+        }
+        // Weights are resident; the activations may come from the previous
+        // kernel of the stream: wait for it only now.
+        if (!waited) {
+            pdl_wait_previous();
+            waited = true;
         }
 #pragma unroll
         for (uint32_t u = 0; u < kUnroll; ++u) {
@@ -853,6 +861,7 @@ __global__ void __launch_bounds__(kGvThreads) gemv_i8_kernel(const GvParams p) {
             for (int o = 16; o > 0; o >>= 1)
                 acc[c][m] += __shfl_xor_sync(0xffffffffu, acc[c][m], o);
 
+    if (!waited) pdl_wait_previous();
     const bool has_bias = p.bias != nullptr;
 #pragma unroll
     for (int c = 0; c < kGvColsPerWarp; ++c) {
@@ -954,12 +963,17 @@ GvParams gv_params(const MatmulI8 &p) {
 
 template <int kM>
 cudaError_t launch_gemv_m(const LaunchCtx &ctx, const GvParams &g, bool aligned) {
-    const unsigned grid = (g.N + kGvColsPerCta - 1) / kGvColsPerCta;
-    if (aligned)
-        gemv_i8_kernel<kM, true><<<grid, kGvThreads, 0, ctx.stream>>>(g);
-    else
-        gemv_i8_kernel<kM, false><<<grid, kGvThreads, 0, ctx.stream>>>(g);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((g.N + kGvColsPerCta - 1) / kGvColsPerCta, 1, 1);
+    cfg.blockDim = dim3(kGvThreads, 1, 1);
+    cfg.stream = ctx.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = std::getenv("VNPU_B200_NO_PDL") ? 0 : 1;
+    if (aligned) return cudaLaunchKernelEx(&cfg, gemv_i8_kernel<kM, true>, g);
+    return cudaLaunchKernelEx(&cfg, gemv_i8_kernel<kM, false>, g);
 }
 
 // Driver entry point for cuTensorMapEncodeTiled, resolved once.
@@ -1183,7 +1197,9 @@ cudaError_t gemv_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
     sp.limit_ns = ctx.wait_limit_ns;
     // Split K over a cluster so that about two CTAs per SM stream weights.
     const uint32_t blocks = (p.N + 127u) / 128u;
-    uint32_t max_c = 8u;
+    // Clusters of 4: measured best on B200 (8-CTA clusters fit the GPCs
+    // less evenly at two CTAs per SM).
+    uint32_t max_c = 4u;
     if (const char *e = std::getenv("VNPU_B200_DECODE_CLUSTER")) max_c = std::max(1, std::atoi(e));
     uint32_t csize = 1;
     while (csize < max_c && blocks * csize * 2u <= 2u * static_cast<uint32_t>(ctx.num_sms) &&
