@@ -163,7 +163,6 @@ constexpr uint32_t kAttBK = 64;
 constexpr uint32_t kAttThreads = 512;
 constexpr uint32_t kAttMaxD = 256;
 constexpr uint32_t kAttMaxChain = kAttMaxD / 8;
-constexpr uint32_t kAttMaxAcc = kAttBQ * kAttMaxD / kAttThreads;  // 8
 
 struct AttParams {
     const float *Q, *K, *V, *mask;
@@ -172,16 +171,21 @@ struct AttParams {
     float scale;
 };
 
+// Layout in shared memory:
+//   Qs [16 q][8 chains][D/8] - chain-major, so a thread reads its chain of a
+//                              query with 16-byte loads (plus the D%8 tail
+//                              [16 q][D%8] after it);
+//   Vs [64 keys][D];  S [16 q][64 keys] scores, then probabilities.
+// Warp q (0..15) owns query q in the softmax and value phases: its online
+// softmax state lives in registers and the two phases need no block barrier.
+template <bool VEC>
 __global__ void __launch_bounds__(kAttThreads) attention_kernel(const AttParams p) {
     extern __shared__ float att_smem[];
     const uint32_t D = p.D;
-    float *Qs = att_smem;                                   // [16][D]
-    float *Vs = Qs + kAttBQ * D;                            // [64][D]
-    float *S = Vs + kAttBK * D;                             // [16][64] scores, then probs
-    float *alpha_s = S + kAttBQ * kAttBK;                   // [16]
-    float *m_s = alpha_s + kAttBQ;                          // [16]
-    float *l_s = m_s + kAttBQ;                              // [16]
-    int *active = reinterpret_cast<int *>(l_s + kAttBQ);    // [16]
+    const uint32_t chains = D / 8, full = chains * 8, tail = D - full;
+    float *Qs = att_smem;                                  // 16*D
+    float *Vs = Qs + kAttBQ * D;                           // 64*D
+    float *S = Vs + kAttBK * D;                            // 16*64
 
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t bh = blockIdx.y;
@@ -196,44 +200,60 @@ __global__ void __launch_bounds__(kAttThreads) attention_kernel(const AttParams 
     const uint32_t causal_offset = p.seq_k > p.seq_q ? p.seq_k - p.seq_q : 0;
 
     for (uint32_t i = tid; i < kAttBQ * D; i += kAttThreads) {
-        const uint32_t q = i / D;
-        Qs[i] = q < qc ? Qh[static_cast<uint64_t>(q0 + q) * D + (i % D)] : 0.0f;
+        const uint32_t q = i / D, e = i % D;
+        const float v = q < qc ? Qh[static_cast<uint64_t>(q0 + q) * D + e] : 0.0f;
+        // element e = 8t + c of the vector part goes to chain c, position t
+        const uint32_t dst = e < full ? q * D + (e & 7u) * chains + (e >> 3) : q * D + e;
+        Qs[dst] = v;
     }
-    if (tid < kAttBQ) {
-        m_s[tid] = -__int_as_float(0x7f800000);
-        l_s[tid] = 0.0f;
-    }
-    float acc[kAttMaxAcc];
-#pragma unroll
-    for (uint32_t r = 0; r < kAttMaxAcc; ++r) acc[r] = 0.0f;
 
-    const uint32_t chains = D / 8;
-    const uint32_t full = chains * 8;
-    // Blocks whose first key is past every query's causal limit are fully
-    // masked: the reference skips them (non-finite block max); so do we.
+    // Per-query state of the query this warp owns (lane-uniform).
+    float m_run = -__int_as_float(0x7f800000), l_run = 0.0f;
+    float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+    float acc_s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+
     uint32_t k_end = p.seq_k;
     if (p.causal) k_end = min(p.seq_k, q0 + qc - 1 + causal_offset + 1);
 
     const uint32_t my_key = tid >> 3, my_chain = tid & 7;
     for (uint32_t k0 = 0; k0 < k_end; k0 += kAttBK) {
         const uint32_t kc = min(kAttBK, p.seq_k - k0);
-        __syncthreads();  // previous block's V / probabilities fully consumed
-        for (uint32_t i = tid; i < kc * D; i += kAttThreads)
-            Vs[i] = Vh[static_cast<uint64_t>(k0) * D + i];
-        // ---- scores
+        __syncthreads();  // previous block's V and probabilities consumed
+        if (VEC) {
+            const float4 *src = reinterpret_cast<const float4 *>(Vh + static_cast<uint64_t>(k0) * D);
+            float4 *dst = reinterpret_cast<float4 *>(Vs);
+            for (uint32_t i = tid; i < kc * D / 4; i += kAttThreads) dst[i] = __ldg(src + i);
+        } else {
+            for (uint32_t i = tid; i < kc * D; i += kAttThreads)
+                Vs[i] = Vh[static_cast<uint64_t>(k0) * D + i];
+        }
+        // ---- scores: thread (key, chain) keeps its chain of K[key] in registers
         float kreg[kAttMaxChain];
         const bool key_ok = my_key < kc;
         const float *krow = Kh + static_cast<uint64_t>(k0 + (key_ok ? my_key : 0)) * D;
 #pragma unroll
         for (uint32_t t = 0; t < kAttMaxChain; ++t)
             kreg[t] = (key_ok && t < chains) ? __ldg(krow + 8 * t + my_chain) : 0.0f;
-        __syncthreads();  // Qs, Vs visible
+        __syncthreads();  // Qs (first block) and Vs visible
         for (uint32_t q = 0; q < qc; ++q) {
-            const float *qrow = Qs + q * D;
+            const float *qchain = Qs + q * D + my_chain * chains;
             float part = 0.0f;
+            if (VEC && (chains & 3u) == 0u) {
 #pragma unroll
-            for (uint32_t t = 0; t < kAttMaxChain; ++t)
-                if (t < chains) part = __fmaf_rn(qrow[8 * t + my_chain], kreg[t], part);
+                for (uint32_t t = 0; t < kAttMaxChain; t += 4) {
+                    if (t < chains) {
+                        const float4 qv = *reinterpret_cast<const float4 *>(qchain + t);
+                        part = __fmaf_rn(qv.x, kreg[t + 0], part);
+                        part = __fmaf_rn(qv.y, kreg[t + 1], part);
+                        part = __fmaf_rn(qv.z, kreg[t + 2], part);
+                        part = __fmaf_rn(qv.w, kreg[t + 3], part);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (uint32_t t = 0; t < kAttMaxChain; ++t)
+                    if (t < chains) part = __fmaf_rn(qchain[t], kreg[t], part);
+            }
             // hsum256 within the 8-lane group
             const float hi = __shfl_down_sync(0xffffffffu, part, 4, 8);
             const float s = __fadd_rn(part, hi);
@@ -242,7 +262,8 @@ __global__ void __launch_bounds__(kAttThreads) attention_kernel(const AttParams 
             const float s23 = __shfl_down_sync(0xffffffffu, s01, 2, 8);
             if (my_chain == 0 && key_ok) {
                 float dot = __fadd_rn(s01, s23);
-                for (uint32_t i = full; i < D; ++i) dot = __fmaf_rn(qrow[i], krow[i], dot);
+                for (uint32_t i = 0; i < tail; ++i)
+                    dot = __fmaf_rn(Qs[q * D + full + i], krow[full + i], dot);
                 const uint32_t qi = q0 + q, ki = k0 + my_key;
                 float sc;
                 if (p.causal && ki > qi + causal_offset) {
@@ -254,58 +275,81 @@ __global__ void __launch_bounds__(kAttThreads) attention_kernel(const AttParams 
                 S[q * kAttBK + my_key] = sc;
             }
         }
-        __syncthreads();
-        // ---- online softmax, one warp per query
-        if (warp < qc) {
-            float* srow = S + warp * kAttBK;
-            float bmax = -__int_as_float(0x7f800000);
-            for (uint32_t j = lane; j < kc; j += 32) bmax = fmaxf(bmax, srow[j]);
-            for (int o = 16; o > 0; o >>= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
-            const bool act = isfinite(bmax);
-            if (act) {
-                const float m_old = m_s[warp];
-                const float nm = fmaxf(m_old, bmax);
-                for (uint32_t j = lane; j < kc; j += 32)
-                    srow[j] = ref_fast_expf(__fsub_rn(srow[j], nm), false);
-                __syncwarp();
-                if (lane == 0) {
-                    const float alpha = ref_fast_expf(__fsub_rn(m_old, nm), false);
-                    float sum_p = 0.0f;
-                    for (uint32_t j = 0; j < kc; ++j) sum_p = __fadd_rn(sum_p, srow[j]);
-                    l_s[warp] = __fadd_rn(__fmul_rn(l_s[warp], alpha), sum_p);
-                    m_s[warp] = nm;
-                    alpha_s[warp] = alpha;
-                }
-            }
-            if (lane == 0) active[warp] = act ? 1 : 0;
-        }
-        __syncthreads();
-        // ---- value accumulation
+        __syncthreads();  // all scores of the block written
+        if (warp >= qc) continue;
+        // ---- online softmax of query `warp` (llm.cpp:516-538)
+        float *srow = S + warp * kAttBK;
+        float bmax = -__int_as_float(0x7f800000);
+        for (uint32_t j = lane; j < kc; j += 32) bmax = fmaxf(bmax, srow[j]);
+        for (int o = 16; o > 0; o >>= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
+        if (!isfinite(bmax)) continue;  // fully masked block: skipped, as in the reference
+        const float nm = fmaxf(m_run, bmax);
+        for (uint32_t j = lane; j < kc; j += 32) srow[j] = ref_fast_expf(__fsub_rn(srow[j], nm), false);
+        const float alpha = ref_fast_expf(__fsub_rn(m_run, nm), false);
+        __syncwarp();
+        float sum_p = 0.0f;
+        if (lane == 0)
+            for (uint32_t j = 0; j < kc; ++j) sum_p = __fadd_rn(sum_p, srow[j]);
+        sum_p = __shfl_sync(0xffffffffu, sum_p, 0);
+        l_run = __fadd_rn(__fmul_rn(l_run, alpha), sum_p);
+        m_run = nm;
+        // ---- values: acc = acc*alpha, then acc = fma(V[j], p_j, acc) in key order
+        if (VEC) {
 #pragma unroll
-        for (uint32_t r = 0; r < kAttMaxAcc; ++r) {
-            const uint32_t idx = tid + r * kAttThreads;
-            if (idx >= qc * D) break;
-            const uint32_t q = idx / D, d = idx % D;
-            if (!active[q]) continue;
-            float a = __fmul_rn(acc[r], alpha_s[q]);
-            const float *prow = S + q * kAttBK;
-            for (uint32_t j = 0; j < kc; ++j) {
-                const float pj = prow[j];
-                if (pj == 0.0f) continue;
-                a = __fmaf_rn(Vs[j * D + d], pj, a);
+            for (uint32_t r = 0; r < 2; ++r) {
+                const uint32_t d4 = lane + 32u * r;
+                if (d4 * 4u >= D) break;
+                float4 a = acc[r];
+                a.x = __fmul_rn(a.x, alpha);
+                a.y = __fmul_rn(a.y, alpha);
+                a.z = __fmul_rn(a.z, alpha);
+                a.w = __fmul_rn(a.w, alpha);
+                for (uint32_t j = 0; j < kc; ++j) {
+                    const float pj = srow[j];
+                    if (pj == 0.0f) continue;
+                    const float4 v = *reinterpret_cast<const float4 *>(Vs + j * D + 4u * d4);
+                    a.x = __fmaf_rn(v.x, pj, a.x);
+                    a.y = __fmaf_rn(v.y, pj, a.y);
+                    a.z = __fmaf_rn(v.z, pj, a.z);
+                    a.w = __fmaf_rn(v.w, pj, a.w);
+                }
+                acc[r] = a;
             }
-            acc[r] = a;
+        } else {
+#pragma unroll
+            for (uint32_t r = 0; r < 8; ++r) {
+                const uint32_t d = lane + 32u * r;
+                if (d >= D) break;
+                float a = __fmul_rn(acc_s[r], alpha);
+                for (uint32_t j = 0; j < kc; ++j) {
+                    const float pj = srow[j];
+                    if (pj == 0.0f) continue;
+                    a = __fmaf_rn(Vs[j * D + d], pj, a);
+                }
+                acc_s[r] = a;
+            }
         }
     }
-    __syncthreads();
+    if (warp < qc) {
+        const float inv = l_run > 0.0f ? __fdiv_rn(1.0f, l_run) : 0.0f;
+        float *orow = p.O + head_q + static_cast<uint64_t>(q0 + warp) * D;
+        if (VEC) {
 #pragma unroll
-    for (uint32_t r = 0; r < kAttMaxAcc; ++r) {
-        const uint32_t idx = tid + r * kAttThreads;
-        if (idx >= qc * D) break;
-        const uint32_t q = idx / D, d = idx % D;
-        const float l = l_s[q];
-        const float inv = l > 0.0f ? __fdiv_rn(1.0f, l) : 0.0f;
-        p.O[head_q + static_cast<uint64_t>(q0 + q) * D + d] = __fmul_rn(acc[r], inv);
+            for (uint32_t r = 0; r < 2; ++r) {
+                const uint32_t d4 = lane + 32u * r;
+                if (d4 * 4u >= D) break;
+                reinterpret_cast<float4 *>(orow)[d4] =
+                    make_float4(__fmul_rn(acc[r].x, inv), __fmul_rn(acc[r].y, inv),
+                                __fmul_rn(acc[r].z, inv), __fmul_rn(acc[r].w, inv));
+            }
+        } else {
+#pragma unroll
+            for (uint32_t r = 0; r < 8; ++r) {
+                const uint32_t d = lane + 32u * r;
+                if (d >= D) break;
+                orow[d] = __fmul_rn(acc_s[r], inv);
+            }
+        }
     }
 }
 
@@ -392,20 +436,22 @@ cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, cons
                       uint32_t seq_q, uint32_t seq_k, uint32_t head_dim, uint32_t causal,
                       float scale) {
     if (head_dim > kAttMaxD || head_dim == 0) return cudaErrorInvalidValue;
-    const size_t smem = sizeof(float) * (kAttBQ * head_dim + kAttBK * head_dim +
-                                         kAttBQ * kAttBK + 3 * kAttBQ) +
-                        sizeof(int) * kAttBQ;
-    static int configured_for = -1;
+    const size_t smem = sizeof(float) * (kAttBQ * head_dim + kAttBK * head_dim + kAttBQ * kAttBK);
+    const bool vec = head_dim % 4 == 0 && (reinterpret_cast<uintptr_t>(V) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(O) & 15) == 0;
+    static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (configured_for != dev) {
-        cudaError_t e = cudaFuncSetAttribute(attention_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(sizeof(float) *
-                                                              (kAttBQ + kAttBK) * kAttMaxD +
-                                                              8192));
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        const int max_smem = static_cast<int>(sizeof(float) * (kAttBQ + kAttBK) * kAttMaxD +
+                                              sizeof(float) * kAttBQ * kAttBK);
+        cudaError_t e = cudaFuncSetAttribute(attention_kernel<true>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(attention_kernel<false>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
         if (e != cudaSuccess) return e;
-        configured_for = dev;
+        configured[dev] = true;
     }
     AttParams ap;
     ap.Q = Q;
@@ -420,7 +466,10 @@ cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, cons
     ap.causal = causal;
     ap.scale = scale;
     dim3 grid((seq_q + kAttBQ - 1) / kAttBQ, batch * heads);
-    attention_kernel<<<grid, kAttThreads, smem, ctx.stream>>>(ap);
+    if (vec)
+        attention_kernel<true><<<grid, kAttThreads, smem, ctx.stream>>>(ap);
+    else
+        attention_kernel<false><<<grid, kAttThreads, smem, ctx.stream>>>(ap);
     count_launch(ctx);
     return cudaGetLastError();
 }
