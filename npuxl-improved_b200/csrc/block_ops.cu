@@ -9,6 +9,7 @@
 // (<= 2 ulp from glibc) with the reference's inverse frequencies computed on
 // the host with the same libm powf.
 #include <cmath>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -353,6 +354,123 @@ __global__ void __launch_bounds__(kAttThreads) attention_kernel(const AttParams 
     }
 }
 
+// Decode attention (one query per head): the same arithmetic as
+// attention_kernel, reorganised for latency.  One CTA per (batch, head):
+//   A. every score of the row at once: thread (key, chain) runs its 16-step
+//      chain (query chain in registers, K from global), hsum256 over the 8
+//      chains, *scale (+mask); keys past the causal limit are -inf;
+//   B. warp 0 walks the 64-key blocks in order: block max, skip if not
+//      finite, p = fast_expf(s - m), alpha, in-order sum; p and alpha are
+//      kept in shared memory;
+//   C. thread d accumulates acc = acc*alpha_b, then fma(V[j][d], p_j, acc)
+//      over the keys in order - the reference's order for every output d.
+constexpr uint32_t kDecThreads = 512;
+constexpr uint32_t kDecMaxKeys = 8192;
+
+__global__ void __launch_bounds__(kDecThreads) attention_decode_kernel(const AttParams p) {
+    extern __shared__ float dec_smem[];
+    const uint32_t D = p.D;
+    const uint32_t chains = D / 8, full = chains * 8, tail = D - full;
+    const uint32_t nblk = (p.seq_k + kAttBK - 1) / kAttBK;
+    float *S = dec_smem;                          // [seq_k] scores, then probabilities
+    float *alpha_b = S + p.seq_k;                 // [nblk]
+    int *active_b = reinterpret_cast<int *>(alpha_b + nblk);  // [nblk]
+    float *l_sh = reinterpret_cast<float *>(active_b + nblk); // [1]
+    float *qv = l_sh + 1;                          // [D]
+
+    const uint32_t tid = threadIdx.x, lane = tid & 31;
+    const uint32_t bh = blockIdx.x;
+    const float *Qh = p.Q + static_cast<uint64_t>(bh) * D;     // seq_q == 1
+    const float *Kh = p.K + static_cast<uint64_t>(bh) * p.seq_k * D;
+    const float *Vh = p.V + static_cast<uint64_t>(bh) * p.seq_k * D;
+    const float *Mh = p.mask ? p.mask + static_cast<uint64_t>(bh) * p.seq_k : nullptr;
+    const uint32_t causal_offset = p.seq_k - 1;   // seq_k > seq_q == 1
+
+    for (uint32_t i = tid; i < D; i += kDecThreads) qv[i] = Qh[i];
+    __syncthreads();
+    // ---- A. scores
+    const uint32_t my_chain = tid & 7, key_lane = tid >> 3;   // 64 keys per pass
+    float qreg[kAttMaxChain];
+#pragma unroll
+    for (uint32_t t = 0; t < kAttMaxChain; ++t) qreg[t] = t < chains ? qv[8 * t + my_chain] : 0.0f;
+    for (uint32_t base = 0; base < p.seq_k; base += kDecThreads / 8) {
+        const uint32_t ki = base + key_lane;
+        const bool key_ok = ki < p.seq_k;
+        const float *krow = Kh + static_cast<uint64_t>(key_ok ? ki : 0) * D;
+        float part = 0.0f;
+#pragma unroll
+        for (uint32_t t = 0; t < kAttMaxChain; ++t)
+            if (t < chains) part = __fmaf_rn(qreg[t], key_ok ? __ldg(krow + 8 * t + my_chain) : 0.0f, part);
+        const float hi = __shfl_down_sync(0xffffffffu, part, 4, 8);
+        const float s = __fadd_rn(part, hi);
+        const float s1 = __shfl_down_sync(0xffffffffu, s, 1, 8);
+        const float s01 = __fadd_rn(s, s1);
+        const float s23 = __shfl_down_sync(0xffffffffu, s01, 2, 8);
+        if (my_chain == 0 && key_ok) {
+            float dot = __fadd_rn(s01, s23);
+            for (uint32_t i = 0; i < tail; ++i) dot = __fmaf_rn(qv[full + i], krow[full + i], dot);
+            float sc;
+            if (p.causal && ki > causal_offset) {
+                sc = -__int_as_float(0x7f800000);
+            } else {
+                sc = __fmul_rn(dot, p.scale);
+                if (Mh) sc = __fadd_rn(sc, Mh[ki]);
+            }
+            S[ki] = sc;
+        }
+    }
+    __syncthreads();
+    // ---- B. online softmax over the blocks, in order (warp 0)
+    if (tid < 32) {
+        float m_run = -__int_as_float(0x7f800000), l_run = 0.0f;
+        for (uint32_t b = 0; b < nblk; ++b) {
+            const uint32_t k0 = b * kAttBK, kc = min(kAttBK, p.seq_k - k0);
+            float *srow = S + k0;
+            float bmax = -__int_as_float(0x7f800000);
+            for (uint32_t j = lane; j < kc; j += 32) bmax = fmaxf(bmax, srow[j]);
+            for (int o = 16; o > 0; o >>= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
+            if (!isfinite(bmax)) {
+                if (lane == 0) active_b[b] = 0;
+                continue;
+            }
+            const float nm = fmaxf(m_run, bmax);
+            for (uint32_t j = lane; j < kc; j += 32) srow[j] = ref_fast_expf(__fsub_rn(srow[j], nm), false);
+            const float alpha = ref_fast_expf(__fsub_rn(m_run, nm), false);
+            __syncwarp();
+            float sum_p = 0.0f;
+            if (lane == 0) {
+                for (uint32_t j = 0; j < kc; ++j) sum_p = __fadd_rn(sum_p, srow[j]);
+                alpha_b[b] = alpha;
+                active_b[b] = 1;
+            }
+            sum_p = __shfl_sync(0xffffffffu, sum_p, 0);
+            l_run = __fadd_rn(__fmul_rn(l_run, alpha), sum_p);
+            m_run = nm;
+            __syncwarp();
+        }
+        if (lane == 0) *l_sh = l_run;
+    }
+    __syncthreads();
+    // ---- C. values, thread d, keys in order
+    const float l = *l_sh;
+    const float inv = l > 0.0f ? __fdiv_rn(1.0f, l) : 0.0f;
+    for (uint32_t d = tid; d < D; d += kDecThreads) {
+        float a = 0.0f;
+        for (uint32_t b = 0; b < nblk; ++b) {
+            if (!active_b[b]) continue;
+            a = __fmul_rn(a, alpha_b[b]);
+            const uint32_t k0 = b * kAttBK, kc = min(kAttBK, p.seq_k - k0);
+#pragma unroll 8
+            for (uint32_t j = 0; j < kc; ++j) {
+                const float pj = S[k0 + j];
+                const float v = __ldg(Vh + static_cast<uint64_t>(k0 + j) * D + d);
+                if (pj != 0.0f) a = __fmaf_rn(v, pj, a);
+            }
+        }
+        p.O[static_cast<uint64_t>(bh) * D + d] = __fmul_rn(a, inv);
+    }
+}
+
 // Spins on a flag nothing sets, bounded by limit_ns: the device-side wait
 // pattern of the GEMM pipeline, exercised on its own.
 __global__ void wait_probe_kernel(const uint32_t *flag, uint64_t limit_ns, uint32_t *err) {
@@ -465,6 +583,22 @@ cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, cons
     ap.D = head_dim;
     ap.causal = causal;
     ap.scale = scale;
+    if (seq_q == 1 && seq_k <= kDecMaxKeys && std::getenv("VNPU_B200_ATTN_GENERAL") == nullptr) {
+        const uint32_t nblk = (seq_k + kAttBK - 1) / kAttBK;
+        const size_t dsmem = sizeof(float) * (seq_k + nblk + nblk + 1 + head_dim);
+        static bool dec_configured[64] = {};
+        if (dev >= 0 && dev < 64 && !dec_configured[dev]) {
+            const cudaError_t e = cudaFuncSetAttribute(
+                attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                static_cast<int>(sizeof(float) * (kDecMaxKeys + 2 * (kDecMaxKeys / kAttBK) + 1 +
+                                                  kAttMaxD)));
+            if (e != cudaSuccess) return e;
+            dec_configured[dev] = true;
+        }
+        attention_decode_kernel<<<batch * heads, kDecThreads, dsmem, ctx.stream>>>(ap);
+        count_launch(ctx);
+        return cudaGetLastError();
+    }
     dim3 grid((seq_q + kAttBQ - 1) / kAttBQ, batch * heads);
     if (vec)
         attention_kernel<true><<<grid, kAttThreads, smem, ctx.stream>>>(ap);
