@@ -329,6 +329,66 @@ def gemv_secondary(lib, dev, st, torch, M, K=4096, N=4096, copies=32, rounds=8):
             "weight_copies": copies, "kernel": lib.b200_matmul_kernel(M, K, N, 0, A8.data_ptr()).decode()}
 
 
+def llm_block_secondary(lib, dev, torch, prefill=512, decode=128, with_reference=True):
+    """d=4096, 32 heads, I=11008, prefill `prefill` tokens then
+    `decode` KV-cached steps (one CUDA graph per step, replayed)."""
+    from llm_block import B200Block, BlockConfig, HostBlock, weight_bytes
+    cfg = BlockConfig(cap=prefill + decode)
+    blk = B200Block(cfg, lib, dev, torch)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    x = torch.empty((prefill, cfg.d), device="cuda").normal_(0, 1, generator=g)
+    st = Stream(lib, dev)
+    blk.forward(x, 0)                         # warm-up (and fills the cache)
+    dev.sync()
+    blk.kc.zero_()
+    blk.vc.zero_()
+    blk.mask.fill_(float("-inf"))
+    e0 = st.event()
+    blk.forward(x, 0)
+    e1 = st.event()
+    dev.sync()
+    e1.synchronize()
+    ms_prefill = e0.elapsed_time(e1)
+    xin = blk._buf("decode_in", (1, cfg.d))
+    xin.normal_(0, 1, generator=g)
+    blk.pos.fill_(prefill)
+    torch.cuda.synchronize()
+    blk.capture_decode(xin)
+    blk.pos.fill_(prefill)
+    torch.cuda.synchronize()
+    e0 = st.event()
+    for _ in range(decode):
+        blk.replay_decode()
+    e1 = st.event()
+    e1.synchronize()
+    ms_decode = e0.elapsed_time(e1)
+    blk.close()
+    out = {"config": f"d={cfg.d} heads={cfg.heads} I={cfg.inter} prefill {prefill} + {decode} decode",
+           "prefill_ms": ms_prefill, "prefill_tok_s": prefill / ms_prefill * 1e3,
+           "decode_ms_per_token": ms_decode / decode, "decode_tok_s": decode / ms_decode * 1e3,
+           "decode_weight_gbs": weight_bytes(cfg) / (ms_decode / decode) / 1e6,
+           "decode": "one CUDA graph per token step (vnpu commands + torch layout glue)"}
+    if with_reference and os.path.exists(REF_LIB):
+        import time as _time
+        os.environ.setdefault("VNPU_FORCE_ISA", "avx2")
+        ref = HostBlock(cfg, lib=vnpu.Lib(REF_LIB), threads=os.cpu_count() or 1)
+        xh = np.random.default_rng(11).normal(0, 1, (prefill, cfg.d)).astype(np.float32)
+        t0 = _time.perf_counter()
+        ref.forward(xh, 0)
+        t_pre = _time.perf_counter() - t0
+        steps = 8
+        t0 = _time.perf_counter()
+        for i in range(steps):
+            ref.forward(np.random.default_rng(i).normal(0, 1, (1, cfg.d)).astype(np.float32),
+                        prefill + i)
+        t_dec = (_time.perf_counter() - t0) / steps
+        ref.close()
+        out["reference_cpu"] = {"prefill_tok_s": prefill / t_pre, "decode_tok_s": 1.0 / t_dec,
+                                "cores": os.cpu_count(), "decode_sample_steps": steps,
+                                "kind": "reference", "isa": "avx2"}
+    return out
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -449,6 +509,9 @@ def run_b200(args):
                 gv = gemv_secondary(lib, dev, st, torch, m)
                 gv["frac_of_hbm"] = gv["gbs"] / pk["hbm_gbs"]
                 secondary[f"gemv_m{m}"] = gv
+            if not args.no_block:
+                secondary["llm_block"] = llm_block_secondary(
+                    lib, dev, torch, with_reference=not args.no_cpu_baseline)
             try:
                 A_ = torch.randint(-128, 128, (8192, 8192), dtype=torch.int8, device="cuda")
                 B_ = torch.randint(-128, 128, (8192, 8192), dtype=torch.int8, device="cuda").t()
@@ -564,6 +627,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-block", action="store_true", help="skip the decoder-block secondary")
     ap.add_argument("--kernel-case", default=None,
                     help="run one small kernel case twice and exit (ncu captures)")
     args = ap.parse_args()

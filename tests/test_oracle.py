@@ -174,3 +174,26 @@ def test_block_ops_vs_reference(ref_lib, oracle, H, sq, sk, D):
         Y = np.empty_like(X)
         d.rmsnorm(X, None, Y, X.shape[0], X.shape[1], 1e-6)
         assert bits_equal(Y, oracle.rmsnorm(X, None, 1e-6, 0))
+
+
+def test_block_driver_host_matches_reference(ref_lib, oracle):
+    """The decoder-block driver on host arrays: the oracle restatement and the
+    reference library give the same bits for prefill and KV-cached decode."""
+    from llm_block import BlockConfig, HostBlock
+    cfg = BlockConfig(d=128, heads=4, inter=352, cap=40)
+    rng = np.random.default_rng(3)
+    x = rng.normal(0, 1, (9, cfg.d)).astype(np.float32)
+    os.environ["VNPU_FORCE_ISA"] = "avx2"
+    try:
+        ref = HostBlock(cfg, lib=ref_lib, threads=4)
+    finally:
+        os.environ.pop("VNPU_FORCE_ISA", None)
+    orc = HostBlock(cfg, oracle=oracle)
+    try:
+        assert bits_equal(ref.forward(x, 0), orc.forward(x, 0))
+        for p in range(9, 13):
+            t = rng.normal(0, 1, (1, cfg.d)).astype(np.float32)
+            assert bits_equal(ref.forward(t, p), orc.forward(t, p)), p
+    finally:
+        ref.close()
+        orc.close()
