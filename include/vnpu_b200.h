@@ -85,6 +85,43 @@ VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_graph_launch(vnpu_b200_graph_t *graph
                                                        vnpu_stream_t *stream);
 VNPU_API void VNPU_CALL vnpu_b200_graph_destroy(vnpu_b200_graph_t *graph);
 
+/*
+ * Per-tensor QUANTIZE_I8 (VNPU_QUANT_PER_TENSOR) that allocates nothing.  No
+ * reference counterpart: the reference quantizes on host memory it already
+ * owns.  Same bits as vnpu_quantize_i8 with axis PER_TENSOR (reference
+ * src/kernels/llm.cpp:421-436).
+ *
+ * For callers that cannot allocate device memory at the point of the call and
+ * hold no vnpu stream (whose creation allocates its error and scratch words):
+ * an engine that reserved all of HBM for weights and its KV-cache pool at
+ * start-up, or code on an out-of-memory path.  The scratch is a static device
+ * array inside this library (65,792 bytes per device); the call makes no
+ * cudaMalloc/cudaMallocAsync/cudaFree and no allocating library call.
+ *
+ * X (rows*cols f32), Y (rows*cols int8) and scale (1 f32) are device memory of
+ * CUDA device `device`; cuda_stream is a cudaStream_t of that device (NULL =
+ * its legacy default stream).  The work is enqueued on the stream; nothing
+ * synchronises.  The device is made current for the call and the caller's
+ * current device is restored.
+ *
+ * Limits and errors (VNPU_ERR_INVALID_ARGUMENT, with a line on stderr, before
+ * anything is enqueued): rows*cols above 2^28 elements (the static scratch
+ * holds one partial maximum per 2^14 elements, for 2^14 chunks), a zero size,
+ * a NULL or host pointer, or a pointer on another device.
+ *
+ * The first call on each device looks up the scratch address
+ * (cudaGetSymbolAddress, with that device current) and zeroes its counter
+ * word with a synchronous cudaMemset; make that first call before any stream
+ * capture on the device.
+ *
+ * There is one scratch per device and process: calls that can overlap on the
+ * same device (different streams with no ordering between them, or several
+ * host threads) race on it and give wrong results.  Order such calls.
+ */
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_quantize_i8_tensor_noalloc(
+    int device, void *cuda_stream, const float *X, int8_t *Y, float *scale, uint64_t rows,
+    uint64_t cols);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

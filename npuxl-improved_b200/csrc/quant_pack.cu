@@ -7,6 +7,10 @@
 //   with std::max(maxabs, |x|).
 // All of it is HBM-bound byte work: rows are read once (kept in registers
 // when they fit), written once.
+#include <cstdio>
+#include <mutex>
+
+#include "../../include/vnpu_b200.h"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -282,3 +286,165 @@ cudaError_t pack_weights(const LaunchCtx &ctx, const int8_t *B, uint32_t K, uint
 }
 
 }  // namespace vnpu_b200
+
+// ---------------------------------------------------------------------------
+// Per-tensor QUANTIZE_I8 that allocates nothing (vnpu_b200_quantize_i8_tensor_noalloc).
+//
+// Same bits as quantize_tensor(): the tensor's absmax is an order-free max.
+// Its scratch is one file-scope device array per device instead of the vnpu
+// stream's scratch word:
+//   words [0, kNoAllocMaxChunks)  one partial absmax per CTA of pass 1 (each
+//                                 is written before it is read: no clearing)
+//   word  kNoAllocCounter         CTAs of pass 1 that have finished; must be
+//                                 zero when a call starts.  Zeroed when the
+//                                 address is first looked up, and the last CTA
+//                                 of every call puts it back to zero.
+//   word  kNoAllocResult          the tensor absmax (IEEE bits), pass 2 reads it
+// Pass 1 gives each CTA a fixed chunk of kNoAllocChunk elements, so the scratch
+// bounds the tensor at kNoAllocChunk * kNoAllocMaxChunks elements (2^28 = 1 GiB
+// of f32); larger tensors are rejected before anything is launched.
+// ---------------------------------------------------------------------------
+namespace vnpu_b200 {
+namespace {
+
+constexpr uint64_t kNoAllocChunk = 1ull << 14;
+constexpr uint32_t kNoAllocMaxChunks = 1u << 14;
+constexpr uint32_t kNoAllocCounter = kNoAllocMaxChunks;       // own 128-byte line
+constexpr uint32_t kNoAllocResult = kNoAllocMaxChunks + 32;   // own 128-byte line
+constexpr uint32_t kNoAllocWords = kNoAllocMaxChunks + 64;    // 65,792 bytes
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) uint32_t g_quant_noalloc_scratch[kNoAllocWords];
+
+// Pass 1: CTA c takes elements [c * kNoAllocChunk, (c + 1) * kNoAllocChunk).
+// The last CTA to finish (threadfence-reduction pattern) folds the partials.
+__global__ void __launch_bounds__(256) tensor_absmax_chunks_kernel(const float *__restrict__ X,
+                                                                   uint64_t n,
+                                                                   uint32_t *scratch) {
+    __shared__ float red[32];
+    __shared__ bool last;
+    const uint64_t base = static_cast<uint64_t>(blockIdx.x) * kNoAllocChunk;
+    const uint64_t end = base + kNoAllocChunk < n ? base + kNoAllocChunk : n;
+    float m = 0.0f;
+#pragma unroll 8
+    for (uint64_t i = base + threadIdx.x; i < end; i += 256) m = fmaxf(m, fabsf(__ldcs(X + i)));
+    m = block_max(m, red);
+    if (threadIdx.x == 0) {
+        scratch[blockIdx.x] = __float_as_uint(m);
+        __threadfence();
+        last = atomicAdd(scratch + kNoAllocCounter, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    uint32_t bits = 0;  // partials are >= 0 (or +inf): IEEE bits order as unsigned
+    for (uint32_t c = threadIdx.x; c < gridDim.x; c += 256) bits = max(bits, __ldcg(scratch + c));
+    m = block_max(__uint_as_float(bits), red);
+    if (threadIdx.x == 0) {
+        scratch[kNoAllocResult] = __float_as_uint(m);
+        scratch[kNoAllocCounter] = 0;
+    }
+}
+
+struct NoAllocDevice {
+    uint32_t *scratch = nullptr;
+    int num_sms = 0;
+};
+NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
+
+void noalloc_error(const char *what) {
+    std::fprintf(stderr, "[vnpu-b200] vnpu_b200_quantize_i8_tensor_noalloc: %s\n", what);
+}
+
+// The scratch address of `device` (the current device).  Looked up once per
+// device; the first call also zeroes the counter synchronously.
+vnpu_status_t noalloc_device(int device, NoAllocDevice *out) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    NoAllocDevice &d = g_noalloc_dev[device];
+    if (!d.scratch) {
+        void *p = nullptr;
+        int sms = 0;
+        if (cudaGetSymbolAddress(&p, g_quant_noalloc_scratch) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+            cudaMemset(static_cast<uint32_t *>(p) + kNoAllocCounter, 0, sizeof(uint32_t)) !=
+                cudaSuccess) {
+            cudaGetLastError();
+            noalloc_error("cannot resolve the static scratch on this device");
+            return VNPU_ERR_DEVICE_ERROR;
+        }
+        d.scratch = static_cast<uint32_t *>(p);
+        d.num_sms = sms;
+    }
+    *out = d;
+    return VNPU_OK;
+}
+
+bool on_device(const void *p, int device) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) &&
+           a.device == device;
+}
+
+vnpu_status_t quantize_tensor_noalloc(int device, cudaStream_t stream, const float *X, int8_t *Y,
+                                      float *scale, uint64_t rows, uint64_t cols) {
+    if (!X || !Y || !scale || !rows || !cols) {
+        noalloc_error("X, Y and scale must be non-null and rows, cols non-zero");
+        return VNPU_ERR_INVALID_ARGUMENT;
+    }
+    if (rows > (kNoAllocChunk * kNoAllocMaxChunks) / cols) {
+        char msg[160];
+        std::snprintf(msg, sizeof msg,
+                      "rows*cols exceeds the static scratch limit of %llu elements",
+                      static_cast<unsigned long long>(kNoAllocChunk * kNoAllocMaxChunks));
+        noalloc_error(msg);
+        return VNPU_ERR_INVALID_ARGUMENT;
+    }
+    if (!on_device(X, device) || !on_device(Y, device) || !on_device(scale, device)) {
+        noalloc_error("X, Y and scale must be device memory of the given device");
+        return VNPU_ERR_INVALID_ARGUMENT;
+    }
+    NoAllocDevice d;
+    const vnpu_status_t st = noalloc_device(device, &d);
+    if (st != VNPU_OK) return st;
+    const uint64_t n = rows * cols;
+    const unsigned chunks = static_cast<unsigned>((n + kNoAllocChunk - 1) / kNoAllocChunk);
+    tensor_absmax_chunks_kernel<<<chunks, 256, 0, stream>>>(X, n, d.scratch);
+    quantize_tensor_kernel<<<static_cast<unsigned>(d.num_sms) * 8, 256, 0, stream>>>(
+        X, Y, scale, n, d.scratch + kNoAllocResult);
+    if (cudaGetLastError() != cudaSuccess) {
+        noalloc_error("kernel launch failed");
+        return VNPU_ERR_DEVICE_ERROR;
+    }
+    return VNPU_OK;
+}
+
+}  // namespace
+}  // namespace vnpu_b200
+
+extern "C" VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_quantize_i8_tensor_noalloc(
+    int device, void *cuda_stream, const float *X, int8_t *Y, float *scale, uint64_t rows,
+    uint64_t cols) {
+    int count = 0;
+    if (device < 0 || device >= vnpu_b200::kNoAllocMaxDevices ||
+        cudaGetDeviceCount(&count) != cudaSuccess || device >= count) {
+        cudaGetLastError();
+        vnpu_b200::noalloc_error("no such CUDA device");
+        return VNPU_ERR_INVALID_ARGUMENT;
+    }
+    int prev = -1;
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != device && cudaSetDevice(device) != cudaSuccess) {
+        cudaGetLastError();
+        vnpu_b200::noalloc_error("cannot make the device current");
+        return VNPU_ERR_DEVICE_ERROR;
+    }
+    const vnpu_status_t st = vnpu_b200::quantize_tensor_noalloc(
+        device, static_cast<cudaStream_t>(cuda_stream), X, Y, scale, rows, cols);
+    if (prev >= 0 && prev != device) cudaSetDevice(prev);
+    return st;
+}
