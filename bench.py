@@ -451,10 +451,11 @@ def run_b200(args):
         barrier()
         # ---- the GEMM kernel alone (roofline), still under the clock sampler
         ms_gemm = max_over_ranks(time_loop(lib, dev, st, [mm], max(3, args.steps)))
+        gemm_kernel = lib.b200_last_matmul_kernel().decode()
     ops_rank = 2.0 * M * K * n
     int8_peak = 2.0 * pk["bf16"]
     achieved = ops_rank / ms_gemm / 1e9
-    traffic = profile_traffic(f"gemm_i8_tcgen05:{M}x{K}x{n}")
+    traffic = profile_traffic(f"{gemm_kernel}:{M}x{K}x{n}")
 
     # ---- e2e through the C ABI with host buffers (pinned)
     hA = torch.empty((M, K), dtype=torch.float32).uniform_(-1, 1).pin_memory()
@@ -542,7 +543,8 @@ def run_b200(args):
                        "epilogue": "none", "bias": False, "parallelism": f"column shard x{world}",
                        "l2": "inputs larger than L2 (A f32 256 MiB, B int8 224 MiB/P, C f32 896 MiB/P)",
                        "step": "QUANTIZE_I8(A) + MATMUL_I8"},
-            "roofline": {"bound": "tensor", "kernel": "gemm_i8_tcgen05_kernel",
+            "roofline": {"bound": "tensor",
+                         "kernel": gemm_kernel,
                          "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
                          "frac": achieved / int8_peak, "traffic": traffic,
                          "peak_source": f"2 x {pk['source']} bf16 dense ({pk['bf16']} TFLOP/s); "

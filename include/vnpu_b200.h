@@ -60,6 +60,12 @@ VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_packed_weights_device(
 VNPU_API const char * VNPU_CALL vnpu_b200_matmul_i8_kernel(uint32_t M, uint32_t K, uint32_t N,
                                                           uint32_t lda, const void *A);
 
+/* Name of the kernel the most recent MATMUL_I8 launch in this process used
+ * ("gemm_i8_tcgen05_pair_wide_kernel", "gemm_i8_tcgen05_pair_kernel",
+ * "gemm_i8_tcgen05_kernel", "gemv_i8_tcgen05_kernel", "gemv_i8_kernel",
+ * "gemm_i8_simt_kernel"; "none" before the first); for tests and the bench. */
+VNPU_API const char * VNPU_CALL vnpu_b200_last_matmul_kernel(void);
+
 /* Device-side wait self-test: launches a kernel that waits on a flag nothing
  * sets, bounded by timeout_us, and returns VNPU_ERR_TIMEOUT when the bound is
  * hit (VNPU_OK would mean the flag was seen).  It exercises the same bounded

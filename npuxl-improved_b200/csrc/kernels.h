@@ -71,6 +71,8 @@ enum class MatmulKernel { kTcgen05, kGemv, kSimt };
 MatmulKernel choose_matmul_kernel(uint32_t M, uint32_t K, uint32_t N, uint32_t lda,
                                   const void *A);
 const char *matmul_kernel_name(MatmulKernel k);
+// Kernel the most recent MATMUL_I8 launch used (any thread, any device).
+const char *last_matmul_kernel();
 
 cudaError_t matmul_i8(const LaunchCtx &ctx, const MatmulI8 &p);
 // Individual kernels (tests pin each against the oracle).

@@ -1377,6 +1377,8 @@ VNPU_API const char *VNPU_CALL vnpu_b200_matmul_i8_kernel(uint32_t M, uint32_t K
     return matmul_kernel_name(choose_matmul_kernel(M, K, N, lda ? lda : K, A));
 }
 
+VNPU_API const char *VNPU_CALL vnpu_b200_last_matmul_kernel(void) { return last_matmul_kernel(); }
+
 VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_selftest_wait_timeout(vnpu_stream_t *stream,
                                                                 uint32_t timeout_us) {
     if (!stream || !timeout_us || timeout_us > 10000000u) return VNPU_ERR_INVALID_ARGUMENT;

@@ -260,6 +260,7 @@ class Lib:
             self.b200_kernel_launches = _sig(h, "vnpu_b200_kernel_launches", u64, vp)
             self.b200_matmul_kernel = _sig(h, "vnpu_b200_matmul_i8_kernel", C.c_char_p, u32, u32,
                                            u32, u32, vp)
+            self.b200_last_matmul_kernel = _sig(h, "vnpu_b200_last_matmul_kernel", C.c_char_p)
             self.b200_selftest_wait = _sig(h, "vnpu_b200_selftest_wait_timeout", _ST, vp, u32)
             self.b200_packed_device = _sig(h, "vnpu_b200_packed_weights_device", _ST, vp,
                                            C.POINTER(vp), C.POINTER(u32), C.POINTER(vp))

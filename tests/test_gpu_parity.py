@@ -340,10 +340,49 @@ def test_pair_and_single_cta_kernels_agree(gpu, oracle, monkeypatch, M, K, N):
         if no_pair:
             monkeypatch.setenv("VNPU_B200_NO_PAIR", "1")
         outs.append(run_matmul(gpu, A, B, sa, sb, bias, 3, 0))
+        # Rows of A that are not 16-byte aligned (K % 16) cannot be TMA
+        # sources: both runs then take the SIMT kernel.
+        assert gpu.lib.b200_last_matmul_kernel().decode() == (
+            "gemm_i8_simt_kernel" if K % 16 else
+            "gemm_i8_tcgen05_kernel" if no_pair else "gemm_i8_tcgen05_pair_kernel")
     monkeypatch.delenv("VNPU_B200_NO_PAIR", raising=False)
     assert bits_equal(outs[0], outs[1])
     rows = np.arange(0, M, 13)
     assert bits_equal(outs[0][rows], oracle.matmul_i8(A[rows], B, sa[rows], sb, bias, 3, 0))
+
+
+@pytest.mark.parametrize("M,K,N,epi,form,pad", [
+    (129, 256, 256, 3, 0, 0),      # one partial 256x512 tile
+    (300, 1008, 700, 2, 0, 0),     # ragged K (8 k-blocks), ragged N
+    (257, 128, 513, 1, 1, 0),      # one k-block: the held-stage prologue is the whole tile
+    (512, 384, 1024, 2, 2, 0),     # three k-blocks < four stages
+    (1024, 2048, 1536, 4, 0, 0),
+    (2000, 640, 2056, 2, 0, 3),    # ldc % 4 != 0: direct stores instead of TMA
+    (4096, 4096, 4096, 0, 0, 0),   # 128 tiles: more than one wave of pairs
+])
+def test_wide_pair_kernel_agrees(gpu, oracle, monkeypatch, M, K, N, epi, form, pad):
+    """The 256x512 CTA-pair kernel (two accumulators in all 512 TMEM columns,
+    D1 deferred at each tile start) gives the same bits as the 256x256 pair
+    kernel and the oracle."""
+    rng = np.random.default_rng(M * 3 + K + N)
+    A, sa = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
+    B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
+    bias = rng.normal(0, 0.01, N).astype(np.float32)
+    ldc = N + pad if pad else 0
+    outs = []
+    for wide in ("1", "0"):
+        monkeypatch.setenv("VNPU_B200_PAIR_WIDE", wide)
+        Cbuf = np.full((M, ldc), np.nan, np.float32) if pad else None
+        C = run_matmul(gpu, A, B, sa, sb, bias, epi, form, ldc=ldc, Cbuf=Cbuf)
+        assert gpu.lib.b200_last_matmul_kernel().decode() == (
+            "gemm_i8_tcgen05_pair_wide_kernel" if wide == "1" else "gemm_i8_tcgen05_pair_kernel")
+        outs.append(C[:, :N].copy())
+        if pad:
+            assert np.isnan(C[:, N:]).all()   # nothing written past N
+    monkeypatch.delenv("VNPU_B200_PAIR_WIDE", raising=False)
+    assert bits_equal(outs[0], outs[1])
+    rows = np.unique(np.r_[np.arange(0, M, 17), M - 1])
+    assert bits_equal(outs[0][rows], oracle.matmul_i8(A[rows], B, sa[rows], sb, bias, epi, form))
 
 
 @pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8])
