@@ -40,7 +40,11 @@ extern "C" {
 #define VNPU_CMD_FLAG_EPI_SCALAR   (1u << 9)
 
 /* The cudaStream_t behind a vnpu stream (as void*), so callers can order
- * their own CUDA work and timing events against it. */
+ * their own CUDA work and timing events against its kernels.  Copies of host
+ * operands run on two further streams of the vnpu stream (uploads, downloads)
+ * joined to this one by events: work ordered after this handle sees a
+ * command's kernels but not the download of its host outputs, which vnpu
+ * events and vnpu_stream_sync do cover. */
 VNPU_API void * VNPU_CALL vnpu_b200_stream_handle(vnpu_stream_t *stream);
 
 /* CUDA device ordinal of a vnpu device. */

@@ -103,10 +103,39 @@ Mem classify(const void *p, int device) {
     }
 }
 
+// Order stream `waiter` after everything enqueued on `signaller` so far.
+void stream_after(cudaStream_t waiter, cudaStream_t signaller) {
+    cudaEvent_t ev = nullptr;
+    cuda_check(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "order event");
+    cudaError_t e = cudaEventRecord(ev, signaller);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(waiter, ev, 0);
+    cudaEventDestroy(ev);
+    cuda_check(e, "stream order");
+}
+
+// Join every pending download into the compute and upload streams.
+void join_downloads(vnpu_stream_t *s) {
+    if (s->pending_down.empty()) return;
+    stream_after(s->cs, s->down);
+    stream_after(s->up, s->down);
+    s->pending_down.clear();
+}
+
+bool overlaps_download(const vnpu_stream_t *s, const void *p, uint64_t bytes) {
+    const char *a = static_cast<const char *>(p);
+    for (const auto &r : s->pending_down)
+        if (a < r.first + r.second && r.first < a + bytes) return true;
+    return false;
+}
+
 class Staging {
 public:
+    // Copies on `s` itself (device-level paths without a vnpu stream).
     Staging(cudaStream_t s, int device, bool capturing = false)
         : s_(s), device_(device), capturing_(capturing) {}
+    // Copies on the vnpu stream's copy-engine streams.
+    explicit Staging(vnpu_stream_t *vs)
+        : s_(vs->cs), device_(vs->device->ordinal), capturing_(vs->capturing), vs_(vs) {}
     ~Staging() {
         for (auto &a : allocs_) cudaFreeAsync(a, s_);
     }
@@ -121,12 +150,32 @@ public:
     T *out(T *p, uint64_t bytes, bool read_too) {
         return static_cast<T *>(stage(p, bytes, read_too, true));
     }
-    // Copy staged outputs back, in stream order.
+    // Copy staged outputs back after the command's kernels.
     void finish() {
-        for (auto &o : outs_)
-            cuda_check(cudaMemcpyAsync(o.host, o.dev, o.bytes, cudaMemcpyDeviceToHost, s_),
+        if (outs_.empty()) return;
+        if (!vs_) {
+            for (auto &o : outs_)
+                cuda_check(cudaMemcpyAsync(o.host, o.dev, o.bytes, cudaMemcpyDeviceToHost, s_),
+                           "copy result to host");
+            outs_.clear();
+            return;
+        }
+        stream_after(vs_->down, s_);
+        for (auto &o : outs_) {
+            cuda_check(cudaMemcpyAsync(o.host, o.dev, o.bytes, cudaMemcpyDeviceToHost, vs_->down),
                        "copy result to host");
+            vs_->pending_down.emplace_back(static_cast<const char *>(o.host), o.bytes);
+        }
+        // Output buffers are released behind their download.
+        for (auto &o : outs_) {
+            auto it = std::find(allocs_.begin(), allocs_.end(), o.dev);
+            if (it != allocs_.end()) {
+                allocs_.erase(it);
+                cudaFreeAsync(o.dev, vs_->down);
+            }
+        }
         outs_.clear();
+        if (vs_->pending_down.size() > 256) join_downloads(vs_);
     }
     uint64_t staged_bytes() const { return staged_; }
 
@@ -145,11 +194,26 @@ private:
             return it->second;
         }
         void *d = nullptr;
-        cuda_check(cudaMallocAsync(&d, bytes, s_), "stage operand");
-        allocs_.push_back(d);
+        if (vs_ && copy_in) {
+            // Upload on the copy-engine stream, after any pending download
+            // into the same host bytes and any host write made on `cs`.
+            if (overlaps_download(vs_, p, bytes)) join_downloads(vs_);
+            if (vs_->cs_wrote_host) {
+                stream_after(vs_->up, s_);
+                vs_->cs_wrote_host = false;
+            }
+            cuda_check(cudaMallocAsync(&d, bytes, vs_->up), "stage operand");
+            allocs_.push_back(d);
+            cuda_check(cudaMemcpyAsync(d, p, bytes, cudaMemcpyHostToDevice, vs_->up), "stage in");
+            stream_after(s_, vs_->up);
+        } else {
+            cuda_check(cudaMallocAsync(&d, bytes, s_), "stage operand");
+            allocs_.push_back(d);
+            if (copy_in)
+                cuda_check(cudaMemcpyAsync(d, p, bytes, cudaMemcpyHostToDevice, s_), "stage in");
+        }
         map_[p] = d;
         staged_ += bytes;
-        if (copy_in) cuda_check(cudaMemcpyAsync(d, p, bytes, cudaMemcpyHostToDevice, s_), "stage in");
         if (copy_out) outs_.push_back({p, d, bytes});
         return d;
     }
@@ -161,6 +225,7 @@ private:
     cudaStream_t s_;
     int device_;
     bool capturing_;
+    vnpu_stream_t *vs_ = nullptr;
     std::vector<void *> allocs_;
     std::vector<Out> outs_;
     std::unordered_map<void *, void *> map_;
@@ -212,7 +277,7 @@ void exec_matmul_i8(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags,
     const uint32_t lda = in.lda ? in.lda : in.K;
     const uint32_t ldc = in.ldc ? in.ldc : in.N;
     if (lda < in.K || ldc < in.N) throw CommandError("invalid int8 leading dimensions");
-    Staging st(s->cs, s->device->ordinal, s->capturing);
+    Staging st(s);
     MatmulI8 p;
     p.A = st.in(in.A, static_cast<uint64_t>(in.M - 1) * lda + in.K);
     p.lda = lda;
@@ -254,7 +319,7 @@ void exec_quantize_i8(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchC
     const uint64_t nscales = a.axis == VNPU_QUANT_PER_ROW      ? a.rows
                              : a.axis == VNPU_QUANT_PER_COLUMN ? a.cols
                                                                : 1;
-    Staging st(s->cs, s->device->ordinal, s->capturing);
+    Staging st(s);
     const float *X = st.in(a.X, total * sizeof(float));
     int8_t *Y = st.out(a.Y, total, false);
     float *sc = st.out(a.scales, nscales * sizeof(float), false);
@@ -279,7 +344,7 @@ void exec_rmsnorm(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &
     const auto &a = cmd.args.rmsnorm;
     if (!a.X || !a.Y || !a.rows || !a.cols) throw CommandError("invalid rmsnorm arguments");
     const uint64_t n = static_cast<uint64_t>(a.rows) * a.cols;
-    Staging st(s->cs, s->device->ordinal, s->capturing);
+    Staging st(s);
     float *Y = st.out(a.Y, n * sizeof(float), a.Y == a.X);
     const float *X = st.in(a.X, n * sizeof(float));
     const float *W = st.in(a.W, sizeof(float) * a.cols);
@@ -314,7 +379,7 @@ void exec_rope(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &ctx
     const uint64_t qn = static_cast<uint64_t>(a.batch) * a.heads * a.q_seq * a.head_dim;
     const uint64_t kn = static_cast<uint64_t>(a.batch) * a.heads * a.k_seq * a.head_dim;
     const uint32_t seq = std::max(a.q_seq, a.k_seq);
-    Staging st(s->cs, s->device->ordinal, s->capturing);
+    Staging st(s);
     float *Q = st.out(a.Q, qn * sizeof(float), true);
     float *K = st.out(a.K, kn * sizeof(float), true);
     const int32_t *pos = st.in(a.positions, sizeof(int32_t) * seq);
@@ -335,7 +400,7 @@ void exec_swiglu(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &c
     const auto &a = cmd.args.swiglu;
     if (!a.gate || !a.up || !a.Y || !a.count) throw CommandError("invalid swiglu arguments");
     const uint64_t bytes = a.count * sizeof(float);
-    Staging st(s->cs, s->device->ordinal, s->capturing);
+    Staging st(s);
     float *Y = st.out(a.Y, bytes, a.Y == a.gate || a.Y == a.up);
     const float *G = st.in(a.gate, bytes);
     const float *U = st.in(a.up, bytes);
@@ -354,7 +419,7 @@ void exec_add(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &ctx,
     if (!a.A || !a.B || !a.Y || !a.count) throw CommandError("invalid binary arguments");
     const bool dflt = a.alpha == 0.0f && a.beta == 0.0f;
     const uint64_t bytes = a.count * sizeof(float);
-    Staging st(s->cs, s->device->ordinal, s->capturing);
+    Staging st(s);
     float *Y = st.out(a.Y, bytes, a.Y == a.A || a.Y == a.B);
     const float *A = st.in(a.A, bytes);
     const float *B = st.in(a.B, bytes);
@@ -382,7 +447,7 @@ void exec_attention(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx
     const uint64_t mn = a.mask ? bh * a.seq_q * a.seq_k : 0;
     const float scale =
         a.scale > 0.0f ? a.scale : 1.0f / std::sqrt(static_cast<float>(a.head_dim));
-    Staging st(s->cs, s->device->ordinal, s->capturing);
+    Staging st(s);
     float *O = st.out(a.O, qn * sizeof(float), false);
     const float *Q = st.in(a.Q, qn * sizeof(float));
     const float *K = st.in(a.K, kn * sizeof(float));
@@ -402,7 +467,10 @@ void exec_copy(vnpu_stream_t *s, const vnpu_command_t &cmd, Accounting &acc) {
     const auto &a = cmd.args.copy;
     if (!a.dst || !a.src || !a.bytes) throw CommandError("invalid copy arguments");
     // Unified addressing tells the two sides apart; `direction` is advisory.
+    // Host bytes a pending download writes are read or overwritten in order.
+    join_downloads(s);
     cuda_check(cudaMemcpyAsync(a.dst, a.src, a.bytes, cudaMemcpyDefault, s->cs), "copy");
+    if (classify(a.dst, s->device->ordinal) == Mem::kHost) s->cs_wrote_host = true;
     acc.bytes_read = a.bytes;
     acc.bytes_written = a.bytes;
     acc.dma = a.bytes;
@@ -418,6 +486,7 @@ void exec_memset(vnpu_stream_t *s, const vnpu_command_t &cmd, Accounting &acc) {
                    "memset");
     } else {
         // Host destination: keep stream order, then fill on the host.
+        join_downloads(s);
         cuda_check(cudaStreamSynchronize(s->cs), "memset order");
         std::memset(a.dst, static_cast<int>(a.value & 0xffu), a.bytes);
     }
@@ -431,6 +500,7 @@ void exec_pack(vnpu_stream_t *s, const vnpu_command_t &cmd, Accounting &acc) {
     if (s->capturing)
         throw CommandError("PACK_WEIGHTS_I8 inside a graph capture", VNPU_ERR_INVALID_ARGUMENT);
     // Stream order: everything before this command must have produced B.
+    join_downloads(s);
     cuda_check(cudaStreamSynchronize(s->cs), "pack order");
     vnpu_packed_weights_t *w = nullptr;
     const vnpu_status_t rc =
@@ -560,7 +630,11 @@ void record_stream_error(vnpu_stream_t *s, vnpu_status_t rc) {
 vnpu_status_t stream_sync_impl(vnpu_stream_t *s) {
     const uint64_t t0 = now_ns();
     cudaSetDevice(s->device->ordinal);
-    const cudaError_t e = cudaStreamSynchronize(s->cs);
+    cudaError_t e = cudaStreamSynchronize(s->cs);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->down);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->up);
+    s->pending_down.clear();
+    s->cs_wrote_host = false;
     if (e != cudaSuccess) {
         debug_log("stream sync: %s", cudaGetErrorString(e));
         record_stream_error(s, VNPU_ERR_DEVICE_ERROR);
@@ -834,6 +908,8 @@ VNPU_API void VNPU_CALL vnpu_device_destroy(vnpu_device_t *device) {
     for (auto *s : streams) {
         stream_sync_impl(s);
         cudaStreamDestroy(s->cs);
+        cudaStreamDestroy(s->up);
+        cudaStreamDestroy(s->down);
         cudaFree(s->d_err);
         delete s;
     }
@@ -963,10 +1039,14 @@ VNPU_API vnpu_status_t VNPU_CALL vnpu_stream_create(vnpu_device_t *device, int p
         // vnpu: larger priority = more urgent; CUDA: numerically lower.
         const int cuda_prio = priority > 0 ? hi : lo;
         if (cudaStreamCreateWithPriority(&s->cs, cudaStreamNonBlocking, cuda_prio) != cudaSuccess ||
+            cudaStreamCreateWithFlags(&s->up, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaStreamCreateWithFlags(&s->down, cudaStreamNonBlocking) != cudaSuccess ||
             cudaMalloc(&s->d_err, 3 * sizeof(uint32_t)) != cudaSuccess ||
             cudaMemset(s->d_err, 0, 3 * sizeof(uint32_t)) != cudaSuccess) {
             cudaGetLastError();
             if (s->cs) cudaStreamDestroy(s->cs);
+            if (s->up) cudaStreamDestroy(s->up);
+            if (s->down) cudaStreamDestroy(s->down);
             delete s;
             return VNPU_ERR_DEVICE_ERROR;
         }
@@ -989,6 +1069,8 @@ VNPU_API void VNPU_CALL vnpu_stream_destroy(vnpu_stream_t *stream) {
     }
     stream_sync_impl(stream);
     cudaStreamDestroy(stream->cs);
+    cudaStreamDestroy(stream->up);
+    cudaStreamDestroy(stream->down);
     cudaFree(stream->d_err);
     delete stream;
 }
@@ -1044,7 +1126,13 @@ VNPU_API vnpu_status_t VNPU_CALL vnpu_stream_submit(vnpu_stream_t *stream,
                     return VNPU_ERR_DEVICE_ERROR;
                 event->ev_device = d->ordinal;
             }
-            cudaEventRecord(event->ev, stream->cs);
+            // The batch is done when its kernels and its downloads are.
+            if (!stream->pending_down.empty()) {
+                stream_after(stream->down, stream->cs);
+                cudaEventRecord(event->ev, stream->down);
+            } else {
+                cudaEventRecord(event->ev, stream->cs);
+            }
             event->recorded = true;
             event->host_signaled = false;
             event->status = batch;

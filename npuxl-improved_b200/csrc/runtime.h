@@ -110,6 +110,14 @@ struct vnpu_stream {
     std::vector<vnpu_b200::PendingTrace> traces;
     bool capturing = false;          // inside vnpu_b200_capture_begin/end
     uint64_t captured_launches = 0;  // kernels recorded by the capture
+    // Copy engines for host operands: uploads run on `up`, downloads on
+    // `down`, each joined to `cs` by events, so a command's download
+    // overlaps the next command's upload and kernels.
+    cudaStream_t up = nullptr;
+    cudaStream_t down = nullptr;
+    // Host ranges that downloads not yet joined into `cs` and `up` write.
+    std::vector<std::pair<const char *, uint64_t>> pending_down;
+    bool cs_wrote_host = false;      // a COPY/MEMSET on `cs` wrote host memory since `up` last waited
 };
 
 struct vnpu_b200_graph {

@@ -325,4 +325,7 @@ class B200Block:
         return y
 
     def replay_decode(self):
-        self.graph.replay()
+        """One decode step: the graph replays on the library stream, ordered
+        with everything else this block submits there."""
+        with self.t.cuda.stream(self.stream):
+            self.graph.replay()

@@ -313,3 +313,127 @@ def test_graph_capture_replay(gpu, b200_lib, oracle):
         assert b200_lib.b200_capture_end(dev2.stream, C.byref(out)) == vnpu.ERR_DEVICE_ERROR
         assert not out.value
     gpu.unpack(w)
+
+
+# ----------------------------------------------------------------- host operands
+# Host inputs are uploaded and host outputs downloaded on two copy-engine
+# streams joined to the kernel stream by events.  These cases chain commands
+# through host memory inside one batch, so a missing join shows as a wrong
+# result.
+def _q_cmd(X, Y, s, rows, cols, axis=0):
+    c = vnpu.Command()
+    c.opcode = vnpu.OP_QUANTIZE_I8
+    c.args.quantize_i8 = vnpu.QuantizeI8Args(vnpu.ptr(X), vnpu.ptr(Y), vnpu.ptr(s), rows, cols,
+                                             axis, 0)
+    return c
+
+
+def _mm_cmd(A, w, sa, bias, Cout, M, K, N, epi=0):
+    c = vnpu.Command()
+    c.opcode = vnpu.OP_MATMUL_I8
+    c.args.matmul_i8 = vnpu.MatmulI8Args(vnpu.ptr(A), w, vnpu.ptr(sa), vnpu.ptr(bias),
+                                         vnpu.ptr(Cout), M, K, N, 0, 0, epi, vnpu.UNIT_GPU)
+    return c
+
+
+def _copy_cmd(dst, src, nbytes):
+    c = vnpu.Command()
+    c.opcode = vnpu.OP_COPY
+    c.args.copy = vnpu.CopyArgs(vnpu.ptr(dst), vnpu.ptr(src), nbytes, 0)
+    return c
+
+
+def test_host_output_feeds_next_command(gpu, oracle):
+    """QUANTIZE_I8 writes host A/sa (download), MATMUL_I8 of the same batch
+    reads them (upload): the upload waits for the download."""
+    rng = np.random.default_rng(21)
+    M, K, N = 300, 1024, 768
+    X = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
+    w = gpu.pack(B, sb, K, N)
+    try:
+        for rep in range(3):
+            A = np.zeros((M, K), np.int8)
+            sa = np.zeros(M, np.float32)
+            Cout = np.full((M, N), np.nan, np.float32)
+            X2 = X * (rep + 1)
+            assert gpu.submit([_q_cmd(X2, A, sa, M, K), _mm_cmd(A, w, sa, None, Cout, M, K, N)]) \
+                == vnpu.OK
+            assert gpu.sync() == vnpu.OK
+            Ao, sao = oracle.quantize(X2, 0)
+            assert bits_equal(A, Ao) and bits_equal(sa, sao)
+            assert bits_equal(Cout, oracle.matmul_i8(Ao, B, sao, sb, None, 0, 0))
+    finally:
+        gpu.unpack(w)
+
+
+def test_copy_reads_pending_download_and_upload_reads_copy(gpu, b200_lib, oracle):
+    """Download -> COPY host->device -> COPY device->host -> upload, one batch."""
+    rng = np.random.default_rng(22)
+    rows, cols = 256, 2048
+    X = rng.normal(0, 1, (rows, cols)).astype(np.float32)
+    Y = np.zeros((rows, cols), np.int8)          # host output of cmd 0
+    s = np.zeros(rows, np.float32)
+    dbuf = vnpu.vp()
+    assert b200_lib.buffer_alloc(gpu.dev, rows * cols, C.byref(dbuf)) == vnpu.OK
+    dev_ptr = b200_lib.buffer_host_ptr(dbuf)
+    Z = np.zeros((rows, cols), np.int8)          # host, written by a COPY on the kernel stream
+    X2 = np.zeros((rows, cols), np.float32)      # host input of the last command
+    Y2 = np.zeros((rows, cols), np.int8)
+    s2 = np.zeros(rows, np.float32)
+    try:
+        cmds = [_q_cmd(X, Y, s, rows, cols),
+                _copy_cmd(dev_ptr, Y, rows * cols),      # reads the pending download
+                _copy_cmd(Z, dev_ptr, rows * cols),      # writes host memory on the kernel stream
+                _copy_cmd(X2, X, X.nbytes),              # host -> host
+                _q_cmd(X2, Y2, s2, rows, cols)]          # uploads what the COPY wrote
+        assert gpu.submit(cmds) == vnpu.OK
+        assert gpu.sync() == vnpu.OK
+        Yo, so = oracle.quantize(X, 0)
+        assert bits_equal(Y, Yo) and np.array_equal(Z, Yo)
+        assert bits_equal(Y2, Yo) and bits_equal(s2, so)
+    finally:
+        b200_lib.buffer_free(dbuf)
+
+
+def test_event_covers_downloads(gpu, b200_lib, oracle):
+    rng = np.random.default_rng(23)
+    M, K, N = 512, 2048, 4096
+    A, sa = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
+    B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
+    w = gpu.pack(B, sb, K, N)
+    ev = vnpu.vp()
+    assert b200_lib.event_create(C.byref(ev)) == vnpu.OK
+    try:
+        Cout = np.full((M, N), np.nan, np.float32)
+        assert gpu.submit([_mm_cmd(A, w, sa, None, Cout, M, K, N)], ev) == vnpu.OK
+        assert b200_lib.event_wait(ev, 10000) == vnpu.OK
+        # no stream sync: the event alone guarantees the host copy
+        assert bits_equal(Cout, oracle.matmul_i8(A, B, sa, sb, None, 0, 0))
+    finally:
+        b200_lib.event_destroy(ev)
+        gpu.unpack(w)
+
+
+def test_pipelined_steps_with_host_buffers(gpu, oracle):
+    """Many QUANTIZE_I8 + MATMUL_I8 steps, each with its own host X and C,
+    submitted back to back and synchronised once (uploads of step i+1 overlap
+    the download of step i)."""
+    rng = np.random.default_rng(24)
+    M, K, N, steps = 256, 1024, 1024, 6
+    B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
+    w = gpu.pack(B, sb, K, N)
+    A8 = np.zeros((M, K), np.int8)   # host, reused by every step (WAR/RAW through host)
+    sa = np.zeros(M, np.float32)
+    Xs = [rng.uniform(-1, 1, (M, K)).astype(np.float32) * (i + 1) for i in range(steps)]
+    Cs = [np.full((M, N), np.nan, np.float32) for _ in range(steps)]
+    try:
+        for i in range(steps):
+            assert gpu.submit([_q_cmd(Xs[i], A8, sa, M, K),
+                               _mm_cmd(A8, w, sa, None, Cs[i], M, K, N)]) == vnpu.OK
+        assert gpu.sync() == vnpu.OK
+        for i in range(steps):
+            Ao, sao = oracle.quantize(Xs[i], 0)
+            assert bits_equal(Cs[i], oracle.matmul_i8(Ao, B, sao, sb, None, 0, 0)), i
+    finally:
+        gpu.unpack(w)
