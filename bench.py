@@ -338,7 +338,8 @@ def llm_block_secondary(lib, dev, torch, prefill=512, decode=128, with_reference
     g = torch.Generator(device="cuda").manual_seed(11)
     x = torch.empty((prefill, cfg.d), device="cuda").normal_(0, 1, generator=g)
     st = Stream(lib, dev)
-    blk.forward(x, 0)                         # warm-up (and fills the cache)
+    for _ in range(3):                        # warm-up: first passes pay one-off costs
+        blk.forward(x, 0)
     dev.sync()
     blk.kc.zero_()
     blk.vc.zero_()
@@ -462,14 +463,19 @@ def run_b200(args):
     hC = torch.empty((M, n), dtype=torch.float32).pin_memory()
     qe = cmd_quantize(hA.data_ptr(), A8.data_ptr(), sa.data_ptr(), M, K)
     me = cmd_matmul(A8.data_ptr(), w, sa.data_ptr(), None, hC.data_ptr(), M, K, n)
-    submit(lib, dev, [qe, me])
-    dev.sync()
-    barrier()
     e_steps = max(2, min(args.steps, 5))
+    arr = (vnpu.Command * 2)(qe, me)
+    # Warm-up: the same back-to-back loop as the timed one, so the staging
+    # allocations reach their steady-state pool size before the clock starts.
+    for _ in range(max(args.warmup, 1)):
+        for _ in range(e_steps):
+            if lib.stream_submit(dev.stream, arr, 2, None) != vnpu.OK:
+                raise RuntimeError("submit failed")
+        dev.sync()
+    barrier()
     # Host-perceived time of e_steps back-to-back steps, each uploading its X
     # and downloading its C (downloads run on the stream's copy-engine
     # stream, so the clock stops at vnpu_stream_sync).
-    arr = (vnpu.Command * 2)(qe, me)
     t0 = time.perf_counter()
     for _ in range(e_steps):
         if lib.stream_submit(dev.stream, arr, 2, None) != vnpu.OK:

@@ -10,6 +10,7 @@
 // the host with the same libm powf.
 #include <cmath>
 #include <cstdlib>
+#include <cstring>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -54,6 +55,65 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ 
     for (uint32_t j = lane; j < cols; j += 32) {
         const float w = W ? W[j] : 1.0f;
         y[j] = j < full ? __fmul_rn(__fmul_rn(x[j], w), inv) : __fmul_rn(__fmul_rn(x[j], inv), w);
+    }
+}
+
+// The same arithmetic with one CTA per row: the row is staged in shared
+// memory by coalesced loads, so the eight sequential chains (lanes 0..7 of
+// warp 0) read it at shared-memory latency instead of global.
+constexpr uint32_t kRmsRowThreads = 256;
+constexpr uint32_t kRmsRowMaxCols = 48 * 1024;   // 192 KiB staged row
+
+__global__ void __launch_bounds__(kRmsRowThreads) rmsnorm_row_kernel(
+    const float *__restrict__ X, const float *__restrict__ W, float *__restrict__ Y,
+    uint32_t cols, float eps, bool vec) {
+    extern __shared__ __align__(16) float xs[];
+    __shared__ float inv_sh;
+    const uint32_t tid = threadIdx.x;
+    const float *x = X + static_cast<uint64_t>(blockIdx.x) * cols;
+    float *y = Y + static_cast<uint64_t>(blockIdx.x) * cols;
+    if (vec) {
+        for (uint32_t i = tid; i < cols / 4; i += kRmsRowThreads)
+            reinterpret_cast<float4 *>(xs)[i] = __ldg(reinterpret_cast<const float4 *>(x) + i);
+    } else {
+        for (uint32_t i = tid; i < cols; i += kRmsRowThreads) xs[i] = __ldg(x + i);
+    }
+    __syncthreads();
+    const uint32_t full = cols & ~7u;
+    if (tid < 32) {
+        float part = 0.0f;
+        if (tid < 8) {
+            uint32_t j = tid;
+#pragma unroll 8
+            for (; j < full; j += 8) part = __fmaf_rn(xs[j], xs[j], part);
+        }
+        const float hi = __shfl_down_sync(0xffffffffu, part, 4);
+        const float s = __fadd_rn(part, hi);
+        const float s1 = __shfl_down_sync(0xffffffffu, s, 1);
+        const float s01 = __fadd_rn(s, s1);
+        const float s23 = __shfl_down_sync(0xffffffffu, s01, 2);
+        if (tid == 0) {
+            float sum = __fadd_rn(s01, s23);
+            for (uint32_t j = full; j < cols; ++j) sum = __fmaf_rn(xs[j], xs[j], sum);
+            inv_sh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(cols)), eps)));
+        }
+    }
+    __syncthreads();
+    const float inv = inv_sh;
+    if (vec && W && (reinterpret_cast<uintptr_t>(W) & 15u) == 0u) {
+        // cols % 8 == 0 here (vec requires it): every element is in the vector part
+        for (uint32_t i = tid; i < cols / 4; i += kRmsRowThreads) {
+            const float4 xv = reinterpret_cast<const float4 *>(xs)[i];
+            const float4 wv = __ldg(reinterpret_cast<const float4 *>(W) + i);
+            reinterpret_cast<float4 *>(y)[i] =
+                make_float4(__fmul_rn(__fmul_rn(xv.x, wv.x), inv), __fmul_rn(__fmul_rn(xv.y, wv.y), inv),
+                            __fmul_rn(__fmul_rn(xv.z, wv.z), inv), __fmul_rn(__fmul_rn(xv.w, wv.w), inv));
+        }
+    } else {
+        for (uint32_t j = tid; j < cols; j += kRmsRowThreads) {
+            const float w = W ? W[j] : 1.0f;
+            y[j] = j < full ? __fmul_rn(__fmul_rn(xs[j], w), inv) : __fmul_rn(__fmul_rn(xs[j], inv), w);
+        }
     }
 }
 
@@ -471,6 +531,222 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode_kernel(const Att
     }
 }
 
+// Decode attention on a cluster of kDcCluster CTAs per (batch, head), same
+// arithmetic again.  The row's keys are split across the cluster for the
+// scores and its dims for the values:
+//   0. every thread starts cp.async copies of this CTA's V slice (all keys,
+//      dims [d0, d0 + dslice)) into shared memory;
+//   A. thread = key of this CTA's key range: the eight chains of the dot
+//      product (K row streamed with 16-byte loads), hsum256 order, *scale
+//      (+mask); each CTA then gathers the other ranges through distributed
+//      shared memory;
+//   B. warp 0 replays the online softmax over the 64-key blocks in order
+//      (every CTA of the cluster does, identically);
+//   C. thread = dim of the slice: acc = acc*alpha_b, fma(V[j][d], p_j, acc)
+//      over the keys in order, from shared memory.
+// Requires D % 16 == 0 and 16-byte aligned V (the caller checks).
+// a = fma(v, p, a) when p != 0, else a unchanged (the reference skips zero
+// probabilities); a predicated FMA keeps the test off the dependency chain.
+__device__ __forceinline__ float fma_if_nonzero(float v, float p, float a) {
+    asm("{\n\t.reg .pred q;\n\tsetp.ne.f32 q, %2, 0f00000000;\n\t@q fma.rn.f32 %0, %1, %2, %0;\n\t}"
+        : "+f"(a)
+        : "f"(v), "f"(p));
+    return a;
+}
+
+constexpr uint32_t kDcCluster = 4;
+constexpr uint32_t kDcThreads = 256;
+constexpr size_t kDcMaxSmem = 200 * 1024;
+
+// The dot product of one query and one key in the reference's AVX2 order:
+// chain c (c = 0..7) accumulates elements 8t + c in t order, then
+// ((c0+c4) + (c1+c5)) + ((c2+c6) + (c3+c7)).  kT > 0: D = 8 kT, every K load
+// issued before the first FMA.
+template <uint32_t kT>
+__device__ __forceinline__ float dot_hsum256(const float *qs, const float *krow, uint32_t D) {
+    float c[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const float4 *k4 = reinterpret_cast<const float4 *>(krow);
+    const float4 *q4 = reinterpret_cast<const float4 *>(qs);
+    if constexpr (kT > 0) {
+        float4 kr[2 * kT];
+#pragma unroll
+        for (uint32_t i = 0; i < 2 * kT; ++i) kr[i] = __ldg(k4 + i);
+#pragma unroll
+        for (uint32_t t = 0; t < kT; ++t) {
+            const float4 ka = kr[2 * t], kb = kr[2 * t + 1];
+            const float4 qa = q4[2 * t], qb = q4[2 * t + 1];
+            c[0] = __fmaf_rn(qa.x, ka.x, c[0]);
+            c[1] = __fmaf_rn(qa.y, ka.y, c[1]);
+            c[2] = __fmaf_rn(qa.z, ka.z, c[2]);
+            c[3] = __fmaf_rn(qa.w, ka.w, c[3]);
+            c[4] = __fmaf_rn(qb.x, kb.x, c[4]);
+            c[5] = __fmaf_rn(qb.y, kb.y, c[5]);
+            c[6] = __fmaf_rn(qb.z, kb.z, c[6]);
+            c[7] = __fmaf_rn(qb.w, kb.w, c[7]);
+        }
+        return __fadd_rn(__fadd_rn(__fadd_rn(c[0], c[4]), __fadd_rn(c[1], c[5])),
+                         __fadd_rn(__fadd_rn(c[2], c[6]), __fadd_rn(c[3], c[7])));
+    }
+#pragma unroll 4
+    for (uint32_t t = 0; t < D / 8; ++t) {
+        const float4 ka = __ldg(k4 + 2 * t), kb = __ldg(k4 + 2 * t + 1);
+        const float4 qa = q4[2 * t], qb = q4[2 * t + 1];
+        c[0] = __fmaf_rn(qa.x, ka.x, c[0]);
+        c[1] = __fmaf_rn(qa.y, ka.y, c[1]);
+        c[2] = __fmaf_rn(qa.z, ka.z, c[2]);
+        c[3] = __fmaf_rn(qa.w, ka.w, c[3]);
+        c[4] = __fmaf_rn(qb.x, kb.x, c[4]);
+        c[5] = __fmaf_rn(qb.y, kb.y, c[5]);
+        c[6] = __fmaf_rn(qb.z, kb.z, c[6]);
+        c[7] = __fmaf_rn(qb.w, kb.w, c[7]);
+    }
+    return __fadd_rn(__fadd_rn(__fadd_rn(c[0], c[4]), __fadd_rn(c[1], c[5])),
+                     __fadd_rn(__fadd_rn(c[2], c[6]), __fadd_rn(c[3], c[7])));
+}
+
+__global__ void __cluster_dims__(kDcCluster, 1, 1) __launch_bounds__(kDcThreads)
+    attention_decode_cluster_kernel(const AttParams p) {
+    extern __shared__ __align__(16) float dc_smem[];
+    const uint32_t D = p.D, L = p.seq_k;
+    const uint32_t nblk = (L + kAttBK - 1) / kAttBK;
+    const uint32_t dslice = D / kDcCluster;
+    float *Vs = dc_smem;                                   // [L][dslice]
+    float *qs = Vs + static_cast<size_t>(L) * dslice;     // [D]
+    float *S = qs + D;                                     // [L]
+    float *alpha_b = S + L;                                // [nblk]
+    int *active_b = reinterpret_cast<int *>(alpha_b + nblk);
+    float *l_sh = reinterpret_cast<float *>(active_b + nblk);
+
+    const uint32_t tid = threadIdx.x, lane = tid & 31;
+    const uint32_t rank = cluster_ctarank();
+    const uint32_t bh = blockIdx.x / kDcCluster;
+    const float *Qh = p.Q + static_cast<uint64_t>(bh) * D;
+    const float *Kh = p.K + static_cast<uint64_t>(bh) * L * D;
+    const float *Vh = p.V + static_cast<uint64_t>(bh) * L * D;
+    const float *Mh = p.mask ? p.mask + static_cast<uint64_t>(bh) * L : nullptr;
+    const uint32_t d0 = rank * dslice;
+
+    // 0. V slice -> shared memory, asynchronously.
+    const uint32_t per_key = dslice / 4;   // 16-byte pieces per key
+    for (uint32_t i = tid; i < L * per_key; i += kDcThreads) {
+        const uint32_t j = i / per_key, c = i % per_key;
+        cp_async_16(Vs + static_cast<size_t>(j) * dslice + 4 * c,
+                    Vh + static_cast<uint64_t>(j) * D + d0 + 4 * c);
+    }
+    for (uint32_t i = tid; i < D; i += kDcThreads) qs[i] = Qh[i];
+    __syncthreads();
+
+    // A. scores of keys [k_lo, k_hi)
+    const uint32_t span = (L + kDcCluster - 1) / kDcCluster;
+    const uint32_t k_lo = min(L, rank * span), k_hi = min(L, k_lo + span);
+    for (uint32_t ki = k_lo + tid; ki < k_hi; ki += kDcThreads) {
+        const float *krow = Kh + static_cast<uint64_t>(ki) * D;
+        const float dot = D == 128 ? dot_hsum256<16>(qs, krow, D) : dot_hsum256<0>(qs, krow, D);
+        float sc = __fmul_rn(dot, p.scale);
+        if (Mh) sc = __fadd_rn(sc, Mh[ki]);
+        S[ki] = sc;   // decode: the causal limit seq_k - 1 masks no key
+    }
+    cluster_sync_all();   // every range written
+    for (uint32_t ki = tid; ki < L; ki += kDcThreads) {
+        const uint32_t owner = ki / span;
+        if (owner != rank) S[ki] = ld_shared_cluster_f32(mapa_shared(smem_addr(S + ki), owner));
+    }
+    cluster_sync_all();   // every gather done before S is overwritten below
+
+    // B. online softmax.  The running max before block b is the max of the
+    // finite block maxima up to b, so: (1) warps find every block's max;
+    // (2) thread 0 walks the blocks for the running max and alpha;
+    // (3) warps exponentiate and sum their blocks (each sum in key order);
+    // (4) thread 0 folds l = l*alpha + sum over the blocks in order.
+    const uint32_t warp = tid >> 5;
+    const float ninf = -__int_as_float(0x7f800000);
+    float *nm_b = l_sh + 1;            // [nblk] running max of each active block
+    float *sum_b = nm_b + nblk;        // [nblk]
+    for (uint32_t b = warp; b < nblk; b += kDcThreads / 32) {
+        const uint32_t k0 = b * kAttBK, kc = min(kAttBK, L - k0);
+        const float s_lo = lane < kc ? S[k0 + lane] : ninf;
+        const float s_hi = lane + 32 < kc ? S[k0 + lane + 32] : ninf;
+        float bmax = fmaxf(s_lo, s_hi);
+        for (int o = 16; o > 0; o >>= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
+        if (lane == 0) nm_b[b] = bmax;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float m_run = ninf;
+        for (uint32_t b = 0; b < nblk; ++b) {
+            const float bmax = nm_b[b];
+            if (!isfinite(bmax)) {
+                active_b[b] = 0;
+                continue;
+            }
+            const float nm = fmaxf(m_run, bmax);
+            alpha_b[b] = ref_fast_expf(__fsub_rn(m_run, nm), false);
+            active_b[b] = 1;
+            nm_b[b] = nm;
+            m_run = nm;
+        }
+    }
+    __syncthreads();
+    for (uint32_t b = warp; b < nblk; b += kDcThreads / 32) {
+        if (!active_b[b]) continue;
+        const uint32_t k0 = b * kAttBK, kc = min(kAttBK, L - k0);
+        const float nm = nm_b[b];
+        const float p_lo = lane < kc ? ref_fast_expf(__fsub_rn(S[k0 + lane], nm), false) : 0.0f;
+        const float p_hi =
+            lane + 32 < kc ? ref_fast_expf(__fsub_rn(S[k0 + lane + 32], nm), false) : 0.0f;
+        if (lane < kc) S[k0 + lane] = p_lo;
+        if (lane + 32 < kc) S[k0 + lane + 32] = p_hi;
+        float sum_p = 0.0f;
+#pragma unroll
+        for (uint32_t j = 0; j < 32; ++j) {
+            const float v = __shfl_sync(0xffffffffu, p_lo, j);
+            if (j < kc) sum_p = __fadd_rn(sum_p, v);
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < 32; ++j) {
+            const float v = __shfl_sync(0xffffffffu, p_hi, j);
+            if (j + 32 < kc) sum_p = __fadd_rn(sum_p, v);
+        }
+        if (lane == 0) sum_b[b] = sum_p;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float l_run = 0.0f;
+        for (uint32_t b = 0; b < nblk; ++b)
+            if (active_b[b]) l_run = __fadd_rn(__fmul_rn(l_run, alpha_b[b]), sum_b[b]);
+        *l_sh = l_run;
+    }
+    cp_async_wait_all();
+    __syncthreads();
+
+    // C. values of dims [d0, d0 + dslice), keys in order
+    if (tid < dslice) {
+        const float l = *l_sh;
+        const float inv = l > 0.0f ? __fdiv_rn(1.0f, l) : 0.0f;
+        float a = 0.0f;
+        for (uint32_t b = 0; b < nblk; ++b) {
+            if (!active_b[b]) continue;
+            a = __fmul_rn(a, alpha_b[b]);
+            const uint32_t k0 = b * kAttBK, kc = min(kAttBK, L - k0);
+            const float *vcol = Vs + static_cast<size_t>(k0) * dslice + tid;
+            const float *prow = S + k0;
+            uint32_t j = 0;
+            for (; j + 8 <= kc; j += 8) {
+                float pv[8], vv[8];
+#pragma unroll
+                for (uint32_t u = 0; u < 8; ++u) {
+                    pv[u] = prow[j + u];
+                    vv[u] = vcol[(j + u) * dslice];
+                }
+#pragma unroll
+                for (uint32_t u = 0; u < 8; ++u) a = fma_if_nonzero(vv[u], pv[u], a);
+            }
+            for (; j < kc; ++j) a = fma_if_nonzero(vcol[j * dslice], prow[j], a);
+        }
+        p.O[static_cast<uint64_t>(bh) * D + d0 + tid] = __fmul_rn(a, inv);
+    }
+}
+
 // Spins on a flag nothing sets, bounded by limit_ns: the device-side wait
 // pattern of the GEMM pipeline, exercised on its own.
 __global__ void wait_probe_kernel(const uint32_t *flag, uint64_t limit_ns, uint32_t *err) {
@@ -495,8 +771,27 @@ unsigned grid_for(uint64_t n, int num_sms, unsigned threads) {
 
 cudaError_t rmsnorm(const LaunchCtx &ctx, const float *X, const float *W, float *Y,
                     uint32_t rows, uint32_t cols, float eps) {
-    const unsigned blocks = (rows + 7) / 8;
-    rmsnorm_kernel<<<blocks, 256, 0, ctx.stream>>>(X, W, Y, rows, cols, eps);
+    if (cols <= kRmsRowMaxCols && std::getenv("VNPU_B200_RMSNORM_WARP") == nullptr) {
+        const size_t smem = sizeof(float) * cols;
+        if (smem > 48 * 1024) {
+            static bool configured[64] = {};
+            int dev = 0;
+            cudaGetDevice(&dev);
+            if (dev >= 0 && dev < 64 && !configured[dev]) {
+                const cudaError_t e = cudaFuncSetAttribute(
+                    rmsnorm_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                    static_cast<int>(sizeof(float) * kRmsRowMaxCols));
+                if (e != cudaSuccess) return e;
+                configured[dev] = true;
+            }
+        }
+        const bool vec = cols % 8 == 0 && (reinterpret_cast<uintptr_t>(X) & 15u) == 0 &&
+                         (reinterpret_cast<uintptr_t>(Y) & 15u) == 0;
+        rmsnorm_row_kernel<<<rows, kRmsRowThreads, smem, ctx.stream>>>(X, W, Y, cols, eps, vec);
+    } else {
+        const unsigned blocks = (rows + 7) / 8;
+        rmsnorm_kernel<<<blocks, 256, 0, ctx.stream>>>(X, W, Y, rows, cols, eps);
+    }
     count_launch(ctx);
     return cudaGetLastError();
 }
@@ -583,7 +878,28 @@ cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, cons
     ap.D = head_dim;
     ap.causal = causal;
     ap.scale = scale;
-    if (seq_q == 1 && seq_k <= kDecMaxKeys && std::getenv("VNPU_B200_ATTN_GENERAL") == nullptr) {
+    const char *attn_env = std::getenv("VNPU_B200_ATTN");   // general | decode | cluster
+    const bool force_general = attn_env && !std::strcmp(attn_env, "general");
+    const bool allow_cluster = !(attn_env && !std::strcmp(attn_env, "decode"));
+    const size_t dc_smem = sizeof(float) * (static_cast<size_t>(seq_k) * (head_dim / kDcCluster) +
+                                            head_dim + seq_k + 4 * ((seq_k + kAttBK - 1) / kAttBK) + 1);
+    if (seq_q == 1 && !force_general && allow_cluster && head_dim % 16 == 0 &&
+        (reinterpret_cast<uintptr_t>(V) & 15) == 0 && (reinterpret_cast<uintptr_t>(K) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(Q) & 15) == 0 && dc_smem <= kDcMaxSmem) {
+        static bool dc_configured[64] = {};
+        if (dev >= 0 && dev < 64 && !dc_configured[dev]) {
+            const cudaError_t e = cudaFuncSetAttribute(attention_decode_cluster_kernel,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       static_cast<int>(kDcMaxSmem));
+            if (e != cudaSuccess) return e;
+            dc_configured[dev] = true;
+        }
+        attention_decode_cluster_kernel<<<batch * heads * kDcCluster, kDcThreads, dc_smem,
+                                          ctx.stream>>>(ap);
+        count_launch(ctx);
+        return cudaGetLastError();
+    }
+    if (seq_q == 1 && seq_k <= kDecMaxKeys && !force_general) {
         const uint32_t nblk = (seq_k + kAttBK - 1) / kAttBK;
         const size_t dsmem = sizeof(float) * (seq_k + nblk + nblk + 1 + head_dim);
         static bool dec_configured[64] = {};

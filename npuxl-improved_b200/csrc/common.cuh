@@ -409,6 +409,23 @@ __device__ __forceinline__ uint32_t cluster_nctarank() {
 }
 
 // 32-bit load from another CTA's shared memory (distributed shared memory).
+// 16-byte global -> shared copy that does not block the issuing thread
+// (completion by cp_async_wait_all).
+__device__ __forceinline__ void cp_async_16(void *smem_dst, const void *gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem_dst)),
+                 "l"(gmem_src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t cluster_addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ int32_t ld_shared_cluster_s32(uint32_t cluster_addr) {
     int32_t v;
     asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(cluster_addr) : "memory");

@@ -258,14 +258,22 @@ def test_rmsnorm_golden(gpu, golden):
     assert bits_equal(Y2, golden["rms2_Y"])
 
 
-def test_rmsnorm_block_sizes(gpu, oracle):
+@pytest.mark.parametrize("kernel", ["row", "warp"])
+def test_rmsnorm_block_sizes(gpu, oracle, monkeypatch, kernel):
+    """The row-staged kernel (default up to 48K columns) and the warp-per-row
+    kernel both equal the oracle: vector/tail splits, no weights, wide rows."""
+    if kernel == "warp":
+        monkeypatch.setenv("VNPU_B200_RMSNORM_WARP", "1")
     rng = np.random.default_rng(3)
-    for rows, cols in ((512, 4096), (1, 4096), (7, 11008), (3, 13)):
+    for rows, cols, weighted in ((512, 4096, True), (1, 4096, True), (7, 11008, True),
+                                 (3, 13, True), (2, 4100, False), (1, 20000, True),
+                                 (2, 49153, True), (5, 7, False)):
         X = rng.normal(0, 1, (rows, cols)).astype(np.float32)
-        W = rng.normal(1, 0.1, cols).astype(np.float32)
+        W = rng.normal(1, 0.1, cols).astype(np.float32) if weighted else None
         Y = np.empty_like(X)
         gpu.rmsnorm(X, W, Y, rows, cols, 1e-6)
-        assert bits_equal(Y, oracle.rmsnorm(X, W, 1e-6, 0))
+        assert bits_equal(Y, oracle.rmsnorm(X, W, 1e-6, 0)), (rows, cols)
+    monkeypatch.delenv("VNPU_B200_RMSNORM_WARP", raising=False)
 
 
 def test_rope_golden(gpu, golden):
@@ -406,14 +414,16 @@ def test_decode_tensor_core_vs_simt(gpu, oracle, monkeypatch, M, K, N):
     assert bits_equal(outs[0], oracle.matmul_i8(A, B, sa, sb, bias, 0, 2))
 
 
-@pytest.mark.parametrize("sk,causal,masked,D", [(1, 1, False, 128), (64, 1, False, 128),
-                                                (65, 0, True, 128), (513, 1, False, 128),
-                                                (640, 0, True, 128), (300, 1, False, 40),
-                                                (1000, 1, True, 256), (77, 0, False, 12)])
-def test_decode_attention_matches_oracle(gpu, oracle, monkeypatch, sk, causal, masked, D):
-    """One query per head (decode): the dedicated kernel equals the general
-    kernel and the reference restatement bit for bit, masks and tails included."""
-    H = 4
+@pytest.mark.parametrize("sk,causal,masked,D,H", [(1, 1, False, 128, 4), (3, 0, False, 16, 4),
+                                                  (64, 1, False, 128, 4), (65, 0, True, 128, 4),
+                                                  (513, 1, False, 128, 4), (640, 0, True, 128, 32),
+                                                  (300, 1, False, 40, 4), (1000, 1, True, 256, 4),
+                                                  (700, 0, True, 256, 2), (1400, 1, False, 128, 3),
+                                                  (77, 0, False, 12, 4)])
+def test_decode_attention_matches_oracle(gpu, oracle, monkeypatch, sk, causal, masked, D, H):
+    """One query per head (decode): the cluster kernel (D % 16 == 0 and the V
+    slices fit in shared memory), the single-CTA decode kernel and the general
+    kernel all equal the reference restatement bit for bit, masks included."""
     rng = np.random.default_rng(sk * 10 + D)
     Q = rng.normal(0, 1, (1, H, 1, D)).astype(np.float32)
     K = rng.normal(0, 1, (1, H, sk, D)).astype(np.float32)
@@ -423,14 +433,10 @@ def test_decode_attention_matches_oracle(gpu, oracle, monkeypatch, sk, causal, m
         M = np.zeros((1, H, 1, sk), np.float32)
         M[..., sk // 2:] = -np.inf          # e.g. KV-cache slots not yet filled
         M[..., :3] += rng.normal(0, 1, 3).astype(np.float32)
-    outs = []
-    for general in (False, True):
-        if general:
-            monkeypatch.setenv("VNPU_B200_ATTN_GENERAL", "1")
+    ref = oracle.attention(Q, K, V, M, 1, H, 1, sk, D, causal, 0.0)
+    for mode in ("cluster", "decode", "general"):
+        monkeypatch.setenv("VNPU_B200_ATTN", mode)
         O = np.empty((1, H, 1, D), np.float32)
         gpu.attention(Q, K, V, M, O, 1, H, 1, sk, D, causal, 0.0)
-        outs.append(O)
-    monkeypatch.delenv("VNPU_B200_ATTN_GENERAL", raising=False)
-    ref = oracle.attention(Q, K, V, M, 1, H, 1, sk, D, causal, 0.0)
-    assert bits_equal(outs[0], ref), f"max ulp {ulp_diff(outs[0], ref)}"
-    assert bits_equal(outs[1], ref)
+        assert bits_equal(O, ref), f"{mode}: max ulp {ulp_diff(O, ref)}"
+    monkeypatch.delenv("VNPU_B200_ATTN", raising=False)
