@@ -39,6 +39,44 @@ extern "C" {
 #define VNPU_CMD_FLAG_EPI_STREAM   (1u << 8)
 #define VNPU_CMD_FLAG_EPI_SCALAR   (1u << 9)
 
+/*
+ * Fused row prologues for MATMUL_I8 (no reference counterpart; the reference
+ * submits RMSNORM_F32 or SWIGLU_F32 and then QUANTIZE_I8 per row).  Opcodes
+ * outside the reference's range, as its ABI rules allow (reference
+ * include/vnpu.h:14); the arguments travel in vnpu_command_t.args.raw
+ * (memcpy the struct there).  Q (rows x cols int8) and scales (rows f32) are
+ * the bits QUANTIZE_I8 per row gives for the f32 result; Y, when not NULL,
+ * receives that f32 result (the bits RMSNORM_F32 / SWIGLU_F32 give).
+ * cols <= 49152.  eps <= 0 means 1e-5 and alpha == 0 means 1, as in the
+ * stand-alone commands.
+ */
+#define VNPU_B200_OP_RMSNORM_QUANTIZE_I8  0x100u
+#define VNPU_B200_OP_SWIGLU_QUANTIZE_I8   0x101u
+
+typedef struct vnpu_b200_rmsnorm_quantize_args_t {
+    const float *X;      /* rows x cols */
+    const float *W;      /* cols, or NULL (1.0) */
+    float *Y;            /* rows x cols f32 result, or NULL */
+    int8_t *Q;           /* rows x cols */
+    float *scales;       /* rows */
+    uint32_t rows;
+    uint32_t cols;
+    float eps;
+    uint32_t reserved0;
+} vnpu_b200_rmsnorm_quantize_args_t;
+
+typedef struct vnpu_b200_swiglu_quantize_args_t {
+    const float *gate;   /* rows x cols */
+    const float *up;     /* rows x cols */
+    float *Y;            /* rows x cols f32 result, or NULL */
+    int8_t *Q;           /* rows x cols */
+    float *scales;       /* rows */
+    uint32_t rows;
+    uint32_t cols;
+    float alpha;
+    uint32_t reserved0;
+} vnpu_b200_swiglu_quantize_args_t;
+
 /* The cudaStream_t behind a vnpu stream (as void*), so callers can order
  * their own CUDA work and timing events against its kernels.  Copies of host
  * operands run on two further streams of the vnpu stream (uploads, downloads)

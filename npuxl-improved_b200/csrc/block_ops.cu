@@ -14,6 +14,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "quant_common.cuh"
 
 namespace vnpu_b200 {
 namespace {
@@ -64,19 +65,17 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ 
 constexpr uint32_t kRmsRowThreads = 256;
 constexpr uint32_t kRmsRowMaxCols = 48 * 1024;   // 192 KiB staged row
 
-__global__ void __launch_bounds__(kRmsRowThreads) rmsnorm_row_kernel(
-    const float *__restrict__ X, const float *__restrict__ W, float *__restrict__ Y,
-    uint32_t cols, float eps, bool vec) {
-    extern __shared__ __align__(16) float xs[];
-    __shared__ float inv_sh;
+// Stage row x into xs (CTA-wide) and return 1/sqrt(ss/cols + eps) with ss in
+// the reference's AVX2 order, computed by lanes 0..7 of warp 0 from xs.
+__device__ __forceinline__ float stage_row_rms_inv(const float *__restrict__ x, float *xs,
+                                                   uint32_t cols, float eps, bool vec,
+                                                   float *inv_sh) {
     const uint32_t tid = threadIdx.x;
-    const float *x = X + static_cast<uint64_t>(blockIdx.x) * cols;
-    float *y = Y + static_cast<uint64_t>(blockIdx.x) * cols;
     if (vec) {
-        for (uint32_t i = tid; i < cols / 4; i += kRmsRowThreads)
+        for (uint32_t i = tid; i < cols / 4; i += blockDim.x)
             reinterpret_cast<float4 *>(xs)[i] = __ldg(reinterpret_cast<const float4 *>(x) + i);
     } else {
-        for (uint32_t i = tid; i < cols; i += kRmsRowThreads) xs[i] = __ldg(x + i);
+        for (uint32_t i = tid; i < cols; i += blockDim.x) xs[i] = __ldg(x + i);
     }
     __syncthreads();
     const uint32_t full = cols & ~7u;
@@ -95,11 +94,23 @@ __global__ void __launch_bounds__(kRmsRowThreads) rmsnorm_row_kernel(
         if (tid == 0) {
             float sum = __fadd_rn(s01, s23);
             for (uint32_t j = full; j < cols; ++j) sum = __fmaf_rn(xs[j], xs[j], sum);
-            inv_sh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(cols)), eps)));
+            *inv_sh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(cols)), eps)));
         }
     }
     __syncthreads();
-    const float inv = inv_sh;
+    return *inv_sh;
+}
+
+__global__ void __launch_bounds__(kRmsRowThreads) rmsnorm_row_kernel(
+    const float *__restrict__ X, const float *__restrict__ W, float *__restrict__ Y,
+    uint32_t cols, float eps, bool vec) {
+    extern __shared__ __align__(16) float xs[];
+    __shared__ float inv_sh;
+    const uint32_t tid = threadIdx.x;
+    const float *x = X + static_cast<uint64_t>(blockIdx.x) * cols;
+    float *y = Y + static_cast<uint64_t>(blockIdx.x) * cols;
+    const uint32_t full = cols & ~7u;
+    const float inv = stage_row_rms_inv(x, xs, cols, eps, vec, &inv_sh);
     if (vec && W && (reinterpret_cast<uintptr_t>(W) & 15u) == 0u) {
         // cols % 8 == 0 here (vec requires it): every element is in the vector part
         for (uint32_t i = tid; i < cols / 4; i += kRmsRowThreads) {
@@ -115,6 +126,133 @@ __global__ void __launch_bounds__(kRmsRowThreads) rmsnorm_row_kernel(
             y[j] = j < full ? __fmul_rn(__fmul_rn(xs[j], w), inv) : __fmul_rn(__fmul_rn(xs[j], inv), w);
         }
     }
+}
+
+// ---------------------------------------------------------------------------
+// Fused row prologues for the next MATMUL_I8 (no reference counterpart: the
+// reference runs RMSNORM_F32 / SWIGLU_F32 and then QUANTIZE_I8 per row).  One
+// CTA per row: the f32 result is formed in shared memory exactly as the
+// stand-alone kernels form it (and optionally written out), then quantized per
+// row from those same values - the bits of the two-command sequence.
+// ---------------------------------------------------------------------------
+// A row is split over a cluster of C CTAs (C = 1 when there are rows enough to
+// fill the GPU): CTA `rank` forms and quantizes columns [c0, c1); the row's
+// absmax is the max of the CTAs' maxima, exchanged through distributed shared
+// memory (a max is order-free, so the scale is the stand-alone one).
+constexpr uint32_t kFqThreads = 256;
+constexpr uint32_t kFqMaxCluster = 8;
+constexpr uint32_t kFqPerThread = 8;    // elements in flight per thread and pass
+
+__device__ __forceinline__ void fq_slice(uint32_t cols, uint32_t &c0, uint32_t &c1) {
+    const uint32_t C = cluster_nctarank(), rank = cluster_ctarank();
+    const uint32_t per = ((cols + C - 1) / C + 15u) & ~15u;   // 16-aligned slices
+    c0 = min(cols, rank * per);
+    c1 = min(cols, c0 + per);
+}
+
+// Finish a row: the CTA's slice of f32 values is in ys[0 .. c1-c0), its
+// largest |y| in `m`; exchange maxima, quantize the slice.
+__device__ __forceinline__ void fq_quantize_slice(const float *ys, uint32_t c0, uint32_t c1,
+                                                  float m, int8_t *__restrict__ q,
+                                                  float *__restrict__ scale_out, float *red,
+                                                  float *maxes) {
+    const uint32_t tid = threadIdx.x;
+    const uint32_t C = cluster_nctarank(), rank = cluster_ctarank();
+    m = block_max(m, red);
+    if (tid < C) st_shared_cluster_f32(mapa_shared(smem_addr(maxes + rank), tid), m);
+    cluster_sync_all();
+    float rowmax = 0.0f;
+    for (uint32_t r = 0; r < C; ++r) rowmax = fmaxf(rowmax, maxes[r]);
+    const float scale = scale_from_absmax(rowmax);
+    const float inv = __fdiv_rn(1.0f, scale);
+    if (tid == 0 && rank == 0) *scale_out = scale;
+    const uint32_t n = c1 - c0;
+    if ((reinterpret_cast<uintptr_t>(q + c0) & 3u) == 0u) {
+        for (uint32_t i = tid; i < n / 4; i += kFqThreads) {
+            const float4 v = reinterpret_cast<const float4 *>(ys)[i];
+            reinterpret_cast<uint32_t *>(q + c0)[i] = pack4(v.x, v.y, v.z, v.w, inv);
+        }
+        for (uint32_t j = (n & ~3u) + tid; j < n; j += kFqThreads) q[c0 + j] = quantize_value(ys[j], inv);
+    } else {
+        for (uint32_t j = tid; j < n; j += kFqThreads) q[c0 + j] = quantize_value(ys[j], inv);
+    }
+}
+
+__global__ void __launch_bounds__(kFqThreads) rmsnorm_quantize_kernel(
+    const float *__restrict__ X, const float *__restrict__ W, float *__restrict__ Y,
+    int8_t *__restrict__ Q, float *__restrict__ scales, uint32_t cols, float eps, bool vec) {
+    extern __shared__ __align__(16) float xs[];   // the whole row
+    __shared__ __align__(16) float maxes[kFqMaxCluster];
+    __shared__ float inv_sh;
+    __shared__ float red[32];
+    const uint32_t tid = threadIdx.x;
+    const uint64_t row = blockIdx.x / cluster_nctarank();
+    // Every CTA stages the row and runs the same in-order chains (no broadcast).
+    const float inv = stage_row_rms_inv(X + row * cols, xs, cols, eps, vec, &inv_sh);
+    uint32_t c0, c1;
+    fq_slice(cols, c0, c1);
+    const uint32_t full = cols & ~7u;
+    float *y = Y ? Y + row * cols : nullptr;
+    float m = 0.0f;
+    for (uint32_t base = c0 + tid; base < c1; base += kFqThreads * kFqPerThread) {
+        float wv[kFqPerThread];
+#pragma unroll
+        for (uint32_t e = 0; e < kFqPerThread; ++e) {
+            const uint32_t j = base + e * kFqThreads;
+            wv[e] = (W && j < c1) ? __ldg(W + j) : 1.0f;
+        }
+#pragma unroll
+        for (uint32_t e = 0; e < kFqPerThread; ++e) {
+            const uint32_t j = base + e * kFqThreads;
+            if (j < c1) {
+                const float v = j < full ? __fmul_rn(__fmul_rn(xs[j], wv[e]), inv)
+                                         : __fmul_rn(__fmul_rn(xs[j], inv), wv[e]);
+                xs[j] = v;   // in place: each element is read once, by its own thread
+                m = fmaxf(m, fabsf(v));
+                if (y) y[j] = v;
+            }
+        }
+    }
+    __syncthreads();
+    fq_quantize_slice(xs + c0, c0, c1, m, Q + row * cols, scales + row, red, maxes);
+}
+
+__global__ void __launch_bounds__(kFqThreads) swiglu_quantize_kernel(
+    const float *__restrict__ G, const float *__restrict__ U, float *__restrict__ Y,
+    int8_t *__restrict__ Q, float *__restrict__ scales, uint32_t cols, float alpha) {
+    extern __shared__ __align__(16) float ys[];   // this CTA's slice
+    __shared__ __align__(16) float maxes[kFqMaxCluster];
+    __shared__ float red[32];
+    const uint32_t tid = threadIdx.x;
+    const uint64_t row = blockIdx.x / cluster_nctarank();
+    uint32_t c0, c1;
+    fq_slice(cols, c0, c1);
+    const float *g = G + row * cols;
+    const float *u = U + row * cols;
+    float *y = Y ? Y + row * cols : nullptr;
+    float m = 0.0f;
+    for (uint32_t base = c0 + tid; base < c1; base += kFqThreads * kFqPerThread) {
+        float gv[kFqPerThread], uv[kFqPerThread];
+#pragma unroll
+        for (uint32_t e = 0; e < kFqPerThread; ++e) {
+            const uint32_t j = base + e * kFqThreads;
+            gv[e] = j < c1 ? __ldg(g + j) : 0.0f;
+            uv[e] = j < c1 ? __ldg(u + j) : 0.0f;
+        }
+#pragma unroll
+        for (uint32_t e = 0; e < kFqPerThread; ++e) {
+            const uint32_t j = base + e * kFqThreads;
+            if (j < c1) {
+                const float v = __fmul_rn(
+                    __fmul_rn(__fdiv_rn(gv[e], __fadd_rn(1.0f, ref_exp256_lane(-gv[e]))), uv[e]), alpha);
+                ys[j - c0] = v;
+                m = fmaxf(m, fabsf(v));
+                if (y) y[j] = v;
+            }
+        }
+    }
+    __syncthreads();
+    fq_quantize_slice(ys, c0, c1, m, Q + row * cols, scales + row, red, maxes);
 }
 
 // ---------------------------------------------------------------------------
@@ -794,6 +932,66 @@ cudaError_t rmsnorm(const LaunchCtx &ctx, const float *X, const float *W, float 
     }
     count_launch(ctx);
     return cudaGetLastError();
+}
+
+namespace {
+// Cluster size for a fused row prologue: split rows only while there are too
+// few of them to occupy the SMs.
+uint32_t fq_cluster(const LaunchCtx &ctx, uint32_t rows) {
+    if (const char *e = std::getenv("VNPU_B200_FUSED_CLUSTER")) {
+        const unsigned long c = std::strtoul(e, nullptr, 10);
+        if (c == 1 || c == 2 || c == 4 || c == 8) return static_cast<uint32_t>(c);
+    }
+    if (rows >= static_cast<uint32_t>(ctx.num_sms)) return 1;
+    if (rows * 2 >= static_cast<uint32_t>(ctx.num_sms)) return 2;
+    if (rows * 4 >= static_cast<uint32_t>(ctx.num_sms)) return 4;
+    return kFqMaxCluster;
+}
+
+template <typename Kernel, typename... Args>
+cudaError_t launch_fq(const LaunchCtx &ctx, Kernel kernel, uint32_t rows, uint32_t csize,
+                      size_t smem, Args... args) {
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(rows * csize, 1, 1);
+    cfg.blockDim = dim3(kFqThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = csize;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+}  // namespace
+
+cudaError_t rmsnorm_quantize(const LaunchCtx &ctx, const float *X, const float *W, float *Y,
+                             int8_t *Q, float *scales, uint32_t rows, uint32_t cols, float eps) {
+    if (cols > kRmsRowMaxCols || rows == 0 || rows > 0x0fffffffu) return cudaErrorInvalidValue;
+    const uint32_t csize = fq_cluster(ctx, rows);
+    const bool vec = cols % 8 == 0 && (reinterpret_cast<uintptr_t>(X) & 15u) == 0;
+    const cudaError_t e = launch_fq(ctx, rmsnorm_quantize_kernel, rows, csize, sizeof(float) * cols,
+                                    X, W, Y, Q, scales, cols, eps, vec);
+    count_launch(ctx);
+    return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+cudaError_t swiglu_quantize(const LaunchCtx &ctx, const float *gate, const float *up, float *Y,
+                            int8_t *Q, float *scales, uint32_t rows, uint32_t cols, float alpha) {
+    if (cols > kRmsRowMaxCols || rows == 0 || rows > 0x0fffffffu) return cudaErrorInvalidValue;
+    const uint32_t csize = fq_cluster(ctx, rows);
+    const size_t slice = ((cols + csize - 1) / csize + 15u) & ~15u;
+    const cudaError_t e = launch_fq(ctx, swiglu_quantize_kernel, rows, csize, sizeof(float) * slice,
+                                    gate, up, Y, Q, scales, cols, alpha);
+    count_launch(ctx);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t rope(const LaunchCtx &ctx, float *Q, float *K, const int32_t *positions,

@@ -92,6 +92,12 @@ bool encode_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *bas
 cudaError_t rmsnorm(const LaunchCtx &ctx, const float *X, const float *W, float *Y,
                     uint32_t rows, uint32_t cols, float eps);
 // inv_freq: host-computed 1/theta^(2j/dim) (or j/dim interleaved), head_dim/2 entries.
+// RMSNORM_F32 then QUANTIZE_I8 per row in one pass (Y may be NULL).
+cudaError_t rmsnorm_quantize(const LaunchCtx &ctx, const float *X, const float *W, float *Y,
+                             int8_t *Q, float *scales, uint32_t rows, uint32_t cols, float eps);
+// SWIGLU_F32 then QUANTIZE_I8 per row in one pass (Y may be NULL).
+cudaError_t swiglu_quantize(const LaunchCtx &ctx, const float *gate, const float *up, float *Y,
+                            int8_t *Q, float *scales, uint32_t rows, uint32_t cols, float alpha);
 cudaError_t rope(const LaunchCtx &ctx, float *Q, float *K, const int32_t *positions,
                  uint32_t batch, uint32_t heads, uint32_t q_seq, uint32_t k_seq,
                  uint32_t head_dim, uint32_t position_offset, uint32_t interleaved,

@@ -395,6 +395,50 @@ void exec_rope(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &ctx
 }
 
 // src/core/scheduler.cpp:537-549
+void exec_rmsnorm_quantize(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &ctx,
+                           Accounting &acc) {
+    vnpu_b200_rmsnorm_quantize_args_t a;
+    std::memcpy(&a, cmd.args.raw, sizeof(a));
+    if (!a.X || !a.Q || !a.scales || !a.rows || !a.cols)
+        throw CommandError("invalid rmsnorm_quantize arguments");
+    const uint64_t n = static_cast<uint64_t>(a.rows) * a.cols;
+    Staging st(s);
+    float *Y = a.Y ? st.out(a.Y, n * sizeof(float), a.Y == a.X) : nullptr;
+    const float *X = st.in(a.X, n * sizeof(float));
+    const float *W = st.in(a.W, sizeof(float) * a.cols);
+    int8_t *Q = st.out(a.Q, n, false);
+    float *sc = st.out(a.scales, sizeof(float) * a.rows, false);
+    const float eps = a.eps > 0.0f ? a.eps : 1e-5f;
+    cuda_check(rmsnorm_quantize(ctx, X, W, Y, Q, sc, a.rows, a.cols, eps), "rmsnorm_quantize launch");
+    st.finish();
+    acc.bytes_read = n * sizeof(float) + (a.W ? a.cols * sizeof(float) : 0);
+    acc.bytes_written = n + (a.Y ? n * sizeof(float) : 0) + a.rows * sizeof(float);
+    acc.flops = n * 8;
+    acc.dma = st.staged_bytes();
+}
+
+void exec_swiglu_quantize(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &ctx,
+                          Accounting &acc) {
+    vnpu_b200_swiglu_quantize_args_t a;
+    std::memcpy(&a, cmd.args.raw, sizeof(a));
+    if (!a.gate || !a.up || !a.Q || !a.scales || !a.rows || !a.cols)
+        throw CommandError("invalid swiglu_quantize arguments");
+    const uint64_t n = static_cast<uint64_t>(a.rows) * a.cols;
+    Staging st(s);
+    float *Y = a.Y ? st.out(a.Y, n * sizeof(float), a.Y == a.gate || a.Y == a.up) : nullptr;
+    const float *G = st.in(a.gate, n * sizeof(float));
+    const float *U = st.in(a.up, n * sizeof(float));
+    int8_t *Q = st.out(a.Q, n, false);
+    float *sc = st.out(a.scales, sizeof(float) * a.rows, false);
+    cuda_check(swiglu_quantize(ctx, G, U, Y, Q, sc, a.rows, a.cols, a.alpha == 0.0f ? 1.0f : a.alpha),
+               "swiglu_quantize launch");
+    st.finish();
+    acc.bytes_read = n * 2 * sizeof(float);
+    acc.bytes_written = n + (a.Y ? n * sizeof(float) : 0) + a.rows * sizeof(float);
+    acc.flops = n * 11;
+    acc.dma = st.staged_bytes();
+}
+
 void exec_swiglu(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &ctx,
                  Accounting &acc) {
     const auto &a = cmd.args.swiglu;
@@ -516,7 +560,9 @@ const char *opcode_name(uint32_t op);
 
 vnpu_status_t execute_command(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags) {
     vnpu_device_t *dev = s->device;
-    if (cmd.opcode >= VNPU_OP_COUNT) return VNPU_ERR_INVALID_COMMAND;
+    if (cmd.opcode >= VNPU_OP_COUNT && cmd.opcode != VNPU_B200_OP_RMSNORM_QUANTIZE_I8 &&
+        cmd.opcode != VNPU_B200_OP_SWIGLU_QUANTIZE_I8)
+        return VNPU_ERR_INVALID_COMMAND;
     dev->last_opcode.store(cmd.opcode);
     const bool tracing = dev->trace.enabled.load();
     PendingTrace pt;
@@ -552,6 +598,8 @@ vnpu_status_t execute_command(vnpu_stream_t *s, const vnpu_command_t &cmd, uint3
         case VNPU_OP_ADD_F32: exec_add(s, cmd, ctx, acc); break;
         case VNPU_OP_ATTENTION_F32: exec_attention(s, cmd, ctx, acc); break;
         case VNPU_OP_COPY: exec_copy(s, cmd, acc); break;
+        case VNPU_B200_OP_RMSNORM_QUANTIZE_I8: exec_rmsnorm_quantize(s, cmd, ctx, acc); break;
+        case VNPU_B200_OP_SWIGLU_QUANTIZE_I8: exec_swiglu_quantize(s, cmd, ctx, acc); break;
         case VNPU_OP_MEMSET: exec_memset(s, cmd, acc); break;
         case VNPU_OP_PACK_WEIGHTS_I8: exec_pack(s, cmd, acc); break;
         default:
@@ -657,6 +705,8 @@ const char *opcode_name(uint32_t op) {
                                   "MUL_F32",       "ATTENTION_F32", "QUANTIZE_I8",
                                   "PACK_WEIGHTS_I8", "MTP_HEAD_F32", "COPY",
                                   "MEMSET",        "BARRIER"};
+    if (op == VNPU_B200_OP_RMSNORM_QUANTIZE_I8) return "RMSNORM_QUANTIZE_I8";
+    if (op == VNPU_B200_OP_SWIGLU_QUANTIZE_I8) return "SWIGLU_QUANTIZE_I8";
     return op < sizeof(names) / sizeof(names[0]) ? names[op] : "UNKNOWN";
 }
 

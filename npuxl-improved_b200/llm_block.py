@@ -193,8 +193,9 @@ def _cmd(op, field, args):
 class B200Block:
     """The block with every tensor resident in HBM."""
 
-    def __init__(self, cfg: BlockConfig, lib, dev, torch):
+    def __init__(self, cfg: BlockConfig, lib, dev, torch, fused: bool = True):
         self.cfg, self.lib, self.dev, self.t = cfg, lib, dev, torch
+        self.fused = fused   # fused RMSNorm/SwiGLU -> QUANTIZE_I8 prologues (B200 opcodes)
         self.stream = torch.cuda.ExternalStream(lib.b200_stream_handle(dev.stream))
         w, (n1, n2) = make_weights(cfg)
         self.n1 = torch.from_numpy(n1).cuda()
@@ -235,18 +236,56 @@ class B200Block:
         if rc != vnpu.OK:
             raise RuntimeError(f"submit failed: {rc}")
 
-    def _gemm_cmds(self, x, name, out_name):
+    def _act_bufs(self, name, M):
+        K = self.w[name][1]
+        return (self._buf("a8_" + name, (M, K), self.t.int8), self._buf("sa_" + name, (M,)))
+
+    def _mm_cmd(self, name, M, out_name):
+        """MATMUL_I8 of the already quantized activations of GEMM `name`."""
         w, K, N = self.w[name]
-        M = x.shape[0]
-        a8 = self._buf("a8_" + name, (M, K), self.t.int8)
-        sa = self._buf("sa_" + name, (M,))
+        a8, sa = self._act_bufs(name, M)
         out = self._buf(out_name, (M, N))
+        return _cmd(vnpu.OP_MATMUL_I8, "matmul_i8",
+                    vnpu.MatmulI8Args(a8.data_ptr(), w, sa.data_ptr(), None, out.data_ptr(), M, K,
+                                      N, 0, 0, 0, vnpu.UNIT_GPU)), out
+
+    def _gemm_cmds(self, x, name, out_name):
+        M, K = x.shape[0], self.w[name][1]
+        a8, sa = self._act_bufs(name, M)
         q = _cmd(vnpu.OP_QUANTIZE_I8, "quantize_i8",
                  vnpu.QuantizeI8Args(x.data_ptr(), a8.data_ptr(), sa.data_ptr(), M, K, 0, 0))
-        mm = _cmd(vnpu.OP_MATMUL_I8, "matmul_i8",
-                  vnpu.MatmulI8Args(a8.data_ptr(), w, sa.data_ptr(), None, out.data_ptr(), M, K,
-                                    N, 0, 0, 0, vnpu.UNIT_GPU))
+        mm, out = self._mm_cmd(name, M, out_name)
         return [q, mm], out
+
+    def _norm_gemm_cmds(self, x, wn, name, out_name):
+        """RMSNorm -> QUANTIZE_I8 -> MATMUL_I8: one fused prologue command
+        (VNPU_B200_OP_RMSNORM_QUANTIZE_I8) when enabled, else the three ops."""
+        if not self.fused:
+            c, xn = self._rms_cmd(x, wn, out_name + "_n")
+            cmds, out = self._gemm_cmds(xn, name, out_name)
+            return [c] + cmds, out
+        M, K = x.shape
+        a8, sa = self._act_bufs(name, M)
+        pro = vnpu.b200_command(vnpu.OP_B200_RMSNORM_QUANTIZE_I8, vnpu.RmsnormQuantizeArgs(
+            x.data_ptr(), wn.data_ptr(), None, a8.data_ptr(), sa.data_ptr(), M, K, self.cfg.eps, 0))
+        mm, out = self._mm_cmd(name, M, out_name)
+        return [pro, mm], out
+
+    def _swiglu_gemm_cmds(self, g, u, name, out_name):
+        """SwiGLU -> QUANTIZE_I8 -> MATMUL_I8 (fused prologue when enabled)."""
+        T, inter = g.shape
+        if not self.fused:
+            ff = self._buf(f"ff{T}", (T, inter))
+            sw = _cmd(vnpu.OP_SWIGLU_F32, "swiglu",
+                      vnpu.SwigluArgs(g.data_ptr(), u.data_ptr(), ff.data_ptr(), T * inter,
+                                      1.0, 0, 0))
+            cmds, out = self._gemm_cmds(ff, name, out_name)
+            return [sw] + cmds, out
+        a8, sa = self._act_bufs(name, T)
+        pro = vnpu.b200_command(vnpu.OP_B200_SWIGLU_QUANTIZE_I8, vnpu.SwigluQuantizeArgs(
+            g.data_ptr(), u.data_ptr(), None, a8.data_ptr(), sa.data_ptr(), T, inter, 1.0, 0))
+        mm, out = self._mm_cmd(name, T, out_name)
+        return [pro, mm], out
 
     def _rms_cmd(self, x, wn, out_name):
         y = self._buf(out_name, tuple(x.shape))
@@ -266,9 +305,8 @@ class B200Block:
         t, cfg = self.t, self.cfg
         T, d, H, hd = x.shape[0], cfg.d, cfg.heads, cfg.head_dim
         with t.cuda.stream(self.stream):
-            c, xn = self._rms_cmd(x, self.n1, f"xn{T}")
-            cmds, qkv = self._gemm_cmds(xn, "qkv", f"qkv{T}")
-            self._submit([c] + cmds)
+            cmds, qkv = self._norm_gemm_cmds(x, self.n1, "qkv", f"qkv{T}")
+            self._submit(cmds)
             Q = qkv[:, :d].reshape(T, H, hd).transpose(0, 1).contiguous()[None]
             K = qkv[:, d:2 * d].reshape(T, H, hd).transpose(0, 1).contiguous()[None]
             V = qkv[:, 2 * d:].reshape(T, H, hd).transpose(0, 1).contiguous()[None]
@@ -295,18 +333,13 @@ class B200Block:
             attn = O[0].transpose(0, 1).reshape(T, d).contiguous()
             cmds, proj = self._gemm_cmds(attn, "o", f"proj{T}")
             a, x1 = self._add_cmd(x, proj, f"x1{T}")
-            c2, xn2 = self._rms_cmd(x1, self.n2, f"xn2{T}")
-            cmds2, gu = self._gemm_cmds(xn2, "gate_up", f"gu{T}")
-            self._submit(cmds + [a, c2] + cmds2)
+            cmds2, gu = self._norm_gemm_cmds(x1, self.n2, "gate_up", f"gu{T}")
+            self._submit(cmds + [a] + cmds2)
             g = gu[:, :cfg.inter].contiguous()
             u = gu[:, cfg.inter:].contiguous()
-            ff = self._buf(f"ff{T}", (T, cfg.inter))
-            sw = _cmd(vnpu.OP_SWIGLU_F32, "swiglu",
-                      vnpu.SwigluArgs(g.data_ptr(), u.data_ptr(), ff.data_ptr(), T * cfg.inter,
-                                      1.0, 0, 0))
-            cmds3, down = self._gemm_cmds(ff, "down", f"down{T}")
+            cmds3, down = self._swiglu_gemm_cmds(g, u, "down", f"down{T}")
             a2, y = self._add_cmd(x1, down, f"y{T}")
-            self._submit([sw] + cmds3 + [a2])
+            self._submit(cmds3 + [a2])
             # keep the temporaries alive until the stream has used them
             self._keep = (Q, K, V, attn, g, u)
         return y

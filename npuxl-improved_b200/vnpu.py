@@ -158,6 +158,29 @@ class MtpHeadArgs(C.Structure):
                 ("reserved0", u32)]
 
 
+# B200 extensions (include/vnpu_b200.h): fused row prologues, args in Command.args.raw
+OP_B200_RMSNORM_QUANTIZE_I8 = 0x100
+OP_B200_SWIGLU_QUANTIZE_I8 = 0x101
+
+
+class RmsnormQuantizeArgs(C.Structure):
+    _fields_ = [("X", vp), ("W", vp), ("Y", vp), ("Q", vp), ("scales", vp), ("rows", u32),
+                ("cols", u32), ("eps", C.c_float), ("reserved0", u32)]
+
+
+class SwigluQuantizeArgs(C.Structure):
+    _fields_ = [("gate", vp), ("up", vp), ("Y", vp), ("Q", vp), ("scales", vp), ("rows", u32),
+                ("cols", u32), ("alpha", C.c_float), ("reserved0", u32)]
+
+
+def b200_command(opcode: int, args: C.Structure) -> "Command":
+    """A command whose arguments are a B200 extension struct (copied into args.raw)."""
+    c = Command()
+    c.opcode = opcode
+    C.memmove(C.addressof(c.args), C.addressof(args), C.sizeof(args))
+    return c
+
+
 class CopyArgs(C.Structure):
     _fields_ = [("dst", vp), ("src", vp), ("bytes", u64), ("direction", u32), ("reserved0", u32)]
 
@@ -360,6 +383,16 @@ class Device:
         if check:
             self.lib.check(rc, "quantize_i8")
         return rc
+
+    def rmsnorm_quantize(self, X, W, Y, Q, scales, rows, cols, eps) -> None:
+        a = RmsnormQuantizeArgs(ptr(X), ptr(W), ptr(Y), ptr(Q), ptr(scales), rows, cols, eps, 0)
+        self.lib.check(self.submit([b200_command(OP_B200_RMSNORM_QUANTIZE_I8, a)]), "submit")
+        self.lib.check(self.sync(), "rmsnorm_quantize")
+
+    def swiglu_quantize(self, G, U, Y, Q, scales, rows, cols, alpha=0.0) -> None:
+        a = SwigluQuantizeArgs(ptr(G), ptr(U), ptr(Y), ptr(Q), ptr(scales), rows, cols, alpha, 0)
+        self.lib.check(self.submit([b200_command(OP_B200_SWIGLU_QUANTIZE_I8, a)]), "submit")
+        self.lib.check(self.sync(), "swiglu_quantize")
 
     def rmsnorm(self, X, W, Y, rows, cols, eps) -> None:
         a = RmsnormArgs(ptr(X), ptr(W), ptr(Y), rows, cols, eps, 0)

@@ -157,3 +157,35 @@ int main(int argc, char **argv) {
     name, abi, rc, _ = out.split(" ", 3)
     assert (name, abi) == ("vnpu-b200", "1")
     assert int(rc) in (vnpu.ERR_UNSUPPORTED, vnpu.OK)
+
+
+def test_b200_extension_structs(tmp_path):
+    """The fused-prologue argument structs (include/vnpu_b200.h) match the
+    ctypes mirror and fit in vnpu_command_t.args.raw."""
+    src = tmp_path / "ext.c"
+    src.write_text(r'''
+#include <stddef.h>
+#include <stdio.h>
+#include "vnpu_b200.h"
+#define F(T, f) printf(#T "." #f " %zu\n", offsetof(T, f))
+int main(void) {
+    printf("rq %zu\nsq %zu\nraw %zu\n", sizeof(vnpu_b200_rmsnorm_quantize_args_t),
+           sizeof(vnpu_b200_swiglu_quantize_args_t), sizeof(((vnpu_command_t *)0)->args.raw));
+    F(vnpu_b200_rmsnorm_quantize_args_t, Q); F(vnpu_b200_rmsnorm_quantize_args_t, eps);
+    F(vnpu_b200_swiglu_quantize_args_t, scales); F(vnpu_b200_swiglu_quantize_args_t, alpha);
+    printf("ops %u %u\n", VNPU_B200_OP_RMSNORM_QUANTIZE_I8, VNPU_B200_OP_SWIGLU_QUANTIZE_I8);
+    return 0;
+}''')
+    exe = tmp_path / "ext"
+    subprocess.run(["gcc", "-std=c11", "-I", INCLUDE, str(src), "-o", str(exe)], check=True)
+    out = dict(l.rsplit(" ", 1) if not l.startswith("ops") else ("ops", l[4:])
+               for l in subprocess.run([str(exe)], check=True, capture_output=True,
+                                       text=True).stdout.strip().splitlines())
+    assert int(out["rq"]) == C.sizeof(vnpu.RmsnormQuantizeArgs) <= int(out["raw"])
+    assert int(out["sq"]) == C.sizeof(vnpu.SwigluQuantizeArgs) <= int(out["raw"])
+    assert int(out["vnpu_b200_rmsnorm_quantize_args_t.Q"]) == vnpu.RmsnormQuantizeArgs.Q.offset
+    assert int(out["vnpu_b200_rmsnorm_quantize_args_t.eps"]) == vnpu.RmsnormQuantizeArgs.eps.offset
+    assert int(out["vnpu_b200_swiglu_quantize_args_t.scales"]) == vnpu.SwigluQuantizeArgs.scales.offset
+    assert int(out["vnpu_b200_swiglu_quantize_args_t.alpha"]) == vnpu.SwigluQuantizeArgs.alpha.offset
+    assert out["ops"].split() == [str(vnpu.OP_B200_RMSNORM_QUANTIZE_I8),
+                                  str(vnpu.OP_B200_SWIGLU_QUANTIZE_I8)]

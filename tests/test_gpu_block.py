@@ -1,8 +1,10 @@
 """The decoder block (configs[3] structure) on the B200, end to end.
 
-* Device-resident driver (torch buffers, CUDA-graph decode) vs the same
-  driver on host arrays through the B200 library: identical bits, which pins
-  the layout glue (QKV split, head-major transposes, KV-cache append, mask).
+* Device-resident driver (torch buffers, CUDA-graph decode; with and without
+  the fused RMSNorm/SwiGLU -> QUANTIZE_I8 prologues) vs the same driver on
+  host arrays through the B200 library with the reference's op sequence:
+  identical bits, which pins the layout glue (QKV split, head-major
+  transposes, KV-cache append, mask) and the fused opcodes.
 * vs the oracle restatement of the reference: within tolerance (RoPE uses the
   device sinf/cosf, a few ulp from glibc; everything else is bit-exact).
 """
@@ -22,10 +24,10 @@ def torch():
     return pytest.importorskip("torch")
 
 
-def _run_device(b200_lib, torch, cfg, x, toks, graph):
+def _run_device(b200_lib, torch, cfg, x, toks, graph, fused=True):
     from llm_block import B200Block
     dev = vnpu.Device(b200_lib)
-    blk = B200Block(cfg, b200_lib, dev, torch)
+    blk = B200Block(cfg, b200_lib, dev, torch, fused=fused)
     outs = [blk.forward(torch.from_numpy(x).cuda(), 0).cpu().numpy()]
     first = True
     for i, t in enumerate(toks):
@@ -50,14 +52,14 @@ def _run_device(b200_lib, torch, cfg, x, toks, graph):
     return outs
 
 
-@pytest.mark.parametrize("graph", [False, True])
-def test_block_device_equals_host_driver(b200_lib, torch, graph):
+@pytest.mark.parametrize("graph,fused", [(False, False), (False, True), (True, True)])
+def test_block_device_equals_host_driver(b200_lib, torch, graph, fused):
     from llm_block import BlockConfig, HostBlock
     cfg = BlockConfig(d=256, heads=4, inter=704, cap=48)
     rng = np.random.default_rng(5)
     x = rng.normal(0, 1, (20, cfg.d)).astype(np.float32)
     toks = [rng.normal(0, 1, (1, cfg.d)).astype(np.float32) for _ in range(5)]
-    dev_outs = _run_device(b200_lib, torch, cfg, x, toks, graph)
+    dev_outs = _run_device(b200_lib, torch, cfg, x, toks, graph, fused)
     host = HostBlock(cfg, lib=b200_lib)
     host_outs = [host.forward(x, 0)] + [host.forward(t, x.shape[0] + i) for i, t in enumerate(toks)]
     host.close()

@@ -276,6 +276,56 @@ def test_rmsnorm_block_sizes(gpu, oracle, monkeypatch, kernel):
     monkeypatch.delenv("VNPU_B200_RMSNORM_WARP", raising=False)
 
 
+@pytest.mark.parametrize("rows,cols,weighted,want_y", [
+    (1, 4096, True, False), (512, 4096, True, True), (7, 11008, False, True),
+    (3, 13, True, True), (2, 4100, True, False), (1, 30000, True, False)])
+def test_rmsnorm_quantize_fused_equals_two_commands(gpu, oracle, rows, cols, weighted, want_y):
+    """VNPU_B200_OP_RMSNORM_QUANTIZE_I8 gives the bits of RMSNORM_F32 then
+    QUANTIZE_I8 per row (both on the GPU and in the oracle)."""
+    rng = np.random.default_rng(rows * 7 + cols)
+    X = rng.normal(0, 1, (rows, cols)).astype(np.float32)
+    X[0, :2] = [0.0, 3.5]
+    W = rng.normal(1, 0.1, cols).astype(np.float32) if weighted else None
+    Y = np.full((rows, cols), np.nan, np.float32) if want_y else None
+    Q = np.zeros((rows, cols), np.int8)
+    s = np.zeros(rows, np.float32)
+    gpu.rmsnorm_quantize(X, W, Y, Q, s, rows, cols, 1e-6)
+    Y2 = np.empty((rows, cols), np.float32)
+    gpu.rmsnorm(X, W, Y2, rows, cols, 1e-6)
+    Q2 = np.empty_like(Q)
+    s2 = np.empty_like(s)
+    gpu.quantize_i8(Y2, Q2, s2, rows, cols, vnpu.QUANT_PER_ROW)
+    assert np.array_equal(Q, Q2) and bits_equal(s, s2)
+    if want_y:
+        assert bits_equal(Y, Y2)
+    Yo = oracle.rmsnorm(X, W, 1e-6, 0)
+    Qo, so = oracle.quantize(Yo, 0)
+    assert np.array_equal(Q, Qo) and bits_equal(s, so)
+
+
+@pytest.mark.parametrize("rows,cols,want_y,alpha", [
+    (1, 11008, False, 0.0), (512, 11008, True, 0.0), (3, 13, True, 1.7), (2, 4098, False, 0.0)])
+def test_swiglu_quantize_fused_equals_two_commands(gpu, oracle, rows, cols, want_y, alpha):
+    rng = np.random.default_rng(rows * 11 + cols)
+    G = rng.normal(0, 2, (rows, cols)).astype(np.float32)
+    U = rng.normal(0, 1, (rows, cols)).astype(np.float32)
+    Y = np.full((rows, cols), np.nan, np.float32) if want_y else None
+    Q = np.zeros((rows, cols), np.int8)
+    s = np.zeros(rows, np.float32)
+    gpu.swiglu_quantize(G, U, Y, Q, s, rows, cols, alpha)
+    Y2 = np.empty((rows, cols), np.float32)
+    gpu.swiglu(G, U, Y2, rows * cols, alpha)
+    Q2 = np.empty_like(Q)
+    s2 = np.empty_like(s)
+    gpu.quantize_i8(Y2, Q2, s2, rows, cols, vnpu.QUANT_PER_ROW)
+    assert np.array_equal(Q, Q2) and bits_equal(s, s2)
+    if want_y:
+        assert bits_equal(Y, Y2)
+    Yo = oracle.swiglu(G, U, alpha, 0)
+    Qo, so = oracle.quantize(Yo.reshape(rows, cols), 0)
+    assert np.array_equal(Q, Qo) and bits_equal(s, so)
+
+
 def test_rope_golden(gpu, golden):
     Q, K = golden["rope_Q"].copy(), golden["rope_K"].copy()
     _, H, T, D = Q.shape
@@ -440,3 +490,27 @@ def test_decode_attention_matches_oracle(gpu, oracle, monkeypatch, sk, causal, m
         gpu.attention(Q, K, V, M, O, 1, H, 1, sk, D, causal, 0.0)
         assert bits_equal(O, ref), f"{mode}: max ulp {ulp_diff(O, ref)}"
     monkeypatch.delenv("VNPU_B200_ATTN", raising=False)
+
+
+@pytest.mark.parametrize("csize", ["1", "2", "4", "8"])
+def test_fused_prologues_any_cluster_size(gpu, oracle, monkeypatch, csize):
+    """The fused prologues split a row over 1-8 CTAs; every split gives the
+    stand-alone bits (ragged slices, a row narrower than the split)."""
+    monkeypatch.setenv("VNPU_B200_FUSED_CLUSTER", csize)
+    rng = np.random.default_rng(int(csize))
+    for rows, cols in ((1, 4096), (3, 11008), (2, 100), (1, 7)):
+        X = rng.normal(0, 1, (rows, cols)).astype(np.float32)
+        W = rng.normal(1, 0.1, cols).astype(np.float32)
+        Q = np.zeros((rows, cols), np.int8)
+        s = np.zeros(rows, np.float32)
+        Y = np.full((rows, cols), np.nan, np.float32)
+        gpu.rmsnorm_quantize(X, W, Y, Q, s, rows, cols, 1e-6)
+        Yo = oracle.rmsnorm(X, W, 1e-6, 0)
+        Qo, so = oracle.quantize(Yo, 0)
+        assert bits_equal(Y, Yo) and np.array_equal(Q, Qo) and bits_equal(s, so), (rows, cols)
+        U = rng.normal(0, 1, (rows, cols)).astype(np.float32)
+        gpu.swiglu_quantize(X, U, Y, Q, s, rows, cols, 0.0)
+        Yo = oracle.swiglu(X, U, 0.0, 0).reshape(rows, cols)
+        Qo, so = oracle.quantize(Yo, 0)
+        assert bits_equal(Y, Yo) and np.array_equal(Q, Qo) and bits_equal(s, so), (rows, cols)
+    monkeypatch.delenv("VNPU_B200_FUSED_CLUSTER", raising=False)
