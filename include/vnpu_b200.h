@@ -77,6 +77,35 @@ typedef struct vnpu_b200_swiglu_quantize_args_t {
     uint32_t reserved0;
 } vnpu_b200_swiglu_quantize_args_t;
 
+/*
+ * KV-cache append for KV-cached decoding (no reference counterpart: the
+ * reference has no KV cache).  Copies head-major K and V ([heads][T][head_dim]
+ * f32, as ROPE_F32 leaves them) into slots pos .. pos+T-1 of the caches
+ * ([heads][capacity][head_dim]) and sets those slots of the additive mask
+ * ([heads][capacity], may be NULL) to 0, so ATTENTION_F32 over the whole
+ * capacity with that mask attends to the filled slots only.  pos is *position
+ * (a device int32, read when the command runs: a captured graph can advance
+ * it) or position_offset when position is NULL.  Slots at or past capacity are
+ * not written: VNPU_ERR_INVALID_ARGUMENT when pos is known on the host, the
+ * stream's device error otherwise.
+ */
+#define VNPU_B200_OP_KV_APPEND  0x102u
+
+typedef struct vnpu_b200_kv_append_args_t {
+    const float *K;
+    const float *V;
+    float *K_cache;
+    float *V_cache;
+    float *mask;
+    const int32_t *position;
+    uint32_t heads;
+    uint32_t T;
+    uint32_t head_dim;
+    uint32_t capacity;
+    uint32_t position_offset;
+    uint32_t reserved0;
+} vnpu_b200_kv_append_args_t;
+
 /* The cudaStream_t behind a vnpu stream (as void*), so callers can order
  * their own CUDA work and timing events against its kernels.  Copies of host
  * operands run on two further streams of the vnpu stream (uploads, downloads)

@@ -885,6 +885,37 @@ __global__ void __cluster_dims__(kDcCluster, 1, 1) __launch_bounds__(kDcThreads)
     }
 }
 
+// KV-cache append: element (h, t, d) of K/V goes to slot pos + t of head h.
+__global__ void kv_append_kernel(const float *__restrict__ K, const float *__restrict__ V,
+                                 float *__restrict__ Kc, float *__restrict__ Vc,
+                                 float *__restrict__ mask, const int32_t *__restrict__ position,
+                                 uint32_t heads, uint32_t T, uint32_t D, uint32_t cap,
+                                 uint32_t pos0, bool vec, uint32_t *err) {
+    const int64_t pos = position ? static_cast<int64_t>(*position) : static_cast<int64_t>(pos0);
+    const uint32_t w = vec ? D / 4 : D;   // units per (h, t) row
+    const uint64_t total = static_cast<uint64_t>(heads) * T * w;
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint64_t ht = i / w;
+        const uint32_t u = static_cast<uint32_t>(i - ht * w);
+        const uint32_t h = static_cast<uint32_t>(ht / T), t = static_cast<uint32_t>(ht % T);
+        const int64_t slot = pos + t;
+        if (slot < 0 || slot >= static_cast<int64_t>(cap)) {
+            if (u == 0) record_error(err, kErrBadConfig);
+            continue;
+        }
+        const uint64_t dst = (static_cast<uint64_t>(h) * cap + static_cast<uint64_t>(slot)) * w + u;
+        if (vec) {
+            reinterpret_cast<float4 *>(Kc)[dst] = __ldg(reinterpret_cast<const float4 *>(K) + i);
+            reinterpret_cast<float4 *>(Vc)[dst] = __ldg(reinterpret_cast<const float4 *>(V) + i);
+        } else {
+            Kc[dst] = __ldg(K + i);
+            Vc[dst] = __ldg(V + i);
+        }
+        if (mask && u == 0) mask[static_cast<uint64_t>(h) * cap + static_cast<uint64_t>(slot)] = 0.0f;
+    }
+}
+
 // Spins on a flag nothing sets, bounded by limit_ns: the device-side wait
 // pattern of the GEMM pipeline, exercised on its own.
 __global__ void wait_probe_kernel(const uint32_t *flag, uint64_t limit_ns, uint32_t *err) {
@@ -1118,6 +1149,21 @@ cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, cons
         attention_kernel<true><<<grid, kAttThreads, smem, ctx.stream>>>(ap);
     else
         attention_kernel<false><<<grid, kAttThreads, smem, ctx.stream>>>(ap);
+    count_launch(ctx);
+    return cudaGetLastError();
+}
+
+cudaError_t kv_append(const LaunchCtx &ctx, const float *K, const float *V, float *K_cache,
+                      float *V_cache, float *mask, const int32_t *position, uint32_t heads,
+                      uint32_t T, uint32_t head_dim, uint32_t capacity, uint32_t position_offset) {
+    const bool vec = head_dim % 4 == 0 &&
+                     ((reinterpret_cast<uintptr_t>(K) | reinterpret_cast<uintptr_t>(V) |
+                       reinterpret_cast<uintptr_t>(K_cache) | reinterpret_cast<uintptr_t>(V_cache)) &
+                      15u) == 0;
+    const uint64_t total = static_cast<uint64_t>(heads) * T * (vec ? head_dim / 4 : head_dim);
+    kv_append_kernel<<<grid_for(total, ctx.num_sms, 256), 256, 0, ctx.stream>>>(
+        K, V, K_cache, V_cache, mask, position, heads, T, head_dim, capacity, position_offset, vec,
+        ctx.err);
     count_launch(ctx);
     return cudaGetLastError();
 }

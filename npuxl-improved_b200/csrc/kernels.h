@@ -98,6 +98,10 @@ cudaError_t rmsnorm_quantize(const LaunchCtx &ctx, const float *X, const float *
 // SWIGLU_F32 then QUANTIZE_I8 per row in one pass (Y may be NULL).
 cudaError_t swiglu_quantize(const LaunchCtx &ctx, const float *gate, const float *up, float *Y,
                             int8_t *Q, float *scales, uint32_t rows, uint32_t cols, float alpha);
+// KV-cache append (VNPU_B200_OP_KV_APPEND); position may be a device pointer.
+cudaError_t kv_append(const LaunchCtx &ctx, const float *K, const float *V, float *K_cache,
+                      float *V_cache, float *mask, const int32_t *position, uint32_t heads,
+                      uint32_t T, uint32_t head_dim, uint32_t capacity, uint32_t position_offset);
 cudaError_t rope(const LaunchCtx &ctx, float *Q, float *K, const int32_t *positions,
                  uint32_t batch, uint32_t heads, uint32_t q_seq, uint32_t k_seq,
                  uint32_t head_dim, uint32_t position_offset, uint32_t interleaved,

@@ -439,6 +439,33 @@ void exec_swiglu_quantize(vnpu_stream_t *s, const vnpu_command_t &cmd, const Lau
     acc.dma = st.staged_bytes();
 }
 
+void exec_kv_append(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &ctx,
+                    Accounting &acc) {
+    vnpu_b200_kv_append_args_t a;
+    std::memcpy(&a, cmd.args.raw, sizeof(a));
+    if (!a.K || !a.V || !a.K_cache || !a.V_cache || !a.heads || !a.T || !a.head_dim ||
+        !a.capacity)
+        throw CommandError("invalid kv_append arguments", VNPU_ERR_INVALID_ARGUMENT);
+    if (!a.position && static_cast<uint64_t>(a.position_offset) + a.T > a.capacity)
+        throw CommandError("kv_append past the cache capacity", VNPU_ERR_INVALID_ARGUMENT);
+    const uint64_t n = static_cast<uint64_t>(a.heads) * a.T * a.head_dim;
+    const uint64_t cn = static_cast<uint64_t>(a.heads) * a.capacity * a.head_dim;
+    Staging st(s);
+    const float *K = st.in(a.K, n * sizeof(float));
+    const float *V = st.in(a.V, n * sizeof(float));
+    float *Kc = st.out(a.K_cache, cn * sizeof(float), true);
+    float *Vc = st.out(a.V_cache, cn * sizeof(float), true);
+    float *M = a.mask ? st.out(a.mask, sizeof(float) * a.heads * a.capacity, true) : nullptr;
+    const int32_t *P = a.position ? st.in(a.position, sizeof(int32_t)) : nullptr;
+    cuda_check(kv_append(ctx, K, V, Kc, Vc, M, P, a.heads, a.T, a.head_dim, a.capacity,
+                         a.position_offset),
+               "kv_append launch");
+    st.finish();
+    acc.bytes_read = 2 * n * sizeof(float);
+    acc.bytes_written = 2 * n * sizeof(float);
+    acc.dma = st.staged_bytes();
+}
+
 void exec_swiglu(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &ctx,
                  Accounting &acc) {
     const auto &a = cmd.args.swiglu;
@@ -561,7 +588,7 @@ const char *opcode_name(uint32_t op);
 vnpu_status_t execute_command(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags) {
     vnpu_device_t *dev = s->device;
     if (cmd.opcode >= VNPU_OP_COUNT && cmd.opcode != VNPU_B200_OP_RMSNORM_QUANTIZE_I8 &&
-        cmd.opcode != VNPU_B200_OP_SWIGLU_QUANTIZE_I8)
+        cmd.opcode != VNPU_B200_OP_SWIGLU_QUANTIZE_I8 && cmd.opcode != VNPU_B200_OP_KV_APPEND)
         return VNPU_ERR_INVALID_COMMAND;
     dev->last_opcode.store(cmd.opcode);
     const bool tracing = dev->trace.enabled.load();
@@ -600,6 +627,7 @@ vnpu_status_t execute_command(vnpu_stream_t *s, const vnpu_command_t &cmd, uint3
         case VNPU_OP_COPY: exec_copy(s, cmd, acc); break;
         case VNPU_B200_OP_RMSNORM_QUANTIZE_I8: exec_rmsnorm_quantize(s, cmd, ctx, acc); break;
         case VNPU_B200_OP_SWIGLU_QUANTIZE_I8: exec_swiglu_quantize(s, cmd, ctx, acc); break;
+        case VNPU_B200_OP_KV_APPEND: exec_kv_append(s, cmd, ctx, acc); break;
         case VNPU_OP_MEMSET: exec_memset(s, cmd, acc); break;
         case VNPU_OP_PACK_WEIGHTS_I8: exec_pack(s, cmd, acc); break;
         default:
@@ -707,6 +735,7 @@ const char *opcode_name(uint32_t op) {
                                   "MEMSET",        "BARRIER"};
     if (op == VNPU_B200_OP_RMSNORM_QUANTIZE_I8) return "RMSNORM_QUANTIZE_I8";
     if (op == VNPU_B200_OP_SWIGLU_QUANTIZE_I8) return "SWIGLU_QUANTIZE_I8";
+    if (op == VNPU_B200_OP_KV_APPEND) return "KV_APPEND";
     return op < sizeof(names) / sizeof(names[0]) ? names[op] : "UNKNOWN";
 }
 

@@ -195,7 +195,7 @@ class B200Block:
 
     def __init__(self, cfg: BlockConfig, lib, dev, torch, fused: bool = True):
         self.cfg, self.lib, self.dev, self.t = cfg, lib, dev, torch
-        self.fused = fused   # fused RMSNorm/SwiGLU -> QUANTIZE_I8 prologues (B200 opcodes)
+        self.fused = fused   # B200 opcodes: fused RMSNorm/SwiGLU -> QUANTIZE_I8, KV_APPEND
         self.stream = torch.cuda.ExternalStream(lib.b200_stream_handle(dev.stream))
         w, (n1, n2) = make_weights(cfg)
         self.n1 = torch.from_numpy(n1).cuda()
@@ -315,17 +315,25 @@ class B200Block:
                                  1, H, T, T, hd, pos0, 0, cfg.theta, 1.0)
             self._submit([_cmd(vnpu.OP_ROPE_F32, "rope", rope)])
             O = self._buf(f"O{T}", (1, H, T, hd))
+            if self.fused:
+                # cache append + mask in one command (VNPU_B200_OP_KV_APPEND)
+                self._submit([vnpu.b200_command(vnpu.OP_B200_KV_APPEND, vnpu.KvAppendArgs(
+                    K.data_ptr(), V.data_ptr(), self.kc.data_ptr(), self.vc.data_ptr(),
+                    self.mask.data_ptr(), positions.data_ptr() if positions is not None else None,
+                    H, T, hd, cfg.cap, pos0, 0))])
             if T > 1:
-                self.kc[:, :, pos0:pos0 + T].copy_(K)
-                self.vc[:, :, pos0:pos0 + T].copy_(V)
-                self.mask[..., pos0:pos0 + T] = 0.0
+                if not self.fused:
+                    self.kc[:, :, pos0:pos0 + T].copy_(K)
+                    self.vc[:, :, pos0:pos0 + T].copy_(V)
+                    self.mask[..., pos0:pos0 + T] = 0.0
                 att = vnpu.AttentionArgs(Q.data_ptr(), K.data_ptr(), V.data_ptr(), None,
                                          O.data_ptr(), None, 0, 1, H, T, T, hd, 1, 0.0, 0)
             else:
-                idx = positions.long() if positions is not None else t.tensor([pos0], device="cuda")
-                self.kc.index_copy_(2, idx, K)
-                self.vc.index_copy_(2, idx, V)
-                self.mask.index_fill_(3, idx, 0.0)
+                if not self.fused:
+                    idx = positions.long() if positions is not None else t.tensor([pos0], device="cuda")
+                    self.kc.index_copy_(2, idx, K)
+                    self.vc.index_copy_(2, idx, V)
+                    self.mask.index_fill_(3, idx, 0.0)
                 att = vnpu.AttentionArgs(Q.data_ptr(), self.kc.data_ptr(), self.vc.data_ptr(),
                                          self.mask.data_ptr(), O.data_ptr(), None, 0, 1, H, 1,
                                          cfg.cap, hd, 0, 0.0, 0)

@@ -173,6 +173,15 @@ class SwigluQuantizeArgs(C.Structure):
                 ("cols", u32), ("alpha", C.c_float), ("reserved0", u32)]
 
 
+OP_B200_KV_APPEND = 0x102
+
+
+class KvAppendArgs(C.Structure):
+    _fields_ = [("K", vp), ("V", vp), ("K_cache", vp), ("V_cache", vp), ("mask", vp),
+                ("position", vp), ("heads", u32), ("T", u32), ("head_dim", u32),
+                ("capacity", u32), ("position_offset", u32), ("reserved0", u32)]
+
+
 def b200_command(opcode: int, args: C.Structure) -> "Command":
     """A command whose arguments are a B200 extension struct (copied into args.raw)."""
     c = Command()

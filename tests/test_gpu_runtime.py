@@ -437,3 +437,63 @@ def test_pipelined_steps_with_host_buffers(gpu, oracle):
             assert bits_equal(Cs[i], oracle.matmul_i8(Ao, B, sao, sb, None, 0, 0)), i
     finally:
         gpu.unpack(w)
+
+
+# ----------------------------------------------------------------- KV_APPEND
+def _kv_cmd(K, V, Kc, Vc, mask, position, heads, T, D, cap, pos0):
+    return vnpu.b200_command(vnpu.OP_B200_KV_APPEND, vnpu.KvAppendArgs(
+        vnpu.ptr(K), vnpu.ptr(V), vnpu.ptr(Kc), vnpu.ptr(Vc), vnpu.ptr(mask), vnpu.ptr(position),
+        heads, T, D, cap, pos0, 0))
+
+
+@pytest.mark.parametrize("T,D,use_pos,with_mask", [(1, 128, True, True), (5, 128, False, True),
+                                                   (3, 6, True, False), (1, 13, False, True)])
+def test_kv_append(gpu, T, D, use_pos, with_mask):
+    """Head-major K/V land in slots pos..pos+T-1 of every head; the mask's
+    slots become 0; nothing else changes.  pos from a device int32 or the
+    offset field."""
+    torch = pytest.importorskip("torch")
+    H, cap, pos = 4, 40, 17
+    rng = np.random.default_rng(T * 100 + D)
+    K = torch.from_numpy(rng.normal(0, 1, (H, T, D)).astype(np.float32)).cuda()
+    V = torch.from_numpy(rng.normal(0, 1, (H, T, D)).astype(np.float32)).cuda()
+    Kc = torch.full((H, cap, D), 7.0, device="cuda")
+    Vc = torch.full((H, cap, D), -7.0, device="cuda")
+    mask = torch.full((H, cap), float("-inf"), device="cuda") if with_mask else None
+    P = torch.tensor([pos], dtype=torch.int32, device="cuda") if use_pos else None
+    torch.cuda.synchronize()
+    assert gpu.submit([_kv_cmd(K, V, Kc, Vc, mask, P, H, T, D, cap, 0 if use_pos else pos)]) == vnpu.OK
+    assert gpu.sync() == vnpu.OK
+    Ke = torch.full((H, cap, D), 7.0); Ke[:, pos:pos + T] = K.cpu()
+    Ve = torch.full((H, cap, D), -7.0); Ve[:, pos:pos + T] = V.cpu()
+    assert torch.equal(Kc.cpu(), Ke) and torch.equal(Vc.cpu(), Ve)
+    if with_mask:
+        Me = torch.full((H, cap), float("-inf")); Me[:, pos:pos + T] = 0.0
+        assert torch.equal(mask.cpu(), Me)
+
+
+def test_kv_append_past_capacity(b200_lib):
+    """A host-known slot past the capacity is refused before launch; a device
+    position past it writes nothing and reports a device error (no fault)."""
+    torch = pytest.importorskip("torch")
+    dev = vnpu.Device(b200_lib)
+    try:
+        H, T, D, cap = 2, 3, 8, 10
+        K = torch.ones((H, T, D), device="cuda")
+        Kc = torch.zeros((H, cap, D), device="cuda")
+        Vc = torch.zeros((H, cap, D), device="cuda")
+        torch.cuda.synchronize()
+        assert dev.submit([_kv_cmd(K, K, Kc, Vc, None, None, H, T, D, cap, 8)]) == vnpu.OK
+        assert dev.sync() == vnpu.ERR_DEVICE_ERROR          # sticky, as for any failed command
+    finally:
+        dev.close()
+    dev = vnpu.Device(b200_lib)
+    try:
+        P = torch.tensor([9], dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        assert dev.submit([_kv_cmd(K, K, Kc, Vc, None, P, H, T, D, cap, 0)]) == vnpu.OK
+        assert dev.sync() == vnpu.ERR_DEVICE_ERROR
+        # slot 9 (in range) was written for t = 0; slots 10, 11 were not
+        assert torch.equal(Kc[:, 9].cpu(), torch.ones((H, D))) and Kc[:, :9].abs().sum().item() == 0
+    finally:
+        dev.close()
