@@ -908,14 +908,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 // shared memory (exact, fixed order) and applies the dequant epilogue.
 // ===========================================================================
 
-constexpr uint32_t kSkStages = 4;
 constexpr uint32_t kSkWBytes = 128 * kBK;   // 16 KiB of weight rows per stage
 constexpr uint32_t kSkXBytes = 8 * kBK;     // 1 KiB of activations per stage
 constexpr uint32_t kSkThreads = 128;
 constexpr uint32_t kSkMaxCluster = 8;
 constexpr uint32_t kSkPartBytes = 128 * 8 * 4;  // one CTA's partial tile [128][8] int32
-constexpr uint32_t kSkSmemBytes =
-    kSkStages * (kSkWBytes + kSkXBytes) + kSkMaxCluster * kSkPartBytes + 1024;
+// Shared memory of a kStages-deep ring with partial tiles for csize ranks.
+constexpr uint32_t sk_smem_bytes(uint32_t stages, uint32_t csize) {
+    return stages * (kSkWBytes + kSkXBytes) + csize * kSkPartBytes + 1024;
+}
 
 struct SkParams {
     const float *scale_a;
@@ -930,7 +931,8 @@ struct SkParams {
     uint64_t limit_ns;
 };
 
-__global__ void __launch_bounds__(kSkThreads, 2)
+template <uint32_t kSkStages, uint32_t kMinBlocks>
+__global__ void __launch_bounds__(kSkThreads, kMinBlocks)
     gemv_i8_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w,
                            const __grid_constant__ CUtensorMap tmap_x, const SkParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -1543,19 +1545,55 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
 
 namespace {
 
-cudaError_t gemv_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
-    static bool attr[64] = {};
+template <uint32_t kStages, uint32_t kMinBlocks>
+cudaError_t gemv_tcgen05_launch(const LaunchCtx &ctx, const MatmulI8 &p, const CUtensorMap &tmap_x,
+                                SkParams sp) {
+    // Split K over a cluster so that about kMinBlocks CTAs per SM stream weights.
+    const uint32_t blocks = (p.N + 127u) / 128u;
+    // Clusters of at most 4: measured best on B200 (8-CTA clusters fit the
+    // GPCs less evenly).
+    uint32_t max_c = 4u;
+    if (const char *e = std::getenv("VNPU_B200_DECODE_CLUSTER")) max_c = std::max(1, std::atoi(e));
+    if (max_c > kSkMaxCluster) max_c = kSkMaxCluster;
+    while (max_c > 1 && sk_smem_bytes(kStages, max_c) > 226u * 1024u) max_c /= 2u;
+    uint32_t csize = 1;
+    while (csize < max_c &&
+           blocks * csize * 2u <= kMinBlocks * static_cast<uint32_t>(ctx.num_sms) &&
+           csize * 2u <= sp.num_kb)
+        csize *= 2u;
+    sp.kb_per_rank = (sp.num_kb + csize - 1) / csize;
+    // Opt in to the shared memory this launch needs (per device, grown on demand).
+    static uint32_t opted[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_i8_tcgen05_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kSkSmemBytes));
+    const uint32_t smem = sk_smem_bytes(kStages, csize);
+    if (dev < 0 || dev >= 64 || opted[dev] < smem) {
+        const cudaError_t e = cudaFuncSetAttribute(gemv_i8_tcgen05_kernel<kStages, kMinBlocks>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(smem));
         if (e != cudaSuccess) return e;
-        e = cudaFuncSetAttribute(gemv_i8_tcgen05_kernel,
-                                 cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
-        attr[dev] = true;
+        if (dev >= 0 && dev < 64) opted[dev] = smem;
     }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks * csize, 1, 1);
+    cfg.blockDim = dim3(kSkThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx.stream;
+    cudaLaunchAttribute attrs[2];
+    attrs[0].id = cudaLaunchAttributeClusterDimension;
+    attrs[0].val.clusterDim.x = csize;
+    attrs[0].val.clusterDim.y = 1;
+    attrs[0].val.clusterDim.z = 1;
+    attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = std::getenv("VNPU_B200_NO_PDL") ? 1 : 2;
+    g_last_kernel.store("gemv_i8_tcgen05_kernel", std::memory_order_relaxed);
+    return cudaLaunchKernelEx(&cfg, gemv_i8_tcgen05_kernel<kStages, kMinBlocks>, *p.tmap_b128,
+                              tmap_x, sp);
+}
+
+cudaError_t gemv_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
     CUtensorMap tmap_x;
     if (!encode_tmap_kmajor_i8(&tmap_x, p.A, p.K, p.M, p.lda, kBK, 8)) return cudaErrorInvalidValue;
     SkParams sp;
@@ -1572,33 +1610,15 @@ cudaError_t gemv_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
     sp.form = p.form;
     sp.err = ctx.err;
     sp.limit_ns = ctx.wait_limit_ns;
-    // Split K over a cluster so that about two CTAs per SM stream weights.
-    const uint32_t blocks = (p.N + 127u) / 128u;
-    // Clusters of 4: measured best on B200 (8-CTA clusters fit the GPCs
-    // less evenly at two CTAs per SM).
-    uint32_t max_c = 4u;
-    if (const char *e = std::getenv("VNPU_B200_DECODE_CLUSTER")) max_c = std::max(1, std::atoi(e));
-    uint32_t csize = 1;
-    while (csize < max_c && blocks * csize * 2u <= 2u * static_cast<uint32_t>(ctx.num_sms) &&
-           csize * 2u <= sp.num_kb)
-        csize *= 2u;
-    sp.kb_per_rank = (sp.num_kb + csize - 1) / csize;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(blocks * csize, 1, 1);
-    cfg.blockDim = dim3(kSkThreads, 1, 1);
-    cfg.dynamicSmemBytes = kSkSmemBytes;
-    cfg.stream = ctx.stream;
-    cudaLaunchAttribute attrs[2];
-    attrs[0].id = cudaLaunchAttributeClusterDimension;
-    attrs[0].val.clusterDim.x = csize;
-    attrs[0].val.clusterDim.y = 1;
-    attrs[0].val.clusterDim.z = 1;
-    attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attrs[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attrs;
-    cfg.numAttrs = std::getenv("VNPU_B200_NO_PDL") ? 1 : 2;
-    g_last_kernel.store("gemv_i8_tcgen05_kernel", std::memory_order_relaxed);
-    return cudaLaunchKernelEx(&cfg, gemv_i8_tcgen05_kernel, *p.tmap_b128, tmap_x, sp);
+    // Five 17 KiB stages at two CTAs per SM: measured best of 4/5/8/12 on B200
+    // (deeper rings at one CTA per SM leave no room for the next launch).
+    uint32_t stages = 5;
+    if (const char *e = std::getenv("VNPU_B200_GEMV_STAGES")) stages = std::atoi(e);
+    switch (stages) {
+    case 4: return gemv_tcgen05_launch<4, 2>(ctx, p, tmap_x, sp);
+    case 8: return gemv_tcgen05_launch<8, 1>(ctx, p, tmap_x, sp);
+    default: return gemv_tcgen05_launch<5, 2>(ctx, p, tmap_x, sp);
+    }
 }
 
 }  // namespace
