@@ -363,6 +363,16 @@ constexpr uint32_t kAttThreads = 512;
 constexpr uint32_t kAttMaxD = 256;
 constexpr uint32_t kAttMaxChain = kAttMaxD / 8;
 
+// Chain-major Q tile: chain c of a query starts at c * att_chain_stride; the
+// stride is 4 mod 8 floats so the eight chains fall in eight distinct groups
+// of four banks (16-byte reads conflict-free).
+__host__ __device__ constexpr uint32_t att_chain_stride(uint32_t chains) {
+    return chains + ((4u + 8u - (chains & 7u)) & 7u);
+}
+__host__ __device__ constexpr uint32_t att_q_stride(uint32_t D) {
+    return 8u * att_chain_stride(D / 8u) + (D & 7u);
+}
+
 struct AttParams {
     const float *Q, *K, *V, *mask;
     float *O;
@@ -382,8 +392,10 @@ __global__ void __launch_bounds__(kAttThreads) attention_kernel(const AttParams 
     extern __shared__ float att_smem[];
     const uint32_t D = p.D;
     const uint32_t chains = D / 8, full = chains * 8, tail = D - full;
-    float *Qs = att_smem;                                  // 16*D
-    float *Vs = Qs + kAttBQ * D;                           // 64*D
+    const uint32_t cstride = att_chain_stride(chains);     // padded: conflict-free chains
+    const uint32_t qstride = att_q_stride(D);
+    float *Qs = att_smem;                                  // 16*qstride
+    float *Vs = Qs + kAttBQ * qstride;                     // 64*D
     float *S = Vs + kAttBK * D;                            // 16*64
 
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -401,8 +413,10 @@ __global__ void __launch_bounds__(kAttThreads) attention_kernel(const AttParams 
     for (uint32_t i = tid; i < kAttBQ * D; i += kAttThreads) {
         const uint32_t q = i / D, e = i % D;
         const float v = q < qc ? Qh[static_cast<uint64_t>(q0 + q) * D + e] : 0.0f;
-        // element e = 8t + c of the vector part goes to chain c, position t
-        const uint32_t dst = e < full ? q * D + (e & 7u) * chains + (e >> 3) : q * D + e;
+        // element e = 8t + c of the vector part goes to chain c, position t;
+        // the D%8 tail follows the eight chains
+        const uint32_t dst = e < full ? q * qstride + (e & 7u) * cstride + (e >> 3)
+                                      : q * qstride + 8u * cstride + (e - full);
         Qs[dst] = v;
     }
 
@@ -435,7 +449,7 @@ __global__ void __launch_bounds__(kAttThreads) attention_kernel(const AttParams 
             kreg[t] = (key_ok && t < chains) ? __ldg(krow + 8 * t + my_chain) : 0.0f;
         __syncthreads();  // Qs (first block) and Vs visible
         for (uint32_t q = 0; q < qc; ++q) {
-            const float *qchain = Qs + q * D + my_chain * chains;
+            const float *qchain = Qs + q * qstride + my_chain * cstride;
             float part = 0.0f;
             if (VEC && (chains & 3u) == 0u) {
 #pragma unroll
@@ -462,7 +476,7 @@ __global__ void __launch_bounds__(kAttThreads) attention_kernel(const AttParams 
             if (my_chain == 0 && key_ok) {
                 float dot = __fadd_rn(s01, s23);
                 for (uint32_t i = 0; i < tail; ++i)
-                    dot = __fmaf_rn(Qs[q * D + full + i], krow[full + i], dot);
+                    dot = __fmaf_rn(Qs[q * qstride + 8u * cstride + i], krow[full + i], dot);
                 const uint32_t qi = q0 + q, ki = k0 + my_key;
                 float sc;
                 if (p.causal && ki > qi + causal_offset) {
@@ -483,13 +497,24 @@ __global__ void __launch_bounds__(kAttThreads) attention_kernel(const AttParams 
         for (int o = 16; o > 0; o >>= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
         if (!isfinite(bmax)) continue;  // fully masked block: skipped, as in the reference
         const float nm = fmaxf(m_run, bmax);
-        for (uint32_t j = lane; j < kc; j += 32) srow[j] = ref_fast_expf(__fsub_rn(srow[j], nm), false);
+        const float p_lo = lane < kc ? ref_fast_expf(__fsub_rn(srow[lane], nm), false) : 0.0f;
+        const float p_hi = lane + 32 < kc ? ref_fast_expf(__fsub_rn(srow[lane + 32], nm), false) : 0.0f;
+        if (lane < kc) srow[lane] = p_lo;
+        if (lane + 32 < kc) srow[lane + 32] = p_hi;
         const float alpha = ref_fast_expf(__fsub_rn(m_run, nm), false);
         __syncwarp();
+        // the in-order sum of p over the block's keys, walked through shuffles
         float sum_p = 0.0f;
-        if (lane == 0)
-            for (uint32_t j = 0; j < kc; ++j) sum_p = __fadd_rn(sum_p, srow[j]);
-        sum_p = __shfl_sync(0xffffffffu, sum_p, 0);
+#pragma unroll
+        for (uint32_t j = 0; j < 32; ++j) {
+            const float v = __shfl_sync(0xffffffffu, p_lo, j);
+            if (j < kc) sum_p = __fadd_rn(sum_p, v);
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < 32; ++j) {
+            const float v = __shfl_sync(0xffffffffu, p_hi, j);
+            if (j + 32 < kc) sum_p = __fadd_rn(sum_p, v);
+        }
         l_run = __fadd_rn(__fmul_rn(l_run, alpha), sum_p);
         m_run = nm;
         // ---- values: acc = acc*alpha, then acc = fma(V[j], p_j, acc) in key order
@@ -1078,15 +1103,16 @@ cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, cons
                       uint32_t seq_q, uint32_t seq_k, uint32_t head_dim, uint32_t causal,
                       float scale) {
     if (head_dim > kAttMaxD || head_dim == 0) return cudaErrorInvalidValue;
-    const size_t smem = sizeof(float) * (kAttBQ * head_dim + kAttBK * head_dim + kAttBQ * kAttBK);
+    const size_t smem =
+        sizeof(float) * (kAttBQ * att_q_stride(head_dim) + kAttBK * head_dim + kAttBQ * kAttBK);
     const bool vec = head_dim % 4 == 0 && (reinterpret_cast<uintptr_t>(V) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(O) & 15) == 0;
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        const int max_smem = static_cast<int>(sizeof(float) * (kAttBQ + kAttBK) * kAttMaxD +
-                                              sizeof(float) * kAttBQ * kAttBK);
+        const int max_smem = static_cast<int>(sizeof(float) * (kAttBQ * att_q_stride(kAttMaxD) +
+                                                               kAttBK * kAttMaxD + kAttBQ * kAttBK));
         cudaError_t e = cudaFuncSetAttribute(attention_kernel<true>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
         if (e == cudaSuccess)

@@ -279,6 +279,10 @@ __device__ __forceinline__ void bulk_commit() {
 __device__ __forceinline__ void bulk_wait_read0() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+// At most one committed bulk store may still be reading shared memory.
+__device__ __forceinline__ void bulk_wait_read1() {
+    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 // Committed bulk stores are complete.
 __device__ __forceinline__ void bulk_wait0() {
     asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");

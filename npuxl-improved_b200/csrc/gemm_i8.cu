@@ -90,37 +90,6 @@ __device__ __forceinline__ void tile_coords(uint32_t t, uint32_t tiles_m, uint32
     nb = r / rows;
 }
 
-// Dequantise 32 accumulators (columns n0..n0+31 of one row) and store them.
-// vec: C row 16-byte aligned, ldc % 4 == 0, bias NULL or 16-byte aligned.
-__device__ __forceinline__ void store_chunk32(const uint32_t (&r)[32], float *crow, uint32_t n0,
-                                              uint32_t N, float sa, const float *scale_b,
-                                              const float *bias, uint32_t epilogue,
-                                              uint32_t form, bool vec) {
-    const bool has_bias = bias != nullptr;
-    if (vec && n0 + 32u <= N) {
-#pragma unroll
-        for (uint32_t j = 0; j < 32u; j += 4u) {
-            const float4 sb = __ldg(reinterpret_cast<const float4 *>(scale_b + n0 + j));
-            const float4 bb = has_bias ? __ldg(reinterpret_cast<const float4 *>(bias + n0 + j))
-                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-            float4 o;
-            o.x = ref_dequant(static_cast<int32_t>(r[j + 0]), sa, sb.x, has_bias, bb.x, epilogue, form);
-            o.y = ref_dequant(static_cast<int32_t>(r[j + 1]), sa, sb.y, has_bias, bb.y, epilogue, form);
-            o.z = ref_dequant(static_cast<int32_t>(r[j + 2]), sa, sb.z, has_bias, bb.z, epilogue, form);
-            o.w = ref_dequant(static_cast<int32_t>(r[j + 3]), sa, sb.w, has_bias, bb.w, epilogue, form);
-            *reinterpret_cast<float4 *>(crow + n0 + j) = o;
-        }
-        return;
-    }
-#pragma unroll
-    for (uint32_t j = 0; j < 32u; ++j) {
-        const uint32_t n = n0 + j;
-        if (n < N)
-            crow[n] = ref_dequant(static_cast<int32_t>(r[j]), sa, __ldg(scale_b + n), has_bias,
-                                  has_bias ? __ldg(bias + n) : 0.0f, epilogue, form);
-    }
-}
-
 // Store 32 finished values of one row (vec: 16-byte aligned row, ldc % 4 == 0).
 __device__ __forceinline__ void store_row32(const float (&v)[32], float *crow, uint32_t n0,
                                             uint32_t N, bool vec) {
@@ -135,101 +104,74 @@ __device__ __forceinline__ void store_row32(const float (&v)[32], float *crow, u
         if (n0 + j < N) crow[n0 + j] = v[j];
 }
 
-// Launch-constant dequant of 32 accumulators of one row into v[] (variant V
-// = epi_variant(); scale_b is padded to a multiple of 256 so the vector
-// loads never leave its allocation; bias is read guarded past N).
-template <uint32_t V>
-__device__ __forceinline__ void dequant32(const uint32_t (&r)[32], float (&v)[32], float sa,
-                                          const float *scale_b, const float *bias, uint32_t n0,
-                                          uint32_t N, bool bias_vec) {
-    constexpr uint32_t ACT = V & 3u, BIAS = (V >> 2) & 3u;
-    constexpr bool FUSED = ((V >> 4) & 1u) != 0u;
-    const bool full = n0 + 32u <= N;
-#pragma unroll
-    for (uint32_t j = 0; j < 32u; j += 4u) {
-        const float4 sb = __ldg(reinterpret_cast<const float4 *>(scale_b + n0 + j));
-        float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
-        if constexpr (BIAS != 0) {
-            if (bias_vec && full) {
-                bb = __ldg(reinterpret_cast<const float4 *>(bias + n0 + j));
-            } else {
-                bb.x = n0 + j + 0 < N ? __ldg(bias + n0 + j + 0) : 0.0f;
-                bb.y = n0 + j + 1 < N ? __ldg(bias + n0 + j + 1) : 0.0f;
-                bb.z = n0 + j + 2 < N ? __ldg(bias + n0 + j + 2) : 0.0f;
-                bb.w = n0 + j + 3 < N ? __ldg(bias + n0 + j + 3) : 0.0f;
-            }
-        }
-        v[j + 0] = ref_dequant_t<ACT, BIAS, FUSED>(static_cast<int32_t>(r[j + 0]), sa, sb.x, bb.x);
-        v[j + 1] = ref_dequant_t<ACT, BIAS, FUSED>(static_cast<int32_t>(r[j + 1]), sa, sb.y, bb.y);
-        v[j + 2] = ref_dequant_t<ACT, BIAS, FUSED>(static_cast<int32_t>(r[j + 2]), sa, sb.z, bb.z);
-        v[j + 3] = ref_dequant_t<ACT, BIAS, FUSED>(static_cast<int32_t>(r[j + 3]), sa, sb.w, bb.w);
-    }
-}
-
 // The 16 variants epi_variant() can produce.
 #define VNPU_B200_EPI_VARIANTS(X)                                                             \
     X(0x10) X(0x11) X(0x12) X(0x13) X(0x14) X(0x15) X(0x16) X(0x17) X(0x18) X(0x19) X(0x1a) \
     X(0x1b) X(0x02) X(0x03) X(0x0a) X(0x0b)
 
-__device__ __forceinline__ void dequant32_any(uint32_t variant, const uint32_t (&r)[32],
-                                              float (&v)[32], float sa, const float *scale_b,
-                                              const float *bias, uint32_t n0, uint32_t N,
-                                              bool bias_vec) {
-    switch (variant) {
-#define VNPU_B200_CASE(V)                                                 \
-    case V:                                                               \
-        dequant32<V>(r, v, sa, scale_b, bias, n0, N, bias_vec);           \
-        break;
-        VNPU_B200_EPI_VARIANTS(VNPU_B200_CASE)
-#undef VNPU_B200_CASE
-    default:
-        break;
-    }
-}
-
-// dequant32 in place: r[j] (int32 accumulator bits) becomes the f32 bits of
-// its output; saves the 32 registers of a separate result array.
+// Dequant of 32 accumulators of one row whose column scales and biases sit one
+// per lane (lane j holds column j's): the epilogue fetches them once per tile,
+// before the accumulators are ready, instead of per chunk after.  All 32 lanes
+// must execute it (warp shuffles).
 template <uint32_t V>
-__device__ __forceinline__ void dequant32_inplace(uint32_t (&r)[32], float sa,
-                                                  const float *scale_b, const float *bias,
-                                                  uint32_t n0, uint32_t N, bool bias_vec) {
+__device__ __forceinline__ void dequant32_shfl(const uint32_t (&r)[32], float (&v)[32], float sa,
+                                               float s_lane, float b_lane) {
     constexpr uint32_t ACT = V & 3u, BIAS = (V >> 2) & 3u;
     constexpr bool FUSED = ((V >> 4) & 1u) != 0u;
-    const bool full = n0 + 32u <= N;
 #pragma unroll
-    for (uint32_t j = 0; j < 32u; j += 4u) {
-        const float4 sb = __ldg(reinterpret_cast<const float4 *>(scale_b + n0 + j));
-        float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
-        if constexpr (BIAS != 0) {
-            if (bias_vec && full) {
-                bb = __ldg(reinterpret_cast<const float4 *>(bias + n0 + j));
-            } else {
-                bb.x = n0 + j + 0 < N ? __ldg(bias + n0 + j + 0) : 0.0f;
-                bb.y = n0 + j + 1 < N ? __ldg(bias + n0 + j + 1) : 0.0f;
-                bb.z = n0 + j + 2 < N ? __ldg(bias + n0 + j + 2) : 0.0f;
-                bb.w = n0 + j + 3 < N ? __ldg(bias + n0 + j + 3) : 0.0f;
-            }
-        }
-        r[j + 0] = __float_as_uint(ref_dequant_t<ACT, BIAS, FUSED>(static_cast<int32_t>(r[j + 0]), sa, sb.x, bb.x));
-        r[j + 1] = __float_as_uint(ref_dequant_t<ACT, BIAS, FUSED>(static_cast<int32_t>(r[j + 1]), sa, sb.y, bb.y));
-        r[j + 2] = __float_as_uint(ref_dequant_t<ACT, BIAS, FUSED>(static_cast<int32_t>(r[j + 2]), sa, sb.z, bb.z));
-        r[j + 3] = __float_as_uint(ref_dequant_t<ACT, BIAS, FUSED>(static_cast<int32_t>(r[j + 3]), sa, sb.w, bb.w));
+    for (uint32_t j = 0; j < 32u; ++j) {
+        const float sb = __shfl_sync(0xffffffffu, s_lane, j);
+        const float bb = BIAS != 0 ? __shfl_sync(0xffffffffu, b_lane, j) : 0.0f;
+        v[j] = ref_dequant_t<ACT, BIAS, FUSED>(static_cast<int32_t>(r[j]), sa, sb, bb);
     }
 }
 
-__device__ __forceinline__ void dequant32_inplace_any(uint32_t variant, uint32_t (&r)[32], float sa,
-                                                      const float *scale_b, const float *bias,
-                                                      uint32_t n0, uint32_t N, bool bias_vec) {
+template <uint32_t V>
+__device__ __forceinline__ void dequant32_shfl_inplace(uint32_t (&r)[32], float sa, float s_lane,
+                                                       float b_lane) {
+    constexpr uint32_t ACT = V & 3u, BIAS = (V >> 2) & 3u;
+    constexpr bool FUSED = ((V >> 4) & 1u) != 0u;
+#pragma unroll
+    for (uint32_t j = 0; j < 32u; ++j) {
+        const float sb = __shfl_sync(0xffffffffu, s_lane, j);
+        const float bb = BIAS != 0 ? __shfl_sync(0xffffffffu, b_lane, j) : 0.0f;
+        r[j] = __float_as_uint(ref_dequant_t<ACT, BIAS, FUSED>(static_cast<int32_t>(r[j]), sa, sb, bb));
+    }
+}
+
+__device__ __forceinline__ void dequant32_shfl_any(uint32_t variant, const uint32_t (&r)[32],
+                                                   float (&v)[32], float sa, float s_lane,
+                                                   float b_lane) {
     switch (variant) {
-#define VNPU_B200_CASE(V)                                                 \
-    case V:                                                               \
-        dequant32_inplace<V>(r, sa, scale_b, bias, n0, N, bias_vec);      \
+#define VNPU_B200_CASE(V)                                      \
+    case V:                                                    \
+        dequant32_shfl<V>(r, v, sa, s_lane, b_lane);           \
         break;
         VNPU_B200_EPI_VARIANTS(VNPU_B200_CASE)
 #undef VNPU_B200_CASE
     default:
         break;
     }
+}
+
+__device__ __forceinline__ void dequant32_shfl_inplace_any(uint32_t variant, uint32_t (&r)[32],
+                                                           float sa, float s_lane, float b_lane) {
+    switch (variant) {
+#define VNPU_B200_CASE(V)                                      \
+    case V:                                                    \
+        dequant32_shfl_inplace<V>(r, sa, s_lane, b_lane);      \
+        break;
+        VNPU_B200_EPI_VARIANTS(VNPU_B200_CASE)
+#undef VNPU_B200_CASE
+    default:
+        break;
+    }
+}
+
+// Column scale and bias of column n for the lane that holds it (n past N: 1, 0).
+__device__ __forceinline__ void fetch_col(const TcParams &p, uint32_t n, float &s, float &b) {
+    s = n < p.N ? __ldg(p.scale_b + n) : 1.0f;
+    b = (p.bias && n < p.N) ? __ldg(p.bias + n) : 0.0f;
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -354,13 +296,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t row = lane_base + lane;
         const bool vec_ok = (p.ldc % 4u == 0u) &&
                             ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0u);
-        const bool bias_vec = (reinterpret_cast<uintptr_t>(p.bias) & 15u) == 0u;
         uint32_t tcount = 0;
         for (uint32_t t = blockIdx.x; t < total_tiles; t += gridDim.x, ++tcount) {
             uint32_t mb, nb;
             tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, mb, nb);
             const uint32_t acc = tcount & 1u;
             const uint32_t use = tcount >> 1;
+            // Row scale, column scales and biases of the tile are fetched
+            // while the accumulators are still being computed.
+            const uint32_t m = mb * kBM + row;
+            const bool row_ok = m < p.M;
+            const float sa = row_ok ? (p.scale_a ? __ldg(p.scale_a + m) : 1.0f) : 0.0f;
+            float sreg[kBN / 32u], breg[kBN / 32u];
+#pragma unroll
+            for (uint32_t c = 0; c < kBN / 32u; ++c) fetch_col(p, nb * kBN + c * 32u + lane, sreg[c], breg[c]);
             // Lane 0 waits, the warp follows its verdict: the tcgen05.ld below
             // is .sync.aligned and needs all 32 lanes together.
             uint32_t ok = 0;
@@ -369,21 +318,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
-            const uint32_t m = mb * kBM + row;
-            const bool row_ok = m < p.M;
-            const float sa = row_ok ? (p.scale_a ? __ldg(p.scale_a + m) : 1.0f) : 0.0f;
             float *crow = p.C + static_cast<uint64_t>(row_ok ? m : 0) * p.ldc;
-#pragma unroll 1
+#pragma unroll
             for (uint32_t c = 0; c < kBN / 32u; ++c) {
                 uint32_t r[32];
                 __syncwarp();
                 tmem_ld_32cols(tmem_base + (lane_base << 16) + acc * kBN + c * 32u, r);
                 tmem_wait_ld();
                 const uint32_t n0 = nb * kBN + c * 32u;
-                if (!row_ok || n0 >= p.N) continue;
+                if (n0 >= p.N) continue;   // warp-uniform
                 float v[32];
-                dequant32_any(p.variant, r, v, sa, p.scale_b, p.bias, n0, p.N, bias_vec);
-                store_row32(v, crow, n0, p.N, vec_ok);
+                dequant32_shfl_any(p.variant, r, v, sa, sreg[c], breg[c]);
+                if (row_ok) store_row32(v, crow, n0, p.N, vec_ok);
             }
             tc_fence_before();
             __syncwarp();
@@ -415,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // No TMA multicast anywhere: each CTA loads only its own tiles.
 // ===========================================================================
 
-constexpr uint32_t kPStages = 6;
+constexpr uint32_t kPStages = 5;
 constexpr uint32_t kPTileM = 256;                 // per pair
 constexpr uint32_t kPTileN = 256;                 // per pair
 constexpr uint32_t kPABytes = 128 * kBK;          // 16 KiB per CTA
@@ -423,8 +369,9 @@ constexpr uint32_t kPBBytes = 128 * kBK;          // 16 KiB per CTA
 constexpr uint32_t kPStageBytes = kPABytes + kPBBytes;
 constexpr uint32_t kPEpiWarps = 8;                // per CTA
 constexpr uint32_t kPThreads = (2 + kPEpiWarps) * 32;
-constexpr uint32_t kPStageOutBytes = 32 * 32 * 4;  // per epilogue warp: 32 rows x 32 floats
-constexpr uint32_t kPSmemBytes = kPStages * kPStageBytes + kPEpiWarps * kPStageOutBytes + 1024;
+constexpr uint32_t kPStageOutBytes = 32 * 32 * 4;  // one 32 rows x 32 floats staging buffer
+// two staging buffers per epilogue warp: a chunk's store overlaps the next chunk
+constexpr uint32_t kPSmemBytes = kPStages * kPStageBytes + kPEpiWarps * 2 * kPStageOutBytes + 1024;
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     gemm_i8_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -559,9 +506,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         const uint32_t row = rank * 128u + lane_base + lane;
         const bool vec_ok = (p.ldc % 4u == 0u) &&
                             ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0u);
-        const bool bias_vec = (reinterpret_cast<uintptr_t>(p.bias) & 15u) == 0u;
-        uint8_t *stage_out = ring + kPStages * kPStageBytes + (warp - 2u) * kPStageOutBytes;
-        float *my_row = reinterpret_cast<float *>(stage_out + lane * 128u);
+        uint8_t *stage_base = ring + kPStages * kPStageBytes + (warp - 2u) * 2u * kPStageOutBytes;
+        uint32_t sbuf = 0;   // staging buffer of the next chunk
         const uint32_t leader_empty0 = mapa_shared(smem_addr(&tmem_empty_bar[0]), 0);
         const uint32_t leader_empty1 = mapa_shared(smem_addr(&tmem_empty_bar[1]), 0);
         uint32_t tcount = 0;
@@ -570,18 +516,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, mb, nb);
             const uint32_t acc = tcount & 1u;
             const uint32_t use = tcount >> 1;
+            // Scales and biases for the tile, fetched before the accumulators are ready.
+            const uint32_t m_first = mb * kPTileM + rank * 128u + lane_base;  // warp's first row
+            const uint32_t m = m_first + lane;
+            const bool row_ok = m < p.M;
+            const float sa = row_ok ? (p.scale_a ? __ldg(p.scale_a + m) : 1.0f) : 0.0f;
+            float sreg[4], breg[4];
+#pragma unroll
+            for (uint32_t c = 0; c < 4u; ++c)
+                fetch_col(p, nb * kPTileN + col_base + c * 32u + lane, sreg[c], breg[c]);
             uint32_t ok = 0;
             if (lane == 0)
                 ok = mbar_wait(&tmem_full_bar[acc], use & 1u, p.limit_ns, p.err, &abort_flag);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
-            const uint32_t m_first = mb * kPTileM + rank * 128u + lane_base;  // warp's first row
-            const uint32_t m = m_first + lane;
-            const bool row_ok = m < p.M;
-            const float sa = row_ok ? (p.scale_a ? __ldg(p.scale_a + m) : 1.0f) : 0.0f;
             float *crow = p.C + static_cast<uint64_t>(row_ok ? m : 0) * p.ldc;
-#pragma unroll 1
+#pragma unroll
             for (uint32_t c = 0; c < 4u; ++c) {
                 uint32_t r[32];
                 const uint32_t col = col_base + c * 32u;
@@ -591,10 +542,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                 const uint32_t n0 = nb * kPTileN + col;
                 if (n0 >= p.N || m_first >= p.M) continue;  // warp-uniform
                 float v[32];
-                dequant32_any(p.variant, r, v, sa, p.scale_b, p.bias, n0, p.N, bias_vec);
+                dequant32_shfl_any(p.variant, r, v, sa, sreg[c], breg[c]);
                 if (p.tma_store) {
-                    if (lane == 0) bulk_wait_read0();  // previous store has read the buffer
+                    // The store two chunks back used this buffer: it must have read it.
+                    if (lane == 0) bulk_wait_read1();
                     __syncwarp();
+                    uint8_t *stage_out = stage_base + sbuf * kPStageOutBytes;
+                    float *my_row = reinterpret_cast<float *>(stage_out + lane * 128u);
+                    sbuf ^= 1u;
 #pragma unroll
                     for (uint32_t j = 0; j < 8u; ++j)
                         *reinterpret_cast<float4 *>(my_row + 4u * (j ^ (lane & 7u))) =
@@ -614,7 +569,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc ? leader_empty1 : leader_empty0);
         }
-        if (lane == 0) bulk_wait0();  // C written before the CTA retires
+        // Shared memory must outlive the stores' reads; their global writes
+        // complete with the grid like any other store.
+        if (lane == 0) bulk_wait_read0();
     }
 
     // ---------------------------------------------------------------- teardown
@@ -820,7 +777,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         const uint32_t col_base = ((warp - 2u) >> 2) * 128u;
         const bool vec_ok = (p.ldc % 4u == 0u) &&
                             ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0u);
-        const bool bias_vec = (reinterpret_cast<uintptr_t>(p.bias) & 15u) == 0u;
         uint8_t *stage_out = ring + kWStages * kWStageBytes + (warp - 2u) * kPStageOutBytes;
         float *my_row = reinterpret_cast<float *>(stage_out + lane * 128u);
         const uint32_t leader_empty0 = mapa_shared(smem_addr(&tmem_empty_bar[0]), 0);
@@ -829,18 +785,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         for (uint32_t t = pair; t < total_tiles; t += npairs, ++tcount) {
             uint32_t mb, nb;
             tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, mb, nb);
+            // Scales and biases for the tile, fetched before the accumulators are ready.
+            const uint32_t m_first = mb * kPTileM + rank * 128u + lane_base;  // warp's first row
+            const uint32_t m = m_first + lane;
+            const bool row_ok = m < p.M;
+            const float sa = row_ok ? (p.scale_a ? __ldg(p.scale_a + m) : 1.0f) : 0.0f;
+            float sreg[8], breg[8];
+#pragma unroll
+            for (uint32_t c = 0; c < 8u; ++c)
+                fetch_col(p, nb * kWTileN + (c >> 2) * 256u + col_base + (c & 3u) * 32u + lane,
+                          sreg[c], breg[c]);
             uint32_t ok = 0;
             if (lane == 0)
                 ok = mbar_wait(&tmem_full_bar, tcount & 1u, p.limit_ns, p.err, &abort_flag);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
-            const uint32_t m_first = mb * kPTileM + rank * 128u + lane_base;  // warp's first row
-            const uint32_t m = m_first + lane;
-            const bool row_ok = m < p.M;
-            const float sa = row_ok ? (p.scale_a ? __ldg(p.scale_a + m) : 1.0f) : 0.0f;
             float *crow = p.C + static_cast<uint64_t>(row_ok ? m : 0) * p.ldc;
-#pragma unroll 1
+#pragma unroll
             for (uint32_t h = 0; h < 2u; ++h) {
                 // The warp's 128 columns of half h go to registers in one
                 // round of loads, and the half is released before any of it
@@ -861,8 +823,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                     const uint32_t col = h * 256u + col_base + c * 32u;
                     const uint32_t n0 = nb * kWTileN + col;
                     if (n0 >= p.N || m_first >= p.M) continue;  // warp-uniform
-                    dequant32_inplace_any(p.variant, r[c], sa, p.scale_b, p.bias, n0, p.N,
-                                          bias_vec);
+                    dequant32_shfl_inplace_any(p.variant, r[c], sa, sreg[h * 4u + c], breg[h * 4u + c]);
                     const float(&v)[32] = reinterpret_cast<const float(&)[32]>(r[c]);
                     if (p.tma_store) {
                         if (lane == 0) bulk_wait_read0();  // previous store has read the buffer
@@ -885,7 +846,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                 }
             }
         }
-        if (lane == 0) bulk_wait0();  // C written before the CTA retires
+        // Shared memory must outlive the stores' reads; their global writes
+        // complete with the grid like any other store.
+        if (lane == 0) bulk_wait_read0();
     }
 
     // ---------------------------------------------------------------- teardown
