@@ -585,7 +585,8 @@ def run_b200(args):
 
 def run_kernel_case(spec: str):
     """One small case of one kernel, launched twice (for ncu captures):
-    gemm:MxKxN[:silu], gemv:MxKxN, quantize:RxC, attention:HxSQxSKxD."""
+    gemm:MxKxN[:silu], gemv:MxKxN, quantize:RxC, attention:HxSQxSKxD, or
+    llm_decode:STEPS (the decoder block's graph-captured decode step)."""
     import torch
 
     lib = vnpu.Lib(vnpu.LIB_PATH)
@@ -626,6 +627,27 @@ def run_kernel_case(spec: str):
         for _ in range(2):
             dev.attention(Q.data_ptr(), Kt.data_ptr(), V.data_ptr(), None, O.data_ptr(), 1, H,
                           SQ, SK, D, 1, 0.0)
+    elif kind == "llm_decode":
+        # configs[3] decoder block: prefill 512 tokens, capture one decode step
+        # as a CUDA graph, replay it `steps` times.
+        from llm_block import B200Block, BlockConfig
+        steps = shape[0]
+        cfg = BlockConfig(cap=640)
+        blk = B200Block(cfg, lib, dev, torch)
+        x = torch.empty((512, cfg.d), device="cuda").normal_(0, 1, generator=g)
+        blk.forward(x, 0)
+        dev.sync()
+        xin = blk._buf("decode_in", (1, cfg.d))
+        xin.normal_(0, 1, generator=g)
+        blk.pos.fill_(512)
+        torch.cuda.synchronize()
+        blk.capture_decode(xin)
+        blk.pos.fill_(512)
+        torch.cuda.synchronize()
+        for _ in range(steps):
+            blk.replay_decode()
+        torch.cuda.synchronize()
+        blk.close()
     else:
         raise SystemExit(f"unknown kernel case {spec}")
     rc = dev.sync()
