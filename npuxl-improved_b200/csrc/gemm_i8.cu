@@ -361,25 +361,35 @@ __global__ void __launch_bounds__(kThreads, 1)
 // No TMA multicast anywhere: each CTA loads only its own tiles.
 // ===========================================================================
 
-constexpr uint32_t kPStages = 5;
+constexpr uint32_t kPStages = 6;                  // stage count of the wide kernel's sibling (8 warps)
 constexpr uint32_t kPTileM = 256;                 // per pair
 constexpr uint32_t kPTileN = 256;                 // per pair
 constexpr uint32_t kPABytes = 128 * kBK;          // 16 KiB per CTA
 constexpr uint32_t kPBBytes = 128 * kBK;          // 16 KiB per CTA
 constexpr uint32_t kPStageBytes = kPABytes + kPBBytes;
-constexpr uint32_t kPEpiWarps = 8;                // per CTA
+constexpr uint32_t kPEpiWarps = 8;                // per CTA (wide kernel)
 constexpr uint32_t kPThreads = (2 + kPEpiWarps) * 32;
+// The 256x256 pair kernel comes in two shapes: 8 epilogue warps and 6 stages
+// for NONE / RELU (the MMA issuer keeps its sub-partition), and 16 epilogue
+// warps and 5 stages for SiLU / GELU, whose dequant epilogue (polynomial exp,
+// IEEE divisions) is latency-bound: four warps per sub-partition hide it
+// behind the next tile's MMAs.
+constexpr uint32_t pair_threads(uint32_t epi_warps) { return (2 + epi_warps) * 32; }
+constexpr uint32_t pair_smem_bytes(uint32_t epi_warps, uint32_t stages) {
+    return stages * (128 * kBK * 2) + epi_warps * 32 * 32 * 4 + 1024;
+}
 constexpr uint32_t kPStageOutBytes = 32 * 32 * 4;  // one 32 rows x 32 floats staging buffer
-// two staging buffers per epilogue warp: a chunk's store overlaps the next chunk
-constexpr uint32_t kPSmemBytes = kPStages * kPStageBytes + kPEpiWarps * 2 * kPStageOutBytes + 1024;
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
+
+template <uint32_t kNEpiWarps, uint32_t kNStages>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWarps), 1)
     gemm_i8_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                 const __grid_constant__ CUtensorMap tmap_b,
                                 const __grid_constant__ CUtensorMap tmap_c, const TcParams p) {
+    constexpr uint32_t kNColsPerWarp = 4u * kPTileN / kNEpiWarps;   // 128 or 64 columns
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t full_bar[kPStages];
-    __shared__ __align__(8) uint64_t empty_bar[kPStages];
+    __shared__ __align__(8) uint64_t full_bar[kNStages];
+    __shared__ __align__(8) uint64_t empty_bar[kNStages];
     __shared__ __align__(8) uint64_t tmem_full_bar[2];
     __shared__ __align__(8) uint64_t tmem_empty_bar[2];
     __shared__ __align__(8) uint64_t drain_bar;
@@ -397,13 +407,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     const uint32_t total_tiles = p.tiles_m * p.tiles_n;   // 256x256 tiles
 
     if (threadIdx.x == 0) {
-        for (uint32_t s = 0; s < kPStages; ++s) {
+        for (uint32_t s = 0; s < kNStages; ++s) {
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], 1);
         }
         for (uint32_t a = 0; a < 2; ++a) {
             mbar_init(&tmem_full_bar[a], 1);
-            mbar_init(&tmem_empty_bar[a], 2 * kPEpiWarps);
+            mbar_init(&tmem_empty_bar[a], 2 * kNEpiWarps);
         }
         mbar_init(&drain_bar, 1);
         abort_flag = 0;
@@ -430,8 +440,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                 uint32_t mb, nb;
                 tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, mb, nb);
                 for (uint32_t kb = 0; kb < p.num_kb; ++kb, ++it) {
-                    const uint32_t s = it % kPStages;
-                    const uint32_t ph = (it / kPStages) & 1u;
+                    const uint32_t s = it % kNStages;
+                    const uint32_t ph = (it / kNStages) & 1u;
                     if (!mbar_wait(&empty_bar[s], ph ^ 1u, p.limit_ns, p.err, &abort_flag)) {
                         ok = false;
                         break;
@@ -450,9 +460,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             // The leader never leaves with copies in flight (its full barriers
             // count the peer's bytes too).
             if (rank == 0) {
-                const uint32_t tail = it < kPStages ? it : kPStages;
+                const uint32_t tail = it < kNStages ? it : kNStages;
                 for (uint32_t i = it - tail; i < it; ++i)
-                    mbar_wait(&full_bar[i % kPStages], (i / kPStages) & 1u, p.limit_ns, p.err,
+                    mbar_wait(&full_bar[i % kNStages], (i / kNStages) & 1u, p.limit_ns, p.err,
                               nullptr);
             }
         }
@@ -471,8 +481,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * kPTileN;
                 for (uint32_t kb = 0; kb < p.num_kb; ++kb, ++it) {
-                    const uint32_t s = it % kPStages;
-                    const uint32_t ph = (it / kPStages) & 1u;
+                    const uint32_t s = it % kNStages;
+                    const uint32_t ph = (it / kNStages) & 1u;
                     if (!mbar_wait(&full_bar[s], ph, p.limit_ns, p.err, &abort_flag)) {
                         ok = false;
                         break;
@@ -495,19 +505,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         }
     } else {
         // ------------------------------------------------------------ epilogue (both CTAs)
-        // Warp w reads TMEM lanes 32*(w%4)..+31; warps 2-5 take columns
-        // 0-127 of the tile, warps 6-9 columns 128-255.  Each 32x32 chunk is
-        // dequantised in registers, written 128B-swizzled into this warp's
-        // 4 KiB staging buffer and stored to C by TMA (rows >= M and columns
-        // >= N are clipped by the tensor map); without a C tensor map the
-        // rows are stored directly.
+        // Warp w reads TMEM lanes 32*(w%4)..+31 and takes the 64 columns
+        // ((w-2)/4)*64 .. +63 of the tile (warps 2-5 columns 0-63, 6-9 64-127,
+        // ...).  Each 32x32 chunk is dequantised in registers, written
+        // 128B-swizzled into this warp's 4 KiB staging buffer and stored to C
+        // by TMA (rows >= M and columns >= N are clipped by the tensor map);
+        // without a C tensor map the rows are stored directly.
         const uint32_t lane_base = (warp & 3u) * 32u;
-        const uint32_t col_base = ((warp - 2u) >> 2) * 128u;
+        const uint32_t col_base = ((warp - 2u) >> 2) * kNColsPerWarp;
         const uint32_t row = rank * 128u + lane_base + lane;
         const bool vec_ok = (p.ldc % 4u == 0u) &&
                             ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0u);
-        uint8_t *stage_base = ring + kPStages * kPStageBytes + (warp - 2u) * 2u * kPStageOutBytes;
-        uint32_t sbuf = 0;   // staging buffer of the next chunk
+        uint8_t *stage_out = ring + kNStages * kPStageBytes + (warp - 2u) * kPStageOutBytes;
+        float *my_row = reinterpret_cast<float *>(stage_out + lane * 128u);
         const uint32_t leader_empty0 = mapa_shared(smem_addr(&tmem_empty_bar[0]), 0);
         const uint32_t leader_empty1 = mapa_shared(smem_addr(&tmem_empty_bar[1]), 0);
         uint32_t tcount = 0;
@@ -521,9 +531,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             const uint32_t m = m_first + lane;
             const bool row_ok = m < p.M;
             const float sa = row_ok ? (p.scale_a ? __ldg(p.scale_a + m) : 1.0f) : 0.0f;
-            float sreg[4], breg[4];
+            float sreg[kNColsPerWarp / 32u], breg[kNColsPerWarp / 32u];
 #pragma unroll
-            for (uint32_t c = 0; c < 4u; ++c)
+            for (uint32_t c = 0; c < kNColsPerWarp / 32u; ++c)
                 fetch_col(p, nb * kPTileN + col_base + c * 32u + lane, sreg[c], breg[c]);
             uint32_t ok = 0;
             if (lane == 0)
@@ -533,7 +543,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             tc_fence_after();
             float *crow = p.C + static_cast<uint64_t>(row_ok ? m : 0) * p.ldc;
 #pragma unroll
-            for (uint32_t c = 0; c < 4u; ++c) {
+            for (uint32_t c = 0; c < kNColsPerWarp / 32u; ++c) {
                 uint32_t r[32];
                 const uint32_t col = col_base + c * 32u;
                 __syncwarp();
@@ -544,12 +554,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                 float v[32];
                 dequant32_shfl_any(p.variant, r, v, sa, sreg[c], breg[c]);
                 if (p.tma_store) {
-                    // The store two chunks back used this buffer: it must have read it.
-                    if (lane == 0) bulk_wait_read1();
+                    if (lane == 0) bulk_wait_read0();  // previous store has read the buffer
                     __syncwarp();
-                    uint8_t *stage_out = stage_base + sbuf * kPStageOutBytes;
-                    float *my_row = reinterpret_cast<float *>(stage_out + lane * 128u);
-                    sbuf ^= 1u;
 #pragma unroll
                     for (uint32_t j = 0; j < 8u; ++j)
                         *reinterpret_cast<float4 *>(my_row + 4u * (j ^ (lane & 7u))) =
@@ -1360,19 +1366,29 @@ cudaError_t device_setup(int &max_pairs, int &max_wide_pairs) {
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(kSmemBytes))) != cudaSuccess)
             return e;
-        if ((e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel,
+        if ((e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<8, 6>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(kPSmemBytes))) != cudaSuccess)
+                                      static_cast<int>(pair_smem_bytes(8, 6)))) != cudaSuccess ||
+            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<16, 5>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(pair_smem_bytes(16, 5)))) != cudaSuccess)
             return e;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2, 1, 1);
-        cfg.blockDim = dim3(kPThreads, 1, 1);
-        cfg.dynamicSmemBytes = kPSmemBytes;
+        cfg.blockDim = dim3(pair_threads(8), 1, 1);
+        cfg.dynamicSmemBytes = pair_smem_bytes(8, 6);
         int clusters = 0;
-        if ((e = cudaOccupancyMaxActiveClusters(&clusters, gemm_i8_tcgen05_pair_kernel, &cfg)) !=
-            cudaSuccess)
+        if ((e = cudaOccupancyMaxActiveClusters(&clusters, gemm_i8_tcgen05_pair_kernel<8, 6>,
+                                                &cfg)) != cudaSuccess)
             return e;
         d.max_pairs = clusters;
+        cfg.blockDim = dim3(pair_threads(16), 1, 1);
+        cfg.dynamicSmemBytes = pair_smem_bytes(16, 5);
+        if ((e = cudaOccupancyMaxActiveClusters(&clusters, gemm_i8_tcgen05_pair_kernel<16, 5>,
+                                                &cfg)) != cudaSuccess)
+            return e;
+        if (clusters < d.max_pairs) d.max_pairs = clusters;
+        cfg.blockDim = dim3(kPThreads, 1, 1);
         if ((e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_wide_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(kWSmemBytes))) != cudaSuccess)
@@ -1467,9 +1483,12 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         if (wide)
             gemm_i8_tcgen05_pair_wide_kernel<<<2 * pairs, kPThreads, kWSmemBytes, ctx.stream>>>(
                 tmap_a, *p.tmap_b128, tmap_c, tp);
+        else if (p.epilogue >= 2)   // SiLU, GELU: latency-bound epilogue, 16 warps
+            gemm_i8_tcgen05_pair_kernel<16, 5><<<2 * pairs, pair_threads(16), pair_smem_bytes(16, 5),
+                                                 ctx.stream>>>(tmap_a, *p.tmap_b128, tmap_c, tp);
         else
-            gemm_i8_tcgen05_pair_kernel<<<2 * pairs, kPThreads, kPSmemBytes, ctx.stream>>>(
-                tmap_a, *p.tmap_b128, tmap_c, tp);
+            gemm_i8_tcgen05_pair_kernel<8, 6><<<2 * pairs, pair_threads(8), pair_smem_bytes(8, 6),
+                                               ctx.stream>>>(tmap_a, *p.tmap_b128, tmap_c, tp);
         g_last_kernel.store(wide ? "gemm_i8_tcgen05_pair_wide_kernel" : "gemm_i8_tcgen05_pair_kernel",
                             std::memory_order_relaxed);
         count_launch(ctx);
