@@ -543,23 +543,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
             tc_fence_after();
             float *crow = p.C + static_cast<uint64_t>(row_ok ? m : 0) * p.ldc;
 #pragma unroll
-            for (uint32_t c = 0; c < kNColsPerWarp / 32u; ++c) {
-                uint32_t r[32];
+            // All of the warp's accumulator columns in one round of tensor-memory
+            // loads (one wait instead of one per chunk); the accumulator is
+            // released before any of it is dequantised or stored.
+            constexpr uint32_t kChunks = kNColsPerWarp / 32u;
+            uint32_t rr[kChunks][32];
+            __syncwarp();
+#pragma unroll
+            for (uint32_t c = 0; c < kChunks; ++c)
+                tmem_ld_32cols(tmem_base + (lane_base << 16) + acc * kPTileN + col_base + c * 32u,
+                               rr[c]);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc ? leader_empty1 : leader_empty0);
+#pragma unroll
+            for (uint32_t c = 0; c < kChunks; ++c) {
                 const uint32_t col = col_base + c * 32u;
-                __syncwarp();
-                tmem_ld_32cols(tmem_base + (lane_base << 16) + acc * kPTileN + col, r);
-                tmem_wait_ld();
                 const uint32_t n0 = nb * kPTileN + col;
                 if (n0 >= p.N || m_first >= p.M) continue;  // warp-uniform
-                float v[32];
-                dequant32_shfl_any(p.variant, r, v, sa, sreg[c], breg[c]);
+                dequant32_shfl_inplace_any(p.variant, rr[c], sa, sreg[c], breg[c]);
+                const float(&v)[32] = reinterpret_cast<const float(&)[32]>(rr[c]);
                 if (p.tma_store) {
                     if (lane == 0) bulk_wait_read0();  // previous store has read the buffer
                     __syncwarp();
 #pragma unroll
                     for (uint32_t j = 0; j < 8u; ++j)
-                        *reinterpret_cast<float4 *>(my_row + 4u * (j ^ (lane & 7u))) =
-                            make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                        *reinterpret_cast<uint4 *>(my_row + 4u * (j ^ (lane & 7u))) =
+                            make_uint4(rr[c][4 * j], rr[c][4 * j + 1], rr[c][4 * j + 2],
+                                       rr[c][4 * j + 3]);
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) {
@@ -571,9 +583,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
                     store_row32(v, crow, n0, p.N, vec_ok);
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(acc ? leader_empty1 : leader_empty0);
         }
         // Shared memory must outlive the stores' reads; their global writes
         // complete with the grid like any other store.
