@@ -717,6 +717,43 @@ __device__ __forceinline__ float fma_if_nonzero(float v, float p, float a) {
     return a;
 }
 
+// The in-order value chain of one dim: acc = acc*alpha_b per active block,
+// then acc = fma(V[j][d], p_j, acc) over its keys (p_j == 0 skipped).  With
+// kSlice > 0 the V row stride is a compile-time constant and 16 keys' loads
+// are issued ahead of their FMAs.
+template <uint32_t kSlice>
+__device__ __forceinline__ float value_chain(const float *Vs, const float *S, const float *alpha_b,
+                                             const int *active_b, uint32_t nblk, uint32_t L,
+                                             uint32_t d, uint32_t dslice = kSlice) {
+    const uint32_t stride = kSlice ? kSlice : dslice;
+    float a = 0.0f;
+    for (uint32_t b = 0; b < nblk; ++b) {
+        if (!active_b[b]) continue;
+        a = __fmul_rn(a, alpha_b[b]);
+        const uint32_t k0 = b * kAttBK, kc = min(kAttBK, L - k0);
+        const float *vcol = Vs + static_cast<size_t>(k0) * stride + d;
+        const float *prow = S + k0;
+        uint32_t j = 0;
+        for (; j + 16 <= kc; j += 16) {
+            float pv[16], vv[16];
+#pragma unroll
+            for (uint32_t u = 0; u < 16; u += 4) {
+                const float4 p4 = *reinterpret_cast<const float4 *>(prow + j + u);
+                pv[u] = p4.x;
+                pv[u + 1] = p4.y;
+                pv[u + 2] = p4.z;
+                pv[u + 3] = p4.w;
+            }
+#pragma unroll
+            for (uint32_t u = 0; u < 16; ++u) vv[u] = vcol[(j + u) * stride];
+#pragma unroll
+            for (uint32_t u = 0; u < 16; ++u) a = fma_if_nonzero(vv[u], pv[u], a);
+        }
+        for (; j < kc; ++j) a = fma_if_nonzero(vcol[j * stride], prow[j], a);
+    }
+    return a;
+}
+
 constexpr uint32_t kDcCluster = 4;
 constexpr uint32_t kDcThreads = 256;
 constexpr size_t kDcMaxSmem = 200 * 1024;
@@ -886,26 +923,8 @@ __global__ void __cluster_dims__(kDcCluster, 1, 1) __launch_bounds__(kDcThreads)
     if (tid < dslice) {
         const float l = *l_sh;
         const float inv = l > 0.0f ? __fdiv_rn(1.0f, l) : 0.0f;
-        float a = 0.0f;
-        for (uint32_t b = 0; b < nblk; ++b) {
-            if (!active_b[b]) continue;
-            a = __fmul_rn(a, alpha_b[b]);
-            const uint32_t k0 = b * kAttBK, kc = min(kAttBK, L - k0);
-            const float *vcol = Vs + static_cast<size_t>(k0) * dslice + tid;
-            const float *prow = S + k0;
-            uint32_t j = 0;
-            for (; j + 8 <= kc; j += 8) {
-                float pv[8], vv[8];
-#pragma unroll
-                for (uint32_t u = 0; u < 8; ++u) {
-                    pv[u] = prow[j + u];
-                    vv[u] = vcol[(j + u) * dslice];
-                }
-#pragma unroll
-                for (uint32_t u = 0; u < 8; ++u) a = fma_if_nonzero(vv[u], pv[u], a);
-            }
-            for (; j < kc; ++j) a = fma_if_nonzero(vcol[j * dslice], prow[j], a);
-        }
+        const float a = dslice == 32 ? value_chain<32>(Vs, S, alpha_b, active_b, nblk, L, tid)
+                                     : value_chain<0>(Vs, S, alpha_b, active_b, nblk, L, tid, dslice);
         p.O[static_cast<uint64_t>(bh) * D + d0 + tid] = __fmul_rn(a, inv);
     }
 }
