@@ -577,6 +577,221 @@ __global__ void __launch_bounds__(kAttThreads) attention_kernel(const AttParams 
     }
 }
 
+// a = fma(v, p, a) when p != 0, else a unchanged (the reference skips zero
+// probabilities); a predicated FMA keeps the test off the dependency chain.
+__device__ __forceinline__ float fma_if_nonzero(float v, float p, float a) {
+    asm("{\n\t.reg .pred q;\n\tsetp.ne.f32 q, %2, 0f00000000;\n\t@q fma.rn.f32 %0, %1, %2, %0;\n\t}"
+        : "+f"(a)
+        : "f"(v), "f"(p));
+    return a;
+}
+
+// Prefill attention for head_dim 128, register-tiled, same arithmetic again.
+// One CTA (8 warps) per (batch*head, 16 queries); keys in blocks of 64.
+//   scores : warp w owns queries 2w, 2w+1; lane l keys 2l, 2l+1 of the block:
+//            each thread keeps the eight AVX2 chains of its 2 x 2 (query,
+//            key) pairs in registers (Q and K rows from padded shared
+//            memory), combines them in hsum256 order, *scale (+mask),
+//            causal keys -inf;
+//   softmax: the same warp, per query: block max, skip if not finite,
+//            fast_expf, in-order sum through shuffles, l = l*alpha + sum;
+//   values : the same warp, lane l dims 4l..4l+3 of both queries:
+//            acc = acc*alpha, then fma(V[j][d], p_j, acc) in key order with
+//            p == 0 skipped.
+// Only the K/V reload of the next block needs the whole CTA in step.
+constexpr uint32_t kApThreads = 256;
+constexpr uint32_t kApD = 128;
+constexpr uint32_t kApRow = kApD + 4;     // padded row: 8 rows in distinct bank groups
+
+__device__ __forceinline__ float hsum256_chains(const float (&c)[8]) {
+    return __fadd_rn(__fadd_rn(__fadd_rn(c[0], c[4]), __fadd_rn(c[1], c[5])),
+                     __fadd_rn(__fadd_rn(c[2], c[6]), __fadd_rn(c[3], c[7])));
+}
+
+__global__ void __launch_bounds__(kApThreads, 2) attention_prefill_kernel(const AttParams p) {
+    extern __shared__ __align__(16) float ap_smem[];
+    float *Qs = ap_smem;                       // [16][kApRow]
+    float *Ks = Qs + kAttBQ * kApRow;          // [64][kApRow]
+    float *Vs = Ks + kAttBK * kApRow;          // [64][128]
+    float *S = Vs + kAttBK * kApD;             // [16][64] scores, then probabilities
+
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t bh = blockIdx.y;
+    const uint32_t q0 = blockIdx.x * kAttBQ;
+    const uint32_t qc = min(kAttBQ, p.seq_q - q0);
+    const uint64_t head_q = static_cast<uint64_t>(bh) * p.seq_q * kApD;
+    const uint64_t head_k = static_cast<uint64_t>(bh) * p.seq_k * kApD;
+    const float *Kh = p.K + head_k;
+    const float *Vh = p.V + head_k;
+    const float *Mh = p.mask ? p.mask + static_cast<uint64_t>(bh) * p.seq_q * p.seq_k : nullptr;
+    const uint32_t causal_offset = p.seq_k > p.seq_q ? p.seq_k - p.seq_q : 0;
+    const float ninf = -__int_as_float(0x7f800000);
+
+    for (uint32_t i = tid; i < kAttBQ * kApD / 4; i += kApThreads) {
+        const uint32_t q = i / (kApD / 4), c4 = i % (kApD / 4);
+        const float4 v = q < qc ? __ldg(reinterpret_cast<const float4 *>(p.Q + head_q +
+                                                                          static_cast<uint64_t>(q0 + q) * kApD) + c4)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4 *>(Qs + q * kApRow + 4 * c4) = v;
+    }
+
+    // Per-query state of the two queries this warp owns (lane-uniform).
+    const uint32_t qa = 2 * warp, qb = 2 * warp + 1;
+    float m_run[2] = {ninf, ninf}, l_run[2] = {0.0f, 0.0f};
+    float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+
+    uint32_t k_end = p.seq_k;
+    if (p.causal) k_end = min(p.seq_k, q0 + qc - 1 + causal_offset + 1);
+
+    for (uint32_t k0 = 0; k0 < k_end; k0 += kAttBK) {
+        const uint32_t kc = min(kAttBK, p.seq_k - k0);
+        __syncthreads();  // the previous block's K and V are no longer read
+        for (uint32_t i = tid; i < kAttBK * kApD / 4; i += kApThreads) {
+            const uint32_t j = i / (kApD / 4), c4 = i % (kApD / 4);
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (j < kc) {
+                kv = __ldg(reinterpret_cast<const float4 *>(Kh + static_cast<uint64_t>(k0 + j) * kApD) + c4);
+                vv = __ldg(reinterpret_cast<const float4 *>(Vh + static_cast<uint64_t>(k0 + j) * kApD) + c4);
+            }
+            *reinterpret_cast<float4 *>(Ks + j * kApRow + 4 * c4) = kv;
+            *reinterpret_cast<float4 *>(Vs + j * kApD + 4 * c4) = vv;
+        }
+        __syncthreads();  // K, V (and Q on the first block) in shared memory
+
+        // ---- scores of queries qa, qb x keys 2*lane, 2*lane+1
+        {
+            float c[4][8];
+#pragma unroll
+            for (uint32_t x = 0; x < 4; ++x)
+#pragma unroll
+                for (uint32_t y = 0; y < 8; ++y) c[x][y] = 0.0f;
+            const float *qra = Qs + qa * kApRow, *qrb = Qs + qb * kApRow;
+            const float *kra = Ks + lane * kApRow, *krb = Ks + (lane + 32) * kApRow;
+#pragma unroll 4
+            for (uint32_t t = 0; t < kApD / 8; ++t) {
+                const float4 a0 = *reinterpret_cast<const float4 *>(qra + 8 * t);
+                const float4 a1 = *reinterpret_cast<const float4 *>(qra + 8 * t + 4);
+                const float4 b0 = *reinterpret_cast<const float4 *>(qrb + 8 * t);
+                const float4 b1 = *reinterpret_cast<const float4 *>(qrb + 8 * t + 4);
+                const float4 x0 = *reinterpret_cast<const float4 *>(kra + 8 * t);
+                const float4 x1 = *reinterpret_cast<const float4 *>(kra + 8 * t + 4);
+                const float4 y0 = *reinterpret_cast<const float4 *>(krb + 8 * t);
+                const float4 y1 = *reinterpret_cast<const float4 *>(krb + 8 * t + 4);
+#define VNPU_AP_CHAINS(ACC, Q0, Q1, K0, K1)                 \
+    ACC[0] = __fmaf_rn(Q0.x, K0.x, ACC[0]);                 \
+    ACC[1] = __fmaf_rn(Q0.y, K0.y, ACC[1]);                 \
+    ACC[2] = __fmaf_rn(Q0.z, K0.z, ACC[2]);                 \
+    ACC[3] = __fmaf_rn(Q0.w, K0.w, ACC[3]);                 \
+    ACC[4] = __fmaf_rn(Q1.x, K1.x, ACC[4]);                 \
+    ACC[5] = __fmaf_rn(Q1.y, K1.y, ACC[5]);                 \
+    ACC[6] = __fmaf_rn(Q1.z, K1.z, ACC[6]);                 \
+    ACC[7] = __fmaf_rn(Q1.w, K1.w, ACC[7]);
+                VNPU_AP_CHAINS(c[0], a0, a1, x0, x1)
+                VNPU_AP_CHAINS(c[1], a0, a1, y0, y1)
+                VNPU_AP_CHAINS(c[2], b0, b1, x0, x1)
+                VNPU_AP_CHAINS(c[3], b0, b1, y0, y1)
+#undef VNPU_AP_CHAINS
+            }
+#pragma unroll
+            for (uint32_t x = 0; x < 4; ++x) {
+                const uint32_t q = x < 2 ? qa : qb;
+                const uint32_t j = lane + 32u * (x & 1u);
+                const uint32_t qi = q0 + q, ki = k0 + j;
+                float sc;
+                if (j >= kc || (p.causal && ki > qi + causal_offset)) {
+                    sc = ninf;
+                } else {
+                    sc = __fmul_rn(hsum256_chains(c[x]), p.scale);
+                    if (Mh && q < qc) sc = __fadd_rn(sc, Mh[static_cast<uint64_t>(qi) * p.seq_k + ki]);
+                }
+                S[q * kAttBK + j] = sc;
+            }
+        }
+        __syncwarp();
+
+        // ---- online softmax of the warp's two queries
+        bool active[2] = {false, false};
+        float alpha[2] = {1.0f, 1.0f};
+#pragma unroll
+        for (uint32_t h = 0; h < 2; ++h) {
+            const uint32_t q = qa + h;
+            if (q >= qc) break;
+            float *srow = S + q * kAttBK;
+            const float s_lo = lane < kc ? srow[lane] : ninf;
+            const float s_hi = lane + 32 < kc ? srow[lane + 32] : ninf;
+            float bmax = fmaxf(s_lo, s_hi);
+            for (int o = 16; o > 0; o >>= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
+            if (!isfinite(bmax)) continue;   // fully masked block: skipped, as in the reference
+            const float nm = fmaxf(m_run[h], bmax);
+            const float p_lo = lane < kc ? ref_fast_expf(__fsub_rn(s_lo, nm), false) : 0.0f;
+            const float p_hi = lane + 32 < kc ? ref_fast_expf(__fsub_rn(s_hi, nm), false) : 0.0f;
+            alpha[h] = ref_fast_expf(__fsub_rn(m_run[h], nm), false);
+            float sum_p = 0.0f;
+#pragma unroll
+            for (uint32_t j = 0; j < 32; ++j) {
+                const float v = __shfl_sync(0xffffffffu, p_lo, j);
+                if (j < kc) sum_p = __fadd_rn(sum_p, v);
+            }
+#pragma unroll
+            for (uint32_t j = 0; j < 32; ++j) {
+                const float v = __shfl_sync(0xffffffffu, p_hi, j);
+                if (j + 32 < kc) sum_p = __fadd_rn(sum_p, v);
+            }
+            l_run[h] = __fadd_rn(__fmul_rn(l_run[h], alpha[h]), sum_p);
+            m_run[h] = nm;
+            srow[lane] = p_lo;            // probabilities (0 past kc)
+            srow[lane + 32] = p_hi;
+            active[h] = true;
+        }
+        __syncwarp();
+        // ---- values of both queries in one pass over V (each query's keys in order)
+#pragma unroll
+        for (uint32_t h = 0; h < 2; ++h)
+            if (active[h]) {
+                acc[h].x = __fmul_rn(acc[h].x, alpha[h]);
+                acc[h].y = __fmul_rn(acc[h].y, alpha[h]);
+                acc[h].z = __fmul_rn(acc[h].z, alpha[h]);
+                acc[h].w = __fmul_rn(acc[h].w, alpha[h]);
+            }
+        if (active[0] || active[1]) {
+            // an inactive query's row is all zero probabilities: no FMA happens
+            const float *pra = S + qa * kAttBK, *prb = S + qb * kAttBK;
+            const float *vcol = Vs + 4 * lane;
+            const bool use_a = active[0], use_b = active[1];
+            for (uint32_t j = 0; j < kc; j += 4) {
+                const float4 pa4 = use_a ? *reinterpret_cast<const float4 *>(pra + j)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 pb4 = use_b ? *reinterpret_cast<const float4 *>(prb + j)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float pa[4] = {pa4.x, pa4.y, pa4.z, pa4.w};
+                const float pb[4] = {pb4.x, pb4.y, pb4.z, pb4.w};
+#pragma unroll
+                for (uint32_t u = 0; u < 4; ++u) {
+                    const float4 v = *reinterpret_cast<const float4 *>(vcol + (j + u) * kApD);
+                    acc[0].x = fma_if_nonzero(v.x, pa[u], acc[0].x);
+                    acc[0].y = fma_if_nonzero(v.y, pa[u], acc[0].y);
+                    acc[0].z = fma_if_nonzero(v.z, pa[u], acc[0].z);
+                    acc[0].w = fma_if_nonzero(v.w, pa[u], acc[0].w);
+                    acc[1].x = fma_if_nonzero(v.x, pb[u], acc[1].x);
+                    acc[1].y = fma_if_nonzero(v.y, pb[u], acc[1].y);
+                    acc[1].z = fma_if_nonzero(v.z, pb[u], acc[1].z);
+                    acc[1].w = fma_if_nonzero(v.w, pb[u], acc[1].w);
+                }
+            }
+        }
+        __syncwarp();
+    }
+#pragma unroll
+    for (uint32_t h = 0; h < 2; ++h) {
+        const uint32_t q = qa + h;
+        if (q >= qc) break;
+        const float inv = l_run[h] > 0.0f ? __fdiv_rn(1.0f, l_run[h]) : 0.0f;
+        reinterpret_cast<float4 *>(p.O + head_q + static_cast<uint64_t>(q0 + q) * kApD)[lane] =
+            make_float4(__fmul_rn(acc[h].x, inv), __fmul_rn(acc[h].y, inv), __fmul_rn(acc[h].z, inv),
+                        __fmul_rn(acc[h].w, inv));
+    }
+}
+
 // Decode attention (one query per head): the same arithmetic as
 // attention_kernel, reorganised for latency.  One CTA per (batch, head):
 //   A. every score of the row at once: thread (key, chain) runs its 16-step
@@ -708,15 +923,6 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode_kernel(const Att
 //   C. thread = dim of the slice: acc = acc*alpha_b, fma(V[j][d], p_j, acc)
 //      over the keys in order, from shared memory.
 // Requires D % 16 == 0 and 16-byte aligned V (the caller checks).
-// a = fma(v, p, a) when p != 0, else a unchanged (the reference skips zero
-// probabilities); a predicated FMA keeps the test off the dependency chain.
-__device__ __forceinline__ float fma_if_nonzero(float v, float p, float a) {
-    asm("{\n\t.reg .pred q;\n\tsetp.ne.f32 q, %2, 0f00000000;\n\t@q fma.rn.f32 %0, %1, %2, %0;\n\t}"
-        : "+f"(a)
-        : "f"(v), "f"(p));
-    return a;
-}
-
 // The in-order value chain of one dim: acc = acc*alpha_b per active block,
 // then acc = fma(V[j][d], p_j, acc) over its keys (p_j == 0 skipped).  With
 // kSlice > 0 the V row stride is a compile-time constant and 16 keys' loads
@@ -1190,6 +1396,24 @@ cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, cons
         return cudaGetLastError();
     }
     dim3 grid((seq_q + kAttBQ - 1) / kAttBQ, batch * heads);
+    const bool aligned_all = ((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) |
+                               reinterpret_cast<uintptr_t>(V) | reinterpret_cast<uintptr_t>(O)) &
+                              15u) == 0;
+    if (head_dim == kApD && aligned_all && !(attn_env && !std::strcmp(attn_env, "general"))) {
+        const size_t ap_smem =
+            sizeof(float) * (kAttBQ * kApRow + kAttBK * kApRow + kAttBK * kApD + kAttBQ * kAttBK);
+        static bool ap_configured[64] = {};
+        if (dev >= 0 && dev < 64 && !ap_configured[dev]) {
+            const cudaError_t e = cudaFuncSetAttribute(
+                attention_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                static_cast<int>(ap_smem));
+            if (e != cudaSuccess) return e;
+            ap_configured[dev] = true;
+        }
+        attention_prefill_kernel<<<grid, kApThreads, ap_smem, ctx.stream>>>(ap);
+        count_launch(ctx);
+        return cudaGetLastError();
+    }
     if (vec)
         attention_kernel<true><<<grid, kAttThreads, smem, ctx.stream>>>(ap);
     else
