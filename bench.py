@@ -235,6 +235,13 @@ def cmd_matmul(A, w, sa, bias, Cp, M, K, N, epi=0, ldc=0):
     return c
 
 
+def _copy_cmd(dst, src, nbytes):
+    c = vnpu.Command()
+    c.opcode = vnpu.OP_COPY
+    c.args.copy = vnpu.CopyArgs(dst, src, nbytes, 0)
+    return c
+
+
 def submit(lib, dev, cmds):
     arr = (vnpu.Command * len(cmds))(*cmds)
     rc = lib.stream_submit(dev.stream, arr, len(cmds), None)
@@ -545,7 +552,70 @@ def run_b200(args):
         allgather = {"ms": ms_ag, "bytes_received_per_rank": recv,
                      "gbs_per_rank": recv / ms_ag / 1e6, "layout": "shard-major [P][M][N/P]",
                      "ms_step_plus_gather": ms_step + ms_ag}
-        del gathered, shard_pad
+        # ---- the same gather fused into the GEMM: MATMUL_I8_SCATTER writes the
+        # rank's shard into every rank's full [M][N] output (CUDA IPC, NVLink
+        # stores from the epilogue); a one-element NCCL all-reduce is the
+        # barrier after which every full output is complete.
+        buf = vnpu.vp()
+        lib.check(lib.buffer_alloc(dev.dev, M * N_TOTAL * 4, vnpu.C.byref(buf)), "buffer_alloc")
+        full = lib.buffer_host_ptr(buf)
+        handles = [None] * world
+        dist.all_gather_object(handles, dev.ipc_handle(full))
+        peers = [full if r == rank else dev.ipc_open(handles[r], local) for r in range(world)]
+        flag = torch.zeros(1, device="cuda")
+        sc_args = vnpu.MatmulI8ScatterArgs(
+            A8.data_ptr(), w, sa.data_ptr(), None,
+            (vnpu.vp * vnpu.B200_SCATTER_MAX)(*(peers + [None] * (vnpu.B200_SCATTER_MAX - world))),
+            M, K, n, 0, N_TOTAL, n0, world, 0)
+        sc_arr = (vnpu.Command * 1)(vnpu.b200_command(vnpu.OP_B200_MATMUL_I8_SCATTER, sc_args))
+
+        def fused_step():
+            if lib.stream_submit(dev.stream, sc_arr, 1, None) != vnpu.OK:
+                raise RuntimeError("submit failed")
+            with torch.cuda.stream(st.cs):
+                dist.all_reduce(flag)
+
+        for _ in range(max(args.warmup, 1)):
+            fused_step()
+        dev.sync()
+        torch.cuda.synchronize()
+        # the fused result equals the NCCL-gathered one (shard-major -> row-major),
+        # both from the activations now in A8
+        lib.check(dev.submit([cmd_matmul(A8.data_ptr(), w, sa.data_ptr(), None, Cm.data_ptr(),
+                                         M, K, n)]), "submit")
+        lib.check(dev.sync(), "matmul")
+        shard_pad[:, :n] = Cm
+        gathered = torch.empty((world, M, width), device="cuda")
+        dist.all_gather_into_tensor(gathered, shard_pad)
+        full_t = torch.empty((M, N_TOTAL), device="cuda")
+        lib.check(dev.submit([_copy_cmd(full_t.data_ptr(), full, M * N_TOTAL * 4)]), "copy")
+        lib.check(dev.sync(), "copy")
+        torch.cuda.synchronize()
+        same = True
+        for r in range(world):
+            r0_, r1_ = column_shard(N_TOTAL, world, r)
+            same &= bool(torch.equal(full_t[:, r0_:r1_], gathered[r, :, :r1_ - r0_]))
+        del gathered, full_t
+        barrier()
+        f0 = st.event()
+        for _ in range(reps):
+            fused_step()
+        f1 = st.event()
+        dev.sync()
+        f1.synchronize()
+        ms_fused = max_over_ranks(f0.elapsed_time(f1) / reps)
+        allgather["fused"] = {
+            "ms_gemm_plus_gather": ms_fused, "ms_separate": ms_gemm + ms_ag,
+            "speedup_vs_separate": (ms_gemm + ms_ag) / ms_fused, "bit_identical_to_nccl": same,
+            "path": "VNPU_B200_OP_MATMUL_I8_SCATTER into every rank's full output over CUDA IPC, "
+                    "then a one-element NCCL all-reduce as the barrier"}
+        barrier()
+        for r in range(world):
+            if r != rank:
+                lib.b200_ipc_close(peers[r])
+        barrier()
+        lib.buffer_free(buf)
+        del shard_pad
 
     out = None
     if rank == 0:

@@ -106,6 +106,52 @@ typedef struct vnpu_b200_kv_append_args_t {
     uint32_t reserved0;
 } vnpu_b200_kv_append_args_t;
 
+/*
+ * Column-sharded MATMUL_I8 fused with the all-gather of its output (no
+ * reference counterpart; the reference's multi-device split is by rows and
+ * F32 only).  The rank's shard C[:, 0:N) is written straight into every
+ * destination's full output at columns col_offset .. col_offset+N-1, tile by
+ * tile from the GEMM epilogue with plain stores (peer destinations over
+ * NVLink), instead of a separate all-gather after the GEMM.
+ *
+ * dst[0..ndst-1] are device memory: this GPU's, or another GPU's mapped with
+ * vnpu_b200_ipc_open (not staged).  Each is a [M][ldd] f32 matrix; ldd,
+ * col_offset and the dst addresses are multiples of 4 floats / 16 bytes.
+ * Other arguments as vnpu_matmul_i8_args_t (A on this GPU, TMA-aligned:
+ * 16-byte aligned A and lda % 16 == 0).  A destination on another GPU is
+ * complete once the writing rank's command has completed: order the readers
+ * after it (a barrier across the ranks).
+ */
+#define VNPU_B200_OP_MATMUL_I8_SCATTER  0x103u
+#define VNPU_B200_SCATTER_MAX  8
+
+typedef struct vnpu_b200_matmul_i8_scatter_args_t {
+    const int8_t *A;
+    vnpu_packed_weights_t *B;
+    const float *scale_a;
+    const float *bias;
+    float *dst[VNPU_B200_SCATTER_MAX];
+    uint32_t M;
+    uint32_t K;
+    uint32_t N;          /* columns of this shard (the packed weights' N) */
+    uint32_t lda;        /* 0 = K */
+    uint32_t ldd;        /* row stride of every destination, floats */
+    uint32_t col_offset; /* first destination column of this shard */
+    uint32_t ndst;       /* 1 .. VNPU_B200_SCATTER_MAX */
+    uint32_t epilogue;
+} vnpu_b200_matmul_i8_scatter_args_t;
+
+/* CUDA IPC between the processes of one node (for scatter destinations):
+ * get_handle exports the cudaMalloc allocation whose base is device_ptr
+ * (vnpu_buffer_alloc memory qualifies) as 64 opaque bytes; open maps such a
+ * handle from another process on `device` (peer access enabled);
+ * close unmaps it. */
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_ipc_get_handle(const void *device_ptr,
+                                                         uint8_t handle[64]);
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_ipc_open(int device, const uint8_t handle[64],
+                                                   void **out_ptr);
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_ipc_close(void *ptr);
+
 /* The cudaStream_t behind a vnpu stream (as void*), so callers can order
  * their own CUDA work and timing events against its kernels.  Copies of host
  * operands run on two further streams of the vnpu stream (uploads, downloads)

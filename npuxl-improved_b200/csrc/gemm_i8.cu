@@ -74,6 +74,12 @@ struct TcParams {
     uint32_t tma_store;    // 1: C written by TMA from shared memory
     uint32_t *err;
     uint64_t limit_ns;
+    // Scatter epilogue (ndst > 0): the tile goes to dst[0..ndst-1], each a
+    // [M][ldd] matrix, at column col_off + n, by plain stores.
+    float *dst[8] = {};
+    uint32_t ndst = 0;
+    uint32_t ldd = 0;
+    uint32_t col_off = 0;
 };
 
 __device__ __forceinline__ void tile_coords(uint32_t t, uint32_t tiles_m, uint32_t tiles_n,
@@ -564,7 +570,44 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
                 if (n0 >= p.N || m_first >= p.M) continue;  // warp-uniform
                 dequant32_shfl_inplace_any(p.variant, rr[c], sa, sreg[c], breg[c]);
                 const float(&v)[32] = reinterpret_cast<const float(&)[32]>(rr[c]);
-                if (p.tma_store) {
+                if (p.ndst) {
+                    // Scatter: the 32x32 chunk is transposed through the staging
+                    // buffer so each store instruction writes four whole 128-byte
+                    // row segments, then goes to every destination (peers over
+                    // NVLink) at column col_off + n.
+                    if (lane == 0) bulk_wait_read0();
+                    __syncwarp();
+#pragma unroll
+                    for (uint32_t j = 0; j < 8u; ++j)
+                        *reinterpret_cast<uint4 *>(my_row + 4u * (j ^ (lane & 7u))) =
+                            make_uint4(rr[c][4 * j], rr[c][4 * j + 1], rr[c][4 * j + 2],
+                                       rr[c][4 * j + 3]);
+                    __syncwarp();
+                    const uint32_t g = lane & 7u;
+                    const uint32_t ncol = n0 + 4u * g;
+#pragma unroll
+                    for (uint32_t i = 0; i < 8u; ++i) {
+                        const uint32_t rrow = 4u * i + (lane >> 3);
+                        const float4 val = *reinterpret_cast<const float4 *>(
+                            stage_out + rrow * 128u + ((g ^ (rrow & 7u)) << 4));
+                        const uint32_t mrow = m_first + rrow;
+                        if (mrow >= p.M || ncol >= p.N) continue;
+                        const uint64_t off = static_cast<uint64_t>(mrow) * p.ldd + p.col_off + ncol;
+#pragma unroll
+                        for (uint32_t d = 0; d < 8u; ++d) {
+                            if (d >= p.ndst) break;
+                            float *o = p.dst[d] + off;
+                            if (ncol + 4u <= p.N) {
+                                *reinterpret_cast<float4 *>(o) = val;
+                            } else {
+                                o[0] = val.x;
+                                if (ncol + 1u < p.N) o[1] = val.y;
+                                if (ncol + 2u < p.N) o[2] = val.z;
+                            }
+                        }
+                    }
+                    __syncwarp();   // the staging buffer is reused by the next chunk
+                } else if (p.tma_store) {
                     if (lane == 0) bulk_wait_read0();  // previous store has read the buffer
                     __syncwarp();
 #pragma unroll
@@ -1431,6 +1474,50 @@ static uint32_t raster_group(uint32_t tiles_m, uint32_t tile_m, uint32_t K) {
     if (g < 1) g = 1;
     if (g > tiles_m) g = tiles_m;
     return static_cast<uint32_t>(g);
+}
+
+cudaError_t matmul_i8_scatter(const LaunchCtx &ctx, const MatmulI8 &p) {
+    int max_pairs = 0, max_wide_pairs = 0;
+    cudaError_t se = device_setup(max_pairs, max_wide_pairs);
+    if (se != cudaSuccess) return se;
+    if (!p.tmap_b128 || max_pairs <= 0) return cudaErrorNotSupported;
+    CUtensorMap tmap_a;
+    if ((reinterpret_cast<uintptr_t>(p.A) % 16u) || (p.lda % 16u) ||
+        !encode_tmap_kmajor_i8(&tmap_a, p.A, p.K, p.M, p.lda, kBK, 128))
+        return cudaErrorNotSupported;
+    TcParams tp;
+    tp.scale_a = p.scale_a;
+    tp.scale_b = p.scale_b;
+    tp.bias = p.bias;
+    tp.C = p.C;
+    tp.ldc = p.ldc;
+    tp.M = p.M;
+    tp.N = p.N;
+    tp.K = p.K;
+    tp.tiles_m = (p.M + kPTileM - 1) / kPTileM;
+    tp.tiles_n = (p.N + kPTileN - 1) / kPTileN;
+    tp.num_kb = (p.K + kBK - 1) / kBK;
+    tp.group_m = raster_group(tp.tiles_m, kPTileM, p.K);
+    tp.epilogue = p.epilogue;
+    tp.form = p.form;
+    tp.variant = epi_variant(p.epilogue, p.bias != nullptr, p.form);
+    tp.tma_store = 0;
+    tp.err = ctx.err;
+    tp.limit_ns = ctx.wait_limit_ns;
+    for (uint32_t d = 0; d < p.ndst && d < 8u; ++d) tp.dst[d] = p.dst[d];
+    tp.ndst = p.ndst;
+    tp.ldd = p.ldd;
+    tp.col_off = p.col_offset;
+    CUtensorMap tmap_c;
+    std::memset(&tmap_c, 0, sizeof(tmap_c));
+    const uint32_t tiles = tp.tiles_m * tp.tiles_n;
+    const uint32_t cap = static_cast<uint32_t>(max_pairs);
+    const uint32_t pairs = tiles < cap ? tiles : cap;
+    gemm_i8_tcgen05_pair_kernel<8, 6><<<2 * pairs, pair_threads(8), pair_smem_bytes(8, 6),
+                                       ctx.stream>>>(tmap_a, *p.tmap_b128, tmap_c, tp);
+    g_last_kernel.store("gemm_i8_tcgen05_pair_kernel", std::memory_order_relaxed);
+    count_launch(ctx);
+    return cudaGetLastError();
 }
 
 cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {

@@ -63,9 +63,18 @@ struct MatmulI8 {
     uint32_t form = 0;              // EpiForm
     const CUtensorMap *tmap_b = nullptr;     // TMA map of Bt (box 128 x 256, SW128)
     const CUtensorMap *tmap_b128 = nullptr;  // same, box 128 x 128 (CTA-pair kernel)
+    // Scatter mode (MATMUL_I8_SCATTER): the shard is written into ndst full
+    // [M][ldd] outputs at column col_offset instead of C.
+    float *dst[8] = {};
+    uint32_t ndst = 0;
+    uint32_t ldd = 0;
+    uint32_t col_offset = 0;
 };
 
 enum class MatmulKernel { kTcgen05, kGemv, kSimt };
+
+// MATMUL_I8 with the scatter epilogue (CTA-pair kernel; TMA-aligned A required).
+cudaError_t matmul_i8_scatter(const LaunchCtx &ctx, const MatmulI8 &p);
 
 // Which kernel a shape goes to (pure function of the arguments).
 MatmulKernel choose_matmul_kernel(uint32_t M, uint32_t K, uint32_t N, uint32_t lda,

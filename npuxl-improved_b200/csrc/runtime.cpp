@@ -307,6 +307,55 @@ void exec_matmul_i8(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags,
     acc.dma = st.staged_bytes();
 }
 
+void exec_matmul_i8_scatter(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags,
+                            const LaunchCtx &ctx, Accounting &acc) {
+    vnpu_b200_matmul_i8_scatter_args_t in;
+    std::memcpy(&in, cmd.args.raw, sizeof(in));
+    vnpu_packed_weights_t *w = in.B;
+    if (!in.A || !w || !in.M || !in.K || !in.N || !in.ndst || in.ndst > VNPU_B200_SCATTER_MAX ||
+        !in.ldd || in.ldd % 4u || in.col_offset % 4u ||
+        static_cast<uint64_t>(in.col_offset) + in.N > in.ldd)
+        throw CommandError("invalid matmul_i8_scatter arguments", VNPU_ERR_INVALID_ARGUMENT);
+    for (uint32_t d = 0; d < in.ndst; ++d)
+        if (!in.dst[d] || reinterpret_cast<uintptr_t>(in.dst[d]) % 16u)
+            throw CommandError("invalid matmul_i8_scatter destination", VNPU_ERR_INVALID_ARGUMENT);
+    if (w->K != in.K || w->N != in.N) throw CommandError("packed weight shape mismatch");
+    if (w->device != s->device) throw CommandError("packed weights belong to another device");
+    const uint32_t lda = in.lda ? in.lda : in.K;
+    if (lda < in.K) throw CommandError("invalid int8 leading dimension");
+    Staging st(s);
+    MatmulI8 p;
+    p.A = st.in(in.A, static_cast<uint64_t>(in.M - 1) * lda + in.K);
+    p.lda = lda;
+    p.Bt = w->bt;
+    p.k_stride = w->k_stride;
+    p.scale_a = st.in(in.scale_a, sizeof(float) * in.M);
+    p.scale_b = w->scales;
+    p.bias = st.in(in.bias, sizeof(float) * in.N);
+    p.C = in.dst[0];
+    p.ldc = in.ldd;
+    p.M = in.M;
+    p.K = in.K;
+    p.N = in.N;
+    p.epilogue = in.epilogue;
+    p.form = epi_form_for(s->device, flags);
+    p.tmap_b = w->tmap_ok ? &w->tmap : nullptr;
+    p.tmap_b128 = w->tmap128_ok ? &w->tmap128 : nullptr;
+    for (uint32_t d = 0; d < in.ndst; ++d) p.dst[d] = in.dst[d];
+    p.ndst = in.ndst;
+    p.ldd = in.ldd;
+    p.col_offset = in.col_offset;
+    const cudaError_t e = matmul_i8_scatter(ctx, p);
+    if (e == cudaErrorNotSupported)
+        throw CommandError("matmul_i8_scatter needs a TMA-aligned A", VNPU_ERR_UNSUPPORTED);
+    cuda_check(e, "matmul_i8_scatter launch");
+    st.finish();
+    acc.bytes_read = static_cast<uint64_t>(in.M) * in.K + static_cast<uint64_t>(in.K) * in.N;
+    acc.bytes_written = static_cast<uint64_t>(in.M) * in.N * sizeof(float) * in.ndst;
+    acc.flops = 2ull * in.M * in.K * in.N;
+    acc.dma = st.staged_bytes();
+}
+
 // src/core/scheduler.cpp:430-473
 void exec_quantize_i8(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &ctx,
                       Accounting &acc) {
@@ -588,7 +637,8 @@ const char *opcode_name(uint32_t op);
 vnpu_status_t execute_command(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags) {
     vnpu_device_t *dev = s->device;
     if (cmd.opcode >= VNPU_OP_COUNT && cmd.opcode != VNPU_B200_OP_RMSNORM_QUANTIZE_I8 &&
-        cmd.opcode != VNPU_B200_OP_SWIGLU_QUANTIZE_I8 && cmd.opcode != VNPU_B200_OP_KV_APPEND)
+        cmd.opcode != VNPU_B200_OP_SWIGLU_QUANTIZE_I8 && cmd.opcode != VNPU_B200_OP_KV_APPEND &&
+        cmd.opcode != VNPU_B200_OP_MATMUL_I8_SCATTER)
         return VNPU_ERR_INVALID_COMMAND;
     dev->last_opcode.store(cmd.opcode);
     const bool tracing = dev->trace.enabled.load();
@@ -628,6 +678,7 @@ vnpu_status_t execute_command(vnpu_stream_t *s, const vnpu_command_t &cmd, uint3
         case VNPU_B200_OP_RMSNORM_QUANTIZE_I8: exec_rmsnorm_quantize(s, cmd, ctx, acc); break;
         case VNPU_B200_OP_SWIGLU_QUANTIZE_I8: exec_swiglu_quantize(s, cmd, ctx, acc); break;
         case VNPU_B200_OP_KV_APPEND: exec_kv_append(s, cmd, ctx, acc); break;
+        case VNPU_B200_OP_MATMUL_I8_SCATTER: exec_matmul_i8_scatter(s, cmd, flags, ctx, acc); break;
         case VNPU_OP_MEMSET: exec_memset(s, cmd, acc); break;
         case VNPU_OP_PACK_WEIGHTS_I8: exec_pack(s, cmd, acc); break;
         default:
@@ -736,6 +787,7 @@ const char *opcode_name(uint32_t op) {
     if (op == VNPU_B200_OP_RMSNORM_QUANTIZE_I8) return "RMSNORM_QUANTIZE_I8";
     if (op == VNPU_B200_OP_SWIGLU_QUANTIZE_I8) return "SWIGLU_QUANTIZE_I8";
     if (op == VNPU_B200_OP_KV_APPEND) return "KV_APPEND";
+    if (op == VNPU_B200_OP_MATMUL_I8_SCATTER) return "MATMUL_I8_SCATTER";
     return op < sizeof(names) / sizeof(names[0]) ? names[op] : "UNKNOWN";
 }
 
@@ -1545,6 +1597,50 @@ VNPU_API const char *VNPU_CALL vnpu_b200_matmul_i8_kernel(uint32_t M, uint32_t K
 }
 
 VNPU_API const char *VNPU_CALL vnpu_b200_last_matmul_kernel(void) { return last_matmul_kernel(); }
+
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_ipc_get_handle(const void *device_ptr,
+                                                         uint8_t handle[64]) {
+    if (!device_ptr || !handle) return VNPU_ERR_INVALID_ARGUMENT;
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, const_cast<void *>(device_ptr)) != cudaSuccess) {
+        cudaGetLastError();
+        return VNPU_ERR_INVALID_ARGUMENT;
+    }
+    std::memcpy(handle, &h, sizeof(h));
+    return VNPU_OK;
+}
+
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_ipc_open(int device, const uint8_t handle[64],
+                                                   void **out_ptr) {
+    if (!handle || !out_ptr) return VNPU_ERR_INVALID_ARGUMENT;
+    *out_ptr = nullptr;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(device) != cudaSuccess) {
+        cudaGetLastError();
+        return VNPU_ERR_INVALID_ARGUMENT;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(out_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        *out_ptr = nullptr;
+        return VNPU_ERR_DEVICE_ERROR;
+    }
+    return VNPU_OK;
+}
+
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_ipc_close(void *ptr) {
+    if (!ptr) return VNPU_ERR_INVALID_ARGUMENT;
+    if (cudaIpcCloseMemHandle(ptr) != cudaSuccess) {
+        cudaGetLastError();
+        return VNPU_ERR_DEVICE_ERROR;
+    }
+    return VNPU_OK;
+}
 
 VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_selftest_wait_timeout(vnpu_stream_t *stream,
                                                                 uint32_t timeout_us) {

@@ -182,6 +182,16 @@ class KvAppendArgs(C.Structure):
                 ("capacity", u32), ("position_offset", u32), ("reserved0", u32)]
 
 
+OP_B200_MATMUL_I8_SCATTER = 0x103
+B200_SCATTER_MAX = 8
+
+
+class MatmulI8ScatterArgs(C.Structure):
+    _fields_ = [("A", vp), ("B", vp), ("scale_a", vp), ("bias", vp),
+                ("dst", vp * B200_SCATTER_MAX), ("M", u32), ("K", u32), ("N", u32), ("lda", u32),
+                ("ldd", u32), ("col_offset", u32), ("ndst", u32), ("epilogue", u32)]
+
+
 def b200_command(opcode: int, args: C.Structure) -> "Command":
     """A command whose arguments are a B200 extension struct (copied into args.raw)."""
     c = Command()
@@ -293,6 +303,11 @@ class Lib:
             self.b200_matmul_kernel = _sig(h, "vnpu_b200_matmul_i8_kernel", C.c_char_p, u32, u32,
                                            u32, u32, vp)
             self.b200_last_matmul_kernel = _sig(h, "vnpu_b200_last_matmul_kernel", C.c_char_p)
+            self.b200_ipc_get_handle = _sig(h, "vnpu_b200_ipc_get_handle", _ST, vp,
+                                            C.POINTER(C.c_uint8))
+            self.b200_ipc_open = _sig(h, "vnpu_b200_ipc_open", _ST, C.c_int,
+                                      C.POINTER(C.c_uint8), C.POINTER(vp))
+            self.b200_ipc_close = _sig(h, "vnpu_b200_ipc_close", _ST, vp)
             self.b200_selftest_wait = _sig(h, "vnpu_b200_selftest_wait_timeout", _ST, vp, u32)
             self.b200_packed_device = _sig(h, "vnpu_b200_packed_weights_device", _ST, vp,
                                            C.POINTER(vp), C.POINTER(u32), C.POINTER(vp))
@@ -392,6 +407,29 @@ class Device:
         if check:
             self.lib.check(rc, "quantize_i8")
         return rc
+
+    def matmul_i8_scatter(self, A, w, scale_a, bias, dsts, M, K, N, ldd, col_offset,
+                          epilogue=EPI_NONE, lda=0, sync=True) -> int:
+        """MATMUL_I8 of a column shard written into every destination in dsts
+        (device pointers, [M][ldd] f32 each) at columns col_offset.."""
+        d = (vp * B200_SCATTER_MAX)(*([ptr(x) for x in dsts] + [None] * (B200_SCATTER_MAX - len(dsts))))
+        a = MatmulI8ScatterArgs(ptr(A), w, ptr(scale_a), ptr(bias), d, M, K, N, lda, ldd,
+                                col_offset, len(dsts), epilogue)
+        rc = self.submit([b200_command(OP_B200_MATMUL_I8_SCATTER, a)])
+        if rc != OK or not sync:
+            return rc
+        return self.sync()
+
+    def ipc_handle(self, device_ptr) -> bytes:
+        h = (C.c_uint8 * 64)()
+        self.lib.check(self.lib.b200_ipc_get_handle(ptr(device_ptr), h), "ipc_get_handle")
+        return bytes(h)
+
+    def ipc_open(self, handle: bytes, device: int) -> int:
+        h = (C.c_uint8 * 64).from_buffer_copy(handle)
+        out = vp()
+        self.lib.check(self.lib.b200_ipc_open(device, h, C.byref(out)), "ipc_open")
+        return out.value
 
     def rmsnorm_quantize(self, X, W, Y, Q, scales, rows, cols, eps) -> None:
         a = RmsnormQuantizeArgs(ptr(X), ptr(W), ptr(Y), ptr(Q), ptr(scales), rows, cols, eps, 0)

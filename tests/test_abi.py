@@ -173,6 +173,8 @@ int main(void) {
            sizeof(vnpu_b200_swiglu_quantize_args_t), sizeof(((vnpu_command_t *)0)->args.raw));
     F(vnpu_b200_rmsnorm_quantize_args_t, Q); F(vnpu_b200_rmsnorm_quantize_args_t, eps);
     F(vnpu_b200_swiglu_quantize_args_t, scales); F(vnpu_b200_swiglu_quantize_args_t, alpha);
+    printf("sc %zu\n", sizeof(vnpu_b200_matmul_i8_scatter_args_t));
+    F(vnpu_b200_matmul_i8_scatter_args_t, dst); F(vnpu_b200_matmul_i8_scatter_args_t, ndst);
     printf("ops %u %u\n", VNPU_B200_OP_RMSNORM_QUANTIZE_I8, VNPU_B200_OP_SWIGLU_QUANTIZE_I8);
     return 0;
 }''')
@@ -187,5 +189,8 @@ int main(void) {
     assert int(out["vnpu_b200_rmsnorm_quantize_args_t.eps"]) == vnpu.RmsnormQuantizeArgs.eps.offset
     assert int(out["vnpu_b200_swiglu_quantize_args_t.scales"]) == vnpu.SwigluQuantizeArgs.scales.offset
     assert int(out["vnpu_b200_swiglu_quantize_args_t.alpha"]) == vnpu.SwigluQuantizeArgs.alpha.offset
+    assert int(out["sc"]) == C.sizeof(vnpu.MatmulI8ScatterArgs) <= int(out["raw"])
+    assert int(out["vnpu_b200_matmul_i8_scatter_args_t.dst"]) == vnpu.MatmulI8ScatterArgs.dst.offset
+    assert int(out["vnpu_b200_matmul_i8_scatter_args_t.ndst"]) == vnpu.MatmulI8ScatterArgs.ndst.offset
     assert out["ops"].split() == [str(vnpu.OP_B200_RMSNORM_QUANTIZE_I8),
                                   str(vnpu.OP_B200_SWIGLU_QUANTIZE_I8)]
