@@ -80,3 +80,63 @@ def test_two_rank_column_shard_gather():
     results = dict(q.get(timeout=5) for _ in range(2))
     assert results == {0: True, 1: True}
     assert all(p.exitcode == 0 for p in procs)
+
+
+def _row_slice_main(rank, world, port, q):
+    """End-to-end input path at N > 1 (bench.py): each rank quantizes its M/N
+    rows of X per row and the int8 rows and scales are all-gathered; every
+    rank then holds the whole matrix's QUANTIZE_I8 result.  Then each rank
+    writes its GEMM column shard into a full output at its column offset (the
+    MATMUL_I8_SCATTER layout); the assembled output equals the whole GEMM."""
+    import torch
+    import torch.distributed as dist
+
+    import vnpu
+    from conftest import ORACLE_LIB
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        orc = vnpu.Oracle(ORACLE_LIB)
+        rng = np.random.default_rng(1)
+        M, K, N = 32, 80, 600
+        X = rng.normal(0, 1, (M, K)).astype(np.float32)
+        X[3, :5] = [2.5, -2.5, 0.0, np.nan, -0.0]
+        rows = M // world
+        A_mine, s_mine = orc.quantize(np.ascontiguousarray(X[rank * rows:(rank + 1) * rows]), 0)
+        a_parts = [torch.zeros((rows, K), dtype=torch.int8) for _ in range(world)]
+        s_parts = [torch.zeros(rows) for _ in range(world)]
+        dist.all_gather(a_parts, torch.from_numpy(A_mine))
+        dist.all_gather(s_parts, torch.from_numpy(s_mine))
+        A = torch.cat(a_parts).numpy()
+        sa = torch.cat(s_parts).numpy()
+        A_ref, s_ref = orc.quantize(X, 0)
+        ok = bool(np.array_equal(A, A_ref) and np.array_equal(sa.view(np.uint32), s_ref.view(np.uint32)))
+        # scatter layout: shard r lands at its column offset in every full output
+        B, sb = orc.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
+        full = np.full((M, N), np.nan, np.float32)
+        for r in range(world):
+            r0, r1 = column_shard(N, world, r)
+            full[:, r0:r1] = orc.matmul_i8(A, np.ascontiguousarray(B[:, r0:r1]), sa, sb[r0:r1],
+                                           None, 0, 0)
+        ref = orc.matmul_i8(A_ref, B, s_ref, sb, None, 0, 0)
+        ok &= bool(np.array_equal(full.view(np.uint32), ref.view(np.uint32)))
+        q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_row_slice_quantize_and_scatter_layout():
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_row_slice_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    results = dict(q.get(timeout=5) for _ in range(2))
+    assert results == {0: True, 1: True}
+    assert all(p.exitcode == 0 for p in procs)
