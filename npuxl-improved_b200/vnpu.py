@@ -289,6 +289,7 @@ class Lib:
                                         C.POINTER(u32), C.POINTER(u64), C.POINTER(vp),
                                         C.POINTER(vp))
         self.matmul_i8 = _sig(h, "vnpu_matmul_i8", _ST, vp, C.POINTER(MatmulI8Args))
+        self.matmul_f32 = _sig(h, "vnpu_matmul_f32", _ST, vp, C.POINTER(MatmulF32Args))
         self.quantize_i8 = _sig(h, "vnpu_quantize_i8", _ST, vp, C.POINTER(QuantizeI8Args))
         self.rmsnorm_f32 = _sig(h, "vnpu_rmsnorm_f32", _ST, vp, C.POINTER(RmsnormArgs))
         self.rope_f32 = _sig(h, "vnpu_rope_f32", _ST, vp, C.POINTER(RopeArgs))
@@ -401,6 +402,26 @@ class Device:
             self.lib.check(rc, "matmul_i8")
         return rc
 
+    def matmul_f32(self, A, B, Cout, M, K, N, bias=None, lda=0, ldb=0, ldc=0, trans_a=0, trans_b=0,
+                   alpha=1.0, beta=0.0, epilogue=0, unit=UNIT_AUTO, tile_mask=None,
+                   mask_tile_m=0, mask_tile_n=0, flags=0, check=True) -> int:
+        a = MatmulF32Args(ptr(A), ptr(B), ptr(bias), ptr(Cout), M, K, N, lda, ldb, ldc, trans_a,
+                          trans_b, alpha, beta, epilogue, unit, 0, ptr(tile_mask), mask_tile_m,
+                          mask_tile_n)
+        if flags:
+            cmd = Command()
+            cmd.opcode = OP_MATMUL_F32
+            cmd.flags = flags
+            cmd.args.matmul_f32 = a
+            rc = self.lib.stream_submit(self.stream, C.byref(cmd), 1, None)
+            if rc == OK:
+                rc = self.lib.stream_sync(self.stream)
+        else:
+            rc = self.lib.matmul_f32(self.stream, C.byref(a))
+        if check:
+            self.lib.check(rc, "matmul_f32")
+        return rc
+
     def quantize_i8(self, X, Y, scales, rows, cols, axis=QUANT_PER_ROW, check=True) -> int:
         a = QuantizeI8Args(ptr(X), ptr(Y), ptr(scales), rows, cols, axis, 0)
         rc = self.lib.quantize_i8(self.stream, C.byref(a))
@@ -507,6 +528,11 @@ class Oracle:
         self._add = _sig(h, "oracle_add", None, vp, vp, vp, u64, f32, f32, C.c_int)
         self._attn = _sig(h, "oracle_attention", None, vp, vp, vp, vp, vp, u32, u32, u32, u32,
                           u32, u32, f32)
+        self._mm_f32 = _sig(h, "oracle_matmul_f32", None, vp, vp, vp, vp, u32, u32, u32, u32, u32,
+                            u32, u32, u32, f32, f32, u32, u32, vp, u32, u32, u32, u32, u32, u32,
+                            C.c_int, C.c_int)
+        self._f32_geom = _sig(h, "oracle_f32_tile_geometry", None, u32, u32, u32, u32, u32, u32,
+                              u32, C.c_int, C.POINTER(u32), C.POINTER(u32), C.POINTER(u32))
         self.fast_expf = _sig(h, "oracle_fast_expf", f32, f32, C.c_int)
         self.dequant = _sig(h, "oracle_dequant", f32, C.c_int32, f32, f32, C.POINTER(f32), u32,
                             C.c_int)
@@ -539,6 +565,26 @@ class Oracle:
         self._matmul(ptr(A), K, ptr(B), ptr(scale_a), ptr(scale_b), ptr(bias), ptr(Cm), N, M, K,
                      N, epilogue, form)
         return Cm
+
+    def matmul_f32(self, A, B, M, K, N, bias=None, C=None, lda=0, ldb=0, ldc=0, trans_a=0,
+                   trans_b=0, alpha=1.0, beta=0.0, epilogue=0, unit=UNIT_VOODOO, tile_mask=None,
+                   mask_tile_m=0, mask_tile_n=0, threads=8, tiles=(128, 128, 64), pack_b=1,
+                   avx2=1) -> np.ndarray:
+        """MATMUL_F32 as a reference device with `threads` threads, tile
+        defaults `tiles`, VNPU_PACK=`pack_b` and the AVX2 (or scalar) ISA
+        computes it.  C (optional) holds the prior contents beta reads."""
+        ldc_ = ldc or N
+        out = np.zeros((M, ldc_), np.float32) if C is None else np.array(C, np.float32, copy=True)
+        self._mm_f32(ptr(A), ptr(B), ptr(bias), ptr(out), M, K, N, lda, ldb, ldc, trans_a, trans_b,
+                     alpha, beta, epilogue, unit, ptr(tile_mask), mask_tile_m, mask_tile_n,
+                     threads, tiles[0], tiles[1], tiles[2], pack_b, avx2)
+        return out
+
+    def f32_tile_geometry(self, unit, M, N, threads=8, tiles=(128, 128, 64), pack_b=1):
+        tm, tk, tn = u32(), u32(), u32()
+        self._f32_geom(unit, M, N, threads, tiles[0], tiles[1], tiles[2], pack_b, C.byref(tm),
+                       C.byref(tk), C.byref(tn))
+        return tm.value, tk.value, tn.value
 
     def column_sums(self, B: np.ndarray, trans_b: int = 0):
         B = np.ascontiguousarray(B, np.int8)

@@ -443,3 +443,202 @@ void oracle_attention(const float *Q, const float *K, const float *V,
     free(scores);
     free(acc);
 }
+
+/* ------------------------------------------------------------------------- */
+/* MATMUL_F32 (src/kernels/kernels.cpp:19-331,480-520;                        */
+/*             src/core/scheduler.cpp:95-207,208-262,274-352)                 */
+/* ------------------------------------------------------------------------- */
+
+/* tile_geometry for F32 (int8 = false), src/core/scheduler.cpp:95-207.  The
+ * reference's tile sizes depend on its thread count, its tile defaults and
+ * VNPU_PACK; which kernel computes an output element, and so the rounding it
+ * sees, depends on the tile it falls in. */
+void oracle_f32_tile_geometry(uint32_t unit, uint32_t M, uint32_t N,
+                              uint32_t threads, uint32_t tile_m,
+                              uint32_t tile_k, uint32_t tile_n, int pack_b,
+                              uint32_t *tm_out, uint32_t *tk_out,
+                              uint32_t *tn_out)
+{
+    uint32_t tm = tile_m ? tile_m : 1, tk = tile_k ? tile_k : 1;
+    uint32_t tn = tile_n ? tile_n : 1;
+    const uint32_t units = threads ? threads : 1;
+    const int voodoo = unit == 1 || unit == 0;
+    if (M <= 8 && voodoo) {
+        /* decode rows: one row block; F32 keeps the 32..64 column tile */
+        tm = M;
+        tn = tn < 32 ? 32 : (tn > 64 ? 64 : tn);
+        if (tn > N) tn = N;
+        goto done;
+    }
+    if (pack_b && voodoo && M >= 3 && (N + 63) / 64 >= 2 * units) {
+        tm = M;
+        tn = 64;
+        goto done;
+    }
+    if (unit == 2) {            /* WILDCAT */
+        if (tm > 32) tm = 32;
+        if (tn > 64) tn = 64;
+        if (tk > 128) tk = 128;
+    } else if (unit == 3) {     /* CELL */
+        if (tm > 16) tm = 16;
+        if (tn > 64) tn = 64;
+        if (tk > 64) tk = 64;
+    }
+    {
+        const uint64_t target = (uint64_t)units * 64;
+        uint64_t tiles = (uint64_t)((M + tm - 1) / tm) * ((N + tn - 1) / tn);
+        while (tiles > target && (tm < M || tn < N)) {
+            if (tm < M) tm = 2 * tm < M ? 2 * tm : M;
+            if (tn < N) tn = 2 * tn < N ? 2 * tn : N;
+            tiles = (uint64_t)((M + tm - 1) / tm) * ((N + tn - 1) / tn);
+        }
+    }
+done:
+    *tm_out = tm;
+    *tk_out = tk;
+    *tn_out = tn;
+}
+
+typedef struct {
+    const float *A, *B, *bias;
+    float *C;
+    uint32_t K, lda, ldb, ldc, trans_a, trans_b, epilogue;
+    float alpha, beta;
+} F32Op;
+
+static float f32_a(const F32Op *p, uint32_t m, uint32_t k)
+{
+    return p->trans_a ? p->A[(size_t)k * p->lda + m] : p->A[(size_t)m * p->lda + k];
+}
+
+static float f32_b(const F32Op *p, uint32_t k, uint32_t n)
+{
+    return p->trans_b ? p->B[(size_t)n * p->ldb + k] : p->B[(size_t)k * p->ldb + n];
+}
+
+/* store_c, src/kernels/kernels.cpp:43-50: alpha*v, + bias, + beta*C,
+ * epilogue.  How GCC fuses it depends on the kernel it is inlined into:
+ *   F32_STORE_BLOCK  - register blocks and row stream: alpha*v+bias and
+ *                      beta*C+out both fused
+ *   F32_STORE_PANEL  - first K panel of the packed tile, and the B^T dot
+ *                      kernel: bias added unfused, beta*C+out fused
+ *   F32_STORE_SCALAR - scalar / Cell kernels: every step rounded. */
+enum { F32_STORE_BLOCK = 0, F32_STORE_PANEL = 1, F32_STORE_SCALAR = 2, F32_STORE_DOT = 3 };
+
+static float f32_store(const F32Op *p, uint32_t m, uint32_t n, float v, int store)
+{
+    float *dst = p->C + (size_t)m * p->ldc + n;
+    float out;
+    if (p->bias && store == F32_STORE_BLOCK) out = fmaf(p->alpha, v, p->bias[n]);
+    else if (p->bias) out = p->alpha * v + p->bias[n];
+    else out = p->alpha * v;
+    if (p->beta != 0.0f)
+        out = store >= F32_STORE_SCALAR ? out + p->beta * *dst : fmaf(p->beta, *dst, out);
+    return oracle_epilogue(out, p->epilogue,
+                           store == F32_STORE_SCALAR ? ORACLE_FORM_SCALAR : ORACLE_FORM_AVX2);
+}
+
+enum { F32_FMA = 0, F32_CHUNKED = 1, F32_UNFUSED = 2, F32_NT8 = 3 };
+
+/* One output element in the given accumulation form. */
+static void f32_element(const F32Op *p, uint32_t m, uint32_t n, int kind)
+{
+    float *dst = p->C + (size_t)m * p->ldc + n;
+    if (kind == F32_UNFUSED) {       /* scalar tile :65-76, Cell tile :409-454 */
+        float acc = 0.0f;
+        for (uint32_t k = 0; k < p->K; ++k) acc = acc + f32_a(p, m, k) * f32_b(p, k, n);
+        *dst = f32_store(p, m, n, acc, F32_STORE_SCALAR);
+    } else if (kind == F32_NT8) {    /* B^T dot products :331-352 */
+        float lane[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        uint32_t k = 0;
+        for (; k + 8 <= p->K; k += 8)
+            for (int l = 0; l < 8; ++l)
+                lane[l] = fmaf(f32_a(p, m, k + l), f32_b(p, k + l, n), lane[l]);
+        float dot = hsum8(lane);
+        /* The scalar tail as GCC -O3 compiles it: whole groups of four take
+         * one SSE multiply and in-order unfused adds, the last 0-3 terms
+         * fuse (checked for every tail length 1-7 against the reference). */
+        const uint32_t quad_end = k + (p->K - k) / 4 * 4;
+        for (; k < quad_end; ++k) dot = dot + f32_a(p, m, k) * f32_b(p, k, n);
+        for (; k < p->K; ++k) dot = fmaf(f32_a(p, m, k), f32_b(p, k, n), dot);
+        *dst = f32_store(p, m, n, dot, F32_STORE_PANEL);
+    } else if (kind == F32_CHUNKED) { /* packed panel tile :241-329, kc = 128 */
+        for (uint32_t k0 = 0; k0 < p->K; k0 += 128) {
+            const uint32_t k1 = p->K - k0 < 128 ? p->K : k0 + 128;
+            float part = 0.0f;
+            for (uint32_t k = k0; k < k1; ++k) part = fmaf(f32_a(p, m, k), f32_b(p, k, n), part);
+            *dst = k0 == 0 ? f32_store(p, m, n, part, F32_STORE_PANEL)
+                           : fmaf(p->alpha, part, *dst);
+        }
+    } else {                         /* register blocks :167-239, row stream :98-145 */
+        float acc = 0.0f;
+        for (uint32_t k = 0; k < p->K; ++k) acc = fmaf(f32_a(p, m, k), f32_b(p, k, n), acc);
+        *dst = f32_store(p, m, n, acc, F32_STORE_BLOCK);
+    }
+}
+
+/* Which form computes (m, n) of a tile, gemm_f32_dispatch_tile :480-520. */
+static int f32_kind(uint32_t unit, int avx2, int pack_b, uint32_t trans_a,
+                    uint32_t trans_b, uint32_t m0, uint32_t rows, uint32_t n0,
+                    uint32_t cols, uint32_t m)
+{
+    (void)n0;
+    if (unit == 3 || !avx2 || trans_a) return F32_UNFUSED;
+    if (trans_b) return F32_NT8;
+    if (pack_b && cols % 32 == 0 && rows >= 3 &&
+        (uint64_t)128 * cols * sizeof(float) <= 256u * 1024u + 64u)
+        return m < m0 + rows / 3 * 3 ? F32_CHUNKED : F32_FMA;
+    return F32_FMA;
+}
+
+void oracle_matmul_f32(const float *A, const float *B, const float *bias,
+                       float *C, uint32_t M, uint32_t K, uint32_t N,
+                       uint32_t lda, uint32_t ldb, uint32_t ldc,
+                       uint32_t trans_a, uint32_t trans_b, float alpha,
+                       float beta, uint32_t epilogue, uint32_t unit,
+                       const uint8_t *tile_mask, uint32_t mask_tile_m,
+                       uint32_t mask_tile_n, uint32_t threads,
+                       uint32_t tile_m, uint32_t tile_k, uint32_t tile_n,
+                       int pack_b, int avx2)
+{
+    F32Op p;
+    p.A = A; p.B = B; p.bias = bias; p.C = C;
+    p.K = K;
+    p.lda = lda ? lda : (trans_a ? M : K);
+    p.ldb = ldb ? ldb : (trans_b ? K : N);
+    p.ldc = ldc ? ldc : N;
+    p.trans_a = trans_a; p.trans_b = trans_b;
+    p.alpha = alpha == 0.0f ? 1.0f : alpha;
+    p.beta = beta;
+    p.epilogue = epilogue;
+    uint32_t tm, tk, tn;
+    oracle_f32_tile_geometry(unit, M, N, threads, tile_m, tile_k, tile_n, pack_b, &tm, &tk, &tn);
+    const uint32_t mt = (M + tm - 1) / tm, nt = (N + tn - 1) / tn;
+    for (uint32_t mi = 0; mi < mt; ++mi) {
+        const uint32_t m0 = mi * tm, rows = M - m0 < tm ? M - m0 : tm;
+        for (uint32_t ni = 0; ni < nt; ++ni) {
+            const uint32_t n0 = ni * tn, cols = N - n0 < tn ? N - n0 : tn;
+            int cull = 0;
+            if (tile_mask && mask_tile_m && mask_tile_n) {   /* :234-243 */
+                uint32_t mm = (uint32_t)(((uint64_t)mi * mask_tile_m) / mt);
+                uint32_t nn = (uint32_t)(((uint64_t)ni * mask_tile_n) / nt);
+                if (mm > mask_tile_m - 1) mm = mask_tile_m - 1;
+                if (nn > mask_tile_n - 1) nn = mask_tile_n - 1;
+                cull = tile_mask[(size_t)mm * mask_tile_n + nn] == 0;
+            }
+            for (uint32_t m = m0; m < m0 + rows; ++m) {
+                for (uint32_t n = n0; n < n0 + cols; ++n) {
+                    if (cull) {                              /* zero_c_tile :52-62 */
+                        float *dst = C + (size_t)m * p.ldc + n;
+                        float out = bias ? bias[n] : 0.0f;
+                        if (beta != 0.0f) out = out + beta * *dst;
+                        *dst = oracle_epilogue(out, epilogue, ORACLE_FORM_SCALAR);
+                        continue;
+                    }
+                    f32_element(&p, m, n, f32_kind(unit, avx2, pack_b, trans_a, trans_b,
+                                                   m0, rows, n0, cols, m));
+                }
+            }
+        }
+    }
+}

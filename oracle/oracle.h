@@ -90,6 +90,29 @@ void oracle_attention(const float *Q, const float *K, const float *V,
                       uint32_t heads, uint32_t seq_q, uint32_t seq_k,
                       uint32_t head_dim, uint32_t causal, float scale);
 
+/* MATMUL_F32 tile sizes (src/core/scheduler.cpp:95-207, F32 branch) for a
+ * reference device with `threads` worker threads and tile defaults
+ * tile_m/k/n (128/128/64 on AVX2 hosts, 32/64/32 scalar); unit is the unit
+ * choose_unit resolved (1 VOODOO, 2 WILDCAT, 3 CELL). */
+void oracle_f32_tile_geometry(uint32_t unit, uint32_t M, uint32_t N,
+                              uint32_t threads, uint32_t tile_m,
+                              uint32_t tile_k, uint32_t tile_n, int pack_b,
+                              uint32_t *tm, uint32_t *tk, uint32_t *tn);
+
+/* MATMUL_F32 (src/kernels/kernels.cpp:19-331,480-520) as the reference
+ * device described by threads / tile_m,k,n / pack_b (VNPU_PACK) / avx2
+ * (0 = VNPU_FORCE_ISA=scalar) computes it, element by element in the
+ * rounding of the kernel that owns the element's tile. */
+void oracle_matmul_f32(const float *A, const float *B, const float *bias,
+                       float *C, uint32_t M, uint32_t K, uint32_t N,
+                       uint32_t lda, uint32_t ldb, uint32_t ldc,
+                       uint32_t trans_a, uint32_t trans_b, float alpha,
+                       float beta, uint32_t epilogue, uint32_t unit,
+                       const uint8_t *tile_mask, uint32_t mask_tile_m,
+                       uint32_t mask_tile_n, uint32_t threads,
+                       uint32_t tile_m, uint32_t tile_k, uint32_t tile_n,
+                       int pack_b, int avx2);
+
 #ifdef __cplusplus
 }
 #endif

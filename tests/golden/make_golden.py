@@ -159,6 +159,51 @@ def main():
         g[f"{name}_shape"] = np.array([h, sq, sk, dd, causal], np.int64)
     d.close()
 
+    # ---- MATMUL_F32 (the GEMM behind the legacy virtual_npu/vgpu_npu shims)
+    # Which reference kernel owns an element depends on the device's thread
+    # count, tile defaults, VNPU_PACK, the unit and the transposes; the cases
+    # cover every kernel (packed panels, register blocks + row stream, B^T
+    # dots with ragged tails, scalar A^T, Cell, scalar ISA, Wildcat culling).
+    frng = np.random.default_rng(20261202)
+    f32_cases = [
+        # M, K, N, isa, threads, pack, unit, ta, tb, bias, alpha, beta, epi, mask
+        (48, 260, 256, "avx2", 2, 1, 1, 0, 0, 1, 1.0, 0.0, 0, None),
+        (40, 200, 130, "avx2", 8, 0, 1, 0, 0, 1, 1.5, 0.7, 2, None),
+        (5, 257, 100, "avx2", 8, 1, 1, 0, 0, 0, 1.0, 0.0, 0, None),
+        (37, 131, 70, "avx2", 3, 1, 1, 0, 1, 1, 1.3, 0.7, 3, None),
+        (33, 90, 50, "avx2", 4, 1, 1, 1, 0, 1, 1.0, -1.3, 1, None),
+        (30, 100, 90, "avx2", 4, 1, 3, 0, 0, 1, 0.75, 0.7, 2, None),
+        (31, 77, 45, "scalar", 4, 1, 1, 0, 0, 1, 1.0, 0.7, 2, None),
+        (100, 64, 200, "avx2", 2, 1, 2, 0, 0, 1, 1.0, 0.5, 0, (3, 2)),
+    ]
+    rows = []
+    for i, (M, K, N, isa, thr, pack, unit, ta, tb, has_bias, alpha, beta, epi,
+            mask) in enumerate(f32_cases):
+        A = frng.normal(0, 1, (K, M) if ta else (M, K)).astype(np.float32)
+        B = frng.normal(0, 1, (N, K) if tb else (K, N)).astype(np.float32)
+        bias = frng.normal(0, 1, N).astype(np.float32) if has_bias else None
+        C0 = frng.normal(0, 1, (M, N)).astype(np.float32)
+        tm = frng.integers(0, 2, mask[0] * mask[1]).astype(np.uint8) if mask else None
+        os.environ["VNPU_PACK"] = str(pack)
+        d = ref_device(lib, isa, thr)
+        os.environ.pop("VNPU_PACK")
+        info = d.info()
+        Cr = C0.copy()
+        d.matmul_f32(A, B, Cr, M, K, N, bias=bias, trans_a=ta, trans_b=tb, alpha=alpha, beta=beta,
+                     epilogue=epi, unit=unit, tile_mask=tm, mask_tile_m=mask[0] if mask else 0,
+                     mask_tile_n=mask[1] if mask else 0)
+        d.close()
+        g[f"f32_{i}_A"], g[f"f32_{i}_B"], g[f"f32_{i}_C0"], g[f"f32_{i}_C"] = A, B, C0, Cr
+        if bias is not None:
+            g[f"f32_{i}_bias"] = bias
+        if tm is not None:
+            g[f"f32_{i}_mask"] = tm
+        rows.append([M, K, N, int(isa == "avx2"), info.num_threads, pack, unit, ta, tb, epi,
+                     info.tile_m, info.tile_k, info.tile_n, mask[0] if mask else 0,
+                     mask[1] if mask else 0])
+        g[f"f32_{i}_ab"] = np.array([alpha, beta], np.float32)
+    g["f32_cases"] = np.array(rows, np.int64)
+
     out = os.path.join(HERE, "golden.npz")
     np.savez_compressed(out, **g)
     print("wrote", out, os.path.getsize(out), "bytes")

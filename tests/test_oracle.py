@@ -78,6 +78,34 @@ def test_fast_expf_properties(oracle):
         assert oracle.fast_expf(n * 0.6931471805599453, 0) == pytest.approx(2.0 ** n, rel=2e-4)
 
 
+def _f32_golden_case(golden, i):
+    M, K, N, avx2, thr, pack, unit, ta, tb, epi, tm, tk, tn, mm, mn = (
+        int(v) for v in golden["f32_cases"][i])
+    alpha, beta = (float(v) for v in golden[f"f32_{i}_ab"])
+    return dict(M=M, K=K, N=N, bias=golden.get(f"f32_{i}_bias"), C=golden[f"f32_{i}_C0"],
+                trans_a=ta, trans_b=tb, alpha=alpha, beta=beta, epilogue=epi, unit=unit,
+                tile_mask=golden.get(f"f32_{i}_mask"), mask_tile_m=mm, mask_tile_n=mn,
+                threads=thr, tiles=(tm, tk, tn), pack_b=pack, avx2=avx2)
+
+
+@pytest.mark.parametrize("i", range(8))
+def test_matmul_f32_golden(oracle, golden, i):
+    kw = _f32_golden_case(golden, i)
+    C = oracle.matmul_f32(golden[f"f32_{i}_A"], golden[f"f32_{i}_B"], **kw)
+    assert bits_equal(C, golden[f"f32_{i}_C"])
+
+
+def test_matmul_f32_golden_needs_the_kernel_map(oracle, golden):
+    """The fixtures tell the kernels apart: computing a case as if every
+    element took another kernel's rounding changes bits."""
+    kw = _f32_golden_case(golden, 0)          # packed panels, K = 260 > 128
+    C = oracle.matmul_f32(golden["f32_0_A"], golden["f32_0_B"], **dict(kw, pack_b=0))
+    assert not bits_equal(C, golden["f32_0_C"])
+    kw = _f32_golden_case(golden, 3)          # B^T dots
+    C = oracle.matmul_f32(golden["f32_3_A"], golden["f32_3_B"], **dict(kw, avx2=0))
+    assert not bits_equal(C, golden["f32_3_C"])
+
+
 # ---------------------------------------------------------------- live reference
 def _ref_device(ref_lib, isa, threads):
     os.environ["VNPU_FORCE_ISA"] = isa
@@ -197,3 +225,49 @@ def test_block_driver_host_matches_reference(ref_lib, oracle):
     finally:
         ref.close()
         orc.close()
+
+
+def test_matmul_f32_vs_reference(ref_lib, oracle):
+    """Seeded random MATMUL_F32 configurations: every kernel, unit, ISA,
+    VNPU_PACK setting, transpose, stride, culling mask and epilogue."""
+    rng = np.random.default_rng(5)
+    for _ in range(60):
+        M = int(rng.choice([1, 3, 5, 8, 9, 31, 64, 97]))
+        K = int(rng.integers(1, 300))
+        N = int(rng.choice([1, 7, 33, 64, 65, 128, 200]))
+        isa = "avx2" if rng.random() < 0.85 else "scalar"
+        threads, pack = int(rng.integers(1, 9)), int(rng.random() < 0.7)
+        unit = int(rng.choice([0, 1, 2, 3]))
+        ta, tb = int(rng.random() < 0.2), int(rng.random() < 0.25)
+        beta = float(rng.choice([0.0, 0.7, -1.3]))
+        alpha = float(rng.choice([0.0, 1.0, -2.1]))
+        epi = int(rng.integers(0, 5))
+        pads = [int(rng.choice([0, 3])) for _ in range(3)]
+        mask, mtm, mtn = None, 0, 0
+        if rng.random() < 0.2:
+            mtm, mtn = int(rng.integers(1, 4)), int(rng.integers(1, 4))
+            mask = (rng.random(mtm * mtn) < 0.6).astype(np.uint8)
+        A = rng.normal(0, 1, (K, M + pads[0]) if ta else (M, K + pads[0])).astype(np.float32)
+        B = rng.normal(0, 1, (N, K + pads[1]) if tb else (K, N + pads[1])).astype(np.float32)
+        C0 = rng.normal(0, 1, (M, N + pads[2])).astype(np.float32)
+        bias = rng.normal(0, 1, N).astype(np.float32) if rng.random() < 0.5 else None
+        ld = dict(lda=A.shape[1] if pads[0] else 0, ldb=B.shape[1] if pads[1] else 0,
+                  ldc=C0.shape[1] if pads[2] else 0)
+        os.environ["VNPU_PACK"] = str(pack)
+        try:
+            d = _ref_device(ref_lib, isa, threads)
+        finally:
+            os.environ.pop("VNPU_PACK", None)
+        with d:
+            info = d.info()
+            Cr = C0.copy()
+            d.matmul_f32(A, B, Cr, M, K, N, bias=bias, trans_a=ta, trans_b=tb, alpha=alpha,
+                         beta=beta, epilogue=epi, unit=unit, tile_mask=mask, mask_tile_m=mtm,
+                         mask_tile_n=mtn, **ld)
+        resolved = unit if unit else (2 if mask is not None else 1)
+        Co = oracle.matmul_f32(A, B, M, K, N, bias=bias, C=C0, trans_a=ta, trans_b=tb, alpha=alpha,
+                               beta=beta, epilogue=epi, unit=resolved, tile_mask=mask,
+                               mask_tile_m=mtm, mask_tile_n=mtn, threads=info.num_threads,
+                               tiles=(info.tile_m, info.tile_k, info.tile_n), pack_b=pack,
+                               avx2=int(isa == "avx2"), **ld)
+        assert bits_equal(Cr, Co), (M, K, N, isa, threads, pack, unit, ta, tb, alpha, beta, epi)
