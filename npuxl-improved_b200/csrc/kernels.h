@@ -97,6 +97,31 @@ bool encode_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *bas
                     uint64_t dim1, uint64_t stride1_bytes, uint32_t box0, uint32_t box1,
                     CUtensorMapSwizzle swizzle);
 
+// ---- MATMUL_F32 (src/kernels/kernels.cpp:19-352,480-520) -----------------------
+// Accumulation form of the reference kernel a command's elements take
+// (gemm_f32.cu has the rules).
+enum F32Mode : uint32_t { kF32Block = 0, kF32Unfused = 1, kF32Dot8 = 2 };
+
+struct MatmulF32 {
+    const float *A = nullptr;       // M x K (K x M when trans_a), row stride lda
+    const float *B = nullptr;       // K x N (N x K when trans_b), row stride ldb
+    const float *bias = nullptr;    // N or NULL
+    float *C = nullptr;             // M x N, row stride ldc; read when beta != 0
+    uint32_t M = 0, K = 0, N = 0, lda = 0, ldb = 0, ldc = 0;
+    uint32_t trans_a = 0, trans_b = 0;
+    float alpha = 1.0f, beta = 0.0f;
+    uint32_t epilogue = 0;
+    uint32_t mode = kF32Block;
+    // The reference's tile geometry for this GEMM (tile_m x tile_n grid) and
+    // whether its packed-panel kernel may own tiles (AVX2, VNPU_PACK, NN).
+    uint32_t tile_m = 1, tile_n = 1;
+    uint32_t packed = 0;
+    const uint8_t *mask = nullptr;  // Wildcat cull mask, mask_m x mask_n bytes
+    uint32_t mask_m = 0, mask_n = 0;
+};
+
+cudaError_t matmul_f32(const LaunchCtx &ctx, const MatmulF32 &p);
+
 // ---- decoder-block ops (src/kernels/llm.cpp) -----------------------------------
 cudaError_t rmsnorm(const LaunchCtx &ctx, const float *X, const float *W, float *Y,
                     uint32_t rows, uint32_t cols, float eps);

@@ -22,7 +22,9 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <set>
 #include <stdexcept>
+#include <string>
 #include <thread>
 #include <unordered_map>
 
@@ -232,6 +234,31 @@ private:
     uint64_t staged_ = 0;
 };
 
+// Physical cores of this host: distinct SMT sibling sets in sysfs (the
+// reference's default worker count, src/core/runtime.cpp:98-145,858-866).
+uint32_t host_physical_cores() {
+    const unsigned logical = std::max(1u, std::thread::hardware_concurrency());
+    std::set<std::string> cores;
+    for (unsigned cpu = 0; cpu < logical; ++cpu) {
+        const std::string path = "/sys/devices/system/cpu/cpu" + std::to_string(cpu) +
+                                 "/topology/core_cpus_list";
+        std::FILE *f = std::fopen(path.c_str(), "r");
+        if (!f) break;
+        char buf[128] = {};
+        const size_t got = std::fread(buf, 1, sizeof(buf) - 1, f);
+        std::fclose(f);
+        std::string key(buf, got);
+        while (!key.empty() && (key.back() == '\n' || key.back() == ' ')) key.pop_back();
+        if (!key.empty()) cores.insert(key);
+    }
+    return cores.empty() ? logical : static_cast<uint32_t>(cores.size());
+}
+
+bool env_is(const char *name, const char *value) {
+    const char *e = std::getenv(name);
+    return e && !std::strcmp(e, value);
+}
+
 uint32_t epi_form_from_env() {
     const char *e = std::getenv("VNPU_B200_EPILOGUE");
     if (!e) return kFormBlock;
@@ -305,6 +332,114 @@ void exec_matmul_i8(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags,
     acc.flops = 2ull * in.M * in.K * in.N;
     acc.tiles = ((in.M + 127) / 128) * ((in.N + 255) / 256);
     acc.dma = st.staged_bytes();
+}
+
+// choose_unit, src/core/scheduler.cpp:43-62 (GPU is this device: the F32
+// path then follows the reference's default unit).
+uint32_t f32_unit(const vnpu_matmul_f32_args_t &a, uint32_t flags) {
+    if (flags & VNPU_CMD_FLAG_CELL_DMA) return VNPU_UNIT_CELL;
+    if (flags & VNPU_CMD_FLAG_VOODOO_FIFO) return VNPU_UNIT_VOODOO;
+    if (a.unit != VNPU_UNIT_AUTO && a.unit != VNPU_UNIT_GPU) return a.unit;
+    if (a.tile_mask || (flags & VNPU_CMD_FLAG_WILDCAT_CULL)) return VNPU_UNIT_WILDCAT;
+    return VNPU_UNIT_VOODOO;
+}
+
+uint32_t ceil_div(uint32_t a, uint32_t b) { return (a + b - 1) / b; }
+
+// F32 tile geometry, src/core/scheduler.cpp:95-207 (int8 = false).
+void f32_geometry(const vnpu_device_t *d, uint32_t unit, uint32_t M, uint32_t N, uint32_t &tm,
+                  uint32_t &tn) {
+    tm = std::max<uint32_t>(1, d->f32_tile_m.load());
+    tn = std::max<uint32_t>(1, d->f32_tile_n.load());
+    const uint32_t units = std::max<uint32_t>(1, d->f32_threads);
+    const bool voodoo = unit == VNPU_UNIT_VOODOO || unit == VNPU_UNIT_AUTO;
+    if (M <= 8 && voodoo) {  // decode rows: the F32 kernels keep a 32..64 column tile
+        tm = M;
+        tn = std::min<uint32_t>(std::max<uint32_t>(32, tn), 64);
+        tn = std::min(tn, N);
+        return;
+    }
+    if (d->f32_pack && voodoo && M >= 3 && ceil_div(N, 64) >= 2 * units) {
+        tm = M;  // one panel-packed tile spans all rows
+        tn = 64;
+        return;
+    }
+    if (unit == VNPU_UNIT_WILDCAT) {
+        tm = std::min<uint32_t>(tm, 32);
+        tn = std::min<uint32_t>(tn, 64);
+    } else if (unit == VNPU_UNIT_CELL) {
+        tm = std::min<uint32_t>(tm, 16);
+        tn = std::min<uint32_t>(tn, 64);
+    }
+    const uint64_t target = static_cast<uint64_t>(units) * 64;
+    auto count = [&] { return static_cast<uint64_t>(ceil_div(M, tm)) * ceil_div(N, tn); };
+    while (count() > target && (tm < M || tn < N)) {
+        if (tm < M) tm = std::min(M, tm * 2);
+        if (tn < N) tn = std::min(N, tn * 2);
+    }
+}
+
+// src/core/scheduler.cpp:274-352 (prepare_matmul_f32 + execute_matmul_f32)
+void exec_matmul_f32(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags,
+                     const LaunchCtx &ctx, Accounting &acc) {
+    const auto &in = cmd.args.matmul_f32;
+    if (!in.A || !in.B || !in.C || !in.M || !in.K || !in.N)
+        throw CommandError("invalid matmul_f32 arguments");
+    if (static_cast<uint64_t>(in.M) * in.K > UINT64_MAX / in.N)
+        throw CommandError("matmul_f32 size overflow");
+    if (in.trans_a > 1 || in.trans_b > 1 || in.epilogue > VNPU_EPILOGUE_GELU_ERF)
+        throw CommandError("invalid matmul_f32 arguments");
+    const uint32_t lda = in.lda ? in.lda : (in.trans_a ? in.M : in.K);
+    const uint32_t ldb = in.ldb ? in.ldb : (in.trans_b ? in.K : in.N);
+    const uint32_t ldc = in.ldc ? in.ldc : in.N;
+    if (lda < (in.trans_a ? in.M : in.K) || ldb < (in.trans_b ? in.K : in.N) || ldc < in.N)
+        throw CommandError("invalid matmul_f32 leading dimensions");
+    const vnpu_device_t *d = s->device;
+    const uint32_t unit = f32_unit(in, flags);
+    const bool scalar_isa = d->f32_scalar || (flags & VNPU_CMD_FLAG_EPI_SCALAR);
+    MatmulF32 p;
+    f32_geometry(d, unit, in.M, in.N, p.tile_m, p.tile_n);
+    if (unit == VNPU_UNIT_CELL || scalar_isa || in.trans_a) p.mode = kF32Unfused;
+    else if (in.trans_b) p.mode = kF32Dot8;
+    else p.mode = kF32Block;
+    p.packed = p.mode == kF32Block && d->f32_pack;
+    Staging st(s);
+    const uint64_t a_span = in.trans_a ? static_cast<uint64_t>(in.K - 1) * lda + in.M
+                                       : static_cast<uint64_t>(in.M - 1) * lda + in.K;
+    const uint64_t b_span = in.trans_b ? static_cast<uint64_t>(in.N - 1) * ldb + in.K
+                                       : static_cast<uint64_t>(in.K - 1) * ldb + in.N;
+    p.A = st.in(in.A, a_span * sizeof(float));
+    p.B = st.in(in.B, b_span * sizeof(float));
+    p.bias = st.in(in.bias, sizeof(float) * in.N);
+    const uint64_t c_span = (static_cast<uint64_t>(in.M - 1) * ldc + in.N) * sizeof(float);
+    p.C = st.out(in.C, c_span, in.beta != 0.0f || ldc != in.N);
+    if (in.tile_mask && in.mask_tile_m && in.mask_tile_n) {
+        p.mask = st.in(in.tile_mask, static_cast<uint64_t>(in.mask_tile_m) * in.mask_tile_n);
+        p.mask_m = in.mask_tile_m;
+        p.mask_n = in.mask_tile_n;
+    }
+    p.M = in.M;
+    p.K = in.K;
+    p.N = in.N;
+    p.lda = lda;
+    p.ldb = ldb;
+    p.ldc = ldc;
+    p.trans_a = in.trans_a;
+    p.trans_b = in.trans_b;
+    p.alpha = in.alpha == 0.0f ? 1.0f : in.alpha;
+    p.beta = in.beta;
+    p.epilogue = in.epilogue;
+    cuda_check(matmul_f32(ctx, p), "matmul_f32 launch");
+    st.finish();
+    const uint64_t a_bytes = static_cast<uint64_t>(in.M) * in.K * sizeof(float);
+    const uint64_t b_bytes = static_cast<uint64_t>(in.K) * in.N * sizeof(float);
+    const uint64_t c_bytes = static_cast<uint64_t>(in.M) * in.N * sizeof(float);
+    acc.bytes_read = a_bytes + b_bytes + (in.bias ? sizeof(float) * in.N : 0) +
+                     (in.beta != 0.0f ? c_bytes : 0);
+    acc.bytes_written = c_bytes;
+    acc.flops = 2ull * in.M * in.K * in.N;
+    acc.tiles = static_cast<uint64_t>(ceil_div(in.M, p.tile_m)) * ceil_div(in.N, p.tile_n);
+    acc.dma = unit == VNPU_UNIT_CELL ? a_bytes + b_bytes : st.staged_bytes();
 }
 
 void exec_matmul_i8_scatter(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags,
@@ -668,6 +803,7 @@ vnpu_status_t execute_command(vnpu_stream_t *s, const vnpu_command_t &cmd, uint3
         case VNPU_OP_NOP:
         case VNPU_OP_BARRIER: break;
         case VNPU_OP_MATMUL_I8: exec_matmul_i8(s, cmd, flags, ctx, acc); break;
+        case VNPU_OP_MATMUL_F32: exec_matmul_f32(s, cmd, flags, ctx, acc); break;
         case VNPU_OP_QUANTIZE_I8: exec_quantize_i8(s, cmd, ctx, acc); break;
         case VNPU_OP_RMSNORM_F32: exec_rmsnorm(s, cmd, ctx, acc); break;
         case VNPU_OP_ROPE_F32: exec_rope(s, cmd, ctx, acc); break;
@@ -682,8 +818,8 @@ vnpu_status_t execute_command(vnpu_stream_t *s, const vnpu_command_t &cmd, uint3
         case VNPU_OP_MEMSET: exec_memset(s, cmd, acc); break;
         case VNPU_OP_PACK_WEIGHTS_I8: exec_pack(s, cmd, acc); break;
         default:
-            // MATMUL_F32, SOFTMAX, GELU, MUL, MTP_HEAD: not part of the int8
-            // hot path this backend implements.
+            // SOFTMAX, GELU, MUL, MTP_HEAD: outside the int8 hot path this
+            // backend implements.
             return VNPU_ERR_UNSUPPORTED;
         }
         return VNPU_OK;
@@ -976,6 +1112,24 @@ VNPU_API vnpu_status_t VNPU_CALL vnpu_device_create(const vnpu_config_t *config,
         d->config = cfg;
         d->num_sms = prop.multiProcessorCount;
         d->epi_form = epi_form_from_env();
+        // The reference device whose MATMUL_F32 results this one reproduces
+        // (src/core/runtime.cpp:858-938).
+        const bool ref_mode = env_is("VNPU_MODE", "reference");
+        d->f32_scalar = ref_mode || env_is("VNPU_FORCE_ISA", "scalar") ||
+                        d->epi_form == kFormScalar;
+        d->f32_pack = !ref_mode && !env_is("VNPU_PACK", "0");
+        const uint32_t logical = std::max(1u, std::thread::hardware_concurrency());
+        d->f32_threads = std::min(cfg.num_threads ? cfg.num_threads : host_physical_cores(),
+                                  logical);
+        if (cfg.tile_m && cfg.tile_k && cfg.tile_n) {
+            d->f32_tile_m.store(cfg.tile_m);
+            d->f32_tile_k.store(cfg.tile_k);
+            d->f32_tile_n.store(cfg.tile_n);
+        } else if (d->f32_scalar) {
+            d->f32_tile_m.store(32);
+            d->f32_tile_k.store(64);
+            d->f32_tile_n.store(32);
+        }
         if (const char *e = std::getenv("VNPU_B200_WAIT_LIMIT_MS"))
             d->wait_limit_ns = static_cast<uint64_t>(std::atoll(e)) * 1000000ull;
         if (cudaStreamCreateWithFlags(&d->aux, cudaStreamNonBlocking) != cudaSuccess) {
@@ -1117,6 +1271,9 @@ VNPU_API vnpu_status_t VNPU_CALL vnpu_device_set_tiles(vnpu_device_t *device, ui
     device->tile_m.store(tile_m);
     device->tile_k.store(tile_k);
     device->tile_n.store(tile_n);
+    device->f32_tile_m.store(tile_m);
+    device->f32_tile_k.store(tile_k);
+    device->f32_tile_n.store(tile_n);
     return VNPU_OK;
 }
 

@@ -154,6 +154,13 @@ struct vnpu_device {
     std::atomic<uint32_t> error{0};
     std::atomic<uint32_t> last_opcode{0};
     std::atomic<uint32_t> tile_m{128}, tile_k{128}, tile_n{256};
+    // MATMUL_F32 reproduces the reference device of the same configuration:
+    // its worker-thread count, tile defaults, VNPU_PACK and ISA decide which
+    // of its kernels, and so which rounding, owns each output element.
+    uint32_t f32_threads = 1;
+    std::atomic<uint32_t> f32_tile_m{128}, f32_tile_k{128}, f32_tile_n{64};
+    bool f32_pack = true;
+    bool f32_scalar = false;
     std::atomic<uint64_t> launches{0};  // kernels launched by this library
     vnpu_interrupt_cb_t irq_cb = nullptr;
     void *irq_user = nullptr;

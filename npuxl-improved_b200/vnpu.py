@@ -326,12 +326,14 @@ class Lib:
 class Device:
     """A vnpu device plus one stream: the unit the tests and the bench drive."""
 
-    def __init__(self, lib: Lib, num_threads: int = 0, ordinal: int = 0):
+    def __init__(self, lib: Lib, num_threads: int = 0, ordinal: int = 0, tiles=None):
         self.lib = lib
         cfg = Config()
         lib.config_init(C.byref(cfg))
         if num_threads:
             cfg.num_threads = num_threads
+        if tiles:
+            cfg.tile_m, cfg.tile_k, cfg.tile_n = tiles
         cfg.reserved0 = ordinal
         dev = vp()
         lib.check(lib.device_create(C.byref(cfg), C.byref(dev)), "device_create")

@@ -81,3 +81,28 @@ def bits_equal(a: np.ndarray, b: np.ndarray) -> bool:
     a = np.ascontiguousarray(a)
     b = np.ascontiguousarray(b)
     return a.shape == b.shape and np.array_equal(a.view(np.uint8), b.view(np.uint8))
+
+
+def read_records(path: str):
+    """Tagged records written by tests/compat/legacy_scenario.c."""
+    import struct
+    data = open(path, "rb").read()
+    out, i = [], 0
+    while i < len(data):
+        (ln,) = struct.unpack_from("<I", data, i)
+        tag = data[i + 4:i + 4 + ln].decode()
+        (n,) = struct.unpack_from("<Q", data, i + 4 + ln)
+        start = i + 12 + ln
+        out.append((tag, data[start:start + n]))
+        i = start + n
+    return out
+
+
+def build_legacy_scenario(out_dir: str, include_dir: str, link_args: list) -> str:
+    """Compile tests/compat/legacy_scenario.c against a header tree and a
+    library; returns the executable's path."""
+    exe = os.path.join(out_dir, "legacy_scenario")
+    subprocess.run(["gcc", "-O1", "-I", include_dir,
+                    os.path.join(ROOT, "tests", "compat", "legacy_scenario.c")] + link_args +
+                   ["-o", exe], check=True)
+    return exe
