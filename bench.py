@@ -315,6 +315,65 @@ def gemm_secondary(lib, dev, st, torch, M, K, N, epi, with_bias, iters=20):
     return out
 
 
+def cmd_matmul_f32(A, B, Cp, M, K, N, trans_b=0):
+    c = vnpu.Command()
+    c.opcode = vnpu.OP_MATMUL_F32
+    c.args.matmul_f32 = vnpu.MatmulF32Args(A, B, None, Cp, M, K, N, 0, 0, 0, 0, trans_b, 1.0,
+                                           0.0, 0, vnpu.UNIT_AUTO, 0, None, 0, 0)
+    return c
+
+
+def f32_secondary(lib, dev, st, torch, M, K, N, trans_b=0, iters=5, ref_rows=64):
+    """MATMUL_F32 (the legacy shims' GEMM): CUDA-core kernels that reproduce
+    the reference's per-tile rounding; inputs larger than L2.  The reference
+    is timed on `ref_rows` rows of the same GEMM on the host cores."""
+    g = torch.Generator(device="cuda").manual_seed(M + K)
+    A = torch.empty((M, K), device="cuda").uniform_(-1, 1, generator=g)
+    B = torch.empty((N, K) if trans_b else (K, N), device="cuda").uniform_(-1, 1, generator=g)
+    Cm = torch.empty((M, N), device="cuda")
+    torch.cuda.synchronize()
+    mm = cmd_matmul_f32(A.data_ptr(), B.data_ptr(), Cm.data_ptr(), M, K, N, trans_b)
+    time_loop(lib, dev, st, [mm], 2)
+    ms = time_loop(lib, dev, st, [mm], iters)
+    out = {"shape": f"{M}x{K}x{N}", "trans_b": trans_b, "ms": ms,
+           "tflops": 2.0 * M * K * N / ms / 1e9,
+           "kernel": "gemm_f32_kernel<%s>" % ("kF32Dot8" if trans_b else "kF32Block")}
+    # Library comparator: cuBLAS FP32 SGEMM (TF32 off) on the same shape; it
+    # sums in its own order, so its bits differ from the reference's.
+    try:
+        prev = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False
+        Bm = B.t() if trans_b else B
+        torch.mm(A, Bm)
+        torch.cuda.synchronize()
+        c0 = torch.cuda.Event(enable_timing=True)
+        c1 = torch.cuda.Event(enable_timing=True)
+        c0.record()
+        for _ in range(iters):
+            torch.mm(A, Bm)
+        c1.record()
+        torch.cuda.synchronize()
+        out["cublas_sgemm_tflops"] = 2.0 * M * K * N / (c0.elapsed_time(c1) / iters) / 1e9
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    except Exception as exc:  # library comparator only
+        out["cublas_sgemm_tflops"] = f"unavailable: {exc}"
+    if os.path.exists(REF_LIB):
+        os.environ.setdefault("VNPU_FORCE_ISA", "avx2")
+        rlib = vnpu.Lib(REF_LIB)
+        with vnpu.Device(rlib, num_threads=os.cpu_count() or 1) as rd:
+            Ah = A[:ref_rows].cpu().numpy()
+            Bh = B.cpu().numpy()
+            Ch = np.empty((ref_rows, N), np.float32)
+            rd.matmul_f32(Ah, Bh, Ch, ref_rows, K, N, trans_b=trans_b)
+            t0 = time.perf_counter()
+            rd.matmul_f32(Ah, Bh, Ch, ref_rows, K, N, trans_b=trans_b)
+            t = time.perf_counter() - t0
+            out["reference_cpu"] = {"tflops": 2.0 * ref_rows * K * N / t / 1e12,
+                                    "cores": rd.info().num_threads,
+                                    "sample": f"{ref_rows} rows ({ref_rows}x{K}x{N}), host buffers"}
+    return out
+
+
 def gemv_secondary(lib, dev, st, torch, M, K=4096, N=4096, copies=32, rounds=8):
     """Decode GEMV with bias; rotates `copies` weight sets (> 4x L2) so the
     16 MiB matrix is read from HBM each launch."""
@@ -631,6 +690,8 @@ def run_b200(args):
                 gv = gemv_secondary(lib, dev, st, torch, m)
                 gv["frac_of_hbm"] = gv["gbs"] / pk["hbm_gbs"]
                 secondary[f"gemv_m{m}"] = gv
+            secondary["matmul_f32_4096_cube"] = f32_secondary(lib, dev, st, torch, 4096, 4096,
+                                                              4096)
             if not args.no_block:
                 secondary["llm_block"] = llm_block_secondary(
                     lib, dev, torch, with_reference=not args.no_cpu_baseline)
@@ -699,7 +760,7 @@ def run_b200(args):
 
 def run_kernel_case(spec: str):
     """One small case of one kernel, launched twice (for ncu captures):
-    gemm:MxKxN[:silu], gemv:MxKxN, quantize:RxC, attention:HxSQxSKxD, or
+    gemm:MxKxN[:silu], gemv:MxKxN, f32:MxKxN[:nt], quantize:RxC, attention:HxSQxSKxD, or
     llm_decode:STEPS (the decoder block's graph-captured decode step)."""
     import torch
 
@@ -723,6 +784,15 @@ def run_kernel_case(spec: str):
             dev.matmul_i8(A8.data_ptr(), w, sa.data_ptr(), None, Cm.data_ptr(), M, K, N,
                           epilogue=epi)
         dev.unpack(w)
+    elif kind == "f32":
+        M, K, N = shape
+        trans_b = 1 if len(parts) > 1 and parts[1] == "nt" else 0
+        A = torch.empty((M, K), device="cuda").uniform_(-1, 1, generator=g)
+        B = torch.empty((N, K) if trans_b else (K, N), device="cuda").uniform_(-1, 1, generator=g)
+        Cm = torch.empty((M, N), device="cuda")
+        torch.cuda.synchronize()
+        for _ in range(2):
+            dev.matmul_f32(A.data_ptr(), B.data_ptr(), Cm.data_ptr(), M, K, N, trans_b=trans_b)
     elif kind == "quantize":
         R, Cc = shape
         X = torch.empty((R, Cc), device="cuda").uniform_(-1, 1, generator=g)

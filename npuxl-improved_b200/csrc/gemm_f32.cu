@@ -20,6 +20,7 @@
 // The host (runtime.cpp) restates the reference's tile geometry for the
 // device's configuration; the kernel derives each element's form and its
 // store rounding (store_c, :43-50) from that geometry.
+#include <atomic>
 #include <cstdint>
 
 #include "common.cuh"
@@ -28,7 +29,7 @@ namespace vnpu_b200 {
 namespace {
 
 constexpr int kF32Threads = 256;
-constexpr int kF32BK = 8;          // k per shared-memory stage
+constexpr int kF32BK = 16;         // k per shared-memory stage
 constexpr int kF32Panel = 128;     // packed-panel depth, kernels.cpp:247
 // packed kernel needs a 128 x tn float panel in 256 KiB + 64 B of scratch
 constexpr uint32_t kF32PanelMaxCols = (256u * 1024u + 64u) / (128u * 4u);
@@ -97,80 +98,186 @@ __device__ __forceinline__ float load_b(const MatmulF32 &p, uint32_t k, uint32_t
                      : p.B[static_cast<uint64_t>(k) * p.ldb + n];
 }
 
-// One CTA computes a BM x BN block of C; 16 x 16 threads, each TM x TN
-// outputs (rows ty*4.. and 64+ty*4.. when TM = 8).  A and B stages live in
-// shared memory k-major (As[k][m], Bs[k][n]) so the inner loop reads
-// float4s; the next stage is prefetched into registers while the current one
-// is consumed.
+// 4-byte asynchronous copy global -> shared; ok = false writes a zero.
+__device__ __forceinline__ void cp_async_4(float *smem_dst, const float *gmem_src, bool ok) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_addr(smem_dst)),
+                 "l"(gmem_src), "r"(ok ? 4 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int kPending>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kPending) : "memory");
+}
+
+// sm_100 two-lane FMA: d.lo = fma(a.lo, b.lo, c.lo), d.hi = fma(a.hi, b.hi,
+// c.hi), each rounded once like fmaf.  Half the issue slots of two FFMAs.
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float half_f32x2(uint64_t v, int hi) {
+    float lo_v, hi_v;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo_v), "=f"(hi_v) : "l"(v));
+    return hi ? hi_v : lo_v;
+}
+__device__ __forceinline__ uint64_t swap_f32x2(uint64_t v) {
+    return pack_f32x2(half_f32x2(v, 1), half_f32x2(v, 0));
+}
+
+template <int kMode> struct F32Shape {
+    static constexpr int BM = kMode == kF32Dot8 ? 64 : 128;   // CTA tile (square)
+    static constexpr int TM = BM / 16;                        // outputs per thread per axis
+    static constexpr int CH = kMode == kF32Dot8 ? 8 : 1;      // chains per output
+    static constexpr int LD = BM + 4;                         // padded stage row
+    static constexpr int STAGE_FLOATS = 2 * kF32BK * LD;      // A and B of one stage
+    static constexpr int MIN_CTAS = kMode == kF32Dot8 ? 1 : 2;
+};
+
+// Dynamic shared memory: two pipeline stages, then (kF32Block with packed
+// panels) one folded-panel value per output: fold[e][thread].
 template <int kMode>
-__global__ void __launch_bounds__(kF32Threads, 1) gemm_f32_kernel(MatmulF32 p) {
-    constexpr int BM = kMode == kF32Dot8 ? 64 : 128;
-    constexpr int BN = BM;
-    constexpr int TM = BM / 16, TN = BN / 16;
-    constexpr int LA = BM * kF32BK / kF32Threads;   // A elements per thread per stage
-    constexpr int LB = BN * kF32BK / kF32Threads;
-    constexpr int CH = kMode == kF32Dot8 ? 8 : 1;   // chains per output
-    __shared__ __align__(16) float As[2][kF32BK][BM + 4];
-    __shared__ __align__(16) float Bs[2][kF32BK][BN + 4];
+constexpr uint32_t f32_smem_bytes(bool folds) {
+    using S = F32Shape<kMode>;
+    return 4u * (2 * S::STAGE_FLOATS + (folds ? S::TM * S::TM * kF32Threads : 0));
+}
+
+// One CTA computes a BM x BM block of C; 16 x 16 threads, each TM x TM
+// outputs (rows ty*4.. and 64+ty*4.. when TM = 8, columns likewise).  Stages
+// of kF32BK k are copied straight into shared memory (k-major: As[k][m],
+// Bs[k][n]) by cp.async, double-buffered, so no registers hold prefetched
+// operands; each thread then walks the stage's k in order with its A/B
+// fragments double-buffered in registers.
+template <int kMode>
+__global__ void __launch_bounds__(kF32Threads, F32Shape<kMode>::MIN_CTAS)
+gemm_f32_kernel(MatmulF32 p) {
+    using S = F32Shape<kMode>;
+    constexpr int BM = S::BM, TM = S::TM, CH = S::CH, LD = S::LD;
+    constexpr int LOADS = BM * kF32BK / kF32Threads;   // elements per operand per thread
+    extern __shared__ __align__(16) float f32_smem[];
+    float *fold = f32_smem + 2 * S::STAGE_FLOATS;
 
     const int tid = threadIdx.x;
     const int tx = tid % 16, ty = tid / 16;
-    const uint32_t m_base = blockIdx.y * BM, n_base = blockIdx.x * BN;
+    const uint32_t m_base = blockIdx.y * BM, n_base = blockIdx.x * BM;
     auto row_of = [&](int i) -> uint32_t {
         return m_base + (TM == 8 ? (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4) : ty * 4 + i);
     };
     auto col_of = [&](int j) -> uint32_t {
-        return n_base + (TN == 8 ? (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4) : tx * 4 + j);
+        return n_base + (TM == 8 ? (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4) : tx * 4 + j);
     };
 
-    // Stage loader: element e of the BM x 8 (A) / 8 x BN (B) stage, mapped so
-    // consecutive threads walk the operand's contiguous dimension.
-    float ra[LA], rb[LB];
-    auto fetch = [&](uint32_t k0) {
-#pragma unroll
-        for (int q = 0; q < LA; ++q) {
-            const int e = tid + q * kF32Threads;
-            const int mm = p.trans_a ? e % BM : e / kF32BK;
-            const int kk = p.trans_a ? e / BM : e % kF32BK;
-            const uint32_t m = m_base + mm, k = k0 + kk;
-            ra[q] = (m < p.M && k < p.K) ? load_a(p, m, k) : 0.0f;
+    // Stage loader.  Element q of this thread's share of a stage sits at a
+    // fixed offset along one axis and steps along the other, so its global
+    // address is base + q * step and only k0 changes between stages.
+    // k-contiguous operand (A, or B^T): row = tid / BK + q * (threads / BK),
+    // k = tid % BK.  Otherwise: row = tid % BM, k = tid / BM + q * (threads / BM).
+    // ("row" is m for A and n for B; shared memory holds [k][row].)
+    struct Loader {
+        const float *g;      // element q = 0 of stage 0
+        uint64_t g_q, g_stage;
+        uint32_t s0, s_q;    // shared-memory float offsets
+        uint32_t var0, var_q, var_lim;  // the stepping coordinate must stay < var_lim
+        uint32_t fix, fix_lim;          // the fixed coordinate must stay < fix_lim
+        bool k_steps;        // the stepping coordinate is k (else the row)
+    };
+    auto make_loader = [&](const float *base, uint32_t ld, bool k_contig, uint32_t row_base,
+                           uint32_t rows, uint32_t soff) {
+        Loader l;
+        if (k_contig) {
+            const uint32_t r = tid / kF32BK, k = tid % kF32BK;
+            l.g = base + static_cast<uint64_t>(row_base + r) * ld + k;
+            l.g_q = static_cast<uint64_t>(kF32Threads / kF32BK) * ld;
+            l.g_stage = kF32BK;
+            l.s0 = soff + k * LD + r;
+            l.s_q = kF32Threads / kF32BK;
+            l.var0 = row_base + r;
+            l.var_q = kF32Threads / kF32BK;
+            l.var_lim = rows;
+            l.fix = k;
+            l.fix_lim = p.K;
+            l.k_steps = false;
+        } else {
+            const uint32_t r = tid % BM, k = tid / BM;
+            l.g = base + static_cast<uint64_t>(k) * ld + row_base + r;
+            l.g_q = static_cast<uint64_t>(kF32Threads / BM) * ld;
+            l.g_stage = static_cast<uint64_t>(kF32BK) * ld;
+            l.s0 = soff + k * LD + r;
+            l.s_q = (kF32Threads / BM) * LD;
+            l.var0 = k;
+            l.var_q = kF32Threads / BM;
+            l.var_lim = p.K;
+            l.fix = row_base + r;
+            l.fix_lim = rows;
+            l.k_steps = true;
         }
+        return l;
+    };
+    const Loader la = make_loader(p.A, p.lda, !p.trans_a, m_base, p.M, 0);
+    const Loader lb = make_loader(p.B, p.ldb, p.trans_b != 0, n_base, p.N, kF32BK * LD);
+    auto issue_operand = [&](const Loader &l, uint32_t t, float *stage, const float *fallback) {
+        const uint32_t k0 = t * kF32BK;
+        const float *g = l.g + t * l.g_stage;
+        // k0 shifts whichever coordinate is k
+        const uint32_t var0 = l.var0 + (l.k_steps ? k0 : 0);
+        const bool fix_ok = (l.fix + (l.k_steps ? 0 : k0)) < l.fix_lim;
 #pragma unroll
-        for (int q = 0; q < LB; ++q) {
-            const int e = tid + q * kF32Threads;
-            const int nn = p.trans_b ? e / kF32BK : e % BN;
-            const int kk = p.trans_b ? e % kF32BK : e / BN;
-            const uint32_t n = n_base + nn, k = k0 + kk;
-            rb[q] = (n < p.N && k < p.K) ? load_b(p, k, n) : 0.0f;
+        for (int q = 0; q < LOADS; ++q) {
+            const bool ok = fix_ok && var0 + q * l.var_q < l.var_lim;
+            cp_async_4(stage + l.s0 + q * l.s_q, ok ? g + q * l.g_q : fallback, ok);
         }
     };
-    auto deposit = [&](int buf) {
-#pragma unroll
-        for (int q = 0; q < LA; ++q) {
-            const int e = tid + q * kF32Threads;
-            const int mm = p.trans_a ? e % BM : e / kF32BK;
-            const int kk = p.trans_a ? e / BM : e % kF32BK;
-            As[buf][kk][mm] = ra[q];
-        }
-#pragma unroll
-        for (int q = 0; q < LB; ++q) {
-            const int e = tid + q * kF32Threads;
-            const int nn = p.trans_b ? e / kF32BK : e % BN;
-            const int kk = p.trans_b ? e % kF32BK : e / BN;
-            Bs[buf][kk][nn] = rb[q];
-        }
+    auto issue = [&](uint32_t t, int buf) {
+        float *stage = f32_smem + buf * S::STAGE_FLOATS;
+        issue_operand(la, t, stage, p.A);
+        issue_operand(lb, t, stage, p.B);
+        cp_async_commit();
     };
 
-    float acc[TM][TN][CH];
+    // Accumulators.  kF32Block keeps them as pairs for fma.rn.f32x2: for
+    // even i, j, pair[i/2][j/2][0] holds outputs (i, j) and (i+1, j+1) and
+    // pair[i/2][j/2][1] holds (i, j+1) and (i+1, j); output (i, j) is in
+    // slot (i % 2 != j % 2), half i % 2.  Every output still gets one fma per
+    // k, in k order.  The other modes keep CH floats per output.
+    constexpr bool kPaired = kMode == kF32Block;
+    float acc[kPaired ? 1 : TM][kPaired ? 1 : TM][CH];
+    uint64_t pair[kPaired ? TM / 2 : 1][kPaired ? TM / 2 : 1][2];
 #pragma unroll
-    for (int i = 0; i < TM; ++i)
+    for (int i = 0; i < (kPaired ? 1 : TM); ++i)
 #pragma unroll
-        for (int j = 0; j < TN; ++j)
+        for (int j = 0; j < (kPaired ? 1 : TM); ++j)
 #pragma unroll
             for (int c = 0; c < CH; ++c) acc[i][j][c] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < (kPaired ? TM / 2 : 1); ++i)
+#pragma unroll
+        for (int j = 0; j < (kPaired ? TM / 2 : 1); ++j) pair[i][j][0] = pair[i][j][1] = 0ull;
+    auto value = [&](int i, int j, int lane) -> float {
+        if constexpr (kPaired)
+            return half_f32x2(pair[i / 2][j / 2][(i & 1) != (j & 1)], i & 1);
+        else
+            return acc[i][j][lane];
+    };
+    auto clear = [&](int i, int j) {
+        if constexpr (kPaired) {
+            uint64_t &v = pair[i / 2][j / 2][(i & 1) != (j & 1)];
+            v = (i & 1) ? pack_f32x2(half_f32x2(v, 0), 0.0f) : pack_f32x2(0.0f, half_f32x2(v, 1));
+        } else {
+            acc[i][j][0] = 0.0f;
+        }
+    };
 
-    // Packed-panel rows (kF32Block only): bit i*TN+j set when the element's
-    // chain restarts every 128 k.  fold[] holds the folded panels.
+    // Packed-panel outputs (kF32Block only): bit i*TM+j set when the
+    // element's chain restarts every 128 k; its folded value lives in
+    // fold[(i*TM+j)*threads + tid].
     uint64_t panel_bits = 0;
     if (kMode == kF32Block && p.packed) {
 #pragma unroll
@@ -178,84 +285,140 @@ __global__ void __launch_bounds__(kF32Threads, 1) gemm_f32_kernel(MatmulF32 p) {
             const uint32_t m = row_of(i);
             if (m >= p.M || !panel_row(p, m)) continue;
 #pragma unroll
-            for (int j = 0; j < TN; ++j) {
+            for (int j = 0; j < TM; ++j) {
                 const uint32_t n = col_of(j);
-                if (n < p.N && panel_col(p, n)) panel_bits |= 1ull << (i * TN + j);
+                if (n < p.N && panel_col(p, n)) panel_bits |= 1ull << (i * TM + j);
             }
         }
     }
-    float fold[kMode == kF32Block ? TM : 1][kMode == kF32Block ? TN : 1];
-    if (kMode == kF32Block) {
-#pragma unroll
-        for (int i = 0; i < TM; ++i)
-#pragma unroll
-            for (int j = 0; j < TN; ++j) fold[i][j] = 0.0f;
-    }
 
-    // kF32Dot8 runs the 8-lane chains over whole stages only; the tail k >=
-    // K8 is summed after the horizontal add.
+    // One k step: fragments from shared memory, then the TM x TM chains.
+    auto load_frag = [&](const float *As, const float *Bs, int kk, float *a, float *b) {
+#pragma unroll
+        for (int h = 0; h < TM / 4; ++h) {
+            const float4 va = *reinterpret_cast<const float4 *>(&As[kk * LD + h * 64 + ty * 4]);
+            const float4 vb = *reinterpret_cast<const float4 *>(&Bs[kk * LD + h * 64 + tx * 4]);
+            a[h * 4 + 0] = va.x; a[h * 4 + 1] = va.y; a[h * 4 + 2] = va.z; a[h * 4 + 3] = va.w;
+            b[h * 4 + 0] = vb.x; b[h * 4 + 1] = vb.y; b[h * 4 + 2] = vb.z; b[h * 4 + 3] = vb.w;
+        }
+    };
+    // kF32Block: fragments as 64-bit pairs straight from shared memory.
+    auto load_frag2 = [&](const float *As, const float *Bs, int kk, uint64_t *a2, uint64_t *b2) {
+#pragma unroll
+        for (int h = 0; h < TM / 4; ++h) {
+            const ulonglong2 va = *reinterpret_cast<const ulonglong2 *>(&As[kk * LD + h * 64 + ty * 4]);
+            const ulonglong2 vb = *reinterpret_cast<const ulonglong2 *>(&Bs[kk * LD + h * 64 + tx * 4]);
+            a2[h * 2 + 0] = va.x; a2[h * 2 + 1] = va.y;
+            b2[h * 2 + 0] = vb.x; b2[h * 2 + 1] = vb.y;
+        }
+    };
+    auto step2 = [&](const uint64_t *a2, const uint64_t *b2) {
+#pragma unroll
+        for (int j = 0; j < TM / 2; ++j) {
+            const uint64_t bx = swap_f32x2(b2[j]);
+#pragma unroll
+            for (int i = 0; i < TM / 2; ++i) {
+                pair[i][j][0] = fma_f32x2(a2[i], b2[j], pair[i][j][0]);
+                pair[i][j][1] = fma_f32x2(a2[i], bx, pair[i][j][1]);
+            }
+        }
+    };
+    auto step = [&](const float *a, const float *b, int lane) {
+        if constexpr (kPaired) {
+            uint64_t a2[TM / 2], b2[TM / 2];
+#pragma unroll
+            for (int h = 0; h < TM / 2; ++h) {
+                a2[h] = pack_f32x2(a[2 * h], a[2 * h + 1]);
+                b2[h] = pack_f32x2(b[2 * h], b[2 * h + 1]);
+            }
+            step2(a2, b2);
+        } else {
+#pragma unroll
+            for (int i = 0; i < TM; ++i)
+#pragma unroll
+                for (int j = 0; j < TM; ++j) {
+                    if (kMode == kF32Unfused)
+                        acc[i][j][0] = __fadd_rn(acc[i][j][0], __fmul_rn(a[i], b[j]));
+                    else
+                        acc[i][j][lane] = __fmaf_rn(a[i], b[j], acc[i][j][lane]);
+                }
+        }
+    };
+
+    // kF32Dot8 runs the 8-lane chains over whole groups of 8 k only; the
+    // tail k >= K8 is summed after the horizontal add.
     const uint32_t k_main = kMode == kF32Dot8 ? p.K / 8 * 8 : p.K;
     const uint32_t stages = (k_main + kF32BK - 1) / kF32BK;
-    if (stages) {
-        fetch(0);
-        deposit(0);
-        __syncthreads();
-    }
+    if (stages) issue(0, 0);
     for (uint32_t t = 0; t < stages; ++t) {
-        const int buf = t & 1;
-        if (t + 1 < stages) fetch((t + 1) * kF32BK);
+        if (t + 1 < stages) {
+            issue(t + 1, (t + 1) & 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const float *As = f32_smem + (t & 1) * S::STAGE_FLOATS;
+        const float *Bs = As + kF32BK * LD;
         const uint32_t kcount = min(static_cast<uint32_t>(kF32BK), k_main - t * kF32BK);
+        if (kcount == kF32BK) {
+            // Two rolled halves of 8 k keep the loop body small enough for
+            // the instruction cache; fragments are double-buffered inside.
+#pragma unroll 1
+            for (int half = 0; half < kF32BK / 8; ++half) {
+                if constexpr (kPaired) {
+                    uint64_t a2[2][TM / 2], b2[2][TM / 2];
+                    load_frag2(As, Bs, half * 8, a2[0], b2[0]);
 #pragma unroll
-        for (int kk = 0; kk < kF32BK; ++kk) {
-            if (kk < static_cast<int>(kcount)) {
-                float a[TM], b[TN];
-#pragma unroll
-                for (int h = 0; h < TM / 4; ++h) {
-                    const float4 v = *reinterpret_cast<const float4 *>(&As[buf][kk][h * 64 + ty * 4]);
-                    a[h * 4 + 0] = v.x; a[h * 4 + 1] = v.y; a[h * 4 + 2] = v.z; a[h * 4 + 3] = v.w;
-                }
-#pragma unroll
-                for (int h = 0; h < TN / 4; ++h) {
-                    const float4 v = *reinterpret_cast<const float4 *>(&Bs[buf][kk][h * 64 + tx * 4]);
-                    b[h * 4 + 0] = v.x; b[h * 4 + 1] = v.y; b[h * 4 + 2] = v.z; b[h * 4 + 3] = v.w;
-                }
-#pragma unroll
-                for (int i = 0; i < TM; ++i)
-#pragma unroll
-                    for (int j = 0; j < TN; ++j) {
-                        if (kMode == kF32Unfused)
-                            acc[i][j][0] = __fadd_rn(acc[i][j][0], __fmul_rn(a[i], b[j]));
-                        else
-                            acc[i][j][kMode == kF32Dot8 ? kk : 0] =
-                                __fmaf_rn(a[i], b[j], acc[i][j][kMode == kF32Dot8 ? kk : 0]);
+                    for (int kk = 0; kk < 8; ++kk) {
+                        if (kk + 1 < 8)
+                            load_frag2(As, Bs, half * 8 + kk + 1, a2[(kk + 1) & 1], b2[(kk + 1) & 1]);
+                        step2(a2[kk & 1], b2[kk & 1]);
                     }
+                } else {
+                    float a[2][TM], b[2][TM];
+                    load_frag(As, Bs, half * 8, a[0], b[0]);
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        if (kk + 1 < 8)
+                            load_frag(As, Bs, half * 8 + kk + 1, a[(kk + 1) & 1], b[(kk + 1) & 1]);
+                        step(a[kk & 1], b[kk & 1], CH == 8 ? kk : 0);
+                    }
+                }
+            }
+        } else {
+#pragma unroll
+            for (int kk = 0; kk < kF32BK; ++kk) {
+                if (kk < static_cast<int>(kcount)) {
+                    float a[TM], b[TM];
+                    load_frag(As, Bs, kk, a, b);
+                    step(a, b, CH == 8 ? kk & 7 : 0);
+                }
             }
         }
         if (kMode == kF32Block && panel_bits) {
-            const uint32_t k_done = (t + 1) * kF32BK;
+            const uint32_t k_done = t * kF32BK + kcount;
             if (k_done % kF32Panel == 0 || t + 1 == stages) {
-                const bool first = k_done <= kF32Panel;
+                const bool first = k_done <= static_cast<uint32_t>(kF32Panel);
 #pragma unroll
                 for (int i = 0; i < TM; ++i)
 #pragma unroll
-                    for (int j = 0; j < TN; ++j) {
-                        if (!((panel_bits >> (i * TN + j)) & 1)) continue;
-                        const uint32_t m = row_of(i), n = col_of(j);
+                    for (int j = 0; j < TM; ++j) {
+                        if (!((panel_bits >> (i * TM + j)) & 1)) continue;
+                        float &f = fold[(i * TM + j) * kF32Threads + tid];
                         if (first) {
+                            const uint32_t m = row_of(i), n = col_of(j);
                             const float dst = p.beta != 0.0f
                                 ? p.C[static_cast<uint64_t>(m) * p.ldc + n] : 0.0f;
-                            fold[i][j] = store_panel(acc[i][j][0], p, n, dst);
+                            f = store_panel(value(i, j, 0), p, n, dst);
                         } else {
-                            fold[i][j] = __fmaf_rn(p.alpha, acc[i][j][0], fold[i][j]);
+                            f = __fmaf_rn(p.alpha, value(i, j, 0), f);
                         }
-                        acc[i][j][0] = 0.0f;
+                        clear(i, j);
                     }
             }
         }
-        if (t + 1 < stages) {
-            deposit(buf ^ 1);
-            __syncthreads();
-        }
+        __syncthreads();  // the next issue overwrites this stage's buffer
     }
 
     // Store.
@@ -264,7 +427,7 @@ __global__ void __launch_bounds__(kF32Threads, 1) gemm_f32_kernel(MatmulF32 p) {
         const uint32_t m = row_of(i);
         if (m >= p.M) continue;
 #pragma unroll
-        for (int j = 0; j < TN; ++j) {
+        for (int j = 0; j < TM; ++j) {
             const uint32_t n = col_of(j);
             if (n >= p.N) continue;
             float *dst = p.C + static_cast<uint64_t>(m) * p.ldc + n;
@@ -273,12 +436,12 @@ __global__ void __launch_bounds__(kF32Threads, 1) gemm_f32_kernel(MatmulF32 p) {
             if (culled(p, m, n)) {
                 out = store_culled(p, n, old);
             } else if (kMode == kF32Unfused) {
-                out = store_scalar(acc[i][j][0], p, n, old);
+                out = store_scalar(value(i, j, 0), p, n, old);
             } else if (kMode == kF32Dot8) {
-                const float s0 = __fadd_rn(acc[i][j][0], acc[i][j][4 % CH]);
-                const float s1 = __fadd_rn(acc[i][j][1 % CH], acc[i][j][5 % CH]);
-                const float s2 = __fadd_rn(acc[i][j][2 % CH], acc[i][j][6 % CH]);
-                const float s3 = __fadd_rn(acc[i][j][3 % CH], acc[i][j][7 % CH]);
+                const float s0 = __fadd_rn(value(i, j, 0), value(i, j, 4 % CH));
+                const float s1 = __fadd_rn(value(i, j, 1 % CH), value(i, j, 5 % CH));
+                const float s2 = __fadd_rn(value(i, j, 2 % CH), value(i, j, 6 % CH));
+                const float s3 = __fadd_rn(value(i, j, 3 % CH), value(i, j, 7 % CH));
                 float dot = __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
                 uint32_t k = k_main;
                 const uint32_t quad_end = k + (p.K - k) / 4 * 4;
@@ -286,14 +449,35 @@ __global__ void __launch_bounds__(kF32Threads, 1) gemm_f32_kernel(MatmulF32 p) {
                     dot = __fadd_rn(dot, __fmul_rn(load_a(p, m, k), load_b(p, k, n)));
                 for (; k < p.K; ++k) dot = __fmaf_rn(load_a(p, m, k), load_b(p, k, n), dot);
                 out = store_panel(dot, p, n, old);
-            } else if ((panel_bits >> (i * TN + j)) & 1) {
-                out = fold[i][j];
+            } else if ((panel_bits >> (i * TM + j)) & 1) {
+                out = fold[(i * TM + j) * kF32Threads + tid];
             } else {
-                out = store_block(acc[i][j][0], p, n, old);
+                out = store_block(value(i, j, 0), p, n, old);
             }
             *dst = out;
         }
     }
+}
+
+template <int kMode>
+cudaError_t launch_f32(const LaunchCtx &ctx, const MatmulF32 &p, dim3 grid) {
+    const bool folds = kMode == kF32Block && p.packed;
+    const uint32_t smem = f32_smem_bytes<kMode>(folds);
+    // Opt in to the largest size once per device.
+    static std::atomic<uint64_t> opted{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(opted.load() & bit)) {
+        e = cudaFuncSetAttribute(gemm_f32_kernel<kMode>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(f32_smem_bytes<kMode>(true)));
+        if (e != cudaSuccess) return e;
+        opted.fetch_or(bit);
+    }
+    gemm_f32_kernel<kMode><<<grid, kF32Threads, smem, ctx.stream>>>(p);
+    return cudaGetLastError();
 }
 
 }  // namespace
@@ -305,14 +489,15 @@ cudaError_t matmul_f32(const LaunchCtx &ctx, const MatmulF32 &p) {
     const uint64_t gx = (p.N + bm - 1) / bm, gy = (p.M + bm - 1) / bm;
     if (gx > 0x7fffffffull || gy > 65535ull) return cudaErrorInvalidValue;
     const dim3 grid(static_cast<uint32_t>(gx), static_cast<uint32_t>(gy));
+    cudaError_t e;
     switch (p.mode) {
-    case kF32Block: gemm_f32_kernel<kF32Block><<<grid, kF32Threads, 0, ctx.stream>>>(p); break;
-    case kF32Unfused: gemm_f32_kernel<kF32Unfused><<<grid, kF32Threads, 0, ctx.stream>>>(p); break;
-    case kF32Dot8: gemm_f32_kernel<kF32Dot8><<<grid, kF32Threads, 0, ctx.stream>>>(p); break;
+    case kF32Block: e = launch_f32<kF32Block>(ctx, p, grid); break;
+    case kF32Unfused: e = launch_f32<kF32Unfused>(ctx, p, grid); break;
+    case kF32Dot8: e = launch_f32<kF32Dot8>(ctx, p, grid); break;
     default: return cudaErrorInvalidValue;
     }
     count_launch(ctx);
-    return cudaGetLastError();
+    return e;
 }
 
 }  // namespace vnpu_b200
