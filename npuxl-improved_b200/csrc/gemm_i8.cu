@@ -1108,9 +1108,6 @@ __global__ void __launch_bounds__(kSkThreads, kMinBlocks)
 // M <= 8 decode GEMV
 // ===========================================================================
 
-constexpr int kGvThreads = 256;
-constexpr int kGvColsPerWarp = 2;
-constexpr int kGvColsPerCta = (kGvThreads / 32) * kGvColsPerWarp;
 
 struct GvParams {
     const int8_t *A;
@@ -1140,10 +1137,14 @@ __device__ __forceinline__ int4 load_a16(const GvParams &p, uint32_t m, uint32_t
                      static_cast<int>(w[3]));
 }
 
-template <int kM, bool kAligned>
-__global__ void __launch_bounds__(kGvThreads) gemv_i8_kernel(const GvParams p) {
+// kCols columns per warp, kUnroll 512-byte K chunks of each in flight per
+// lane.  One row fragment of A (16 bytes per row) serves all kCols columns,
+// so more columns per warp cut the L1 traffic of A for M > 1.
+template <int kM, bool kAligned, int kCols, int kUnroll, int kThreads>
+__global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const GvParams p) {
+    constexpr int kGvColsPerWarp = kCols;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t n_first = blockIdx.x * kGvColsPerCta + warp * kGvColsPerWarp;
+    const uint32_t n_first = blockIdx.x * (kThreads / 32 * kCols) + warp * kGvColsPerWarp;
     int32_t acc[kGvColsPerWarp][kM];
 #pragma unroll
     for (int c = 0; c < kGvColsPerWarp; ++c)
@@ -1156,9 +1157,9 @@ __global__ void __launch_bounds__(kGvThreads) gemv_i8_kernel(const GvParams p) {
         const uint32_t n = min(n_first + c, p.N - 1);
         bcol[c] = reinterpret_cast<const int4 *>(p.Bt + static_cast<uint64_t>(n) * p.k_stride);
     }
-    // Each lane owns 16 bytes of every 512-byte K chunk; 8 chunks (4 KiB of
-    // each column) in flight, so K <= 4096 is a single DRAM round trip.
-    constexpr uint32_t kUnroll = 8;
+    // Each lane owns 16 bytes of every 512-byte K chunk; kUnroll chunks of
+    // each column in flight (M = 1: 8 chunks, 4 KiB, so K <= 4096 is one DRAM
+    // round trip).
     const uint32_t k_end = p.K;
     pdl_launch_dependents();
     bool waited = false;
@@ -1307,9 +1308,14 @@ GvParams gv_params(const MatmulI8 &p) {
 
 template <int kM>
 cudaError_t launch_gemv_m(const LaunchCtx &ctx, const GvParams &g, bool aligned) {
+    // 2 columns per warp, 8 chunks in flight, 256 threads.  (4 columns per
+    // warp with 4 chunks and 128 threads measured 1.6-3.4x slower for
+    // M = 2..8; the tensor-core GEMV takes those rows anyway.)
+    constexpr int kCols = 2, kUnroll = 8, kThreads = 256;
+    constexpr int kColsPerCta = kThreads / 32 * kCols;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((g.N + kGvColsPerCta - 1) / kGvColsPerCta, 1, 1);
-    cfg.blockDim = dim3(kGvThreads, 1, 1);
+    cfg.gridDim = dim3((g.N + kColsPerCta - 1) / kColsPerCta, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.stream = ctx.stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1317,8 +1323,9 @@ cudaError_t launch_gemv_m(const LaunchCtx &ctx, const GvParams &g, bool aligned)
     cfg.attrs = attr;
     cfg.numAttrs = std::getenv("VNPU_B200_NO_PDL") ? 0 : 1;
     g_last_kernel.store("gemv_i8_kernel", std::memory_order_relaxed);
-    if (aligned) return cudaLaunchKernelEx(&cfg, gemv_i8_kernel<kM, true>, g);
-    return cudaLaunchKernelEx(&cfg, gemv_i8_kernel<kM, false>, g);
+    if (aligned)
+        return cudaLaunchKernelEx(&cfg, gemv_i8_kernel<kM, true, kCols, kUnroll, kThreads>, g);
+    return cudaLaunchKernelEx(&cfg, gemv_i8_kernel<kM, false, kCols, kUnroll, kThreads>, g);
 }
 
 // Driver entry point for cuTensorMapEncodeTiled, resolved once.
