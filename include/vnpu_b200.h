@@ -141,6 +141,79 @@ typedef struct vnpu_b200_matmul_i8_scatter_args_t {
     uint32_t epilogue;
 } vnpu_b200_matmul_i8_scatter_args_t;
 
+/*
+ * QKV projection with RoPE and the KV-cache append in its epilogue (the
+ * reference builds this from MATMUL_I8, a host split into head-major Q/K/V,
+ * ROPE_F32 and a cache copy, tools/llm_bench.cpp:256-311).  Same bits as
+ * MATMUL_I8 of A (T x K) with the packed QKV weights B (N = 3 * heads *
+ * head_dim, columns [Q | K | V], each head-contiguous), then ROPE_F32
+ * (non-interleaved, theta_base / scaling as vnpu_rope_f32_args_t) of the Q and
+ * K parts, then VNPU_B200_OP_KV_APPEND of K and V.  Token t has position
+ * p = pos + t, pos being *position (device int32, read when the command runs)
+ * or position_offset when position is NULL: p is both its rotation position
+ * and its cache slot.
+ *   Q       [heads][T][head_dim]    rotated queries (required)
+ *   K_out   [heads][T][head_dim]    rotated keys, or NULL
+ *   V_out   [heads][T][head_dim]    values, or NULL
+ *   K_cache, V_cache [heads][capacity][head_dim], mask [heads][capacity]
+ *           (mask may be NULL): slot p of every head written, mask slot 0.
+ * head_dim even, <= 512.  Slots outside the capacity are not written (the
+ * stream's device error).  One kernel when T = 1 (the decode step's GEMV
+ * computes each rotation pair in one warp); otherwise MATMUL_I8 plus one
+ * split / rotate / append kernel.
+ */
+#define VNPU_B200_OP_QKV_ROPE_APPEND  0x104u
+
+typedef struct vnpu_b200_qkv_rope_append_args_t {
+    const int8_t *A;
+    vnpu_packed_weights_t *B;
+    const float *scale_a;
+    const float *bias;
+    float *Q;
+    float *K_out;
+    float *V_out;
+    float *K_cache;
+    float *V_cache;
+    float *mask;
+    const int32_t *position;
+    uint32_t T;
+    uint32_t K;
+    uint32_t heads;
+    uint32_t head_dim;
+    uint32_t capacity;
+    uint32_t position_offset;
+    float theta_base;   /* <= 0: 10000 */
+    float scaling;      /* <= 0: 1 */
+    uint32_t epilogue;  /* MATMUL_I8 epilogue of the projection */
+    uint32_t reserved0;
+} vnpu_b200_qkv_rope_append_args_t;
+
+/*
+ * MATMUL_I8 plus a residual: C = R + matmul_i8(A, B) with one rounding of the
+ * sum, the bits of ADD_F32 (alpha = beta = 1) of R and the MATMUL_I8 output
+ * (the decoder block's x + proj, tools/llm_bench.cpp:296-326).  R may be C
+ * (in place).  M <= 8 with a 16-byte aligned A runs it in the GEMV's
+ * epilogue; other shapes run MATMUL_I8 into C and then the addition.
+ */
+#define VNPU_B200_OP_MATMUL_I8_RESIDUAL  0x105u
+
+typedef struct vnpu_b200_matmul_i8_residual_args_t {
+    const int8_t *A;
+    vnpu_packed_weights_t *B;
+    const float *scale_a;
+    const float *bias;
+    const float *R;     /* M x N residual, row stride ldr */
+    float *C;
+    uint32_t M;
+    uint32_t K;
+    uint32_t N;
+    uint32_t lda;       /* 0 = K */
+    uint32_t ldr;       /* 0 = N */
+    uint32_t ldc;       /* 0 = N */
+    uint32_t epilogue;
+    uint32_t reserved0;
+} vnpu_b200_matmul_i8_residual_args_t;
+
 /* CUDA IPC between the processes of one node (for scatter destinations):
  * get_handle exports the cudaMalloc allocation whose base is device_ptr
  * (vnpu_buffer_alloc memory qualifies) as 64 opaque bytes; open maps such a

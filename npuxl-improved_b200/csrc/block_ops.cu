@@ -33,6 +33,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ 
                                                       const float *__restrict__ W,
                                                       float *__restrict__ Y, uint32_t rows,
                                                       uint32_t cols, float eps) {
+    pdl_enter();
     const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint32_t lane = threadIdx.x & 31;
     if (warp >= rows) return;
@@ -104,6 +105,7 @@ __device__ __forceinline__ float stage_row_rms_inv(const float *__restrict__ x, 
 __global__ void __launch_bounds__(kRmsRowThreads) rmsnorm_row_kernel(
     const float *__restrict__ X, const float *__restrict__ W, float *__restrict__ Y,
     uint32_t cols, float eps, bool vec) {
+    pdl_enter();
     extern __shared__ __align__(16) float xs[];
     __shared__ float inv_sh;
     const uint32_t tid = threadIdx.x;
@@ -181,6 +183,7 @@ __device__ __forceinline__ void fq_quantize_slice(const float *ys, uint32_t c0, 
 __global__ void __launch_bounds__(kFqThreads) rmsnorm_quantize_kernel(
     const float *__restrict__ X, const float *__restrict__ W, float *__restrict__ Y,
     int8_t *__restrict__ Q, float *__restrict__ scales, uint32_t cols, float eps, bool vec) {
+    pdl_enter();
     extern __shared__ __align__(16) float xs[];   // the whole row
     __shared__ __align__(16) float maxes[kFqMaxCluster];
     __shared__ float inv_sh;
@@ -220,6 +223,7 @@ __global__ void __launch_bounds__(kFqThreads) rmsnorm_quantize_kernel(
 __global__ void __launch_bounds__(kFqThreads) swiglu_quantize_kernel(
     const float *__restrict__ G, const float *__restrict__ U, float *__restrict__ Y,
     int8_t *__restrict__ Q, float *__restrict__ scales, uint32_t cols, float alpha) {
+    pdl_enter();
     extern __shared__ __align__(16) float ys[];   // this CTA's slice
     __shared__ __align__(16) float maxes[kFqMaxCluster];
     __shared__ float red[32];
@@ -276,6 +280,7 @@ __global__ void rope_kernel(float *__restrict__ Q, float *__restrict__ K,
                             uint32_t q_seq, uint32_t k_seq, uint32_t head_dim,
                             uint32_t position_offset, uint32_t interleaved, float scaling,
                             const RopeFreq freq) {
+    pdl_enter();
     const uint32_t pairs = head_dim / 2;
     const uint32_t seq = max(q_seq, k_seq);
     const uint64_t total = static_cast<uint64_t>(bh_count) * seq * pairs;
@@ -302,6 +307,7 @@ __global__ void rope_kernel(float *__restrict__ Q, float *__restrict__ K,
 // ---------------------------------------------------------------------------
 __global__ void swiglu_kernel(const float *__restrict__ G, const float *__restrict__ U,
                               float *__restrict__ Y, uint64_t n, float alpha) {
+    pdl_enter();
     for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
         const float g = G[i];
@@ -312,6 +318,7 @@ __global__ void swiglu_kernel(const float *__restrict__ G, const float *__restri
 
 __global__ void swiglu_vec_kernel(const float4 *__restrict__ G, const float4 *__restrict__ U,
                                   float4 *__restrict__ Y, uint64_t n4, float alpha) {
+    pdl_enter();
     for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n4;
          i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
         const float4 g = G[i], u = U[i];
@@ -326,6 +333,7 @@ __global__ void swiglu_vec_kernel(const float4 *__restrict__ G, const float4 *__
 
 __global__ void add_kernel(const float *__restrict__ A, const float *__restrict__ B,
                            float *__restrict__ Y, uint64_t n, float alpha, float beta) {
+    pdl_enter();
     for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
         Y[i] = __fmaf_rn(A[i], alpha, __fmul_rn(B[i], beta));
@@ -333,6 +341,7 @@ __global__ void add_kernel(const float *__restrict__ A, const float *__restrict_
 
 __global__ void add_vec_kernel(const float4 *__restrict__ A, const float4 *__restrict__ B,
                                float4 *__restrict__ Y, uint64_t n4, float alpha, float beta) {
+    pdl_enter();
     for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n4;
          i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
         const float4 a = A[i], b = B[i];
@@ -389,6 +398,7 @@ struct AttParams {
 // softmax state lives in registers and the two phases need no block barrier.
 template <bool VEC>
 __global__ void __launch_bounds__(kAttThreads) attention_kernel(const AttParams p) {
+    pdl_enter();
     extern __shared__ float att_smem[];
     const uint32_t D = p.D;
     const uint32_t chains = D / 8, full = chains * 8, tail = D - full;
@@ -609,6 +619,7 @@ __device__ __forceinline__ float hsum256_chains(const float (&c)[8]) {
 }
 
 __global__ void __launch_bounds__(kApThreads, 2) attention_prefill_kernel(const AttParams p) {
+    pdl_enter();
     extern __shared__ __align__(16) float ap_smem[];
     float *Qs = ap_smem;                       // [16][kApRow]
     float *Ks = Qs + kAttBQ * kApRow;          // [64][kApRow]
@@ -806,6 +817,7 @@ constexpr uint32_t kDecThreads = 512;
 constexpr uint32_t kDecMaxKeys = 8192;
 
 __global__ void __launch_bounds__(kDecThreads) attention_decode_kernel(const AttParams p) {
+    pdl_enter();
     extern __shared__ float dec_smem[];
     const uint32_t D = p.D;
     const uint32_t chains = D / 8, full = chains * 8, tail = D - full;
@@ -1012,6 +1024,7 @@ __device__ __forceinline__ float dot_hsum256(const float *qs, const float *krow,
 
 __global__ void __cluster_dims__(kDcCluster, 1, 1) __launch_bounds__(kDcThreads)
     attention_decode_cluster_kernel(const AttParams p) {
+    pdl_enter();
     extern __shared__ __align__(16) float dc_smem[];
     const uint32_t D = p.D, L = p.seq_k;
     const uint32_t nblk = (L + kAttBK - 1) / kAttBK;
@@ -1135,12 +1148,66 @@ __global__ void __cluster_dims__(kDcCluster, 1, 1) __launch_bounds__(kDcThreads)
     }
 }
 
+// QKV split + RoPE + KV append for T tokens (VNPU_B200_OP_QKV_ROPE_APPEND,
+// T > 1): one thread per (token, part, head, rotation pair) reads the two
+// columns of the MATMUL_I8 output C [T][3*heads*D], rotates Q and K exactly as
+// rope_kernel does and writes the head-major outputs and the cache slot.
+__global__ void qkv_split_rope_append_kernel(const float *__restrict__ C, uint32_t T,
+                                             float *__restrict__ Q, float *__restrict__ Kout,
+                                             float *__restrict__ Vout, float *__restrict__ Kc,
+                                             float *__restrict__ Vc, float *__restrict__ mask,
+                                             const int32_t *__restrict__ position,
+                                             uint32_t heads, uint32_t D, uint32_t cap,
+                                             uint32_t pos0, float scaling, const RopeFreq freq,
+                                             uint32_t *err) {
+    pdl_enter();
+    const uint32_t half = D / 2;
+    const uint64_t per_token = 3ull * heads * half;
+    const uint64_t total = per_token * T;
+    const int32_t base = position ? *position : static_cast<int32_t>(pos0);
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t t = static_cast<uint32_t>(i / per_token);
+        const uint32_t r = static_cast<uint32_t>(i - static_cast<uint64_t>(t) * per_token);
+        const uint32_t sec = r / (heads * half);
+        const uint32_t hj = r - sec * heads * half;
+        const uint32_t h = hj / half, j = hj - h * half;
+        const float *row = C + static_cast<uint64_t>(t) * 3 * heads * D + sec * heads * D + h * D;
+        float x0 = row[j], x1 = row[j + half];
+        const int32_t pos = base + static_cast<int32_t>(t);
+        if (sec < 2) {
+            float v[2] = {x0, x1};
+            rotate_pair(v, 0, 1, __fmul_rn(__fmul_rn(static_cast<float>(pos), scaling), freq.inv[j]));
+            x0 = v[0];
+            x1 = v[1];
+        }
+        const uint64_t o = (static_cast<uint64_t>(h) * T + t) * D + j;
+        float *out = sec == 0 ? Q : (sec == 1 ? Kout : Vout);
+        if (out) {
+            out[o] = x0;
+            out[o + half] = x1;
+        }
+        if (sec == 0) continue;
+        if (pos < 0 || static_cast<uint32_t>(pos) >= cap) {
+            if (sec == 1 && j == 0) record_error(err, kErrBadConfig);
+            continue;
+        }
+        const uint64_t c = (static_cast<uint64_t>(h) * cap + static_cast<uint32_t>(pos)) * D + j;
+        float *cache = sec == 1 ? Kc : Vc;
+        cache[c] = x0;
+        cache[c + half] = x1;
+        if (sec == 1 && j == 0 && mask)
+            mask[static_cast<uint64_t>(h) * cap + static_cast<uint32_t>(pos)] = 0.0f;
+    }
+}
+
 // KV-cache append: element (h, t, d) of K/V goes to slot pos + t of head h.
 __global__ void kv_append_kernel(const float *__restrict__ K, const float *__restrict__ V,
                                  float *__restrict__ Kc, float *__restrict__ Vc,
                                  float *__restrict__ mask, const int32_t *__restrict__ position,
                                  uint32_t heads, uint32_t T, uint32_t D, uint32_t cap,
                                  uint32_t pos0, bool vec, uint32_t *err) {
+    pdl_enter();
     const int64_t pos = position ? static_cast<int64_t>(*position) : static_cast<int64_t>(pos0);
     const uint32_t w = vec ? D / 4 : D;   // units per (h, t) row
     const uint64_t total = static_cast<uint64_t>(heads) * T * w;
@@ -1206,10 +1273,10 @@ cudaError_t rmsnorm(const LaunchCtx &ctx, const float *X, const float *W, float 
         }
         const bool vec = cols % 8 == 0 && (reinterpret_cast<uintptr_t>(X) & 15u) == 0 &&
                          (reinterpret_cast<uintptr_t>(Y) & 15u) == 0;
-        rmsnorm_row_kernel<<<rows, kRmsRowThreads, smem, ctx.stream>>>(X, W, Y, cols, eps, vec);
+        VNPU_LAUNCH(launch_pdl(ctx.stream, rmsnorm_row_kernel, dim3(rows), dim3(kRmsRowThreads), smem, X, W, Y, cols, eps, vec));
     } else {
         const unsigned blocks = (rows + 7) / 8;
-        rmsnorm_kernel<<<blocks, 256, 0, ctx.stream>>>(X, W, Y, rows, cols, eps);
+        VNPU_LAUNCH(launch_pdl(ctx.stream, rmsnorm_kernel, dim3(blocks), dim3(256), 0, X, W, Y, rows, cols, eps));
     }
     count_launch(ctx);
     return cudaGetLastError();
@@ -1242,13 +1309,15 @@ cudaError_t launch_fq(const LaunchCtx &ctx, Kernel kernel, uint32_t rows, uint32
     cfg.blockDim = dim3(kFqThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = ctx.stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = csize;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_allowed() ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 }  // namespace
@@ -1284,9 +1353,24 @@ cudaError_t rope(const LaunchCtx &ctx, float *Q, float *K, const int32_t *positi
     for (uint32_t j = 0; j < head_dim / 2; ++j) f.inv[j] = inv_freq_host[j];
     const uint64_t total = static_cast<uint64_t>(batch) * heads * (q_seq > k_seq ? q_seq : k_seq) *
                            (head_dim / 2);
-    rope_kernel<<<grid_for(total, ctx.num_sms, 256), 256, 0, ctx.stream>>>(
+    VNPU_LAUNCH(launch_pdl(ctx.stream, rope_kernel, dim3(grid_for(total, ctx.num_sms, 256)), dim3(256), 0, 
         Q, K, positions, batch * heads, q_seq, k_seq, head_dim, position_offset, interleaved,
-        scaling, f);
+        scaling, f));
+    count_launch(ctx);
+    return cudaGetLastError();
+}
+
+cudaError_t qkv_split_rope_append(const LaunchCtx &ctx, const float *C, uint32_t T,
+                                  const QkvRope &q) {
+    if (q.head_dim == 0 || (q.head_dim & 1u) || q.head_dim / 2 > kRopeMaxPairs || T == 0)
+        return cudaErrorInvalidValue;
+    RopeFreq f;
+    for (uint32_t j = 0; j < q.head_dim / 2; ++j) f.inv[j] = q.inv_freq[j];
+    const uint64_t total = 3ull * q.heads * (q.head_dim / 2) * T;
+    VNPU_LAUNCH(launch_pdl(ctx.stream, qkv_split_rope_append_kernel,
+                           dim3(grid_for(total, ctx.num_sms, 256)), dim3(256), 0, C, T, q.Q,
+                           q.K_out, q.V_out, q.K_cache, q.V_cache, q.mask, q.position, q.heads,
+                           q.head_dim, q.capacity, q.position_offset, q.scaling, f, ctx.err));
     count_launch(ctx);
     return cudaGetLastError();
 }
@@ -1297,12 +1381,12 @@ cudaError_t swiglu(const LaunchCtx &ctx, const float *gate, const float *up, flo
                      (reinterpret_cast<uintptr_t>(up) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(Y) & 15) == 0;
     if (vec)
-        swiglu_vec_kernel<<<grid_for(count / 4, ctx.num_sms, 256), 256, 0, ctx.stream>>>(
+        VNPU_LAUNCH(launch_pdl(ctx.stream, swiglu_vec_kernel, dim3(grid_for(count / 4, ctx.num_sms, 256)), dim3(256), 0, 
             reinterpret_cast<const float4 *>(gate), reinterpret_cast<const float4 *>(up),
-            reinterpret_cast<float4 *>(Y), count / 4, alpha);
+            reinterpret_cast<float4 *>(Y), count / 4, alpha));
     else
-        swiglu_kernel<<<grid_for(count, ctx.num_sms, 256), 256, 0, ctx.stream>>>(gate, up, Y,
-                                                                                 count, alpha);
+        VNPU_LAUNCH(launch_pdl(ctx.stream, swiglu_kernel, dim3(grid_for(count, ctx.num_sms, 256)), dim3(256), 0, gate, up, Y,
+                                                                                 count, alpha));
     count_launch(ctx);
     return cudaGetLastError();
 }
@@ -1313,12 +1397,12 @@ cudaError_t add(const LaunchCtx &ctx, const float *A, const float *B, float *Y, 
                      (reinterpret_cast<uintptr_t>(B) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(Y) & 15) == 0;
     if (vec)
-        add_vec_kernel<<<grid_for(count / 4, ctx.num_sms, 256), 256, 0, ctx.stream>>>(
+        VNPU_LAUNCH(launch_pdl(ctx.stream, add_vec_kernel, dim3(grid_for(count / 4, ctx.num_sms, 256)), dim3(256), 0, 
             reinterpret_cast<const float4 *>(A), reinterpret_cast<const float4 *>(B),
-            reinterpret_cast<float4 *>(Y), count / 4, alpha, beta);
+            reinterpret_cast<float4 *>(Y), count / 4, alpha, beta));
     else
-        add_kernel<<<grid_for(count, ctx.num_sms, 256), 256, 0, ctx.stream>>>(A, B, Y, count,
-                                                                              alpha, beta);
+        VNPU_LAUNCH(launch_pdl(ctx.stream, add_kernel, dim3(grid_for(count, ctx.num_sms, 256)), dim3(256), 0, A, B, Y, count,
+                                                                              alpha, beta));
     count_launch(ctx);
     return cudaGetLastError();
 }
@@ -1374,8 +1458,7 @@ cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, cons
             if (e != cudaSuccess) return e;
             dc_configured[dev] = true;
         }
-        attention_decode_cluster_kernel<<<batch * heads * kDcCluster, kDcThreads, dc_smem,
-                                          ctx.stream>>>(ap);
+        VNPU_LAUNCH(launch_pdl(ctx.stream, attention_decode_cluster_kernel, dim3(batch * heads * kDcCluster), dim3(kDcThreads), dc_smem, ap));
         count_launch(ctx);
         return cudaGetLastError();
     }
@@ -1391,7 +1474,7 @@ cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, cons
             if (e != cudaSuccess) return e;
             dec_configured[dev] = true;
         }
-        attention_decode_kernel<<<batch * heads, kDecThreads, dsmem, ctx.stream>>>(ap);
+        VNPU_LAUNCH(launch_pdl(ctx.stream, attention_decode_kernel, dim3(batch * heads), dim3(kDecThreads), dsmem, ap));
         count_launch(ctx);
         return cudaGetLastError();
     }
@@ -1410,14 +1493,14 @@ cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, cons
             if (e != cudaSuccess) return e;
             ap_configured[dev] = true;
         }
-        attention_prefill_kernel<<<grid, kApThreads, ap_smem, ctx.stream>>>(ap);
+        VNPU_LAUNCH(launch_pdl(ctx.stream, attention_prefill_kernel, dim3(grid), dim3(kApThreads), ap_smem, ap));
         count_launch(ctx);
         return cudaGetLastError();
     }
     if (vec)
-        attention_kernel<true><<<grid, kAttThreads, smem, ctx.stream>>>(ap);
+        VNPU_LAUNCH(launch_pdl(ctx.stream, attention_kernel<true>, dim3(grid), dim3(kAttThreads), smem, ap));
     else
-        attention_kernel<false><<<grid, kAttThreads, smem, ctx.stream>>>(ap);
+        VNPU_LAUNCH(launch_pdl(ctx.stream, attention_kernel<false>, dim3(grid), dim3(kAttThreads), smem, ap));
     count_launch(ctx);
     return cudaGetLastError();
 }
@@ -1430,9 +1513,9 @@ cudaError_t kv_append(const LaunchCtx &ctx, const float *K, const float *V, floa
                        reinterpret_cast<uintptr_t>(K_cache) | reinterpret_cast<uintptr_t>(V_cache)) &
                       15u) == 0;
     const uint64_t total = static_cast<uint64_t>(heads) * T * (vec ? head_dim / 4 : head_dim);
-    kv_append_kernel<<<grid_for(total, ctx.num_sms, 256), 256, 0, ctx.stream>>>(
+    VNPU_LAUNCH(launch_pdl(ctx.stream, kv_append_kernel, dim3(grid_for(total, ctx.num_sms, 256)), dim3(256), 0, 
         K, V, K_cache, V_cache, mask, position, heads, T, head_dim, capacity, position_offset, vec,
-        ctx.err);
+        ctx.err));
     count_launch(ctx);
     return cudaGetLastError();
 }

@@ -12,6 +12,8 @@
 #pragma once
 
 #include <cstdint>
+#include <cstdlib>
+#include <utility>
 #include <cuda_runtime.h>
 
 #include "kernels.h"
@@ -455,6 +457,42 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 }
 __device__ __forceinline__ void pdl_wait_previous() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// Programmatic dependent launch at kernel entry: let the stream's next kernel
+// be scheduled now (its CTAs then wait in their own pdl_enter), and wait
+// until the previous kernel has finished and its writes are visible.  Both
+// are no-ops for a kernel launched without the PDL attribute.
+__device__ __forceinline__ void pdl_enter() {
+    pdl_launch_dependents();
+    pdl_wait_previous();
+}
+
+// Host: launch a kernel that begins with pdl_enter() with programmatic
+// dependent launch allowed (VNPU_B200_NO_PDL turns it off), so a chain of
+// short dependent kernels hides its launch latency.
+inline bool pdl_allowed() {
+    static const bool allowed = std::getenv("VNPU_B200_NO_PDL") == nullptr;
+    return allowed;
+}
+#define VNPU_LAUNCH(expr)                                  \
+    do {                                                   \
+        const cudaError_t vnpu_launch_rc_ = (expr);        \
+        if (vnpu_launch_rc_ != cudaSuccess) return vnpu_launch_rc_; \
+    } while (0)
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(cudaStream_t stream, void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                              size_t smem, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_allowed() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // Arrive on an mbarrier of another CTA of the cluster.

@@ -27,6 +27,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <type_traits>
 #include <atomic>
 #include <mutex>
 
@@ -1140,11 +1141,59 @@ __device__ __forceinline__ int4 load_a16(const GvParams &p, uint32_t m, uint32_t
 // kCols columns per warp, kUnroll 512-byte K chunks of each in flight per
 // lane.  One row fragment of A (16 bytes per row) serves all kCols columns,
 // so more columns per warp cut the L1 traffic of A for M > 1.
-template <int kM, bool kAligned, int kCols, int kUnroll, int kThreads>
-__global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const GvParams p) {
+// Epilogue variants of the streaming GEMV (the extra kernel argument).
+struct GvPlain {};
+// C = R + out (VNPU_B200_OP_MATMUL_I8_RESIDUAL).
+struct GvResidual {
+    const float *R;
+    uint32_t ldr;
+};
+// QKV projection + RoPE + KV-cache append for one token
+// (VNPU_B200_OP_QKV_ROPE_APPEND): warp w computes rotation pair w, the
+// columns (j, j + D/2) of one head of the Q, K or V part.
+constexpr uint32_t kGvMaxPairs = 256;
+struct GvQkv {
+    float *Q, *Kout, *Vout, *Kc, *Vc, *mask;
+    const int32_t *position;
+    uint32_t *err;
+    uint32_t heads, D, cap, pos0;
+    float scaling;
+    float inv[kGvMaxPairs];   // 1 / theta^(2j/D), computed on the host like ROPE_F32
+};
+
+// The two columns a warp of the QKV variant owns.
+__device__ __forceinline__ void qkv_pair_columns(const GvQkv &x, uint32_t pair, uint32_t &sec,
+                                                 uint32_t &h, uint32_t &j, uint32_t &n0) {
+    const uint32_t half = x.D / 2, per_sec = x.heads * half;
+    sec = pair / per_sec;
+    const uint32_t r = pair - sec * per_sec;
+    h = r / half;
+    j = r - h * half;
+    n0 = sec * x.heads * x.D + h * x.D + j;
+}
+
+template <int kM, bool kAligned, int kCols, int kUnroll, int kThreads, typename Extra>
+__global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const GvParams p, const Extra x) {
+    constexpr bool kQkv = std::is_same<Extra, GvQkv>::value;
+    static_assert(!kQkv || (kM == 1 && kCols == 2), "the QKV epilogue is one token, column pairs");
     constexpr int kGvColsPerWarp = kCols;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t n_first = blockIdx.x * (kThreads / 32 * kCols) + warp * kGvColsPerWarp;
+    // Columns of this warp (QKV: a rotation pair, D/2 apart).
+    uint32_t ncol[kGvColsPerWarp];
+    uint32_t q_sec = 0, q_h = 0, q_j = 0;
+    bool warp_valid = true;
+    if constexpr (kQkv) {
+        const uint32_t pair = blockIdx.x * (kThreads / 32) + warp;
+        warp_valid = pair < 3 * x.heads * (x.D / 2);
+        uint32_t n0 = 0;
+        if (warp_valid) qkv_pair_columns(x, pair, q_sec, q_h, q_j, n0);
+        ncol[0] = n0;
+        ncol[1] = n0 + x.D / 2;
+    } else {
+#pragma unroll
+        for (int c = 0; c < kGvColsPerWarp; ++c) ncol[c] = n_first + c;
+    }
     int32_t acc[kGvColsPerWarp][kM];
 #pragma unroll
     for (int c = 0; c < kGvColsPerWarp; ++c)
@@ -1154,7 +1203,7 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const GvParams p) {
     const int4 *bcol[kGvColsPerWarp];
 #pragma unroll
     for (int c = 0; c < kGvColsPerWarp; ++c) {
-        const uint32_t n = min(n_first + c, p.N - 1);
+        const uint32_t n = min(ncol[c], p.N - 1);
         bcol[c] = reinterpret_cast<const int4 *>(p.Bt + static_cast<uint64_t>(n) * p.k_stride);
     }
     // Each lane owns 16 bytes of every 512-byte K chunk; kUnroll chunks of
@@ -1208,17 +1257,62 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const GvParams p) {
 
     if (!waited) pdl_wait_previous();
     const bool has_bias = p.bias != nullptr;
+    if constexpr (kQkv) {
+        // Lane 0 holds both columns of the pair: dequantize them as MATMUL_I8
+        // would, rotate Q/K as ROPE_F32 does, place them as KV_APPEND does.
+        if (lane != 0 || !warp_valid) return;
+        const float sa = p.scale_a ? __ldg(p.scale_a) : 1.0f;
+        float v[2];
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+            v[c] = ref_dequant(acc[c][0], sa, __ldg(p.scale_b + ncol[c]), has_bias,
+                               has_bias ? __ldg(p.bias + ncol[c]) : 0.0f, p.epilogue, p.form);
+        const int32_t pos = x.position ? *x.position : static_cast<int32_t>(x.pos0);
+        if (q_sec < 2) {
+            const float angle = __fmul_rn(__fmul_rn(static_cast<float>(pos), x.scaling), x.inv[q_j]);
+            float sn, cs;
+            sincosf(angle, &sn, &cs);
+            const float x0 = v[0], x1 = v[1];
+            v[0] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+            v[1] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+        }
+        const uint64_t row = static_cast<uint64_t>(q_h) * x.D + q_j;   // [h][t = 0][j]
+        const uint32_t half = x.D / 2;
+        if (q_sec == 0) {
+            x.Q[row] = v[0];
+            x.Q[row + half] = v[1];
+            return;
+        }
+        float *out = q_sec == 1 ? x.Kout : x.Vout;
+        if (out) {
+            out[row] = v[0];
+            out[row + half] = v[1];
+        }
+        if (pos < 0 || static_cast<uint32_t>(pos) >= x.cap) {
+            if (q_sec == 1 && q_j == 0) record_error(x.err, kErrBadConfig);
+            return;
+        }
+        const uint64_t slot = (static_cast<uint64_t>(q_h) * x.cap + static_cast<uint32_t>(pos)) * x.D + q_j;
+        float *cache = q_sec == 1 ? x.Kc : x.Vc;
+        cache[slot] = v[0];
+        cache[slot + half] = v[1];
+        if (q_sec == 1 && q_j == 0 && x.mask)
+            x.mask[static_cast<uint64_t>(q_h) * x.cap + static_cast<uint32_t>(pos)] = 0.0f;
+        return;
+    }
 #pragma unroll
     for (int c = 0; c < kGvColsPerWarp; ++c) {
-        const uint32_t n = n_first + c;
+        const uint32_t n = ncol[c];
         if (n >= p.N) continue;
 #pragma unroll
         for (int m = 0; m < kM; ++m) {
             if (static_cast<uint32_t>(m) == lane && static_cast<uint32_t>(m) < p.M) {
                 const float sa = p.scale_a ? __ldg(p.scale_a + m) : 1.0f;
-                p.C[static_cast<uint64_t>(m) * p.ldc + n] =
-                    ref_dequant(acc[c][m], sa, __ldg(p.scale_b + n), has_bias,
-                                has_bias ? __ldg(p.bias + n) : 0.0f, p.epilogue, p.form);
+                float out = ref_dequant(acc[c][m], sa, __ldg(p.scale_b + n), has_bias,
+                                        has_bias ? __ldg(p.bias + n) : 0.0f, p.epilogue, p.form);
+                if constexpr (std::is_same<Extra, GvResidual>::value)
+                    out = __fadd_rn(x.R[static_cast<uint64_t>(m) * x.ldr + n], out);
+                p.C[static_cast<uint64_t>(m) * p.ldc + n] = out;
             }
         }
     }
@@ -1306,8 +1400,9 @@ GvParams gv_params(const MatmulI8 &p) {
     return g;
 }
 
-template <int kM>
-cudaError_t launch_gemv_m(const LaunchCtx &ctx, const GvParams &g, bool aligned) {
+template <int kM, typename Extra = GvPlain>
+cudaError_t launch_gemv_m(const LaunchCtx &ctx, const GvParams &g, bool aligned,
+                          const Extra &x = Extra()) {
     // 2 columns per warp, 8 chunks in flight, 256 threads.  (4 columns per
     // warp with 4 chunks and 128 threads measured 1.6-3.4x slower for
     // M = 2..8; the tensor-core GEMV takes those rows anyway.)
@@ -1324,8 +1419,10 @@ cudaError_t launch_gemv_m(const LaunchCtx &ctx, const GvParams &g, bool aligned)
     cfg.numAttrs = std::getenv("VNPU_B200_NO_PDL") ? 0 : 1;
     g_last_kernel.store("gemv_i8_kernel", std::memory_order_relaxed);
     if (aligned)
-        return cudaLaunchKernelEx(&cfg, gemv_i8_kernel<kM, true, kCols, kUnroll, kThreads>, g);
-    return cudaLaunchKernelEx(&cfg, gemv_i8_kernel<kM, false, kCols, kUnroll, kThreads>, g);
+        return cudaLaunchKernelEx(&cfg, gemv_i8_kernel<kM, true, kCols, kUnroll, kThreads, Extra>,
+                                  g, x);
+    return cudaLaunchKernelEx(&cfg, gemv_i8_kernel<kM, false, kCols, kUnroll, kThreads, Extra>,
+                              g, x);
 }
 
 // Driver entry point for cuTensorMapEncodeTiled, resolved once.
@@ -1728,6 +1825,42 @@ cudaError_t matmul_i8_gemv(const LaunchCtx &ctx, const MatmulI8 &p) {
     case 4: e = launch_gemv_m<4>(ctx, g, aligned); break;
     default: e = launch_gemv_m<8>(ctx, g, aligned); break;
     }
+    count_launch(ctx);
+    return e;
+}
+
+cudaError_t matmul_i8_gemv_residual(const LaunchCtx &ctx, const MatmulI8 &p, const float *R,
+                                    uint32_t ldr) {
+    if (p.M != 1) return cudaErrorInvalidValue;
+    const GvParams g = gv_params(p);
+    const bool aligned = (reinterpret_cast<uintptr_t>(p.A) % 16u == 0u) && (p.lda % 16u == 0u);
+    const cudaError_t e = launch_gemv_m<1>(ctx, g, aligned, GvResidual{R, ldr});
+    count_launch(ctx);
+    return e;
+}
+
+cudaError_t qkv_rope_append_gemv(const LaunchCtx &ctx, const MatmulI8 &p, const QkvRope &q) {
+    if (p.M != 1 || q.head_dim == 0 || (q.head_dim & 1u) || q.head_dim / 2 > kGvMaxPairs ||
+        p.N != 3u * q.heads * q.head_dim)
+        return cudaErrorInvalidValue;
+    const GvParams g = gv_params(p);
+    const bool aligned = (reinterpret_cast<uintptr_t>(p.A) % 16u == 0u) && (p.lda % 16u == 0u);
+    GvQkv x;
+    x.Q = q.Q;
+    x.Kout = q.K_out;
+    x.Vout = q.V_out;
+    x.Kc = q.K_cache;
+    x.Vc = q.V_cache;
+    x.mask = q.mask;
+    x.position = q.position;
+    x.err = ctx.err;
+    x.heads = q.heads;
+    x.D = q.head_dim;
+    x.cap = q.capacity;
+    x.pos0 = q.position_offset;
+    x.scaling = q.scaling;
+    for (uint32_t j = 0; j < q.head_dim / 2; ++j) x.inv[j] = q.inv_freq[j];
+    const cudaError_t e = launch_gemv_m<1>(ctx, g, aligned, x);
     count_launch(ctx);
     return e;
 }

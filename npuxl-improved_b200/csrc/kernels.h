@@ -97,6 +97,30 @@ bool encode_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *bas
                     uint64_t dim1, uint64_t stride1_bytes, uint32_t box0, uint32_t box1,
                     CUtensorMapSwizzle swizzle);
 
+// QKV projection epilogue (VNPU_B200_OP_QKV_ROPE_APPEND): where the rotated
+// Q/K and the V of each token go.  Token t has position (*position or
+// position_offset) + t, used for the rotation and as its cache slot.
+struct QkvRope {
+    float *Q = nullptr;         // [heads][T][head_dim]
+    float *K_out = nullptr;     // [heads][T][head_dim] or NULL
+    float *V_out = nullptr;     // [heads][T][head_dim] or NULL
+    float *K_cache = nullptr;   // [heads][capacity][head_dim]
+    float *V_cache = nullptr;
+    float *mask = nullptr;      // [heads][capacity] or NULL
+    const int32_t *position = nullptr;
+    uint32_t heads = 0, head_dim = 0, capacity = 0, position_offset = 0;
+    float scaling = 1.0f;
+    const float *inv_freq = nullptr;   // host, head_dim/2 entries (ROPE_F32's table)
+};
+// One token (M = 1): the streaming GEMV with the rotation pairs in one warp.
+cudaError_t qkv_rope_append_gemv(const LaunchCtx &ctx, const MatmulI8 &p, const QkvRope &q);
+// Any T: C is the MATMUL_I8 output [T][3*heads*head_dim] already computed.
+cudaError_t qkv_split_rope_append(const LaunchCtx &ctx, const float *C, uint32_t T,
+                                  const QkvRope &q);
+// C = R + MATMUL_I8 for M = 1 in the GEMV's epilogue.
+cudaError_t matmul_i8_gemv_residual(const LaunchCtx &ctx, const MatmulI8 &p, const float *R,
+                                    uint32_t ldr);
+
 // ---- MATMUL_F32 (src/kernels/kernels.cpp:19-352,480-520) -----------------------
 // Accumulation form of the reference kernel a command's elements take
 // (gemm_f32.cu has the rules).

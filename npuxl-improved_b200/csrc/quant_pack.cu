@@ -27,6 +27,7 @@ __global__ void __launch_bounds__(kQThreads) quantize_rows_kernel(const float *_
                                                                   int8_t *__restrict__ Y,
                                                                   float *__restrict__ scales,
                                                                   uint64_t cols) {
+    pdl_enter();
     __shared__ float red[32];
     const uint64_t r = blockIdx.x;
     const float *x = X + r * cols;
@@ -200,11 +201,11 @@ cudaError_t quantize_rows(const LaunchCtx &ctx, const float *X, int8_t *Y, float
     const bool vec = (cols % 4 == 0) && (reinterpret_cast<uintptr_t>(X) % 16 == 0) &&
                      (reinterpret_cast<uintptr_t>(Y) % 4 == 0);
     if (vec)
-        quantize_rows_kernel<true><<<static_cast<unsigned>(rows), kQThreads, 0, ctx.stream>>>(
-            X, Y, scales, cols);
+        VNPU_LAUNCH(launch_pdl(ctx.stream, quantize_rows_kernel<true>, dim3(static_cast<unsigned>(rows)), dim3(kQThreads), 0, 
+            X, Y, scales, cols));
     else
-        quantize_rows_kernel<false><<<static_cast<unsigned>(rows), kQThreads, 0, ctx.stream>>>(
-            X, Y, scales, cols);
+        VNPU_LAUNCH(launch_pdl(ctx.stream, quantize_rows_kernel<false>, dim3(static_cast<unsigned>(rows)), dim3(kQThreads), 0, 
+            X, Y, scales, cols));
     count_launch(ctx);
     return cudaGetLastError();
 }

@@ -542,6 +542,17 @@ void exec_rmsnorm(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &
 }
 
 // src/core/scheduler.cpp:510-535 + rotate_vector's frequencies (llm.cpp:188-217)
+// RoPE inverse frequencies, src/kernels/llm.cpp:188-217: the same float libm
+// calls as the reference, evaluated once per pair on the host.
+void rope_inv_freq(float theta, uint32_t head_dim, bool interleaved, float *inv) {
+    for (uint32_t j = 0; j < head_dim / 2; ++j) {
+        const float expo = interleaved
+                               ? static_cast<float>(2 * j) / static_cast<float>(head_dim)
+                               : 2.0f * static_cast<float>(j) / static_cast<float>(head_dim);
+        inv[j] = 1.0f / std::pow(theta, expo);
+    }
+}
+
 void exec_rope(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &ctx,
                Accounting &acc) {
     const auto &a = cmd.args.rope;
@@ -551,15 +562,8 @@ void exec_rope(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx &ctx
     if (a.head_dim > 512) throw CommandError("rope head_dim above 512", VNPU_ERR_UNSUPPORTED);
     const float theta = a.theta_base > 0.0f ? a.theta_base : 10000.0f;
     const float scaling = a.scaling > 0.0f ? a.scaling : 1.0f;
-    // The same float libm calls as the reference, evaluated once per pair.
     float inv[256];
-    const uint32_t pairs = a.head_dim / 2;
-    for (uint32_t j = 0; j < pairs; ++j) {
-        const float expo = a.interleaved
-                               ? static_cast<float>(2 * j) / static_cast<float>(a.head_dim)
-                               : 2.0f * static_cast<float>(j) / static_cast<float>(a.head_dim);
-        inv[j] = 1.0f / std::pow(theta, expo);
-    }
+    rope_inv_freq(theta, a.head_dim, a.interleaved != 0, inv);
     const uint64_t qn = static_cast<uint64_t>(a.batch) * a.heads * a.q_seq * a.head_dim;
     const uint64_t kn = static_cast<uint64_t>(a.batch) * a.heads * a.k_seq * a.head_dim;
     const uint32_t seq = std::max(a.q_seq, a.k_seq);
@@ -647,6 +651,151 @@ void exec_kv_append(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx
     st.finish();
     acc.bytes_read = 2 * n * sizeof(float);
     acc.bytes_written = 2 * n * sizeof(float);
+    acc.dma = st.staged_bytes();
+}
+
+static_assert(sizeof(vnpu_b200_qkv_rope_append_args_t) <= sizeof(vnpu_command_t::args),
+              "QKV args fit the command");
+static_assert(sizeof(vnpu_b200_matmul_i8_residual_args_t) <= sizeof(vnpu_command_t::args),
+              "residual args fit the command");
+
+// MATMUL_I8 (QKV weights) + ROPE_F32 + KV_APPEND in one command.
+void exec_qkv_rope_append(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags,
+                          const LaunchCtx &ctx, Accounting &acc) {
+    vnpu_b200_qkv_rope_append_args_t a;
+    std::memcpy(&a, cmd.args.raw, sizeof(a));
+    vnpu_packed_weights_t *w = a.B;
+    if (!a.A || !w || !a.Q || !a.K_cache || !a.V_cache || !a.T || !a.K || !a.heads ||
+        !a.head_dim || (a.head_dim & 1u) || !a.capacity)
+        throw CommandError("invalid qkv_rope_append arguments", VNPU_ERR_INVALID_ARGUMENT);
+    if (a.head_dim > 512)
+        throw CommandError("qkv_rope_append head_dim above 512", VNPU_ERR_UNSUPPORTED);
+    const uint64_t N = 3ull * a.heads * a.head_dim;
+    if (w->K != a.K || w->N != N) throw CommandError("packed QKV weight shape mismatch");
+    if (w->device != s->device) throw CommandError("packed weights belong to another device");
+    if (!a.position && static_cast<uint64_t>(a.position_offset) + a.T > a.capacity)
+        throw CommandError("qkv_rope_append past the cache capacity", VNPU_ERR_INVALID_ARGUMENT);
+    const float theta = a.theta_base > 0.0f ? a.theta_base : 10000.0f;
+    float inv[256];
+    rope_inv_freq(theta, a.head_dim, false, inv);
+    const uint64_t n = static_cast<uint64_t>(a.heads) * a.T * a.head_dim;
+    const uint64_t cn = static_cast<uint64_t>(a.heads) * a.capacity * a.head_dim;
+    Staging st(s);
+    MatmulI8 p;
+    p.A = st.in(a.A, static_cast<uint64_t>(a.T) * a.K);
+    p.lda = a.K;
+    p.Bt = w->bt;
+    p.k_stride = w->k_stride;
+    p.scale_a = st.in(a.scale_a, sizeof(float) * a.T);
+    p.scale_b = w->scales;
+    p.bias = st.in(a.bias, sizeof(float) * N);
+    p.M = a.T;
+    p.K = a.K;
+    p.N = static_cast<uint32_t>(N);
+    p.ldc = static_cast<uint32_t>(N);
+    p.epilogue = a.epilogue;
+    p.form = epi_form_for(s->device, flags);
+    p.tmap_b = w->tmap_ok ? &w->tmap : nullptr;
+    p.tmap_b128 = w->tmap128_ok ? &w->tmap128 : nullptr;
+    QkvRope q;
+    q.Q = st.out(a.Q, n * sizeof(float), false);
+    q.K_out = st.out(a.K_out, n * sizeof(float), false);
+    q.V_out = st.out(a.V_out, n * sizeof(float), false);
+    q.K_cache = st.out(a.K_cache, cn * sizeof(float), true);
+    q.V_cache = st.out(a.V_cache, cn * sizeof(float), true);
+    q.mask = a.mask ? st.out(a.mask, sizeof(float) * a.heads * a.capacity, true) : nullptr;
+    q.position = a.position ? st.in(a.position, sizeof(int32_t)) : nullptr;
+    q.heads = a.heads;
+    q.head_dim = a.head_dim;
+    q.capacity = a.capacity;
+    q.position_offset = a.position_offset;
+    q.scaling = a.scaling > 0.0f ? a.scaling : 1.0f;
+    q.inv_freq = inv;
+    if (a.T == 1) {
+        cuda_check(qkv_rope_append_gemv(ctx, p, q), "qkv_rope_append launch");
+    } else {
+        // MATMUL_I8 into a stream-ordered scratch, then split / rotate / append.
+        float *tmp = nullptr;
+        cuda_check(cudaMallocAsync(reinterpret_cast<void **>(&tmp), N * a.T * sizeof(float),
+                                   ctx.stream),
+                   "qkv scratch");
+        p.C = tmp;
+        cudaError_t e = matmul_i8(ctx, p);
+        if (e == cudaSuccess) e = qkv_split_rope_append(ctx, tmp, a.T, q);
+        cudaFreeAsync(tmp, ctx.stream);
+        cuda_check(e, "qkv_rope_append launch");
+    }
+    st.finish();
+    acc.bytes_read = static_cast<uint64_t>(a.T) * a.K + static_cast<uint64_t>(a.K) * N;
+    acc.bytes_written = 4 * n * sizeof(float);
+    acc.flops = 2ull * a.T * a.K * N;
+    acc.dma = st.staged_bytes();
+}
+
+// C = R + MATMUL_I8(A, B): the GEMV epilogue for one row, else MATMUL_I8
+// then ADD_F32's addition.
+void exec_matmul_i8_residual(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags,
+                             const LaunchCtx &ctx, Accounting &acc) {
+    vnpu_b200_matmul_i8_residual_args_t a;
+    std::memcpy(&a, cmd.args.raw, sizeof(a));
+    vnpu_packed_weights_t *w = a.B;
+    if (!a.A || !w || !a.R || !a.C || !a.M || !a.K || !a.N)
+        throw CommandError("invalid matmul_i8_residual arguments", VNPU_ERR_INVALID_ARGUMENT);
+    if (w->K != a.K || w->N != a.N) throw CommandError("packed weight shape mismatch");
+    if (w->device != s->device) throw CommandError("packed weights belong to another device");
+    const uint32_t lda = a.lda ? a.lda : a.K;
+    const uint32_t ldr = a.ldr ? a.ldr : a.N;
+    const uint32_t ldc = a.ldc ? a.ldc : a.N;
+    if (lda < a.K || ldr < a.N || ldc < a.N)
+        throw CommandError("invalid matmul_i8_residual leading dimensions",
+                           VNPU_ERR_INVALID_ARGUMENT);
+    if (a.M > 1 && (ldr != a.N || ldc != a.N))
+        throw CommandError("matmul_i8_residual with M > 1 needs dense R and C",
+                           VNPU_ERR_UNSUPPORTED);
+    Staging st(s);
+    MatmulI8 p;
+    p.A = st.in(a.A, static_cast<uint64_t>(a.M - 1) * lda + a.K);
+    p.lda = lda;
+    p.Bt = w->bt;
+    p.k_stride = w->k_stride;
+    p.scale_a = st.in(a.scale_a, sizeof(float) * a.M);
+    p.scale_b = w->scales;
+    p.bias = st.in(a.bias, sizeof(float) * a.N);
+    const uint64_t r_span = (static_cast<uint64_t>(a.M - 1) * ldr + a.N) * sizeof(float);
+    const uint64_t c_span = (static_cast<uint64_t>(a.M - 1) * ldc + a.N) * sizeof(float);
+    const float *R = st.in(a.R, r_span);
+    p.C = st.out(a.C, c_span, ldc != a.N);
+    p.ldc = ldc;
+    p.M = a.M;
+    p.K = a.K;
+    p.N = a.N;
+    p.epilogue = a.epilogue;
+    p.form = epi_form_for(s->device, flags);
+    p.tmap_b = w->tmap_ok ? &w->tmap : nullptr;
+    p.tmap_b128 = w->tmap128_ok ? &w->tmap128 : nullptr;
+    if (a.M == 1) {
+        cuda_check(matmul_i8_gemv_residual(ctx, p, R, ldr), "matmul_i8_residual launch");
+    } else {
+        const uint64_t count = static_cast<uint64_t>(a.M) * a.N;
+        const bool aliased = R < p.C + count && p.C < R + count;
+        float *out = p.C;
+        float *tmp = nullptr;
+        if (aliased) {
+            cuda_check(cudaMallocAsync(reinterpret_cast<void **>(&tmp), count * sizeof(float),
+                                       ctx.stream),
+                       "residual scratch");
+            p.C = tmp;
+        }
+        cudaError_t e = matmul_i8(ctx, p);
+        if (e == cudaSuccess) e = add(ctx, R, p.C, out, count, 1.0f, 1.0f);
+        if (tmp) cudaFreeAsync(tmp, ctx.stream);
+        cuda_check(e, "matmul_i8_residual launch");
+    }
+    st.finish();
+    acc.bytes_read = static_cast<uint64_t>(a.M) * a.K + static_cast<uint64_t>(a.K) * a.N +
+                     static_cast<uint64_t>(a.M) * a.N * sizeof(float);
+    acc.bytes_written = static_cast<uint64_t>(a.M) * a.N * sizeof(float);
+    acc.flops = 2ull * a.M * a.K * a.N;
     acc.dma = st.staged_bytes();
 }
 
@@ -773,7 +922,8 @@ vnpu_status_t execute_command(vnpu_stream_t *s, const vnpu_command_t &cmd, uint3
     vnpu_device_t *dev = s->device;
     if (cmd.opcode >= VNPU_OP_COUNT && cmd.opcode != VNPU_B200_OP_RMSNORM_QUANTIZE_I8 &&
         cmd.opcode != VNPU_B200_OP_SWIGLU_QUANTIZE_I8 && cmd.opcode != VNPU_B200_OP_KV_APPEND &&
-        cmd.opcode != VNPU_B200_OP_MATMUL_I8_SCATTER)
+        cmd.opcode != VNPU_B200_OP_MATMUL_I8_SCATTER &&
+        cmd.opcode != VNPU_B200_OP_QKV_ROPE_APPEND && cmd.opcode != VNPU_B200_OP_MATMUL_I8_RESIDUAL)
         return VNPU_ERR_INVALID_COMMAND;
     dev->last_opcode.store(cmd.opcode);
     const bool tracing = dev->trace.enabled.load();
@@ -815,6 +965,8 @@ vnpu_status_t execute_command(vnpu_stream_t *s, const vnpu_command_t &cmd, uint3
         case VNPU_B200_OP_SWIGLU_QUANTIZE_I8: exec_swiglu_quantize(s, cmd, ctx, acc); break;
         case VNPU_B200_OP_KV_APPEND: exec_kv_append(s, cmd, ctx, acc); break;
         case VNPU_B200_OP_MATMUL_I8_SCATTER: exec_matmul_i8_scatter(s, cmd, flags, ctx, acc); break;
+        case VNPU_B200_OP_QKV_ROPE_APPEND: exec_qkv_rope_append(s, cmd, flags, ctx, acc); break;
+        case VNPU_B200_OP_MATMUL_I8_RESIDUAL: exec_matmul_i8_residual(s, cmd, flags, ctx, acc); break;
         case VNPU_OP_MEMSET: exec_memset(s, cmd, acc); break;
         case VNPU_OP_PACK_WEIGHTS_I8: exec_pack(s, cmd, acc); break;
         default:
@@ -924,6 +1076,8 @@ const char *opcode_name(uint32_t op) {
     if (op == VNPU_B200_OP_SWIGLU_QUANTIZE_I8) return "SWIGLU_QUANTIZE_I8";
     if (op == VNPU_B200_OP_KV_APPEND) return "KV_APPEND";
     if (op == VNPU_B200_OP_MATMUL_I8_SCATTER) return "MATMUL_I8_SCATTER";
+    if (op == VNPU_B200_OP_QKV_ROPE_APPEND) return "QKV_ROPE_APPEND";
+    if (op == VNPU_B200_OP_MATMUL_I8_RESIDUAL) return "MATMUL_I8_RESIDUAL";
     return op < sizeof(names) / sizeof(names[0]) ? names[op] : "UNKNOWN";
 }
 

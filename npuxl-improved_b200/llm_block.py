@@ -195,7 +195,9 @@ class B200Block:
 
     def __init__(self, cfg: BlockConfig, lib, dev, torch, fused: bool = True):
         self.cfg, self.lib, self.dev, self.t = cfg, lib, dev, torch
-        self.fused = fused   # B200 opcodes: fused RMSNorm/SwiGLU -> QUANTIZE_I8, KV_APPEND
+        # B200 opcodes: fused RMSNorm/SwiGLU -> QUANTIZE_I8 prologues, the QKV
+        # projection with RoPE + cache append, projections with the residual add
+        self.fused = fused
         self.stream = torch.cuda.ExternalStream(lib.b200_stream_handle(dev.stream))
         w, (n1, n2) = make_weights(cfg)
         self.n1 = torch.from_numpy(n1).cuda()
@@ -240,21 +242,27 @@ class B200Block:
         K = self.w[name][1]
         return (self._buf("a8_" + name, (M, K), self.t.int8), self._buf("sa_" + name, (M,)))
 
-    def _mm_cmd(self, name, M, out_name):
-        """MATMUL_I8 of the already quantized activations of GEMM `name`."""
+    def _mm_cmd(self, name, M, out_name, residual=None):
+        """MATMUL_I8 of the already quantized activations of GEMM `name`;
+        with `residual`, out = residual + product in one command
+        (VNPU_B200_OP_MATMUL_I8_RESIDUAL, the bits of MATMUL_I8 then ADD_F32)."""
         w, K, N = self.w[name]
         a8, sa = self._act_bufs(name, M)
         out = self._buf(out_name, (M, N))
+        if residual is not None:
+            return vnpu.b200_command(vnpu.OP_B200_MATMUL_I8_RESIDUAL, vnpu.MatmulI8ResidualArgs(
+                a8.data_ptr(), w, sa.data_ptr(), None, residual.data_ptr(), out.data_ptr(), M, K,
+                N, 0, 0, 0, 0, 0)), out
         return _cmd(vnpu.OP_MATMUL_I8, "matmul_i8",
                     vnpu.MatmulI8Args(a8.data_ptr(), w, sa.data_ptr(), None, out.data_ptr(), M, K,
                                       N, 0, 0, 0, vnpu.UNIT_GPU)), out
 
-    def _gemm_cmds(self, x, name, out_name):
+    def _gemm_cmds(self, x, name, out_name, residual=None):
         M, K = x.shape[0], self.w[name][1]
         a8, sa = self._act_bufs(name, M)
         q = _cmd(vnpu.OP_QUANTIZE_I8, "quantize_i8",
                  vnpu.QuantizeI8Args(x.data_ptr(), a8.data_ptr(), sa.data_ptr(), M, K, 0, 0))
-        mm, out = self._mm_cmd(name, M, out_name)
+        mm, out = self._mm_cmd(name, M, out_name, residual)
         return [q, mm], out
 
     def _norm_gemm_cmds(self, x, wn, name, out_name):
@@ -271,7 +279,7 @@ class B200Block:
         mm, out = self._mm_cmd(name, M, out_name)
         return [pro, mm], out
 
-    def _swiglu_gemm_cmds(self, g, u, name, out_name):
+    def _swiglu_gemm_cmds(self, g, u, name, out_name, residual=None):
         """SwiGLU -> QUANTIZE_I8 -> MATMUL_I8 (fused prologue when enabled)."""
         T, inter = g.shape
         if not self.fused:
@@ -279,12 +287,12 @@ class B200Block:
             sw = _cmd(vnpu.OP_SWIGLU_F32, "swiglu",
                       vnpu.SwigluArgs(g.data_ptr(), u.data_ptr(), ff.data_ptr(), T * inter,
                                       1.0, 0, 0))
-            cmds, out = self._gemm_cmds(ff, name, out_name)
+            cmds, out = self._gemm_cmds(ff, name, out_name, residual)
             return [sw] + cmds, out
         a8, sa = self._act_bufs(name, T)
         pro = vnpu.b200_command(vnpu.OP_B200_SWIGLU_QUANTIZE_I8, vnpu.SwigluQuantizeArgs(
             g.data_ptr(), u.data_ptr(), None, a8.data_ptr(), sa.data_ptr(), T, inter, 1.0, 0))
-        mm, out = self._mm_cmd(name, T, out_name)
+        mm, out = self._mm_cmd(name, T, out_name, residual)
         return [pro, mm], out
 
     def _rms_cmd(self, x, wn, out_name):
@@ -305,22 +313,36 @@ class B200Block:
         t, cfg = self.t, self.cfg
         T, d, H, hd = x.shape[0], cfg.d, cfg.heads, cfg.head_dim
         with t.cuda.stream(self.stream):
-            cmds, qkv = self._norm_gemm_cmds(x, self.n1, "qkv", f"qkv{T}")
-            self._submit(cmds)
-            Q = qkv[:, :d].reshape(T, H, hd).transpose(0, 1).contiguous()[None]
-            K = qkv[:, d:2 * d].reshape(T, H, hd).transpose(0, 1).contiguous()[None]
-            V = qkv[:, 2 * d:].reshape(T, H, hd).transpose(0, 1).contiguous()[None]
-            rope = vnpu.RopeArgs(Q.data_ptr(), K.data_ptr(),
-                                 positions.data_ptr() if positions is not None else None,
-                                 1, H, T, T, hd, pos0, 0, cfg.theta, 1.0)
-            self._submit([_cmd(vnpu.OP_ROPE_F32, "rope", rope)])
-            O = self._buf(f"O{T}", (1, H, T, hd))
             if self.fused:
-                # cache append + mask in one command (VNPU_B200_OP_KV_APPEND)
-                self._submit([vnpu.b200_command(vnpu.OP_B200_KV_APPEND, vnpu.KvAppendArgs(
-                    K.data_ptr(), V.data_ptr(), self.kc.data_ptr(), self.vc.data_ptr(),
-                    self.mask.data_ptr(), positions.data_ptr() if positions is not None else None,
-                    H, T, hd, cfg.cap, pos0, 0))])
+                # RMSNorm -> QUANTIZE_I8, then the QKV projection with RoPE and
+                # the cache append in its epilogue (VNPU_B200_OP_QKV_ROPE_APPEND).
+                w, K_in, _ = self.w["qkv"]
+                a8, sa = self._act_bufs("qkv", T)
+                pro = vnpu.b200_command(vnpu.OP_B200_RMSNORM_QUANTIZE_I8, vnpu.RmsnormQuantizeArgs(
+                    x.data_ptr(), self.n1.data_ptr(), None, a8.data_ptr(), sa.data_ptr(), T, d,
+                    cfg.eps, 0))
+                Q = self._buf(f"Q{T}", (1, H, T, hd))
+                K = self._buf(f"K{T}", (1, H, T, hd)) if T > 1 else None
+                V = self._buf(f"V{T}", (1, H, T, hd)) if T > 1 else None
+                qkv = vnpu.b200_command(vnpu.OP_B200_QKV_ROPE_APPEND, vnpu.QkvRopeAppendArgs(
+                    a8.data_ptr(), w, sa.data_ptr(), None, Q.data_ptr(),
+                    K.data_ptr() if K is not None else None,
+                    V.data_ptr() if V is not None else None, self.kc.data_ptr(),
+                    self.vc.data_ptr(), self.mask.data_ptr(),
+                    positions.data_ptr() if positions is not None else None, T, K_in, H, hd,
+                    cfg.cap, pos0, cfg.theta, 1.0, 0, 0))
+                self._submit([pro, qkv])
+            else:
+                cmds, qkv = self._norm_gemm_cmds(x, self.n1, "qkv", f"qkv{T}")
+                self._submit(cmds)
+                Q = qkv[:, :d].reshape(T, H, hd).transpose(0, 1).contiguous()[None]
+                K = qkv[:, d:2 * d].reshape(T, H, hd).transpose(0, 1).contiguous()[None]
+                V = qkv[:, 2 * d:].reshape(T, H, hd).transpose(0, 1).contiguous()[None]
+                rope = vnpu.RopeArgs(Q.data_ptr(), K.data_ptr(),
+                                     positions.data_ptr() if positions is not None else None,
+                                     1, H, T, T, hd, pos0, 0, cfg.theta, 1.0)
+                self._submit([_cmd(vnpu.OP_ROPE_F32, "rope", rope)])
+            O = self._buf(f"O{T}", (1, H, T, hd))
             if T > 1:
                 if not self.fused:
                     self.kc[:, :, pos0:pos0 + T].copy_(K)
@@ -339,15 +361,26 @@ class B200Block:
                                          cfg.cap, hd, 0, 0.0, 0)
             self._submit([_cmd(vnpu.OP_ATTENTION_F32, "attention", att)])
             attn = O[0].transpose(0, 1).reshape(T, d).contiguous()
-            cmds, proj = self._gemm_cmds(attn, "o", f"proj{T}")
-            a, x1 = self._add_cmd(x, proj, f"x1{T}")
-            cmds2, gu = self._norm_gemm_cmds(x1, self.n2, "gate_up", f"gu{T}")
-            self._submit(cmds + [a] + cmds2)
+            if self.fused:
+                # the residual adds ride on the O and down projections
+                # (VNPU_B200_OP_MATMUL_I8_RESIDUAL)
+                cmds, x1 = self._gemm_cmds(attn, "o", f"x1{T}", residual=x)
+                cmds2, gu = self._norm_gemm_cmds(x1, self.n2, "gate_up", f"gu{T}")
+                self._submit(cmds + cmds2)
+            else:
+                cmds, proj = self._gemm_cmds(attn, "o", f"proj{T}")
+                a, x1 = self._add_cmd(x, proj, f"x1{T}")
+                cmds2, gu = self._norm_gemm_cmds(x1, self.n2, "gate_up", f"gu{T}")
+                self._submit(cmds + [a] + cmds2)
             g = gu[:, :cfg.inter].contiguous()
             u = gu[:, cfg.inter:].contiguous()
-            cmds3, down = self._swiglu_gemm_cmds(g, u, "down", f"down{T}")
-            a2, y = self._add_cmd(x1, down, f"y{T}")
-            self._submit(cmds3 + [a2])
+            if self.fused:
+                cmds3, y = self._swiglu_gemm_cmds(g, u, "down", f"y{T}", residual=x1)
+                self._submit(cmds3)
+            else:
+                cmds3, down = self._swiglu_gemm_cmds(g, u, "down", f"down{T}")
+                a2, y = self._add_cmd(x1, down, f"y{T}")
+                self._submit(cmds3 + [a2])
             # keep the temporaries alive until the stream has used them
             self._keep = (Q, K, V, attn, g, u)
         return y

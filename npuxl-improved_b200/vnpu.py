@@ -192,6 +192,26 @@ class MatmulI8ScatterArgs(C.Structure):
                 ("ldd", u32), ("col_offset", u32), ("ndst", u32), ("epilogue", u32)]
 
 
+OP_B200_QKV_ROPE_APPEND = 0x104
+
+
+class QkvRopeAppendArgs(C.Structure):
+    _fields_ = [("A", vp), ("B", vp), ("scale_a", vp), ("bias", vp), ("Q", vp), ("K_out", vp),
+                ("V_out", vp), ("K_cache", vp), ("V_cache", vp), ("mask", vp), ("position", vp),
+                ("T", u32), ("K", u32), ("heads", u32), ("head_dim", u32), ("capacity", u32),
+                ("position_offset", u32), ("theta_base", C.c_float), ("scaling", C.c_float),
+                ("epilogue", u32), ("reserved0", u32)]
+
+
+OP_B200_MATMUL_I8_RESIDUAL = 0x105
+
+
+class MatmulI8ResidualArgs(C.Structure):
+    _fields_ = [("A", vp), ("B", vp), ("scale_a", vp), ("bias", vp), ("R", vp), ("C", vp),
+                ("M", u32), ("K", u32), ("N", u32), ("lda", u32), ("ldr", u32), ("ldc", u32),
+                ("epilogue", u32), ("reserved0", u32)]
+
+
 def b200_command(opcode: int, args: C.Structure) -> "Command":
     """A command whose arguments are a B200 extension struct (copied into args.raw)."""
     c = Command()

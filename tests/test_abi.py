@@ -175,7 +175,14 @@ int main(void) {
     F(vnpu_b200_swiglu_quantize_args_t, scales); F(vnpu_b200_swiglu_quantize_args_t, alpha);
     printf("sc %zu\n", sizeof(vnpu_b200_matmul_i8_scatter_args_t));
     F(vnpu_b200_matmul_i8_scatter_args_t, dst); F(vnpu_b200_matmul_i8_scatter_args_t, ndst);
-    printf("ops %u %u\n", VNPU_B200_OP_RMSNORM_QUANTIZE_I8, VNPU_B200_OP_SWIGLU_QUANTIZE_I8);
+    printf("qkv %zu\n", sizeof(vnpu_b200_qkv_rope_append_args_t));
+    F(vnpu_b200_qkv_rope_append_args_t, position); F(vnpu_b200_qkv_rope_append_args_t, T);
+    F(vnpu_b200_qkv_rope_append_args_t, theta_base); F(vnpu_b200_qkv_rope_append_args_t, epilogue);
+    printf("res %zu\n", sizeof(vnpu_b200_matmul_i8_residual_args_t));
+    F(vnpu_b200_matmul_i8_residual_args_t, R); F(vnpu_b200_matmul_i8_residual_args_t, ldr);
+    F(vnpu_b200_matmul_i8_residual_args_t, epilogue);
+    printf("ops %u %u %u %u\n", VNPU_B200_OP_RMSNORM_QUANTIZE_I8, VNPU_B200_OP_SWIGLU_QUANTIZE_I8,
+           VNPU_B200_OP_QKV_ROPE_APPEND, VNPU_B200_OP_MATMUL_I8_RESIDUAL);
     return 0;
 }''')
     exe = tmp_path / "ext"
@@ -192,5 +199,15 @@ int main(void) {
     assert int(out["sc"]) == C.sizeof(vnpu.MatmulI8ScatterArgs) <= int(out["raw"])
     assert int(out["vnpu_b200_matmul_i8_scatter_args_t.dst"]) == vnpu.MatmulI8ScatterArgs.dst.offset
     assert int(out["vnpu_b200_matmul_i8_scatter_args_t.ndst"]) == vnpu.MatmulI8ScatterArgs.ndst.offset
+    assert int(out["qkv"]) == C.sizeof(vnpu.QkvRopeAppendArgs) <= int(out["raw"])
+    for f in ("position", "T", "theta_base", "epilogue"):
+        assert int(out[f"vnpu_b200_qkv_rope_append_args_t.{f}"]) == \
+            getattr(vnpu.QkvRopeAppendArgs, f).offset
+    assert int(out["res"]) == C.sizeof(vnpu.MatmulI8ResidualArgs) <= int(out["raw"])
+    for f in ("R", "ldr", "epilogue"):
+        assert int(out[f"vnpu_b200_matmul_i8_residual_args_t.{f}"]) == \
+            getattr(vnpu.MatmulI8ResidualArgs, f).offset
     assert out["ops"].split() == [str(vnpu.OP_B200_RMSNORM_QUANTIZE_I8),
-                                  str(vnpu.OP_B200_SWIGLU_QUANTIZE_I8)]
+                                  str(vnpu.OP_B200_SWIGLU_QUANTIZE_I8),
+                                  str(vnpu.OP_B200_QKV_ROPE_APPEND),
+                                  str(vnpu.OP_B200_MATMUL_I8_RESIDUAL)]
