@@ -2,12 +2,21 @@
 // src/core/backend.cpp:8-60, layout include/vnpu_backend.h:101-148) and the
 // ABI entry points that are outside the B200 int8 path.
 //
-// The cluster / remote-node / speculative-decoding entry points belong to the
+// The local cluster (vnpu_cluster_* over this library's devices) is built;
+// remote nodes, the node server and speculative decoding belong to the
 // reference's TCP appliance (src/cluster/*), which this backend does not
-// rebuild: they exist so engines keep linking and report
-// VNPU_ERR_UNSUPPORTED.  The column-sharded multi-GPU GEMM is driven one
-// process per GPU (see bench.py / tests) with NCCL from torch.distributed.
+// rebuild: those entry points exist so engines keep linking and report
+// VNPU_ERR_UNSUPPORTED.  The column-sharded multi-GPU int8 GEMM is driven one
+// process per GPU (bench.py, tests) with NCCL from torch.distributed.
+#include <algorithm>
+#include <atomic>
 #include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
 
 #include "../../include/vnpu_backend.h"
 #include "runtime.h"
@@ -39,38 +48,214 @@ VNPU_API void VNPU_CALL vnpu_cluster_config_init(vnpu_cluster_config_t *config) 
     config->request_timeout_ms = 30000;
 }
 
-VNPU_API vnpu_status_t VNPU_CALL vnpu_cluster_create(const vnpu_cluster_config_t *,
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Local cluster (reference src/cluster/cluster.cpp:243-546, local workers
+// only): MATMUL_F32 with its rows split across vnpu devices by weight.  Each
+// worker is a stream on one device; the cached weights live in each device's
+// HBM (uploaded on the first GEMM that device runs), the rows of A and C stay
+// where the caller has them and are staged per worker.  Workers run in
+// parallel host threads, so devices on different GPUs compute at once.
+// Remote nodes are the reference's TCP appliance: not rebuilt here.
+// ---------------------------------------------------------------------------
+struct vnpu_weight_handle {
+    std::string key;
+    uint32_t K = 0, N = 0, trans_b = 0;
+    std::vector<float> host;   // canonical K x N (transposed when trans_b)
+    std::mutex mutex;
+    std::map<vnpu_device_t *, float *> on_device;
+};
+
+struct vnpu_cluster {
+    struct Worker {
+        vnpu_device_t *device;
+        vnpu_stream_t *stream;
+        uint32_t weight;
+    };
+    vnpu_cluster_config_t config{};
+    std::string name;
+    std::vector<Worker> workers;
+    std::vector<std::unique_ptr<vnpu_weight_handle>> weights;
+    std::atomic<uint64_t> local_jobs{0}, total_jobs{0}, failed_jobs{0};
+    std::atomic<uint64_t> local_time_ns{0}, speedup_x1000{0};
+};
+
+namespace {
+
+// The handle's weights in `device`'s HBM (uploaded once).
+float *device_weights(vnpu_weight_handle *h, vnpu_device_t *device) {
+    std::lock_guard<std::mutex> g(h->mutex);
+    auto it = h->on_device.find(device);
+    if (it != h->on_device.end()) return it->second;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(device->ordinal) != cudaSuccess) return nullptr;
+    float *d = nullptr;
+    const size_t bytes = h->host.size() * sizeof(float);
+    if (cudaMalloc(reinterpret_cast<void **>(&d), bytes) != cudaSuccess ||
+        cudaMemcpy(d, h->host.data(), bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+        if (d) cudaFree(d);
+        cudaGetLastError();
+        cudaSetDevice(prev);
+        return nullptr;
+    }
+    cudaSetDevice(prev);
+    h->on_device[device] = d;
+    return d;
+}
+
+}  // namespace
+
+extern "C" {
+
+VNPU_API vnpu_status_t VNPU_CALL vnpu_cluster_create(const vnpu_cluster_config_t *config,
                                                      vnpu_cluster_t **out) {
-    if (out) *out = nullptr;
-    return VNPU_ERR_UNSUPPORTED;
+    if (!out) return VNPU_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    auto *c = new (std::nothrow) vnpu_cluster_t();
+    if (!c) return VNPU_ERR_OUT_OF_MEMORY;
+    if (config) c->config = *config;
+    else vnpu_cluster_config_init(&c->config);
+    if (!c->config.abi_version) c->config.abi_version = VNPU_ABI_VERSION;
+    if (!c->config.num_streams) c->config.num_streams = 1;
+    if (!c->config.request_timeout_ms) c->config.request_timeout_ms = 30000;
+    c->name = c->config.cluster_name ? c->config.cluster_name : "vnpu-cluster";
+    *out = c;
+    return VNPU_OK;
 }
-VNPU_API void VNPU_CALL vnpu_cluster_destroy(vnpu_cluster_t *) {}
-VNPU_API vnpu_status_t VNPU_CALL vnpu_cluster_add_device(vnpu_cluster_t *, vnpu_device_t *,
-                                                         uint32_t) {
-    return VNPU_ERR_UNSUPPORTED;
+
+VNPU_API void VNPU_CALL vnpu_cluster_destroy(vnpu_cluster_t *c) {
+    if (!c) return;
+    for (auto &w : c->workers) vnpu_stream_destroy(w.stream);
+    for (auto &h : c->weights)
+        for (auto &kv : h->on_device) {
+            cudaSetDevice(kv.first->ordinal);
+            cudaFree(kv.second);
+        }
+    delete c;
 }
+
+VNPU_API vnpu_status_t VNPU_CALL vnpu_cluster_add_device(vnpu_cluster_t *c, vnpu_device_t *device,
+                                                         uint32_t weight) {
+    if (!c || !device) return VNPU_ERR_INVALID_ARGUMENT;
+    for (uint32_t i = 0; i < std::max<uint32_t>(1, c->config.num_streams); ++i) {
+        vnpu_stream_t *s = nullptr;
+        const vnpu_status_t rc = vnpu_stream_create(device, 0, &s);
+        if (rc != VNPU_OK) return rc;
+        c->workers.push_back({device, s, weight ? weight : 1});
+    }
+    return VNPU_OK;
+}
+
 VNPU_API vnpu_status_t VNPU_CALL vnpu_cluster_add_remote(vnpu_cluster_t *,
                                                          const vnpu_remote_node_config_t *,
                                                          vnpu_remote_node_t **out) {
     if (out) *out = nullptr;
     return VNPU_ERR_UNSUPPORTED;
 }
-VNPU_API vnpu_status_t VNPU_CALL vnpu_cluster_get_stats(const vnpu_cluster_t *,
+
+VNPU_API vnpu_status_t VNPU_CALL vnpu_cluster_get_stats(const vnpu_cluster_t *c,
                                                         vnpu_cluster_stats_t *stats) {
-    if (stats) std::memset(stats, 0, sizeof(*stats));
-    return VNPU_ERR_UNSUPPORTED;
+    if (!c || !stats) return VNPU_ERR_INVALID_ARGUMENT;
+    std::memset(stats, 0, sizeof(*stats));
+    stats->local_jobs = c->local_jobs.load();
+    stats->total_jobs = c->total_jobs.load();
+    stats->failed_jobs = c->failed_jobs.load();
+    stats->local_time_ns = static_cast<double>(c->local_time_ns.load());
+    stats->speedup_estimate = static_cast<double>(c->speedup_x1000.load()) / 1000.0;
+    return VNPU_OK;
 }
-VNPU_API vnpu_status_t VNPU_CALL vnpu_cluster_cache_weights_f32(vnpu_cluster_t *, const char *,
-                                                                const float *, uint32_t,
-                                                                uint32_t, uint32_t,
+
+VNPU_API vnpu_status_t VNPU_CALL vnpu_cluster_cache_weights_f32(vnpu_cluster_t *c,
+                                                                const char *key,
+                                                                const float *B, uint32_t K,
+                                                                uint32_t N, uint32_t trans_b,
                                                                 vnpu_weight_handle_t **out) {
-    if (out) *out = nullptr;
-    return VNPU_ERR_UNSUPPORTED;
+    if (!c || !B || !K || !N || !out || trans_b > 1) return VNPU_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    auto h = std::make_unique<vnpu_weight_handle>();
+    h->key = key && key[0] ? key : "weights-" + std::to_string(c->weights.size());
+    h->K = K;
+    h->N = N;
+    h->trans_b = trans_b;
+    h->host.resize(static_cast<size_t>(K) * N);
+    if (trans_b) {
+        for (uint32_t k = 0; k < K; ++k)
+            for (uint32_t n = 0; n < N; ++n)
+                h->host[static_cast<size_t>(k) * N + n] = B[static_cast<size_t>(n) * K + k];
+    } else {
+        std::memcpy(h->host.data(), B, h->host.size() * sizeof(float));
+    }
+    *out = h.get();
+    c->weights.push_back(std::move(h));
+    return VNPU_OK;
 }
-VNPU_API vnpu_status_t VNPU_CALL vnpu_cluster_matmul_f32(vnpu_cluster_t *, vnpu_weight_handle_t *,
-                                                         const float *, float *, uint32_t,
-                                                         uint32_t, uint32_t, uint32_t) {
-    return VNPU_ERR_UNSUPPORTED;
+
+VNPU_API vnpu_status_t VNPU_CALL vnpu_cluster_matmul_f32(vnpu_cluster_t *c,
+                                                         vnpu_weight_handle_t *w, const float *A,
+                                                         float *C, uint32_t M, uint32_t K,
+                                                         uint32_t N, uint32_t unit) {
+    if (!c || !w || !A || !C || !M || !K || !N) return VNPU_ERR_INVALID_ARGUMENT;
+    if (w->K != K || w->N != N) return VNPU_ERR_INVALID_ARGUMENT;
+    if (c->workers.empty()) return VNPU_ERR_DEVICE_ERROR;
+    // Rows by weight, the last worker taking the remainder
+    // (src/cluster/cluster.cpp:455-470).
+    const size_t n = c->workers.size();
+    uint64_t total = 0;
+    for (const auto &wk : c->workers) total += std::max<uint32_t>(1, wk.weight);
+    std::vector<uint32_t> start(n), rows(n);
+    uint32_t cursor = 0;
+    for (size_t i = 0; i < n; ++i) {
+        uint32_t r = static_cast<uint32_t>(static_cast<uint64_t>(M) *
+                                           std::max<uint32_t>(1, c->workers[i].weight) / total);
+        if (i + 1 == n) r = M - cursor;
+        if (cursor + r > M) r = M - cursor;
+        start[i] = cursor;
+        rows[i] = r;
+        cursor += r;
+    }
+    std::vector<vnpu_status_t> rc(n, VNPU_OK);
+    std::vector<uint64_t> ns(n, 0);
+    std::vector<std::thread> threads;
+    for (size_t i = 0; i < n; ++i) {
+        if (!rows[i]) continue;
+        threads.emplace_back([&, i]() {
+            const uint64_t t0 = vnpu_b200::now_ns();
+            const auto &wk = c->workers[i];
+            float *Bd = device_weights(w, wk.device);
+            if (!Bd) {
+                rc[i] = VNPU_ERR_OUT_OF_MEMORY;
+            } else {
+                vnpu_matmul_f32_args_t a{};
+                a.A = A + static_cast<size_t>(start[i]) * K;
+                a.B = Bd;
+                a.C = C + static_cast<size_t>(start[i]) * N;
+                a.M = rows[i];
+                a.K = K;
+                a.N = N;
+                a.alpha = 1.0f;
+                a.beta = 0.0f;
+                a.unit = unit;
+                rc[i] = vnpu_matmul_f32(wk.stream, &a);
+            }
+            ns[i] = vnpu_b200::now_ns() - t0;
+            c->local_jobs.fetch_add(1);
+            c->local_time_ns.fetch_add(ns[i]);
+            if (rc[i] != VNPU_OK) c->failed_jobs.fetch_add(1);
+        });
+    }
+    for (auto &t : threads) t.join();
+    c->total_jobs.fetch_add(1);
+    uint64_t sum = 0, mx = 0;
+    for (uint64_t t : ns) {
+        sum += t;
+        mx = std::max(mx, t);
+    }
+    if (mx) c->speedup_x1000.store(static_cast<uint64_t>(1000.0 * sum / mx));
+    for (vnpu_status_t r : rc)
+        if (r != VNPU_OK) return r;
+    return VNPU_OK;
 }
 
 VNPU_API void VNPU_CALL vnpu_node_config_init(vnpu_node_config_t *config) {

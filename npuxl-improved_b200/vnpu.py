@@ -91,6 +91,20 @@ class TraceSummary(C.Structure):
                ("hot_opcode", u32), ("hot_time_ns", u64), ("trace_overhead_ns", C.c_double)]
 
 
+class ClusterConfig(C.Structure):
+    _fields_ = [("abi_version", u32), ("num_streams", u32), ("flags", u32),
+                ("request_timeout_ms", u32), ("auth_token", C.c_char_p),
+                ("cluster_name", C.c_char_p)]
+
+
+class ClusterStats(C.Structure):
+    _fields_ = [(n, u64) for n in ("local_jobs", "remote_jobs", "total_jobs",
+                                   "network_bytes_sent", "network_bytes_received", "failed_jobs",
+                                   "culled_tiles")] + \
+              [("local_time_ns", C.c_double), ("remote_time_ns", C.c_double),
+               ("speedup_estimate", C.c_double)]
+
+
 class MatmulF32Args(C.Structure):
     _fields_ = [("A", vp), ("B", vp), ("bias", vp), ("C", vp), ("M", u32), ("K", u32), ("N", u32),
                 ("lda", u32), ("ldb", u32), ("ldc", u32), ("trans_a", u32), ("trans_b", u32),
@@ -317,6 +331,19 @@ class Lib:
         self.add_f32 = _sig(h, "vnpu_add_f32", _ST, vp, C.POINTER(BinaryArgs))
         self.attention_f32 = _sig(h, "vnpu_attention_f32", _ST, vp, C.POINTER(AttentionArgs))
         self.get_backend_v1 = _sig(h, "vnpu_get_backend_v1", vp)
+        self.cluster_config_init = _sig(h, "vnpu_cluster_config_init", None,
+                                        C.POINTER(ClusterConfig))
+        self.cluster_create = _sig(h, "vnpu_cluster_create", _ST, C.POINTER(ClusterConfig),
+                                   C.POINTER(vp))
+        self.cluster_destroy = _sig(h, "vnpu_cluster_destroy", None, vp)
+        self.cluster_add_device = _sig(h, "vnpu_cluster_add_device", _ST, vp, vp, u32)
+        self.cluster_add_remote = _sig(h, "vnpu_cluster_add_remote", _ST, vp, vp, C.POINTER(vp))
+        self.cluster_get_stats = _sig(h, "vnpu_cluster_get_stats", _ST, vp,
+                                      C.POINTER(ClusterStats))
+        self.cluster_cache_weights_f32 = _sig(h, "vnpu_cluster_cache_weights_f32", _ST, vp,
+                                              C.c_char_p, vp, u32, u32, u32, C.POINTER(vp))
+        self.cluster_matmul_f32 = _sig(h, "vnpu_cluster_matmul_f32", _ST, vp, vp, vp, vp, u32,
+                                       u32, u32, u32)
         self.is_b200 = hasattr(h, "vnpu_b200_stream_handle")
         if self.is_b200:
             self.b200_stream_handle = _sig(h, "vnpu_b200_stream_handle", vp, vp)
