@@ -1400,13 +1400,27 @@ GvParams gv_params(const MatmulI8 &p) {
     return g;
 }
 
+template <int kM, int kCols, int kUnroll, int kThreads, typename Extra>
+cudaError_t launch_gemv_cfg(const LaunchCtx &ctx, const GvParams &g, bool aligned, const Extra &x);
+
 template <int kM, typename Extra = GvPlain>
 cudaError_t launch_gemv_m(const LaunchCtx &ctx, const GvParams &g, bool aligned,
                           const Extra &x = Extra()) {
-    // 2 columns per warp, 8 chunks in flight, 256 threads.  (4 columns per
-    // warp with 4 chunks and 128 threads measured 1.6-3.4x slower for
-    // M = 2..8; the tensor-core GEMV takes those rows anyway.)
-    constexpr int kCols = 2, kUnroll = 8, kThreads = 256;
+    // One column per warp, 8 chunks (4 KiB of it) in flight per lane,
+    // 128-thread CTAs.  Measured for M = 1 on 4096x4096 / 4096x22016 /
+    // 11008x4096 (graphs over weight copies larger than L2): 4.2 / 5.7 / 4.5
+    // TB/s, against 3.9 / 5.1 / 4.3 with two columns per warp and 256
+    // threads; for M = 2 / 4 / 8 on 4096x4096: 5.95 / 9.7 / 16.7 us against
+    // 6.6 / 10.7 / 19.3 (the tensor-core GEMV, 6.2 / 6.6 / 7.2 us, takes
+    // M > 2).  The QKV epilogue needs its two columns per warp.
+    if constexpr (kM == 1 && std::is_same<Extra, GvQkv>::value)
+        return launch_gemv_cfg<1, 2, 8, 128>(ctx, g, aligned, x);
+    else
+        return launch_gemv_cfg<kM, 1, 8, 128>(ctx, g, aligned, x);
+}
+
+template <int kM, int kCols, int kUnroll, int kThreads, typename Extra>
+cudaError_t launch_gemv_cfg(const LaunchCtx &ctx, const GvParams &g, bool aligned, const Extra &x) {
     constexpr int kColsPerCta = kThreads / 32 * kCols;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((g.N + kColsPerCta - 1) / kColsPerCta, 1, 1);
@@ -1809,7 +1823,7 @@ cudaError_t gemv_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
 cudaError_t matmul_i8_gemv(const LaunchCtx &ctx, const MatmulI8 &p) {
     const GvParams g = gv_params(p);
     const bool aligned = (reinterpret_cast<uintptr_t>(p.A) % 16u == 0u) && (p.lda % 16u == 0u);
-    bool use_tc = p.M > 1;
+    bool use_tc = p.M > 2;
     if (const char *e = std::getenv("VNPU_B200_DECODE")) use_tc = std::strcmp(e, "tc") == 0;
     if (std::getenv("VNPU_B200_SIMT_GEMV")) use_tc = false;
     if (use_tc && aligned && p.K >= 16u && p.tmap_b128) {

@@ -484,7 +484,10 @@ def test_decode_tensor_core_vs_simt(gpu, oracle, monkeypatch, M, K, N):
     outs = []
     for simt in (False, True):
         if simt:
+            monkeypatch.delenv("VNPU_B200_DECODE", raising=False)
             monkeypatch.setenv("VNPU_B200_SIMT_GEMV", "1")
+        else:
+            monkeypatch.setenv("VNPU_B200_DECODE", "tc")   # the tensor core for every M
         outs.append(run_matmul(gpu, A, B, sa, sb, bias, 0, 2))
     monkeypatch.delenv("VNPU_B200_SIMT_GEMV", raising=False)
     assert bits_equal(outs[0], outs[1])
