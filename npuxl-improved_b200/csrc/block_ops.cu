@@ -387,6 +387,8 @@ struct AttParams {
     float *O;
     uint32_t heads, seq_q, seq_k, D, causal;
     float scale;
+    uint32_t *err;       // stream error word (bounded waits)
+    uint64_t wait_ns;    // bound of every device-side wait
 };
 
 // Layout in shared memory:
@@ -1022,19 +1024,69 @@ __device__ __forceinline__ float dot_hsum256(const float *qs, const float *krow,
                      __fadd_rn(__fadd_rn(c[2], c[6]), __fadd_rn(c[3], c[7])));
 }
 
+// dot_hsum256 with the key row in shared memory (plain loads).
+__device__ __forceinline__ float dot_hsum256_shared(const float *qs, const float *krow,
+                                                    uint32_t D) {
+    float c[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const float4 *k4 = reinterpret_cast<const float4 *>(krow);
+    const float4 *q4 = reinterpret_cast<const float4 *>(qs);
+#pragma unroll 4
+    for (uint32_t t = 0; t < D / 8; ++t) {
+        const float4 ka = k4[2 * t], kb = k4[2 * t + 1];
+        const float4 qa = q4[2 * t], qb = q4[2 * t + 1];
+        c[0] = __fmaf_rn(qa.x, ka.x, c[0]);
+        c[1] = __fmaf_rn(qa.y, ka.y, c[1]);
+        c[2] = __fmaf_rn(qa.z, ka.z, c[2]);
+        c[3] = __fmaf_rn(qa.w, ka.w, c[3]);
+        c[4] = __fmaf_rn(qb.x, kb.x, c[4]);
+        c[5] = __fmaf_rn(qb.y, kb.y, c[5]);
+        c[6] = __fmaf_rn(qb.z, kb.z, c[6]);
+        c[7] = __fmaf_rn(qb.w, kb.w, c[7]);
+    }
+    return __fadd_rn(__fadd_rn(__fadd_rn(c[0], c[4]), __fadd_rn(c[1], c[5])),
+                     __fadd_rn(__fadd_rn(c[2], c[6]), __fadd_rn(c[3], c[7])));
+}
+
+// Shared memory of the decode cluster kernel, in floats (the host sizes it
+// with the same function): V slice [L][D/4], K rows of this CTA's key range
+// [span][D+4], q [D], S [L], the compacted nonzero keys and probabilities
+// [L] + [L], then per-block words and two mbarriers.
+constexpr uint32_t kDcVBox = 64;   // V rows per TMA box
+// This CTA's K rows, [span][D+4] (padded: no bank conflicts in the scores).
+__host__ __device__ inline size_t dc_region_floats(uint32_t L, uint32_t D) {
+    const size_t span = (L + kDcCluster - 1) / kDcCluster;
+    return span * (D + 4);
+}
+__host__ __device__ inline size_t dc_smem_floats(uint32_t L, uint32_t D) {
+    const size_t nblk = (L + kAttBK - 1) / kAttBK;
+    const size_t vrows = (L + kDcVBox - 1) / kDcVBox * kDcVBox;   // whole boxes
+    const size_t words = vrows * (D / kDcCluster) + dc_region_floats(L, D) + D + 3 * L + 6 * nblk + 1;
+    return (words + 3) / 4 * 4 + 4;   // + two 8-byte mbarriers, 16-byte aligned
+}
+
 __global__ void __cluster_dims__(kDcCluster, 1, 1) __launch_bounds__(kDcThreads)
-    attention_decode_cluster_kernel(const AttParams p) {
+    attention_decode_cluster_kernel(const AttParams p, const __grid_constant__ CUtensorMap vmap) {
     pdl_enter();
     extern __shared__ __align__(16) float dc_smem[];
     const uint32_t D = p.D, L = p.seq_k;
     const uint32_t nblk = (L + kAttBK - 1) / kAttBK;
     const uint32_t dslice = D / kDcCluster;
-    float *Vs = dc_smem;                                   // [L][dslice]
-    float *qs = Vs + static_cast<size_t>(L) * dslice;     // [D]
+    const uint32_t span = (L + kDcCluster - 1) / kDcCluster;
+    const uint32_t kld = D + 4;                            // padded K row: no bank conflicts
+    const uint32_t vboxes = (L + kDcVBox - 1) / kDcVBox;
+    float *Vs = dc_smem;                                   // [vboxes * 64][dslice]
+    float *Ks = Vs + static_cast<size_t>(vboxes) * kDcVBox * dslice;   // [span][kld]
+    float *qs = Ks + dc_region_floats(L, D);               // [D]
     float *S = qs + D;                                     // [L]
-    float *alpha_b = S + L;                                // [nblk]
+    float *nz_p = S + L;                                   // [L] nonzero probabilities, per block
+    int *nz_k = reinterpret_cast<int *>(nz_p + L);         // [L] their keys
+    float *alpha_b = reinterpret_cast<float *>(nz_k + L);  // [nblk]
     int *active_b = reinterpret_cast<int *>(alpha_b + nblk);
-    float *l_sh = reinterpret_cast<float *>(active_b + nblk);
+    int *nz_cnt = active_b + nblk;                         // [nblk]
+    float *nm_b = reinterpret_cast<float *>(nz_cnt + nblk);   // [nblk]
+    float *sum_b = nm_b + nblk;                            // [nblk]
+    float *l_sh = sum_b + nblk;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(dc_smem + dc_smem_floats(L, D) - 4);
 
     const uint32_t tid = threadIdx.x, lane = tid & 31;
     const uint32_t rank = cluster_ctarank();
@@ -1044,26 +1096,40 @@ __global__ void __cluster_dims__(kDcCluster, 1, 1) __launch_bounds__(kDcThreads)
     const float *Vh = p.V + static_cast<uint64_t>(bh) * L * D;
     const float *Mh = p.mask ? p.mask + static_cast<uint64_t>(bh) * L : nullptr;
     const uint32_t d0 = rank * dslice;
+    const uint32_t k_lo = min(L, rank * span), k_hi = min(L, k_lo + span);
+    const uint32_t krows = k_hi - k_lo;
 
-    // 0. V slice -> shared memory, asynchronously.
-    const uint32_t per_key = dslice / 4;   // 16-byte pieces per key
-    for (uint32_t i = tid; i < L * per_key; i += kDcThreads) {
-        const uint32_t j = i / per_key, c = i % per_key;
-        cp_async_16(Vs + static_cast<size_t>(j) * dslice + 4 * c,
-                    Vh + static_cast<uint64_t>(j) * D + d0 + 4 * c);
+    // 0. The TMA unit copies this CTA's K rows (one bulk copy per row, into
+    //    padded rows) and its V slice (64-row boxes of the [rows][D] tensor
+    //    map: the rows of this head, columns [d0, d0 + dslice)) into shared
+    //    memory; bars[0] counts the K bytes, bars[1] the V bytes.
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_barrier_init();
+        mbar_arrive_expect_tx(&bars[0], krows * D * 4u);
+        mbar_arrive_expect_tx(&bars[1], vboxes * kDcVBox * dslice * 4u);
+        for (uint32_t v = 0; v < vboxes; ++v)
+            tma_load_2d(Vs + static_cast<size_t>(v) * kDcVBox * dslice, &vmap, &bars[1],
+                        static_cast<int32_t>(d0), static_cast<int32_t>(bh * L + v * kDcVBox));
     }
+    __syncthreads();
+    for (uint32_t r = tid; r < krows; r += kDcThreads)
+        bulk_load_1d(Ks + static_cast<size_t>(r) * kld, Kh + static_cast<uint64_t>(k_lo + r) * D,
+                     D * 4u, &bars[0]);
+    (void)Vh;
     for (uint32_t i = tid; i < D; i += kDcThreads) qs[i] = Qh[i];
     __syncthreads();
+    // A timed-out wait leaves an error in the stream's word; the CTA carries
+    // on to the cluster barriers so that its partners do not wait for it.
+    mbar_wait(&bars[0], 0, p.wait_ns, p.err, nullptr);
 
-    // A. scores of keys [k_lo, k_hi)
-    const uint32_t span = (L + kDcCluster - 1) / kDcCluster;
-    const uint32_t k_lo = min(L, rank * span), k_hi = min(L, k_lo + span);
-    for (uint32_t ki = k_lo + tid; ki < k_hi; ki += kDcThreads) {
-        const float *krow = Kh + static_cast<uint64_t>(ki) * D;
-        const float dot = D == 128 ? dot_hsum256<16>(qs, krow, D) : dot_hsum256<0>(qs, krow, D);
+    // A. scores of keys [k_lo, k_hi), from the K rows in shared memory
+    for (uint32_t r = tid; r < krows; r += kDcThreads) {
+        const float dot = dot_hsum256_shared(qs, Ks + static_cast<size_t>(r) * kld, D);
         float sc = __fmul_rn(dot, p.scale);
-        if (Mh) sc = __fadd_rn(sc, Mh[ki]);
-        S[ki] = sc;   // decode: the causal limit seq_k - 1 masks no key
+        if (Mh) sc = __fadd_rn(sc, Mh[k_lo + r]);
+        S[k_lo + r] = sc;   // decode: the causal limit seq_k - 1 masks no key
     }
     cluster_sync_all();   // every range written
     for (uint32_t ki = tid; ki < L; ki += kDcThreads) {
@@ -1075,12 +1141,11 @@ __global__ void __cluster_dims__(kDcCluster, 1, 1) __launch_bounds__(kDcThreads)
     // B. online softmax.  The running max before block b is the max of the
     // finite block maxima up to b, so: (1) warps find every block's max;
     // (2) thread 0 walks the blocks for the running max and alpha;
-    // (3) warps exponentiate and sum their blocks (each sum in key order);
+    // (3) warps exponentiate and sum their blocks (each sum in key order)
+    //     and list each block's nonzero probabilities in key order;
     // (4) thread 0 folds l = l*alpha + sum over the blocks in order.
     const uint32_t warp = tid >> 5;
     const float ninf = -__int_as_float(0x7f800000);
-    float *nm_b = l_sh + 1;            // [nblk] running max of each active block
-    float *sum_b = nm_b + nblk;        // [nblk]
     for (uint32_t b = warp; b < nblk; b += kDcThreads / 32) {
         const uint32_t k0 = b * kAttBK, kc = min(kAttBK, L - k0);
         const float s_lo = lane < kc ? S[k0 + lane] : ninf;
@@ -1126,7 +1191,25 @@ __global__ void __cluster_dims__(kDcCluster, 1, 1) __launch_bounds__(kDcThreads)
             const float v = __shfl_sync(0xffffffffu, p_hi, j);
             if (j + 32 < kc) sum_p = __fadd_rn(sum_p, v);
         }
-        if (lane == 0) sum_b[b] = sum_p;
+        // The value chain skips p == 0 (as the reference does): keep the
+        // others, in key order.
+        const uint32_t m_lo = __ballot_sync(0xffffffffu, lane < kc && p_lo != 0.0f);
+        const uint32_t m_hi = __ballot_sync(0xffffffffu, lane + 32 < kc && p_hi != 0.0f);
+        const uint32_t below = (1u << lane) - 1u;
+        if ((m_lo >> lane) & 1u) {
+            const uint32_t at = k0 + __popc(m_lo & below);
+            nz_p[at] = p_lo;
+            nz_k[at] = static_cast<int>(k0 + lane);
+        }
+        if ((m_hi >> lane) & 1u) {
+            const uint32_t at = k0 + __popc(m_lo) + __popc(m_hi & below);
+            nz_p[at] = p_hi;
+            nz_k[at] = static_cast<int>(k0 + lane + 32);
+        }
+        if (lane == 0) {
+            sum_b[b] = sum_p;
+            nz_cnt[b] = static_cast<int>(__popc(m_lo) + __popc(m_hi));
+        }
     }
     __syncthreads();
     if (tid == 0) {
@@ -1135,15 +1218,82 @@ __global__ void __cluster_dims__(kDcCluster, 1, 1) __launch_bounds__(kDcThreads)
             if (active_b[b]) l_run = __fadd_rn(__fmul_rn(l_run, alpha_b[b]), sum_b[b]);
         *l_sh = l_run;
     }
-    cp_async_wait_all();
+    mbar_wait(&bars[1], 0, p.wait_ns, p.err, nullptr);
     __syncthreads();
 
-    // C. values of dims [d0, d0 + dslice), keys in order
+    // C. values of dims [d0, d0 + dslice): acc = acc*alpha_b per active
+    // block, then fma(V[k][d], p_k, acc) over the block's keys in order,
+    // skipping p == 0: blocks without a zero run a plain FMA chain, the
+    // others walk their list of nonzero keys.
     if (tid < dslice) {
         const float l = *l_sh;
         const float inv = l > 0.0f ? __fdiv_rn(1.0f, l) : 0.0f;
-        const float a = dslice == 32 ? value_chain<32>(Vs, S, alpha_b, active_b, nblk, L, tid)
-                                     : value_chain<0>(Vs, S, alpha_b, active_b, nblk, L, tid, dslice);
+        const float *vcol = Vs + tid;   // V[k][d0 + tid] = vcol[k * dslice]
+        float a = 0.0f;
+        for (uint32_t b = 0; b < nblk; ++b) {
+            if (!active_b[b]) continue;
+            a = __fmul_rn(a, alpha_b[b]);
+            const uint32_t k0 = b * kAttBK, kc = min(kAttBK, L - k0);
+            if (static_cast<uint32_t>(nz_cnt[b]) == kc) {
+                // 16-key chunks, the next chunk's V values and probabilities
+                // loaded while the current one runs through the chain.
+                const uint32_t chunks = kc / 16;
+                float vv[2][16], pv[2][16];
+                auto load = [&](uint32_t c, float *v, float *pp) {
+                    const uint32_t k = k0 + c * 16;
+#pragma unroll
+                    for (uint32_t u = 0; u < 16; ++u) v[u] = vcol[static_cast<size_t>(k + u) * dslice];
+#pragma unroll
+                    for (uint32_t q = 0; q < 4; ++q) {
+                        const float4 p4 = *reinterpret_cast<const float4 *>(S + k + 4 * q);
+                        pp[4 * q] = p4.x;
+                        pp[4 * q + 1] = p4.y;
+                        pp[4 * q + 2] = p4.z;
+                        pp[4 * q + 3] = p4.w;
+                    }
+                };
+                if (chunks) load(0, vv[0], pv[0]);
+                for (uint32_t c = 0; c < chunks; c += 2) {
+                    if (c + 1 < chunks) load(c + 1, vv[1], pv[1]);
+#pragma unroll
+                    for (uint32_t u = 0; u < 16; ++u) a = __fmaf_rn(vv[0][u], pv[0][u], a);
+                    if (c + 1 >= chunks) break;
+                    if (c + 2 < chunks) load(c + 2, vv[0], pv[0]);
+#pragma unroll
+                    for (uint32_t u = 0; u < 16; ++u) a = __fmaf_rn(vv[1][u], pv[1][u], a);
+                }
+                for (uint32_t k = k0 + chunks * 16; k < k0 + kc; ++k)
+                    a = __fmaf_rn(vcol[static_cast<size_t>(k) * dslice], S[k], a);
+                continue;
+            }
+            const uint32_t n = static_cast<uint32_t>(nz_cnt[b]);
+            // Groups of 8 keys, the next group's keys, probabilities and V
+            // values loaded while the current one runs through the chain.
+            const uint32_t groups = n / 8;
+            float pv[2][8], vv[2][8];
+            auto load = [&](uint32_t g, float *pp, float *vp) {
+                int kk[8];
+#pragma unroll
+                for (uint32_t u = 0; u < 8; ++u) kk[u] = nz_k[k0 + g * 8 + u];
+#pragma unroll
+                for (uint32_t u = 0; u < 8; ++u) {
+                    pp[u] = nz_p[k0 + g * 8 + u];
+                    vp[u] = vcol[static_cast<size_t>(kk[u]) * dslice];
+                }
+            };
+            if (groups) load(0, pv[0], vv[0]);
+            for (uint32_t g = 0; g < groups; g += 2) {
+                if (g + 1 < groups) load(g + 1, pv[1], vv[1]);
+#pragma unroll
+                for (uint32_t u = 0; u < 8; ++u) a = __fmaf_rn(vv[0][u], pv[0][u], a);
+                if (g + 1 >= groups) break;
+                if (g + 2 < groups) load(g + 2, pv[0], vv[0]);
+#pragma unroll
+                for (uint32_t u = 0; u < 8; ++u) a = __fmaf_rn(vv[1][u], pv[1][u], a);
+            }
+            for (uint32_t i = groups * 8; i < n; ++i)
+                a = __fmaf_rn(vcol[static_cast<size_t>(nz_k[k0 + i]) * dslice], nz_p[k0 + i], a);
+        }
         p.O[static_cast<uint64_t>(bh) * D + d0 + tid] = __fmul_rn(a, inv);
     }
 }
@@ -1442,11 +1592,12 @@ cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, cons
     ap.D = head_dim;
     ap.causal = causal;
     ap.scale = scale;
+    ap.err = ctx.err;
+    ap.wait_ns = ctx.wait_limit_ns;
     const char *attn_env = std::getenv("VNPU_B200_ATTN");   // general | decode | cluster
     const bool force_general = attn_env && !std::strcmp(attn_env, "general");
     const bool allow_cluster = !(attn_env && !std::strcmp(attn_env, "decode"));
-    const size_t dc_smem = sizeof(float) * (static_cast<size_t>(seq_k) * (head_dim / kDcCluster) +
-                                            head_dim + seq_k + 4 * ((seq_k + kAttBK - 1) / kAttBK) + 1);
+    const size_t dc_smem = sizeof(float) * dc_smem_floats(seq_k, head_dim);
     if (seq_q == 1 && !force_general && allow_cluster && head_dim % 16 == 0 &&
         (reinterpret_cast<uintptr_t>(V) & 15) == 0 && (reinterpret_cast<uintptr_t>(K) & 15) == 0 &&
         (reinterpret_cast<uintptr_t>(Q) & 15) == 0 && dc_smem <= kDcMaxSmem) {
@@ -1458,7 +1609,14 @@ cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, cons
             if (e != cudaSuccess) return e;
             dc_configured[dev] = true;
         }
-        VNPU_LAUNCH(launch_pdl(ctx.stream, attention_decode_cluster_kernel, dim3(batch * heads * kDcCluster), dim3(kDcThreads), dc_smem, ap));
+        CUtensorMap vmap;
+        if (!encode_tmap_2d(&vmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, V, head_dim,
+                            static_cast<uint64_t>(batch) * heads * seq_k, head_dim * 4ull,
+                            head_dim / kDcCluster, kDcVBox, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return cudaErrorInvalidValue;
+        VNPU_LAUNCH(launch_pdl(ctx.stream, attention_decode_cluster_kernel,
+                               dim3(batch * heads * kDcCluster), dim3(kDcThreads), dc_smem, ap,
+                               vmap));
         count_launch(ctx);
         return cudaGetLastError();
     }

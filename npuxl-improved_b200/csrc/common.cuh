@@ -274,6 +274,18 @@ __device__ __forceinline__ void tma_store_2d(const void *tmap, const void *smem_
         "r"(smem_addr(smem_src)), "r"(x), "r"(y)
         : "memory");
 }
+// One contiguous global -> shared copy by the TMA unit (no tensor map, no
+// multicast): both addresses 16-byte aligned, bytes a multiple of 16; the
+// bytes complete on `bar` (expect them with mbar_arrive_expect_tx).
+__device__ __forceinline__ void bulk_load_1d(void *smem_dst, const void *gmem_src, uint32_t bytes,
+                                             uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_addr(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
