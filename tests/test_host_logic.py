@@ -82,10 +82,36 @@ def test_null_arguments(b200_lib):
     assert b200_lib.packed_weights_info(None, None, None, None, None, None) \
         == vnpu.ERR_INVALID_ARGUMENT
     assert b200_lib.matmul_i8(None, None) == vnpu.ERR_INVALID_ARGUMENT
-    h.vnpu_cluster_create.restype = C.c_int
-    assert h.vnpu_cluster_create(None, C.byref(vnpu.vp())) == vnpu.ERR_UNSUPPORTED
     h.vnpu_node_run.restype = C.c_int
     assert h.vnpu_node_run(None) == vnpu.ERR_UNSUPPORTED
+
+
+def test_cluster_without_devices(b200_lib):
+    """The local cluster's host logic (src/cluster/cluster.cpp:243-546): a
+    cluster with no worker refuses a GEMM with DEVICE_ERROR, remote nodes are
+    unsupported, weights are cached, stats start at zero."""
+    lib = b200_lib
+    cl = vnpu.vp()
+    assert lib.cluster_create(None, C.byref(cl)) == vnpu.OK and cl.value
+    try:
+        B = np.arange(12, dtype=np.float32).reshape(3, 4)
+        h = vnpu.vp()
+        assert lib.cluster_cache_weights_f32(cl, b"w", B.ctypes.data, 3, 4, 0, C.byref(h)) == vnpu.OK
+        assert lib.cluster_cache_weights_f32(cl, b"w", B.ctypes.data, 3, 4, 2,
+                                             C.byref(vnpu.vp())) == vnpu.ERR_INVALID_ARGUMENT
+        A = np.ones((2, 3), np.float32)
+        Cm = np.zeros((2, 4), np.float32)
+        assert lib.cluster_matmul_f32(cl, h, A.ctypes.data, Cm.ctypes.data, 2, 3, 4, 0) \
+            == vnpu.ERR_DEVICE_ERROR
+        assert lib.cluster_matmul_f32(cl, h, A.ctypes.data, Cm.ctypes.data, 2, 5, 4, 0) \
+            == vnpu.ERR_INVALID_ARGUMENT
+        assert lib.cluster_add_remote(cl, None, C.byref(vnpu.vp())) == vnpu.ERR_UNSUPPORTED
+        st = vnpu.ClusterStats()
+        assert lib.cluster_get_stats(cl, C.byref(st)) == vnpu.OK
+        assert st.total_jobs == 0 and st.local_jobs == 0
+        assert lib.cluster_add_device(cl, None, 1) == vnpu.ERR_INVALID_ARGUMENT
+    finally:
+        lib.cluster_destroy(cl)
 
 
 def test_events_without_work(b200_lib):
