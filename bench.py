@@ -311,6 +311,30 @@ def gemm_secondary(lib, dev, st, torch, M, K, N, epi, with_bias, iters=20):
         ms_g = e0.elapsed_time(e1) / 200
         lib.b200_graph_destroy(graph)
         out.update({"ms_graph": ms_g, "tops_graph": 2.0 * M * K * N / ms_g / 1e9})
+        # Library comparator at the same launch-bound size: cuBLAS int8
+        # (torch._int_mm) in a CUDA graph of 20 launches.
+        try:
+            A_ = torch.randint(-128, 128, (M, K), dtype=torch.int8, device="cuda")
+            B_ = torch.randint(-128, 128, (N, K), dtype=torch.int8, device="cuda").t()
+            torch._int_mm(A_, B_)
+            torch.cuda.synchronize()
+            g_ = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_):
+                for _ in range(20):
+                    torch._int_mm(A_, B_)
+            g_.replay()
+            torch.cuda.synchronize()
+            c0 = torch.cuda.Event(enable_timing=True)
+            c1 = torch.cuda.Event(enable_timing=True)
+            c0.record()
+            for _ in range(10):
+                g_.replay()
+            c1.record()
+            torch.cuda.synchronize()
+            out["cublas_int8_ms_graph"] = c0.elapsed_time(c1) / 200
+            del g_, A_, B_
+        except Exception as exc:  # library comparator only
+            out["cublas_int8_ms_graph"] = f"unavailable: {exc}"
     dev.unpack(w)
     return out
 
