@@ -194,6 +194,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ volatile int abort_flag;
 
     // 1024-byte aligned tile ring (128B swizzle atoms are 1024 bytes).
+    // The stream's next kernel may be scheduled now; it waits for this one
+    // to finish before it touches memory.
+    pdl_launch_dependents();
     const uint32_t raw_addr = smem_addr(smem_raw);
     uint8_t *ring = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
 
@@ -223,6 +226,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // Set-up above overlapped the previous kernel of the stream; wait for it
+    // before the first global-memory access (a no-op without PDL).
+    pdl_wait_previous();
     const uint32_t tmem_base = tmem_base_slot;
 
     if (warp == 0) {
@@ -403,6 +409,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
     __shared__ uint32_t tmem_base_slot;
     __shared__ volatile int abort_flag;
 
+    // The stream's next kernel may be scheduled now; it waits for this one
+    // to finish before it touches memory.
+    pdl_launch_dependents();
     const uint32_t raw_addr = smem_addr(smem_raw);
     uint8_t *ring = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
 
@@ -436,6 +445,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
     tc_fence_before();
     cluster_sync_all();   // both CTAs' barriers initialised, tensor memory allocated
     tc_fence_after();
+    // Set-up above overlapped the previous kernel of the stream; wait for it
+    // before the first global-memory access (a no-op without PDL).
+    pdl_wait_previous();
     const uint32_t tmem_base = tmem_base_slot;
 
     if (warp == 0) {
@@ -682,6 +694,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     __shared__ uint32_t tmem_base_slot;
     __shared__ volatile int abort_flag;
 
+    // The stream's next kernel may be scheduled now; it waits for this one
+    // to finish before it touches memory.
+    pdl_launch_dependents();
     const uint32_t raw_addr = smem_addr(smem_raw);
     uint8_t *ring = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
 
@@ -714,6 +729,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     tc_fence_before();
     cluster_sync_all();   // both CTAs' barriers initialised, tensor memory allocated
     tc_fence_after();
+    // Set-up above overlapped the previous kernel of the stream; wait for it
+    // before the first global-memory access (a no-op without PDL).
+    pdl_wait_previous();
     const uint32_t tmem_base = tmem_base_slot;
 
     if (warp == 0) {
@@ -1631,8 +1649,9 @@ cudaError_t matmul_i8_scatter(const LaunchCtx &ctx, const MatmulI8 &p) {
     const uint32_t tiles = tp.tiles_m * tp.tiles_n;
     const uint32_t cap = static_cast<uint32_t>(max_pairs);
     const uint32_t pairs = tiles < cap ? tiles : cap;
-    gemm_i8_tcgen05_pair_kernel<8, 6><<<2 * pairs, pair_threads(8), pair_smem_bytes(8, 6),
-                                       ctx.stream>>>(tmap_a, *p.tmap_b128, tmap_c, tp);
+    VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, 6>, dim3(2 * pairs),
+                           dim3(pair_threads(8)), pair_smem_bytes(8, 6), tmap_a, *p.tmap_b128,
+                           tmap_c, tp));
     g_last_kernel.store("gemm_i8_tcgen05_pair_kernel", std::memory_order_relaxed);
     count_launch(ctx);
     return cudaGetLastError();
@@ -1696,14 +1715,17 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         const uint32_t cap = static_cast<uint32_t>(wide ? max_wide_pairs : max_pairs);
         const uint32_t pairs = tiles < cap ? tiles : cap;
         if (wide)
-            gemm_i8_tcgen05_pair_wide_kernel<<<2 * pairs, kPThreads, kWSmemBytes, ctx.stream>>>(
-                tmap_a, *p.tmap_b128, tmap_c, tp);
+            VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_wide_kernel, dim3(2 * pairs),
+                                   dim3(kPThreads), kWSmemBytes, tmap_a, *p.tmap_b128, tmap_c,
+                                   tp));
         else if (p.epilogue >= 2)   // SiLU, GELU: latency-bound epilogue, 16 warps
-            gemm_i8_tcgen05_pair_kernel<16, 5><<<2 * pairs, pair_threads(16), pair_smem_bytes(16, 5),
-                                                 ctx.stream>>>(tmap_a, *p.tmap_b128, tmap_c, tp);
+            VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<16, 5>, dim3(2 * pairs),
+                                   dim3(pair_threads(16)), pair_smem_bytes(16, 5), tmap_a,
+                                   *p.tmap_b128, tmap_c, tp));
         else
-            gemm_i8_tcgen05_pair_kernel<8, 6><<<2 * pairs, pair_threads(8), pair_smem_bytes(8, 6),
-                                               ctx.stream>>>(tmap_a, *p.tmap_b128, tmap_c, tp);
+            VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, 6>, dim3(2 * pairs),
+                                   dim3(pair_threads(8)), pair_smem_bytes(8, 6), tmap_a,
+                                   *p.tmap_b128, tmap_c, tp));
         g_last_kernel.store(wide ? "gemm_i8_tcgen05_pair_wide_kernel" : "gemm_i8_tcgen05_pair_kernel",
                             std::memory_order_relaxed);
         count_launch(ctx);
@@ -1734,7 +1756,8 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
     const uint32_t tiles = tp.tiles_m * tp.tiles_n;
     const uint32_t grid = tiles < static_cast<uint32_t>(ctx.num_sms) ? tiles
                                                                      : static_cast<uint32_t>(ctx.num_sms);
-    gemm_i8_tcgen05_kernel<<<grid, kThreads, kSmemBytes, ctx.stream>>>(tmap_a, *p.tmap_b, tp);
+    VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_kernel, dim3(grid), dim3(kThreads),
+                           kSmemBytes, tmap_a, *p.tmap_b, tp));
     g_last_kernel.store("gemm_i8_tcgen05_kernel", std::memory_order_relaxed);
     count_launch(ctx);
     return cudaGetLastError();
