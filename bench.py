@@ -784,8 +784,9 @@ def run_b200(args):
 
 def run_kernel_case(spec: str):
     """One small case of one kernel, launched twice (for ncu captures):
-    gemm:MxKxN[:silu], gemv:MxKxN, f32:MxKxN[:nt], quantize:RxC, attention:HxSQxSKxD, or
-    llm_decode:STEPS (the decoder block's graph-captured decode step)."""
+    gemm:MxKxN[:silu], gemv:MxKxN, f32:MxKxN[:nt], quantize:RxC, attention:HxSQxSKxD,
+    llm_prefill:T (the decoder block's prefill of T tokens, twice) or llm_decode:STEPS (the
+    decoder block's graph-captured decode step)."""
     import torch
 
     lib = vnpu.Lib(vnpu.LIB_PATH)
@@ -835,6 +836,18 @@ def run_kernel_case(spec: str):
         for _ in range(2):
             dev.attention(Q.data_ptr(), Kt.data_ptr(), V.data_ptr(), None, O.data_ptr(), 1, H,
                           SQ, SK, D, 1, 0.0)
+    elif kind == "llm_prefill":
+        # configs[3] decoder block: prefill T tokens twice (positions 0 and T).
+        from llm_block import B200Block, BlockConfig
+        T = shape[0]
+        cfg = BlockConfig(cap=2 * T)
+        blk = B200Block(cfg, lib, dev, torch)
+        x = torch.empty((T, cfg.d), device="cuda").normal_(0, 1, generator=g)
+        torch.cuda.synchronize()
+        blk.forward(x, 0)
+        blk.forward(x, T)
+        dev.sync()
+        blk.close()
     elif kind == "llm_decode":
         # configs[3] decoder block: prefill 512 tokens, capture one decode step
         # as a CUDA graph, replay it `steps` times.

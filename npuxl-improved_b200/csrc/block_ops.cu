@@ -598,40 +598,69 @@ __device__ __forceinline__ float fma_if_nonzero(float v, float p, float a) {
     return a;
 }
 
-// Prefill attention for head_dim 128, register-tiled, same arithmetic again.
-// One CTA (8 warps) per (batch*head, 16 queries); keys in blocks of 64.
-//   scores : warp w owns queries 2w, 2w+1; lane l keys 2l, 2l+1 of the block:
-//            each thread keeps the eight AVX2 chains of its 2 x 2 (query,
-//            key) pairs in registers (Q and K rows from padded shared
-//            memory), combines them in hsum256 order, *scale (+mask),
-//            causal keys -inf;
-//   softmax: the same warp, per query: block max, skip if not finite,
-//            fast_expf, in-order sum through shuffles, l = l*alpha + sum;
-//   values : the same warp, lane l dims 4l..4l+3 of both queries:
-//            acc = acc*alpha, then fma(V[j][d], p_j, acc) in key order with
-//            p == 0 skipped.
-// Only the K/V reload of the next block needs the whole CTA in step.
+// Prefill attention for head_dim 128: the same arithmetic again, tiled for
+// the CUDA cores.  One CTA (8 warps) per (batch*head, 64 queries), one CTA
+// per SM, the CTAs with the most causal keys first; K and V blocks of 64
+// keys double-buffered in shared memory by cp.async.  Warp w owns queries
+// 8w..8w+7 through all three phases, so only the block loads need the whole
+// CTA in step:
+//   scores : lane (qs, kl) = (lane/8, lane%8) computes queries 2qs, 2qs+1 x
+//            keys kl + 8u (u < 4) of a 32-key half: the eight AVX2 chains of
+//            each (query, key) pair in registers (Q and K rows from padded
+//            shared memory), combined in hsum256 order, *scale (+mask);
+//   softmax: lane (q, quarter) = (lane/4, lane%4) holds keys 16*quarter..+15
+//            of query q: causal and ragged keys -inf, block max, skip if not
+//            finite, fast_expf, the in-order sum handed from quarter to
+//            quarter, l = l*alpha + sum;
+//   values : lane l owns dims 4l..4l+3 of all 8 queries: acc = acc*alpha,
+//            then fma(V[j][d], p_j, acc) in key order.  The reference skips
+//            zero probabilities; where every query's nonzero probabilities
+//            are a prefix of the block (all keys, or a causal diagonal), the
+//            FMAs below the shortest prefix need no test.
 constexpr uint32_t kApThreads = 256;
+constexpr uint32_t kApBQ = 64;
 constexpr uint32_t kApD = 128;
-constexpr uint32_t kApRow = kApD + 4;     // padded row: 8 rows in distinct bank groups
+constexpr uint32_t kApRow = kApD + 4;     // padded Q/K row: 8 rows in distinct bank groups
+constexpr size_t kApSmemFloats = static_cast<size_t>(kApBQ) * kApRow + 2u * kAttBK * kApRow +
+                                 2u * kAttBK * kApD + static_cast<size_t>(kApBQ) * kAttBK;
 
 __device__ __forceinline__ float hsum256_chains(const float (&c)[8]) {
     return __fadd_rn(__fadd_rn(__fadd_rn(c[0], c[4]), __fadd_rn(c[1], c[5])),
                      __fadd_rn(__fadd_rn(c[2], c[6]), __fadd_rn(c[3], c[7])));
 }
 
-__global__ void __launch_bounds__(kApThreads, 2) attention_prefill_kernel(const AttParams p) {
+// Block k0 of K and V (64 rows; rows past seq_k zero) into one stage.
+__device__ __forceinline__ void ap_load_kv(float *Ks, float *Vs, const float *Kh, const float *Vh,
+                                           uint32_t k0, uint32_t seq_k, uint32_t tid) {
+#pragma unroll
+    for (uint32_t i = tid; i < kAttBK * kApD / 4; i += kApThreads) {
+        const uint32_t j = i >> 5, c4 = i & 31u;
+        const bool ok = k0 + j < seq_k;
+        const uint64_t row = ok ? k0 + j : k0;
+        cp_async_16_zfill(Ks + j * kApRow + 4 * c4, Kh + row * kApD + 4 * c4, ok);
+        cp_async_16_zfill(Vs + j * kApD + 4 * c4, Vh + row * kApD + 4 * c4, ok);
+    }
+}
+
+__device__ __forceinline__ void fma4(float4 &a, const float4 &v, float p) {
+    a.x = __fmaf_rn(v.x, p, a.x);
+    a.y = __fmaf_rn(v.y, p, a.y);
+    a.z = __fmaf_rn(v.z, p, a.z);
+    a.w = __fmaf_rn(v.w, p, a.w);
+}
+
+__global__ void __launch_bounds__(kApThreads, 1) attention_prefill_kernel(const AttParams p) {
     pdl_enter();
     extern __shared__ __align__(16) float ap_smem[];
-    float *Qs = ap_smem;                       // [16][kApRow]
-    float *Ks = Qs + kAttBQ * kApRow;          // [64][kApRow]
-    float *Vs = Ks + kAttBK * kApRow;          // [64][128]
-    float *S = Vs + kAttBK * kApD;             // [16][64] scores, then probabilities
+    float *Qs = ap_smem;                          // [64][kApRow]
+    float *Kst = Qs + kApBQ * kApRow;             // [2][64][kApRow]
+    float *Vst = Kst + 2 * kAttBK * kApRow;       // [2][64][128]
+    float *S = Vst + 2 * kAttBK * kApD;           // [64][64] scores, then probabilities
 
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t bh = blockIdx.y;
-    const uint32_t q0 = blockIdx.x * kAttBQ;
-    const uint32_t qc = min(kAttBQ, p.seq_q - q0);
+    const uint32_t bh = blockIdx.x;
+    const uint32_t q0 = (gridDim.y - 1 - blockIdx.y) * kApBQ;
+    const uint32_t qc = min(kApBQ, p.seq_q - q0);
     const uint64_t head_q = static_cast<uint64_t>(bh) * p.seq_q * kApD;
     const uint64_t head_k = static_cast<uint64_t>(bh) * p.seq_k * kApD;
     const float *Kh = p.K + head_k;
@@ -640,168 +669,237 @@ __global__ void __launch_bounds__(kApThreads, 2) attention_prefill_kernel(const 
     const uint32_t causal_offset = p.seq_k > p.seq_q ? p.seq_k - p.seq_q : 0;
     const float ninf = -__int_as_float(0x7f800000);
 
-    for (uint32_t i = tid; i < kAttBQ * kApD / 4; i += kApThreads) {
-        const uint32_t q = i / (kApD / 4), c4 = i % (kApD / 4);
-        const float4 v = q < qc ? __ldg(reinterpret_cast<const float4 *>(p.Q + head_q +
-                                                                          static_cast<uint64_t>(q0 + q) * kApD) + c4)
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
-        *reinterpret_cast<float4 *>(Qs + q * kApRow + 4 * c4) = v;
-    }
-
-    // Per-query state of the two queries this warp owns (lane-uniform).
-    const uint32_t qa = 2 * warp, qb = 2 * warp + 1;
-    float m_run[2] = {ninf, ninf}, l_run[2] = {0.0f, 0.0f};
-    float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
-
     uint32_t k_end = p.seq_k;
     if (p.causal) k_end = min(p.seq_k, q0 + qc - 1 + causal_offset + 1);
+    const uint32_t nblk = (k_end + kAttBK - 1) / kAttBK;
 
-    for (uint32_t k0 = 0; k0 < k_end; k0 += kAttBK) {
+    // Q rows (zero past seq_q) and the first K/V block: copy group 0.
+#pragma unroll
+    for (uint32_t i = tid; i < kApBQ * kApD / 4; i += kApThreads) {
+        const uint32_t q = i >> 5, c4 = i & 31u;
+        const bool ok = q < qc;
+        cp_async_16_zfill(Qs + q * kApRow + 4 * c4,
+                          p.Q + head_q + static_cast<uint64_t>(q0 + (ok ? q : 0u)) * kApD + 4 * c4, ok);
+    }
+    if (nblk > 0) ap_load_kv(Kst, Vst, Kh, Vh, 0, p.seq_k, tid);
+    cp_async_commit();
+
+    // softmax lanes: state of query row 8*warp + lane/4 (the four lanes agree)
+    const uint32_t sq = lane >> 2, quarter = lane & 3u;
+    const uint32_t srow = 8 * warp + sq;
+    const uint32_t sqi = q0 + srow;
+    float m_run = ninf, l_run = 0.0f;
+    // value lanes: dims 4*lane..4*lane+3 of the warp's 8 queries
+    float4 acc[8];
+#pragma unroll
+    for (uint32_t q = 0; q < 8; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+    const uint32_t wq_last = q0 + 8 * warp + 7;   // last query row of the warp
+    for (uint32_t b = 0; b < nblk; ++b) {
+        const uint32_t k0 = b * kAttBK;
         const uint32_t kc = min(kAttBK, p.seq_k - k0);
-        __syncthreads();  // the previous block's K and V are no longer read
-        for (uint32_t i = tid; i < kAttBK * kApD / 4; i += kApThreads) {
-            const uint32_t j = i / (kApD / 4), c4 = i % (kApD / 4);
-            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-            if (j < kc) {
-                kv = __ldg(reinterpret_cast<const float4 *>(Kh + static_cast<uint64_t>(k0 + j) * kApD) + c4);
-                vv = __ldg(reinterpret_cast<const float4 *>(Vh + static_cast<uint64_t>(k0 + j) * kApD) + c4);
-            }
-            *reinterpret_cast<float4 *>(Ks + j * kApRow + 4 * c4) = kv;
-            *reinterpret_cast<float4 *>(Vs + j * kApD + 4 * c4) = vv;
+        if (b + 1 < nblk) {
+            const uint32_t nx = (b + 1) & 1u;
+            ap_load_kv(Kst + nx * kAttBK * kApRow, Vst + nx * kAttBK * kApD, Kh, Vh, k0 + kAttBK,
+                       p.seq_k, tid);
+            cp_async_commit();
+            cp_async_wait_group<1>();
+        } else {
+            cp_async_wait_group<0>();
         }
-        __syncthreads();  // K, V (and Q on the first block) in shared memory
+        __syncthreads();   // block b (and Q) visible to every warp
+        const float *Ks = Kst + (b & 1u) * kAttBK * kApRow;
+        const float *Vs = Vst + (b & 1u) * kAttBK * kApD;
 
-        // ---- scores of queries qa, qb x keys 2*lane, 2*lane+1
+        // ---- scores: queries qa, qa+1 x keys jb + kl + 8u
         {
-            float c[4][8];
+            const uint32_t qs = lane >> 3, kl = lane & 7u;
+            const uint32_t qa = 8 * warp + 2 * qs;
+            const float *qra = Qs + qa * kApRow, *qrb = qra + kApRow;
+#pragma unroll 1
+            for (uint32_t jb = 0; jb < kAttBK; jb += 32) {
+                // a half whose keys are past kc, or causal-masked for every
+                // query of the warp, is left out (the softmax masks it)
+                if (jb >= kc || (p.causal && k0 + jb > wq_last + causal_offset)) break;
+                float c[2][4][8];
+#pragma unroll
+                for (uint32_t h = 0; h < 2; ++h)
+#pragma unroll
+                    for (uint32_t u = 0; u < 4; ++u)
+#pragma unroll
+                        for (uint32_t y = 0; y < 8; ++y) c[h][u][y] = 0.0f;
+                const float *kr = Ks + (jb + kl) * kApRow;
+#pragma unroll 2
+                for (uint32_t t = 0; t < kApD / 8; ++t) {
+                    const float4 a0 = *reinterpret_cast<const float4 *>(qra + 8 * t);
+                    const float4 a1 = *reinterpret_cast<const float4 *>(qra + 8 * t + 4);
+                    const float4 b0 = *reinterpret_cast<const float4 *>(qrb + 8 * t);
+                    const float4 b1 = *reinterpret_cast<const float4 *>(qrb + 8 * t + 4);
+#pragma unroll
+                    for (uint32_t u = 0; u < 4; ++u) {
+                        const float4 x0 = *reinterpret_cast<const float4 *>(kr + 8 * u * kApRow + 8 * t);
+                        const float4 x1 =
+                            *reinterpret_cast<const float4 *>(kr + 8 * u * kApRow + 8 * t + 4);
+#define VNPU_AP_CHAINS(ACC, Q0, Q1)                 \
+    ACC[0] = __fmaf_rn(Q0.x, x0.x, ACC[0]);         \
+    ACC[1] = __fmaf_rn(Q0.y, x0.y, ACC[1]);         \
+    ACC[2] = __fmaf_rn(Q0.z, x0.z, ACC[2]);         \
+    ACC[3] = __fmaf_rn(Q0.w, x0.w, ACC[3]);         \
+    ACC[4] = __fmaf_rn(Q1.x, x1.x, ACC[4]);         \
+    ACC[5] = __fmaf_rn(Q1.y, x1.y, ACC[5]);         \
+    ACC[6] = __fmaf_rn(Q1.z, x1.z, ACC[6]);         \
+    ACC[7] = __fmaf_rn(Q1.w, x1.w, ACC[7]);
+                        VNPU_AP_CHAINS(c[0][u], a0, a1)
+                        VNPU_AP_CHAINS(c[1][u], b0, b1)
+#undef VNPU_AP_CHAINS
+                    }
+                }
+#pragma unroll
+                for (uint32_t h = 0; h < 2; ++h)
+#pragma unroll
+                    for (uint32_t u = 0; u < 4; ++u) {
+                        const uint32_t q = qa + h, j = jb + kl + 8 * u;
+                        const uint32_t qi = q0 + q;
+                        float sc = __fmul_rn(hsum256_chains(c[h][u]), p.scale);
+                        if (Mh && qi < p.seq_q && j < kc)
+                            sc = __fadd_rn(sc, Mh[static_cast<uint64_t>(qi) * p.seq_k + k0 + j]);
+                        S[q * kAttBK + j] = sc;
+                    }
+            }
+        }
+        __syncwarp();
+
+        // ---- online softmax, lane (sq, quarter)
+        float alpha = 1.0f;
+        uint32_t info;   // bit 0 active, bit 1 nonzero keys form a prefix, bits 2.. their count
+        {
+            float *Sr = S + srow * kAttBK + 16 * quarter;
+            float s[16];
+#pragma unroll
+            for (uint32_t i4 = 0; i4 < 4; ++i4) {
+                const float4 v = *reinterpret_cast<const float4 *>(Sr + 4 * i4);
+                s[4 * i4] = v.x;
+                s[4 * i4 + 1] = v.y;
+                s[4 * i4 + 2] = v.z;
+                s[4 * i4 + 3] = v.w;
+            }
+            float bmax = ninf;
+#pragma unroll
+            for (uint32_t i = 0; i < 16; ++i) {
+                const uint32_t j = 16 * quarter + i;
+                if (j >= kc || (p.causal && k0 + j > sqi + causal_offset)) s[i] = ninf;
+                bmax = fmaxf(bmax, s[i]);
+            }
+            bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));
+            bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 2));
+            const bool act = isfinite(bmax);   // fully masked block: skipped, as in the reference
+            const float nm = fmaxf(m_run, bmax);
+            float pr[16];
+            uint32_t nzm = 0;
+#pragma unroll
+            for (uint32_t i = 0; i < 16; ++i) {
+                pr[i] = act && 16 * quarter + i < kc ? ref_fast_expf(__fsub_rn(s[i], nm), false)
+                                                     : 0.0f;
+                nzm |= (pr[i] != 0.0f ? 1u : 0u) << i;
+            }
+            if (act) alpha = ref_fast_expf(__fsub_rn(m_run, nm), false);
+            float run = 0.0f;
+#pragma unroll
+            for (uint32_t ph = 0; ph < 4; ++ph) {
+                if (quarter == ph && act) {
+#pragma unroll
+                    for (uint32_t i = 0; i < 16; ++i)
+                        if (16 * ph + i < kc) run = __fadd_rn(run, pr[i]);
+                }
+                run = __shfl_sync(0xffffffffu, run, (lane & ~3u) | ph);
+            }
+            if (act) {
+                l_run = __fadd_rn(__fmul_rn(l_run, alpha), run);
+                m_run = nm;
+            }
+#pragma unroll
+            for (uint32_t i4 = 0; i4 < 4; ++i4)
+                *reinterpret_cast<float4 *>(Sr + 4 * i4) =
+                    make_float4(pr[4 * i4], pr[4 * i4 + 1], pr[4 * i4 + 2], pr[4 * i4 + 3]);
+            uint64_t nz = 0;
 #pragma unroll
             for (uint32_t x = 0; x < 4; ++x)
-#pragma unroll
-                for (uint32_t y = 0; y < 8; ++y) c[x][y] = 0.0f;
-            const float *qra = Qs + qa * kApRow, *qrb = Qs + qb * kApRow;
-            const float *kra = Ks + lane * kApRow, *krb = Ks + (lane + 32) * kApRow;
-#pragma unroll 4
-            for (uint32_t t = 0; t < kApD / 8; ++t) {
-                const float4 a0 = *reinterpret_cast<const float4 *>(qra + 8 * t);
-                const float4 a1 = *reinterpret_cast<const float4 *>(qra + 8 * t + 4);
-                const float4 b0 = *reinterpret_cast<const float4 *>(qrb + 8 * t);
-                const float4 b1 = *reinterpret_cast<const float4 *>(qrb + 8 * t + 4);
-                const float4 x0 = *reinterpret_cast<const float4 *>(kra + 8 * t);
-                const float4 x1 = *reinterpret_cast<const float4 *>(kra + 8 * t + 4);
-                const float4 y0 = *reinterpret_cast<const float4 *>(krb + 8 * t);
-                const float4 y1 = *reinterpret_cast<const float4 *>(krb + 8 * t + 4);
-#define VNPU_AP_CHAINS(ACC, Q0, Q1, K0, K1)                 \
-    ACC[0] = __fmaf_rn(Q0.x, K0.x, ACC[0]);                 \
-    ACC[1] = __fmaf_rn(Q0.y, K0.y, ACC[1]);                 \
-    ACC[2] = __fmaf_rn(Q0.z, K0.z, ACC[2]);                 \
-    ACC[3] = __fmaf_rn(Q0.w, K0.w, ACC[3]);                 \
-    ACC[4] = __fmaf_rn(Q1.x, K1.x, ACC[4]);                 \
-    ACC[5] = __fmaf_rn(Q1.y, K1.y, ACC[5]);                 \
-    ACC[6] = __fmaf_rn(Q1.z, K1.z, ACC[6]);                 \
-    ACC[7] = __fmaf_rn(Q1.w, K1.w, ACC[7]);
-                VNPU_AP_CHAINS(c[0], a0, a1, x0, x1)
-                VNPU_AP_CHAINS(c[1], a0, a1, y0, y1)
-                VNPU_AP_CHAINS(c[2], b0, b1, x0, x1)
-                VNPU_AP_CHAINS(c[3], b0, b1, y0, y1)
-#undef VNPU_AP_CHAINS
-            }
-#pragma unroll
-            for (uint32_t x = 0; x < 4; ++x) {
-                const uint32_t q = x < 2 ? qa : qb;
-                const uint32_t j = lane + 32u * (x & 1u);
-                const uint32_t qi = q0 + q, ki = k0 + j;
-                float sc;
-                if (j >= kc || (p.causal && ki > qi + causal_offset)) {
-                    sc = ninf;
-                } else {
-                    sc = __fmul_rn(hsum256_chains(c[x]), p.scale);
-                    if (Mh && q < qc) sc = __fadd_rn(sc, Mh[static_cast<uint64_t>(qi) * p.seq_k + ki]);
-                }
-                S[q * kAttBK + j] = sc;
-            }
+                nz |= static_cast<uint64_t>(__shfl_sync(0xffffffffu, nzm, (lane & ~3u) | x)) << (16 * x);
+            const uint32_t n = static_cast<uint32_t>(__popcll(nz));
+            const bool prefix = nz == (n == 64 ? ~0ull : ((1ull << n) - 1ull));
+            info = (act ? 1u : 0u) | (prefix ? 2u : 0u) | (n << 2);
         }
         __syncwarp();
 
-        // ---- online softmax of the warp's two queries
-        bool active[2] = {false, false};
-        float alpha[2] = {1.0f, 1.0f};
+        // ---- values, lane = dims 4*lane..4*lane+3 of the warp's 8 queries
+        {
+            uint32_t nq[8];
+            uint32_t nmin = kAttBK, nmax = 0;
+            bool allpre = true;
 #pragma unroll
-        for (uint32_t h = 0; h < 2; ++h) {
-            const uint32_t q = qa + h;
-            if (q >= qc) break;
-            float *srow = S + q * kAttBK;
-            const float s_lo = lane < kc ? srow[lane] : ninf;
-            const float s_hi = lane + 32 < kc ? srow[lane + 32] : ninf;
-            float bmax = fmaxf(s_lo, s_hi);
-            for (int o = 16; o > 0; o >>= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
-            if (!isfinite(bmax)) continue;   // fully masked block: skipped, as in the reference
-            const float nm = fmaxf(m_run[h], bmax);
-            const float p_lo = lane < kc ? ref_fast_expf(__fsub_rn(s_lo, nm), false) : 0.0f;
-            const float p_hi = lane + 32 < kc ? ref_fast_expf(__fsub_rn(s_hi, nm), false) : 0.0f;
-            alpha[h] = ref_fast_expf(__fsub_rn(m_run[h], nm), false);
-            float sum_p = 0.0f;
-#pragma unroll
-            for (uint32_t j = 0; j < 32; ++j) {
-                const float v = __shfl_sync(0xffffffffu, p_lo, j);
-                if (j < kc) sum_p = __fadd_rn(sum_p, v);
+            for (uint32_t q = 0; q < 8; ++q) {
+                const uint32_t iq = __shfl_sync(0xffffffffu, info, 4 * q);
+                const float aq = __shfl_sync(0xffffffffu, alpha, 4 * q);
+                nq[q] = iq >> 2;
+                nmin = min(nmin, nq[q]);
+                nmax = max(nmax, nq[q]);
+                allpre = allpre && (iq & 2u);
+                if (iq & 1u) {
+                    acc[q].x = __fmul_rn(acc[q].x, aq);
+                    acc[q].y = __fmul_rn(acc[q].y, aq);
+                    acc[q].z = __fmul_rn(acc[q].z, aq);
+                    acc[q].w = __fmul_rn(acc[q].w, aq);
+                }
             }
-#pragma unroll
-            for (uint32_t j = 0; j < 32; ++j) {
-                const float v = __shfl_sync(0xffffffffu, p_hi, j);
-                if (j + 32 < kc) sum_p = __fadd_rn(sum_p, v);
-            }
-            l_run[h] = __fadd_rn(__fmul_rn(l_run[h], alpha[h]), sum_p);
-            m_run[h] = nm;
-            srow[lane] = p_lo;            // probabilities (0 past kc)
-            srow[lane + 32] = p_hi;
-            active[h] = true;
-        }
-        __syncwarp();
-        // ---- values of both queries in one pass over V (each query's keys in order)
-#pragma unroll
-        for (uint32_t h = 0; h < 2; ++h)
-            if (active[h]) {
-                acc[h].x = __fmul_rn(acc[h].x, alpha[h]);
-                acc[h].y = __fmul_rn(acc[h].y, alpha[h]);
-                acc[h].z = __fmul_rn(acc[h].z, alpha[h]);
-                acc[h].w = __fmul_rn(acc[h].w, alpha[h]);
-            }
-        if (active[0] || active[1]) {
-            // an inactive query's row is all zero probabilities: no FMA happens
-            const float *pra = S + qa * kAttBK, *prb = S + qb * kAttBK;
             const float *vcol = Vs + 4 * lane;
-            const bool use_a = active[0], use_b = active[1];
-            for (uint32_t j = 0; j < kc; j += 4) {
-                const float4 pa4 = use_a ? *reinterpret_cast<const float4 *>(pra + j)
-                                         : make_float4(0.f, 0.f, 0.f, 0.f);
-                const float4 pb4 = use_b ? *reinterpret_cast<const float4 *>(prb + j)
-                                         : make_float4(0.f, 0.f, 0.f, 0.f);
-                const float pa[4] = {pa4.x, pa4.y, pa4.z, pa4.w};
-                const float pb[4] = {pb4.x, pb4.y, pb4.z, pb4.w};
+            const float *Pw = S + 8 * warp * kAttBK;
+            if (allpre) {
+                uint32_t j = 0;
+#pragma unroll 1
+                for (; j + 4 <= nmin; j += 4) {
+                    float4 v[4];
 #pragma unroll
-                for (uint32_t u = 0; u < 4; ++u) {
-                    const float4 v = *reinterpret_cast<const float4 *>(vcol + (j + u) * kApD);
-                    acc[0].x = fma_if_nonzero(v.x, pa[u], acc[0].x);
-                    acc[0].y = fma_if_nonzero(v.y, pa[u], acc[0].y);
-                    acc[0].z = fma_if_nonzero(v.z, pa[u], acc[0].z);
-                    acc[0].w = fma_if_nonzero(v.w, pa[u], acc[0].w);
-                    acc[1].x = fma_if_nonzero(v.x, pb[u], acc[1].x);
-                    acc[1].y = fma_if_nonzero(v.y, pb[u], acc[1].y);
-                    acc[1].z = fma_if_nonzero(v.z, pb[u], acc[1].z);
-                    acc[1].w = fma_if_nonzero(v.w, pb[u], acc[1].w);
+                    for (uint32_t u = 0; u < 4; ++u)
+                        v[u] = *reinterpret_cast<const float4 *>(vcol + (j + u) * kApD);
+#pragma unroll
+                    for (uint32_t q = 0; q < 8; ++q) {
+                        const float4 pp = *reinterpret_cast<const float4 *>(Pw + q * kAttBK + j);
+                        fma4(acc[q], v[0], pp.x);
+                        fma4(acc[q], v[1], pp.y);
+                        fma4(acc[q], v[2], pp.z);
+                        fma4(acc[q], v[3], pp.w);
+                    }
+                }
+#pragma unroll 1
+                for (; j < nmax; ++j) {
+                    const float4 v = *reinterpret_cast<const float4 *>(vcol + j * kApD);
+#pragma unroll
+                    for (uint32_t q = 0; q < 8; ++q)
+                        if (j < nq[q]) fma4(acc[q], v, Pw[q * kAttBK + j]);
+                }
+            } else {
+#pragma unroll 1
+                for (uint32_t j = 0; j < kc; ++j) {
+                    const float4 v = *reinterpret_cast<const float4 *>(vcol + j * kApD);
+#pragma unroll
+                    for (uint32_t q = 0; q < 8; ++q) {
+                        const float pq = Pw[q * kAttBK + j];
+                        if (pq != 0.0f) fma4(acc[q], v, pq);
+                    }
                 }
             }
         }
-        __syncwarp();
+        __syncthreads();   // stage b & 1 is refilled by the next iteration
     }
 #pragma unroll
-    for (uint32_t h = 0; h < 2; ++h) {
-        const uint32_t q = qa + h;
-        if (q >= qc) break;
-        const float inv = l_run[h] > 0.0f ? __fdiv_rn(1.0f, l_run[h]) : 0.0f;
-        reinterpret_cast<float4 *>(p.O + head_q + static_cast<uint64_t>(q0 + q) * kApD)[lane] =
-            make_float4(__fmul_rn(acc[h].x, inv), __fmul_rn(acc[h].y, inv), __fmul_rn(acc[h].z, inv),
-                        __fmul_rn(acc[h].w, inv));
+    for (uint32_t q = 0; q < 8; ++q) {
+        const float lq = __shfl_sync(0xffffffffu, l_run, 4 * q);
+        const uint32_t qi = q0 + 8 * warp + q;
+        if (qi >= p.seq_q) continue;
+        const float inv = lq > 0.0f ? __fdiv_rn(1.0f, lq) : 0.0f;
+        reinterpret_cast<float4 *>(p.O + head_q + static_cast<uint64_t>(qi) * kApD)[lane] =
+            make_float4(__fmul_rn(acc[q].x, inv), __fmul_rn(acc[q].y, inv),
+                        __fmul_rn(acc[q].z, inv), __fmul_rn(acc[q].w, inv));
     }
 }
 
@@ -1640,9 +1738,12 @@ cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, cons
     const bool aligned_all = ((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) |
                                reinterpret_cast<uintptr_t>(V) | reinterpret_cast<uintptr_t>(O)) &
                               15u) == 0;
-    if (head_dim == kApD && aligned_all && !(attn_env && !std::strcmp(attn_env, "general"))) {
-        const size_t ap_smem =
-            sizeof(float) * (kAttBQ * kApRow + kAttBK * kApRow + kAttBK * kApD + kAttBQ * kAttBK);
+    if (head_dim == kApD && aligned_all && (seq_q + kApBQ - 1) / kApBQ <= 65535u &&
+        !(attn_env && !std::strcmp(attn_env, "general"))) {
+        // (batch*head, 64-query block): blocks are dispatched x-fastest, so
+        // every head's longest causal block comes before any shorter one
+        const dim3 ap_grid(batch * heads, (seq_q + kApBQ - 1) / kApBQ);
+        const size_t ap_smem = sizeof(float) * kApSmemFloats;
         static bool ap_configured[64] = {};
         if (dev >= 0 && dev < 64 && !ap_configured[dev]) {
             const cudaError_t e = cudaFuncSetAttribute(
@@ -1651,7 +1752,8 @@ cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, cons
             if (e != cudaSuccess) return e;
             ap_configured[dev] = true;
         }
-        VNPU_LAUNCH(launch_pdl(ctx.stream, attention_prefill_kernel, dim3(grid), dim3(kApThreads), ap_smem, ap));
+        VNPU_LAUNCH(launch_pdl(ctx.stream, attention_prefill_kernel, ap_grid, dim3(kApThreads),
+                               ap_smem, ap));
         count_launch(ctx);
         return cudaGetLastError();
     }

@@ -437,6 +437,21 @@ __device__ __forceinline__ void cp_async_16(void *smem_dst, const void *gmem_src
 __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
+// The same copy with zero fill: `valid` false writes 16 zero bytes and reads
+// nothing (gmem_src must still be a mapped address).
+__device__ __forceinline__ void cp_async_16_zfill(void *smem_dst, const void *gmem_src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(smem_dst)),
+                 "l"(gmem_src), "r"(valid ? 16u : 0u)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// Wait until at most N of this thread's committed cp.async groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 __device__ __forceinline__ void st_shared_cluster_f32(uint32_t cluster_addr, float v) {
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");

@@ -373,7 +373,8 @@ def test_attention_golden(gpu, golden, name):
 
 @pytest.mark.parametrize("sq,sk,causal,masked", [
     (512, 512, 1, False), (16, 16, 1, False), (17, 100, 1, True), (33, 33, 0, False),
-    (100, 300, 1, False), (64, 63, 0, True), (2, 2, 1, False), (129, 130, 0, True)])
+    (100, 300, 1, False), (64, 63, 0, True), (2, 2, 1, False), (129, 130, 0, True),
+    (65, 65, 1, False), (200, 456, 1, True), (640, 640, 1, False)])
 def test_prefill_attention_tiled_vs_general(gpu, oracle, monkeypatch, sq, sk, causal, masked):
     """head_dim 128: the register-tiled prefill kernel and the general kernel
     both equal the reference restatement bit for bit (ragged query and key
@@ -396,6 +397,27 @@ def test_prefill_attention_tiled_vs_general(gpu, oracle, monkeypatch, sq, sk, ca
         gpu.attention(Q, K, V, M, O, 1, H, sq, sk, D, causal, 0.0)
         assert bits_equal(O, ref), f"{mode}: max ulp {ulp_diff(O, ref)}"
     monkeypatch.delenv("VNPU_B200_ATTN", raising=False)
+
+
+@pytest.mark.parametrize("sq,sk,causal,masked", [(512, 512, 1, False), (130, 200, 0, True),
+                                                 (77, 77, 1, True)])
+def test_prefill_attention_zero_probabilities(gpu, oracle, sq, sk, causal, masked):
+    """Scores spread over hundreds: probabilities underflow to zero in the
+    middle of key blocks, so the value phase takes its per-key test (the
+    reference skips p == 0) instead of the prefix fast path; bit-exact."""
+    H, D = 4, 128
+    rng = np.random.default_rng(sq + 31 * sk)
+    Q = (rng.normal(0, 1, (1, H, sq, D)) * 25.0).astype(np.float32)
+    K = rng.normal(0, 1, (1, H, sk, D)).astype(np.float32)
+    V = rng.normal(0, 1, (1, H, sk, D)).astype(np.float32)
+    M = None
+    if masked:
+        M = rng.normal(0, 1, (1, H, sq, sk)).astype(np.float32)
+        M[..., 5:9] = -np.inf
+    ref = oracle.attention(Q, K, V, M, 1, H, sq, sk, D, causal, 0.0)
+    O = np.full((1, H, sq, D), np.nan, np.float32)
+    gpu.attention(Q, K, V, M, O, 1, H, sq, sk, D, causal, 0.0)
+    assert bits_equal(O, ref), f"max ulp {ulp_diff(O, ref)}"
 
 
 @pytest.mark.parametrize("sq,sk", [(512, 512), (1, 513), (1, 640), (16, 16), (17, 100)])
