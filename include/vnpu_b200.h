@@ -66,15 +66,16 @@ typedef struct vnpu_b200_rmsnorm_quantize_args_t {
 } vnpu_b200_rmsnorm_quantize_args_t;
 
 typedef struct vnpu_b200_swiglu_quantize_args_t {
-    const float *gate;   /* rows x cols */
-    const float *up;     /* rows x cols */
-    float *Y;            /* rows x cols f32 result, or NULL */
+    const float *gate;   /* rows x cols, row stride ld */
+    const float *up;     /* rows x cols, row stride ld */
+    float *Y;            /* rows x cols f32 result (dense), or NULL */
     int8_t *Q;           /* rows x cols */
     float *scales;       /* rows */
     uint32_t rows;
     uint32_t cols;
     float alpha;
-    uint32_t reserved0;
+    uint32_t ld;         /* elements between rows of gate and up; 0 = cols.  gate and up
+                            may be the two halves of one [rows][2*cols] GEMM output */
 } vnpu_b200_swiglu_quantize_args_t;
 
 /*

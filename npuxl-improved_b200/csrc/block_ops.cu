@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(kFqThreads) rmsnorm_quantize_kernel(
 
 __global__ void __launch_bounds__(kFqThreads) swiglu_quantize_kernel(
     const float *__restrict__ G, const float *__restrict__ U, float *__restrict__ Y,
-    int8_t *__restrict__ Q, float *__restrict__ scales, uint32_t cols, float alpha) {
+    int8_t *__restrict__ Q, float *__restrict__ scales, uint32_t cols, uint32_t ld, float alpha) {
     pdl_enter();
     extern __shared__ __align__(16) float ys[];   // this CTA's slice
     __shared__ __align__(16) float maxes[kFqMaxCluster];
@@ -231,8 +231,8 @@ __global__ void __launch_bounds__(kFqThreads) swiglu_quantize_kernel(
     const uint64_t row = blockIdx.x / cluster_nctarank();
     uint32_t c0, c1;
     fq_slice(cols, c0, c1);
-    const float *g = G + row * cols;
-    const float *u = U + row * cols;
+    const float *g = G + row * ld;
+    const float *u = U + row * ld;
     float *y = Y ? Y + row * cols : nullptr;
     float m = 0.0f;
     for (uint32_t base = c0 + tid; base < c1; base += kFqThreads * kFqPerThread) {
@@ -855,7 +855,7 @@ __global__ void __launch_bounds__(kApThreads, 1) attention_prefill_kernel(const 
             const float *Pw = S + 8 * warp * kAttBK;
             if (allpre) {
                 uint32_t j = 0;
-#pragma unroll 1
+#pragma unroll 2
                 for (; j + 4 <= nmin; j += 4) {
                     float4 v[4];
 #pragma unroll
@@ -1582,12 +1582,14 @@ cudaError_t rmsnorm_quantize(const LaunchCtx &ctx, const float *X, const float *
 }
 
 cudaError_t swiglu_quantize(const LaunchCtx &ctx, const float *gate, const float *up, float *Y,
-                            int8_t *Q, float *scales, uint32_t rows, uint32_t cols, float alpha) {
-    if (cols > kRmsRowMaxCols || rows == 0 || rows > 0x0fffffffu) return cudaErrorInvalidValue;
+                            int8_t *Q, float *scales, uint32_t rows, uint32_t cols, uint32_t ld,
+                            float alpha) {
+    if (cols > kRmsRowMaxCols || rows == 0 || rows > 0x0fffffffu || ld < cols)
+        return cudaErrorInvalidValue;
     const uint32_t csize = fq_cluster(ctx, rows);
     const size_t slice = ((cols + csize - 1) / csize + 15u) & ~15u;
     const cudaError_t e = launch_fq(ctx, swiglu_quantize_kernel, rows, csize, sizeof(float) * slice,
-                                    gate, up, Y, Q, scales, cols, alpha);
+                                    gate, up, Y, Q, scales, cols, ld, alpha);
     count_launch(ctx);
     return e != cudaSuccess ? e : cudaGetLastError();
 }

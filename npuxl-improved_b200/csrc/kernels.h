@@ -153,9 +153,11 @@ cudaError_t rmsnorm(const LaunchCtx &ctx, const float *X, const float *W, float 
 // RMSNORM_F32 then QUANTIZE_I8 per row in one pass (Y may be NULL).
 cudaError_t rmsnorm_quantize(const LaunchCtx &ctx, const float *X, const float *W, float *Y,
                              int8_t *Q, float *scales, uint32_t rows, uint32_t cols, float eps);
-// SWIGLU_F32 then QUANTIZE_I8 per row in one pass (Y may be NULL).
+// SWIGLU_F32 then QUANTIZE_I8 per row in one pass (Y may be NULL); gate and
+// up rows are ld elements apart (ld >= cols), Y, Q dense.
 cudaError_t swiglu_quantize(const LaunchCtx &ctx, const float *gate, const float *up, float *Y,
-                            int8_t *Q, float *scales, uint32_t rows, uint32_t cols, float alpha);
+                            int8_t *Q, float *scales, uint32_t rows, uint32_t cols, uint32_t ld,
+                            float alpha);
 // KV-cache append (VNPU_B200_OP_KV_APPEND); position may be a device pointer.
 cudaError_t kv_append(const LaunchCtx &ctx, const float *K, const float *V, float *K_cache,
                       float *V_cache, float *mask, const int32_t *position, uint32_t heads,

@@ -609,16 +609,19 @@ void exec_swiglu_quantize(vnpu_stream_t *s, const vnpu_command_t &cmd, const Lau
                           Accounting &acc) {
     vnpu_b200_swiglu_quantize_args_t a;
     std::memcpy(&a, cmd.args.raw, sizeof(a));
-    if (!a.gate || !a.up || !a.Q || !a.scales || !a.rows || !a.cols)
+    const uint32_t ld = a.ld ? a.ld : a.cols;
+    if (!a.gate || !a.up || !a.Q || !a.scales || !a.rows || !a.cols || ld < a.cols)
         throw CommandError("invalid swiglu_quantize arguments");
     const uint64_t n = static_cast<uint64_t>(a.rows) * a.cols;
+    const uint64_t span = static_cast<uint64_t>(a.rows - 1) * ld + a.cols;   // gate / up extent
     Staging st(s);
     float *Y = a.Y ? st.out(a.Y, n * sizeof(float), a.Y == a.gate || a.Y == a.up) : nullptr;
-    const float *G = st.in(a.gate, n * sizeof(float));
-    const float *U = st.in(a.up, n * sizeof(float));
+    const float *G = st.in(a.gate, span * sizeof(float));
+    const float *U = st.in(a.up, span * sizeof(float));
     int8_t *Q = st.out(a.Q, n, false);
     float *sc = st.out(a.scales, sizeof(float) * a.rows, false);
-    cuda_check(swiglu_quantize(ctx, G, U, Y, Q, sc, a.rows, a.cols, a.alpha == 0.0f ? 1.0f : a.alpha),
+    cuda_check(swiglu_quantize(ctx, G, U, Y, Q, sc, a.rows, a.cols, ld,
+                               a.alpha == 0.0f ? 1.0f : a.alpha),
                "swiglu_quantize launch");
     st.finish();
     acc.bytes_read = n * 2 * sizeof(float);

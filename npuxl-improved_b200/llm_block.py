@@ -291,7 +291,8 @@ class B200Block:
             return [sw] + cmds, out
         a8, sa = self._act_bufs(name, T)
         pro = vnpu.b200_command(vnpu.OP_B200_SWIGLU_QUANTIZE_I8, vnpu.SwigluQuantizeArgs(
-            g.data_ptr(), u.data_ptr(), None, a8.data_ptr(), sa.data_ptr(), T, inter, 1.0, 0))
+            g.data_ptr(), u.data_ptr(), None, a8.data_ptr(), sa.data_ptr(), T, inter, 1.0,
+            g.stride(0)))
         mm, out = self._mm_cmd(name, T, out_name, residual)
         return [pro, mm], out
 
@@ -372,8 +373,12 @@ class B200Block:
                 a, x1 = self._add_cmd(x, proj, f"x1{T}")
                 cmds2, gu = self._norm_gemm_cmds(x1, self.n2, "gate_up", f"gu{T}")
                 self._submit(cmds + [a] + cmds2)
-            g = gu[:, :cfg.inter].contiguous()
-            u = gu[:, cfg.inter:].contiguous()
+            if self.fused:
+                # SWIGLU_QUANTIZE_I8 reads the two halves of gu in place (ld)
+                g, u = gu[:, :cfg.inter], gu[:, cfg.inter:]
+            else:
+                g = gu[:, :cfg.inter].contiguous()
+                u = gu[:, cfg.inter:].contiguous()
             if self.fused:
                 cmds3, y = self._swiglu_gemm_cmds(g, u, "down", f"y{T}", residual=x1)
                 self._submit(cmds3)

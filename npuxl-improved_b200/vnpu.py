@@ -184,7 +184,7 @@ class RmsnormQuantizeArgs(C.Structure):
 
 class SwigluQuantizeArgs(C.Structure):
     _fields_ = [("gate", vp), ("up", vp), ("Y", vp), ("Q", vp), ("scales", vp), ("rows", u32),
-                ("cols", u32), ("alpha", C.c_float), ("reserved0", u32)]
+                ("cols", u32), ("alpha", C.c_float), ("ld", u32)]
 
 
 OP_B200_KV_APPEND = 0x102
@@ -506,8 +506,8 @@ class Device:
         self.lib.check(self.submit([b200_command(OP_B200_RMSNORM_QUANTIZE_I8, a)]), "submit")
         self.lib.check(self.sync(), "rmsnorm_quantize")
 
-    def swiglu_quantize(self, G, U, Y, Q, scales, rows, cols, alpha=0.0) -> None:
-        a = SwigluQuantizeArgs(ptr(G), ptr(U), ptr(Y), ptr(Q), ptr(scales), rows, cols, alpha, 0)
+    def swiglu_quantize(self, G, U, Y, Q, scales, rows, cols, alpha=0.0, ld=0) -> None:
+        a = SwigluQuantizeArgs(ptr(G), ptr(U), ptr(Y), ptr(Q), ptr(scales), rows, cols, alpha, ld)
         self.lib.check(self.submit([b200_command(OP_B200_SWIGLU_QUANTIZE_I8, a)]), "submit")
         self.lib.check(self.sync(), "swiglu_quantize")
 

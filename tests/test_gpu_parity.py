@@ -324,6 +324,15 @@ def test_swiglu_quantize_fused_equals_two_commands(gpu, oracle, rows, cols, want
     Yo = oracle.swiglu(G, U, alpha, 0)
     Qo, so = oracle.quantize(Yo.reshape(rows, cols), 0)
     assert np.array_equal(Q, Qo) and bits_equal(s, so)
+    # gate and up as the two halves of one [rows][2*cols] GEMM output (ld)
+    GU = np.concatenate([G, U], axis=1)
+    Yl = np.full((rows, cols), np.nan, np.float32) if want_y else None
+    Ql = np.zeros((rows, cols), np.int8)
+    sl = np.zeros(rows, np.float32)
+    gpu.swiglu_quantize(GU[:, :cols], GU[:, cols:], Yl, Ql, sl, rows, cols, alpha, ld=2 * cols)
+    assert np.array_equal(Ql, Q) and bits_equal(sl, s)
+    if want_y:
+        assert bits_equal(Yl, Y)
 
 
 def test_rope_golden(gpu, golden):
