@@ -1397,40 +1397,48 @@ __global__ void __cluster_dims__(kDcCluster, 1, 1) __launch_bounds__(kDcThreads)
 }
 
 // QKV split + RoPE + KV append for T tokens (VNPU_B200_OP_QKV_ROPE_APPEND,
-// T > 1): one thread per (token, part, head, rotation pair) reads the two
-// columns of the MATMUL_I8 output C [T][3*heads*D], rotates Q and K exactly as
-// rope_kernel does and writes the head-major outputs and the cache slot.
-__global__ void qkv_split_rope_append_kernel(const float *__restrict__ C, uint32_t T,
-                                             float *__restrict__ Q, float *__restrict__ Kout,
-                                             float *__restrict__ Vout, float *__restrict__ Kc,
-                                             float *__restrict__ Vc, float *__restrict__ mask,
-                                             const int32_t *__restrict__ position,
-                                             uint32_t heads, uint32_t D, uint32_t cap,
-                                             uint32_t pos0, float scaling, const RopeFreq freq,
-                                             uint32_t *err) {
+// T > 1): thread (head, pair j) of block (head group, part, token run) reads
+// columns j and j + D/2 of the MATMUL_I8 output C [T][3*heads*D] for
+// kQsTokens tokens, rotates Q and K exactly as rope_kernel does and writes
+// the head-major outputs and the cache slot.  The inverse frequencies are
+// copied to shared memory once per block (lanes index them by pair).
+constexpr uint32_t kQsThreads = 256;
+constexpr uint32_t kQsTokens = 8;
+
+__global__ void __launch_bounds__(kQsThreads) qkv_split_rope_append_kernel(
+    const float *__restrict__ C, uint32_t T, float *__restrict__ Q, float *__restrict__ Kout,
+    float *__restrict__ Vout, float *__restrict__ Kc, float *__restrict__ Vc,
+    float *__restrict__ mask, const int32_t *__restrict__ position, uint32_t heads, uint32_t D,
+    uint32_t cap, uint32_t pos0, float scaling, const RopeFreq freq, uint32_t *err) {
     pdl_enter();
+    __shared__ float inv_s[kRopeMaxPairs];
     const uint32_t half = D / 2;
-    const uint64_t per_token = 3ull * heads * half;
-    const uint64_t total = per_token * T;
+    const uint32_t sec = blockIdx.y;
+    if (sec < 2)
+        for (uint32_t i = threadIdx.x; i < half; i += kQsThreads) inv_s[i] = freq.inv[i];
+    __syncthreads();
+    const uint32_t per_block = kQsThreads / half;          // heads per block (half <= 256)
+    const uint32_t hl = threadIdx.x / half;
+    const uint32_t j = threadIdx.x - hl * half;
+    const uint32_t h = blockIdx.x * per_block + hl;
+    if (hl >= per_block || h >= heads) return;
     const int32_t base = position ? *position : static_cast<int32_t>(pos0);
-    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-        const uint32_t t = static_cast<uint32_t>(i / per_token);
-        const uint32_t r = static_cast<uint32_t>(i - static_cast<uint64_t>(t) * per_token);
-        const uint32_t sec = r / (heads * half);
-        const uint32_t hj = r - sec * heads * half;
-        const uint32_t h = hj / half, j = hj - h * half;
-        const float *row = C + static_cast<uint64_t>(t) * 3 * heads * D + sec * heads * D + h * D;
+    const float inv = sec < 2 ? inv_s[j] : 0.0f;
+    float *out = sec == 0 ? Q : (sec == 1 ? Kout : Vout);
+    float *cache = sec == 1 ? Kc : Vc;
+    const uint64_t ldc = 3ull * heads * D;
+    const uint32_t t1 = min(T, (blockIdx.z + 1) * kQsTokens);
+    for (uint32_t t = blockIdx.z * kQsTokens; t < t1; ++t) {
+        const float *row = C + t * ldc + (static_cast<uint64_t>(sec) * heads + h) * D;
         float x0 = row[j], x1 = row[j + half];
         const int32_t pos = base + static_cast<int32_t>(t);
         if (sec < 2) {
             float v[2] = {x0, x1};
-            rotate_pair(v, 0, 1, __fmul_rn(__fmul_rn(static_cast<float>(pos), scaling), freq.inv[j]));
+            rotate_pair(v, 0, 1, __fmul_rn(__fmul_rn(static_cast<float>(pos), scaling), inv));
             x0 = v[0];
             x1 = v[1];
         }
         const uint64_t o = (static_cast<uint64_t>(h) * T + t) * D + j;
-        float *out = sec == 0 ? Q : (sec == 1 ? Kout : Vout);
         if (out) {
             out[o] = x0;
             out[o + half] = x1;
@@ -1441,7 +1449,6 @@ __global__ void qkv_split_rope_append_kernel(const float *__restrict__ C, uint32
             continue;
         }
         const uint64_t c = (static_cast<uint64_t>(h) * cap + static_cast<uint32_t>(pos)) * D + j;
-        float *cache = sec == 1 ? Kc : Vc;
         cache[c] = x0;
         cache[c + half] = x1;
         if (sec == 1 && j == 0 && mask)
@@ -1616,11 +1623,14 @@ cudaError_t qkv_split_rope_append(const LaunchCtx &ctx, const float *C, uint32_t
         return cudaErrorInvalidValue;
     RopeFreq f;
     for (uint32_t j = 0; j < q.head_dim / 2; ++j) f.inv[j] = q.inv_freq[j];
-    const uint64_t total = 3ull * q.heads * (q.head_dim / 2) * T;
-    VNPU_LAUNCH(launch_pdl(ctx.stream, qkv_split_rope_append_kernel,
-                           dim3(grid_for(total, ctx.num_sms, 256)), dim3(256), 0, C, T, q.Q,
-                           q.K_out, q.V_out, q.K_cache, q.V_cache, q.mask, q.position, q.heads,
-                           q.head_dim, q.capacity, q.position_offset, q.scaling, f, ctx.err));
+    const uint32_t per_block = kQsThreads / (q.head_dim / 2);
+    const uint32_t runs = (T + kQsTokens - 1) / kQsTokens;
+    if (runs > 65535u) return cudaErrorInvalidValue;
+    const dim3 grid((q.heads + per_block - 1) / per_block, 3, runs);
+    VNPU_LAUNCH(launch_pdl(ctx.stream, qkv_split_rope_append_kernel, grid, dim3(kQsThreads), 0,
+                           C, T, q.Q, q.K_out, q.V_out, q.K_cache, q.V_cache, q.mask, q.position,
+                           q.heads, q.head_dim, q.capacity, q.position_offset, q.scaling, f,
+                           ctx.err));
     count_launch(ctx);
     return cudaGetLastError();
 }

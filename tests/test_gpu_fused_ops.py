@@ -39,10 +39,11 @@ def _submit(gpu, cmds):
     return gpu.sync()
 
 
-def _matmul_cmd(A, w, sa, bias, Cp, M, K, N):
+def _matmul_cmd(A, w, sa, bias, Cp, M, K, N, epilogue=0):
     c = vnpu.Command()
     c.opcode = vnpu.OP_MATMUL_I8
-    c.args.matmul_i8 = vnpu.MatmulI8Args(A, w, sa, bias, Cp, M, K, N, 0, 0, 0, vnpu.UNIT_GPU)
+    c.args.matmul_i8 = vnpu.MatmulI8Args(A, w, sa, bias, Cp, M, K, N, 0, 0, epilogue,
+                                         vnpu.UNIT_GPU)
     return c
 
 
@@ -164,10 +165,14 @@ def test_qkv_rope_append_position_past_capacity(b200_lib, oracle, torch):
         d.unpack(w)
 
 
-@pytest.mark.parametrize("M,K,N,inplace", [(1, 4096, 4096, False), (1, 1000, 333, True),
-                                           (4, 512, 1024, False), (300, 256, 512, True),
-                                           (300, 256, 512, False)])
-def test_residual_equals_matmul_then_add(gpu, oracle, torch, M, K, N, inplace):
+@pytest.mark.parametrize("M,K,N,inplace,epi", [
+    (1, 4096, 4096, False, 0), (1, 1000, 333, True, 0), (4, 512, 1024, False, 0),
+    (300, 256, 512, True, 0), (300, 256, 512, False, 0), (512, 4096, 4096, False, 0),
+    (777, 1000, 1000, False, 1), (260, 4096, 11008, False, 0), (300, 256, 512, False, 2)])
+def test_residual_equals_matmul_then_add(gpu, oracle, torch, M, K, N, inplace, epi):
+    """MATMUL_I8_RESIDUAL equals MATMUL_I8 then ADD_F32 bit for bit: the GEMV
+    epilogue (M = 1) and the two-pass form (M > 1, R aliasing C or not, ragged
+    N, epilogues)."""
     rng = np.random.default_rng(M + K + N)
     w = _weights(gpu, oracle, rng, K, N)
     A8h, sah = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
@@ -178,7 +183,7 @@ def test_residual_equals_matmul_then_add(gpu, oracle, torch, M, K, N, inplace):
         P = torch.empty((M, N), device="cuda")
         torch.cuda.synchronize()
         assert _submit(gpu, [_matmul_cmd(A8.data_ptr(), w, sa.data_ptr(), bias.data_ptr(),
-                                         P.data_ptr(), M, K, N)]) == vnpu.OK
+                                         P.data_ptr(), M, K, N, epi)]) == vnpu.OK
         ref = torch.empty((M, N), device="cuda")
         torch.cuda.synchronize()
         gpu.add(R.data_ptr(), P.data_ptr(), ref.data_ptr(), M * N, 1.0, 1.0)
@@ -186,7 +191,7 @@ def test_residual_equals_matmul_then_add(gpu, oracle, torch, M, K, N, inplace):
         Rp = out if inplace else R
         torch.cuda.synchronize()
         args = vnpu.MatmulI8ResidualArgs(A8.data_ptr(), w, sa.data_ptr(), bias.data_ptr(),
-                                         Rp.data_ptr(), out.data_ptr(), M, K, N, 0, 0, 0, 0, 0)
+                                         Rp.data_ptr(), out.data_ptr(), M, K, N, 0, 0, 0, epi, 0)
         assert _submit(gpu, [vnpu.b200_command(vnpu.OP_B200_MATMUL_I8_RESIDUAL, args)]) == vnpu.OK
         assert bits_equal(out.cpu().numpy(), ref.cpu().numpy())
     finally:
