@@ -83,9 +83,18 @@ __device__ __forceinline__ float stage_row_rms_inv(const float *__restrict__ x, 
     if (tid < 32) {
         float part = 0.0f;
         if (tid < 8) {
-            uint32_t j = tid;
-#pragma unroll 8
-            for (; j < full; j += 8) part = __fmaf_rn(xs[j], xs[j], part);
+            // 16 loads ahead of the dependent FMAs, so the chain runs at FMA
+            // latency rather than shared-memory latency.
+            const uint32_t steps = full / 8;
+            uint32_t k = 0;
+            for (; k + 16 <= steps; k += 16) {
+                float v[16];
+#pragma unroll
+                for (uint32_t u = 0; u < 16; ++u) v[u] = xs[tid + 8 * (k + u)];
+#pragma unroll
+                for (uint32_t u = 0; u < 16; ++u) part = __fmaf_rn(v[u], v[u], part);
+            }
+            for (; k < steps; ++k) part = __fmaf_rn(xs[tid + 8 * k], xs[tid + 8 * k], part);
         }
         const float hi = __shfl_down_sync(0xffffffffu, part, 4);
         const float s = __fadd_rn(part, hi);
