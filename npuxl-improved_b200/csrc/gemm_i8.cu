@@ -62,25 +62,32 @@ constexpr uint32_t kEpiWarps = 4;
 constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024;  // + alignment slack
 
 struct TcParams {
-    const float *scale_a;
-    const float *scale_b;
-    const float *bias;
-    float *C;
-    uint32_t ldc;
-    uint32_t M, N, K;
-    uint32_t tiles_m, tiles_n, num_kb;
-    uint32_t group_m;      // raster band height in m-tiles
-    uint32_t epilogue, form;
-    uint32_t variant;      // epi_variant(epilogue, bias != NULL, form)
-    uint32_t tma_store;    // 1: C written by TMA from shared memory
-    uint32_t *err;
-    uint64_t limit_ns;
+    const float *scale_a = nullptr;
+    const float *scale_b = nullptr;
+    const float *bias = nullptr;
+    float *C = nullptr;
+    uint32_t ldc = 0;
+    uint32_t M = 0, N = 0, K = 0;
+    uint32_t tiles_m = 0, tiles_n = 0, num_kb = 0;
+    uint32_t group_m = 1;  // raster band height in m-tiles
+    uint32_t epilogue = 0, form = 0;
+    uint32_t variant = 0;  // epi_variant(epilogue, bias != NULL, form)
+    uint32_t tma_store = 0;  // 1: C written by TMA from shared memory
+    uint32_t *err = nullptr;
+    uint64_t limit_ns = 2000000000ull;
     // Scatter epilogue (ndst > 0): the tile goes to dst[0..ndst-1], each a
     // [M][ldd] matrix, at column col_off + n, by plain stores.
     float *dst[8] = {};
     uint32_t ndst = 0;
     uint32_t ldd = 0;
     uint32_t col_off = 0;
+    // Split K (pair kernel): work unit u is tile u / splits, k-blocks
+    // [s * kb_per_split, ...) of split s = u % splits; with splits > 1 the
+    // epilogue stores the raw int32 sums to rows s * m_pad + m of the
+    // workspace (C, ldc = N) and splitk_finish_kernel adds and dequantises.
+    uint32_t splits = 1;
+    uint32_t kb_per_split = 0;
+    uint32_t m_pad = 0;
 };
 
 __device__ __forceinline__ void tile_coords(uint32_t t, uint32_t tiles_m, uint32_t tiles_n,
@@ -420,7 +427,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
     const uint32_t rank = cluster_ctarank();
     const uint32_t pair = blockIdx.x >> 1;
     const uint32_t npairs = gridDim.x >> 1;
-    const uint32_t total_tiles = p.tiles_m * p.tiles_n;   // 256x256 tiles
+    const uint32_t total_tiles = p.tiles_m * p.tiles_n * p.splits;   // work units
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < kNStages; ++s) {
@@ -457,8 +464,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
             bool ok = true;
             for (uint32_t t = pair; t < total_tiles && ok; t += npairs) {
                 uint32_t mb, nb;
-                tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, mb, nb);
-                for (uint32_t kb = 0; kb < p.num_kb; ++kb, ++it) {
+                const uint32_t tile = t / p.splits, split = t - tile * p.splits;
+                tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, mb, nb);
+                const uint32_t kbps = p.splits > 1 ? p.kb_per_split : p.num_kb;
+                const uint32_t kb0 = split * kbps;
+                const uint32_t kb1 = min(p.num_kb, kb0 + kbps);
+                for (uint32_t kb = kb0; kb < kb1; ++kb, ++it) {
                     const uint32_t s = it % kNStages;
                     const uint32_t ph = (it / kNStages) & 1u;
                     if (!mbar_wait(&empty_bar[s], ph ^ 1u, p.limit_ns, p.err, &abort_flag)) {
@@ -499,7 +510,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
                     break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * kPTileN;
-                for (uint32_t kb = 0; kb < p.num_kb; ++kb, ++it) {
+                const uint32_t split = t % p.splits;
+                const uint32_t kbps = p.splits > 1 ? p.kb_per_split : p.num_kb;
+                const uint32_t kb0 = split * kbps;
+                const uint32_t kb1 = min(p.num_kb, kb0 + kbps);
+                for (uint32_t kb = kb0; kb < kb1; ++kb, ++it) {
                     const uint32_t s = it % kNStages;
                     const uint32_t ph = (it / kNStages) & 1u;
                     if (!mbar_wait(&full_bar[s], ph, p.limit_ns, p.err, &abort_flag)) {
@@ -513,7 +528,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
 #pragma unroll
                     for (uint32_t kk = 0; kk < kBK / kUmmaK; ++kk)
                         umma_i8_pair(d_tmem, adesc + 2u * kk, bdesc + 2u * kk, idesc,
-                                     (kb | kk) != 0u);
+                                     kb != kb0 || kk != 0u);
                     umma_commit_pair_mc(&empty_bar[s], 0x3);
                 }
                 if (!ok) break;
@@ -542,7 +557,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
         uint32_t tcount = 0;
         for (uint32_t t = pair; t < total_tiles; t += npairs, ++tcount) {
             uint32_t mb, nb;
-            tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, mb, nb);
+            const uint32_t tile = t / p.splits, split = t - tile * p.splits;
+            tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, mb, nb);
+            // split K: raw int32 sums into this split's slice of the workspace
+            const uint32_t row_off = p.splits > 1 ? split * p.m_pad : 0u;
             const uint32_t acc = tcount & 1u;
             const uint32_t use = tcount >> 1;
             // Scales and biases for the tile, fetched before the accumulators are ready.
@@ -560,7 +578,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
-            float *crow = p.C + static_cast<uint64_t>(row_ok ? m : 0) * p.ldc;
+            float *crow = p.C + static_cast<uint64_t>(row_off + (row_ok ? m : 0)) * p.ldc;
 #pragma unroll
             // All of the warp's accumulator columns in one round of tensor-memory
             // loads (one wait instead of one per chunk); the accumulator is
@@ -581,7 +599,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
                 const uint32_t col = col_base + c * 32u;
                 const uint32_t n0 = nb * kPTileN + col;
                 if (n0 >= p.N || m_first >= p.M) continue;  // warp-uniform
-                dequant32_shfl_inplace_any(p.variant, rr[c], sa, sreg[c], breg[c]);
+                if (p.splits == 1) dequant32_shfl_inplace_any(p.variant, rr[c], sa, sreg[c], breg[c]);
                 const float(&v)[32] = reinterpret_cast<const float(&)[32]>(rr[c]);
                 if (p.ndst) {
                     // Scatter: the 32x32 chunk is transposed through the staging
@@ -632,7 +650,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
                     __syncwarp();
                     if (lane == 0) {
                         tma_store_2d(&tmap_c, stage_out, static_cast<int32_t>(n0),
-                                     static_cast<int32_t>(m_first));
+                                     static_cast<int32_t>(row_off + m_first));
                         bulk_commit();
                     }
                 } else if (row_ok) {
@@ -652,6 +670,56 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc_pair(tmem_base, kTmemCols);
+    }
+}
+
+// Split-K finish: C[m][n] = dequant(sum over splits of ws[s][m][n]) - the
+// int32 sums are exact, so the result is the single-pass GEMM's bit for bit.
+// ws rows are s * m_pad + m, N columns; four columns per thread (N % 4 == 0).
+__global__ void __launch_bounds__(256) splitk_finish_kernel(
+    const int4 *__restrict__ ws, uint32_t splits, uint32_t m_pad, uint32_t M, uint32_t N,
+    const float *__restrict__ scale_a, const float *__restrict__ scale_b,
+    const float *__restrict__ bias, float *__restrict__ C, uint32_t ldc, uint32_t epilogue,
+    uint32_t form) {
+    pdl_enter();
+    const uint32_t n4 = N / 4;
+    const uint32_t total = M * n4;
+    const uint32_t slice4 = m_pad * n4;
+    const bool has_bias = bias != nullptr;
+    const bool vec = (ldc % 4u == 0u) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0u);
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const uint32_t m = i / n4;
+        const uint32_t n = (i - m * n4) * 4u;
+        int4 a = __ldcs(ws + i);   // m * n4 + n / 4 == i
+        for (uint32_t sp = 1; sp < splits; ++sp) {
+            const int4 b = __ldcs(ws + sp * slice4 + i);
+            a.x += b.x;
+            a.y += b.y;
+            a.z += b.z;
+            a.w += b.w;
+        }
+        const float sa = scale_a ? __ldg(scale_a + m) : 1.0f;
+        const float4 sb = __ldg(reinterpret_cast<const float4 *>(scale_b) + n / 4u);
+        float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (has_bias) {
+            bv.x = __ldg(bias + n);
+            bv.y = __ldg(bias + n + 1);
+            bv.z = __ldg(bias + n + 2);
+            bv.w = __ldg(bias + n + 3);
+        }
+        const float4 o = make_float4(ref_dequant(a.x, sa, sb.x, has_bias, bv.x, epilogue, form),
+                                     ref_dequant(a.y, sa, sb.y, has_bias, bv.y, epilogue, form),
+                                     ref_dequant(a.z, sa, sb.z, has_bias, bv.z, epilogue, form),
+                                     ref_dequant(a.w, sa, sb.w, has_bias, bv.w, epilogue, form));
+        float *c = C + static_cast<uint64_t>(m) * ldc + n;
+        if (vec) {
+            *reinterpret_cast<float4 *>(c) = o;
+        } else {
+            c[0] = o.x;
+            c[1] = o.y;
+            c[2] = o.z;
+            c[3] = o.w;
+        }
     }
 }
 
@@ -1657,6 +1725,44 @@ cudaError_t matmul_i8_scatter(const LaunchCtx &ctx, const MatmulI8 &p) {
     return cudaGetLastError();
 }
 
+// The CTA-pair GEMM split over K (tp filled for 256x256 tiles, tp.kb_per_split
+// set): raw int32 sums of each split into a workspace, then
+// splitk_finish_kernel.
+cudaError_t matmul_i8_pair_splitk(const LaunchCtx &ctx, const MatmulI8 &p, TcParams tp,
+                                  const CUtensorMap &tmap_a, uint32_t splits, uint32_t max_pairs) {
+    tp.splits = splits;
+    tp.m_pad = tp.tiles_m * kPTileM;
+    const uint64_t rows = static_cast<uint64_t>(splits) * tp.m_pad;
+    int32_t *ws = nullptr;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void **>(&ws),
+                                    rows * p.N * sizeof(int32_t), ctx.stream);
+    if (e != cudaSuccess) return e;
+    CUtensorMap tmap_w;
+    tp.C = reinterpret_cast<float *>(ws);
+    tp.ldc = p.N;
+    tp.tma_store = encode_tmap_2d(&tmap_w, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws, p.N, rows,
+                                  static_cast<uint64_t>(p.N) * 4u, 32, 32,
+                                  CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!tp.tma_store) std::memset(&tmap_w, 0, sizeof(tmap_w));
+    const uint32_t units = tp.tiles_m * tp.tiles_n * splits;
+    const uint32_t pairs = units < max_pairs ? units : max_pairs;
+    e = launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, 6>, dim3(2 * pairs),
+                   dim3(pair_threads(8)), pair_smem_bytes(8, 6), tmap_a, *p.tmap_b128, tmap_w, tp);
+    count_launch(ctx);
+    if (e == cudaSuccess) {
+        const uint32_t total = p.M * (p.N / 4u);
+        const uint32_t blocks = std::min<uint32_t>((total + 255u) / 256u,
+                                                   static_cast<uint32_t>(ctx.num_sms) * 8u);
+        e = launch_pdl(ctx.stream, splitk_finish_kernel, dim3(blocks), dim3(256), 0,
+                       reinterpret_cast<const int4 *>(ws), splits, tp.m_pad, p.M, p.N, p.scale_a,
+                       p.scale_b, p.bias, p.C, p.ldc, p.epilogue, p.form);
+        count_launch(ctx);
+    }
+    cudaFreeAsync(ws, ctx.stream);
+    g_last_kernel.store("gemm_i8_tcgen05_pair_kernel+splitk", std::memory_order_relaxed);
+    return e != cudaSuccess ? e : cudaGetLastError();
+}
+
 cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
     int max_pairs = 0, max_wide_pairs = 0;
     cudaError_t se = device_setup(max_pairs, max_wide_pairs);
@@ -1699,12 +1805,28 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         tp.tiles_m = tiles_m;
         tp.tiles_n = (p.N + (wide ? kWTileN : kPTileN) - 1) / (wide ? kWTileN : kPTileN);
         tp.num_kb = (p.K + kBK - 1) / kBK;
+        // Split K when the 256x256 tiles leave at least half of the pairs idle
+        // and K is long: each split (at least 8 k-blocks) sums its range into
+        // a stream-ordered int32 workspace, a second kernel adds the splits
+        // (exact) and applies the epilogue.
         tp.group_m = raster_group(tp.tiles_m, kPTileM, p.K);
         tp.epilogue = p.epilogue;
         tp.form = p.form;
         tp.variant = epi_variant(p.epilogue, p.bias != nullptr, p.form);
         tp.err = ctx.err;
         tp.limit_ns = ctx.wait_limit_ns;
+        uint32_t splits = 1;
+        if (!wide && p.N % 4u == 0u && std::getenv("VNPU_B200_NO_SPLITK") == nullptr) {
+            uint32_t sk = pp / tiles_p;
+            sk = std::min(sk, 4u);
+            sk = std::min(sk, tp.num_kb / 8u);
+            if (sk >= 2) {
+                tp.kb_per_split = (tp.num_kb + sk - 1) / sk;
+                splits = (tp.num_kb + tp.kb_per_split - 1) / tp.kb_per_split;
+            }
+        }
+        if (splits > 1)   // every other field of tp is set above
+            return matmul_i8_pair_splitk(ctx, p, tp, tmap_a, splits, static_cast<uint32_t>(max_pairs));
         CUtensorMap tmap_c;
         tp.tma_store = (reinterpret_cast<uintptr_t>(p.C) % 16u == 0u) && (p.ldc % 4u == 0u) &&
                        encode_tmap_2d(&tmap_c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.C, p.N, p.M,
@@ -1718,7 +1840,9 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
             VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_wide_kernel, dim3(2 * pairs),
                                    dim3(kPThreads), kWSmemBytes, tmap_a, *p.tmap_b128, tmap_c,
                                    tp));
-        else if (p.epilogue >= 2)   // SiLU, GELU: latency-bound epilogue, 16 warps
+        // 16 epilogue warps: SiLU / GELU (latency-bound epilogue), or one short
+        // tile per pair (the epilogue is most of the time): 512^3 9.3 -> 8.8 us
+        else if (p.epilogue >= 2 || (tiles <= cap && tp.num_kb <= 8u))
             VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<16, 5>, dim3(2 * pairs),
                                    dim3(pair_threads(16)), pair_smem_bytes(16, 5), tmap_a,
                                    *p.tmap_b128, tmap_c, tp));

@@ -451,6 +451,7 @@ def test_pair_and_single_cta_kernels_agree(gpu, oracle, monkeypatch, M, K, N):
     A, sa = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
     B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
     bias = rng.normal(0, 0.01, N).astype(np.float32)
+    monkeypatch.setenv("VNPU_B200_NO_SPLITK", "1")
     outs = []
     for no_pair in (False, True):
         if no_pair:
@@ -465,6 +466,42 @@ def test_pair_and_single_cta_kernels_agree(gpu, oracle, monkeypatch, M, K, N):
     assert bits_equal(outs[0], outs[1])
     rows = np.arange(0, M, 13)
     assert bits_equal(outs[0][rows], oracle.matmul_i8(A[rows], B, sa[rows], sb, bias, 3, 0))
+
+
+@pytest.mark.parametrize("M,K,N,epi,form,pad,bias_on", [
+    (512, 4096, 4096, 0, 0, 0, False),   # the decoder block's O projection: 2 splits
+    (512, 11008, 4096, 0, 0, 0, True),   # its down projection: 2 splits of 43 k-blocks
+    (300, 2048, 1000, 2, 0, 0, True),    # ragged M and N, SiLU
+    (129, 4096, 512, 1, 1, 0, True),     # two tiles: 4 splits, stream form
+    (256, 3008, 256, 4, 2, 0, True),     # ragged K: 3 splits of 8 k-blocks, scalar form
+    (300, 2048, 1000, 0, 0, 3, True),    # ldc % 4 != 0: scalar stores in the finish kernel
+])
+def test_splitk_pair_kernel_agrees(gpu, oracle, monkeypatch, M, K, N, epi, form, pad, bias_on):
+    """The CTA-pair GEMM split over K (raw int32 sums of each split in a
+    workspace, added exactly and dequantised by a second kernel) gives the
+    same bits as the single pass and the oracle."""
+    rng = np.random.default_rng(M * 5 + K + N)
+    A, sa = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
+    B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
+    bias = rng.normal(0, 0.01, N).astype(np.float32) if bias_on else None
+    ldc = N + pad if pad else 0
+    outs = []
+    for split in (True, False):
+        if split:
+            monkeypatch.delenv("VNPU_B200_NO_SPLITK", raising=False)
+        else:
+            monkeypatch.setenv("VNPU_B200_NO_SPLITK", "1")
+        Cbuf = np.full((M, ldc), np.nan, np.float32) if pad else None
+        C = run_matmul(gpu, A, B, sa, sb, bias, epi, form, ldc=ldc, Cbuf=Cbuf)
+        assert gpu.lib.b200_last_matmul_kernel().decode() == (
+            "gemm_i8_tcgen05_pair_kernel+splitk" if split else "gemm_i8_tcgen05_pair_kernel")
+        outs.append(C[:, :N].copy())
+        if pad:
+            assert np.isnan(C[:, N:]).all()
+    monkeypatch.delenv("VNPU_B200_NO_SPLITK", raising=False)
+    assert bits_equal(outs[0], outs[1])
+    rows = np.unique(np.r_[np.arange(0, M, 37), M - 1])
+    assert bits_equal(outs[0][rows], oracle.matmul_i8(A[rows], B, sa[rows], sb, bias, epi, form))
 
 
 @pytest.mark.parametrize("M,K,N,epi,form,pad", [
@@ -485,6 +522,7 @@ def test_wide_pair_kernel_agrees(gpu, oracle, monkeypatch, M, K, N, epi, form, p
     B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
     bias = rng.normal(0, 0.01, N).astype(np.float32)
     ldc = N + pad if pad else 0
+    monkeypatch.setenv("VNPU_B200_NO_SPLITK", "1")
     outs = []
     for wide in ("1", "0"):
         monkeypatch.setenv("VNPU_B200_PAIR_WIDE", wide)
