@@ -613,10 +613,11 @@ __device__ __forceinline__ float fma_if_nonzero(float v, float p, float a) {
 // keys double-buffered in shared memory by cp.async.  Warp w owns queries
 // 8w..8w+7 through all three phases, so only the block loads need the whole
 // CTA in step:
-//   scores : lane (qs, kl) = (lane/8, lane%8) computes queries 2qs, 2qs+1 x
-//            keys kl + 8u (u < 4) of a 32-key half: the eight AVX2 chains of
-//            each (query, key) pair in registers (Q and K rows from padded
-//            shared memory), combined in hsum256 order, *scale (+mask);
+//   scores : lane (c, kg) = (lane%8, lane/8) runs AVX2 chain c of the warp's
+//            8 queries x keys 8kg..8kg+7 of a 32-key half (Q and K rows
+//            chain-major in shared memory: 16 loaded floats per 64 FMAs), then
+//            three shuffle steps add the chains in hsum256 order; *scale
+//            (+mask);
 //   softmax: lane (q, quarter) = (lane/4, lane%4) holds keys 16*quarter..+15
 //            of query q: causal and ragged keys -inf, block max, skip if not
 //            finite, fast_expf, the in-order sum handed from quarter to
@@ -629,24 +630,37 @@ __device__ __forceinline__ float fma_if_nonzero(float v, float p, float a) {
 constexpr uint32_t kApThreads = 256;
 constexpr uint32_t kApBQ = 64;
 constexpr uint32_t kApD = 128;
-constexpr uint32_t kApRow = kApD + 4;     // padded Q/K row: 8 rows in distinct bank groups
-constexpr size_t kApSmemFloats = static_cast<size_t>(kApBQ) * kApRow + 2u * kAttBK * kApRow +
+// Q and K rows are kept chain-major: element d of a row at (d % 8) * kApCS + d / 8,
+// so a lane reads four steps of its chain with one 16-byte load; the chain
+// stride of 20 floats puts the eight chains in distinct bank groups.
+constexpr uint32_t kApCS = 20;
+constexpr uint32_t kApTRow = 8 * kApCS;   // floats per chain-major row
+constexpr size_t kApSmemFloats = static_cast<size_t>(kApBQ) * kApTRow + 2u * kAttBK * kApTRow +
                                  2u * kAttBK * kApD + static_cast<size_t>(kApBQ) * kAttBK;
 
-__device__ __forceinline__ float hsum256_chains(const float (&c)[8]) {
-    return __fadd_rn(__fadd_rn(__fadd_rn(c[0], c[4]), __fadd_rn(c[1], c[5])),
-                     __fadd_rn(__fadd_rn(c[2], c[6]), __fadd_rn(c[3], c[7])));
+// 64 rows of 128 floats (rows >= valid zero) into chain-major rows, by
+// 4-byte copies (a warp reads 128 contiguous bytes and writes 32 distinct banks).
+__device__ __forceinline__ void ap_load_rows_t(float *T, const float *src, uint32_t valid,
+                                               uint32_t tid) {
+#pragma unroll 4
+    for (uint32_t e = tid; e < 64u * kApD; e += kApThreads) {
+        const uint32_t row = e >> 7, d = e & 127u;
+        const bool ok = row < valid;
+        cp_async_4_zfill(T + row * kApTRow + (d & 7u) * kApCS + (d >> 3),
+                         src + static_cast<uint64_t>(ok ? row : 0u) * kApD + d, ok);
+    }
 }
 
-// Block k0 of K and V (64 rows; rows past seq_k zero) into one stage.
+// Block k0 of K (chain-major) and V (64 rows; rows past seq_k zero) into one stage.
 __device__ __forceinline__ void ap_load_kv(float *Ks, float *Vs, const float *Kh, const float *Vh,
                                            uint32_t k0, uint32_t seq_k, uint32_t tid) {
+    const uint32_t valid = min(64u, seq_k - k0);
+    ap_load_rows_t(Ks, Kh + static_cast<uint64_t>(k0) * kApD, valid, tid);
 #pragma unroll
     for (uint32_t i = tid; i < kAttBK * kApD / 4; i += kApThreads) {
         const uint32_t j = i >> 5, c4 = i & 31u;
-        const bool ok = k0 + j < seq_k;
+        const bool ok = j < valid;
         const uint64_t row = ok ? k0 + j : k0;
-        cp_async_16_zfill(Ks + j * kApRow + 4 * c4, Kh + row * kApD + 4 * c4, ok);
         cp_async_16_zfill(Vs + j * kApD + 4 * c4, Vh + row * kApD + 4 * c4, ok);
     }
 }
@@ -661,9 +675,9 @@ __device__ __forceinline__ void fma4(float4 &a, const float4 &v, float p) {
 __global__ void __launch_bounds__(kApThreads, 1) attention_prefill_kernel(const AttParams p) {
     pdl_enter();
     extern __shared__ __align__(16) float ap_smem[];
-    float *Qs = ap_smem;                          // [64][kApRow]
-    float *Kst = Qs + kApBQ * kApRow;             // [2][64][kApRow]
-    float *Vst = Kst + 2 * kAttBK * kApRow;       // [2][64][128]
+    float *Qs = ap_smem;                          // [64][kApTRow] chain-major
+    float *Kst = Qs + kApBQ * kApTRow;            // [2][64][kApTRow] chain-major
+    float *Vst = Kst + 2 * kAttBK * kApTRow;      // [2][64][128]
     float *S = Vst + 2 * kAttBK * kApD;           // [64][64] scores, then probabilities
 
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -683,13 +697,7 @@ __global__ void __launch_bounds__(kApThreads, 1) attention_prefill_kernel(const 
     const uint32_t nblk = (k_end + kAttBK - 1) / kAttBK;
 
     // Q rows (zero past seq_q) and the first K/V block: copy group 0.
-#pragma unroll
-    for (uint32_t i = tid; i < kApBQ * kApD / 4; i += kApThreads) {
-        const uint32_t q = i >> 5, c4 = i & 31u;
-        const bool ok = q < qc;
-        cp_async_16_zfill(Qs + q * kApRow + 4 * c4,
-                          p.Q + head_q + static_cast<uint64_t>(q0 + (ok ? q : 0u)) * kApD + 4 * c4, ok);
-    }
+    ap_load_rows_t(Qs, p.Q + head_q + static_cast<uint64_t>(q0) * kApD, qc, tid);
     if (nblk > 0) ap_load_kv(Kst, Vst, Kh, Vh, 0, p.seq_k, tid);
     cp_async_commit();
 
@@ -704,12 +712,18 @@ __global__ void __launch_bounds__(kApThreads, 1) attention_prefill_kernel(const 
     for (uint32_t q = 0; q < 8; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
 
     const uint32_t wq_last = q0 + 8 * warp + 7;   // last query row of the warp
+    // score lanes: chain c = lane % 8; slot r holds query 8*warp + (r ^ mq)
+    const uint32_t c_ = lane & 7u;
+    const uint32_t mq = ((c_ >> 2) & 1u) * 4u + (c_ & 1u) * 2u + ((c_ >> 1) & 1u);
+    const float *qptr[8];
+#pragma unroll
+    for (uint32_t r = 0; r < 8; ++r) qptr[r] = Qs + (8 * warp + (r ^ mq)) * kApTRow + c_ * kApCS;
     for (uint32_t b = 0; b < nblk; ++b) {
         const uint32_t k0 = b * kAttBK;
         const uint32_t kc = min(kAttBK, p.seq_k - k0);
         if (b + 1 < nblk) {
             const uint32_t nx = (b + 1) & 1u;
-            ap_load_kv(Kst + nx * kAttBK * kApRow, Vst + nx * kAttBK * kApD, Kh, Vh, k0 + kAttBK,
+            ap_load_kv(Kst + nx * kAttBK * kApTRow, Vst + nx * kAttBK * kApD, Kh, Vh, k0 + kAttBK,
                        p.seq_k, tid);
             cp_async_commit();
             cp_async_wait_group<1>();
@@ -717,63 +731,73 @@ __global__ void __launch_bounds__(kApThreads, 1) attention_prefill_kernel(const 
             cp_async_wait_group<0>();
         }
         __syncthreads();   // block b (and Q) visible to every warp
-        const float *Ks = Kst + (b & 1u) * kAttBK * kApRow;
+        const float *Ks = Kst + (b & 1u) * kAttBK * kApTRow;
         const float *Vs = Vst + (b & 1u) * kAttBK * kApD;
 
-        // ---- scores: queries qa, qa+1 x keys jb + kl + 8u
+        // ---- scores: lane (c, kg) runs chain c of the warp's 8 queries x keys
+        // jb + 8kg + u (u < 8), then the eight chains of each pair are summed
+        // across lanes in hsum256 order
         {
-            const uint32_t qs = lane >> 3, kl = lane & 7u;
-            const uint32_t qa = 8 * warp + 2 * qs;
-            const float *qra = Qs + qa * kApRow, *qrb = qra + kApRow;
+            const uint32_t c = lane & 7u, kg = lane >> 3;
 #pragma unroll 1
             for (uint32_t jb = 0; jb < kAttBK; jb += 32) {
                 // a half whose keys are past kc, or causal-masked for every
                 // query of the warp, is left out (the softmax masks it)
                 if (jb >= kc || (p.causal && k0 + jb > wq_last + causal_offset)) break;
-                float c[2][4][8];
+                float acc[8][8];
 #pragma unroll
-                for (uint32_t h = 0; h < 2; ++h)
+                for (uint32_t r = 0; r < 8; ++r)
 #pragma unroll
-                    for (uint32_t u = 0; u < 4; ++u)
+                    for (uint32_t u = 0; u < 8; ++u) acc[r][u] = 0.0f;
+                const float *kc_ = Ks + (jb + 8u * kg) * kApTRow + c * kApCS;
+#pragma unroll 1
+                for (uint32_t tg = 0; tg < 4; ++tg) {
+                    float4 qv[8];
 #pragma unroll
-                        for (uint32_t y = 0; y < 8; ++y) c[h][u][y] = 0.0f;
-                const float *kr = Ks + (jb + kl) * kApRow;
-#pragma unroll 2
-                for (uint32_t t = 0; t < kApD / 8; ++t) {
-                    const float4 a0 = *reinterpret_cast<const float4 *>(qra + 8 * t);
-                    const float4 a1 = *reinterpret_cast<const float4 *>(qra + 8 * t + 4);
-                    const float4 b0 = *reinterpret_cast<const float4 *>(qrb + 8 * t);
-                    const float4 b1 = *reinterpret_cast<const float4 *>(qrb + 8 * t + 4);
+                    for (uint32_t r = 0; r < 8; ++r)
+                        qv[r] = *reinterpret_cast<const float4 *>(qptr[r] + 4 * tg);
 #pragma unroll
-                    for (uint32_t u = 0; u < 4; ++u) {
-                        const float4 x0 = *reinterpret_cast<const float4 *>(kr + 8 * u * kApRow + 8 * t);
-                        const float4 x1 =
-                            *reinterpret_cast<const float4 *>(kr + 8 * u * kApRow + 8 * t + 4);
-#define VNPU_AP_CHAINS(ACC, Q0, Q1)                 \
-    ACC[0] = __fmaf_rn(Q0.x, x0.x, ACC[0]);         \
-    ACC[1] = __fmaf_rn(Q0.y, x0.y, ACC[1]);         \
-    ACC[2] = __fmaf_rn(Q0.z, x0.z, ACC[2]);         \
-    ACC[3] = __fmaf_rn(Q0.w, x0.w, ACC[3]);         \
-    ACC[4] = __fmaf_rn(Q1.x, x1.x, ACC[4]);         \
-    ACC[5] = __fmaf_rn(Q1.y, x1.y, ACC[5]);         \
-    ACC[6] = __fmaf_rn(Q1.z, x1.z, ACC[6]);         \
-    ACC[7] = __fmaf_rn(Q1.w, x1.w, ACC[7]);
-                        VNPU_AP_CHAINS(c[0][u], a0, a1)
-                        VNPU_AP_CHAINS(c[1][u], b0, b1)
-#undef VNPU_AP_CHAINS
+                    for (uint32_t u = 0; u < 8; ++u) {
+                        const float4 kv = *reinterpret_cast<const float4 *>(kc_ + u * kApTRow + 4 * tg);
+#pragma unroll
+                        for (uint32_t r = 0; r < 8; ++r) {
+                            acc[r][u] = __fmaf_rn(qv[r].x, kv.x, acc[r][u]);
+                            acc[r][u] = __fmaf_rn(qv[r].y, kv.y, acc[r][u]);
+                            acc[r][u] = __fmaf_rn(qv[r].z, kv.z, acc[r][u]);
+                            acc[r][u] = __fmaf_rn(qv[r].w, kv.w, acc[r][u]);
+                        }
                     }
                 }
+                // Slot r of lane c holds query r ^ mq: each step keeps the
+                // lower slots and adds the partner's upper ones, which hold
+                // the same queries; partners c^4, c^1, c^2 give
+                // ((c0+c4)+(c1+c5))+((c2+c6)+(c3+c7)) (each add commutes).
 #pragma unroll
-                for (uint32_t h = 0; h < 2; ++h)
+                for (uint32_t r = 0; r < 4; ++r)
 #pragma unroll
-                    for (uint32_t u = 0; u < 4; ++u) {
-                        const uint32_t q = qa + h, j = jb + kl + 8 * u;
-                        const uint32_t qi = q0 + q;
-                        float sc = __fmul_rn(hsum256_chains(c[h][u]), p.scale);
-                        if (Mh && qi < p.seq_q && j < kc)
-                            sc = __fadd_rn(sc, Mh[static_cast<uint64_t>(qi) * p.seq_k + k0 + j]);
-                        S[q * kAttBK + j] = sc;
-                    }
+                    for (uint32_t u = 0; u < 8; ++u)
+                        acc[r][u] = __fadd_rn(acc[r][u], __shfl_xor_sync(0xffffffffu, acc[r + 4][u], 4));
+#pragma unroll
+                for (uint32_t r = 0; r < 2; ++r)
+#pragma unroll
+                    for (uint32_t u = 0; u < 8; ++u)
+                        acc[r][u] = __fadd_rn(acc[r][u], __shfl_xor_sync(0xffffffffu, acc[r + 2][u], 1));
+#pragma unroll
+                for (uint32_t u = 0; u < 8; ++u)
+                    acc[0][u] = __fadd_rn(acc[0][u], __shfl_xor_sync(0xffffffffu, acc[1][u], 2));
+                const uint32_t q = 8 * warp + mq;
+                const uint32_t qi = q0 + q;
+                float sc[8];
+#pragma unroll
+                for (uint32_t u = 0; u < 8; ++u) {
+                    const uint32_t jj = jb + 8u * kg + u;
+                    sc[u] = __fmul_rn(acc[0][u], p.scale);
+                    if (Mh && qi < p.seq_q && jj < kc)
+                        sc[u] = __fadd_rn(sc[u], Mh[static_cast<uint64_t>(qi) * p.seq_k + k0 + jj]);
+                }
+                float4 *srow4 = reinterpret_cast<float4 *>(S + q * kAttBK + jb + 8u * kg);
+                srow4[0] = make_float4(sc[0], sc[1], sc[2], sc[3]);
+                srow4[1] = make_float4(sc[4], sc[5], sc[6], sc[7]);
             }
         }
         __syncwarp();

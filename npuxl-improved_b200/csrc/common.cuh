@@ -444,6 +444,12 @@ __device__ __forceinline__ void cp_async_16_zfill(void *smem_dst, const void *gm
                  "l"(gmem_src), "r"(valid ? 16u : 0u)
                  : "memory");
 }
+// 4-byte form (any 4-aligned addresses, e.g. to transpose while copying).
+__device__ __forceinline__ void cp_async_4_zfill(void *smem_dst, const void *gmem_src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_addr(smem_dst)),
+                 "l"(gmem_src), "r"(valid ? 4u : 0u)
+                 : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() {
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
