@@ -676,11 +676,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
 // Split-K finish: C[m][n] = dequant(sum over splits of ws[s][m][n]) - the
 // int32 sums are exact, so the result is the single-pass GEMM's bit for bit.
 // ws rows are s * m_pad + m, N columns; four columns per thread (N % 4 == 0).
+// With R (MATMUL_I8_RESIDUAL) C = R + that, ADD_F32's single rounding.
 __global__ void __launch_bounds__(256) splitk_finish_kernel(
     const int4 *__restrict__ ws, uint32_t splits, uint32_t m_pad, uint32_t M, uint32_t N,
     const float *__restrict__ scale_a, const float *__restrict__ scale_b,
     const float *__restrict__ bias, float *__restrict__ C, uint32_t ldc, uint32_t epilogue,
-    uint32_t form) {
+    uint32_t form, const float *__restrict__ R, uint32_t ldr) {
     pdl_enter();
     const uint32_t n4 = N / 4;
     const uint32_t total = M * n4;
@@ -707,10 +708,17 @@ __global__ void __launch_bounds__(256) splitk_finish_kernel(
             bv.z = __ldg(bias + n + 2);
             bv.w = __ldg(bias + n + 3);
         }
-        const float4 o = make_float4(ref_dequant(a.x, sa, sb.x, has_bias, bv.x, epilogue, form),
-                                     ref_dequant(a.y, sa, sb.y, has_bias, bv.y, epilogue, form),
-                                     ref_dequant(a.z, sa, sb.z, has_bias, bv.z, epilogue, form),
-                                     ref_dequant(a.w, sa, sb.w, has_bias, bv.w, epilogue, form));
+        float4 o = make_float4(ref_dequant(a.x, sa, sb.x, has_bias, bv.x, epilogue, form),
+                               ref_dequant(a.y, sa, sb.y, has_bias, bv.y, epilogue, form),
+                               ref_dequant(a.z, sa, sb.z, has_bias, bv.z, epilogue, form),
+                               ref_dequant(a.w, sa, sb.w, has_bias, bv.w, epilogue, form));
+        if (R) {
+            const float *r = R + static_cast<uint64_t>(m) * ldr + n;
+            o.x = __fadd_rn(__ldg(r), o.x);
+            o.y = __fadd_rn(__ldg(r + 1), o.y);
+            o.z = __fadd_rn(__ldg(r + 2), o.z);
+            o.w = __fadd_rn(__ldg(r + 3), o.w);
+        }
         float *c = C + static_cast<uint64_t>(m) * ldc + n;
         if (vec) {
             *reinterpret_cast<float4 *>(c) = o;
@@ -1755,7 +1763,7 @@ cudaError_t matmul_i8_pair_splitk(const LaunchCtx &ctx, const MatmulI8 &p, TcPar
                                                    static_cast<uint32_t>(ctx.num_sms) * 8u);
         e = launch_pdl(ctx.stream, splitk_finish_kernel, dim3(blocks), dim3(256), 0,
                        reinterpret_cast<const int4 *>(ws), splits, tp.m_pad, p.M, p.N, p.scale_a,
-                       p.scale_b, p.bias, p.C, p.ldc, p.epilogue, p.form);
+                       p.scale_b, p.bias, p.C, p.ldc, p.epilogue, p.form, p.R, p.ldr);
         count_launch(ctx);
     }
     cudaFreeAsync(ws, ctx.stream);
@@ -1827,6 +1835,7 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         }
         if (splits > 1)   // every other field of tp is set above
             return matmul_i8_pair_splitk(ctx, p, tp, tmap_a, splits, static_cast<uint32_t>(max_pairs));
+        if (p.R) return cudaErrorNotSupported;   // the residual rides on the split-K finish only
         CUtensorMap tmap_c;
         tp.tma_store = (reinterpret_cast<uintptr_t>(p.C) % 16u == 0u) && (p.ldc % 4u == 0u) &&
                        encode_tmap_2d(&tmap_c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.C, p.N, p.M,
@@ -1855,6 +1864,7 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         count_launch(ctx);
         return cudaGetLastError();
     }
+    if (p.R) return cudaErrorNotSupported;
     CUtensorMap tmap_a;
     if (!encode_tmap_kmajor_i8(&tmap_a, p.A, p.K, p.M, p.lda, kBK, kBM))
         return cudaErrorInvalidValue;
@@ -2033,6 +2043,13 @@ cudaError_t matmul_i8_simt(const LaunchCtx &ctx, const MatmulI8 &p) {
     g_last_kernel.store("gemm_i8_simt_kernel", std::memory_order_relaxed);
     count_launch(ctx);
     return cudaGetLastError();
+}
+
+cudaError_t matmul_i8_split_residual(const LaunchCtx &ctx, const MatmulI8 &p) {
+    if (!p.R || p.ndst != 0 ||
+        choose_matmul_kernel(p.M, p.K, p.N, p.lda, p.A) != MatmulKernel::kTcgen05)
+        return cudaErrorNotSupported;
+    return matmul_i8_tcgen05(ctx, p);
 }
 
 cudaError_t matmul_i8(const LaunchCtx &ctx, const MatmulI8 &p) {

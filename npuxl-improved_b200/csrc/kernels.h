@@ -69,9 +69,18 @@ struct MatmulI8 {
     uint32_t ndst = 0;
     uint32_t ldd = 0;
     uint32_t col_offset = 0;
+    // Residual (MATMUL_I8_RESIDUAL): C = R + out, R [M][ldr]; taken only by
+    // matmul_i8_split_residual.
+    const float *R = nullptr;
+    uint32_t ldr = 0;
 };
 
 enum class MatmulKernel { kTcgen05, kGemv, kSimt };
+
+// MATMUL_I8 with the residual add (p.R) folded into the split-K finish
+// kernel of the CTA-pair GEMM; cudaErrorNotSupported, with nothing launched,
+// when the shape does not take that path (the caller then adds separately).
+cudaError_t matmul_i8_split_residual(const LaunchCtx &ctx, const MatmulI8 &p);
 
 // MATMUL_I8 with the scatter epilogue (CTA-pair kernel; TMA-aligned A required).
 cudaError_t matmul_i8_scatter(const LaunchCtx &ctx, const MatmulI8 &p);

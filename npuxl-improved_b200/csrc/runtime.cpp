@@ -789,8 +789,18 @@ void exec_matmul_i8_residual(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32
                        "residual scratch");
             p.C = tmp;
         }
-        cudaError_t e = matmul_i8(ctx, p);
-        if (e == cudaSuccess) e = add(ctx, R, p.C, out, count, 1.0f, 1.0f);
+        cudaError_t e = cudaErrorNotSupported;
+        if (!aliased) {
+            // split-K shapes add R in the finish kernel
+            MatmulI8 f = p;
+            f.R = R;
+            f.ldr = ldr;
+            e = matmul_i8_split_residual(ctx, f);
+        }
+        if (e == cudaErrorNotSupported) {
+            e = matmul_i8(ctx, p);
+            if (e == cudaSuccess) e = add(ctx, R, p.C, out, count, 1.0f, 1.0f);
+        }
         if (tmp) cudaFreeAsync(tmp, ctx.stream);
         cuda_check(e, "matmul_i8_residual launch");
     }

@@ -168,11 +168,13 @@ def test_qkv_rope_append_position_past_capacity(b200_lib, oracle, torch):
 @pytest.mark.parametrize("M,K,N,inplace,epi", [
     (1, 4096, 4096, False, 0), (1, 1000, 333, True, 0), (4, 512, 1024, False, 0),
     (300, 256, 512, True, 0), (300, 256, 512, False, 0), (512, 4096, 4096, False, 0),
-    (777, 1000, 1000, False, 1), (260, 4096, 11008, False, 0), (300, 256, 512, False, 2)])
+    (777, 1000, 1000, False, 1), (260, 4096, 11008, False, 0), (300, 256, 512, False, 2),
+    (300, 2048, 1000, False, 1), (512, 11008, 4096, False, 0), (512, 4096, 4096, True, 0)])
 def test_residual_equals_matmul_then_add(gpu, oracle, torch, M, K, N, inplace, epi):
     """MATMUL_I8_RESIDUAL equals MATMUL_I8 then ADD_F32 bit for bit: the GEMV
-    epilogue (M = 1) and the two-pass form (M > 1, R aliasing C or not, ragged
-    N, epilogues)."""
+    epilogue (M = 1), the add in the split-K finish kernel (M = 300, 512 with
+    long K), and the two-pass form otherwise (R aliasing C, ragged N,
+    epilogues)."""
     rng = np.random.default_rng(M + K + N)
     w = _weights(gpu, oracle, rng, K, N)
     A8h, sah = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
