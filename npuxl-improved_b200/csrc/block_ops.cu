@@ -635,7 +635,13 @@ constexpr uint32_t kApD = 128;
 // stride of 20 floats puts the eight chains in distinct bank groups.
 constexpr uint32_t kApCS = 20;
 constexpr uint32_t kApTRow = 8 * kApCS;   // floats per chain-major row
-constexpr size_t kApSmemFloats = static_cast<size_t>(kApBQ) * kApTRow + 2u * kAttBK * kApTRow +
+// K rows go in pairs, interleaved: keys 2i and 2i+1 of chain c at step t sit
+// side by side, so a 16-byte load gives two steps of a key pair as two f32x2
+// operands; 36 floats per chain keep the eight chains in distinct bank groups.
+constexpr uint32_t kApKCS = 36;
+constexpr uint32_t kApKPRow = 8 * kApKCS;   // floats per key pair
+constexpr uint32_t kApKStage = (kAttBK / 2) * kApKPRow;
+constexpr size_t kApSmemFloats = static_cast<size_t>(kApBQ) * kApTRow + 2u * kApKStage +
                                  2u * kAttBK * kApD + static_cast<size_t>(kApBQ) * kAttBK;
 
 // 64 rows of 128 floats (rows >= valid zero) into chain-major rows, by
@@ -651,11 +657,19 @@ __device__ __forceinline__ void ap_load_rows_t(float *T, const float *src, uint3
     }
 }
 
-// Block k0 of K (chain-major) and V (64 rows; rows past seq_k zero) into one stage.
+// Block k0 of K (chain-major, key pairs interleaved) and V (64 rows; rows
+// past seq_k zero) into one stage.
 __device__ __forceinline__ void ap_load_kv(float *Ks, float *Vs, const float *Kh, const float *Vh,
                                            uint32_t k0, uint32_t seq_k, uint32_t tid) {
     const uint32_t valid = min(64u, seq_k - k0);
-    ap_load_rows_t(Ks, Kh + static_cast<uint64_t>(k0) * kApD, valid, tid);
+    const float *src = Kh + static_cast<uint64_t>(k0) * kApD;
+#pragma unroll 4
+    for (uint32_t e = tid; e < 64u * kApD; e += kApThreads) {
+        const uint32_t row = e >> 7, d = e & 127u;
+        const bool ok = row < valid;
+        cp_async_4_zfill(Ks + (row >> 1) * kApKPRow + (d & 7u) * kApKCS + (d >> 3) * 2u + (row & 1u),
+                         src + static_cast<uint64_t>(ok ? row : 0u) * kApD + d, ok);
+    }
 #pragma unroll
     for (uint32_t i = tid; i < kAttBK * kApD / 4; i += kApThreads) {
         const uint32_t j = i >> 5, c4 = i & 31u;
@@ -665,19 +679,20 @@ __device__ __forceinline__ void ap_load_kv(float *Ks, float *Vs, const float *Kh
     }
 }
 
-__device__ __forceinline__ void fma4(float4 &a, const float4 &v, float p) {
-    a.x = __fmaf_rn(v.x, p, a.x);
-    a.y = __fmaf_rn(v.y, p, a.y);
-    a.z = __fmaf_rn(v.z, p, a.z);
-    a.w = __fmaf_rn(v.w, p, a.w);
+// a += v * p for four dims held as two f32 pairs: fma(v[d], p, a[d]) each,
+// two per fma.rn.f32x2.
+__device__ __forceinline__ void fma4x2(uint64_t (&a)[2], const ulonglong2 &v, float p) {
+    const uint64_t pp = pack_f32x2(p, p);
+    a[0] = fma_f32x2(v.x, pp, a[0]);
+    a[1] = fma_f32x2(v.y, pp, a[1]);
 }
 
 __global__ void __launch_bounds__(kApThreads, 1) attention_prefill_kernel(const AttParams p) {
     pdl_enter();
     extern __shared__ __align__(16) float ap_smem[];
     float *Qs = ap_smem;                          // [64][kApTRow] chain-major
-    float *Kst = Qs + kApBQ * kApTRow;            // [2][64][kApTRow] chain-major
-    float *Vst = Kst + 2 * kAttBK * kApTRow;      // [2][64][128]
+    float *Kst = Qs + kApBQ * kApTRow;            // [2][32 key pairs][kApKPRow]
+    float *Vst = Kst + 2 * kApKStage;             // [2][64][128]
     float *S = Vst + 2 * kAttBK * kApD;           // [64][64] scores, then probabilities
 
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -707,9 +722,10 @@ __global__ void __launch_bounds__(kApThreads, 1) attention_prefill_kernel(const 
     const uint32_t sqi = q0 + srow;
     float m_run = ninf, l_run = 0.0f;
     // value lanes: dims 4*lane..4*lane+3 of the warp's 8 queries
-    float4 acc[8];
+    // as pairs (dims 0-1, 2-3) for fma.rn.f32x2: two independent fmaf per instruction
+    uint64_t acc[8][2];
 #pragma unroll
-    for (uint32_t q = 0; q < 8; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint32_t q = 0; q < 8; ++q) acc[q][0] = acc[q][1] = 0ull;
 
     const uint32_t wq_last = q0 + 8 * warp + 7;   // last query row of the warp
     // score lanes: chain c = lane % 8; slot r holds query 8*warp + (r ^ mq)
@@ -723,7 +739,7 @@ __global__ void __launch_bounds__(kApThreads, 1) attention_prefill_kernel(const 
         const uint32_t kc = min(kAttBK, p.seq_k - k0);
         if (b + 1 < nblk) {
             const uint32_t nx = (b + 1) & 1u;
-            ap_load_kv(Kst + nx * kAttBK * kApTRow, Vst + nx * kAttBK * kApD, Kh, Vh, k0 + kAttBK,
+            ap_load_kv(Kst + nx * kApKStage, Vst + nx * kAttBK * kApD, Kh, Vh, k0 + kAttBK,
                        p.seq_k, tid);
             cp_async_commit();
             cp_async_wait_group<1>();
@@ -731,7 +747,7 @@ __global__ void __launch_bounds__(kApThreads, 1) attention_prefill_kernel(const 
             cp_async_wait_group<0>();
         }
         __syncthreads();   // block b (and Q) visible to every warp
-        const float *Ks = Kst + (b & 1u) * kAttBK * kApTRow;
+        const float *Ks = Kst + (b & 1u) * kApKStage;
         const float *Vs = Vst + (b & 1u) * kAttBK * kApD;
 
         // ---- scores: lane (c, kg) runs chain c of the warp's 8 queries x keys
@@ -744,30 +760,49 @@ __global__ void __launch_bounds__(kApThreads, 1) attention_prefill_kernel(const 
                 // a half whose keys are past kc, or causal-masked for every
                 // query of the warp, is left out (the softmax masks it)
                 if (jb >= kc || (p.causal && k0 + jb > wq_last + causal_offset)) break;
-                float acc[8][8];
+                // acc2[r][i]: keys 2i, 2i+1 of slot r, one fma.rn.f32x2 per step
+                uint64_t acc2[8][4];
 #pragma unroll
                 for (uint32_t r = 0; r < 8; ++r)
 #pragma unroll
-                    for (uint32_t u = 0; u < 8; ++u) acc[r][u] = 0.0f;
-                const float *kc_ = Ks + (jb + 8u * kg) * kApTRow + c * kApCS;
+                    for (uint32_t i = 0; i < 4; ++i) acc2[r][i] = 0ull;
+                const float *kp_ = Ks + (jb / 2u + 4u * kg) * kApKPRow + c * kApKCS;
 #pragma unroll 1
                 for (uint32_t tg = 0; tg < 4; ++tg) {
                     float4 qv[8];
 #pragma unroll
                     for (uint32_t r = 0; r < 8; ++r)
                         qv[r] = *reinterpret_cast<const float4 *>(qptr[r] + 4 * tg);
+                    // kk[i][0] = steps 4tg, 4tg+1 of key pair i; kk[i][1] = steps 4tg+2, 4tg+3
+                    ulonglong2 kk[4][2];
 #pragma unroll
-                    for (uint32_t u = 0; u < 8; ++u) {
-                        const float4 kv = *reinterpret_cast<const float4 *>(kc_ + u * kApTRow + 4 * tg);
+                    for (uint32_t i = 0; i < 4; ++i) {
+                        kk[i][0] = *reinterpret_cast<const ulonglong2 *>(kp_ + i * kApKPRow + 8 * tg);
+                        kk[i][1] = *reinterpret_cast<const ulonglong2 *>(kp_ + i * kApKPRow + 8 * tg + 4);
+                    }
 #pragma unroll
-                        for (uint32_t r = 0; r < 8; ++r) {
-                            acc[r][u] = __fmaf_rn(qv[r].x, kv.x, acc[r][u]);
-                            acc[r][u] = __fmaf_rn(qv[r].y, kv.y, acc[r][u]);
-                            acc[r][u] = __fmaf_rn(qv[r].z, kv.z, acc[r][u]);
-                            acc[r][u] = __fmaf_rn(qv[r].w, kv.w, acc[r][u]);
+                    for (uint32_t r = 0; r < 8; ++r) {
+                        const float qs[4] = {qv[r].x, qv[r].y, qv[r].z, qv[r].w};
+#pragma unroll
+                        for (uint32_t st = 0; st < 4; ++st) {
+                            const uint64_t qq = pack_f32x2(qs[st], qs[st]);
+#pragma unroll
+                            for (uint32_t i = 0; i < 4; ++i) {
+                                const uint64_t kpair = st == 0 ? kk[i][0].x : st == 1 ? kk[i][0].y
+                                                     : st == 2 ? kk[i][1].x : kk[i][1].y;
+                                acc2[r][i] = fma_f32x2(qq, kpair, acc2[r][i]);
+                            }
                         }
                     }
                 }
+                float acc[8][8];
+#pragma unroll
+                for (uint32_t r = 0; r < 8; ++r)
+#pragma unroll
+                    for (uint32_t i = 0; i < 4; ++i) {
+                        acc[r][2 * i] = half_f32x2(acc2[r][i], 0);
+                        acc[r][2 * i + 1] = half_f32x2(acc2[r][i], 1);
+                    }
                 // Slot r of lane c holds query r ^ mq: each step keeps the
                 // lower slots and adds the partner's upper ones, which hold
                 // the same queries; partners c^4, c^1, c^2 give
@@ -878,10 +913,10 @@ __global__ void __launch_bounds__(kApThreads, 1) attention_prefill_kernel(const 
                 nmax = max(nmax, nq[q]);
                 allpre = allpre && (iq & 2u);
                 if (iq & 1u) {
-                    acc[q].x = __fmul_rn(acc[q].x, aq);
-                    acc[q].y = __fmul_rn(acc[q].y, aq);
-                    acc[q].z = __fmul_rn(acc[q].z, aq);
-                    acc[q].w = __fmul_rn(acc[q].w, aq);
+#pragma unroll
+                    for (uint32_t h = 0; h < 2; ++h)
+                        acc[q][h] = pack_f32x2(__fmul_rn(half_f32x2(acc[q][h], 0), aq),
+                                               __fmul_rn(half_f32x2(acc[q][h], 1), aq));
                 }
             }
             const float *vcol = Vs + 4 * lane;
@@ -890,34 +925,34 @@ __global__ void __launch_bounds__(kApThreads, 1) attention_prefill_kernel(const 
                 uint32_t j = 0;
 #pragma unroll 2
                 for (; j + 4 <= nmin; j += 4) {
-                    float4 v[4];
+                    ulonglong2 v[4];
 #pragma unroll
                     for (uint32_t u = 0; u < 4; ++u)
-                        v[u] = *reinterpret_cast<const float4 *>(vcol + (j + u) * kApD);
+                        v[u] = *reinterpret_cast<const ulonglong2 *>(vcol + (j + u) * kApD);
 #pragma unroll
                     for (uint32_t q = 0; q < 8; ++q) {
                         const float4 pp = *reinterpret_cast<const float4 *>(Pw + q * kAttBK + j);
-                        fma4(acc[q], v[0], pp.x);
-                        fma4(acc[q], v[1], pp.y);
-                        fma4(acc[q], v[2], pp.z);
-                        fma4(acc[q], v[3], pp.w);
+                        fma4x2(acc[q], v[0], pp.x);
+                        fma4x2(acc[q], v[1], pp.y);
+                        fma4x2(acc[q], v[2], pp.z);
+                        fma4x2(acc[q], v[3], pp.w);
                     }
                 }
 #pragma unroll 1
                 for (; j < nmax; ++j) {
-                    const float4 v = *reinterpret_cast<const float4 *>(vcol + j * kApD);
+                    const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(vcol + j * kApD);
 #pragma unroll
                     for (uint32_t q = 0; q < 8; ++q)
-                        if (j < nq[q]) fma4(acc[q], v, Pw[q * kAttBK + j]);
+                        if (j < nq[q]) fma4x2(acc[q], v, Pw[q * kAttBK + j]);
                 }
             } else {
 #pragma unroll 1
                 for (uint32_t j = 0; j < kc; ++j) {
-                    const float4 v = *reinterpret_cast<const float4 *>(vcol + j * kApD);
+                    const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(vcol + j * kApD);
 #pragma unroll
                     for (uint32_t q = 0; q < 8; ++q) {
                         const float pq = Pw[q * kAttBK + j];
-                        if (pq != 0.0f) fma4(acc[q], v, pq);
+                        if (pq != 0.0f) fma4x2(acc[q], v, pq);
                     }
                 }
             }
@@ -931,8 +966,10 @@ __global__ void __launch_bounds__(kApThreads, 1) attention_prefill_kernel(const 
         if (qi >= p.seq_q) continue;
         const float inv = lq > 0.0f ? __fdiv_rn(1.0f, lq) : 0.0f;
         reinterpret_cast<float4 *>(p.O + head_q + static_cast<uint64_t>(qi) * kApD)[lane] =
-            make_float4(__fmul_rn(acc[q].x, inv), __fmul_rn(acc[q].y, inv),
-                        __fmul_rn(acc[q].z, inv), __fmul_rn(acc[q].w, inv));
+            make_float4(__fmul_rn(half_f32x2(acc[q][0], 0), inv),
+                        __fmul_rn(half_f32x2(acc[q][0], 1), inv),
+                        __fmul_rn(half_f32x2(acc[q][1], 0), inv),
+                        __fmul_rn(half_f32x2(acc[q][1], 1), inv));
     }
 }
 

@@ -444,6 +444,27 @@ __device__ __forceinline__ void cp_async_16_zfill(void *smem_dst, const void *gm
                  "l"(gmem_src), "r"(valid ? 16u : 0u)
                  : "memory");
 }
+// sm_100 two-lane FMA: d.lo = fma(a.lo, b.lo, c.lo), d.hi = fma(a.hi, b.hi,
+// c.hi), each rounded once like fmaf.  Half the issue slots of two FFMAs.
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float half_f32x2(uint64_t v, int hi) {
+    float lo_v, hi_v;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo_v), "=f"(hi_v) : "l"(v));
+    return hi ? hi_v : lo_v;
+}
+__device__ __forceinline__ uint64_t swap_f32x2(uint64_t v) {
+    return pack_f32x2(half_f32x2(v, 1), half_f32x2(v, 0));
+}
+
 // 4-byte form (any 4-aligned addresses, e.g. to transpose while copying).
 __device__ __forceinline__ void cp_async_4_zfill(void *smem_dst, const void *gmem_src, bool valid) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_addr(smem_dst)),

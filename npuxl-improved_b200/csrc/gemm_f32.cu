@@ -112,27 +112,6 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(kPending) : "memory");
 }
 
-// sm_100 two-lane FMA: d.lo = fma(a.lo, b.lo, c.lo), d.hi = fma(a.hi, b.hi,
-// c.hi), each rounded once like fmaf.  Half the issue slots of two FFMAs.
-__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ float half_f32x2(uint64_t v, int hi) {
-    float lo_v, hi_v;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo_v), "=f"(hi_v) : "l"(v));
-    return hi ? hi_v : lo_v;
-}
-__device__ __forceinline__ uint64_t swap_f32x2(uint64_t v) {
-    return pack_f32x2(half_f32x2(v, 1), half_f32x2(v, 0));
-}
-
 template <int kMode> struct F32Shape {
     static constexpr int BM = kMode == kF32Dot8 ? 64 : 128;   // CTA tile (square)
     static constexpr int TM = BM / 16;                        // outputs per thread per axis
