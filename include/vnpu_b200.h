@@ -40,6 +40,16 @@ extern "C" {
 #define VNPU_CMD_FLAG_EPI_SCALAR   (1u << 9)
 
 /*
+ * ATTENTION_F32 output layout (no reference counterpart): with this flag O is
+ * written token-major, [batch][seq_q][heads][head_dim], the row layout the
+ * next projection reads, instead of the reference's head-major
+ * [batch][heads][seq_q][head_dim] (reference include/vnpu.h attention args).
+ * The values are the same bits; only their places differ.  Q, K, V and the
+ * mask keep the reference's layouts.
+ */
+#define VNPU_CMD_FLAG_ATTN_TOKEN_MAJOR (1u << 10)
+
+/*
  * Fused row prologues for MATMUL_I8 (no reference counterpart; the reference
  * submits RMSNORM_F32 or SWIGLU_F32 and then QUANTIZE_I8 per row).  Opcodes
  * outside the reference's range, as its ABI rules allow (reference

@@ -398,7 +398,17 @@ struct AttParams {
     float scale;
     uint32_t *err;       // stream error word (bounded waits)
     uint64_t wait_ns;    // bound of every device-side wait
+    uint32_t o_tokens = 0;   // 1: O is [batch][seq_q][heads][D] (token-major rows)
 };
+
+// Output row of query qi of (batch * heads + h) = bh: head-major as the
+// reference lays it out, or token-major (VNPU_CMD_FLAG_ATTN_TOKEN_MAJOR).
+// With seq_q == 1 the two are the same addresses.
+__device__ __forceinline__ float *att_out_row(const AttParams &p, uint32_t bh, uint32_t qi) {
+    if (!p.o_tokens) return p.O + (static_cast<uint64_t>(bh) * p.seq_q + qi) * p.D;
+    const uint32_t b = bh / p.heads, h = bh - b * p.heads;
+    return p.O + ((static_cast<uint64_t>(b) * p.seq_q + qi) * p.heads + h) * p.D;
+}
 
 // Layout in shared memory:
 //   Qs [16 q][8 chains][D/8] - chain-major, so a thread reads its chain of a
@@ -577,7 +587,7 @@ __global__ void __launch_bounds__(kAttThreads) attention_kernel(const AttParams 
     }
     if (warp < qc) {
         const float inv = l_run > 0.0f ? __fdiv_rn(1.0f, l_run) : 0.0f;
-        float *orow = p.O + head_q + static_cast<uint64_t>(q0 + warp) * D;
+        float *orow = att_out_row(p, bh, q0 + warp);
         if (VEC) {
 #pragma unroll
             for (uint32_t r = 0; r < 2; ++r) {
@@ -965,7 +975,7 @@ __global__ void __launch_bounds__(kApThreads, 1) attention_prefill_kernel(const 
         const uint32_t qi = q0 + 8 * warp + q;
         if (qi >= p.seq_q) continue;
         const float inv = lq > 0.0f ? __fdiv_rn(1.0f, lq) : 0.0f;
-        reinterpret_cast<float4 *>(p.O + head_q + static_cast<uint64_t>(qi) * kApD)[lane] =
+        reinterpret_cast<float4 *>(att_out_row(p, bh, qi))[lane] =
             make_float4(__fmul_rn(half_f32x2(acc[q][0], 0), inv),
                         __fmul_rn(half_f32x2(acc[q][0], 1), inv),
                         __fmul_rn(half_f32x2(acc[q][1], 0), inv),
@@ -1740,7 +1750,7 @@ cudaError_t add(const LaunchCtx &ctx, const float *A, const float *B, float *Y, 
 cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, const float *V,
                       const float *mask, float *O, uint32_t batch, uint32_t heads,
                       uint32_t seq_q, uint32_t seq_k, uint32_t head_dim, uint32_t causal,
-                      float scale) {
+                      float scale, bool o_token_major) {
     if (head_dim > kAttMaxD || head_dim == 0) return cudaErrorInvalidValue;
     const size_t smem =
         sizeof(float) * (kAttBQ * att_q_stride(head_dim) + kAttBK * head_dim + kAttBQ * kAttBK);
@@ -1772,6 +1782,7 @@ cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, cons
     ap.D = head_dim;
     ap.causal = causal;
     ap.scale = scale;
+    ap.o_tokens = o_token_major ? 1u : 0u;
     ap.err = ctx.err;
     ap.wait_ns = ctx.wait_limit_ns;
     const char *attn_env = std::getenv("VNPU_B200_ATTN");   // general | decode | cluster

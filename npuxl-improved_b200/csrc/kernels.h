@@ -179,10 +179,12 @@ cudaError_t swiglu(const LaunchCtx &ctx, const float *gate, const float *up, flo
                    uint64_t count, float alpha);
 cudaError_t add(const LaunchCtx &ctx, const float *A, const float *B, float *Y, uint64_t count,
                 float alpha, float beta);
+// o_token_major: O as [batch][seq_q][heads][head_dim] instead of the
+// reference's [batch][heads][seq_q][head_dim] (VNPU_CMD_FLAG_ATTN_TOKEN_MAJOR).
 cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, const float *V,
                       const float *mask, float *O, uint32_t batch, uint32_t heads,
                       uint32_t seq_q, uint32_t seq_k, uint32_t head_dim, uint32_t causal,
-                      float scale);
+                      float scale, bool o_token_major = false);
 
 // ---- device-wait self test -------------------------------------------------------
 cudaError_t wait_timeout_probe(const LaunchCtx &ctx, const uint32_t *flag, uint64_t limit_ns);

@@ -871,7 +871,7 @@ void exec_attention(vnpu_stream_t *s, const vnpu_command_t &cmd, const LaunchCtx
     const float *V = st.in(a.V, kn * sizeof(float));
     const float *M = st.in(a.mask, mn * sizeof(float));
     cuda_check(attention(ctx, Q, K, V, M, O, a.batch, a.heads, a.seq_q, a.seq_k, a.head_dim,
-                         a.causal, scale),
+                         a.causal, scale, (cmd.flags & VNPU_CMD_FLAG_ATTN_TOKEN_MAJOR) != 0u),
                "attention launch");
     st.finish();
     acc.bytes_read = (qn + 2 * kn + mn) * sizeof(float);

@@ -343,7 +343,10 @@ class B200Block:
                                      positions.data_ptr() if positions is not None else None,
                                      1, H, T, T, hd, pos0, 0, cfg.theta, 1.0)
                 self._submit([_cmd(vnpu.OP_ROPE_F32, "rope", rope)])
-            O = self._buf(f"O{T}", (1, H, T, hd))
+            # fused prefill: the attention writes token-major rows, the O
+            # projection's input, so no transpose copy follows
+            tok_major = self.fused and T > 1
+            O = self._buf(f"O{T}", (T, d) if tok_major else (1, H, T, hd))
             if T > 1:
                 if not self.fused:
                     self.kc[:, :, pos0:pos0 + T].copy_(K)
@@ -360,8 +363,11 @@ class B200Block:
                 att = vnpu.AttentionArgs(Q.data_ptr(), self.kc.data_ptr(), self.vc.data_ptr(),
                                          self.mask.data_ptr(), O.data_ptr(), None, 0, 1, H, 1,
                                          cfg.cap, hd, 0, 0.0, 0)
-            self._submit([_cmd(vnpu.OP_ATTENTION_F32, "attention", att)])
-            attn = O[0].transpose(0, 1).reshape(T, d).contiguous()
+            acmd = _cmd(vnpu.OP_ATTENTION_F32, "attention", att)
+            if tok_major:
+                acmd.flags = vnpu.CMD_FLAG_ATTN_TOKEN_MAJOR
+            self._submit([acmd])
+            attn = O if tok_major else O[0].transpose(0, 1).reshape(T, d).contiguous()
             if self.fused:
                 # the residual adds ride on the O and down projections
                 # (VNPU_B200_OP_MATMUL_I8_RESIDUAL)

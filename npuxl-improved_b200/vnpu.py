@@ -50,6 +50,7 @@ FEATURE_GPU_FUTURE = 1 << 31
 # B200 extensions (include/vnpu_b200.h)
 CMD_FLAG_EPI_STREAM = 1 << 8
 CMD_FLAG_EPI_SCALAR = 1 << 9
+CMD_FLAG_ATTN_TOKEN_MAJOR = 1 << 10   # ATTENTION_F32 writes O as [batch][seq_q][heads][D]
 # oracle form index (oracle/oracle.h) -> command flags of the B200 library
 FORM_FLAGS = {0: 0, 1: CMD_FLAG_EPI_SCALAR, 2: CMD_FLAG_EPI_STREAM}
 
@@ -530,10 +531,20 @@ class Device:
         self.lib.check(self.lib.add_f32(self.stream, C.byref(a)), "add_f32")
 
     def attention(self, Q, K, V, mask, O, batch, heads, seq_q, seq_k, head_dim, causal=1,
-                  scale=0.0) -> None:
+                  scale=0.0, flags=0) -> None:
         a = AttentionArgs(ptr(Q), ptr(K), ptr(V), ptr(mask), ptr(O), None, 0, batch, heads, seq_q,
                           seq_k, head_dim, causal, scale, 0)
-        self.lib.check(self.lib.attention_f32(self.stream, C.byref(a)), "attention_f32")
+        if flags:
+            cmd = Command()
+            cmd.opcode = OP_ATTENTION_F32
+            cmd.flags = flags
+            cmd.args.attention = a
+            rc = self.lib.stream_submit(self.stream, C.byref(cmd), 1, None)
+            if rc == OK:
+                rc = self.lib.stream_sync(self.stream)
+            self.lib.check(rc, "attention_f32")
+        else:
+            self.lib.check(self.lib.attention_f32(self.stream, C.byref(a)), "attention_f32")
 
     def submit(self, cmds, event=None) -> int:
         arr = (Command * len(cmds))(*cmds)

@@ -429,6 +429,29 @@ def test_prefill_attention_zero_probabilities(gpu, oracle, sq, sk, causal, maske
     assert bits_equal(O, ref), f"max ulp {ulp_diff(O, ref)}"
 
 
+@pytest.mark.parametrize("B,H,sq,sk,D,causal,masked", [
+    (1, 4, 512, 512, 128, 1, False),    # 64-query prefill kernel
+    (2, 3, 100, 300, 128, 1, True),     # batch 2, ragged query block, causal offset
+    (1, 4, 33, 33, 64, 0, False),       # general kernel (head_dim 64)
+    (2, 2, 20, 45, 40, 1, True),        # general kernel, head_dim 40
+    (1, 32, 1, 640, 128, 0, True),      # decode: both layouts are the same addresses
+])
+def test_attention_token_major_output(gpu, B, H, sq, sk, D, causal, masked):
+    """VNPU_CMD_FLAG_ATTN_TOKEN_MAJOR writes the same bits as the reference
+    layout, at [batch][seq_q][heads][D] instead of [batch][heads][seq_q][D]."""
+    rng = np.random.default_rng(B * 100 + sq + sk + D)
+    Q = rng.normal(0, 1, (B, H, sq, D)).astype(np.float32)
+    K = rng.normal(0, 1, (B, H, sk, D)).astype(np.float32)
+    V = rng.normal(0, 1, (B, H, sk, D)).astype(np.float32)
+    M = rng.normal(0, 1, (B, H, sq, sk)).astype(np.float32) if masked else None
+    O = np.full((B, H, sq, D), np.nan, np.float32)
+    gpu.attention(Q, K, V, M, O, B, H, sq, sk, D, causal, 0.0)
+    Ot = np.full((B, sq, H, D), np.nan, np.float32)
+    gpu.attention(Q, K, V, M, Ot, B, H, sq, sk, D, causal, 0.0,
+                  flags=vnpu.CMD_FLAG_ATTN_TOKEN_MAJOR)
+    assert bits_equal(Ot, np.ascontiguousarray(O.transpose(0, 2, 1, 3)))
+
+
 @pytest.mark.parametrize("sq,sk", [(512, 512), (1, 513), (1, 640), (16, 16), (17, 100)])
 def test_attention_block_shapes(gpu, oracle, sq, sk):
     H, D = 32 if sq <= 16 else 8, 128
