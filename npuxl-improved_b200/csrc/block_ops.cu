@@ -170,10 +170,13 @@ __device__ __forceinline__ void fq_quantize_slice(const float *ys, uint32_t c0, 
     const uint32_t tid = threadIdx.x;
     const uint32_t C = cluster_nctarank(), rank = cluster_ctarank();
     m = block_max(m, red);
-    if (tid < C) st_shared_cluster_f32(mapa_shared(smem_addr(maxes + rank), tid), m);
-    cluster_sync_all();
-    float rowmax = 0.0f;
-    for (uint32_t r = 0; r < C; ++r) rowmax = fmaxf(rowmax, maxes[r]);
+    float rowmax = m;   // >= 0, never NaN (fmaxf from 0)
+    if (C > 1) {        // a row over several CTAs: exchange their maxima
+        if (tid < C) st_shared_cluster_f32(mapa_shared(smem_addr(maxes + rank), tid), m);
+        cluster_sync_all();
+        rowmax = 0.0f;
+        for (uint32_t r = 0; r < C; ++r) rowmax = fmaxf(rowmax, maxes[r]);
+    }
     const float scale = scale_from_absmax(rowmax);
     const float inv = __fdiv_rn(1.0f, scale);
     if (tid == 0 && rank == 0) *scale_out = scale;
