@@ -527,6 +527,51 @@ def test_splitk_pair_kernel_agrees(gpu, oracle, monkeypatch, M, K, N, epi, form,
     assert bits_equal(outs[0][rows], oracle.matmul_i8(A[rows], B, sa[rows], sb, bias, epi, form))
 
 
+def test_splitk_in_cuda_graph(gpu, oracle):
+    """A split-K GEMM (stream-ordered workspace allocated and freed inside the
+    command) recorded as a CUDA graph and replayed twice gives the eager bits,
+    with and without the residual folded into its finish kernel."""
+    import torch
+    M, K, N = 512, 4096, 4096
+    rng = np.random.default_rng(4242)
+    A, sa = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
+    B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
+    w = gpu.pack(B, sb, K, N)
+    try:
+        Ad, sad = torch.from_numpy(A).cuda(), torch.from_numpy(sa).cuda()
+        R = torch.from_numpy(rng.normal(0, 1, (M, N)).astype(np.float32)).cuda()
+        C1 = torch.full((M, N), float("nan"), device="cuda")
+        C2 = torch.full((M, N), float("nan"), device="cuda")
+        mm = vnpu.Command()
+        mm.opcode = vnpu.OP_MATMUL_I8
+        mm.args.matmul_i8 = vnpu.MatmulI8Args(Ad.data_ptr(), w, sad.data_ptr(), None,
+                                              C1.data_ptr(), M, K, N, 0, 0, 0, vnpu.UNIT_AUTO)
+        res = vnpu.b200_command(vnpu.OP_B200_MATMUL_I8_RESIDUAL, vnpu.MatmulI8ResidualArgs(
+            Ad.data_ptr(), w, sad.data_ptr(), None, R.data_ptr(), C2.data_ptr(), M, K, N, 0, 0, 0,
+            0, 0))
+        torch.cuda.synchronize()
+        assert gpu.submit([mm, res]) == vnpu.OK and gpu.sync() == vnpu.OK
+        assert gpu.lib.b200_last_matmul_kernel().decode() == "gemm_i8_tcgen05_pair_kernel+splitk"
+        eager1, eager2 = C1.cpu().numpy(), C2.cpu().numpy()
+        rows = np.arange(0, M, 61)
+        assert bits_equal(eager1[rows], oracle.matmul_i8(A[rows], B, sa[rows], sb, None, 0, 0))
+        assert bits_equal(eager2, oracle.add(R.cpu().numpy(), eager1, 1.0, 1.0, 0))
+        g = gpu.capture([mm, res])
+        try:
+            for _ in range(2):
+                C1.fill_(float("nan"))
+                C2.fill_(float("nan"))
+                torch.cuda.synchronize()
+                gpu.replay(g)
+                assert gpu.sync() == vnpu.OK
+                assert bits_equal(C1.cpu().numpy(), eager1)
+                assert bits_equal(C2.cpu().numpy(), eager2)
+        finally:
+            gpu.lib.b200_graph_destroy(g)
+    finally:
+        gpu.unpack(w)
+
+
 @pytest.mark.parametrize("M,K,N,epi,form,pad", [
     (129, 256, 256, 3, 0, 0),      # one partial 256x512 tile
     (300, 1008, 700, 2, 0, 0),     # ragged K (8 k-blocks), ragged N
