@@ -141,7 +141,9 @@ def reference_sample(rows: int, steps: int, warmup: int, threads: int):
     Bf = rng.normal(0, 0.02, (K_TOTAL, n)).astype(np.float32)
     A = rng.uniform(-1, 1, (rows, K_TOTAL)).astype(np.float32)
     if lib is None:
-        orc = vnpu.Oracle(ORACLE_LIB)
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        from vnpu_oracle import Oracle
+        orc = Oracle(ORACLE_LIB)
         B8, sb = orc.quantize(Bf, 1)
         del Bf
         times = []

@@ -143,9 +143,12 @@ __device__ __forceinline__ float ref_dequant_t(int32_t acc, float sa, float sb, 
     return ref_activation_t<ACT, FUSED>(out);
 }
 
-// Launch-constant epilogue variant: act | bias << 2 | fused << 4.
+// Launch-constant epilogue variant: act | bias << 2 | fused << 4, or
+// kVariantMixed when the form varies by element (FormMap, form_at).
+constexpr uint32_t kVariantMixed = 0x40u;
 __host__ __device__ constexpr uint32_t epi_variant(uint32_t epilogue, bool has_bias,
                                                    uint32_t form) {
+    if (form == kFormMixed) return kVariantMixed;
     const uint32_t act = epilogue == 1 ? 1u : epilogue == 2 ? 2u : (epilogue == 3 || epilogue == 4) ? 3u : 0u;
     const uint32_t bias = !has_bias ? 0u : (form == kFormBlock ? 1u : 2u);
     const uint32_t fused = (act >= 2 && form == kFormScalar) ? 0u : 1u;
@@ -165,6 +168,24 @@ __device__ __forceinline__ float ref_dequant(int32_t acc, float sa, float sb, bo
         out = __fadd_rn(__fmul_rn(t, sb), bias);
     }
     return ref_activation(out, epilogue, form != kFormScalar);
+}
+
+// The form of element (m, n) of a launch (n the launch's own column; fm.col_base
+// places it in the whole output whose reference tile grid fm describes).  m is
+// below fm.M for every element that is stored.
+__device__ __forceinline__ uint32_t form_at(const FormMap &fm, uint32_t m, uint32_t n) {
+    if (fm.form != kFormMixed) return fm.form;
+    const uint32_t m0 = m / fm.tm * fm.tm;
+    const uint32_t left = fm.M - m0;                       // rows from the tile start on
+    const uint32_t rows = left < fm.tm ? left : fm.tm;
+    const uint32_t rc = (left <= fm.tm ? 2u : 0u) |
+                        (((rows & 1u) != 0u && m - m0 == rows - 1u) ? 1u : 0u);
+    const uint32_t c = n + fm.col_base;
+    const uint32_t n0 = c / fm.tn * fm.tn;
+    const uint32_t cleft = fm.N - n0;
+    const uint32_t cols = cleft < fm.tn ? cleft : fm.tn;
+    const uint32_t cc = (cleft <= fm.tn ? 2u : 0u) | (c - n0 >= (cols & ~31u) ? 1u : 0u);
+    return (fm.table >> (2u * (rc * 4u + cc))) & 3u;
 }
 
 // ---------------------------------------------------------------------------

@@ -70,8 +70,9 @@ struct TcParams {
     uint32_t M = 0, N = 0, K = 0;
     uint32_t tiles_m = 0, tiles_n = 0, num_kb = 0;
     uint32_t group_m = 1;  // raster band height in m-tiles
-    uint32_t epilogue = 0, form = 0;
-    uint32_t variant = 0;  // epi_variant(epilogue, bias != NULL, form)
+    uint32_t epilogue = 0;
+    FormMap fmap;          // rounding form of each element
+    uint32_t variant = 0;  // epi_variant(epilogue, bias != NULL, fmap.form)
     uint32_t tma_store = 0;  // 1: C written by TMA from shared memory
     uint32_t *err = nullptr;
     uint64_t limit_ns = 2000000000ull;
@@ -153,30 +154,55 @@ __device__ __forceinline__ void dequant32_shfl_inplace(uint32_t (&r)[32], float 
     }
 }
 
-__device__ __forceinline__ void dequant32_shfl_any(uint32_t variant, const uint32_t (&r)[32],
-                                                   float (&v)[32], float sa, float s_lane,
-                                                   float b_lane) {
-    switch (variant) {
+// kVariantMixed: each element's form from the form map (row m, columns n0..n0+31).
+__device__ __forceinline__ void dequant32_shfl_mixed(const TcParams &p, uint32_t m, uint32_t n0,
+                                                     const uint32_t (&r)[32], float (&v)[32],
+                                                     float sa, float s_lane, float b_lane) {
+    const bool has_bias = p.bias != nullptr;
+#pragma unroll 4
+    for (uint32_t j = 0; j < 32u; ++j) {
+        const float sb = __shfl_sync(0xffffffffu, s_lane, j);
+        const float bb = __shfl_sync(0xffffffffu, b_lane, j);
+        v[j] = ref_dequant(static_cast<int32_t>(r[j]), sa, sb, has_bias, bb, p.epilogue,
+                           form_at(p.fmap, m, n0 + j));
+    }
+}
+
+__device__ __forceinline__ void dequant32_shfl_any(const TcParams &p, uint32_t m, uint32_t n0,
+                                                   const uint32_t (&r)[32], float (&v)[32],
+                                                   float sa, float s_lane, float b_lane) {
+    switch (p.variant) {
 #define VNPU_B200_CASE(V)                                      \
     case V:                                                    \
         dequant32_shfl<V>(r, v, sa, s_lane, b_lane);           \
         break;
         VNPU_B200_EPI_VARIANTS(VNPU_B200_CASE)
 #undef VNPU_B200_CASE
+    case kVariantMixed:
+        dequant32_shfl_mixed(p, m, n0, r, v, sa, s_lane, b_lane);
+        break;
     default:
         break;
     }
 }
 
-__device__ __forceinline__ void dequant32_shfl_inplace_any(uint32_t variant, uint32_t (&r)[32],
+__device__ __forceinline__ void dequant32_shfl_inplace_any(const TcParams &p, uint32_t m,
+                                                           uint32_t n0, uint32_t (&r)[32],
                                                            float sa, float s_lane, float b_lane) {
-    switch (variant) {
+    switch (p.variant) {
 #define VNPU_B200_CASE(V)                                      \
     case V:                                                    \
         dequant32_shfl_inplace<V>(r, sa, s_lane, b_lane);      \
         break;
         VNPU_B200_EPI_VARIANTS(VNPU_B200_CASE)
 #undef VNPU_B200_CASE
+    case kVariantMixed: {
+        float v[32];
+        dequant32_shfl_mixed(p, m, n0, r, v, sa, s_lane, b_lane);
+#pragma unroll
+        for (uint32_t j = 0; j < 32u; ++j) r[j] = __float_as_uint(v[j]);
+        break;
+    }
     default:
         break;
     }
@@ -348,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t n0 = nb * kBN + c * 32u;
                 if (n0 >= p.N) continue;   // warp-uniform
                 float v[32];
-                dequant32_shfl_any(p.variant, r, v, sa, sreg[c], breg[c]);
+                dequant32_shfl_any(p, m, n0, r, v, sa, sreg[c], breg[c]);
                 if (row_ok) store_row32(v, crow, n0, p.N, vec_ok);
             }
             tc_fence_before();
@@ -599,7 +625,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
                 const uint32_t col = col_base + c * 32u;
                 const uint32_t n0 = nb * kPTileN + col;
                 if (n0 >= p.N || m_first >= p.M) continue;  // warp-uniform
-                if (p.splits == 1) dequant32_shfl_inplace_any(p.variant, rr[c], sa, sreg[c], breg[c]);
+                if (p.splits == 1) dequant32_shfl_inplace_any(p, m, n0, rr[c], sa, sreg[c], breg[c]);
                 const float(&v)[32] = reinterpret_cast<const float(&)[32]>(rr[c]);
                 if (p.ndst) {
                     // Scatter: the 32x32 chunk is transposed through the staging
@@ -681,7 +707,7 @@ __global__ void __launch_bounds__(256) splitk_finish_kernel(
     const int4 *__restrict__ ws, uint32_t splits, uint32_t m_pad, uint32_t M, uint32_t N,
     const float *__restrict__ scale_a, const float *__restrict__ scale_b,
     const float *__restrict__ bias, float *__restrict__ C, uint32_t ldc, uint32_t epilogue,
-    uint32_t form, const float *__restrict__ R, uint32_t ldr) {
+    const FormMap fm, const float *__restrict__ R, uint32_t ldr) {
     pdl_enter();
     const uint32_t n4 = N / 4;
     const uint32_t total = M * n4;
@@ -708,10 +734,11 @@ __global__ void __launch_bounds__(256) splitk_finish_kernel(
             bv.z = __ldg(bias + n + 2);
             bv.w = __ldg(bias + n + 3);
         }
-        float4 o = make_float4(ref_dequant(a.x, sa, sb.x, has_bias, bv.x, epilogue, form),
-                               ref_dequant(a.y, sa, sb.y, has_bias, bv.y, epilogue, form),
-                               ref_dequant(a.z, sa, sb.z, has_bias, bv.z, epilogue, form),
-                               ref_dequant(a.w, sa, sb.w, has_bias, bv.w, epilogue, form));
+        float4 o = make_float4(
+            ref_dequant(a.x, sa, sb.x, has_bias, bv.x, epilogue, form_at(fm, m, n)),
+            ref_dequant(a.y, sa, sb.y, has_bias, bv.y, epilogue, form_at(fm, m, n + 1u)),
+            ref_dequant(a.z, sa, sb.z, has_bias, bv.z, epilogue, form_at(fm, m, n + 2u)),
+            ref_dequant(a.w, sa, sb.w, has_bias, bv.w, epilogue, form_at(fm, m, n + 3u)));
         if (R) {
             const float *r = R + static_cast<uint64_t>(m) * ldr + n;
             o.x = __fadd_rn(__ldg(r), o.x);
@@ -976,7 +1003,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                     const uint32_t col = h * 256u + col_base + c * 32u;
                     const uint32_t n0 = nb * kWTileN + col;
                     if (n0 >= p.N || m_first >= p.M) continue;  // warp-uniform
-                    dequant32_shfl_inplace_any(p.variant, r[c], sa, sreg[h * 4u + c], breg[h * 4u + c]);
+                    dequant32_shfl_inplace_any(p, m, n0, r[c], sa, sreg[h * 4u + c], breg[h * 4u + c]);
                     const float(&v)[32] = reinterpret_cast<const float(&)[32]>(r[c]);
                     if (p.tma_store) {
                         if (lane == 0) bulk_wait_read0();  // previous store has read the buffer
@@ -1042,7 +1069,8 @@ struct SkParams {
     uint32_t ldc;
     uint32_t M, N, K;
     uint32_t num_kb, kb_per_rank;
-    uint32_t epilogue, form;
+    uint32_t epilogue;
+    FormMap fmap;
     uint32_t *err;
     uint64_t limit_ns;
 };
@@ -1188,7 +1216,7 @@ __global__ void __launch_bounds__(kSkThreads, kMinBlocks)
                 if (m < p.M) {
                     const float sa = p.scale_a ? __ldg(p.scale_a + m) : 1.0f;
                     p.C[static_cast<uint64_t>(m) * p.ldc + n] =
-                        ref_dequant(acc[m], sa, sb, has_bias, bv, p.epilogue, p.form);
+                        ref_dequant(acc[m], sa, sb, has_bias, bv, p.epilogue, form_at(p.fmap, m, n));
                 }
             }
         }
@@ -1215,7 +1243,8 @@ struct GvParams {
     float *C;
     uint32_t ldc;
     uint32_t M, K, N;
-    uint32_t epilogue, form;
+    uint32_t epilogue;
+    FormMap fmap;
 };
 
 // 16 bytes of row m of A starting at k (zeros past K; B is zero there too).
@@ -1360,7 +1389,8 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const GvParams p, con
 #pragma unroll
         for (int c = 0; c < 2; ++c)
             v[c] = ref_dequant(acc[c][0], sa, __ldg(p.scale_b + ncol[c]), has_bias,
-                               has_bias ? __ldg(p.bias + ncol[c]) : 0.0f, p.epilogue, p.form);
+                               has_bias ? __ldg(p.bias + ncol[c]) : 0.0f, p.epilogue,
+                               form_at(p.fmap, 0u, ncol[c]));
         const int32_t pos = x.position ? *x.position : static_cast<int32_t>(x.pos0);
         if (q_sec < 2) {
             const float angle = __fmul_rn(__fmul_rn(static_cast<float>(pos), x.scaling), x.inv[q_j]);
@@ -1403,7 +1433,8 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const GvParams p, con
             if (static_cast<uint32_t>(m) == lane && static_cast<uint32_t>(m) < p.M) {
                 const float sa = p.scale_a ? __ldg(p.scale_a + m) : 1.0f;
                 float out = ref_dequant(acc[c][m], sa, __ldg(p.scale_b + n), has_bias,
-                                        has_bias ? __ldg(p.bias + n) : 0.0f, p.epilogue, p.form);
+                                        has_bias ? __ldg(p.bias + n) : 0.0f, p.epilogue,
+                                        form_at(p.fmap, static_cast<uint32_t>(m), n));
                 if constexpr (std::is_same<Extra, GvResidual>::value)
                     out = __fadd_rn(x.R[static_cast<uint64_t>(m) * x.ldr + n], out);
                 p.C[static_cast<uint64_t>(m) * p.ldc + n] = out;
@@ -1470,7 +1501,7 @@ __global__ void __launch_bounds__(256) gemm_i8_simt_kernel(const GvParams p) {
             if (n >= p.N) continue;
             p.C[static_cast<uint64_t>(m) * p.ldc + n] =
                 ref_dequant(acc[i][j], sa, p.scale_b[n], has_bias, has_bias ? p.bias[n] : 0.0f,
-                            p.epilogue, p.form);
+                            p.epilogue, form_at(p.fmap, m, n));
         }
     }
 }
@@ -1490,7 +1521,7 @@ GvParams gv_params(const MatmulI8 &p) {
     g.K = p.K;
     g.N = p.N;
     g.epilogue = p.epilogue;
-    g.form = p.form;
+    g.fmap = p.fmap;
     return g;
 }
 
@@ -1711,8 +1742,8 @@ cudaError_t matmul_i8_scatter(const LaunchCtx &ctx, const MatmulI8 &p) {
     tp.num_kb = (p.K + kBK - 1) / kBK;
     tp.group_m = raster_group(tp.tiles_m, kPTileM, p.K);
     tp.epilogue = p.epilogue;
-    tp.form = p.form;
-    tp.variant = epi_variant(p.epilogue, p.bias != nullptr, p.form);
+    tp.fmap = p.fmap;
+    tp.variant = epi_variant(p.epilogue, p.bias != nullptr, p.fmap.form);
     tp.tma_store = 0;
     tp.err = ctx.err;
     tp.limit_ns = ctx.wait_limit_ns;
@@ -1763,7 +1794,7 @@ cudaError_t matmul_i8_pair_splitk(const LaunchCtx &ctx, const MatmulI8 &p, TcPar
                                                    static_cast<uint32_t>(ctx.num_sms) * 8u);
         e = launch_pdl(ctx.stream, splitk_finish_kernel, dim3(blocks), dim3(256), 0,
                        reinterpret_cast<const int4 *>(ws), splits, tp.m_pad, p.M, p.N, p.scale_a,
-                       p.scale_b, p.bias, p.C, p.ldc, p.epilogue, p.form, p.R, p.ldr);
+                       p.scale_b, p.bias, p.C, p.ldc, p.epilogue, p.fmap, p.R, p.ldr);
         count_launch(ctx);
     }
     cudaFreeAsync(ws, ctx.stream);
@@ -1819,8 +1850,8 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         // (exact) and applies the epilogue.
         tp.group_m = raster_group(tp.tiles_m, kPTileM, p.K);
         tp.epilogue = p.epilogue;
-        tp.form = p.form;
-        tp.variant = epi_variant(p.epilogue, p.bias != nullptr, p.form);
+        tp.fmap = p.fmap;
+        tp.variant = epi_variant(p.epilogue, p.bias != nullptr, p.fmap.form);
         tp.err = ctx.err;
         tp.limit_ns = ctx.wait_limit_ns;
         uint32_t splits = 1;
@@ -1882,8 +1913,8 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
     tp.num_kb = (p.K + kBK - 1) / kBK;
     tp.group_m = raster_group(tp.tiles_m, kBM, p.K);
     tp.epilogue = p.epilogue;
-    tp.form = p.form;
-    tp.variant = epi_variant(p.epilogue, p.bias != nullptr, p.form);
+    tp.fmap = p.fmap;
+    tp.variant = epi_variant(p.epilogue, p.bias != nullptr, p.fmap.form);
     tp.tma_store = 0;
     tp.err = ctx.err;
     tp.limit_ns = ctx.wait_limit_ns;
@@ -1961,7 +1992,7 @@ cudaError_t gemv_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
     sp.K = p.K;
     sp.num_kb = (p.K + kBK - 1) / kBK;
     sp.epilogue = p.epilogue;
-    sp.form = p.form;
+    sp.fmap = p.fmap;
     sp.err = ctx.err;
     sp.limit_ns = ctx.wait_limit_ns;
     // Five 17 KiB stages at two CTAs per SM: measured best of 4/5/8/12 on B200

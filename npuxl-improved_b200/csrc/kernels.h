@@ -20,8 +20,27 @@ enum DeviceError : uint32_t {
     kErrTmemAlloc = 1u << 2,     // tensor memory allocation returned nonsense
 };
 
-// Dequant epilogue forms (vnpu_b200.h: block / stream / scalar).
-enum EpiForm : uint32_t { kFormBlock = 0, kFormStream = 1, kFormScalar = 2 };
+// Dequant epilogue forms (vnpu_b200.h: block / stream / scalar); kFormMixed
+// marks a FormMap whose form varies from element to element.
+enum EpiForm : uint32_t { kFormBlock = 0, kFormStream = 1, kFormScalar = 2, kFormMixed = 3 };
+
+// The rounding form of each element of a MATMUL_I8 output.  The reference
+// device rounds an element's dequant epilogue in the form of the CPU kernel
+// that owns its tile (src/kernels/kernels.cpp:922-978), and its tile grid
+// (src/core/scheduler.cpp:75-207) depends on M, N, its thread count, its tile
+// defaults and VNPU_PACK.  runtime.cpp builds the map from the same rules:
+// either one form for the whole output (form != kFormMixed, the usual case),
+// or a 16-entry table of 2-bit forms indexed by the element's row class
+// (last row tile?, the odd row of its tile?) and column class (last column
+// tile?, in the tile's column tail past its last whole 32 columns?).
+struct FormMap {
+    uint32_t form = kFormBlock;   // every element's form, or kFormMixed
+    uint32_t tm = 1, tn = 1;      // the reference's tile rows / columns
+    uint32_t M = 0, N = 0;        // the whole output those tiles cover
+    uint32_t col_base = 0;        // whole-output column of the launch's column 0
+    uint32_t table = 0;           // form of class (row * 4 + column) at bits 2i..2i+1
+    uint32_t reserved = 0;
+};
 
 struct LaunchCtx {
     cudaStream_t stream = nullptr;
@@ -60,7 +79,7 @@ struct MatmulI8 {
     uint32_t ldc = 0;
     uint32_t M = 0, K = 0, N = 0;
     uint32_t epilogue = 0;
-    uint32_t form = 0;              // EpiForm
+    FormMap fmap;                   // rounding form of each output element
     const CUtensorMap *tmap_b = nullptr;     // TMA map of Bt (box 128 x 256, SW128)
     const CUtensorMap *tmap_b128 = nullptr;  // same, box 128 x 128 (CTA-pair kernel)
     // Scatter mode (MATMUL_I8_SCATTER): the shard is written into ndst full

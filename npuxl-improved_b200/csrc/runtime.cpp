@@ -28,6 +28,8 @@
 #include <thread>
 #include <unordered_map>
 
+#include <unistd.h>
+
 #include "kernels.h"
 
 using vnpu_b200::LaunchCtx;
@@ -259,19 +261,26 @@ bool env_is(const char *name, const char *value) {
     return e && !std::strcmp(e, value);
 }
 
-uint32_t epi_form_from_env() {
+// VNPU_B200_EPILOGUE=block|stream|scalar rounds every MATMUL_I8 element in
+// that one form; unset (or "reference"), each element takes the form the
+// reference device gives it (i8_form_map).
+bool epi_form_from_env(uint32_t &form) {
     const char *e = std::getenv("VNPU_B200_EPILOGUE");
-    if (!e) return kFormBlock;
-    if (!std::strcmp(e, "stream")) return kFormStream;
-    if (!std::strcmp(e, "scalar")) return kFormScalar;
-    return kFormBlock;
+    if (!e) return false;
+    if (!std::strcmp(e, "block")) form = kFormBlock;
+    else if (!std::strcmp(e, "stream")) form = kFormStream;
+    else if (!std::strcmp(e, "scalar")) form = kFormScalar;
+    else return false;
+    return true;
 }
 
-uint32_t epi_form_for(const vnpu_device_t *d, uint32_t flags) {
-    if (flags & VNPU_CMD_FLAG_EPI_SCALAR) return kFormScalar;
-    if (flags & VNPU_CMD_FLAG_EPI_STREAM) return kFormStream;
-    return d->epi_form;
-}
+// Bytes of per-worker scratch the reference kernels stage into
+// (VNPU_LOCAL_STORE_BYTES, include/vnpu.h:51).
+constexpr uint64_t kRefScratchBytes = 256u * 1024u;
+
+FormMap i8_form_map(const vnpu_device_t *d, uint32_t unit, uint32_t flags, uint32_t M, uint32_t K,
+                    uint32_t N, bool has_bias, uint32_t epilogue, uint32_t n_full = 0,
+                    uint32_t col_base = 0);
 
 struct Accounting {
     uint64_t bytes_read = 0, bytes_written = 0, flops = 0, tiles = 0, dma = 0;
@@ -320,7 +329,8 @@ void exec_matmul_i8(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags,
     p.K = in.K;
     p.N = in.N;
     p.epilogue = in.epilogue;
-    p.form = epi_form_for(s->device, flags);
+    p.fmap = i8_form_map(s->device, in.unit, flags, in.M, in.K, in.N, in.bias != nullptr,
+                         in.epilogue);
     p.tmap_b = w->tmap_ok ? &w->tmap : nullptr;
     p.tmap_b128 = w->tmap128_ok ? &w->tmap128 : nullptr;
     cuda_check(matmul_i8(ctx, p), "matmul_i8 launch");
@@ -346,16 +356,34 @@ uint32_t f32_unit(const vnpu_matmul_f32_args_t &a, uint32_t flags) {
 
 uint32_t ceil_div(uint32_t a, uint32_t b) { return (a + b - 1) / b; }
 
-// F32 tile geometry, src/core/scheduler.cpp:95-207 (int8 = false).
-void f32_geometry(const vnpu_device_t *d, uint32_t unit, uint32_t M, uint32_t N, uint32_t &tm,
-                  uint32_t &tn) {
+// Widest int8 decode column tile, src/core/scheduler.cpp:75-93: half of the
+// host L2 shared by `rows` int32 staging rows, at most what a worker's 256 KiB
+// scratch stages, whole 32-column groups, at least 256.
+uint32_t decode_tile_cap(uint64_t l2, uint32_t rows) {
+    if (!l2) l2 = 512u * 1024u;
+    uint64_t cols = std::min<uint64_t>(l2 / (8ull * rows), kRefScratchBytes / (4ull * rows));
+    cols &= ~uint64_t{31};
+    return static_cast<uint32_t>(std::min<uint64_t>(std::max<uint64_t>(cols, 256), 0x7fffffffu));
+}
+
+// The reference's tile geometry, src/core/scheduler.cpp:95-207.
+void ref_tile_geometry(const vnpu_device_t *d, uint32_t unit, uint32_t M, uint32_t N, bool int8,
+                       uint32_t &tm, uint32_t &tn) {
     tm = std::max<uint32_t>(1, d->f32_tile_m.load());
     tn = std::max<uint32_t>(1, d->f32_tile_n.load());
     const uint32_t units = std::max<uint32_t>(1, d->f32_threads);
     const bool voodoo = unit == VNPU_UNIT_VOODOO || unit == VNPU_UNIT_AUTO;
-    if (M <= 8 && voodoo) {  // decode rows: the F32 kernels keep a 32..64 column tile
+    if (M <= 8 && voodoo) {
         tm = M;
-        tn = std::min<uint32_t>(std::max<uint32_t>(32, tn), 64);
+        if (int8 && M <= 3 && N / units >= 1024u) {
+            // one contiguous column slice per worker, bounded by the staging cap
+            uint32_t tiles = std::min<uint32_t>(units, std::max<uint32_t>(1, N / 256u));
+            const uint32_t cap = decode_tile_cap(d->host_l2, M);
+            if (ceil_div(N, tiles) > cap) tiles = ceil_div(ceil_div(N, cap), units) * units;
+            tn = std::min<uint32_t>(N, std::max<uint32_t>(1, (ceil_div(N, tiles) + 31u) & ~31u));
+            return;
+        }
+        tn = std::min<uint32_t>(std::max<uint32_t>(32, tn), 64);  // 32..64 column tiles
         tn = std::min(tn, N);
         return;
     }
@@ -379,6 +407,109 @@ void f32_geometry(const vnpu_device_t *d, uint32_t unit, uint32_t M, uint32_t N,
     }
 }
 
+// choose_unit for MATMUL_I8 (src/core/scheduler.cpp:43-62, :378-382): the
+// GPU unit is this device and follows the default unit.
+uint32_t i8_unit(uint32_t unit, uint32_t flags) {
+    if (flags & VNPU_CMD_FLAG_CELL_DMA) return VNPU_UNIT_CELL;
+    if (flags & VNPU_CMD_FLAG_VOODOO_FIFO) return VNPU_UNIT_VOODOO;
+    if (unit != VNPU_UNIT_AUTO && unit != VNPU_UNIT_GPU) return unit;
+    if (flags & VNPU_CMD_FLAG_WILDCAT_CULL) return VNPU_UNIT_WILDCAT;
+    return VNPU_UNIT_VOODOO;
+}
+
+// The form in which the reference's AVX2 kernels round the dequant epilogue
+// of an element of a rows x cols tile (gemm_i8_dispatch_tile,
+// src/kernels/kernels.cpp:922-978).  `single`: the element's row is the odd
+// last row of the tile; `tail`: its column lies past the tile's last whole
+// 32 columns.  Which kernel GCC fused where was found element by element
+// against the reference build (the oracle's restatement is pinned to it):
+//   rank-2/3 staged streams (:581-632)                        stream
+//   packed panel or unpacked 2x32 / 1x32 register blocks      block
+//   the scalar tile over a row pair's column tail             stream
+//   the scalar tile over a single row's column tail           scalar
+//   the rank-1 row stream of an unpacked single row (:746-764) stream
+uint32_t ref_tile_form(uint32_t rows, uint32_t cols, uint32_t K, bool pack, bool single,
+                       bool tail) {
+    const uint64_t stride8 = (static_cast<uint64_t>(cols) + 7u) & ~uint64_t{7};
+    if (cols >= 1024u && (rows == 2u || rows == 3u) && stride8 * rows * 4u <= kRefScratchBytes)
+        return kFormStream;
+    if (pack && rows >= 3u && static_cast<uint64_t>(K) * cols <= kRefScratchBytes)
+        return tail ? (single ? kFormScalar : kFormStream) : kFormBlock;
+    if (!single) return tail ? kFormStream : kFormBlock;
+    if (static_cast<uint64_t>(cols) * 4u <= kRefScratchBytes) return kFormStream;
+    return tail ? kFormScalar : kFormBlock;   // the 1x32 blocked walk, scalar tail
+}
+
+// MATMUL_I8's epilogue rounding, element by element, as the reference device
+// this one models computes an M x K x N product (n_full columns in all, this
+// launch's column 0 at col_base; n_full 0 = N).  Command flags and
+// VNPU_B200_EPILOGUE force one form.  The map collapses to one form when every
+// class of element that occurs rounds to the same bits: without a bias the
+// block and stream forms agree, with NONE / RELU the stream and scalar ones.
+FormMap i8_form_map(const vnpu_device_t *d, uint32_t unit, uint32_t flags, uint32_t M, uint32_t K,
+                    uint32_t N, bool has_bias, uint32_t epilogue, uint32_t n_full,
+                    uint32_t col_base) {
+    FormMap fm;
+    if (!n_full) n_full = N;
+    const bool act = epilogue >= VNPU_EPILOGUE_SILU && epilogue <= VNPU_EPILOGUE_GELU_ERF;
+    auto canon = [&](uint32_t f) -> uint32_t {
+        if (!has_bias) return (act && f == kFormScalar) ? kFormScalar : kFormBlock;
+        if (!act) return f == kFormBlock ? kFormBlock : kFormStream;
+        return f;
+    };
+    if (flags & VNPU_CMD_FLAG_EPI_SCALAR) fm.form = kFormScalar;
+    else if (flags & VNPU_CMD_FLAG_EPI_STREAM) fm.form = kFormStream;
+    else if (d->epi_forced) fm.form = d->epi_form;
+    else {
+        unit = i8_unit(unit, flags);
+        if (d->f32_scalar || unit == VNPU_UNIT_CELL) {
+            fm.form = kFormScalar;   // scalar ISA / Cell tile: nothing fused
+        } else {
+            uint32_t tm, tn;
+            ref_tile_geometry(d, unit, M, n_full, true, tm, tn);
+            const uint32_t tiles_m = ceil_div(M, tm), tiles_n = ceil_div(n_full, tn);
+            const uint32_t rows_last = M - (tiles_m - 1) * tm;
+            const uint32_t cols_last = n_full - (tiles_n - 1) * tn;
+            // classes that occur: row (last tile?, odd single row?), column
+            // (last tile?, tail?)
+            bool row_cls[4] = {}, col_cls[4] = {};
+            if (tiles_m > 1) {
+                row_cls[0] = tm >= 2;
+                row_cls[1] = (tm & 1u) != 0;
+            }
+            row_cls[2] = rows_last >= 2;
+            row_cls[3] = (rows_last & 1u) != 0;
+            if (tiles_n > 1) {
+                col_cls[0] = tn >= 32;
+                col_cls[1] = (tn & 31u) != 0;
+            }
+            col_cls[2] = cols_last >= 32;
+            col_cls[3] = (cols_last & 31u) != 0;
+            uint32_t seen = 0;   // canonical forms present, one bit each
+            for (uint32_t rc = 0; rc < 4; ++rc)
+                for (uint32_t cc = 0; cc < 4; ++cc) {
+                    const uint32_t rows = (rc & 2u) ? rows_last : tm;
+                    const uint32_t cols = (cc & 2u) ? cols_last : tn;
+                    const uint32_t f = ref_tile_form(rows, cols, K, d->f32_pack, rc & 1u, cc & 1u);
+                    fm.table |= f << (2u * (rc * 4u + cc));
+                    if (row_cls[rc] && col_cls[cc]) seen |= 1u << canon(f);
+                }
+            if (seen && !(seen & (seen - 1u))) {
+                fm.form = static_cast<uint32_t>(__builtin_ctz(seen));
+                fm.table = 0;
+            } else {
+                fm.form = kFormMixed;
+                fm.tm = tm;
+                fm.tn = tn;
+            }
+        }
+    }
+    fm.M = M;
+    fm.N = n_full;
+    fm.col_base = col_base;
+    return fm;
+}
+
 // src/core/scheduler.cpp:274-352 (prepare_matmul_f32 + execute_matmul_f32)
 void exec_matmul_f32(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags,
                      const LaunchCtx &ctx, Accounting &acc) {
@@ -398,7 +529,7 @@ void exec_matmul_f32(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags
     const uint32_t unit = f32_unit(in, flags);
     const bool scalar_isa = d->f32_scalar || (flags & VNPU_CMD_FLAG_EPI_SCALAR);
     MatmulF32 p;
-    f32_geometry(d, unit, in.M, in.N, p.tile_m, p.tile_n);
+    ref_tile_geometry(d, unit, in.M, in.N, false, p.tile_m, p.tile_n);
     if (unit == VNPU_UNIT_CELL || scalar_isa || in.trans_a) p.mode = kF32Unfused;
     else if (in.trans_b) p.mode = kF32Dot8;
     else p.mode = kF32Block;
@@ -473,7 +604,10 @@ void exec_matmul_i8_scatter(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_
     p.K = in.K;
     p.N = in.N;
     p.epilogue = in.epilogue;
-    p.form = epi_form_for(s->device, flags);
+    // the shard's columns round as columns col_offset.. of the whole ldd-wide
+    // product the reference device would compute
+    p.fmap = i8_form_map(s->device, VNPU_UNIT_AUTO, flags, in.M, in.K, in.N, in.bias != nullptr,
+                         in.epilogue, in.ldd, in.col_offset);
     p.tmap_b = w->tmap_ok ? &w->tmap : nullptr;
     p.tmap_b128 = w->tmap128_ok ? &w->tmap128 : nullptr;
     for (uint32_t d = 0; d < in.ndst; ++d) p.dst[d] = in.dst[d];
@@ -697,7 +831,8 @@ void exec_qkv_rope_append(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t 
     p.N = static_cast<uint32_t>(N);
     p.ldc = static_cast<uint32_t>(N);
     p.epilogue = a.epilogue;
-    p.form = epi_form_for(s->device, flags);
+    p.fmap = i8_form_map(s->device, VNPU_UNIT_AUTO, flags, a.T, a.K, static_cast<uint32_t>(N),
+                         a.bias != nullptr, a.epilogue);
     p.tmap_b = w->tmap_ok ? &w->tmap : nullptr;
     p.tmap_b128 = w->tmap128_ok ? &w->tmap128 : nullptr;
     QkvRope q;
@@ -773,7 +908,8 @@ void exec_matmul_i8_residual(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32
     p.K = a.K;
     p.N = a.N;
     p.epilogue = a.epilogue;
-    p.form = epi_form_for(s->device, flags);
+    p.fmap = i8_form_map(s->device, VNPU_UNIT_AUTO, flags, a.M, a.K, a.N, a.bias != nullptr,
+                         a.epilogue);
     p.tmap_b = w->tmap_ok ? &w->tmap : nullptr;
     p.tmap_b128 = w->tmap128_ok ? &w->tmap128 : nullptr;
     if (a.M == 1) {
@@ -1278,16 +1414,22 @@ VNPU_API vnpu_status_t VNPU_CALL vnpu_device_create(const vnpu_config_t *config,
         d->ordinal = ordinal;
         d->config = cfg;
         d->num_sms = prop.multiProcessorCount;
-        d->epi_form = epi_form_from_env();
+        d->epi_forced = epi_form_from_env(d->epi_form);
         // The reference device whose MATMUL_F32 results this one reproduces
         // (src/core/runtime.cpp:858-938).
         const bool ref_mode = env_is("VNPU_MODE", "reference");
         d->f32_scalar = ref_mode || env_is("VNPU_FORCE_ISA", "scalar") ||
-                        d->epi_form == kFormScalar;
+                        (d->epi_forced && d->epi_form == kFormScalar);
         d->f32_pack = !ref_mode && !env_is("VNPU_PACK", "0");
         const uint32_t logical = std::max(1u, std::thread::hardware_concurrency());
         d->f32_threads = std::min(cfg.num_threads ? cfg.num_threads : host_physical_cores(),
                                   logical);
+        {
+            // as the reference reads it (src/core/runtime.cpp:174-179), 256 KiB
+            // when unknown (src/internal.h:187)
+            const long l2 = sysconf(_SC_LEVEL2_CACHE_SIZE);
+            d->host_l2 = l2 > 0 ? static_cast<uint64_t>(l2) : 256u * 1024u;
+        }
         if (cfg.tile_m && cfg.tile_k && cfg.tile_n) {
             d->f32_tile_m.store(cfg.tile_m);
             d->f32_tile_k.store(cfg.tile_k);

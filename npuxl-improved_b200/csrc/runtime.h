@@ -132,7 +132,10 @@ struct vnpu_device {
     vnpu_config_t config{};
     vnpu_device_info_t info{};
     int num_sms = 148;
+    // MATMUL_I8 epilogue rounding: the reference device's per-element choice
+    // (epi_forced false), or one form for every element (VNPU_B200_EPILOGUE).
     uint32_t epi_form = 0;
+    bool epi_forced = false;
     uint64_t wait_limit_ns = 2000000000ull;
     cudaStream_t aux = nullptr;  // device-level work (pack) and status reads
     vnpu_b200::TraceState trace;
@@ -154,13 +157,15 @@ struct vnpu_device {
     std::atomic<uint32_t> error{0};
     std::atomic<uint32_t> last_opcode{0};
     std::atomic<uint32_t> tile_m{128}, tile_k{128}, tile_n{256};
-    // MATMUL_F32 reproduces the reference device of the same configuration:
-    // its worker-thread count, tile defaults, VNPU_PACK and ISA decide which
-    // of its kernels, and so which rounding, owns each output element.
+    // MATMUL_F32 and MATMUL_I8 reproduce the reference device of the same
+    // configuration: its worker-thread count, tile defaults, VNPU_PACK, ISA
+    // and host L2 size decide which of its kernels, and so which rounding,
+    // owns each output element.
     uint32_t f32_threads = 1;
     std::atomic<uint32_t> f32_tile_m{128}, f32_tile_k{128}, f32_tile_n{64};
     bool f32_pack = true;
     bool f32_scalar = false;
+    uint64_t host_l2 = 256u * 1024u;   // the host's L2 bytes, as the reference reads it
     std::atomic<uint64_t> launches{0};  // kernels launched by this library
     vnpu_interrupt_cb_t irq_cb = nullptr;
     void *irq_user = nullptr;

@@ -562,124 +562,3 @@ class Device:
 
     def replay(self, graph: int) -> None:
         self.lib.check(self.lib.b200_graph_launch(graph, self.stream), "graph_launch")
-
-
-# ---------------------------------------------------------------------------
-# The C restatement oracle (oracle/liboracle.so) - test infrastructure only.
-# ---------------------------------------------------------------------------
-
-class Oracle:
-    FORM_AVX2 = 0
-    FORM_SCALAR = 1
-
-    def __init__(self, path: str):
-        self.h = C.CDLL(path)
-        h = self.h
-        i8p = C.c_void_p
-        self._matmul = _sig(h, "oracle_matmul_i8", None, i8p, u32, i8p, vp, vp, vp, vp, u32, u32,
-                            u32, u32, u32, C.c_int)
-        self._acc = _sig(h, "oracle_gemm_i8_acc", None, i8p, u32, i8p, u32, vp, u32, u32, u32)
-        self._quant = _sig(h, "oracle_quantize_i8", C.c_int, vp, vp, vp, u64, u64, u32)
-        self._colsums = _sig(h, "oracle_column_sums", None, vp, u32, u32, u32, u32, vp, vp)
-        self._rms = _sig(h, "oracle_rmsnorm", None, vp, vp, vp, u32, u32, f32, C.c_int)
-        self._rope = _sig(h, "oracle_rope", None, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32,
-                          f32, f32)
-        self._swiglu = _sig(h, "oracle_swiglu", None, vp, vp, vp, u64, f32, C.c_int)
-        self._add = _sig(h, "oracle_add", None, vp, vp, vp, u64, f32, f32, C.c_int)
-        self._attn = _sig(h, "oracle_attention", None, vp, vp, vp, vp, vp, u32, u32, u32, u32,
-                          u32, u32, f32)
-        self._mm_f32 = _sig(h, "oracle_matmul_f32", None, vp, vp, vp, vp, u32, u32, u32, u32, u32,
-                            u32, u32, u32, f32, f32, u32, u32, vp, u32, u32, u32, u32, u32, u32,
-                            C.c_int, C.c_int)
-        self._f32_geom = _sig(h, "oracle_f32_tile_geometry", None, u32, u32, u32, u32, u32, u32,
-                              u32, C.c_int, C.POINTER(u32), C.POINTER(u32), C.POINTER(u32))
-        self.fast_expf = _sig(h, "oracle_fast_expf", f32, f32, C.c_int)
-        self.dequant = _sig(h, "oracle_dequant", f32, C.c_int32, f32, f32, C.POINTER(f32), u32,
-                            C.c_int)
-
-    def quantize(self, X: np.ndarray, axis: int = QUANT_PER_ROW):
-        X = np.ascontiguousarray(X, dtype=np.float32)
-        rows, cols = X.shape
-        Y = np.empty((rows, cols), np.int8)
-        n = rows if axis == QUANT_PER_ROW else (cols if axis == QUANT_PER_COLUMN else 1)
-        s = np.empty(n, np.float32)
-        rc = self._quant(ptr(X), ptr(Y), ptr(s), rows, cols, axis)
-        assert rc == 0
-        return Y, s
-
-    def gemm_acc(self, A: np.ndarray, B: np.ndarray) -> np.ndarray:
-        A = np.ascontiguousarray(A, np.int8)
-        B = np.ascontiguousarray(B, np.int8)
-        M, K = A.shape
-        N = B.shape[1]
-        acc = np.empty((M, N), np.int32)
-        self._acc(ptr(A), K, ptr(B), N, ptr(acc), M, K, N)
-        return acc
-
-    def matmul_i8(self, A, B, scale_a, scale_b, bias=None, epilogue=0, form=0) -> np.ndarray:
-        A = np.ascontiguousarray(A, np.int8)
-        B = np.ascontiguousarray(B, np.int8)
-        M, K = A.shape
-        N = B.shape[1]
-        Cm = np.empty((M, N), np.float32)
-        self._matmul(ptr(A), K, ptr(B), ptr(scale_a), ptr(scale_b), ptr(bias), ptr(Cm), N, M, K,
-                     N, epilogue, form)
-        return Cm
-
-    def matmul_f32(self, A, B, M, K, N, bias=None, C=None, lda=0, ldb=0, ldc=0, trans_a=0,
-                   trans_b=0, alpha=1.0, beta=0.0, epilogue=0, unit=UNIT_VOODOO, tile_mask=None,
-                   mask_tile_m=0, mask_tile_n=0, threads=8, tiles=(128, 128, 64), pack_b=1,
-                   avx2=1) -> np.ndarray:
-        """MATMUL_F32 as a reference device with `threads` threads, tile
-        defaults `tiles`, VNPU_PACK=`pack_b` and the AVX2 (or scalar) ISA
-        computes it.  C (optional) holds the prior contents beta reads."""
-        ldc_ = ldc or N
-        out = np.zeros((M, ldc_), np.float32) if C is None else np.array(C, np.float32, copy=True)
-        self._mm_f32(ptr(A), ptr(B), ptr(bias), ptr(out), M, K, N, lda, ldb, ldc, trans_a, trans_b,
-                     alpha, beta, epilogue, unit, ptr(tile_mask), mask_tile_m, mask_tile_n,
-                     threads, tiles[0], tiles[1], tiles[2], pack_b, avx2)
-        return out
-
-    def f32_tile_geometry(self, unit, M, N, threads=8, tiles=(128, 128, 64), pack_b=1):
-        tm, tk, tn = u32(), u32(), u32()
-        self._f32_geom(unit, M, N, threads, tiles[0], tiles[1], tiles[2], pack_b, C.byref(tm),
-                       C.byref(tk), C.byref(tn))
-        return tm.value, tk.value, tn.value
-
-    def column_sums(self, B: np.ndarray, trans_b: int = 0):
-        B = np.ascontiguousarray(B, np.int8)
-        K, N = (B.shape[1], B.shape[0]) if trans_b else B.shape
-        sums = np.empty(N, np.int32)
-        canon = np.empty((K, N), np.int8)
-        self._colsums(ptr(B), K, N, 0, trans_b, ptr(sums), ptr(canon))
-        return sums, canon
-
-    def rmsnorm(self, X, W, eps, form=0):
-        X = np.ascontiguousarray(X, np.float32)
-        Y = np.empty_like(X)
-        self._rms(ptr(X), ptr(W), ptr(Y), X.shape[0], X.shape[1], eps, form)
-        return Y
-
-    def rope(self, Q, K, positions, batch, heads, q_seq, k_seq, head_dim, position_offset=0,
-             interleaved=0, theta=10000.0, scaling=1.0):
-        Q = None if Q is None else np.array(Q, np.float32, copy=True)
-        K = None if K is None else np.array(K, np.float32, copy=True)
-        self._rope(ptr(Q), ptr(K), ptr(positions), batch, heads, q_seq, k_seq, head_dim,
-                   position_offset, interleaved, theta, scaling)
-        return Q, K
-
-    def swiglu(self, g, u, alpha=1.0, form=0):
-        Y = np.empty_like(g)
-        self._swiglu(ptr(g), ptr(u), ptr(Y), g.size, alpha, form)
-        return Y
-
-    def add(self, A, B, alpha=1.0, beta=1.0, form=0):
-        Y = np.empty_like(A)
-        self._add(ptr(A), ptr(B), ptr(Y), A.size, alpha, beta, form)
-        return Y
-
-    def attention(self, Q, K, V, mask, batch, heads, seq_q, seq_k, head_dim, causal=1, scale=0.0):
-        O = np.empty((batch, heads, seq_q, head_dim), np.float32)
-        self._attn(ptr(Q), ptr(K), ptr(V), ptr(mask), ptr(O), batch, heads, seq_q, seq_k,
-                   head_dim, causal, scale)
-        return O

@@ -155,6 +155,125 @@ void oracle_matmul_i8(const int8_t *A, uint32_t lda, const int8_t *B,
 }
 
 /* ------------------------------------------------------------------------- */
+/* MATMUL_I8 as a reference device computes it: which kernel owns each      */
+/* output element, and so which form its dequant epilogue is rounded in.     */
+/* ------------------------------------------------------------------------- */
+
+/* Per-worker scratch the reference kernels stage into (VNPU_LOCAL_STORE_BYTES,
+ * include/vnpu.h:51); thread_scratch() hands out that plus one cache line and
+ * each kernel asks for its bytes plus one cache line, so the cache lines
+ * cancel in every "fits" test below. */
+#define ORACLE_LOCAL_STORE 262144u
+
+/* decode_max_tile_columns, src/core/scheduler.cpp:75-93: the widest decode
+ * column tile, half of L2 shared by `rows` int32 staging rows, bounded by the
+ * scratch, rounded down to 32 columns, at least 256. */
+static uint32_t i8_decode_cap(uint64_t l2_bytes, uint32_t rows)
+{
+    uint64_t l2 = l2_bytes ? l2_bytes : 512u * 1024u;
+    uint64_t cols = l2 / (8u * (uint64_t)rows);
+    uint64_t scratch = ORACLE_LOCAL_STORE / (4u * (uint64_t)rows);
+    if (cols > scratch) cols = scratch;
+    cols &= ~(uint64_t)31u;
+    if (cols < 256u) cols = 256u;
+    if (cols > 0x7fffffffu) cols = 0x7fffffffu;
+    return (uint32_t)cols;
+}
+
+void oracle_i8_tile_geometry(uint32_t unit, uint32_t M, uint32_t N,
+                             uint32_t threads, uint32_t tile_m,
+                             uint32_t tile_n, int pack_b, uint64_t l2_bytes,
+                             uint32_t *tm_out, uint32_t *tn_out)
+{
+    const uint32_t units = threads ? threads : 1;
+    uint32_t tk;
+    /* Decode rows (src/core/scheduler.cpp:107-175): M <= 3 rows of int8 get
+     * one contiguous column slice per worker once a worker's share of N
+     * reaches 1024 columns; every other case is the F32 geometry. */
+    if (M <= 3 && (unit == 0 || unit == 1) && N / units >= 1024u) {
+        uint32_t tiles = N / 256u;
+        if (tiles < 1) tiles = 1;
+        if (tiles > units) tiles = units;
+        const uint32_t cap = i8_decode_cap(l2_bytes, M);
+        if ((N + tiles - 1) / tiles > cap) {
+            tiles = (N + cap - 1) / cap;
+            tiles = (tiles + units - 1) / units * units;
+        }
+        uint32_t wide = ((N + tiles - 1) / tiles + 31u) & ~31u;
+        if (wide < 1) wide = 1;
+        *tm_out = M;
+        *tn_out = wide < N ? wide : N;
+        return;
+    }
+    oracle_f32_tile_geometry(unit, M, N, threads, tile_m, 1, tile_n, pack_b,
+                             tm_out, &tk, tn_out);
+}
+
+/* The form of output element (m, n), gemm_i8_dispatch_tile
+ * (src/kernels/kernels.cpp:922-978) applied to the tile (m, n) falls in.
+ * The AVX2 kernels round store_i8_c differently depending on where GCC
+ * inlined and fused it (found element by element against the reference
+ * build, tests/test_oracle.py):
+ *   2x32 register blocks, packed or not (:634-700, :779-842)   block
+ *   rank-2/3 streams (:581-632), the rank-1 row stream (:746-764) stream
+ *   the scalar tile for the column tail of a row pair           stream
+ *   the scalar tile for the column tail of a single row         scalar
+ * and the scalar ISA and the Cell unit (:880-920) are scalar throughout. */
+int oracle_i8_element_form(uint32_t unit, int avx2, int pack_b, uint32_t K,
+                           uint32_t M, uint32_t N, uint32_t tm, uint32_t tn,
+                           uint32_t m, uint32_t n)
+{
+    if (!avx2 || unit == 3) return ORACLE_FORM_SCALAR;
+    const uint32_t m0 = m / tm * tm, n0 = n / tn * tn;
+    const uint32_t rows = M - m0 < tm ? M - m0 : tm;
+    const uint32_t cols = N - n0 < tn ? N - n0 : tn;
+    const int tail = n - n0 >= (cols & ~31u);
+    const int single = (rows & 1u) && m - m0 == rows - 1u;
+    const uint64_t stride8 = ((uint64_t)cols + 7u) & ~(uint64_t)7u;
+    if (cols >= 1024u && (rows == 2u || rows == 3u) &&
+        stride8 * rows * 4u <= ORACLE_LOCAL_STORE)
+        return ORACLE_FORM_STREAM;                      /* rank-R stream */
+    if (pack_b && rows >= 3u && (uint64_t)K * cols <= ORACLE_LOCAL_STORE) {
+        if (!tail) return ORACLE_FORM_AVX2;             /* packed panel blocks */
+        return single ? ORACLE_FORM_SCALAR : ORACLE_FORM_STREAM;
+    }
+    if (!single) return tail ? ORACLE_FORM_STREAM : ORACLE_FORM_AVX2;
+    if ((uint64_t)cols * 4u <= ORACLE_LOCAL_STORE) return ORACLE_FORM_STREAM;
+    /* no room to stage the row: the 1x32 blocked walk, scalar tail */
+    return tail ? ORACLE_FORM_SCALAR : ORACLE_FORM_AVX2;
+}
+
+void oracle_matmul_i8_device(const int8_t *A, uint32_t lda, const int8_t *B,
+                             const float *scale_a, const float *scale_b,
+                             const float *bias, float *C, uint32_t ldc,
+                             uint32_t M, uint32_t K, uint32_t N,
+                             uint32_t epilogue, uint32_t unit,
+                             uint32_t threads, uint32_t tile_m,
+                             uint32_t tile_n, int pack_b, int avx2,
+                             uint64_t l2_bytes)
+{
+    uint32_t tm, tn;
+    if (unit == 0) unit = 1;  /* choose_unit: AUTO resolves to VOODOO */
+    oracle_i8_tile_geometry(unit, M, N, threads, tile_m, tile_n, pack_b,
+                            l2_bytes, &tm, &tn);
+    int32_t *row = (int32_t *)malloc(sizeof(int32_t) * (N ? N : 1));
+    if (!row) return;
+    for (uint32_t m = 0; m < M; ++m) {
+        oracle_gemm_i8_acc(A + (size_t)m * lda, lda, B, N, row, 1, K, N);
+        const float sa = scale_a ? scale_a[m] : 1.0f;
+        for (uint32_t n = 0; n < N; ++n) {
+            const float sb = scale_b ? scale_b[n] : 1.0f;
+            const int form = oracle_i8_element_form(unit, avx2, pack_b, K, M,
+                                                    N, tm, tn, m, n);
+            C[(size_t)m * ldc + n] = oracle_dequant(row[n], sa, sb,
+                                                    bias ? bias + n : NULL,
+                                                    epilogue, form);
+        }
+    }
+    free(row);
+}
+
+/* ------------------------------------------------------------------------- */
 /* QUANTIZE_I8 (src/kernels/llm.cpp:387-436)                                  */
 /* ------------------------------------------------------------------------- */
 

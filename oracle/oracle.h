@@ -53,6 +53,34 @@ void oracle_matmul_i8(const int8_t *A, uint32_t lda, const int8_t *B,
                       const float *bias, float *C, uint32_t ldc, uint32_t M,
                       uint32_t K, uint32_t N, uint32_t epilogue, int form);
 
+/* MATMUL_I8 tile sizes (src/core/scheduler.cpp:75-207, int8 branch) for a
+ * reference device with `threads` workers, tile defaults tile_m / tile_n,
+ * VNPU_PACK = pack_b and an L2 of l2_bytes (0: the reference's 512 KiB
+ * default); unit as resolved by choose_unit (1 VOODOO, 2 WILDCAT, 3 CELL). */
+void oracle_i8_tile_geometry(uint32_t unit, uint32_t M, uint32_t N,
+                             uint32_t threads, uint32_t tile_m,
+                             uint32_t tile_n, int pack_b, uint64_t l2_bytes,
+                             uint32_t *tm, uint32_t *tn);
+
+/* ORACLE_FORM_* of output element (m, n) of an M x K x N MATMUL_I8 on tiles
+ * tm x tn (gemm_i8_dispatch_tile, src/kernels/kernels.cpp:922-978). */
+int oracle_i8_element_form(uint32_t unit, int avx2, int pack_b, uint32_t K,
+                           uint32_t M, uint32_t N, uint32_t tm, uint32_t tn,
+                           uint32_t m, uint32_t n);
+
+/* MATMUL_I8 exactly as the reference device described by threads /
+ * tile_m, tile_n / pack_b / avx2 (0 = VNPU_FORCE_ISA=scalar) / l2_bytes
+ * computes it with no flags: each element in its kernel's form.  unit 0
+ * (AUTO) resolves to VOODOO. */
+void oracle_matmul_i8_device(const int8_t *A, uint32_t lda, const int8_t *B,
+                             const float *scale_a, const float *scale_b,
+                             const float *bias, float *C, uint32_t ldc,
+                             uint32_t M, uint32_t K, uint32_t N,
+                             uint32_t epilogue, uint32_t unit,
+                             uint32_t threads, uint32_t tile_m,
+                             uint32_t tile_n, int pack_b, int avx2,
+                             uint64_t l2_bytes);
+
 /* Dequant epilogue for one accumulator (store_i8_c). */
 float oracle_dequant(int32_t acc, float sa, float sb, const float *bias_n,
                      uint32_t epilogue, int form);

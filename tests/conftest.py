@@ -17,12 +17,27 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 PKG = os.path.join(ROOT, "npuxl-improved_b200")
 sys.path.insert(0, PKG)
 sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
 import vnpu  # noqa: E402
+from vnpu_oracle import Oracle  # noqa: E402
 
 ORACLE_LIB = os.path.join(ROOT, "oracle", "liboracle.so")
 REF_LIB = os.path.join(ROOT, "oracle", "_ref", "libvnpu_ref.so")
 GOLDEN = os.path.join(ROOT, "tests", "golden", "golden.npz")
+
+
+def reference_dir() -> str:
+    """The reference checkout: VNPU_REFERENCE_DIR, else the directory
+    oracle/_ref was built from (oracle/Makefile records it); "" if neither."""
+    env = os.environ.get("VNPU_REFERENCE_DIR")
+    if env:
+        return env
+    try:
+        with open(os.path.join(ROOT, "oracle", "_ref", "REFERENCE_DIR")) as f:
+            return f.read().strip()
+    except OSError:
+        return ""
 
 
 def pytest_configure(config):
@@ -37,7 +52,7 @@ def _ensure_oracle():
 @pytest.fixture(scope="session")
 def oracle():
     _ensure_oracle()
-    return vnpu.Oracle(ORACLE_LIB)
+    return Oracle(ORACLE_LIB)
 
 
 @pytest.fixture(scope="session")

@@ -24,6 +24,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(ROOT, "npuxl-improved_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
 import vnpu  # noqa: E402
 
 REF_LIB = os.path.join(ROOT, "oracle", "_ref", "libvnpu_ref.so")
@@ -47,7 +48,8 @@ def which_form(orc, out, A, B, sa, sb, bias, epi):
 
 def main():
     lib = vnpu.Lib(REF_LIB)
-    orc = vnpu.Oracle(ORACLE_LIB)
+    from vnpu_oracle import Oracle
+    orc = Oracle(ORACLE_LIB)
     rng = np.random.default_rng(20261201)
     g = {}
 

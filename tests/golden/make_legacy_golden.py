@@ -33,7 +33,9 @@ def run_reference(out_path: str, reference_dir: str) -> None:
 
 
 def main():
-    ref = os.environ.get("VNPU_REFERENCE_DIR", "/root/reference")
+    ref = os.environ.get("VNPU_REFERENCE_DIR", "")
+    if not ref:
+        sys.exit("set VNPU_REFERENCE_DIR to the reference checkout")
     if not os.path.exists(REF_ARCHIVE):
         sys.exit("build the reference first: make -C oracle ref REF=" + ref)
     out = os.path.join(HERE, "legacy_scenario.bin")

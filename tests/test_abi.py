@@ -16,11 +16,10 @@ import subprocess
 import pytest
 
 import vnpu
-from conftest import ROOT
+from conftest import ROOT, reference_dir
 
 INCLUDE = os.path.join(ROOT, "include")
-REFERENCE_INCLUDE = os.path.join(os.environ.get("VNPU_REFERENCE_DIR", "/root/reference"),
-                                 "include")
+REFERENCE_INCLUDE = os.path.join(reference_dir(), "include") if reference_dir() else ""
 HEADERS = ["vnpu.h", "vnpu_backend.h", "vnpu_b200.h"]
 
 
@@ -47,6 +46,8 @@ def test_library_exports_every_declared_function(b200_lib):
 
 def test_exported_surface_matches_reference_library(b200_lib, ref_lib):
     """Every function the reference exports from vnpu.h / vnpu_backend.h exists here."""
+    if not os.path.isdir(REFERENCE_INCLUDE):
+        pytest.skip("reference checkout not present")
     ref_text = "".join(open(os.path.join(REFERENCE_INCLUDE, h)).read()
                        for h in ("vnpu.h", "vnpu_backend.h"))
     ref_names = set(re.findall(r"VNPU_API\s+[^;]*?VNPU_CALL\s+(\w+)\s*\(", ref_text))

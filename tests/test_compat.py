@@ -22,10 +22,10 @@ import numpy as np
 import pytest
 
 import vnpu
-from conftest import ROOT, bits_equal, build_legacy_scenario, read_records
+from conftest import ROOT, bits_equal, build_legacy_scenario, read_records, reference_dir
 
 INCLUDE = os.path.join(ROOT, "include")
-REF_DIR = os.environ.get("VNPU_REFERENCE_DIR", "/root/reference")
+REF_DIR = reference_dir()
 GOLDEN = os.path.join(ROOT, "tests", "golden", "legacy_scenario.bin")
 LIB_DIR = os.path.dirname(vnpu.LIB_PATH)
 

@@ -271,3 +271,89 @@ def test_matmul_f32_vs_reference(ref_lib, oracle):
                                tiles=(info.tile_m, info.tile_k, info.tile_n), pack_b=pack,
                                avx2=int(isa == "avx2"), **ld)
         assert bits_equal(Cr, Co), (M, K, N, isa, threads, pack, unit, ta, tb, alpha, beta, epi)
+
+
+# ---------------------------------------------------------------- MATMUL_I8 default rounding
+def _ref_device_cfg(ref_lib, isa, threads, pack, tiles=None):
+    os.environ["VNPU_FORCE_ISA"] = isa
+    os.environ["VNPU_PACK"] = str(pack)
+    try:
+        return vnpu.Device(ref_lib, num_threads=threads, tiles=tiles)
+    finally:
+        os.environ.pop("VNPU_FORCE_ISA", None)
+        os.environ.pop("VNPU_PACK", None)
+
+
+def test_matmul_i8_device_model_vs_reference(ref_lib, oracle):
+    """MATMUL_I8 with no command flags: the reference rounds each output in
+    the form of the kernel that owns its tile (block / stream / scalar), which
+    its tile geometry picks from M, N, the thread count, the tile defaults and
+    VNPU_PACK.  oracle_matmul_i8_device restates that choice element by
+    element; seeded shapes cover the rank-1/2/3 streams, packed panels, the
+    unpacked 2x32 blocks, column tails, leftover rows, wide decode slices
+    whose last slice is narrower than 1024 columns, WILDCAT/CELL units and
+    the scalar ISA."""
+    rng = np.random.default_rng(11)
+    for _ in range(70):
+        M = int(rng.choice([1, 2, 3, 4, 5, 7, 8, 9, 11, 16, 31, 33, 64, 130]))
+        K = int(rng.choice([16, 64, 200, 4100, 5000]))
+        N = int(rng.choice([20, 45, 64, 70, 100, 300, 1030, 2100, 3100]))
+        threads = int(rng.integers(1, 5))
+        pack = int(rng.random() < 0.75)
+        unit = int(rng.choice([0, 1, 1, 1, 2, 3]))
+        isa = "avx2" if rng.random() < 0.9 else "scalar"
+        tiles = None
+        if rng.random() < 0.3:
+            tiles = (int(rng.choice([8, 32, 128])), 128, int(rng.choice([16, 40, 64, 100, 2048])))
+        epi = int(rng.choice([0, 2, 3]))
+        A, sa = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
+        B, sb = oracle.quantize(rng.uniform(-1, 1, (K, N)).astype(np.float32), 1)
+        bias = rng.normal(0, 0.5, N).astype(np.float32)
+        with _ref_device_cfg(ref_lib, isa, threads, pack, tiles) as d:
+            info = d.info()
+            w = d.pack(B, sb, K, N)
+            C = np.empty((M, N), np.float32)
+            d.matmul_i8(A, w, sa, bias, C, M, K, N, epilogue=epi, unit=unit)
+            d.unpack(w)
+        Co = oracle.matmul_i8_device(A, B, sa, sb, bias, epi, unit, info.num_threads,
+                                     (info.tile_m, info.tile_k, info.tile_n), pack,
+                                     int(isa == "avx2"), info.l2_bytes)
+        assert bits_equal(C, Co), (M, K, N, threads, pack, unit, isa, tiles, epi)
+
+
+def test_matmul_i8_device_model_needs_every_form(oracle):
+    """The forms the model assigns differ where the reference's kernels do:
+    rank-1 stream for one row, packed blocks with stream / scalar column
+    tails, rank-2 stream slices next to a narrow last slice."""
+    F = oracle.i8_forms(1, 64, 100, threads=1)
+    assert np.all(F == oracle.FORM_STREAM)
+    F = oracle.i8_forms(5, 64, 100, threads=1)          # packed, 64-column tiles
+    assert F[0, 0] == oracle.FORM_AVX2 and F[0, 97] == oracle.FORM_STREAM
+    assert F[4, 97] == oracle.FORM_SCALAR and F[4, 10] == oracle.FORM_AVX2
+    F = oracle.i8_forms(2, 64, 3100, threads=3)         # slices 1056, 1056, 988
+    assert np.all(F[:, :2112] == oracle.FORM_STREAM)
+    assert F[0, 2112] == oracle.FORM_AVX2 and F[1, 3099] == oracle.FORM_STREAM
+    F = oracle.i8_forms(3, 5000, 40, threads=1)         # packed (K x 40 fits the scratch)
+    assert F[2, 0] == oracle.FORM_AVX2 and F[2, 39] == oracle.FORM_SCALAR
+    F = oracle.i8_forms(3, 8192, 40, threads=1)         # unpacked: the odd row streams
+    assert np.all(F[2] == oracle.FORM_STREAM) and F[0, 0] == oracle.FORM_AVX2
+
+
+@pytest.mark.parametrize("M", [1, 4, 8])
+def test_matmul_i8_decode_config_vs_reference(ref_lib, oracle, M):
+    """The decode GEMV configuration (M in {1,4,8}, K = N = 4096, bias
+    N(0, 0.01)) through the reference with no flags, against the model."""
+    rng = np.random.default_rng(100 + M)
+    A, sa = oracle.quantize(rng.uniform(-1, 1, (M, 4096)).astype(np.float32), 0)
+    B, sb = oracle.quantize(rng.normal(0, 0.02, (4096, 4096)).astype(np.float32), 1)
+    bias = rng.normal(0, 0.01, 4096).astype(np.float32)
+    for threads in (4, 16):
+        with _ref_device_cfg(ref_lib, "avx2", threads, 1) as d:
+            info = d.info()
+            w = d.pack(B, sb, 4096, 4096)
+            C = np.empty((M, 4096), np.float32)
+            d.matmul_i8(A, w, sa, bias, C, M, 4096, 4096)
+            d.unpack(w)
+        Co = oracle.matmul_i8_device(A, B, sa, sb, bias, 0, 0, info.num_threads,
+                                     (info.tile_m, info.tile_k, info.tile_n), 1, 1, info.l2_bytes)
+        assert bits_equal(C, Co), (M, threads)

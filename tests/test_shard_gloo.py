@@ -44,7 +44,8 @@ def _rank_main(rank, world, port, q):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         import torch
-        orc = vnpu.Oracle(ORACLE_LIB)
+        from vnpu_oracle import Oracle
+        orc = Oracle(ORACLE_LIB)
         rng = np.random.default_rng(0)
         M, K, N = 24, 96, 700
         A, sa = orc.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
@@ -97,7 +98,8 @@ def _row_slice_main(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        orc = vnpu.Oracle(ORACLE_LIB)
+        from vnpu_oracle import Oracle
+        orc = Oracle(ORACLE_LIB)
         rng = np.random.default_rng(1)
         M, K, N = 32, 80, 600
         X = rng.normal(0, 1, (M, K)).astype(np.float32)
