@@ -16,28 +16,35 @@ extern "C" {
 #endif
 
 /*
- * Dequant epilogue form for MATMUL_I8 (command flags; no reference
- * counterpart - the reference has no switch, its form follows from how GCC
- * compiled each of its kernels).  With a bias and/or an activation, the
- * reference's outputs differ in the last bits between its own code paths:
+ * Dequant epilogue rounding of MATMUL_I8 and the int8 B200 opcodes.  With a
+ * bias and/or an activation, the reference's outputs differ in the last bits
+ * between its own CPU kernels, and which kernel computes an element depends
+ * on the tile it falls in (src/core/scheduler.cpp:75-207 tile grid from M, N,
+ * the worker-thread count, the tile defaults and VNPU_PACK;
+ * src/kernels/kernels.cpp:922-978 kernel per tile):
  *
- *   block  (default)  out = fmaf(float(acc)*sa, sb, bias), activation
- *                     polynomial evaluated with FMAs.  The reference's
- *                     register-block AVX2 kernels (2x32 block, packed panel;
- *                     src/kernels/kernels.cpp:634-701,779-869).
- *   stream            out = (float(acc)*sa)*sb + bias (two roundings), FMA
- *                     polynomial.  The reference's AVX2 rank-1 / rank-R decode
- *                     streams (kernels.cpp:581-632,702-767): M=1 always, M=2/3
- *                     when a thread's column slice is >= 1024.
- *   scalar            no fused operation anywhere: VNPU_FORCE_ISA=scalar and
- *                     VNPU_MODE=reference (kernels.cpp:537-550).
+ *   block    out = fmaf(float(acc)*sa, sb, bias), activation polynomial
+ *            evaluated with FMAs: the register-block AVX2 kernels (2x32 /
+ *            1x32 blocks, packed panel; kernels.cpp:634-701,779-869).
+ *   stream   out = (float(acc)*sa)*sb + bias (two roundings), FMA
+ *            polynomial: the rank-1 / rank-R decode streams
+ *            (kernels.cpp:581-632,702-767) and the column tail of a row pair.
+ *   scalar   no fused operation anywhere: the column tail of a single row,
+ *            the Cell unit, VNPU_FORCE_ISA=scalar and VNPU_MODE=reference
+ *            (kernels.cpp:537-550).
  *
- * Without bias and with epilogue NONE or RELU all three forms are the same
- * bits.  VNPU_B200_EPILOGUE=block|stream|scalar in the environment sets the
- * default of devices created afterwards.
+ * By default every element takes the form the reference device of the same
+ * configuration (vnpu_config_t.num_threads, else the host's physical cores;
+ * tile_m / tile_n; VNPU_PACK; VNPU_FORCE_ISA / VNPU_MODE; the host L2 size)
+ * gives it, so an unflagged command returns the reference's bits.  These
+ * command flags (no reference counterpart) force one form for every element
+ * instead; VNPU_B200_EPILOGUE=block|stream|scalar in the environment does the
+ * same for devices created afterwards.  Without bias and with epilogue NONE
+ * or RELU all forms are the same bits.
  */
 #define VNPU_CMD_FLAG_EPI_STREAM   (1u << 8)
 #define VNPU_CMD_FLAG_EPI_SCALAR   (1u << 9)
+#define VNPU_CMD_FLAG_EPI_BLOCK    (1u << 11)
 
 /*
  * ATTENTION_F32 output layout (no reference counterpart): with this flag O is
@@ -249,6 +256,25 @@ VNPU_API int VNPU_CALL vnpu_b200_device_ordinal(const vnpu_device_t *device);
 
 /* Number of kernels this library has launched on the device so far. */
 VNPU_API uint64_t VNPU_CALL vnpu_b200_kernel_launches(const vnpu_device_t *device);
+
+/* The reference device whose rounding this device reproduces (no reference
+ * counterpart): MATMUL_I8's per-element epilogue form and MATMUL_F32's
+ * per-tile accumulation order are those of a reference device
+ * (src/core/runtime.cpp:858-938) with these settings.  epilogue_forced != 0
+ * when VNPU_B200_EPILOGUE fixed one form (epilogue_form: 0 block, 1 stream,
+ * 2 scalar) for every element instead. */
+typedef struct vnpu_b200_reference_model {
+    uint32_t num_threads;          /* worker threads */
+    uint32_t tile_m, tile_k, tile_n;
+    uint32_t pack_b;               /* VNPU_PACK */
+    uint32_t scalar_isa;           /* VNPU_FORCE_ISA=scalar or VNPU_MODE=reference */
+    uint64_t l2_bytes;             /* the host L2 size it reads */
+    uint32_t epilogue_forced;
+    uint32_t epilogue_form;
+} vnpu_b200_reference_model_t;
+
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_reference_model(const vnpu_device_t *device,
+                                                          vnpu_b200_reference_model_t *out);
 
 /* Device address of the packed K-major weight matrix ([N][k_stride] int8)
  * and of its scales, for callers that fuse their own kernels around it. */

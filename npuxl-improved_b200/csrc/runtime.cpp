@@ -459,6 +459,7 @@ FormMap i8_form_map(const vnpu_device_t *d, uint32_t unit, uint32_t flags, uint3
     };
     if (flags & VNPU_CMD_FLAG_EPI_SCALAR) fm.form = kFormScalar;
     else if (flags & VNPU_CMD_FLAG_EPI_STREAM) fm.form = kFormStream;
+    else if (flags & VNPU_CMD_FLAG_EPI_BLOCK) fm.form = kFormBlock;
     else if (d->epi_forced) fm.form = d->epi_form;
     else {
         unit = i8_unit(unit, flags);
@@ -2045,6 +2046,22 @@ VNPU_API int VNPU_CALL vnpu_b200_device_ordinal(const vnpu_device_t *device) {
 
 VNPU_API uint64_t VNPU_CALL vnpu_b200_kernel_launches(const vnpu_device_t *device) {
     return device ? device->launches.load() : 0;
+}
+
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_reference_model(const vnpu_device_t *device,
+                                                          vnpu_b200_reference_model_t *out) {
+    if (!device || !out) return VNPU_ERR_INVALID_ARGUMENT;
+    std::memset(out, 0, sizeof(*out));
+    out->num_threads = device->f32_threads;
+    out->tile_m = device->f32_tile_m.load();
+    out->tile_k = device->f32_tile_k.load();
+    out->tile_n = device->f32_tile_n.load();
+    out->pack_b = device->f32_pack ? 1u : 0u;
+    out->scalar_isa = device->f32_scalar ? 1u : 0u;
+    out->l2_bytes = device->host_l2;
+    out->epilogue_forced = device->epi_forced ? 1u : 0u;
+    out->epilogue_form = device->epi_form;
+    return VNPU_OK;
 }
 
 VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_packed_weights_device(

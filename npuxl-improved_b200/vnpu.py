@@ -51,8 +51,9 @@ FEATURE_GPU_FUTURE = 1 << 31
 CMD_FLAG_EPI_STREAM = 1 << 8
 CMD_FLAG_EPI_SCALAR = 1 << 9
 CMD_FLAG_ATTN_TOKEN_MAJOR = 1 << 10   # ATTENTION_F32 writes O as [batch][seq_q][heads][D]
+CMD_FLAG_EPI_BLOCK = 1 << 11
 # oracle form index (oracle/oracle.h) -> command flags of the B200 library
-FORM_FLAGS = {0: 0, 1: CMD_FLAG_EPI_SCALAR, 2: CMD_FLAG_EPI_STREAM}
+FORM_FLAGS = {0: CMD_FLAG_EPI_BLOCK, 1: CMD_FLAG_EPI_SCALAR, 2: CMD_FLAG_EPI_STREAM}
 
 vp = C.c_void_p
 u32 = C.c_uint32
@@ -90,6 +91,13 @@ class TraceSummary(C.Structure):
                                    "bytes_written", "flops")] + \
               [("achieved_gflops", C.c_double), ("achieved_gbytes_s", C.c_double),
                ("hot_opcode", u32), ("hot_time_ns", u64), ("trace_overhead_ns", C.c_double)]
+
+
+class ReferenceModel(C.Structure):
+    """vnpu_b200_reference_model_t (include/vnpu_b200.h)."""
+    _fields_ = [("num_threads", u32), ("tile_m", u32), ("tile_k", u32), ("tile_n", u32),
+                ("pack_b", u32), ("scalar_isa", u32), ("l2_bytes", u64),
+                ("epilogue_forced", u32), ("epilogue_form", u32)]
 
 
 class ClusterConfig(C.Structure):
@@ -349,6 +357,8 @@ class Lib:
         if self.is_b200:
             self.b200_stream_handle = _sig(h, "vnpu_b200_stream_handle", vp, vp)
             self.b200_kernel_launches = _sig(h, "vnpu_b200_kernel_launches", u64, vp)
+            self.b200_reference_model = _sig(h, "vnpu_b200_reference_model", _ST, vp,
+                                             C.POINTER(ReferenceModel))
             self.b200_matmul_kernel = _sig(h, "vnpu_b200_matmul_i8_kernel", C.c_char_p, u32, u32,
                                            u32, u32, vp)
             self.b200_last_matmul_kernel = _sig(h, "vnpu_b200_last_matmul_kernel", C.c_char_p)
@@ -406,6 +416,13 @@ class Device:
         inf = DeviceInfo()
         self.lib.check(self.lib.device_get_info(self.dev, C.byref(inf)), "device_get_info")
         return inf
+
+    def reference_model(self) -> ReferenceModel:
+        """The reference device configuration whose rounding this B200 device
+        reproduces (B200 library only)."""
+        rm = ReferenceModel()
+        self.lib.check(self.lib.b200_reference_model(self.dev, C.byref(rm)), "reference_model")
+        return rm
 
     def status(self) -> DeviceStatus:
         s = DeviceStatus()
@@ -480,13 +497,15 @@ class Device:
         return rc
 
     def matmul_i8_scatter(self, A, w, scale_a, bias, dsts, M, K, N, ldd, col_offset,
-                          epilogue=EPI_NONE, lda=0, sync=True) -> int:
+                          epilogue=EPI_NONE, lda=0, sync=True, flags=0) -> int:
         """MATMUL_I8 of a column shard written into every destination in dsts
         (device pointers, [M][ldd] f32 each) at columns col_offset.."""
         d = (vp * B200_SCATTER_MAX)(*([ptr(x) for x in dsts] + [None] * (B200_SCATTER_MAX - len(dsts))))
         a = MatmulI8ScatterArgs(ptr(A), w, ptr(scale_a), ptr(bias), d, M, K, N, lda, ldd,
                                 col_offset, len(dsts), epilogue)
-        rc = self.submit([b200_command(OP_B200_MATMUL_I8_SCATTER, a)])
+        cmd = b200_command(OP_B200_MATMUL_I8_SCATTER, a)
+        cmd.flags = flags
+        rc = self.submit([cmd])
         if rc != OK or not sync:
             return rc
         return self.sync()

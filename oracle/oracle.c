@@ -243,6 +243,20 @@ int oracle_i8_element_form(uint32_t unit, int avx2, int pack_b, uint32_t K,
     return tail ? ORACLE_FORM_SCALAR : ORACLE_FORM_AVX2;
 }
 
+void oracle_i8_form_map(uint32_t unit, uint32_t M, uint32_t K, uint32_t N,
+                        uint32_t threads, uint32_t tile_m, uint32_t tile_n,
+                        int pack_b, int avx2, uint64_t l2_bytes, int32_t *forms)
+{
+    uint32_t tm, tn;
+    if (unit == 0) unit = 1;
+    oracle_i8_tile_geometry(unit, M, N, threads, tile_m, tile_n, pack_b,
+                            l2_bytes, &tm, &tn);
+    for (uint32_t m = 0; m < M; ++m)
+        for (uint32_t n = 0; n < N; ++n)
+            forms[(size_t)m * N + n] = oracle_i8_element_form(
+                unit, avx2, pack_b, K, M, N, tm, tn, m, n);
+}
+
 void oracle_matmul_i8_device(const int8_t *A, uint32_t lda, const int8_t *B,
                              const float *scale_a, const float *scale_b,
                              const float *bias, float *C, uint32_t ldc,

@@ -68,6 +68,11 @@ int oracle_i8_element_form(uint32_t unit, int avx2, int pack_b, uint32_t K,
                            uint32_t M, uint32_t N, uint32_t tm, uint32_t tn,
                            uint32_t m, uint32_t n);
 
+/* The form of every element (M x N int32, row-major) of the same product. */
+void oracle_i8_form_map(uint32_t unit, uint32_t M, uint32_t K, uint32_t N,
+                        uint32_t threads, uint32_t tile_m, uint32_t tile_n,
+                        int pack_b, int avx2, uint64_t l2_bytes, int32_t *forms);
+
 /* MATMUL_I8 exactly as the reference device described by threads /
  * tile_m, tile_n / pack_b / avx2 (0 = VNPU_FORCE_ISA=scalar) / l2_bytes
  * computes it with no flags: each element in its kernel's form.  unit 0

@@ -48,6 +48,8 @@ class Oracle:
                             u32, u32, u32, u32, u32, u32, u32, u32, C.c_int, C.c_int, u64)
         self._i8_geom = _sig(h, "oracle_i8_tile_geometry", None, u32, u32, u32, u32, u32, u32,
                              C.c_int, u64, C.POINTER(u32), C.POINTER(u32))
+        self._i8_map = _sig(h, "oracle_i8_form_map", None, u32, u32, u32, u32, u32, u32, u32,
+                            C.c_int, C.c_int, u64, vp)
         self._i8_form = _sig(h, "oracle_i8_element_form", C.c_int, u32, C.c_int, C.c_int, u32, u32,
                              u32, u32, u32, u32, u32)
         self.fast_expf = _sig(h, "oracle_fast_expf", f32, f32, C.c_int)
@@ -107,13 +109,29 @@ class Oracle:
     def i8_forms(self, M, K, N, unit=UNIT_VOODOO, threads=8, tiles=(128, 128, 64), pack_b=1,
                  avx2=1, l2_bytes=0) -> np.ndarray:
         """ORACLE form of every element of an M x K x N MATMUL_I8."""
-        unit = unit or UNIT_VOODOO
-        tm, tn = self.i8_tile_geometry(unit, M, N, threads, tiles, pack_b, l2_bytes)
         F = np.empty((M, N), np.int32)
-        for m in range(M):
-            for n in range(N):
-                F[m, n] = self._i8_form(unit, avx2, pack_b, K, M, N, tm, tn, m, n)
+        self._i8_map(unit, M, K, N, threads, tiles[0], tiles[2], pack_b, avx2, l2_bytes, ptr(F))
         return F
+
+    def matmul_i8_model(self, model, A, B, scale_a, scale_b, bias=None, epilogue=0, rows=None,
+                        n_full=0, col_base=0, unit=0) -> np.ndarray:
+        """Rows `rows` (all if None) of MATMUL_I8 as the reference device
+        `model` (a B200 device's vnpu_b200_reference_model_t) rounds them, for
+        a product whose output has n_full columns (0: B's) of which B holds
+        columns col_base.. ; the tile map is that of all M rows of A."""
+        M, K = A.shape
+        N = B.shape[1]
+        n_full = n_full or N
+        if model.epilogue_forced:
+            F = np.full((M, N), {0: 0, 1: 2, 2: 1}[model.epilogue_form], np.int32)
+        else:
+            F = self.i8_forms(M, K, n_full, unit, model.num_threads,
+                              (model.tile_m, model.tile_k, model.tile_n), model.pack_b,
+                              0 if model.scalar_isa else 1, model.l2_bytes)[:, col_base:col_base + N]
+        rows = np.arange(M) if rows is None else np.asarray(rows)
+        outs = [self.matmul_i8(A[rows], B, scale_a[rows] if scale_a is not None else None,
+                               scale_b, bias, epilogue, f).view(np.int32) for f in (0, 1, 2)]
+        return np.choose(F[rows], outs).view(np.float32)
 
     def matmul_f32(self, A, B, M, K, N, bias=None, C=None, lda=0, ldb=0, ldc=0, trans_a=0,
                    trans_b=0, alpha=1.0, beta=0.0, epilogue=0, unit=UNIT_VOODOO, tile_mask=None,

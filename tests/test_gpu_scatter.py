@@ -43,19 +43,28 @@ def test_scatter_matches_matmul(gpu, oracle, torch, M, K, N, ldd, col, epi, with
         Ad = torch.from_numpy(A).cuda()
         sad = torch.from_numpy(sa).cuda()
         bd = torch.from_numpy(bias).cuda() if with_bias else None
+        rows = np.arange(0, M, 7)
+        # one form forced for both: the scatter equals MATMUL_I8 of the shard
+        flags = vnpu.CMD_FLAG_EPI_BLOCK
         dsts = [torch.full((M, ldd), float("nan"), device="cuda") for _ in range(2)]
         torch.cuda.synchronize()
-        assert gpu.matmul_i8_scatter(Ad, w, sad, bd, dsts, M, K, N, ldd, col, epi) == vnpu.OK
+        assert gpu.matmul_i8_scatter(Ad, w, sad, bd, dsts, M, K, N, ldd, col, epi,
+                                     flags=flags) == vnpu.OK
         Cref = torch.full((M, N), float("nan"), device="cuda")
         torch.cuda.synchronize()
-        gpu.matmul_i8(Ad, w, sad, bd, Cref, M, K, N, epilogue=epi)
+        gpu.matmul_i8(Ad, w, sad, bd, Cref, M, K, N, epilogue=epi, flags=flags)
         ref = Cref.cpu().numpy()
         for d in dsts:
             h = d.cpu().numpy()
             assert bits_equal(h[:, col:col + N], ref)
             assert np.isnan(h[:, :col]).all() and np.isnan(h[:, col + N:]).all()
-        rows = np.arange(0, M, 7)
         assert bits_equal(ref[rows], oracle.matmul_i8(A[rows], B, sa[rows], sb, bias, epi, 0))
+        # no flags: the shard rounds as columns col.. of the ldd-wide product
+        assert gpu.matmul_i8_scatter(Ad, w, sad, bd, dsts[:1], M, K, N, ldd, col, epi) == vnpu.OK
+        got = dsts[0].cpu().numpy()[:, col:col + N]
+        want = oracle.matmul_i8_model(gpu.reference_model(), A, B, sa, sb, bias, epi, rows=rows,
+                                      n_full=ldd, col_base=col)
+        assert bits_equal(got[rows], want)
     finally:
         gpu.unpack(w)
 
