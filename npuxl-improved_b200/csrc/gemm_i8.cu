@@ -70,9 +70,8 @@ struct TcParams {
     uint32_t M = 0, N = 0, K = 0;
     uint32_t tiles_m = 0, tiles_n = 0, num_kb = 0;
     uint32_t group_m = 1;  // raster band height in m-tiles
-    uint32_t epilogue = 0;
-    FormMap fmap;          // rounding form of each element
-    uint32_t variant = 0;  // epi_variant(epilogue, bias != NULL, fmap.form)
+    uint32_t epilogue = 0, form = 0;
+    uint32_t variant = 0;  // epi_variant(epilogue, bias != NULL, form)
     uint32_t tma_store = 0;  // 1: C written by TMA from shared memory
     uint32_t *err = nullptr;
     uint64_t limit_ns = 2000000000ull;
@@ -154,55 +153,34 @@ __device__ __forceinline__ void dequant32_shfl_inplace(uint32_t (&r)[32], float 
     }
 }
 
-// kVariantMixed: each element's form from the form map (row m, columns n0..n0+31).
-__device__ __forceinline__ void dequant32_shfl_mixed(const TcParams &p, uint32_t m, uint32_t n0,
-                                                     const uint32_t (&r)[32], float (&v)[32],
-                                                     float sa, float s_lane, float b_lane) {
-    const bool has_bias = p.bias != nullptr;
-#pragma unroll 4
-    for (uint32_t j = 0; j < 32u; ++j) {
-        const float sb = __shfl_sync(0xffffffffu, s_lane, j);
-        const float bb = __shfl_sync(0xffffffffu, b_lane, j);
-        v[j] = ref_dequant(static_cast<int32_t>(r[j]), sa, sb, has_bias, bb, p.epilogue,
-                           form_at(p.fmap, m, n0 + j));
-    }
-}
-
-__device__ __forceinline__ void dequant32_shfl_any(const TcParams &p, uint32_t m, uint32_t n0,
-                                                   const uint32_t (&r)[32], float (&v)[32],
-                                                   float sa, float s_lane, float b_lane) {
-    switch (p.variant) {
+// One launch-constant form per tcgen05 GEMM launch: a command whose elements
+// take more than one form (FormMap kFormMixed) never reaches these kernels'
+// epilogues (matmul_i8_tcgen05 routes it to raw split-K sums and the finish
+// kernel, or to the SIMT kernel).
+__device__ __forceinline__ void dequant32_shfl_any(uint32_t variant, const uint32_t (&r)[32],
+                                                   float (&v)[32], float sa, float s_lane,
+                                                   float b_lane) {
+    switch (variant) {
 #define VNPU_B200_CASE(V)                                      \
     case V:                                                    \
         dequant32_shfl<V>(r, v, sa, s_lane, b_lane);           \
         break;
         VNPU_B200_EPI_VARIANTS(VNPU_B200_CASE)
 #undef VNPU_B200_CASE
-    case kVariantMixed:
-        dequant32_shfl_mixed(p, m, n0, r, v, sa, s_lane, b_lane);
-        break;
     default:
         break;
     }
 }
 
-__device__ __forceinline__ void dequant32_shfl_inplace_any(const TcParams &p, uint32_t m,
-                                                           uint32_t n0, uint32_t (&r)[32],
+__device__ __forceinline__ void dequant32_shfl_inplace_any(uint32_t variant, uint32_t (&r)[32],
                                                            float sa, float s_lane, float b_lane) {
-    switch (p.variant) {
+    switch (variant) {
 #define VNPU_B200_CASE(V)                                      \
     case V:                                                    \
         dequant32_shfl_inplace<V>(r, sa, s_lane, b_lane);      \
         break;
         VNPU_B200_EPI_VARIANTS(VNPU_B200_CASE)
 #undef VNPU_B200_CASE
-    case kVariantMixed: {
-        float v[32];
-        dequant32_shfl_mixed(p, m, n0, r, v, sa, s_lane, b_lane);
-#pragma unroll
-        for (uint32_t j = 0; j < 32u; ++j) r[j] = __float_as_uint(v[j]);
-        break;
-    }
     default:
         break;
     }
@@ -374,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t n0 = nb * kBN + c * 32u;
                 if (n0 >= p.N) continue;   // warp-uniform
                 float v[32];
-                dequant32_shfl_any(p, m, n0, r, v, sa, sreg[c], breg[c]);
+                dequant32_shfl_any(p.variant, r, v, sa, sreg[c], breg[c]);
                 if (row_ok) store_row32(v, crow, n0, p.N, vec_ok);
             }
             tc_fence_before();
@@ -625,7 +603,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
                 const uint32_t col = col_base + c * 32u;
                 const uint32_t n0 = nb * kPTileN + col;
                 if (n0 >= p.N || m_first >= p.M) continue;  // warp-uniform
-                if (p.splits == 1) dequant32_shfl_inplace_any(p, m, n0, rr[c], sa, sreg[c], breg[c]);
+                if (p.splits == 1) dequant32_shfl_inplace_any(p.variant, rr[c], sa, sreg[c], breg[c]);
                 const float(&v)[32] = reinterpret_cast<const float(&)[32]>(rr[c]);
                 if (p.ndst) {
                     // Scatter: the 32x32 chunk is transposed through the staging
@@ -1003,7 +981,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                     const uint32_t col = h * 256u + col_base + c * 32u;
                     const uint32_t n0 = nb * kWTileN + col;
                     if (n0 >= p.N || m_first >= p.M) continue;  // warp-uniform
-                    dequant32_shfl_inplace_any(p, m, n0, r[c], sa, sreg[h * 4u + c], breg[h * 4u + c]);
+                    dequant32_shfl_inplace_any(p.variant, r[c], sa, sreg[h * 4u + c], breg[h * 4u + c]);
                     const float(&v)[32] = reinterpret_cast<const float(&)[32]>(r[c]);
                     if (p.tma_store) {
                         if (lane == 0) bulk_wait_read0();  // previous store has read the buffer
@@ -1723,7 +1701,7 @@ cudaError_t matmul_i8_scatter(const LaunchCtx &ctx, const MatmulI8 &p) {
     int max_pairs = 0, max_wide_pairs = 0;
     cudaError_t se = device_setup(max_pairs, max_wide_pairs);
     if (se != cudaSuccess) return se;
-    if (!p.tmap_b128 || max_pairs <= 0) return cudaErrorNotSupported;
+    if (!p.tmap_b128 || max_pairs <= 0 || p.fmap.form == kFormMixed) return cudaErrorNotSupported;
     CUtensorMap tmap_a;
     if ((reinterpret_cast<uintptr_t>(p.A) % 16u) || (p.lda % 16u) ||
         !encode_tmap_kmajor_i8(&tmap_a, p.A, p.K, p.M, p.lda, kBK, 128))
@@ -1742,7 +1720,7 @@ cudaError_t matmul_i8_scatter(const LaunchCtx &ctx, const MatmulI8 &p) {
     tp.num_kb = (p.K + kBK - 1) / kBK;
     tp.group_m = raster_group(tp.tiles_m, kPTileM, p.K);
     tp.epilogue = p.epilogue;
-    tp.fmap = p.fmap;
+    tp.form = p.fmap.form;
     tp.variant = epi_variant(p.epilogue, p.bias != nullptr, p.fmap.form);
     tp.tma_store = 0;
     tp.err = ctx.err;
@@ -1807,6 +1785,9 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
     cudaError_t se = device_setup(max_pairs, max_wide_pairs);
     if (se != cudaSuccess) return se;
     if (!p.tmap_b) return cudaErrorInvalidValue;
+    // Elements in more than one rounding form: raw int32 sums split over K
+    // and the finish kernel's per-element epilogue, or the SIMT kernel.
+    const bool mixed = p.fmap.form == kFormMixed;
     // Pairs of CTAs (256x256 tiles) whenever M fills more than one 128-row
     // tile; the single-CTA 128x256 kernel otherwise.
     const bool use_pair = p.M > kBM && p.tmap_b128 && max_pairs > 0 &&
@@ -1841,6 +1822,7 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
                     200u * waves_w < speedup_pct * waves_p;
         if (const char *e = std::getenv("VNPU_B200_PAIR_WIDE"))
             wide = max_wide_pairs > 0 && e[0] == '1';
+        if (mixed) wide = false;
         tp.tiles_m = tiles_m;
         tp.tiles_n = (p.N + (wide ? kWTileN : kPTileN) - 1) / (wide ? kWTileN : kPTileN);
         tp.num_kb = (p.K + kBK - 1) / kBK;
@@ -1850,7 +1832,7 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         // (exact) and applies the epilogue.
         tp.group_m = raster_group(tp.tiles_m, kPTileM, p.K);
         tp.epilogue = p.epilogue;
-        tp.fmap = p.fmap;
+        tp.form = p.fmap.form;
         tp.variant = epi_variant(p.epilogue, p.bias != nullptr, p.fmap.form);
         tp.err = ctx.err;
         tp.limit_ns = ctx.wait_limit_ns;
@@ -1864,6 +1846,12 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
                 splits = (tp.num_kb + tp.kb_per_split - 1) / tp.kb_per_split;
             }
         }
+        if (mixed && splits == 1 && p.N % 4u == 0u && tp.num_kb >= 2u) {
+            tp.kb_per_split = (tp.num_kb + 1u) / 2u;
+            splits = (tp.num_kb + tp.kb_per_split - 1u) / tp.kb_per_split;
+        }
+        if (mixed && splits == 1)
+            return p.R ? cudaErrorNotSupported : matmul_i8_simt(ctx, p);
         if (splits > 1)   // every other field of tp is set above
             return matmul_i8_pair_splitk(ctx, p, tp, tmap_a, splits, static_cast<uint32_t>(max_pairs));
         if (p.R) return cudaErrorNotSupported;   // the residual rides on the split-K finish only
@@ -1896,6 +1884,7 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         return cudaGetLastError();
     }
     if (p.R) return cudaErrorNotSupported;
+    if (mixed) return matmul_i8_simt(ctx, p);
     CUtensorMap tmap_a;
     if (!encode_tmap_kmajor_i8(&tmap_a, p.A, p.K, p.M, p.lda, kBK, kBM))
         return cudaErrorInvalidValue;
@@ -1913,7 +1902,7 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
     tp.num_kb = (p.K + kBK - 1) / kBK;
     tp.group_m = raster_group(tp.tiles_m, kBM, p.K);
     tp.epilogue = p.epilogue;
-    tp.fmap = p.fmap;
+    tp.form = p.fmap.form;
     tp.variant = epi_variant(p.epilogue, p.bias != nullptr, p.fmap.form);
     tp.tma_store = 0;
     tp.err = ctx.err;
@@ -2011,8 +2000,16 @@ cudaError_t gemv_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
 cudaError_t matmul_i8_gemv(const LaunchCtx &ctx, const MatmulI8 &p) {
     const GvParams g = gv_params(p);
     const bool aligned = (reinterpret_cast<uintptr_t>(p.A) % 16u == 0u) && (p.lda % 16u == 0u);
+    // The shared-memory streaming kernel for every M <= 8 it takes;
+    // VNPU_B200_DECODE=tc|simt selects the tensor-core GEMV or the
+    // register-streaming SIMT GEMV instead (tests compare them).
+    const char *decode = std::getenv("VNPU_B200_DECODE");
+    if (!decode && !std::getenv("VNPU_B200_SIMT_GEMV") && gemv_bulk_supported(p)) {
+        g_last_kernel.store("gemv_i8_bulk_kernel", std::memory_order_relaxed);
+        return matmul_i8_gemv_bulk(ctx, p);
+    }
     bool use_tc = p.M > 2;
-    if (const char *e = std::getenv("VNPU_B200_DECODE")) use_tc = std::strcmp(e, "tc") == 0;
+    if (decode) use_tc = std::strcmp(decode, "tc") == 0;
     if (std::getenv("VNPU_B200_SIMT_GEMV")) use_tc = false;
     if (use_tc && aligned && p.K >= 16u && p.tmap_b128) {
         const cudaError_t e = gemv_tcgen05(ctx, p);
@@ -2034,6 +2031,11 @@ cudaError_t matmul_i8_gemv(const LaunchCtx &ctx, const MatmulI8 &p) {
 cudaError_t matmul_i8_gemv_residual(const LaunchCtx &ctx, const MatmulI8 &p, const float *R,
                                     uint32_t ldr) {
     if (p.M != 1) return cudaErrorInvalidValue;
+    if (!std::getenv("VNPU_B200_DECODE") && !std::getenv("VNPU_B200_SIMT_GEMV") &&
+        gemv_bulk_supported(p)) {
+        g_last_kernel.store("gemv_i8_bulk_kernel", std::memory_order_relaxed);
+        return matmul_i8_gemv_bulk(ctx, p, R, ldr);
+    }
     const GvParams g = gv_params(p);
     const bool aligned = (reinterpret_cast<uintptr_t>(p.A) % 16u == 0u) && (p.lda % 16u == 0u);
     const cudaError_t e = launch_gemv_m<1>(ctx, g, aligned, GvResidual{R, ldr});

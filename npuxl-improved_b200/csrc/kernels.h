@@ -112,6 +112,11 @@ const char *matmul_kernel_name(MatmulKernel k);
 const char *last_matmul_kernel();
 
 cudaError_t matmul_i8(const LaunchCtx &ctx, const MatmulI8 &p);
+// The M <= 8 GEMV streamed through shared memory by the TMA unit
+// (gemv_bulk.cu): TMA-aligned A, k_stride <= 12288.  R: C = R + out.
+bool gemv_bulk_supported(const MatmulI8 &p);
+cudaError_t matmul_i8_gemv_bulk(const LaunchCtx &ctx, const MatmulI8 &p, const float *R = nullptr,
+                                uint32_t ldr = 0);
 // Individual kernels (tests pin each against the oracle).
 cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p);
 cudaError_t matmul_i8_gemv(const LaunchCtx &ctx, const MatmulI8 &p);

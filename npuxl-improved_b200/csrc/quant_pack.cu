@@ -323,20 +323,26 @@ void noalloc_error(const char *what) {
     std::fprintf(stderr, "[vnpu-b200] vnpu_b200_quantize_i8_tensor_noalloc: %s\n", what);
 }
 
-// The scratch address of `device` (the current device).  Looked up once per
-// device; the first call also zeroes the counter synchronously.
+// The scratch address of `device` (the current device), resolved on every
+// call (cheap once the module is loaded).  When it differs from the one seen
+// before - the first call on the device, or a new context after
+// cudaDeviceReset reloaded the module - the counter is zeroed synchronously.
 vnpu_status_t noalloc_device(int device, NoAllocDevice *out) {
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
     NoAllocDevice &d = g_noalloc_dev[device];
-    if (!d.scratch) {
-        void *p = nullptr;
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_quant_noalloc_scratch) != cudaSuccess) {
+        cudaGetLastError();
+        noalloc_error("cannot resolve the static scratch on this device");
+        return VNPU_ERR_DEVICE_ERROR;
+    }
+    if (p != d.scratch) {
         int sms = 0;
-        if (cudaGetSymbolAddress(&p, g_quant_noalloc_scratch) != cudaSuccess ||
-            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
             cudaMemset(static_cast<uint32_t *>(p) + kNoAllocCounter, 0, sizeof(uint32_t)) !=
                 cudaSuccess) {
             cudaGetLastError();
-            noalloc_error("cannot resolve the static scratch on this device");
+            noalloc_error("cannot initialise the static scratch on this device");
             return VNPU_ERR_DEVICE_ERROR;
         }
         d.scratch = static_cast<uint32_t *>(p);
@@ -377,13 +383,24 @@ vnpu_status_t quantize_tensor_noalloc(int device, cudaStream_t stream, const flo
     NoAllocDevice d;
     const vnpu_status_t st = noalloc_device(device, &d);
     if (st != VNPU_OK) return st;
-    const uint64_t n = rows * cols;
+    uint64_t n = rows * cols;
     const unsigned chunks = static_cast<unsigned>((n + kNoAllocChunk - 1) / kNoAllocChunk);
-    tensor_absmax_chunks_kernel<<<chunks, 256, 0, stream>>>(X, n, d.scratch);
-    quantize_tensor_kernel<<<static_cast<unsigned>(d.num_sms) * 8, 256, 0, stream>>>(
-        X, Y, scale, n, d.scratch + kNoAllocResult);
-    if (cudaGetLastError() != cudaSuccess) {
+    // Launch errors come back from each launch itself, so an error the caller
+    // left pending on the thread is neither reported nor cleared here.  If the
+    // second launch fails the first one is already enqueued.
+    uint32_t *scratch = d.scratch;
+    void *absmax_args[] = {const_cast<float **>(&X), &n, &scratch};
+    if (cudaLaunchKernel(reinterpret_cast<const void *>(tensor_absmax_chunks_kernel), dim3(chunks),
+                         dim3(256), absmax_args, 0, stream) != cudaSuccess) {
         noalloc_error("kernel launch failed");
+        return VNPU_ERR_DEVICE_ERROR;
+    }
+    uint32_t *result = d.scratch + kNoAllocResult;
+    void *quant_args[] = {const_cast<float **>(&X), &Y, &scale, &n, &result};
+    if (cudaLaunchKernel(reinterpret_cast<const void *>(quantize_tensor_kernel),
+                         dim3(static_cast<unsigned>(d.num_sms) * 8), dim3(256), quant_args, 0,
+                         stream) != cudaSuccess) {
+        noalloc_error("kernel launch failed after the first of its two kernels was enqueued");
         return VNPU_ERR_DEVICE_ERROR;
     }
     return VNPU_OK;

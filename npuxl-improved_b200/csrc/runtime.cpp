@@ -609,6 +609,10 @@ void exec_matmul_i8_scatter(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_
     // product the reference device would compute
     p.fmap = i8_form_map(s->device, VNPU_UNIT_AUTO, flags, in.M, in.K, in.N, in.bias != nullptr,
                          in.epilogue, in.ldd, in.col_offset);
+    if (p.fmap.form == kFormMixed)
+        throw CommandError("matmul_i8_scatter: the reference device rounds this shard's elements "
+                           "in more than one form; submit MATMUL_I8 per shard or force one form "
+                           "with a VNPU_CMD_FLAG_EPI_* flag", VNPU_ERR_UNSUPPORTED);
     p.tmap_b = w->tmap_ok ? &w->tmap : nullptr;
     p.tmap_b128 = w->tmap128_ok ? &w->tmap128 : nullptr;
     for (uint32_t d = 0; d < in.ndst; ++d) p.dst[d] = in.dst[d];

@@ -141,3 +141,27 @@ def test_rejections(torch, noalloc):
     assert noalloc(0, st, host.ctypes.data, *ok[1:], 1, 16) == vnpu.ERR_INVALID_ARGUMENT
     torch.cuda.synchronize()
     assert float(s) == 0.0 and not Y.any()
+
+
+def test_allocates_no_device_memory(gpu, torch, noalloc):
+    """Device memory in use (the driver's count, which a cudaMalloc or a pool
+    growth of any library would change) and torch's allocator are the same
+    before and after calls made once the scratch is set up on the device."""
+    g = torch.Generator(device="cuda").manual_seed(9)
+    rows, cols = 300, 7 * CHUNK // 300 + 11
+    X = torch.empty(rows * cols, device="cuda").normal_(0, 3, generator=g)
+    Y = torch.empty(rows * cols, dtype=torch.int8, device="cuda")
+    s = torch.empty(1, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    assert noalloc(0, st, X.data_ptr(), Y.data_ptr(), s.data_ptr(), rows, cols) == vnpu.OK
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    torch0 = torch.cuda.memory_allocated()
+    for _ in range(3):
+        assert noalloc(0, st, X.data_ptr(), Y.data_ptr(), s.data_ptr(), rows, cols) == vnpu.OK
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    assert torch.cuda.memory_allocated() == torch0
+    Ye, se = _existing(gpu, torch, X, rows, cols)
+    assert torch.equal(Y, Ye) and bits_equal(s.cpu().numpy(), se.cpu().numpy())
