@@ -2000,13 +2000,13 @@ cudaError_t gemv_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
 cudaError_t matmul_i8_gemv(const LaunchCtx &ctx, const MatmulI8 &p) {
     const GvParams g = gv_params(p);
     const bool aligned = (reinterpret_cast<uintptr_t>(p.A) % 16u == 0u) && (p.lda % 16u == 0u);
-    // The shared-memory streaming kernel for every M <= 8 it takes;
+    // M <= 2: the shared-memory streaming GEMV where it takes the shape;
     // VNPU_B200_DECODE=tc|simt selects the tensor-core GEMV or the
     // register-streaming SIMT GEMV instead (tests compare them).
     const char *decode = std::getenv("VNPU_B200_DECODE");
-    if (!decode && !std::getenv("VNPU_B200_SIMT_GEMV") && gemv_bulk_supported(p)) {
-        g_last_kernel.store("gemv_i8_bulk_kernel", std::memory_order_relaxed);
-        return matmul_i8_gemv_bulk(ctx, p);
+    if (!decode && !std::getenv("VNPU_B200_SIMT_GEMV") && gemv_stream_supported(p, 1)) {
+        g_last_kernel.store("gemv_i8_stream_kernel", std::memory_order_relaxed);
+        return matmul_i8_gemv_stream(ctx, p);
     }
     bool use_tc = p.M > 2;
     if (decode) use_tc = std::strcmp(decode, "tc") == 0;
@@ -2032,9 +2032,9 @@ cudaError_t matmul_i8_gemv_residual(const LaunchCtx &ctx, const MatmulI8 &p, con
                                     uint32_t ldr) {
     if (p.M != 1) return cudaErrorInvalidValue;
     if (!std::getenv("VNPU_B200_DECODE") && !std::getenv("VNPU_B200_SIMT_GEMV") &&
-        gemv_bulk_supported(p)) {
-        g_last_kernel.store("gemv_i8_bulk_kernel", std::memory_order_relaxed);
-        return matmul_i8_gemv_bulk(ctx, p, R, ldr);
+        gemv_stream_supported(p, 1)) {
+        g_last_kernel.store("gemv_i8_stream_kernel", std::memory_order_relaxed);
+        return matmul_i8_gemv_stream(ctx, p, R, ldr);
     }
     const GvParams g = gv_params(p);
     const bool aligned = (reinterpret_cast<uintptr_t>(p.A) % 16u == 0u) && (p.lda % 16u == 0u);
@@ -2047,6 +2047,11 @@ cudaError_t qkv_rope_append_gemv(const LaunchCtx &ctx, const MatmulI8 &p, const 
     if (p.M != 1 || q.head_dim == 0 || (q.head_dim & 1u) || q.head_dim / 2 > kGvMaxPairs ||
         p.N != 3u * q.heads * q.head_dim)
         return cudaErrorInvalidValue;
+    if (!std::getenv("VNPU_B200_DECODE") && !std::getenv("VNPU_B200_SIMT_GEMV") &&
+        gemv_stream_supported(p, 2)) {
+        g_last_kernel.store("gemv_i8_stream_kernel", std::memory_order_relaxed);
+        return qkv_rope_append_gemv_stream(ctx, p, q);
+    }
     const GvParams g = gv_params(p);
     const bool aligned = (reinterpret_cast<uintptr_t>(p.A) % 16u == 0u) && (p.lda % 16u == 0u);
     GvQkv x;

@@ -1,0 +1,360 @@
+// gemv_stream.cu - MATMUL_I8 for M <= 2 (the decode GEMV) with each warp's
+// weight column landed in shared memory by cp.async before the programmatic
+// wait for the previous kernel.
+//
+// Bound: HBM.  A decode GEMV reads every weight byte once (K*N int8) plus a
+// few KB of activations, so its time is the weight stream plus fixed costs
+// per launch: the launch itself, the first DRAM round trip and the wait for
+// the previous kernel.  In a chain of kernels on one stream (programmatic
+// dependent launch, triggered at entry) this kernel's CTAs become resident
+// while the previous kernel still runs, and each warp issues the copies of
+// its whole column (k_stride bytes, 16 bytes a lane per cp.async) into its
+// own slice of shared memory at once: the weights do not depend on the
+// previous kernel, the activations and the output do.  A warp waits only for
+// the copies it issued itself, reads back only the chunks it copied
+// (k = lane * 16 + 512 j), multiplies them with the activation row(s) by
+// __dp4a (exact int32), reduces over its lanes and applies store_i8_c's
+// dequant epilogue (src/kernels/kernels.cpp:526-535) in the element's
+// reference form.  Shared memory rather than registers holds the prefetched
+// bytes, so the next kernel of the stream also fits beside this one.
+//
+// Epilogue variants: plain, residual (C = R + out, ADD_F32's rounding), and
+// the QKV projection of one token (VNPU_B200_OP_QKV_ROPE_APPEND), where a
+// warp owns the two columns of a rotation pair (j, j + D/2 of one head) so
+// lane 0 can rotate them as ROPE_F32 does and place them as KV_APPEND does.
+//
+// Measured alternatives (B200, 4096 x 4096, graph of 32 launches over 32
+// weight copies): registers as the landing buffer 3.6-4.0 us; a producer
+// warp feeding a ring of shared-memory stages (TMA cp.async.bulk or cp.async,
+// consumer warps splitting K) 11.5 us; L2 prefetch at entry then loads from
+// L2 4.2 us; a K split where each thread copies its own chunks of every
+// column of a CTA-wide range 4.5 us; this kernel 3.6 us with a bare store and
+// 3.95 us with the full dequant epilogue (the epilogue is on the critical
+// path of a chain of dependent kernels), against 3.96 us for the register-
+// streaming GEMV; at 4096 x 12288 / 4096 x 22016 10.2 / 15.9 us against
+// 10.9 / 16.1 us.  The activation chunks are read by plain batched loads and
+// the epilogue's scales and bias are fetched before the products: byte-wise
+// guarded loads and fetching them after cost 4.4 -> 3.95 us and 14.8 ->
+// 10.8 us at K = 11008.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <mutex>
+#include <type_traits>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace vnpu_b200 {
+
+namespace {
+
+constexpr uint32_t kGsWarps = 8;                      // warps (columns) per CTA
+constexpr uint32_t kGsThreads = kGsWarps * 32;
+constexpr uint32_t kGsMaxSmem = 200u * 1024u;         // largest shared slice set per CTA
+constexpr uint32_t kGsMaxPairs = 256;                 // head_dim / 2 of the QKV variant
+
+struct GsParams {
+    const int8_t *A;
+    uint32_t lda;
+    const int8_t *Bt;
+    uint32_t k_stride;
+    const float *scale_a;
+    const float *scale_b;
+    const float *bias;
+    float *C;
+    uint32_t ldc;
+    uint32_t M, K, N;
+    uint32_t epilogue;
+    FormMap fmap;
+};
+
+struct GsPlain {};
+struct GsResidual {
+    const float *R;
+    uint32_t ldr;
+};
+struct GsQkv {
+    float *Q, *Kout, *Vout, *Kc, *Vc, *mask;
+    const int32_t *position;
+    uint32_t *err;
+    uint32_t heads, D, cap, pos0;
+    float scaling;
+    float inv[kGsMaxPairs];   // 1 / theta^(2j/D), computed on the host like ROPE_F32
+};
+
+// 16 activation bytes of row m at k (zeros past K; the packed weights are zero there too).
+__device__ __forceinline__ int4 gs_act16(const GsParams &p, uint32_t m, uint32_t k) {
+    if (k >= p.K) return make_int4(0, 0, 0, 0);
+    const int8_t *row = p.A + static_cast<uint64_t>(m) * p.lda;
+    if (k + 16u <= p.K) return __ldg(reinterpret_cast<const int4 *>(row + k));
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (uint32_t b = 0; b < 16u; ++b)
+        if (k + b < p.K)
+            w[b >> 2] |= static_cast<uint32_t>(static_cast<uint8_t>(row[k + b])) << (8u * (b & 3u));
+    return make_int4(static_cast<int>(w[0]), static_cast<int>(w[1]), static_cast<int>(w[2]),
+                     static_cast<int>(w[3]));
+}
+
+// The rotation pair a warp of the QKV variant owns: section (Q, K, V), head,
+// index j < D/2, and the first column (the second is D/2 further).
+__device__ __forceinline__ void gs_qkv_pair(const GsQkv &x, uint32_t pair, uint32_t &sec,
+                                            uint32_t &h, uint32_t &j, uint32_t &n0) {
+    const uint32_t half = x.D / 2, per_sec = x.heads * half;
+    sec = pair / per_sec;
+    const uint32_t r = pair - sec * per_sec;
+    h = r / half;
+    j = r - h * half;
+    n0 = sec * x.heads * x.D + h * x.D + j;
+}
+
+// kC columns per warp (2 for the QKV variant), kM rows.  Dynamic shared
+// memory: kGsWarps * kC slices of k_stride bytes.
+template <int kM, int kC, typename Extra>
+__global__ void __launch_bounds__(kGsThreads) gemv_i8_stream_kernel(const GsParams p,
+                                                                   const Extra x) {
+    constexpr bool kQkv = std::is_same<Extra, GsQkv>::value;
+    static_assert(!kQkv || (kM == 1 && kC == 2), "the QKV epilogue is one token, column pairs");
+    extern __shared__ __align__(16) uint8_t gs_smem[];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint32_t ncol[kC];
+    bool warp_valid = true;
+    uint32_t q_sec = 0, q_h = 0, q_j = 0;
+    if constexpr (kQkv) {
+        const uint32_t pair = blockIdx.x * kGsWarps + warp;
+        warp_valid = pair < 3u * x.heads * (x.D / 2u);
+        uint32_t n0 = 0;
+        if (warp_valid) gs_qkv_pair(x, pair, q_sec, q_h, q_j, n0);
+        ncol[0] = n0;
+        ncol[1] = n0 + x.D / 2u;
+    } else {
+#pragma unroll
+        for (int c = 0; c < kC; ++c) ncol[c] = (blockIdx.x * kGsWarps + warp) * kC + c;
+    }
+    // Copy this warp's columns; every lane copies (and later reads) only its
+    // own 16-byte chunks, so no lane waits for another's data.
+    uint8_t *slice = gs_smem + static_cast<size_t>(warp) * kC * p.k_stride;
+#pragma unroll
+    for (int c = 0; c < kC; ++c) {
+        if (warp_valid && ncol[c] < p.N) {
+            const int8_t *src = p.Bt + static_cast<uint64_t>(ncol[c]) * p.k_stride;
+            for (uint32_t k = lane * 16u; k < p.k_stride; k += 512u)
+                cp_async_16(slice + c * p.k_stride + k, src + k);
+        }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    // The stream's next kernel may start now; the activations, the scales,
+    // the bias and C may belong to the previous one.
+    pdl_enter();
+    // Lane 0 fetches the epilogue's operands now, so their latency overlaps
+    // the products instead of following them.
+    const bool has_bias = p.bias != nullptr;
+    float e_sa[kM], e_sb[kC], e_bias[kC];
+    int32_t e_pos = 0;
+    if (lane == 0 && warp_valid) {
+#pragma unroll
+        for (int m = 0; m < kM; ++m) e_sa[m] = p.scale_a ? __ldg(p.scale_a + m) : 1.0f;
+#pragma unroll
+        for (int c = 0; c < kC; ++c) {
+            const uint32_t n = ncol[c] < p.N ? ncol[c] : 0u;
+            e_sb[c] = __ldg(p.scale_b + n);
+            e_bias[c] = has_bias ? __ldg(p.bias + n) : 0.0f;
+        }
+        if constexpr (kQkv) e_pos = x.position ? *x.position : static_cast<int32_t>(x.pos0);
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    int32_t acc[kC][kM];
+#pragma unroll
+    for (int c = 0; c < kC; ++c)
+#pragma unroll
+        for (int m = 0; m < kM; ++m) acc[c][m] = 0;
+    // Whole 16-byte chunks by plain loads the compiler can batch; the ragged
+    // chunk past the last multiple of 16 (if any) byte by byte.
+    const uint32_t k16 = p.K & ~15u;
+    auto mac = [&](const int4 (&a)[kM], uint32_t k) {
+#pragma unroll
+        for (int c = 0; c < kC; ++c) {
+            const int4 w = *reinterpret_cast<const int4 *>(slice + c * p.k_stride + k);
+#pragma unroll
+            for (int m = 0; m < kM; ++m) {
+                int s = acc[c][m];
+                s = __dp4a(a[m].x, w.x, s);
+                s = __dp4a(a[m].y, w.y, s);
+                s = __dp4a(a[m].z, w.z, s);
+                s = __dp4a(a[m].w, w.w, s);
+                acc[c][m] = s;
+            }
+        }
+    };
+#pragma unroll 4
+    for (uint32_t k = lane * 16u; k < k16; k += 512u) {
+        int4 a[kM];
+#pragma unroll
+        for (int m = 0; m < kM; ++m)
+            a[m] = __ldg(reinterpret_cast<const int4 *>(p.A + static_cast<uint64_t>(m) * p.lda + k));
+        mac(a, k);
+    }
+    if (k16 < p.K && lane == (k16 / 16u) % 32u) {
+        int4 a[kM];
+#pragma unroll
+        for (int m = 0; m < kM; ++m) a[m] = gs_act16(p, m, k16);
+        mac(a, k16);
+    }
+#pragma unroll
+    for (int c = 0; c < kC; ++c)
+#pragma unroll
+        for (int m = 0; m < kM; ++m)
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+                acc[c][m] += __shfl_xor_sync(0xffffffffu, acc[c][m], o);
+    if (lane != 0 || !warp_valid) return;
+    if constexpr (kQkv) {
+        // Both columns of the pair: dequantize as MATMUL_I8 would, rotate Q/K
+        // as ROPE_F32 does (src/kernels/llm.cpp:188-217), place as KV_APPEND.
+        float v[2];
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+            v[c] = ref_dequant(acc[c][0], e_sa[0], e_sb[c], has_bias, e_bias[c], p.epilogue,
+                               form_at(p.fmap, 0u, ncol[c]));
+        const int32_t pos = e_pos;
+        if (q_sec < 2) {
+            const float angle = __fmul_rn(__fmul_rn(static_cast<float>(pos), x.scaling), x.inv[q_j]);
+            float sn, cs;
+            sincosf(angle, &sn, &cs);
+            const float x0 = v[0], x1 = v[1];
+            v[0] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+            v[1] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+        }
+        const uint64_t row = static_cast<uint64_t>(q_h) * x.D + q_j;   // [h][t = 0][j]
+        const uint32_t half = x.D / 2;
+        if (q_sec == 0) {
+            x.Q[row] = v[0];
+            x.Q[row + half] = v[1];
+            return;
+        }
+        float *out = q_sec == 1 ? x.Kout : x.Vout;
+        if (out) {
+            out[row] = v[0];
+            out[row + half] = v[1];
+        }
+        if (pos < 0 || static_cast<uint32_t>(pos) >= x.cap) {
+            if (q_sec == 1 && q_j == 0) record_error(x.err, kErrBadConfig);
+            return;
+        }
+        const uint64_t slot = (static_cast<uint64_t>(q_h) * x.cap + static_cast<uint32_t>(pos)) * x.D + q_j;
+        float *cache = q_sec == 1 ? x.Kc : x.Vc;
+        cache[slot] = v[0];
+        cache[slot + half] = v[1];
+        if (q_sec == 1 && q_j == 0 && x.mask)
+            x.mask[static_cast<uint64_t>(q_h) * x.cap + static_cast<uint32_t>(pos)] = 0.0f;
+        return;
+    } else {
+#pragma unroll
+        for (int c = 0; c < kC; ++c) {
+            const uint32_t n = ncol[c];
+            if (n >= p.N) continue;
+#pragma unroll
+            for (int m = 0; m < kM; ++m) {
+                float out = ref_dequant(acc[c][m], e_sa[m], e_sb[c], has_bias, e_bias[c],
+                                        p.epilogue, form_at(p.fmap, static_cast<uint32_t>(m), n));
+                if constexpr (std::is_same<Extra, GsResidual>::value)
+                    out = __fadd_rn(x.R[static_cast<uint64_t>(m) * x.ldr + n], out);
+                p.C[static_cast<uint64_t>(m) * p.ldc + n] = out;
+            }
+        }
+    }
+}
+
+template <int kM, int kC, typename Extra>
+cudaError_t gs_launch(const LaunchCtx &ctx, const GsParams &g, uint32_t grid, const Extra &x) {
+    static std::mutex mu;
+    static bool opted[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
+    {
+        std::lock_guard<std::mutex> l(mu);
+        if (dev < 0 || dev >= 64 || !opted[dev]) {
+            const cudaError_t e = cudaFuncSetAttribute(gemv_i8_stream_kernel<kM, kC, Extra>,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       static_cast<int>(kGsMaxSmem));
+            if (e != cudaSuccess) return e;
+            if (dev >= 0 && dev < 64) opted[dev] = true;
+        }
+    }
+    const uint32_t smem = kGsWarps * kC * g.k_stride;
+    if (ctx.launch_counter) ++*ctx.launch_counter;
+    return launch_pdl(ctx.stream, gemv_i8_stream_kernel<kM, kC, Extra>, dim3(grid),
+                      dim3(kGsThreads), smem, g, x);
+}
+
+GsParams gs_params(const MatmulI8 &p) {
+    GsParams g;
+    g.A = p.A;
+    g.lda = p.lda;
+    g.Bt = p.Bt;
+    g.k_stride = p.k_stride;
+    g.scale_a = p.scale_a;
+    g.scale_b = p.scale_b;
+    g.bias = p.bias;
+    g.C = p.C;
+    g.ldc = p.ldc;
+    g.M = p.M;
+    g.K = p.K;
+    g.N = p.N;
+    g.epilogue = p.epilogue;
+    g.fmap = p.fmap;
+    return g;
+}
+
+}  // namespace
+
+// K up to 8192: past that (e.g. 11008, 88 KiB of columns per CTA, two CTAs
+// per SM) the register-streaming GEMV measured faster (9.9 against 10.7 us
+// at 11008 x 4096).
+bool gemv_stream_supported(const MatmulI8 &p, uint32_t cols_per_warp) {
+    return p.M >= 1 && p.M <= 2 && p.K >= 1 && p.k_stride <= 8192u && p.k_stride % 16u == 0u &&
+           static_cast<uint64_t>(kGsWarps) * cols_per_warp * p.k_stride <= kGsMaxSmem &&
+           (reinterpret_cast<uintptr_t>(p.A) % 16u) == 0u && p.lda % 16u == 0u &&
+           (reinterpret_cast<uintptr_t>(p.Bt) % 16u) == 0u;
+}
+
+cudaError_t matmul_i8_gemv_stream(const LaunchCtx &ctx, const MatmulI8 &p, const float *R,
+                                  uint32_t ldr) {
+    if (!gemv_stream_supported(p, 1)) return cudaErrorInvalidValue;
+    const GsParams g = gs_params(p);
+    const uint32_t grid = (p.N + kGsWarps - 1) / kGsWarps;
+    if (R) {
+        const GsResidual x{R, ldr};
+        return p.M == 1 ? gs_launch<1, 1>(ctx, g, grid, x) : gs_launch<2, 1>(ctx, g, grid, x);
+    }
+    return p.M == 1 ? gs_launch<1, 1>(ctx, g, grid, GsPlain{})
+                    : gs_launch<2, 1>(ctx, g, grid, GsPlain{});
+}
+
+cudaError_t qkv_rope_append_gemv_stream(const LaunchCtx &ctx, const MatmulI8 &p,
+                                        const QkvRope &q) {
+    if (p.M != 1 || q.head_dim == 0 || (q.head_dim & 1u) || q.head_dim / 2 > kGsMaxPairs ||
+        p.N != 3u * q.heads * q.head_dim || !gemv_stream_supported(p, 2))
+        return cudaErrorInvalidValue;
+    GsQkv x;
+    x.Q = q.Q;
+    x.Kout = q.K_out;
+    x.Vout = q.V_out;
+    x.Kc = q.K_cache;
+    x.Vc = q.V_cache;
+    x.mask = q.mask;
+    x.position = q.position;
+    x.err = ctx.err;
+    x.heads = q.heads;
+    x.D = q.head_dim;
+    x.cap = q.capacity;
+    x.pos0 = q.position_offset;
+    x.scaling = q.scaling;
+    for (uint32_t j = 0; j < q.head_dim / 2; ++j) x.inv[j] = q.inv_freq[j];
+    const uint32_t pairs = 3u * q.heads * (q.head_dim / 2u);
+    return gs_launch<1, 2>(ctx, gs_params(p), (pairs + kGsWarps - 1) / kGsWarps, x);
+}
+
+}  // namespace vnpu_b200

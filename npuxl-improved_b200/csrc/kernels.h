@@ -112,11 +112,14 @@ const char *matmul_kernel_name(MatmulKernel k);
 const char *last_matmul_kernel();
 
 cudaError_t matmul_i8(const LaunchCtx &ctx, const MatmulI8 &p);
-// The M <= 8 GEMV streamed through shared memory by the TMA unit
-// (gemv_bulk.cu): TMA-aligned A, k_stride <= 12288.  R: C = R + out.
-bool gemv_bulk_supported(const MatmulI8 &p);
-cudaError_t matmul_i8_gemv_bulk(const LaunchCtx &ctx, const MatmulI8 &p, const float *R = nullptr,
-                                uint32_t ldr = 0);
+// The M <= 2 GEMV with each warp's column landed in shared memory before the
+// programmatic wait (gemv_stream.cu): 16-byte aligned A and lda, 8 x
+// cols_per_warp x k_stride bytes of shared memory per CTA (<= 200 KiB).
+// R: C = R + out.
+bool gemv_stream_supported(const MatmulI8 &p, uint32_t cols_per_warp);
+cudaError_t matmul_i8_gemv_stream(const LaunchCtx &ctx, const MatmulI8 &p, const float *R = nullptr,
+                                  uint32_t ldr = 0);
+
 // Individual kernels (tests pin each against the oracle).
 cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p);
 cudaError_t matmul_i8_gemv(const LaunchCtx &ctx, const MatmulI8 &p);
@@ -147,6 +150,8 @@ struct QkvRope {
 };
 // One token (M = 1): the streaming GEMV with the rotation pairs in one warp.
 cudaError_t qkv_rope_append_gemv(const LaunchCtx &ctx, const MatmulI8 &p, const QkvRope &q);
+// The same on the shared-memory streaming GEMV (gemv_stream.cu).
+cudaError_t qkv_rope_append_gemv_stream(const LaunchCtx &ctx, const MatmulI8 &p, const QkvRope &q);
 // Any T: C is the MATMUL_I8 output [T][3*heads*head_dim] already computed.
 cudaError_t qkv_split_rope_append(const LaunchCtx &ctx, const float *C, uint32_t T,
                                   const QkvRope &q);

@@ -683,24 +683,22 @@ def test_fused_prologues_any_cluster_size(gpu, oracle, monkeypatch, csize):
     monkeypatch.delenv("VNPU_B200_FUSED_CLUSTER", raising=False)
 
 
-@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 6, 7, 8])
+@pytest.mark.parametrize("M", [1, 2, 3, 8])
 @pytest.mark.parametrize("K,N", [(4096, 4096), (11008, 4096), (4096, 11008), (100, 300),
                                  (16, 128), (1000, 1000), (130, 12288), (12288, 130), (20, 5),
-                                 (8192, 300), (4096, 147)])
-def test_decode_bulk_kernel_agrees(gpu, oracle, monkeypatch, M, K, N):
-    """The shared-memory streaming GEMV (TMA bulk copies into a ring, K split
-    over eight warps, butterfly reduction) gives the bits of the tensor-core
-    GEMV, the register-streaming GEMV and the oracle, with bias, for every
-    M <= 8 and K / N shapes with ragged tails, fewer columns than SMs and
-    more K than one pass of the warps covers."""
+                                 (8192, 300), (4096, 147), (30000, 64)])
+def test_decode_stream_kernel_agrees(gpu, oracle, monkeypatch, M, K, N):
+    """The M <= 2 shared-memory streaming GEMV (each warp lands its column in
+    shared memory before the programmatic wait) gives the bits of the
+    tensor-core GEMV, the register-streaming GEMV and the oracle, with bias,
+    for K / N shapes with ragged tails, fewer columns than a CTA covers and K
+    too long for its shared memory (which takes the register kernel)."""
     rng = np.random.default_rng(M * 7919 + K * 13 + N)
     A, sa = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
     B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
     bias = rng.normal(0, 0.01, N).astype(np.float32)
     outs = {}
-    if not os.environ.get("VNPU_B200_GEMV_BULK"):
-        pytest.skip("the shared-memory streaming GEMV is opt-in (VNPU_B200_GEMV_BULK=1)")
-    for mode in ("bulk", "tc", "simt"):
+    for mode in ("default", "tc", "simt"):
         monkeypatch.delenv("VNPU_B200_DECODE", raising=False)
         monkeypatch.delenv("VNPU_B200_SIMT_GEMV", raising=False)
         if mode == "tc":
@@ -709,9 +707,10 @@ def test_decode_bulk_kernel_agrees(gpu, oracle, monkeypatch, M, K, N):
             monkeypatch.setenv("VNPU_B200_SIMT_GEMV", "1")
         outs[mode] = run_matmul(gpu, A, B, sa, sb, bias, 2, 2)
         kernel = gpu.lib.b200_last_matmul_kernel().decode()
-        if mode == "bulk":
-            bulk_ok = K <= (4096 if M > 4 else 12288) and K % 16 == 0   # lda = K, TMA-aligned
-            assert (kernel == "gemv_i8_bulk_kernel") == bulk_ok, kernel
+        if mode == "default" and M <= 2:
+            k_stride = -(-K // 128) * 128
+            stream_ok = K % 16 == 0 and k_stride <= 8192
+            assert (kernel == "gemv_i8_stream_kernel") == stream_ok, kernel
     monkeypatch.delenv("VNPU_B200_DECODE", raising=False)
     monkeypatch.delenv("VNPU_B200_SIMT_GEMV", raising=False)
     want = oracle.matmul_i8(A, B, sa, sb, bias, 2, 2)
@@ -719,9 +718,9 @@ def test_decode_bulk_kernel_agrees(gpu, oracle, monkeypatch, M, K, N):
         assert bits_equal(C, want), (mode, ulp_diff(C, want))
 
 
-def test_decode_bulk_kernel_residual(gpu, oracle, monkeypatch):
-    """MATMUL_I8_RESIDUAL at M = 1 on the streaming GEMV: C = R + out with
-    ADD_F32's single rounding, equal to the register-streaming GEMV's."""
+def test_decode_stream_kernel_residual(gpu, oracle, monkeypatch):
+    """MATMUL_I8_RESIDUAL at M = 1 on the shared-memory streaming GEMV: C = R +
+    out with ADD_F32's single rounding, equal to the register-streaming GEMV's."""
     torch = pytest.importorskip("torch")
     rng = np.random.default_rng(5)
     for K, N in ((4096, 4096), (11008, 4096), (300, 1000)):
