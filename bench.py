@@ -128,9 +128,13 @@ class ClockSampler:
 # ===========================================================================
 # CPU reference arm / baseline
 # ===========================================================================
-def reference_sample(rows: int, steps: int, warmup: int, threads: int):
-    """Time QUANTIZE_I8 + MATMUL_I8 of `rows` rows of the workload on the
-    reference's CPU implementation (host buffers, its own thread pool)."""
+def reference_sample(rows: int, steps: int, warmup: int, threads: int, A=None, B8=None, sb=None):
+    """Time QUANTIZE_I8 and MATMUL_I8 (each separately) of `rows` rows of the
+    workload on the reference's CPU implementation (host buffers, its own
+    thread pool).  A (rows x K f32) and the weights B8 (K x N int8, per-column
+    scales sb) may be given (the GPU arm passes its own, to check its rows);
+    otherwise they are drawn with the workload's distributions.  Returns the
+    timings and the sample's output rows."""
     if os.path.exists(REF_LIB):
         lib, kind = vnpu.Lib(REF_LIB), "reference"
         os.environ.setdefault("VNPU_FORCE_ISA", "avx2")
@@ -138,48 +142,61 @@ def reference_sample(rows: int, steps: int, warmup: int, threads: int):
         lib, kind = None, "port"
     rng = np.random.default_rng(1)
     n = N_TOTAL
-    Bf = rng.normal(0, 0.02, (K_TOTAL, n)).astype(np.float32)
-    A = rng.uniform(-1, 1, (rows, K_TOTAL)).astype(np.float32)
+    if A is None:
+        A = rng.uniform(-1, 1, (rows, K_TOTAL)).astype(np.float32)
     if lib is None:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         from vnpu_oracle import Oracle
         orc = Oracle(ORACLE_LIB)
-        B8, sb = orc.quantize(Bf, 1)
-        del Bf
-        times = []
+        if B8 is None:
+            B8, sb = orc.quantize(rng.normal(0, 0.02, (K_TOTAL, n)).astype(np.float32), 1)
+        tq, tm = [], []
         for i in range(warmup + steps):
             t0 = time.perf_counter()
             A8, sa = orc.quantize(A, 0)
-            orc.matmul_i8(A8, B8, sa, sb, None, 0, 0)
+            t1 = time.perf_counter()
+            Cout = orc.matmul_i8(A8, B8, sa, sb, None, 0, 0)
+            t2 = time.perf_counter()
             if i >= warmup:
-                times.append(time.perf_counter() - t0)
+                tq.append(t1 - t0)
+                tm.append(t2 - t1)
         cores = 1
     else:
         dev = vnpu.Device(lib, num_threads=threads)
-        B8 = np.empty((K_TOTAL, n), np.int8)
-        sb = np.empty(n, np.float32)
-        dev.quantize_i8(Bf, B8, sb, K_TOTAL, n, vnpu.QUANT_PER_COLUMN)
-        del Bf
+        if B8 is None:
+            Bf = rng.normal(0, 0.02, (K_TOTAL, n)).astype(np.float32)
+            B8 = np.empty((K_TOTAL, n), np.int8)
+            sb = np.empty(n, np.float32)
+            dev.quantize_i8(Bf, B8, sb, K_TOTAL, n, vnpu.QUANT_PER_COLUMN)
+            del Bf
         w = dev.pack(B8, sb, K_TOTAL, n)
         A8 = np.empty((rows, K_TOTAL), np.int8)
         sa = np.empty(rows, np.float32)
         Cout = np.empty((rows, n), np.float32)
-        times = []
+        tq, tm = [], []
         for i in range(warmup + steps):
             t0 = time.perf_counter()
             dev.quantize_i8(A, A8, sa, rows, K_TOTAL, vnpu.QUANT_PER_ROW)
+            t1 = time.perf_counter()
             dev.matmul_i8(A8, w, sa, None, Cout, rows, K_TOTAL, n, unit=vnpu.UNIT_VOODOO)
+            t2 = time.perf_counter()
             if i >= warmup:
-                times.append(time.perf_counter() - t0)
+                tq.append(t1 - t0)
+                tm.append(t2 - t1)
         cores = dev.info().num_threads
         dev.unpack(w)
         dev.close()
-    t = statistics.median(times)
+    q, m = statistics.median(tq), statistics.median(tm)
+    t = q + m
     ops = 2.0 * rows * K_TOTAL * n
     return {"value": ops / t / 1e12, "unit": "TOPS", "cores": cores, "kind": kind,
             "sample": f"{rows} rows of A ({rows}x{K_TOTAL}x{n}, quantize+matmul, host buffers), "
-                      f"median of {len(times)} steps, {t:.3f} s/step",
-            "seconds_per_step": t}
+                      f"median of {len(tq)} steps, {t:.3f} s/step",
+            "seconds_per_step": t,
+            "quantize_i8": {"seconds": q, "gbs": 5.0 * rows * K_TOTAL / q / 1e9,
+                            "bytes": 5 * rows * K_TOTAL},
+            "matmul_i8": {"seconds": m, "tops": ops / m / 1e12},
+            "C": Cout}
 
 
 def run_reference(args):
@@ -197,7 +214,8 @@ def run_reference(args):
         "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "config": {"workload": WORKLOAD, "sample_rows": rows, "M": M_TOTAL, "K": K_TOTAL,
                    "N": N_TOTAL, "isa": os.environ.get("VNPU_FORCE_ISA", "port")},
-        "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample",
+                                           "quantize_i8", "matmul_i8")},
         "e2e": {"value": r["value"], "unit": "TOPS", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -266,8 +284,9 @@ def time_loop(lib, dev, st, cmds, iters):
     return e0.elapsed_time(e1) / iters
 
 
-def make_weights(lib, dev, torch, K, N, seed, shard=None):
-    """f32 N(0,0.02) weights -> QUANTIZE_I8 per column on the GPU -> pack."""
+def make_weights(lib, dev, torch, K, N, seed, shard=None, keep_int8=False):
+    """f32 N(0,0.02) weights -> QUANTIZE_I8 per column on the GPU -> pack.
+    keep_int8: also return the K x N int8 matrix (a 4th value)."""
     g = torch.Generator(device="cuda").manual_seed(seed)
     n0, n1 = shard if shard else (0, N)
     Bf = torch.empty((K, N), device="cuda").normal_(0, 0.02, generator=g)[:, n0:n1].contiguous()
@@ -277,7 +296,10 @@ def make_weights(lib, dev, torch, K, N, seed, shard=None):
     torch.cuda.synchronize()
     dev.quantize_i8(Bf.data_ptr(), B8.data_ptr(), sb.data_ptr(), K, n, vnpu.QUANT_PER_COLUMN)
     w = dev.pack(B8.data_ptr(), sb.data_ptr(), K, n)
-    del Bf, B8
+    del Bf
+    if keep_int8:
+        return w, sb, n, B8
+    del B8
     return w, sb, n
 
 
@@ -507,9 +529,9 @@ def run_b200(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+        from shard import VNPU_OK, join_group
+        if join_group("nccl", rank, world, 300.0, device_id=torch.device("cuda", local)) != VNPU_OK:
+            raise SystemExit(f"rank {rank}: not every rank joined within 300 s")
     lib = vnpu.Lib(vnpu.LIB_PATH)
     dev = vnpu.Device(lib, ordinal=local)
     st = Stream(lib, dev)
@@ -517,7 +539,9 @@ def run_b200(args):
 
     M, K = M_TOTAL, K_TOTAL
     n0, n1 = column_shard(N_TOTAL, world, rank)
-    w, sb, n = make_weights(lib, dev, torch, K, N_TOTAL, seed=1, shard=(n0, n1))
+    w, sb, n, *kept = make_weights(lib, dev, torch, K, N_TOTAL, seed=1, shard=(n0, n1),
+                                   keep_int8=world == 1)
+    B8_dev = kept[0] if kept else None
     g = torch.Generator(device="cuda").manual_seed(0)
     Af = torch.empty((M, K), device="cuda").uniform_(-1, 1, generator=g)
     A8 = torch.empty((M, K), dtype=torch.int8, device="cuda")
@@ -617,8 +641,10 @@ def run_b200(args):
     # ---- all-gather of the shards over NCCL (config 5's collective)
     allgather = None
     if world > 1:
-        shard_pad = torch.zeros((M, -(-N_TOTAL // world // 256) * 256 + 256), device="cuda")
-        width = shard_pad.shape[1]
+        # shard-major [P][M][width]: width = the widest shard (all shards are
+        # equal when N / P is a multiple of 256, as here: no padding)
+        width = max(b - a for a, b in (column_shard(N_TOTAL, world, r) for r in range(world)))
+        shard_pad = torch.zeros((M, width), device="cuda")
         shard_pad[:, :n] = Cm
         gathered = torch.empty((world, M, width), device="cuda")
         dist.all_gather_into_tensor(gathered, shard_pad)
@@ -691,6 +717,12 @@ def run_b200(args):
         ms_fused = max_over_ranks(f0.elapsed_time(f1) / reps)
         allgather["fused"] = {
             "ms_gemm_plus_gather": ms_fused, "ms_separate": ms_gemm + ms_ag,
+            "tops_whole_job": 2.0 * M * K * N_TOTAL / ms_fused / 1e9,
+            "bound": ("NVLink: every rank receives (P-1)/P of the f32 output, "
+                      f"{(world - 1) * M * N_TOTAL * 4 / world / 1e6:.0f} MB, "
+                      f"{(world - 1) * M * N_TOTAL * 4 / world / 770e9 * 1e3:.3f} ms at the measured "
+                      "770 GB/s per direction, against the GEMM's "
+                      f"{ms_gemm:.3f} ms"),
             "speedup_vs_separate": (ms_gemm + ms_ag) / ms_fused, "bit_identical_to_nccl": same,
             "path": "VNPU_B200_OP_MATMUL_I8_SCATTER into every rank's full output over CUDA IPC, "
                     "then a one-element NCCL all-reduce as the barrier"}
@@ -738,9 +770,17 @@ def run_b200(args):
             except Exception as exc:  # library comparator only
                 secondary["cublas_int8_8192_cube_tops"] = f"unavailable: {exc}"
         if world == 1 and not args.no_cpu_baseline:
-            r = reference_sample(int(os.environ.get("VNPU_BENCH_REF_ROWS", "32")), 3, 1,
-                                 os.cpu_count() or 1)
-            cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            # The CPU implementation on the first rows of the very inputs the
+            # timed steps used (A f32, the int8 weights and scales): its rows
+            # must be the GPU's C bit for bit.
+            rows = int(os.environ.get("VNPU_BENCH_REF_ROWS", "32"))
+            r = reference_sample(rows, 3, 1, os.cpu_count() or 1, A=Af[:rows].cpu().numpy(),
+                                 B8=B8_dev.cpu().numpy(), sb=sb.cpu().numpy())
+            cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample", "quantize_i8",
+                                     "matmul_i8")}
+            gpu_rows = Cm[:rows].cpu().numpy()
+            cpu["check"] = {"rows": rows, "bit_exact_vs_gpu_C": bool(np.array_equal(
+                gpu_rows.view(np.uint32), r["C"].view(np.uint32)))}
         total_ops = 2.0 * M * K * N_TOTAL
         out = {
             "metric": METRIC, "value": total_ops / ms_step / 1e9, "unit": "TOPS",

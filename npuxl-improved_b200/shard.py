@@ -34,3 +34,40 @@ def gathered_to_row_major(shards, m: int) -> "list":
     import numpy as np
 
     return np.concatenate([np.asarray(s).reshape(m, -1) for s in shards], axis=1)
+
+
+# Status codes of include/vnpu.h returned by join_group.
+VNPU_OK = 0
+VNPU_ERR_TIMEOUT = -7
+
+
+def join_group(backend: str, rank: int, world: int, timeout_s: float,
+               device_id=None) -> int:
+    """Join the process group of the column-sharded GEMM within a deadline.
+
+    A rank that never joins (a crashed or hung peer) would otherwise leave the
+    others blocked in the rendezvous or in their first collective.  The join
+    and a first barrier must both finish within ``timeout_s`` seconds (the
+    process group's own timeout, which also bounds every later collective);
+    otherwise the group is torn down and ``VNPU_ERR_TIMEOUT`` is returned, as
+    the reference reports a wait that ran out (include/vnpu.h, vnpu_event_wait).
+    Returns ``VNPU_OK`` when every rank has joined.
+    """
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    kwargs = {"timeout": timedelta(seconds=timeout_s)}
+    if device_id is not None:
+        kwargs["device_id"] = device_id
+    try:
+        dist.init_process_group(backend, rank=rank, world_size=world, **kwargs)
+        dist.barrier()
+        return VNPU_OK
+    except (RuntimeError, TimeoutError, ValueError) as exc:   # rendezvous or barrier ran out
+        if "timeout" not in str(exc).lower() and "timed out" not in str(exc).lower() \
+                and not isinstance(exc, TimeoutError):
+            raise
+        if dist.is_initialized():
+            dist.destroy_process_group()
+        return VNPU_ERR_TIMEOUT

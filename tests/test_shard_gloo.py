@@ -142,3 +142,74 @@ def test_two_rank_row_slice_quantize_and_scatter_layout():
     results = dict(q.get(timeout=5) for _ in range(2))
     assert results == {0: True, 1: True}
     assert all(p.exitcode == 0 for p in procs)
+
+
+def _join_main(rank, world, port, q, timeout_s):
+    import time
+
+    from shard import join_group
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    if rank == world - 1:
+        time.sleep(3600)          # this rank never joins; the test kills it
+        return
+    t0 = time.monotonic()
+    rc = join_group("gloo", rank, world, timeout_s)
+    q.put((rank, rc, time.monotonic() - t0))
+
+
+def test_rank_that_never_joins_times_out():
+    """SURVEY-listed failure case on CPU ranks: one of three ranks never joins
+    the group.  The others get VNPU_ERR_TIMEOUT once the deadline passes
+    instead of blocking; no GPU is involved."""
+    import multiprocessing as mp
+
+    from shard import VNPU_ERR_TIMEOUT
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    world, timeout_s = 3, 4.0
+    procs = [ctx.Process(target=_join_main, args=(r, world, port, q, timeout_s))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        results = [q.get(timeout=120) for _ in range(world - 1)]
+    finally:
+        procs[-1].kill()
+        for p in procs:
+            p.join(timeout=30)
+    for rank, rc, elapsed in results:
+        assert rc == VNPU_ERR_TIMEOUT, (rank, rc)
+        assert elapsed < timeout_s * 10, (rank, elapsed)
+
+
+def test_all_ranks_join():
+    import multiprocessing as mp
+
+    from shard import VNPU_OK
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+
+    procs = [ctx.Process(target=_join_ok_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=30)
+    assert all(rc == VNPU_OK for _, rc in results)
+
+
+def _join_ok_main(rank, world, port, q):
+    import torch.distributed as dist
+
+    from shard import join_group
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    rc = join_group("gloo", rank, world, 30.0)
+    q.put((rank, rc))
+    if dist.is_initialized():
+        dist.destroy_process_group()
