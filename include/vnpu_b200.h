@@ -232,6 +232,61 @@ typedef struct vnpu_b200_matmul_i8_residual_args_t {
     uint32_t reserved0;
 } vnpu_b200_matmul_i8_residual_args_t;
 
+/*
+ * MATMUL_I8 of one column shard of a wider product (no reference
+ * counterpart; the reference has no int8 multi-device split).  B holds the
+ * shard's N columns, which are columns col_base .. col_base + N - 1 of an
+ * M x K x n_full product; C receives the shard (M x N, row stride ldc).
+ * Every element is rounded in the form the reference device gives that
+ * element of the whole n_full-wide product, so shards assembled side by side
+ * are the bits of one MATMUL_I8 of the whole weight.  bias holds the shard's
+ * N entries.  n_full = 0 means N (a whole product).
+ */
+#define VNPU_B200_OP_MATMUL_I8_SHARD  0x106u
+
+typedef struct vnpu_b200_matmul_i8_shard_args_t {
+    const int8_t *A;
+    vnpu_packed_weights_t *B;
+    const float *scale_a;
+    const float *bias;
+    float *C;
+    uint32_t M;
+    uint32_t K;
+    uint32_t N;
+    uint32_t lda;       /* 0 = K */
+    uint32_t ldc;       /* 0 = N */
+    uint32_t epilogue;
+    uint32_t n_full;    /* columns of the whole product (0 = N) */
+    uint32_t col_base;  /* whole-product column of the shard's column 0 */
+} vnpu_b200_matmul_i8_shard_args_t;
+
+/*
+ * Column-sharded int8 GEMM over a local cluster's devices (no reference
+ * counterpart: the reference's cluster splits MATMUL_F32 rows only,
+ * src/cluster/cluster.cpp:437-546).  cache_weights_i8 splits the K x N int8
+ * weights B (host memory, row stride ldb; scales N floats or NULL = 1.0) by
+ * columns over the cluster's devices, in proportion to their weights and in
+ * multiples of 256 columns, and packs each device's shard into that
+ * device's HBM.  matmul_i8 runs every device's shard in parallel
+ * (VNPU_B200_OP_MATMUL_I8_SHARD; A M x K int8 with per-row scale_a, bias N
+ * floats or NULL, all host memory) and places each shard's columns in C
+ * (M x N f32, row stride ldc, host memory or any device's memory).  The
+ * result is the bits of one vnpu_matmul_i8 of the whole weight on one device.
+ * Also in the backend table's reserved[6] and reserved[7].
+ */
+VNPU_API vnpu_status_t VNPU_CALL vnpu_cluster_cache_weights_i8(vnpu_cluster_t *cluster,
+                                                              const char *key,
+                                                              const int8_t *B,
+                                                              const float *scales, uint32_t K,
+                                                              uint32_t N, uint32_t ldb,
+                                                              vnpu_weight_handle_t **out);
+VNPU_API vnpu_status_t VNPU_CALL vnpu_cluster_matmul_i8(vnpu_cluster_t *cluster,
+                                                       vnpu_weight_handle_t *weights,
+                                                       const int8_t *A, const float *scale_a,
+                                                       const float *bias, float *C, uint32_t M,
+                                                       uint32_t K, uint32_t N, uint32_t ldc,
+                                                       uint32_t epilogue);
+
 /* CUDA IPC between the processes of one node (for scatter destinations):
  * get_handle exports the cudaMalloc allocation whose base is device_ptr
  * (vnpu_buffer_alloc memory qualifies) as 64 opaque bytes; open maps such a

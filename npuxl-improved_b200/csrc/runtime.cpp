@@ -344,6 +344,54 @@ void exec_matmul_i8(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags,
     acc.dma = st.staged_bytes();
 }
 
+static_assert(sizeof(vnpu_b200_matmul_i8_shard_args_t) <= sizeof(vnpu_command_t::args),
+              "shard args fit the command");
+
+// MATMUL_I8 of the columns col_base.. of an n_full-wide product: the same
+// validation and kernels as exec_matmul_i8, with every element rounded as in
+// the whole product.
+void exec_matmul_i8_shard(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags,
+                          const LaunchCtx &ctx, Accounting &acc) {
+    vnpu_b200_matmul_i8_shard_args_t in;
+    std::memcpy(&in, cmd.args.raw, sizeof(in));
+    vnpu_packed_weights_t *w = in.B;
+    const uint32_t n_full = in.n_full ? in.n_full : in.N;
+    if (!in.A || !w || !in.C || !in.M || !in.K || !in.N ||
+        static_cast<uint64_t>(in.col_base) + in.N > n_full)
+        throw CommandError("invalid matmul_i8_shard arguments", VNPU_ERR_INVALID_ARGUMENT);
+    if (w->K != in.K || w->N != in.N) throw CommandError("packed weight shape mismatch");
+    if (w->device != s->device) throw CommandError("packed weights belong to another device");
+    const uint32_t lda = in.lda ? in.lda : in.K;
+    const uint32_t ldc = in.ldc ? in.ldc : in.N;
+    if (lda < in.K || ldc < in.N) throw CommandError("invalid int8 leading dimensions");
+    Staging st(s);
+    MatmulI8 p;
+    p.A = st.in(in.A, static_cast<uint64_t>(in.M - 1) * lda + in.K);
+    p.lda = lda;
+    p.Bt = w->bt;
+    p.k_stride = w->k_stride;
+    p.scale_a = st.in(in.scale_a, sizeof(float) * in.M);
+    p.scale_b = w->scales;
+    p.bias = st.in(in.bias, sizeof(float) * in.N);
+    const uint64_t c_span = (static_cast<uint64_t>(in.M - 1) * ldc + in.N) * sizeof(float);
+    p.C = st.out(in.C, c_span, ldc != in.N);
+    p.ldc = ldc;
+    p.M = in.M;
+    p.K = in.K;
+    p.N = in.N;
+    p.epilogue = in.epilogue;
+    p.fmap = i8_form_map(s->device, VNPU_UNIT_AUTO, flags, in.M, in.K, in.N, in.bias != nullptr,
+                         in.epilogue, n_full, in.col_base);
+    p.tmap_b = w->tmap_ok ? &w->tmap : nullptr;
+    p.tmap_b128 = w->tmap128_ok ? &w->tmap128 : nullptr;
+    cuda_check(matmul_i8(ctx, p), "matmul_i8_shard launch");
+    st.finish();
+    acc.bytes_read = static_cast<uint64_t>(in.M) * in.K + static_cast<uint64_t>(in.K) * in.N;
+    acc.bytes_written = static_cast<uint64_t>(in.M) * in.N * sizeof(float);
+    acc.flops = 2ull * in.M * in.K * in.N;
+    acc.dma = st.staged_bytes();
+}
+
 // choose_unit, src/core/scheduler.cpp:43-62 (GPU is this device: the F32
 // path then follows the reference's default unit).
 uint32_t f32_unit(const vnpu_matmul_f32_args_t &a, uint32_t flags) {
@@ -1077,7 +1125,8 @@ vnpu_status_t execute_command(vnpu_stream_t *s, const vnpu_command_t &cmd, uint3
     if (cmd.opcode >= VNPU_OP_COUNT && cmd.opcode != VNPU_B200_OP_RMSNORM_QUANTIZE_I8 &&
         cmd.opcode != VNPU_B200_OP_SWIGLU_QUANTIZE_I8 && cmd.opcode != VNPU_B200_OP_KV_APPEND &&
         cmd.opcode != VNPU_B200_OP_MATMUL_I8_SCATTER &&
-        cmd.opcode != VNPU_B200_OP_QKV_ROPE_APPEND && cmd.opcode != VNPU_B200_OP_MATMUL_I8_RESIDUAL)
+        cmd.opcode != VNPU_B200_OP_QKV_ROPE_APPEND && cmd.opcode != VNPU_B200_OP_MATMUL_I8_RESIDUAL &&
+        cmd.opcode != VNPU_B200_OP_MATMUL_I8_SHARD)
         return VNPU_ERR_INVALID_COMMAND;
     dev->last_opcode.store(cmd.opcode);
     const bool tracing = dev->trace.enabled.load();
@@ -1121,6 +1170,7 @@ vnpu_status_t execute_command(vnpu_stream_t *s, const vnpu_command_t &cmd, uint3
         case VNPU_B200_OP_MATMUL_I8_SCATTER: exec_matmul_i8_scatter(s, cmd, flags, ctx, acc); break;
         case VNPU_B200_OP_QKV_ROPE_APPEND: exec_qkv_rope_append(s, cmd, flags, ctx, acc); break;
         case VNPU_B200_OP_MATMUL_I8_RESIDUAL: exec_matmul_i8_residual(s, cmd, flags, ctx, acc); break;
+        case VNPU_B200_OP_MATMUL_I8_SHARD: exec_matmul_i8_shard(s, cmd, flags, ctx, acc); break;
         case VNPU_OP_MEMSET: exec_memset(s, cmd, acc); break;
         case VNPU_OP_PACK_WEIGHTS_I8: exec_pack(s, cmd, acc); break;
         default:
@@ -1232,6 +1282,7 @@ const char *opcode_name(uint32_t op) {
     if (op == VNPU_B200_OP_MATMUL_I8_SCATTER) return "MATMUL_I8_SCATTER";
     if (op == VNPU_B200_OP_QKV_ROPE_APPEND) return "QKV_ROPE_APPEND";
     if (op == VNPU_B200_OP_MATMUL_I8_RESIDUAL) return "MATMUL_I8_RESIDUAL";
+    if (op == VNPU_B200_OP_MATMUL_I8_SHARD) return "MATMUL_I8_SHARD";
     return op < sizeof(names) / sizeof(names[0]) ? names[op] : "UNKNOWN";
 }
 

@@ -235,6 +235,15 @@ class MatmulI8ResidualArgs(C.Structure):
                 ("epilogue", u32), ("reserved0", u32)]
 
 
+OP_B200_MATMUL_I8_SHARD = 0x106
+
+
+class MatmulI8ShardArgs(C.Structure):
+    _fields_ = [("A", vp), ("B", vp), ("scale_a", vp), ("bias", vp), ("C", vp),
+                ("M", u32), ("K", u32), ("N", u32), ("lda", u32), ("ldc", u32),
+                ("epilogue", u32), ("n_full", u32), ("col_base", u32)]
+
+
 def b200_command(opcode: int, args: C.Structure) -> "Command":
     """A command whose arguments are a B200 extension struct (copied into args.raw)."""
     c = Command()
@@ -353,6 +362,12 @@ class Lib:
                                               C.c_char_p, vp, u32, u32, u32, C.POINTER(vp))
         self.cluster_matmul_f32 = _sig(h, "vnpu_cluster_matmul_f32", _ST, vp, vp, vp, vp, u32,
                                        u32, u32, u32)
+        if hasattr(h, "vnpu_cluster_matmul_i8"):
+            self.cluster_cache_weights_i8 = _sig(h, "vnpu_cluster_cache_weights_i8", _ST, vp,
+                                                 C.c_char_p, vp, vp, u32, u32, u32,
+                                                 C.POINTER(vp))
+            self.cluster_matmul_i8 = _sig(h, "vnpu_cluster_matmul_i8", _ST, vp, vp, vp, vp, vp,
+                                          vp, u32, u32, u32, u32, u32)
         self.is_b200 = hasattr(h, "vnpu_b200_stream_handle")
         if self.is_b200:
             self.b200_stream_handle = _sig(h, "vnpu_b200_stream_handle", vp, vp)

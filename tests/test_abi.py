@@ -129,8 +129,10 @@ def test_vtable(b200_lib):
     assert all(getattr(t, f"fn{i}") for i in range(42))
     # slot 15 is matmul_i8 (include/vnpu_backend.h field order)
     assert t.fn15 == C.cast(b200_lib.h.vnpu_matmul_i8, C.c_void_p).value
-    assert all(t.reserved[i] for i in range(6)) and not t.reserved[6] and not t.reserved[7]
+    assert all(t.reserved[i] for i in range(8))
     assert t.reserved[0] == C.cast(b200_lib.h.vnpu_b200_stream_handle, C.c_void_p).value
+    assert t.reserved[6] == C.cast(b200_lib.h.vnpu_cluster_cache_weights_i8, C.c_void_p).value
+    assert t.reserved[7] == C.cast(b200_lib.h.vnpu_cluster_matmul_i8, C.c_void_p).value
 
 
 def test_dynamic_load_example_links(tmp_path, b200_lib):

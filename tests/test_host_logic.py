@@ -110,6 +110,16 @@ def test_cluster_without_devices(b200_lib):
         assert lib.cluster_get_stats(cl, C.byref(st)) == vnpu.OK
         assert st.total_jobs == 0 and st.local_jobs == 0
         assert lib.cluster_add_device(cl, None, 1) == vnpu.ERR_INVALID_ARGUMENT
+        # the int8 column-sharded entries: no device to hold a shard, an f32
+        # handle is not an int8 one, shapes are checked
+        B8 = np.ones((3, 4), np.int8)
+        assert lib.cluster_cache_weights_i8(cl, b"q", B8.ctypes.data, None, 3, 4, 0,
+                                            C.byref(vnpu.vp())) == vnpu.ERR_DEVICE_ERROR
+        assert lib.cluster_cache_weights_i8(cl, b"q", B8.ctypes.data, None, 3, 4, 2,
+                                            C.byref(vnpu.vp())) == vnpu.ERR_INVALID_ARGUMENT
+        A8 = np.ones((2, 3), np.int8)
+        assert lib.cluster_matmul_i8(cl, h, A8.ctypes.data, None, None, Cm.ctypes.data,
+                                     2, 3, 4, 0, 0) == vnpu.ERR_INVALID_ARGUMENT
     finally:
         lib.cluster_destroy(cl)
 
