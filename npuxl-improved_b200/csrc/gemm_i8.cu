@@ -2000,13 +2000,21 @@ cudaError_t gemv_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
 cudaError_t matmul_i8_gemv(const LaunchCtx &ctx, const MatmulI8 &p) {
     const GvParams g = gv_params(p);
     const bool aligned = (reinterpret_cast<uintptr_t>(p.A) % 16u == 0u) && (p.lda % 16u == 0u);
-    // M <= 2: the shared-memory streaming GEMV where it takes the shape;
-    // VNPU_B200_DECODE=tc|simt selects the tensor-core GEMV or the
-    // register-streaming SIMT GEMV instead (tests compare them).
+    // The mma.sync GEMV (M <= 8) and the one-column-per-warp streaming GEMV
+    // (M <= 2) where they take the shape; VNPU_B200_DECODE=mma|stream|tc|simt
+    // selects one kernel (tests compare them).
     const char *decode = std::getenv("VNPU_B200_DECODE");
-    if (!decode && !std::getenv("VNPU_B200_SIMT_GEMV") && gemv_stream_supported(p, 1)) {
-        g_last_kernel.store("gemv_i8_stream_kernel", std::memory_order_relaxed);
-        return matmul_i8_gemv_stream(ctx, p);
+    if (!std::getenv("VNPU_B200_SIMT_GEMV")) {
+        const bool mma = decode ? std::strcmp(decode, "mma") == 0 && gemv_mma_supported(p)
+                                : gemv_mma_preferred(p);
+        if (mma) {
+            g_last_kernel.store("gemv_i8_mma_kernel", std::memory_order_relaxed);
+            return matmul_i8_gemv_mma(ctx, p, nullptr, 0, 0);
+        }
+        if ((!decode || std::strcmp(decode, "stream") == 0) && gemv_stream_supported(p, 1)) {
+            g_last_kernel.store("gemv_i8_stream_kernel", std::memory_order_relaxed);
+            return matmul_i8_gemv_stream(ctx, p);
+        }
     }
     bool use_tc = p.M > 2;
     if (decode) use_tc = std::strcmp(decode, "tc") == 0;
@@ -2031,10 +2039,18 @@ cudaError_t matmul_i8_gemv(const LaunchCtx &ctx, const MatmulI8 &p) {
 cudaError_t matmul_i8_gemv_residual(const LaunchCtx &ctx, const MatmulI8 &p, const float *R,
                                     uint32_t ldr) {
     if (p.M != 1) return cudaErrorInvalidValue;
-    if (!std::getenv("VNPU_B200_DECODE") && !std::getenv("VNPU_B200_SIMT_GEMV") &&
-        gemv_stream_supported(p, 1)) {
-        g_last_kernel.store("gemv_i8_stream_kernel", std::memory_order_relaxed);
-        return matmul_i8_gemv_stream(ctx, p, R, ldr);
+    const char *decode = std::getenv("VNPU_B200_DECODE");
+    if (!std::getenv("VNPU_B200_SIMT_GEMV")) {
+        const bool mma = decode ? std::strcmp(decode, "mma") == 0 && gemv_mma_supported(p)
+                                : gemv_mma_preferred(p);
+        if (mma) {
+            g_last_kernel.store("gemv_i8_mma_kernel", std::memory_order_relaxed);
+            return matmul_i8_gemv_mma(ctx, p, R, ldr, 0);
+        }
+        if ((!decode || std::strcmp(decode, "stream") == 0) && gemv_stream_supported(p, 1)) {
+            g_last_kernel.store("gemv_i8_stream_kernel", std::memory_order_relaxed);
+            return matmul_i8_gemv_stream(ctx, p, R, ldr);
+        }
     }
     const GvParams g = gv_params(p);
     const bool aligned = (reinterpret_cast<uintptr_t>(p.A) % 16u == 0u) && (p.lda % 16u == 0u);

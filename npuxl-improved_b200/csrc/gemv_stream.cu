@@ -1,6 +1,7 @@
-// gemv_stream.cu - MATMUL_I8 for M <= 2 (the decode GEMV) with each warp's
-// weight column landed in shared memory by cp.async before the programmatic
-// wait for the previous kernel.
+// gemv_stream.cu - MATMUL_I8 for M <= 8 (the decode GEMV) with the weights
+// landed in shared memory by cp.async before the programmatic wait for the
+// previous kernel: one column per warp with __dp4a products (M <= 2), and
+// 8-column groups with the products on mma.sync (M <= 8, below).
 //
 // Bound: HBM.  A decode GEMV reads every weight byte once (K*N int8) plus a
 // few KB of activations, so its time is the weight stream plus fixed costs
@@ -36,6 +37,15 @@
 // the epilogue's scales and bias are fetched before the products: byte-wise
 // guarded loads and fetching them after cost 4.4 -> 3.95 us and 14.8 ->
 // 10.8 us at K = 11008.
+//
+// The mma.sync kernel (graph of launches over distinct weights, bias, no
+// activation): 4096 x 4096 at M = 1 / 4 / 8 3.73 / 3.71 / 3.89 us, against
+// 3.91 us for the one-column kernel at M = 1 and 6.5 / 7.3 us for the
+// tcgen05 swap-AB GEMV at M = 4 / 8; 4096 x 12288 and 4096 x 22016 at M = 8
+// 11.2 / 18.1 us with one group per CTA.  Activations staged in shared
+// memory instead of registers, four warps per CTA, or four groups per CTA
+// all measured slower; K = 11008 (88 KiB of weights per 8 columns) is
+// faster on the register-streaming GEMV.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -289,6 +299,149 @@ cudaError_t gs_launch(const LaunchCtx &ctx, const GsParams &g, uint32_t grid, co
                       dim3(kGsThreads), smem, g, x);
 }
 
+// ---------------------------------------------------------------------------
+// M = 3..8: the products on the tensor core by mma.sync m16n8k32 (s8 x s8 ->
+// s32, exact like __dp4a), the activation rows as the A operand (rows 0..7,
+// 8..15 zero) and 8 weight columns as the B operand.  Eight warps split K
+// into 64-byte chunks (chunk c to warp c % 8); a CTA owns 8 * kG columns.
+// Which physical k a fragment slot holds is free as long as both operands
+// agree, so lane (g, t) = (lane / 4, lane % 4) reads 16 contiguous bytes of
+// its activation row g and of weight column g at k = 64 c + 16 t: the bytes
+// 0-7 feed the first mma of the chunk, 8-15 the second.  Each lane lands its
+// own weight bytes by cp.async before the programmatic wait, as above; the
+// warps' partial sums meet in shared memory and one thread per output
+// applies the element's dequant epilogue.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kGmWarps = 8;
+constexpr uint32_t kGmThreads = kGmWarps * 32;
+
+__device__ __forceinline__ void mma_s8_m16n8k32(int32_t (&d)[4], uint32_t a0, uint32_t a2,
+                                                uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
+// kNci: chunks per warp at most (K <= 64 * 8 * kNci).  Dynamic shared
+// memory: the weight slots (8 warps x nci chunks x kG groups x 512 bytes)
+// then the partial sums (8 warps x kG x 64 int32).
+template <int kG, int kNci, typename Extra>
+__global__ void __launch_bounds__(kGmThreads) gemv_i8_mma_kernel(const GsParams p, const Extra x) {
+    extern __shared__ __align__(16) uint8_t gm_smem[];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t g = lane >> 2, t = lane & 3;
+    const uint32_t n0 = blockIdx.x * 8u * kG;
+    const uint32_t nch = (p.k_stride + 63u) / 64u;
+    const uint32_t nci = (nch + kGmWarps - 1u) / kGmWarps;
+    uint8_t *wslots = gm_smem + static_cast<size_t>(warp) * nci * kG * 512u;
+#pragma unroll
+    for (int i = 0; i < kNci; ++i) {
+        const uint32_t c = warp + kGmWarps * i;
+        const uint32_t k = c * 64u + t * 16u;
+        if (c < nch && k < p.k_stride) {
+#pragma unroll
+            for (int q = 0; q < kG; ++q) {
+                const uint32_t n = n0 + 8u * q + g;
+                if (n < p.N)
+                    cp_async_16(wslots + (i * kG + q) * 512u + lane * 16u,
+                                p.Bt + static_cast<uint64_t>(n) * p.k_stride + k);
+            }
+        }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    pdl_enter();
+    // This thread's output (if any): its epilogue operands now.
+    const uint32_t o = threadIdx.x;
+    const uint32_t oq = o / 64u, orr = o % 64u, oln = orr / 2u;
+    const uint32_t om = oln >> 2, on = n0 + 8u * oq + 2u * (oln & 3u) + (orr & 1u);
+    const bool has_out = o < 64u * kG && om < p.M && on < p.N;
+    const bool has_bias = p.bias != nullptr;
+    float e_sa = 1.0f, e_sb = 1.0f, e_bias = 0.0f;
+    if (has_out) {
+        e_sa = p.scale_a ? __ldg(p.scale_a + om) : 1.0f;
+        e_sb = __ldg(p.scale_b + on);
+        e_bias = has_bias ? __ldg(p.bias + on) : 0.0f;
+    }
+    int4 a[kNci];
+#pragma unroll
+    for (int i = 0; i < kNci; ++i) {
+        const uint32_t k = (warp + kGmWarps * i) * 64u + t * 16u;
+        if (g < p.M && k + 16u <= p.K)
+            a[i] = __ldg(reinterpret_cast<const int4 *>(p.A + static_cast<uint64_t>(g) * p.lda + k));
+        else if (g < p.M && k < p.K)
+            a[i] = gs_act16(p, g, k);
+        else
+            a[i] = make_int4(0, 0, 0, 0);
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    int32_t acc[kG][4];
+#pragma unroll
+    for (int q = 0; q < kG; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0;
+#pragma unroll
+    for (int i = 0; i < kNci; ++i) {
+        if (warp + kGmWarps * i < nch) {
+#pragma unroll
+            for (int q = 0; q < kG; ++q) {
+                const int4 w = *reinterpret_cast<const int4 *>(wslots + (i * kG + q) * 512u + lane * 16u);
+                mma_s8_m16n8k32(acc[q], a[i].x, a[i].y, w.x, w.y);
+                mma_s8_m16n8k32(acc[q], a[i].z, a[i].w, w.z, w.w);
+            }
+        }
+    }
+    // Partial sums of (row g, columns 8q + 2t, 8q + 2t + 1) to shared memory.
+    int32_t *red = reinterpret_cast<int32_t *>(gm_smem + static_cast<size_t>(kGmWarps) * nci * kG * 512u);
+#pragma unroll
+    for (int q = 0; q < kG; ++q) {
+        red[(warp * kG + q) * 64u + lane * 2u] = acc[q][0];
+        red[(warp * kG + q) * 64u + lane * 2u + 1u] = acc[q][1];
+    }
+    __syncthreads();
+    if (!has_out) return;
+    int32_t s = 0;
+#pragma unroll
+    for (uint32_t w = 0; w < kGmWarps; ++w) s += red[(w * kG + oq) * 64u + orr];
+    float out = ref_dequant(s, e_sa, e_sb, has_bias, e_bias, p.epilogue, form_at(p.fmap, om, on));
+    if constexpr (std::is_same<Extra, GsResidual>::value)
+        out = __fadd_rn(x.R[static_cast<uint64_t>(om) * x.ldr + on], out);
+    p.C[static_cast<uint64_t>(om) * p.ldc + on] = out;
+}
+
+template <int kG, int kNci, typename Extra>
+cudaError_t gm_launch(const LaunchCtx &ctx, const GsParams &g, const Extra &x) {
+    static std::mutex mu;
+    static bool opted[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
+    {
+        std::lock_guard<std::mutex> l(mu);
+        if (dev < 0 || dev >= 64 || !opted[dev]) {
+            const cudaError_t e = cudaFuncSetAttribute(gemv_i8_mma_kernel<kG, kNci, Extra>,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       static_cast<int>(kGsMaxSmem));
+            if (e != cudaSuccess) return e;
+            if (dev >= 0 && dev < 64) opted[dev] = true;
+        }
+    }
+    const uint32_t nch = (g.k_stride + 63u) / 64u;
+    const uint32_t nci = (nch + kGmWarps - 1u) / kGmWarps;
+    const uint32_t smem = kGmWarps * nci * kG * 512u + kGmWarps * kG * 64u * 4u;
+    const uint32_t grid = (g.N + 8u * kG - 1u) / (8u * kG);
+    if (ctx.launch_counter) ++*ctx.launch_counter;
+    return launch_pdl(ctx.stream, gemv_i8_mma_kernel<kG, kNci, Extra>, dim3(grid),
+                      dim3(kGmThreads), smem, g, x);
+}
+
+template <typename Extra>
+cudaError_t gm_dispatch(const LaunchCtx &ctx, const GsParams &g, uint32_t groups, const Extra &x) {
+    const bool short_k = g.k_stride <= 64u * kGmWarps * 8u;
+    switch (groups) {
+    case 2: return short_k ? gm_launch<2, 8>(ctx, g, x) : gm_launch<2, 16>(ctx, g, x);
+    case 4: return short_k ? gm_launch<4, 8>(ctx, g, x) : gm_launch<4, 16>(ctx, g, x);
+    default: return short_k ? gm_launch<1, 8>(ctx, g, x) : gm_launch<1, 16>(ctx, g, x);
+    }
+}
+
 GsParams gs_params(const MatmulI8 &p) {
     GsParams g;
     g.A = p.A;
@@ -331,6 +484,35 @@ cudaError_t matmul_i8_gemv_stream(const LaunchCtx &ctx, const MatmulI8 &p, const
     }
     return p.M == 1 ? gs_launch<1, 1>(ctx, g, grid, GsPlain{})
                     : gs_launch<2, 1>(ctx, g, grid, GsPlain{});
+}
+
+bool gemv_mma_supported(const MatmulI8 &p) {
+    return p.M >= 1 && p.M <= 8 && p.K >= 1 && p.k_stride <= 8192u && p.k_stride % 16u == 0u &&
+           (reinterpret_cast<uintptr_t>(p.A) % 16u) == 0u && p.lda % 16u == 0u &&
+           (reinterpret_cast<uintptr_t>(p.Bt) % 16u) == 0u;
+}
+
+// Two 8-column groups per CTA while every CTA of the launch and of the next
+// one fit on the GPU at once (N <= 32 x 148, K <= 4096); one group past that.
+static bool gemv_mma_small(const MatmulI8 &p) {
+    return p.N <= 32u * 148u && p.k_stride <= 4096u;
+}
+
+// The mma GEMV for M = 2..8 wherever it takes the shape, and for M = 1 at the
+// small shapes where it measured faster than the one-column-per-warp kernel
+// (4096 x 4096: 3.73 against 3.91 us; 4096 x 12288: 10.8 against 10.2 us).
+bool gemv_mma_preferred(const MatmulI8 &p) {
+    if (!gemv_mma_supported(p)) return false;
+    return p.M >= 2 || gemv_mma_small(p);
+}
+
+cudaError_t matmul_i8_gemv_mma(const LaunchCtx &ctx, const MatmulI8 &p, const float *R,
+                               uint32_t ldr, uint32_t groups) {
+    if (!gemv_mma_supported(p)) return cudaErrorInvalidValue;
+    if (groups == 0) groups = gemv_mma_small(p) ? 2u : 1u;
+    const GsParams g = gs_params(p);
+    if (R) return gm_dispatch(ctx, g, groups, GsResidual{R, ldr});
+    return gm_dispatch(ctx, g, groups, GsPlain{});
 }
 
 cudaError_t qkv_rope_append_gemv_stream(const LaunchCtx &ctx, const MatmulI8 &p,

@@ -117,6 +117,12 @@ cudaError_t matmul_i8(const LaunchCtx &ctx, const MatmulI8 &p);
 // cols_per_warp x k_stride bytes of shared memory per CTA (<= 200 KiB).
 // R: C = R + out.
 bool gemv_stream_supported(const MatmulI8 &p, uint32_t cols_per_warp);
+// M <= 8 with the products on mma.sync (gemv_stream.cu); groups = 8-column
+// groups per CTA (1, 2 or 4).
+bool gemv_mma_supported(const MatmulI8 &p);
+bool gemv_mma_preferred(const MatmulI8 &p);
+cudaError_t matmul_i8_gemv_mma(const LaunchCtx &ctx, const MatmulI8 &p, const float *R,
+                               uint32_t ldr, uint32_t groups);
 cudaError_t matmul_i8_gemv_stream(const LaunchCtx &ctx, const MatmulI8 &p, const float *R = nullptr,
                                   uint32_t ldr = 0);
 

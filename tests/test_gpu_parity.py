@@ -683,33 +683,45 @@ def test_fused_prologues_any_cluster_size(gpu, oracle, monkeypatch, csize):
     monkeypatch.delenv("VNPU_B200_FUSED_CLUSTER", raising=False)
 
 
-@pytest.mark.parametrize("M", [1, 2, 3, 8])
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8])
 @pytest.mark.parametrize("K,N", [(4096, 4096), (11008, 4096), (4096, 11008), (100, 300),
                                  (16, 128), (1000, 1000), (130, 12288), (12288, 130), (20, 5),
                                  (8192, 300), (4096, 147), (30000, 64)])
 def test_decode_stream_kernel_agrees(gpu, oracle, monkeypatch, M, K, N):
-    """The M <= 2 shared-memory streaming GEMV (each warp lands its column in
-    shared memory before the programmatic wait) gives the bits of the
-    tensor-core GEMV, the register-streaming GEMV and the oracle, with bias,
-    for K / N shapes with ragged tails, fewer columns than a CTA covers and K
-    too long for its shared memory (which takes the register kernel)."""
+    """The decode GEMVs that land their weights in shared memory before the
+    programmatic wait - the mma.sync kernel (M <= 8) and the one-column-per-
+    warp kernel (M <= 2) - give the bits of the tensor-core GEMV, the
+    register-streaming GEMV and the oracle, with bias, for K / N shapes with
+    ragged tails, fewer columns than a CTA covers and K too long for their
+    shared memory (which takes the other kernels)."""
     rng = np.random.default_rng(M * 7919 + K * 13 + N)
     A, sa = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
     B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
     bias = rng.normal(0, 0.01, N).astype(np.float32)
+    k_stride = -(-K // 128) * 128
+    mma_ok = K % 16 == 0 and k_stride <= 8192
+    stream_ok = M <= 2 and mma_ok
+    preferred = mma_ok and (M >= 2 or (N <= 32 * 148 and k_stride <= 4096))
     outs = {}
-    for mode in ("default", "tc", "simt"):
+    for mode in ("default", "mma", "stream", "tc", "simt"):
         monkeypatch.delenv("VNPU_B200_DECODE", raising=False)
         monkeypatch.delenv("VNPU_B200_SIMT_GEMV", raising=False)
-        if mode == "tc":
-            monkeypatch.setenv("VNPU_B200_DECODE", "tc")
+        if mode in ("tc", "mma", "stream"):
+            monkeypatch.setenv("VNPU_B200_DECODE", mode)
         elif mode == "simt":
             monkeypatch.setenv("VNPU_B200_SIMT_GEMV", "1")
         outs[mode] = run_matmul(gpu, A, B, sa, sb, bias, 2, 2)
         kernel = gpu.lib.b200_last_matmul_kernel().decode()
-        if mode == "default" and M <= 2:
-            k_stride = -(-K // 128) * 128
-            stream_ok = K % 16 == 0 and k_stride <= 8192
+        if mode == "default":
+            want_kernel = ("gemv_i8_mma_kernel" if preferred else
+                           "gemv_i8_stream_kernel" if stream_ok else None)
+            if want_kernel:
+                assert kernel == want_kernel, kernel
+            else:
+                assert kernel not in ("gemv_i8_mma_kernel", "gemv_i8_stream_kernel"), kernel
+        elif mode == "mma":
+            assert (kernel == "gemv_i8_mma_kernel") == mma_ok, kernel
+        elif mode == "stream":
             assert (kernel == "gemv_i8_stream_kernel") == stream_ok, kernel
     monkeypatch.delenv("VNPU_B200_DECODE", raising=False)
     monkeypatch.delenv("VNPU_B200_SIMT_GEMV", raising=False)
@@ -719,11 +731,13 @@ def test_decode_stream_kernel_agrees(gpu, oracle, monkeypatch, M, K, N):
 
 
 def test_decode_stream_kernel_residual(gpu, oracle, monkeypatch):
-    """MATMUL_I8_RESIDUAL at M = 1 on the shared-memory streaming GEMV: C = R +
-    out with ADD_F32's single rounding, equal to the register-streaming GEMV's."""
+    """MATMUL_I8_RESIDUAL at M = 1 on the shared-memory GEMVs (the mma.sync
+    kernel at 4096 x 4096 and 3000 x 1000, the one-column kernel at 4096 x
+    12288): C = R + out with ADD_F32's single rounding, equal to the
+    register-streaming GEMV's."""
     torch = pytest.importorskip("torch")
     rng = np.random.default_rng(5)
-    for K, N in ((4096, 4096), (11008, 4096), (300, 1000)):
+    for K, N in ((4096, 4096), (11008, 4096), (3008, 1000), (4096, 12288)):
         A, sa = oracle.quantize(rng.uniform(-1, 1, (1, K)).astype(np.float32), 0)
         B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
         R = rng.normal(0, 1, (1, N)).astype(np.float32)
