@@ -464,41 +464,51 @@ def llm_block_secondary(lib, dev, torch, prefill=512, decode=128, with_reference
     `decode` KV-cached steps (one CUDA graph per step, replayed)."""
     from llm_block import B200Block, BlockConfig, HostBlock, weight_bytes
     cfg = BlockConfig(cap=prefill + decode)
-    blk = B200Block(cfg, lib, dev, torch)
-    g = torch.Generator(device="cuda").manual_seed(11)
-    x = torch.empty((prefill, cfg.d), device="cuda").normal_(0, 1, generator=g)
     st = Stream(lib, dev)
-    for _ in range(3):                        # warm-up: first passes pay one-off costs
+
+    def run(swiglu_epilogue):
+        blk = B200Block(cfg, lib, dev, torch, swiglu_epilogue=swiglu_epilogue)
+        g = torch.Generator(device="cuda").manual_seed(11)
+        x = torch.empty((prefill, cfg.d), device="cuda").normal_(0, 1, generator=g)
+        for _ in range(3):                        # warm-up: first passes pay one-off costs
+            blk.forward(x, 0)
+        dev.sync()
+        blk.kc.zero_()
+        blk.vc.zero_()
+        blk.mask.fill_(float("-inf"))
+        e0 = st.event()
         blk.forward(x, 0)
-    dev.sync()
-    blk.kc.zero_()
-    blk.vc.zero_()
-    blk.mask.fill_(float("-inf"))
-    e0 = st.event()
-    blk.forward(x, 0)
-    e1 = st.event()
-    dev.sync()
-    e1.synchronize()
-    ms_prefill = e0.elapsed_time(e1)
-    xin = blk._buf("decode_in", (1, cfg.d))
-    xin.normal_(0, 1, generator=g)
-    blk.pos.fill_(prefill)
-    torch.cuda.synchronize()
-    blk.capture_decode(xin)
-    blk.pos.fill_(prefill)
-    torch.cuda.synchronize()
-    e0 = st.event()
-    for _ in range(decode):
-        blk.replay_decode()
-    e1 = st.event()
-    e1.synchronize()
-    ms_decode = e0.elapsed_time(e1)
-    blk.close()
+        e1 = st.event()
+        dev.sync()
+        e1.synchronize()
+        ms_prefill = e0.elapsed_time(e1)
+        xin = blk._buf("decode_in", (1, cfg.d))
+        xin.normal_(0, 1, generator=g)
+        blk.pos.fill_(prefill)
+        torch.cuda.synchronize()
+        blk.capture_decode(xin)
+        blk.pos.fill_(prefill)
+        torch.cuda.synchronize()
+        e0 = st.event()
+        for _ in range(decode):
+            blk.replay_decode()
+        e1 = st.event()
+        e1.synchronize()
+        ms_decode = e0.elapsed_time(e1)
+        blk.close()
+        return ms_prefill, ms_decode
+
+    ms_prefill, ms_decode = run(True)
+    pro_prefill, pro_decode = run(False)
     out = {"config": f"d={cfg.d} heads={cfg.heads} I={cfg.inter} prefill {prefill} + {decode} decode",
            "prefill_ms": ms_prefill, "prefill_tok_s": prefill / ms_prefill * 1e3,
            "decode_ms_per_token": ms_decode / decode, "decode_tok_s": decode / ms_decode * 1e3,
            "decode_weight_gbs": weight_bytes(cfg) / (ms_decode / decode) / 1e6,
-           "decode": "one CUDA graph per token step (vnpu commands + torch layout glue)"}
+           "decode": "one CUDA graph per token step (vnpu commands + torch layout glue)",
+           "gate_up": "MATMUL_I8_SWIGLU (SwiGLU in the gate/up GEMM's epilogue) -> QUANTIZE_I8",
+           "swiglu_prologue": {"gate_up": "MATMUL_I8 (2I columns) -> SWIGLU_QUANTIZE_I8",
+                               "prefill_ms": pro_prefill,
+                               "decode_ms_per_token": pro_decode / decode}}
     if with_reference and os.path.exists(REF_LIB):
         import time as _time
         os.environ.setdefault("VNPU_FORCE_ISA", "avx2")
@@ -797,7 +807,8 @@ def run_b200(args):
                          "frac": achieved / int8_peak, "traffic": traffic,
                          "peak_source": f"2 x {pk['source']} bf16 dense ({pk['bf16']} TFLOP/s); "
                                         f"nominal int8 dense 4500 TOPS",
-                         "frac_of_nominal": achieved / 4500.0, "ms_per_launch": ms_gemm},
+                         "frac_of_nominal": achieved / 4500.0, "ms_per_launch": ms_gemm,
+                         "work": "2*M*K*N/P int8 ops per launch"},
             "e2e": {"value": total_ops / ms_e2e / 1e9, "unit": "TOPS",
                     "h2d_bytes_per_step": M * K * 4, "d2h_bytes_per_step": M * N_TOTAL * 4,
                     "ms_per_step": ms_e2e,

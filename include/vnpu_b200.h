@@ -233,6 +233,37 @@ typedef struct vnpu_b200_matmul_i8_residual_args_t {
 } vnpu_b200_matmul_i8_residual_args_t;
 
 /*
+ * The gate/up projection with its SwiGLU (no reference counterpart; the
+ * reference block runs MATMUL_I8 on the [K][2I] gate/up weight, splits the
+ * [T][2I] output into gate and up on the host and submits SWIGLU_F32:
+ * tools/llm_bench.cpp:298-311).  B holds 2I columns (gate 0..I-1, up
+ * I..2I-1); Y (M x I, row stride ldy) receives the bits SWIGLU_F32 (with
+ * alpha) gives for the halves of that MATMUL_I8's output, each element of
+ * which keeps the rounding form it has in the 2I-wide product.  The SwiGLU
+ * runs in the GEMM's epilogue where the CTA-pair tensor-core GEMM (M > 128)
+ * or the streaming decode GEMV (M <= 2) takes the shape, so the 2I-wide
+ * product never reaches memory; elsewhere the product goes to stream-ordered
+ * scratch first.  alpha == 0 means 1, as in SWIGLU_F32.
+ */
+#define VNPU_B200_OP_MATMUL_I8_SWIGLU  0x108u
+
+typedef struct vnpu_b200_matmul_i8_swiglu_args_t {
+    const int8_t *A;
+    vnpu_packed_weights_t *B;   /* K x 2I */
+    const float *scale_a;
+    const float *bias;          /* 2I entries or NULL */
+    float *Y;                   /* M x I */
+    uint32_t M;
+    uint32_t K;
+    uint32_t N;                 /* 2I, the columns of B */
+    uint32_t lda;               /* 0 = K */
+    uint32_t ldy;               /* 0 = I */
+    uint32_t epilogue;          /* of the MATMUL_I8, before the SwiGLU */
+    float alpha;
+    uint32_t reserved0;
+} vnpu_b200_matmul_i8_swiglu_args_t;
+
+/*
  * MATMUL_I8 of one column shard of a wider product (no reference
  * counterpart; the reference has no int8 multi-device split).  B holds the
  * shard's N columns, which are columns col_base .. col_base + N - 1 of an

@@ -328,6 +328,22 @@ __global__ void swiglu_kernel(const float *__restrict__ G, const float *__restri
     }
 }
 
+// Y[r][j] = swiglu(C[r][j], C[r][I + j]) * alpha: the gate/up halves of one
+// [rows][2I] projection output (row stride ldc), the same expression.
+__global__ void swiglu_rows_kernel(const float *__restrict__ C, uint32_t ldc, float *__restrict__ Y,
+                                   uint32_t ldy, uint32_t rows, uint32_t I, float alpha) {
+    pdl_enter();
+    const uint64_t n = static_cast<uint64_t>(rows) * I;
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint64_t r = i / I;
+        const uint32_t j = static_cast<uint32_t>(i - r * I);
+        const float g = C[r * ldc + j];
+        const float s = __fdiv_rn(g, __fadd_rn(1.0f, ref_exp256_lane(-g)));
+        Y[r * ldy + j] = __fmul_rn(__fmul_rn(s, C[r * ldc + I + j]), alpha);
+    }
+}
+
 __global__ void swiglu_vec_kernel(const float4 *__restrict__ G, const float4 *__restrict__ U,
                                   float4 *__restrict__ Y, uint64_t n4, float alpha) {
     pdl_enter();
@@ -1716,6 +1732,15 @@ cudaError_t qkv_split_rope_append(const LaunchCtx &ctx, const float *C, uint32_t
                            ctx.err));
     count_launch(ctx);
     return cudaGetLastError();
+}
+
+cudaError_t swiglu_rows(const LaunchCtx &ctx, const float *C, uint32_t ldc, float *Y, uint32_t ldy,
+                        uint32_t rows, uint32_t I, float alpha) {
+    const uint64_t n = static_cast<uint64_t>(rows) * I;
+    if (n == 0) return cudaSuccess;
+    if (ctx.launch_counter) ++*ctx.launch_counter;
+    return launch_pdl(ctx.stream, swiglu_rows_kernel, dim3(grid_for(n, ctx.num_sms, 256)), dim3(256),
+                      0, C, ldc, Y, ldy, rows, I, alpha);
 }
 
 cudaError_t swiglu(const LaunchCtx &ctx, const float *gate, const float *up, float *Y,

@@ -31,8 +31,7 @@
 #include <atomic>
 #include <mutex>
 
-#include "common.cuh"
-#include "kernels.h"
+#include "gemm_tc.cuh"
 
 namespace vnpu_b200 {
 namespace {
@@ -42,154 +41,6 @@ std::atomic<const char *> g_last_kernel{"none"};
 
 inline void count_launch(const LaunchCtx &ctx) {
     if (ctx.launch_counter) *ctx.launch_counter += 1;
-}
-
-// ===========================================================================
-// tcgen05 tensor-core GEMM
-// ===========================================================================
-
-constexpr uint32_t kBM = 128;                 // rows per tile (UMMA M)
-constexpr uint32_t kBN = 256;                 // columns per tile (UMMA N)
-constexpr uint32_t kBK = 128;                 // K bytes per stage (one 128B swizzle atom)
-constexpr uint32_t kUmmaK = 32;               // K per tcgen05.mma kind::i8
-constexpr uint32_t kStages = 4;
-constexpr uint32_t kABytes = kBM * kBK;       // 16 KiB
-constexpr uint32_t kBBytes = kBN * kBK;       // 32 KiB
-constexpr uint32_t kStageBytes = kABytes + kBBytes;
-constexpr uint32_t kTmemCols = 2 * kBN;       // two accumulators
-constexpr uint32_t kThreads = 192;            // 6 warps
-constexpr uint32_t kEpiWarps = 4;
-constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024;  // + alignment slack
-
-struct TcParams {
-    const float *scale_a = nullptr;
-    const float *scale_b = nullptr;
-    const float *bias = nullptr;
-    float *C = nullptr;
-    uint32_t ldc = 0;
-    uint32_t M = 0, N = 0, K = 0;
-    uint32_t tiles_m = 0, tiles_n = 0, num_kb = 0;
-    uint32_t group_m = 1;  // raster band height in m-tiles
-    uint32_t epilogue = 0, form = 0;
-    uint32_t variant = 0;  // epi_variant(epilogue, bias != NULL, form)
-    uint32_t tma_store = 0;  // 1: C written by TMA from shared memory
-    uint32_t *err = nullptr;
-    uint64_t limit_ns = 2000000000ull;
-    // Scatter epilogue (ndst > 0): the tile goes to dst[0..ndst-1], each a
-    // [M][ldd] matrix, at column col_off + n, by plain stores.
-    float *dst[8] = {};
-    uint32_t ndst = 0;
-    uint32_t ldd = 0;
-    uint32_t col_off = 0;
-    // Split K (pair kernel): work unit u is tile u / splits, k-blocks
-    // [s * kb_per_split, ...) of split s = u % splits; with splits > 1 the
-    // epilogue stores the raw int32 sums to rows s * m_pad + m of the
-    // workspace (C, ldc = N) and splitk_finish_kernel adds and dequantises.
-    uint32_t splits = 1;
-    uint32_t kb_per_split = 0;
-    uint32_t m_pad = 0;
-};
-
-__device__ __forceinline__ void tile_coords(uint32_t t, uint32_t tiles_m, uint32_t tiles_n,
-                                            uint32_t group_m, uint32_t &mb, uint32_t &nb) {
-    // Grouped raster: bands of group_m m-tiles walk all n-tiles, so a wave of
-    // CTAs shares the band's A row-panels and a contiguous run of B panels in
-    // L2; B is streamed from HBM once per band.
-    const uint32_t per_band = group_m * tiles_n;
-    const uint32_t band = t / per_band;
-    const uint32_t first_m = band * group_m;
-    const uint32_t rows = min(group_m, tiles_m - first_m);
-    const uint32_t r = t - band * per_band;
-    mb = first_m + r % rows;
-    nb = r / rows;
-}
-
-// Store 32 finished values of one row (vec: 16-byte aligned row, ldc % 4 == 0).
-__device__ __forceinline__ void store_row32(const float (&v)[32], float *crow, uint32_t n0,
-                                            uint32_t N, bool vec) {
-    if (vec && n0 + 32u <= N) {
-#pragma unroll
-        for (uint32_t j = 0; j < 32u; j += 4u)
-            *reinterpret_cast<float4 *>(crow + n0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        return;
-    }
-#pragma unroll
-    for (uint32_t j = 0; j < 32u; ++j)
-        if (n0 + j < N) crow[n0 + j] = v[j];
-}
-
-// The 16 variants epi_variant() can produce.
-#define VNPU_B200_EPI_VARIANTS(X)                                                             \
-    X(0x10) X(0x11) X(0x12) X(0x13) X(0x14) X(0x15) X(0x16) X(0x17) X(0x18) X(0x19) X(0x1a) \
-    X(0x1b) X(0x02) X(0x03) X(0x0a) X(0x0b)
-
-// Dequant of 32 accumulators of one row whose column scales and biases sit one
-// per lane (lane j holds column j's): the epilogue fetches them once per tile,
-// before the accumulators are ready, instead of per chunk after.  All 32 lanes
-// must execute it (warp shuffles).
-template <uint32_t V>
-__device__ __forceinline__ void dequant32_shfl(const uint32_t (&r)[32], float (&v)[32], float sa,
-                                               float s_lane, float b_lane) {
-    constexpr uint32_t ACT = V & 3u, BIAS = (V >> 2) & 3u;
-    constexpr bool FUSED = ((V >> 4) & 1u) != 0u;
-#pragma unroll
-    for (uint32_t j = 0; j < 32u; ++j) {
-        const float sb = __shfl_sync(0xffffffffu, s_lane, j);
-        const float bb = BIAS != 0 ? __shfl_sync(0xffffffffu, b_lane, j) : 0.0f;
-        v[j] = ref_dequant_t<ACT, BIAS, FUSED>(static_cast<int32_t>(r[j]), sa, sb, bb);
-    }
-}
-
-template <uint32_t V>
-__device__ __forceinline__ void dequant32_shfl_inplace(uint32_t (&r)[32], float sa, float s_lane,
-                                                       float b_lane) {
-    constexpr uint32_t ACT = V & 3u, BIAS = (V >> 2) & 3u;
-    constexpr bool FUSED = ((V >> 4) & 1u) != 0u;
-#pragma unroll
-    for (uint32_t j = 0; j < 32u; ++j) {
-        const float sb = __shfl_sync(0xffffffffu, s_lane, j);
-        const float bb = BIAS != 0 ? __shfl_sync(0xffffffffu, b_lane, j) : 0.0f;
-        r[j] = __float_as_uint(ref_dequant_t<ACT, BIAS, FUSED>(static_cast<int32_t>(r[j]), sa, sb, bb));
-    }
-}
-
-// One launch-constant form per tcgen05 GEMM launch: a command whose elements
-// take more than one form (FormMap kFormMixed) never reaches these kernels'
-// epilogues (matmul_i8_tcgen05 routes it to raw split-K sums and the finish
-// kernel, or to the SIMT kernel).
-__device__ __forceinline__ void dequant32_shfl_any(uint32_t variant, const uint32_t (&r)[32],
-                                                   float (&v)[32], float sa, float s_lane,
-                                                   float b_lane) {
-    switch (variant) {
-#define VNPU_B200_CASE(V)                                      \
-    case V:                                                    \
-        dequant32_shfl<V>(r, v, sa, s_lane, b_lane);           \
-        break;
-        VNPU_B200_EPI_VARIANTS(VNPU_B200_CASE)
-#undef VNPU_B200_CASE
-    default:
-        break;
-    }
-}
-
-__device__ __forceinline__ void dequant32_shfl_inplace_any(uint32_t variant, uint32_t (&r)[32],
-                                                           float sa, float s_lane, float b_lane) {
-    switch (variant) {
-#define VNPU_B200_CASE(V)                                      \
-    case V:                                                    \
-        dequant32_shfl_inplace<V>(r, sa, s_lane, b_lane);      \
-        break;
-        VNPU_B200_EPI_VARIANTS(VNPU_B200_CASE)
-#undef VNPU_B200_CASE
-    default:
-        break;
-    }
-}
-
-// Column scale and bias of column n for the lane that holds it (n past N: 1, 0).
-__device__ __forceinline__ void fetch_col(const TcParams &p, uint32_t n, float &s, float &b) {
-    s = n < p.N ? __ldg(p.scale_b + n) : 1.0f;
-    b = (p.bias && n < p.N) ? __ldg(p.bias + n) : 0.0f;
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -385,32 +236,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 // No TMA multicast anywhere: each CTA loads only its own tiles.
 // ===========================================================================
 
-constexpr uint32_t kPStages = 6;                  // stage count of the wide kernel's sibling (8 warps)
-constexpr uint32_t kPTileM = 256;                 // per pair
-constexpr uint32_t kPTileN = 256;                 // per pair
-constexpr uint32_t kPABytes = 128 * kBK;          // 16 KiB per CTA
-constexpr uint32_t kPBBytes = 128 * kBK;          // 16 KiB per CTA
-constexpr uint32_t kPStageBytes = kPABytes + kPBBytes;
-constexpr uint32_t kPEpiWarps = 8;                // per CTA (wide kernel)
-constexpr uint32_t kPThreads = (2 + kPEpiWarps) * 32;
-// The 256x256 pair kernel comes in two shapes: 8 epilogue warps and 6 stages
-// for NONE / RELU (the MMA issuer keeps its sub-partition), and 16 epilogue
-// warps and 5 stages for SiLU / GELU, whose dequant epilogue (polynomial exp,
-// IEEE divisions) is latency-bound: four warps per sub-partition hide it
-// behind the next tile's MMAs.
-constexpr uint32_t pair_threads(uint32_t epi_warps) { return (2 + epi_warps) * 32; }
-constexpr uint32_t pair_smem_bytes(uint32_t epi_warps, uint32_t stages) {
-    return stages * (128 * kBK * 2) + epi_warps * 32 * 32 * 4 + 1024;
-}
-constexpr uint32_t kPStageOutBytes = 32 * 32 * 4;  // one 32 rows x 32 floats staging buffer
-
-
-template <uint32_t kNEpiWarps, uint32_t kNStages>
+template <uint32_t kNEpiWarps, uint32_t kNStages, uint32_t kTN = kPTileN, bool kSwiglu = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWarps), 1)
     gemm_i8_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                 const __grid_constant__ CUtensorMap tmap_b,
                                 const __grid_constant__ CUtensorMap tmap_c, const TcParams p) {
-    constexpr uint32_t kNColsPerWarp = 4u * kPTileN / kNEpiWarps;   // 128 or 64 columns
+    static_assert(kTN % 32u == 0u && kTN >= 64u && kTN <= 256u, "pair tile width");
+    constexpr uint32_t kBRows = kTN / 2u;                      // B rows per CTA
+    constexpr uint32_t kStageB = pair_stage_bytes(kTN);        // A + B bytes per CTA and stage
+    // The tile's 32-column chunks are dealt to kNEpiWarps / 4 column groups of
+    // warps, kChunks consecutive chunks each (the last group may get fewer).
+    constexpr uint32_t kGroups = kNEpiWarps / 4u;
+    constexpr uint32_t kTileChunks = kTN / 32u;
+    constexpr uint32_t kChunks = (kTileChunks + kGroups - 1u) / kGroups;
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[kNStages];
     __shared__ __align__(8) uint64_t empty_bar[kNStages];
@@ -481,14 +319,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
                         break;
                     }
                     // The leader's full barrier counts both CTAs' bytes.
-                    if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * kPStageBytes);
+                    if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * kStageB);
                     const uint32_t leader_full = mapa_shared(smem_addr(&full_bar[s]), 0);
-                    uint8_t *sa = ring + s * kPStageBytes;
+                    uint8_t *sa = ring + s * kStageB;
                     uint8_t *sb = sa + kPABytes;
                     tma_load_2d_pair(sa, &tmap_a, leader_full, static_cast<int32_t>(kb * kBK),
                                      static_cast<int32_t>(mb * kPTileM + rank * 128u));
+                    // SwiGLU: CTA 0 holds gate rows nb*128.., CTA 1 the up rows
+                    // I + nb*128.. (D columns 0-127 gate, 128-255 up).
+                    const uint32_t brow = kSwiglu ? (rank ? p.swiglu_i : 0u) + nb * 128u
+                                                  : nb * kTN + rank * kBRows;
                     tma_load_2d_pair(sb, &tmap_b, leader_full, static_cast<int32_t>(kb * kBK),
-                                     static_cast<int32_t>(nb * kPTileN + rank * 128u));
+                                     static_cast<int32_t>(brow));
                 }
             }
             // The leader never leaves with copies in flight (its full barriers
@@ -503,7 +345,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer (leader)
         if (rank == 0 && lane == 0) {
-            constexpr uint32_t idesc = umma_idesc_i8(kPTileM, kPTileN);
+            constexpr uint32_t idesc = umma_idesc_i8(kPTileM, kTN);
             uint32_t it = 0, tcount = 0;
             bool ok = true;
             for (uint32_t t = pair; t < total_tiles && ok; t += npairs, ++tcount) {
@@ -513,7 +355,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
                                &abort_flag))
                     break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * kPTileN;
+                const uint32_t d_tmem = tmem_base + acc * kTN;
                 const uint32_t split = t % p.splits;
                 const uint32_t kbps = p.splits > 1 ? p.kb_per_split : p.num_kb;
                 const uint32_t kb0 = split * kbps;
@@ -526,7 +368,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t sa = smem_addr(ring + s * kPStageBytes);
+                    const uint32_t sa = smem_addr(ring + s * kStageB);
                     const uint64_t adesc = umma_desc_k_sw128(sa);
                     const uint64_t bdesc = umma_desc_k_sw128(sa + kPABytes);
 #pragma unroll
@@ -543,18 +385,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
         }
     } else {
         // ------------------------------------------------------------ epilogue (both CTAs)
-        // Warp w reads TMEM lanes 32*(w%4)..+31 and takes the 64 columns
-        // ((w-2)/4)*64 .. +63 of the tile (warps 2-5 columns 0-63, 6-9 64-127,
-        // ...).  Each 32x32 chunk is dequantised in registers, written
+        // Warp w reads TMEM lanes 32*(w%4)..+31 and takes the kChunks 32-column
+        // chunks of column group (w-2)/4 (with 8 warps and kTN = 256: warps 2-5
+        // columns 0-127, 6-9 columns 128-255).  Each 32x32 chunk is dequantised in registers, written
         // 128B-swizzled into this warp's 4 KiB staging buffer and stored to C
         // by TMA (rows >= M and columns >= N are clipped by the tensor map);
         // without a C tensor map the rows are stored directly.
         const uint32_t lane_base = (warp & 3u) * 32u;
-        const uint32_t col_base = ((warp - 2u) >> 2) * kNColsPerWarp;
+        const uint32_t chunk0 = ((warp - 2u) >> 2) * kChunks;   // first chunk of the group
+        const uint32_t col_base = chunk0 * 32u;
         const uint32_t row = rank * 128u + lane_base + lane;
         const bool vec_ok = (p.ldc % 4u == 0u) &&
                             ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0u);
-        uint8_t *stage_out = ring + kNStages * kPStageBytes + (warp - 2u) * kPStageOutBytes;
+        uint8_t *stage_out = ring + kNStages * kStageB + (warp - 2u) * kPStageOutBytes;
         float *my_row = reinterpret_cast<float *>(stage_out + lane * 128u);
         const uint32_t leader_empty0 = mapa_shared(smem_addr(&tmem_empty_bar[0]), 0);
         const uint32_t leader_empty1 = mapa_shared(smem_addr(&tmem_empty_bar[1]), 0);
@@ -572,10 +415,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
             const uint32_t m = m_first + lane;
             const bool row_ok = m < p.M;
             const float sa = row_ok ? (p.scale_a ? __ldg(p.scale_a + m) : 1.0f) : 0.0f;
-            float sreg[kNColsPerWarp / 32u], breg[kNColsPerWarp / 32u];
+            float sreg[kChunks], breg[kChunks];
+            // SwiGLU: the warp's first kChunks / 2 chunks are gate columns
+            // sw_col.., the rest the matching up columns (TMEM 128 + sw_col..).
+            constexpr uint32_t kHalf = kChunks / 2u;
+            const uint32_t sw_col = ((warp - 2u) >> 2) * kHalf * 32u;
 #pragma unroll
-            for (uint32_t c = 0; c < kNColsPerWarp / 32u; ++c)
-                fetch_col(p, nb * kPTileN + col_base + c * 32u + lane, sreg[c], breg[c]);
+            for (uint32_t c = 0; c < kChunks; ++c) {
+                const uint32_t wcol =
+                    kSwiglu ? (c < kHalf ? nb * 128u + sw_col + c * 32u
+                                         : p.swiglu_i + nb * 128u + sw_col + (c - kHalf) * 32u)
+                            : nb * kTN + col_base + c * 32u;
+                fetch_col(p, wcol + lane, sreg[c], breg[c]);
+            }
             uint32_t ok = 0;
             if (lane == 0)
                 ok = mbar_wait(&tmem_full_bar[acc], use & 1u, p.limit_ns, p.err, &abort_flag);
@@ -587,22 +439,66 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
             // All of the warp's accumulator columns in one round of tensor-memory
             // loads (one wait instead of one per chunk); the accumulator is
             // released before any of it is dequantised or stored.
-            constexpr uint32_t kChunks = kNColsPerWarp / 32u;
             uint32_t rr[kChunks][32];
             __syncwarp();
 #pragma unroll
             for (uint32_t c = 0; c < kChunks; ++c)
-                tmem_ld_32cols(tmem_base + (lane_base << 16) + acc * kPTileN + col_base + c * 32u,
-                               rr[c]);
+                if (chunk0 + c < kTileChunks) {  // warp-uniform
+                    const uint32_t tcol = kSwiglu ? (c < kHalf ? sw_col + c * 32u
+                                                               : 128u + sw_col + (c - kHalf) * 32u)
+                                                  : col_base + c * 32u;
+                    tmem_ld_32cols(tmem_base + (lane_base << 16) + acc * kTN + tcol, rr[c]);
+                }
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc ? leader_empty1 : leader_empty0);
+            if constexpr (kSwiglu) {
+                // gate and up dequantised, then SWIGLU_F32's expression
+                // (src/kernels/llm.cpp:289-306), stored as kHalf output chunks.
+                if (m_first < p.M) {
+#pragma unroll
+                    for (uint32_t c = 0; c < kChunks; ++c)
+                        dequant32_shfl_inplace_any(p.variant, rr[c], sa, sreg[c], breg[c]);
+                }
+#pragma unroll
+                for (uint32_t k = 0; k < kHalf; ++k) {
+                    const uint32_t n0 = nb * 128u + sw_col + k * 32u;
+                    if (n0 >= p.swiglu_i || m_first >= p.M) continue;  // warp-uniform
+#pragma unroll
+                    for (uint32_t j = 0; j < 32u; ++j) {
+                        const float g = __uint_as_float(rr[k][j]);
+                        const float s = __fdiv_rn(g, __fadd_rn(1.0f, ref_exp256_lane(-g)));
+                        rr[k][j] = __float_as_uint(
+                            __fmul_rn(__fmul_rn(s, __uint_as_float(rr[k + kHalf][j])), p.swiglu_alpha));
+                    }
+                    if (p.tma_store) {
+                        if (lane == 0) bulk_wait_read0();
+                        __syncwarp();
+#pragma unroll
+                        for (uint32_t j = 0; j < 8u; ++j)
+                            *reinterpret_cast<uint4 *>(my_row + 4u * (j ^ (lane & 7u))) =
+                                make_uint4(rr[k][4 * j], rr[k][4 * j + 1], rr[k][4 * j + 2],
+                                           rr[k][4 * j + 3]);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&tmap_c, stage_out, static_cast<int32_t>(n0),
+                                         static_cast<int32_t>(m_first));
+                            bulk_commit();
+                        }
+                    } else if (row_ok) {
+                        store_row32(reinterpret_cast<const float(&)[32]>(rr[k]), crow, n0,
+                                    p.swiglu_i, vec_ok);
+                    }
+                }
+                continue;
+            }
 #pragma unroll
             for (uint32_t c = 0; c < kChunks; ++c) {
                 const uint32_t col = col_base + c * 32u;
-                const uint32_t n0 = nb * kPTileN + col;
-                if (n0 >= p.N || m_first >= p.M) continue;  // warp-uniform
+                const uint32_t n0 = nb * kTN + col;
+                if (chunk0 + c >= kTileChunks || n0 >= p.N || m_first >= p.M) continue;  // warp-uniform
                 if (p.splits == 1) dequant32_shfl_inplace_any(p.variant, rr[c], sa, sreg[c], breg[c]);
                 const float(&v)[32] = reinterpret_cast<const float(&)[32]>(rr[c]);
                 if (p.ndst) {
@@ -733,289 +629,6 @@ __global__ void __launch_bounds__(256) splitk_finish_kernel(
             c[2] = o.z;
             c[3] = o.w;
         }
-    }
-}
-
-// ===========================================================================
-// Wide tcgen05 pair GEMM: a CTA pair computes a 256x512 output tile as two
-// 256x256 accumulators (TMEM columns 0-255 and 256-511 of each CTA: all 512).
-// Per 128-deep K step each SM loads 16 KiB of A and 2 x 16 KiB of B for
-// 128x512 outputs: a quarter fewer operand bytes per MAC than the 256x256
-// pair tile, whose rate is bounded by how fast TMA delivers tiles from L2.
-// With both halves of tensor memory in use there is no second accumulator
-// set, so the epilogue drains D0 then D1 and releases each half as soon as it
-// is read; at the start of a tile the MMA issuer runs D0's MMAs over every
-// k-block already staged (holding those stages) while D1 is still being
-// drained, then issues D1's MMAs on the held stages and releases them.
-//   barriers: full[s] (leader) counts both CTAs' bytes; empty[s] (both) is
-//             arrived by the leader's multicast commit; tmem_full (both);
-//             tmem_empty[h] (leader) gets 16 arrivals, one per epilogue warp
-//             of the pair, when half h has been read.
-// No TMA multicast: each CTA loads only its own tiles.
-// ===========================================================================
-
-constexpr uint32_t kWStages = 4;
-constexpr uint32_t kWTileN = 512;                          // per pair
-constexpr uint32_t kWStageBytes = kPABytes + 2 * kPBBytes;  // 48 KiB per CTA
-constexpr uint32_t kWSmemBytes = kWStages * kWStageBytes + kPEpiWarps * kPStageOutBytes + 1024;
-constexpr uint32_t kWTmemCols = 512;
-static_assert(kWSmemBytes <= 227u * 1024u, "wide pair tile exceeds shared memory");
-
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
-    gemm_i8_tcgen05_pair_wide_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                                     const __grid_constant__ CUtensorMap tmap_b,
-                                     const __grid_constant__ CUtensorMap tmap_c,
-                                     const TcParams p) {
-    extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t full_bar[kWStages];
-    __shared__ __align__(8) uint64_t empty_bar[kWStages];
-    __shared__ __align__(8) uint64_t tmem_full_bar;
-    __shared__ __align__(8) uint64_t tmem_empty_bar[2];
-    __shared__ __align__(8) uint64_t drain_bar;
-    __shared__ uint32_t tmem_base_slot;
-    __shared__ volatile int abort_flag;
-
-    // The stream's next kernel may be scheduled now; it waits for this one
-    // to finish before it touches memory.
-    pdl_launch_dependents();
-    const uint32_t raw_addr = smem_addr(smem_raw);
-    uint8_t *ring = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
-
-    const uint32_t warp = threadIdx.x >> 5;
-    const uint32_t lane = threadIdx.x & 31;
-    const uint32_t rank = cluster_ctarank();
-    const uint32_t pair = blockIdx.x >> 1;
-    const uint32_t npairs = gridDim.x >> 1;
-    const uint32_t total_tiles = p.tiles_m * p.tiles_n;   // 256x512 tiles
-
-    if (threadIdx.x == 0) {
-        for (uint32_t s = 0; s < kWStages; ++s) {
-            mbar_init(&full_bar[s], 1);
-            mbar_init(&empty_bar[s], 1);
-        }
-        mbar_init(&tmem_full_bar, 1);
-        mbar_init(&tmem_empty_bar[0], 2 * kPEpiWarps);
-        mbar_init(&tmem_empty_bar[1], 2 * kPEpiWarps);
-        mbar_init(&drain_bar, 1);
-        abort_flag = 0;
-        fence_barrier_init();
-        tma_prefetch_desc(&tmap_a);
-        tma_prefetch_desc(&tmap_b);
-        if (p.tma_store) tma_prefetch_desc(&tmap_c);
-    }
-    if (warp == 1) {
-        tmem_alloc_pair(&tmem_base_slot, kWTmemCols);
-        tmem_relinquish_pair();
-    }
-    tc_fence_before();
-    cluster_sync_all();   // both CTAs' barriers initialised, tensor memory allocated
-    tc_fence_after();
-    // Set-up above overlapped the previous kernel of the stream; wait for it
-    // before the first global-memory access (a no-op without PDL).
-    pdl_wait_previous();
-    const uint32_t tmem_base = tmem_base_slot;
-
-    if (warp == 0) {
-        // ------------------------------------------------------------ TMA producer (both CTAs)
-        if (lane == 0) {
-            uint32_t it = 0;
-            bool ok = true;
-            for (uint32_t t = pair; t < total_tiles && ok; t += npairs) {
-                uint32_t mb, nb;
-                tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, mb, nb);
-                for (uint32_t kb = 0; kb < p.num_kb; ++kb, ++it) {
-                    const uint32_t s = it % kWStages;
-                    const uint32_t ph = (it / kWStages) & 1u;
-                    if (!mbar_wait(&empty_bar[s], ph ^ 1u, p.limit_ns, p.err, &abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * kWStageBytes);
-                    const uint32_t leader_full = mapa_shared(smem_addr(&full_bar[s]), 0);
-                    uint8_t *sa = ring + s * kWStageBytes;
-                    const int32_t k0 = static_cast<int32_t>(kb * kBK);
-                    const uint32_t n_first = nb * kWTileN + rank * 128u;
-                    tma_load_2d_pair(sa, &tmap_a, leader_full, k0,
-                                     static_cast<int32_t>(mb * kPTileM + rank * 128u));
-                    tma_load_2d_pair(sa + kPABytes, &tmap_b, leader_full, k0,
-                                     static_cast<int32_t>(n_first));
-                    tma_load_2d_pair(sa + kPABytes + kPBBytes, &tmap_b, leader_full, k0,
-                                     static_cast<int32_t>(n_first + 256u));
-                }
-            }
-            if (rank == 0) {
-                const uint32_t tail = it < kWStages ? it : kWStages;
-                for (uint32_t i = it - tail; i < it; ++i)
-                    mbar_wait(&full_bar[i % kWStages], (i / kWStages) & 1u, p.limit_ns, p.err,
-                              nullptr);
-            }
-        }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer (leader)
-        if (rank == 0 && lane == 0) {
-            constexpr uint32_t idesc = umma_idesc_i8(kPTileM, 256);
-            uint32_t it = 0, tcount = 0;
-            bool ok = true;
-            for (uint32_t t = pair; t < total_tiles && ok; t += npairs, ++tcount) {
-                const uint32_t empty_par = (tcount & 1u) ^ 1u;
-                const uint32_t hold = p.num_kb < kWStages ? p.num_kb : kWStages;
-                // D0 over the first `hold` k-blocks (stages held).
-                if (!mbar_wait(&tmem_empty_bar[0], empty_par, p.limit_ns, p.err, &abort_flag))
-                    break;
-                tc_fence_after();
-                for (uint32_t kb = 0; kb < hold; ++kb) {
-                    const uint32_t i = it + kb;
-                    if (!mbar_wait(&full_bar[i % kWStages], (i / kWStages) & 1u, p.limit_ns,
-                                   p.err, &abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t sa = smem_addr(ring + (i % kWStages) * kWStageBytes);
-                    const uint64_t adesc = umma_desc_k_sw128(sa);
-                    const uint64_t b0 = umma_desc_k_sw128(sa + kPABytes);
-#pragma unroll
-                    for (uint32_t kk = 0; kk < kBK / kUmmaK; ++kk)
-                        umma_i8_pair(tmem_base, adesc + 2u * kk, b0 + 2u * kk, idesc,
-                                     (kb | kk) != 0u);
-                }
-                if (!ok) break;
-                // D1 over the held k-blocks once the epilogue has read D1.
-                if (!mbar_wait(&tmem_empty_bar[1], empty_par, p.limit_ns, p.err, &abort_flag))
-                    break;
-                tc_fence_after();
-                for (uint32_t kb = 0; kb < hold; ++kb) {
-                    const uint32_t i = it + kb;
-                    const uint32_t sa = smem_addr(ring + (i % kWStages) * kWStageBytes);
-                    const uint64_t adesc = umma_desc_k_sw128(sa);
-                    const uint64_t b1 = umma_desc_k_sw128(sa + kPABytes + kPBBytes);
-#pragma unroll
-                    for (uint32_t kk = 0; kk < kBK / kUmmaK; ++kk)
-                        umma_i8_pair(tmem_base + 256u, adesc + 2u * kk, b1 + 2u * kk, idesc,
-                                     (kb | kk) != 0u);
-                    umma_commit_pair_mc(&empty_bar[i % kWStages], 0x3);
-                }
-                it += hold;
-                // Remaining k-blocks: D0 and D1 per stage.
-                for (uint32_t kb = hold; kb < p.num_kb; ++kb, ++it) {
-                    const uint32_t s = it % kWStages;
-                    if (!mbar_wait(&full_bar[s], (it / kWStages) & 1u, p.limit_ns, p.err,
-                                   &abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t sa = smem_addr(ring + s * kWStageBytes);
-                    const uint64_t adesc = umma_desc_k_sw128(sa);
-                    const uint64_t b0 = umma_desc_k_sw128(sa + kPABytes);
-                    const uint64_t b1 = umma_desc_k_sw128(sa + kPABytes + kPBBytes);
-#pragma unroll
-                    for (uint32_t kk = 0; kk < kBK / kUmmaK; ++kk) {
-                        umma_i8_pair(tmem_base, adesc + 2u * kk, b0 + 2u * kk, idesc, true);
-                        umma_i8_pair(tmem_base + 256u, adesc + 2u * kk, b1 + 2u * kk, idesc,
-                                     true);
-                    }
-                    umma_commit_pair_mc(&empty_bar[s], 0x3);
-                }
-                if (!ok) break;
-                umma_commit_pair_mc(&tmem_full_bar, 0x3);
-            }
-            umma_commit_pair_mc(&drain_bar, 0x1);
-            mbar_wait(&drain_bar, 0, p.limit_ns, p.err, nullptr);
-        }
-    } else {
-        // ------------------------------------------------------------ epilogue (both CTAs)
-        // Warp w reads TMEM lanes 32*(w%4)..+31.  For half h, warps 2-5 take
-        // tile columns 256h + 0..127 and warps 6-9 256h + 128..255, in 32x32
-        // chunks: dequantised in registers, written 128B-swizzled into the
-        // warp's 4 KiB staging buffer and stored to C by TMA (rows >= M and
-        // columns >= N clipped by the tensor map), or stored directly without
-        // a C tensor map.
-        const uint32_t lane_base = (warp & 3u) * 32u;
-        const uint32_t col_base = ((warp - 2u) >> 2) * 128u;
-        const bool vec_ok = (p.ldc % 4u == 0u) &&
-                            ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0u);
-        uint8_t *stage_out = ring + kWStages * kWStageBytes + (warp - 2u) * kPStageOutBytes;
-        float *my_row = reinterpret_cast<float *>(stage_out + lane * 128u);
-        const uint32_t leader_empty0 = mapa_shared(smem_addr(&tmem_empty_bar[0]), 0);
-        const uint32_t leader_empty1 = mapa_shared(smem_addr(&tmem_empty_bar[1]), 0);
-        uint32_t tcount = 0;
-        for (uint32_t t = pair; t < total_tiles; t += npairs, ++tcount) {
-            uint32_t mb, nb;
-            tile_coords(t, p.tiles_m, p.tiles_n, p.group_m, mb, nb);
-            // Scales and biases for the tile, fetched before the accumulators are ready.
-            const uint32_t m_first = mb * kPTileM + rank * 128u + lane_base;  // warp's first row
-            const uint32_t m = m_first + lane;
-            const bool row_ok = m < p.M;
-            const float sa = row_ok ? (p.scale_a ? __ldg(p.scale_a + m) : 1.0f) : 0.0f;
-            float sreg[8], breg[8];
-#pragma unroll
-            for (uint32_t c = 0; c < 8u; ++c)
-                fetch_col(p, nb * kWTileN + (c >> 2) * 256u + col_base + (c & 3u) * 32u + lane,
-                          sreg[c], breg[c]);
-            uint32_t ok = 0;
-            if (lane == 0)
-                ok = mbar_wait(&tmem_full_bar, tcount & 1u, p.limit_ns, p.err, &abort_flag);
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) break;
-            tc_fence_after();
-            float *crow = p.C + static_cast<uint64_t>(row_ok ? m : 0) * p.ldc;
-#pragma unroll
-            for (uint32_t h = 0; h < 2u; ++h) {
-                // The warp's 128 columns of half h go to registers in one
-                // round of loads, and the half is released before any of it
-                // is dequantised or stored: the next tile's MMAs into this
-                // half wait only for the tensor-memory reads.
-                uint32_t r[4][32];
-                __syncwarp();
-#pragma unroll
-                for (uint32_t c = 0; c < 4u; ++c)
-                    tmem_ld_32cols(tmem_base + (lane_base << 16) + h * 256u + col_base + c * 32u,
-                                   r[c]);
-                tmem_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(h ? leader_empty1 : leader_empty0);
-#pragma unroll
-                for (uint32_t c = 0; c < 4u; ++c) {
-                    const uint32_t col = h * 256u + col_base + c * 32u;
-                    const uint32_t n0 = nb * kWTileN + col;
-                    if (n0 >= p.N || m_first >= p.M) continue;  // warp-uniform
-                    dequant32_shfl_inplace_any(p.variant, r[c], sa, sreg[h * 4u + c], breg[h * 4u + c]);
-                    const float(&v)[32] = reinterpret_cast<const float(&)[32]>(r[c]);
-                    if (p.tma_store) {
-                        if (lane == 0) bulk_wait_read0();  // previous store has read the buffer
-                        __syncwarp();
-#pragma unroll
-                        for (uint32_t j = 0; j < 8u; ++j)
-                            *reinterpret_cast<uint4 *>(my_row + 4u * (j ^ (lane & 7u))) =
-                                make_uint4(r[c][4 * j], r[c][4 * j + 1], r[c][4 * j + 2],
-                                           r[c][4 * j + 3]);
-                        fence_proxy_async_smem();
-                        __syncwarp();
-                        if (lane == 0) {
-                            tma_store_2d(&tmap_c, stage_out, static_cast<int32_t>(n0),
-                                         static_cast<int32_t>(m_first));
-                            bulk_commit();
-                        }
-                    } else if (row_ok) {
-                        store_row32(v, crow, n0, p.N, vec_ok);
-                    }
-                }
-            }
-        }
-        // Shared memory must outlive the stores' reads; their global writes
-        // complete with the grid like any other store.
-        if (lane == 0) bulk_wait_read0();
-    }
-
-    // ---------------------------------------------------------------- teardown
-    tc_fence_before();
-    __syncthreads();
-    cluster_sync_all();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc_pair(tmem_base, kWTmemCols);
     }
 }
 
@@ -1661,17 +1274,17 @@ cudaError_t device_setup(int &max_pairs, int &max_wide_pairs) {
                                                 &cfg)) != cudaSuccess)
             return e;
         if (clusters < d.max_pairs) d.max_pairs = clusters;
-        cfg.blockDim = dim3(kPThreads, 1, 1);
-        if ((e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_wide_kernel,
+        if ((e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<8, 6, 224>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(kWSmemBytes))) != cudaSuccess)
+                                      static_cast<int>(pair_smem_bytes(8, 6, 224)))) != cudaSuccess ||
+            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<16, 5, 224>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(pair_smem_bytes(16, 5, 224)))) != cudaSuccess ||
+            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<8, 6, 256, true>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(pair_smem_bytes(8, 6)))) != cudaSuccess)
             return e;
-        cfg.dynamicSmemBytes = kWSmemBytes;
-        clusters = 0;
-        if ((e = cudaOccupancyMaxActiveClusters(&clusters, gemm_i8_tcgen05_pair_wide_kernel,
-                                                &cfg)) != cudaSuccess)
-            return e;
-        d.max_wide_pairs = clusters;
+        if ((e = wide_device_setup(d.max_wide_pairs)) != cudaSuccess) return e;
         d.done = true;
         if (std::getenv("VNPU_DEBUG"))
             std::fprintf(stderr, "[vnpu-b200] device %d: %d co-resident CTA pairs (256x256), %d (256x512)\n",
@@ -1697,6 +1310,61 @@ static uint32_t raster_group(uint32_t tiles_m, uint32_t tile_m, uint32_t K) {
     return static_cast<uint32_t>(g);
 }
 
+// Tile shape of the CTA-pair GEMM: 256x256 or 256x224 (pair kernel),
+// 256x512 or 256x448 (wide kernel), whichever has the least estimated time:
+// waves (tiles over co-resident pairs, rounded up) x tile width / the tile's
+// rate per output column relative to the 256x256 tile.  The wide tiles read a
+// quarter fewer operand bytes per MAC (about 10% faster per column at
+// K >= 8192, 2% at K = 4096, where more of the epilogue shows); 224-column
+// tiles read more operand bytes per MAC than the 256-column ones.  Rates
+// measured on B200 at M = K = 8192 (GEMM alone, us): N = 3584 pair 185.0,
+// pair-224 188.5, wide 186.7, wide-224 179.3; N = 7168 353.1 / 367.7 /
+// 339.6 / 322.0; N = 14336 683.8 / 806.8 / 651.2 / 633.7; N = 28672 wide
+// 1265-1345, wide-224 1304.  The wide kernel only takes NONE / RELU
+// epilogues (SiLU and GELU measured slower on it).
+// VNPU_B200_PAIR_WIDE=0|1 and VNPU_B200_PAIR_TN=224|256 pin the choice.
+// Returns the chosen shape's estimated cost (0 when none qualifies);
+// wide_only limits the choice to the wide kernel.
+double pick_pair_tile(uint32_t M, uint32_t N, uint32_t K, uint32_t epilogue, uint32_t pairs,
+                      uint32_t wide_pairs, bool have_wide, bool &wide, uint32_t &tn,
+                      bool wide_only = false) {
+    const uint32_t tiles_m = (M + kPTileM - 1) / kPTileM;
+    const double wide_rate = K >= 8192u ? 1.10 : 1.02;
+    const char *fw = std::getenv("VNPU_B200_PAIR_WIDE");
+    const char *ft = std::getenv("VNPU_B200_PAIR_TN");
+    double best = 0.0;
+    bool first = true;
+    for (int w = wide_only ? 1 : 0; w < 2; ++w) {
+        if (w && (!have_wide || (epilogue > 1u && !fw))) continue;
+        if (fw && (fw[0] == '1') != (w == 1)) continue;
+        for (uint32_t t : {256u, 224u}) {
+            if (ft && static_cast<uint32_t>(std::atoi(ft)) != t) continue;
+            const uint32_t cols = w ? 2u * t : t;
+            const uint32_t tiles = tiles_m * ((N + cols - 1) / cols);
+            const uint32_t cap = w ? wide_pairs : pairs;
+            // the wide tile needs a full wave to pay for its idle accumulator set
+            if (w && tiles < cap && !fw) continue;
+            const uint32_t waves = (tiles + cap - 1) / cap;
+            const double rate = (w ? wide_rate : 1.0) * (t == 224u ? (w ? 0.94 : 0.88) : 1.0);
+            const double cost = waves * static_cast<double>(cols) / rate;
+            // a 224-column tile must win clearly (3%): its rates are measured
+            // at M = K = 8192 only
+            if (first || cost < best * (t == 224u ? 0.97 : 0.995)) {
+                best = cost;
+                wide = w == 1;
+                tn = t;
+                first = false;
+            }
+        }
+    }
+    if (first) {
+        wide = false;
+        tn = 256;
+        return 0.0;
+    }
+    return best;
+}
+
 cudaError_t matmul_i8_scatter(const LaunchCtx &ctx, const MatmulI8 &p) {
     int max_pairs = 0, max_wide_pairs = 0;
     cudaError_t se = device_setup(max_pairs, max_wide_pairs);
@@ -1715,8 +1383,13 @@ cudaError_t matmul_i8_scatter(const LaunchCtx &ctx, const MatmulI8 &p) {
     tp.M = p.M;
     tp.N = p.N;
     tp.K = p.K;
+    // The pair kernel's tile width (256 or 224) by the same estimate as
+    // MATMUL_I8; the scatter epilogue has no wide-kernel form.
+    bool wide = false;
+    uint32_t tn = 256;
+    pick_pair_tile(p.M, p.N, p.K, p.epilogue, static_cast<uint32_t>(max_pairs), 0, false, wide, tn);
     tp.tiles_m = (p.M + kPTileM - 1) / kPTileM;
-    tp.tiles_n = (p.N + kPTileN - 1) / kPTileN;
+    tp.tiles_n = (p.N + tn - 1) / tn;
     tp.num_kb = (p.K + kBK - 1) / kBK;
     tp.group_m = raster_group(tp.tiles_m, kPTileM, p.K);
     tp.epilogue = p.epilogue;
@@ -1734,10 +1407,20 @@ cudaError_t matmul_i8_scatter(const LaunchCtx &ctx, const MatmulI8 &p) {
     const uint32_t tiles = tp.tiles_m * tp.tiles_n;
     const uint32_t cap = static_cast<uint32_t>(max_pairs);
     const uint32_t pairs = tiles < cap ? tiles : cap;
-    VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, 6>, dim3(2 * pairs),
-                           dim3(pair_threads(8)), pair_smem_bytes(8, 6), tmap_a, *p.tmap_b128,
-                           tmap_c, tp));
-    g_last_kernel.store("gemm_i8_tcgen05_pair_kernel", std::memory_order_relaxed);
+    if (tn == 224u) {
+        CUtensorMap tmap_b112;
+        if (!encode_tmap_kmajor_i8(&tmap_b112, p.Bt, p.k_stride, p.N, p.k_stride, kBK, 112))
+            return cudaErrorInvalidValue;
+        VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, 6, 224>, dim3(2 * pairs),
+                               dim3(pair_threads(8)), pair_smem_bytes(8, 6, 224), tmap_a, tmap_b112,
+                               tmap_c, tp));
+    } else {
+        VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, 6>, dim3(2 * pairs),
+                               dim3(pair_threads(8)), pair_smem_bytes(8, 6), tmap_a, *p.tmap_b128,
+                               tmap_c, tp));
+    }
+    g_last_kernel.store(tn == 224u ? "gemm_i8_tcgen05_pair_kernel<224>" : "gemm_i8_tcgen05_pair_kernel",
+                        std::memory_order_relaxed);
     count_launch(ctx);
     return cudaGetLastError();
 }
@@ -1780,6 +1463,79 @@ cudaError_t matmul_i8_pair_splitk(const LaunchCtx &ctx, const MatmulI8 &p, TcPar
     return e != cudaSuccess ? e : cudaGetLastError();
 }
 
+cudaError_t matmul_i8_swiglu(const LaunchCtx &ctx, const MatmulI8 &p, float *Y, uint32_t ldy,
+                             float alpha) {
+    const uint32_t I = p.N / 2u;
+    if ((p.N & 1u) || I == 0 || p.R || p.ndst) return cudaErrorInvalidValue;
+    const bool no_epi = std::getenv("VNPU_B200_NO_SWIGLU_EPI") != nullptr;
+    // Decode: one warp streams gate column j and up column I + j.
+    if (!no_epi && p.M <= 2u) {
+        const cudaError_t e = matmul_i8_swiglu_gemv_stream(ctx, p, Y, ldy, I, alpha);
+        if (e != cudaErrorInvalidValue) {
+            if (e == cudaSuccess) g_last_kernel.store("gemv_i8_stream_kernel+swiglu", std::memory_order_relaxed);
+            return e;
+        }
+    }
+    int max_pairs = 0, max_wide_pairs = 0;
+    cudaError_t se = device_setup(max_pairs, max_wide_pairs);
+    if (se != cudaSuccess) return se;
+    // The CTA pair's two B halves are the gate rows and the matching up rows.
+    CUtensorMap tmap_a;
+    const bool pair_ok = !no_epi && p.M > kBM && p.tmap_b128 && max_pairs > 0 &&
+                         p.fmap.form != kFormMixed &&
+                         choose_matmul_kernel(p.M, p.K, p.N, p.lda, p.A) == MatmulKernel::kTcgen05 &&
+                         encode_tmap_kmajor_i8(&tmap_a, p.A, p.K, p.M, p.lda, kBK, 128);
+    if (pair_ok) {
+        TcParams tp;
+        tp.scale_a = p.scale_a;
+        tp.scale_b = p.scale_b;
+        tp.bias = p.bias;
+        tp.C = Y;
+        tp.ldc = ldy;
+        tp.M = p.M;
+        tp.N = p.N;
+        tp.K = p.K;
+        tp.tiles_m = (p.M + kPTileM - 1) / kPTileM;
+        tp.tiles_n = (I + 127u) / 128u;
+        tp.num_kb = (p.K + kBK - 1) / kBK;
+        tp.group_m = raster_group(tp.tiles_m, kPTileM, p.K);
+        tp.epilogue = p.epilogue;
+        tp.form = p.fmap.form;
+        tp.variant = epi_variant(p.epilogue, p.bias != nullptr, p.fmap.form);
+        tp.err = ctx.err;
+        tp.limit_ns = ctx.wait_limit_ns;
+        tp.swiglu_i = I;
+        tp.swiglu_alpha = alpha;
+        CUtensorMap tmap_c;
+        tp.tma_store = (reinterpret_cast<uintptr_t>(Y) % 16u == 0u) && (ldy % 4u == 0u) &&
+                       encode_tmap_2d(&tmap_c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, Y, I, p.M,
+                                      static_cast<uint64_t>(ldy) * 4u, 32, 32,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!tp.tma_store) std::memset(&tmap_c, 0, sizeof(tmap_c));
+        const uint32_t tiles = tp.tiles_m * tp.tiles_n;
+        const uint32_t pairs = tiles < static_cast<uint32_t>(max_pairs) ? tiles
+                                                                        : static_cast<uint32_t>(max_pairs);
+        VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, 6, 256, true>,
+                               dim3(2 * pairs), dim3(pair_threads(8)), pair_smem_bytes(8, 6), tmap_a,
+                               *p.tmap_b128, tmap_c, tp));
+        g_last_kernel.store("gemm_i8_tcgen05_pair_kernel+swiglu", std::memory_order_relaxed);
+        count_launch(ctx);
+        return cudaGetLastError();
+    }
+    // Elsewhere: the product into stream-ordered scratch, then the halves.
+    float *scratch = nullptr;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void **>(&scratch),
+                                    static_cast<size_t>(p.M) * p.N * sizeof(float), ctx.stream);
+    if (e != cudaSuccess) return e;
+    MatmulI8 q = p;
+    q.C = scratch;
+    q.ldc = p.N;
+    e = matmul_i8(ctx, q);
+    if (e == cudaSuccess) e = swiglu_rows(ctx, scratch, p.N, Y, ldy, p.M, I, alpha);
+    cudaFreeAsync(scratch, ctx.stream);
+    return e;
+}
+
 cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
     int max_pairs = 0, max_wide_pairs = 0;
     cudaError_t se = device_setup(max_pairs, max_wide_pairs);
@@ -1811,20 +1567,23 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         // half-hidden epilogue weighs more), and the epilogue is light (NONE /
         // RELU: SiLU and GELU epilogues are slower on the wide tile).
         const uint32_t tiles_m = (p.M + kPTileM - 1) / kPTileM;
-        const uint32_t tiles_w = tiles_m * ((p.N + kWTileN - 1) / kWTileN);
         const uint32_t tiles_p = tiles_m * ((p.N + kPTileN - 1) / kPTileN);
         const uint32_t wp = static_cast<uint32_t>(max_wide_pairs > 0 ? max_wide_pairs : 1);
         const uint32_t pp = static_cast<uint32_t>(max_pairs > 0 ? max_pairs : 1);
-        const uint32_t waves_w = (tiles_w + wp - 1) / wp, waves_p = (tiles_p + pp - 1) / pp;
-        const uint32_t speedup_pct = p.K >= 8192u ? 110u : 102u;
-        bool wide = max_wide_pairs > 0 && tiles_w >= wp &&
-                    p.epilogue <= 1u /* NONE, RELU */ &&
-                    200u * waves_w < speedup_pct * waves_p;
-        if (const char *e = std::getenv("VNPU_B200_PAIR_WIDE"))
-            wide = max_wide_pairs > 0 && e[0] == '1';
-        if (mixed) wide = false;
+        // Tile shape: the one with the least estimated time, waves x tile
+        // width / relative rate per column (pair_tile_cost).
+        // (Shapes that split K keep the 256x256 tile: the split rule below.)
+        uint32_t tn = 256;
+        bool wide = false;
+        const bool no_splitk = std::getenv("VNPU_B200_NO_SPLITK") != nullptr;
+        const uint32_t kb_total = (p.K + kBK - 1) / kBK;
+        const bool splits_k = !no_splitk && p.N % 4u == 0u &&
+                              std::min(std::min(pp / tiles_p, 4u), kb_total / 8u) >= 2u;
+        if (!mixed && !splits_k)
+            pick_pair_tile(p.M, p.N, p.K, p.epilogue, pp, wp, max_wide_pairs > 0, wide, tn);
         tp.tiles_m = tiles_m;
-        tp.tiles_n = (p.N + (wide ? kWTileN : kPTileN) - 1) / (wide ? kWTileN : kPTileN);
+        const uint32_t tile_cols = wide ? 2u * tn : tn;
+        tp.tiles_n = (p.N + tile_cols - 1) / tile_cols;
         tp.num_kb = (p.K + kBK - 1) / kBK;
         // Split K when the 256x256 tiles leave at least half of the pairs idle
         // and K is long: each split (at least 8 k-blocks) sums its range into
@@ -1837,7 +1596,7 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         tp.err = ctx.err;
         tp.limit_ns = ctx.wait_limit_ns;
         uint32_t splits = 1;
-        if (!wide && p.N % 4u == 0u && std::getenv("VNPU_B200_NO_SPLITK") == nullptr) {
+        if (!wide && tn == 256u && p.N % 4u == 0u && !no_splitk) {
             uint32_t sk = pp / tiles_p;
             sk = std::min(sk, 4u);
             sk = std::min(sk, tp.num_kb / 8u);
@@ -1864,21 +1623,40 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         const uint32_t tiles = tp.tiles_m * tp.tiles_n;
         const uint32_t cap = static_cast<uint32_t>(wide ? max_wide_pairs : max_pairs);
         const uint32_t pairs = tiles < cap ? tiles : cap;
-        if (wide)
-            VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_wide_kernel, dim3(2 * pairs),
-                                   dim3(kPThreads), kWSmemBytes, tmap_a, *p.tmap_b128, tmap_c,
-                                   tp));
+        // 224-column tiles: each CTA loads 112 weight rows per stage (its own
+        // box height); the 128-row map serves the 256-column tiles.
+        CUtensorMap tmap_b112;
+        const CUtensorMap *tmap_b = p.tmap_b128;
+        if (tn == 224u) {
+            if (!encode_tmap_kmajor_i8(&tmap_b112, p.Bt, p.k_stride, p.N, p.k_stride, kBK, 112))
+                return cudaErrorInvalidValue;
+            tmap_b = &tmap_b112;
+        }
         // 16 epilogue warps: SiLU / GELU (latency-bound epilogue), or one short
         // tile per pair (the epilogue is most of the time): 512^3 9.3 -> 8.8 us
-        else if (p.epilogue >= 2 || (tiles <= cap && tp.num_kb <= 8u))
+        const bool epi16 = p.epilogue >= 2 || (tiles <= cap && tp.num_kb <= 8u);
+        if (wide)
+            VNPU_LAUNCH(launch_wide_pair(ctx.stream, tn, pairs, tmap_a, *tmap_b, tmap_c, tp));
+        else if (epi16 && tn == 224u)
+            VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<16, 5, 224>,
+                                   dim3(2 * pairs), dim3(pair_threads(16)),
+                                   pair_smem_bytes(16, 5, 224), tmap_a, *tmap_b, tmap_c, tp));
+        else if (epi16)
             VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<16, 5>, dim3(2 * pairs),
                                    dim3(pair_threads(16)), pair_smem_bytes(16, 5), tmap_a,
-                                   *p.tmap_b128, tmap_c, tp));
+                                   *tmap_b, tmap_c, tp));
+        else if (tn == 224u)
+            VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, 6, 224>,
+                                   dim3(2 * pairs), dim3(pair_threads(8)),
+                                   pair_smem_bytes(8, 6, 224), tmap_a, *tmap_b, tmap_c, tp));
         else
             VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, 6>, dim3(2 * pairs),
                                    dim3(pair_threads(8)), pair_smem_bytes(8, 6), tmap_a,
-                                   *p.tmap_b128, tmap_c, tp));
-        g_last_kernel.store(wide ? "gemm_i8_tcgen05_pair_wide_kernel" : "gemm_i8_tcgen05_pair_kernel",
+                                   *tmap_b, tmap_c, tp));
+        g_last_kernel.store(wide ? (tn == 224u ? "gemm_i8_tcgen05_pair_wide_kernel<224>"
+                                               : "gemm_i8_tcgen05_pair_wide_kernel")
+                                 : (tn == 224u ? "gemm_i8_tcgen05_pair_kernel<224>"
+                                               : "gemm_i8_tcgen05_pair_kernel"),
                             std::memory_order_relaxed);
         count_launch(ctx);
         return cudaGetLastError();

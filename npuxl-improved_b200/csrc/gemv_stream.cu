@@ -108,6 +108,16 @@ __device__ __forceinline__ int4 gs_act16(const GsParams &p, uint32_t m, uint32_t
                      static_cast<int>(w[3]));
 }
 
+// The gate/up projection with its SwiGLU (VNPU_B200_OP_MATMUL_I8_SWIGLU): a
+// warp owns gate column j and up column I + j of the [K][2I] weight and
+// writes Y[m][j] = swiglu(gate, up) * alpha.
+struct GsSwiglu {
+    float *Y;
+    uint32_t ldy;
+    uint32_t I;
+    float alpha;
+};
+
 // The rotation pair a warp of the QKV variant owns: section (Q, K, V), head,
 // index j < D/2, and the first column (the second is D/2 further).
 __device__ __forceinline__ void gs_qkv_pair(const GsQkv &x, uint32_t pair, uint32_t &sec,
@@ -126,7 +136,9 @@ template <int kM, int kC, typename Extra>
 __global__ void __launch_bounds__(kGsThreads) gemv_i8_stream_kernel(const GsParams p,
                                                                    const Extra x) {
     constexpr bool kQkv = std::is_same<Extra, GsQkv>::value;
+    constexpr bool kSw = std::is_same<Extra, GsSwiglu>::value;
     static_assert(!kQkv || (kM == 1 && kC == 2), "the QKV epilogue is one token, column pairs");
+    static_assert(!kSw || kC == 2, "the SwiGLU epilogue pairs a gate and an up column");
     extern __shared__ __align__(16) uint8_t gs_smem[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint32_t ncol[kC];
@@ -139,6 +151,11 @@ __global__ void __launch_bounds__(kGsThreads) gemv_i8_stream_kernel(const GsPara
         if (warp_valid) gs_qkv_pair(x, pair, q_sec, q_h, q_j, n0);
         ncol[0] = n0;
         ncol[1] = n0 + x.D / 2u;
+    } else if constexpr (kSw) {
+        const uint32_t j = blockIdx.x * kGsWarps + warp;
+        warp_valid = j < x.I;
+        ncol[0] = j;
+        ncol[1] = x.I + j;
     } else {
 #pragma unroll
         for (int c = 0; c < kC; ++c) ncol[c] = (blockIdx.x * kGsWarps + warp) * kC + c;
@@ -260,6 +277,18 @@ __global__ void __launch_bounds__(kGsThreads) gemv_i8_stream_kernel(const GsPara
         if (q_sec == 1 && q_j == 0 && x.mask)
             x.mask[static_cast<uint64_t>(q_h) * x.cap + static_cast<uint32_t>(pos)] = 0.0f;
         return;
+    } else if constexpr (kSw) {
+        // Gate and up dequantised as MATMUL_I8 would, then SWIGLU_F32's
+        // expression (src/kernels/llm.cpp:289-306).
+#pragma unroll
+        for (int m = 0; m < kM; ++m) {
+            const float g = ref_dequant(acc[0][m], e_sa[m], e_sb[0], has_bias, e_bias[0],
+                                        p.epilogue, form_at(p.fmap, static_cast<uint32_t>(m), ncol[0]));
+            const float u = ref_dequant(acc[1][m], e_sa[m], e_sb[1], has_bias, e_bias[1],
+                                        p.epilogue, form_at(p.fmap, static_cast<uint32_t>(m), ncol[1]));
+            const float s = __fdiv_rn(g, __fadd_rn(1.0f, ref_exp256_lane(-g)));
+            x.Y[static_cast<uint64_t>(m) * x.ldy + ncol[0]] = __fmul_rn(__fmul_rn(s, u), x.alpha);
+        }
     } else {
 #pragma unroll
         for (int c = 0; c < kC; ++c) {
@@ -484,6 +513,15 @@ cudaError_t matmul_i8_gemv_stream(const LaunchCtx &ctx, const MatmulI8 &p, const
     }
     return p.M == 1 ? gs_launch<1, 1>(ctx, g, grid, GsPlain{})
                     : gs_launch<2, 1>(ctx, g, grid, GsPlain{});
+}
+
+cudaError_t matmul_i8_swiglu_gemv_stream(const LaunchCtx &ctx, const MatmulI8 &p, float *Y,
+                                         uint32_t ldy, uint32_t I, float alpha) {
+    if (p.N != 2u * I || I == 0 || !gemv_stream_supported(p, 2)) return cudaErrorInvalidValue;
+    const GsSwiglu x{Y, ldy, I, alpha};
+    const uint32_t grid = (I + kGsWarps - 1) / kGsWarps;
+    return p.M == 1 ? gs_launch<1, 2>(ctx, gs_params(p), grid, x)
+                    : gs_launch<2, 2>(ctx, gs_params(p), grid, x);
 }
 
 bool gemv_mma_supported(const MatmulI8 &p) {

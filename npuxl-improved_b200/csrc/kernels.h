@@ -117,6 +117,15 @@ cudaError_t matmul_i8(const LaunchCtx &ctx, const MatmulI8 &p);
 // cols_per_warp x k_stride bytes of shared memory per CTA (<= 200 KiB).
 // R: C = R + out.
 bool gemv_stream_supported(const MatmulI8 &p, uint32_t cols_per_warp);
+// The gate/up GEMV (M <= 2) with the SwiGLU epilogue: B is [K][2I].
+cudaError_t matmul_i8_swiglu_gemv_stream(const LaunchCtx &ctx, const MatmulI8 &p, float *Y,
+                                         uint32_t ldy, uint32_t I, float alpha);
+// MATMUL_I8 of a [K][2I] gate/up weight followed by SWIGLU_F32 of its halves
+// into Y (rows x I, row stride ldy): the SwiGLU in the GEMM's epilogue where
+// the CTA-pair kernel or the streaming GEMV takes the shape, else MATMUL_I8
+// into stream-ordered scratch and swiglu_rows.
+cudaError_t matmul_i8_swiglu(const LaunchCtx &ctx, const MatmulI8 &p, float *Y, uint32_t ldy,
+                             float alpha);
 // M <= 8 with the products on mma.sync (gemv_stream.cu); groups = 8-column
 // groups per CTA (1, 2 or 4).
 bool gemv_mma_supported(const MatmulI8 &p);
@@ -210,6 +219,9 @@ cudaError_t rope(const LaunchCtx &ctx, float *Q, float *K, const int32_t *positi
                  uint32_t batch, uint32_t heads, uint32_t q_seq, uint32_t k_seq,
                  uint32_t head_dim, uint32_t position_offset, uint32_t interleaved,
                  float scaling, const float *inv_freq_host);
+// Y[r][j] = swiglu(C[r][j], C[r][I + j]) * alpha, the SWIGLU_F32 expression.
+cudaError_t swiglu_rows(const LaunchCtx &ctx, const float *C, uint32_t ldc, float *Y, uint32_t ldy,
+                        uint32_t rows, uint32_t I, float alpha);
 cudaError_t swiglu(const LaunchCtx &ctx, const float *gate, const float *up, float *Y,
                    uint64_t count, float alpha);
 cudaError_t add(const LaunchCtx &ctx, const float *A, const float *B, float *Y, uint64_t count,

@@ -347,6 +347,54 @@ void exec_matmul_i8(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags,
 static_assert(sizeof(vnpu_b200_matmul_i8_shard_args_t) <= sizeof(vnpu_command_t::args),
               "shard args fit the command");
 
+static_assert(sizeof(vnpu_b200_matmul_i8_swiglu_args_t) <= sizeof(vnpu_command_t::args),
+              "matmul + swiglu args fit the command");
+
+// MATMUL_I8 of a [K][2I] gate/up weight, then SWIGLU_F32 of its halves: the
+// validation of exec_matmul_i8, the rounding forms of the 2I-wide product.
+void exec_matmul_i8_swiglu(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags,
+                           const LaunchCtx &ctx, Accounting &acc) {
+    vnpu_b200_matmul_i8_swiglu_args_t in;
+    std::memcpy(&in, cmd.args.raw, sizeof(in));
+    vnpu_packed_weights_t *w = in.B;
+    if (!in.A || !w || !in.Y || !in.M || !in.K || !in.N || (in.N & 1u))
+        throw CommandError("invalid matmul_i8_swiglu arguments", VNPU_ERR_INVALID_ARGUMENT);
+    if (w->K != in.K || w->N != in.N) throw CommandError("packed weight shape mismatch");
+    if (w->device != s->device) throw CommandError("packed weights belong to another device");
+    const uint32_t I = in.N / 2u;
+    const uint32_t lda = in.lda ? in.lda : in.K;
+    const uint32_t ldy = in.ldy ? in.ldy : I;
+    if (lda < in.K || ldy < I)
+        throw CommandError("invalid leading dimensions", VNPU_ERR_INVALID_ARGUMENT);
+    Staging st(s);
+    MatmulI8 p;
+    p.A = st.in(in.A, static_cast<uint64_t>(in.M - 1) * lda + in.K);
+    p.lda = lda;
+    p.Bt = w->bt;
+    p.k_stride = w->k_stride;
+    p.scale_a = st.in(in.scale_a, sizeof(float) * in.M);
+    p.scale_b = w->scales;
+    p.bias = st.in(in.bias, sizeof(float) * in.N);
+    const uint64_t y_span = (static_cast<uint64_t>(in.M - 1) * ldy + I) * sizeof(float);
+    float *Y = st.out(in.Y, y_span, ldy != I);
+    p.C = nullptr;
+    p.M = in.M;
+    p.K = in.K;
+    p.N = in.N;
+    p.epilogue = in.epilogue;
+    p.fmap = i8_form_map(s->device, VNPU_UNIT_AUTO, flags, in.M, in.K, in.N, in.bias != nullptr,
+                         in.epilogue);
+    p.tmap_b = w->tmap_ok ? &w->tmap : nullptr;
+    p.tmap_b128 = w->tmap128_ok ? &w->tmap128 : nullptr;
+    cuda_check(matmul_i8_swiglu(ctx, p, Y, ldy, in.alpha == 0.0f ? 1.0f : in.alpha),
+               "matmul_i8_swiglu launch");
+    st.finish();
+    acc.bytes_read = static_cast<uint64_t>(in.M) * in.K + static_cast<uint64_t>(in.K) * in.N;
+    acc.bytes_written = static_cast<uint64_t>(in.M) * I * sizeof(float);
+    acc.flops = 2ull * in.M * in.K * in.N + 4ull * in.M * I;
+    acc.dma = st.staged_bytes();
+}
+
 // MATMUL_I8 of the columns col_base.. of an n_full-wide product: the same
 // validation and kernels as exec_matmul_i8, with every element rounded as in
 // the whole product.
@@ -1126,7 +1174,7 @@ vnpu_status_t execute_command(vnpu_stream_t *s, const vnpu_command_t &cmd, uint3
         cmd.opcode != VNPU_B200_OP_SWIGLU_QUANTIZE_I8 && cmd.opcode != VNPU_B200_OP_KV_APPEND &&
         cmd.opcode != VNPU_B200_OP_MATMUL_I8_SCATTER &&
         cmd.opcode != VNPU_B200_OP_QKV_ROPE_APPEND && cmd.opcode != VNPU_B200_OP_MATMUL_I8_RESIDUAL &&
-        cmd.opcode != VNPU_B200_OP_MATMUL_I8_SHARD)
+        cmd.opcode != VNPU_B200_OP_MATMUL_I8_SHARD && cmd.opcode != VNPU_B200_OP_MATMUL_I8_SWIGLU)
         return VNPU_ERR_INVALID_COMMAND;
     dev->last_opcode.store(cmd.opcode);
     const bool tracing = dev->trace.enabled.load();
@@ -1171,6 +1219,7 @@ vnpu_status_t execute_command(vnpu_stream_t *s, const vnpu_command_t &cmd, uint3
         case VNPU_B200_OP_QKV_ROPE_APPEND: exec_qkv_rope_append(s, cmd, flags, ctx, acc); break;
         case VNPU_B200_OP_MATMUL_I8_RESIDUAL: exec_matmul_i8_residual(s, cmd, flags, ctx, acc); break;
         case VNPU_B200_OP_MATMUL_I8_SHARD: exec_matmul_i8_shard(s, cmd, flags, ctx, acc); break;
+        case VNPU_B200_OP_MATMUL_I8_SWIGLU: exec_matmul_i8_swiglu(s, cmd, flags, ctx, acc); break;
         case VNPU_OP_MEMSET: exec_memset(s, cmd, acc); break;
         case VNPU_OP_PACK_WEIGHTS_I8: exec_pack(s, cmd, acc); break;
         default:
@@ -1283,6 +1332,7 @@ const char *opcode_name(uint32_t op) {
     if (op == VNPU_B200_OP_QKV_ROPE_APPEND) return "QKV_ROPE_APPEND";
     if (op == VNPU_B200_OP_MATMUL_I8_RESIDUAL) return "MATMUL_I8_RESIDUAL";
     if (op == VNPU_B200_OP_MATMUL_I8_SHARD) return "MATMUL_I8_SHARD";
+    if (op == VNPU_B200_OP_MATMUL_I8_SWIGLU) return "MATMUL_I8_SWIGLU";
     return op < sizeof(names) / sizeof(names[0]) ? names[op] : "UNKNOWN";
 }
 

@@ -193,11 +193,16 @@ def _cmd(op, field, args):
 class B200Block:
     """The block with every tensor resident in HBM."""
 
-    def __init__(self, cfg: BlockConfig, lib, dev, torch, fused: bool = True):
+    def __init__(self, cfg: BlockConfig, lib, dev, torch, fused: bool = True,
+                 swiglu_epilogue: bool = True):
         self.cfg, self.lib, self.dev, self.t = cfg, lib, dev, torch
         # B200 opcodes: fused RMSNorm/SwiGLU -> QUANTIZE_I8 prologues, the QKV
         # projection with RoPE + cache append, projections with the residual add
         self.fused = fused
+        # with fused: the gate/up projection with the SwiGLU in its epilogue
+        # (VNPU_B200_OP_MATMUL_I8_SWIGLU) instead of the SwiGLU -> QUANTIZE_I8
+        # prologue of the down projection
+        self.swiglu_epilogue = fused and swiglu_epilogue
         self.stream = torch.cuda.ExternalStream(lib.b200_stream_handle(dev.stream))
         w, (n1, n2) = make_weights(cfg)
         self.n1 = torch.from_numpy(n1).cuda()
@@ -368,6 +373,24 @@ class B200Block:
                 acmd.flags = vnpu.CMD_FLAG_ATTN_TOKEN_MAJOR
             self._submit([acmd])
             attn = O if tok_major else O[0].transpose(0, 1).reshape(T, d).contiguous()
+            if self.swiglu_epilogue:
+                # O projection + residual; RMSNorm -> QUANTIZE_I8; the gate/up
+                # projection writes swiglu(gate, up) (MATMUL_I8_SWIGLU); the
+                # down projection quantizes it and adds the residual.
+                cmds, x1 = self._gemm_cmds(attn, "o", f"x1{T}", residual=x)
+                w, K_in, N_gu = self.w["gate_up"]
+                a8, sa = self._act_bufs("gate_up", T)
+                pro = vnpu.b200_command(vnpu.OP_B200_RMSNORM_QUANTIZE_I8, vnpu.RmsnormQuantizeArgs(
+                    x1.data_ptr(), self.n2.data_ptr(), None, a8.data_ptr(), sa.data_ptr(), T, d,
+                    cfg.eps, 0))
+                ff = self._buf(f"ff{T}", (T, cfg.inter))
+                sw = vnpu.b200_command(vnpu.OP_B200_MATMUL_I8_SWIGLU, vnpu.MatmulI8SwigluArgs(
+                    a8.data_ptr(), w, sa.data_ptr(), None, ff.data_ptr(), T, K_in, N_gu, 0, 0, 0,
+                    1.0, 0))
+                cmds3, y = self._gemm_cmds(ff, "down", f"y{T}", residual=x1)
+                self._submit(cmds + [pro, sw] + cmds3)
+                self._keep = (Q, K, V, attn, ff)
+                return y
             if self.fused:
                 # the residual adds ride on the O and down projections
                 # (VNPU_B200_OP_MATMUL_I8_RESIDUAL)

@@ -244,6 +244,15 @@ class MatmulI8ShardArgs(C.Structure):
                 ("epilogue", u32), ("n_full", u32), ("col_base", u32)]
 
 
+OP_B200_MATMUL_I8_SWIGLU = 0x108
+
+
+class MatmulI8SwigluArgs(C.Structure):
+    _fields_ = [("A", vp), ("B", vp), ("scale_a", vp), ("bias", vp), ("Y", vp),
+                ("M", u32), ("K", u32), ("N", u32), ("lda", u32), ("ldy", u32), ("epilogue", u32),
+                ("alpha", C.c_float), ("reserved0", u32)]
+
+
 def b200_command(opcode: int, args: C.Structure) -> "Command":
     """A command whose arguments are a B200 extension struct (copied into args.raw)."""
     c = Command()
@@ -510,6 +519,19 @@ class Device:
         if check:
             self.lib.check(rc, "quantize_i8")
         return rc
+
+    def matmul_i8_swiglu(self, A, w, scale_a, bias, Y, M, K, N, lda=0, ldy=0, epilogue=EPI_NONE,
+                         alpha=1.0, flags=0, sync=True) -> int:
+        """MATMUL_I8 of the [K][N = 2I] gate/up weight and SWIGLU_F32 of its
+        halves into Y (M x I), as one VNPU_B200_OP_MATMUL_I8_SWIGLU command."""
+        a = MatmulI8SwigluArgs(ptr(A), w, ptr(scale_a), ptr(bias), ptr(Y), M, K, N, lda, ldy,
+                               epilogue, alpha, 0)
+        cmd = b200_command(OP_B200_MATMUL_I8_SWIGLU, a)
+        cmd.flags = flags
+        rc = self.submit([cmd])
+        if rc != OK or not sync:
+            return rc
+        return self.sync()
 
     def matmul_i8_scatter(self, A, w, scale_a, bias, dsts, M, K, N, ldd, col_offset,
                           epilogue=EPI_NONE, lda=0, sync=True, flags=0) -> int:

@@ -24,10 +24,10 @@ def torch():
     return pytest.importorskip("torch")
 
 
-def _run_device(b200_lib, torch, cfg, x, toks, graph, fused=True):
+def _run_device(b200_lib, torch, cfg, x, toks, graph, fused=True, swiglu_epilogue=True):
     from llm_block import B200Block
     dev = vnpu.Device(b200_lib)
-    blk = B200Block(cfg, b200_lib, dev, torch, fused=fused)
+    blk = B200Block(cfg, b200_lib, dev, torch, fused=fused, swiglu_epilogue=swiglu_epilogue)
     outs = [blk.forward(torch.from_numpy(x).cuda(), 0).cpu().numpy()]
     first = True
     for i, t in enumerate(toks):
@@ -52,14 +52,17 @@ def _run_device(b200_lib, torch, cfg, x, toks, graph, fused=True):
     return outs
 
 
-@pytest.mark.parametrize("graph,fused", [(False, False), (False, True), (True, True)])
-def test_block_device_equals_host_driver(b200_lib, torch, graph, fused):
+@pytest.mark.parametrize("graph,fused,swiglu_epilogue", [
+    (False, False, False), (False, True, True), (True, True, True),
+    (True, True, False),   # the SwiGLU -> QUANTIZE_I8 prologue instead of the epilogue
+])
+def test_block_device_equals_host_driver(b200_lib, torch, graph, fused, swiglu_epilogue):
     from llm_block import BlockConfig, HostBlock
     cfg = BlockConfig(d=256, heads=4, inter=704, cap=48)
     rng = np.random.default_rng(5)
     x = rng.normal(0, 1, (20, cfg.d)).astype(np.float32)
     toks = [rng.normal(0, 1, (1, cfg.d)).astype(np.float32) for _ in range(5)]
-    dev_outs = _run_device(b200_lib, torch, cfg, x, toks, graph, fused)
+    dev_outs = _run_device(b200_lib, torch, cfg, x, toks, graph, fused, swiglu_epilogue)
     host = HostBlock(cfg, lib=b200_lib)
     host_outs = [host.forward(x, 0)] + [host.forward(t, x.shape[0] + i) for i, t in enumerate(toks)]
     host.close()

@@ -216,3 +216,74 @@ def test_residual_host_operands(gpu, oracle):
         assert bits_equal(out, oracle.add(R, prod, 1.0, 1.0, 0))
     finally:
         gpu.unpack(w)
+
+
+# ------------------------------------------------------------------ MATMUL_I8_SWIGLU
+@pytest.mark.parametrize("M,K,I,bias_on,ldy_pad,alpha,kernel", [
+    (1, 4096, 1024, False, 0, 1.0, "gemv_i8_stream_kernel+swiglu"),   # decode token
+    (1, 4096, 1000, True, 3, 0.5, "gemv_i8_stream_kernel+swiglu"),    # bias: the 2I-wide forms
+    (2, 1024, 520, False, 0, 1.0, "gemv_i8_stream_kernel+swiglu"),
+    (5, 1024, 700, True, 0, 1.0, None),                                # product, then the halves
+    (300, 512, 1000, False, 0, 1.0, "gemm_i8_tcgen05_pair_kernel+swiglu"),  # ragged I
+    (257, 128, 256, False, 1, 2.0, "gemm_i8_tcgen05_pair_kernel+swiglu"),   # direct stores
+    (512, 4096, 11008, False, 0, 1.0, "gemm_i8_tcgen05_pair_kernel+swiglu"),  # block prefill
+])
+def test_matmul_swiglu_equals_matmul_then_swiglu(gpu, oracle, torch, M, K, I, bias_on, ldy_pad,
+                                                 alpha, kernel):
+    """VNPU_B200_OP_MATMUL_I8_SWIGLU gives the bits of MATMUL_I8 on the
+    [K][2I] gate/up weight followed by SWIGLU_F32 of the output's halves (the
+    reference block, tools/llm_bench.cpp:298-311), unflagged: each element in
+    the rounding form it has in the 2I-wide product."""
+    rng = np.random.default_rng(M * 3 + K + I)
+    N = 2 * I
+    w = _weights(gpu, oracle, rng, K, N)
+    try:
+        A, sa = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
+        A_d = torch.from_numpy(A).cuda()
+        sa_d = torch.from_numpy(sa).cuda()
+        bias = (torch.from_numpy(rng.normal(0, 0.01, N).astype(np.float32)).cuda()
+                if bias_on else None)
+        C = torch.full((M, N), float("nan"), device="cuda")
+        assert _submit(gpu, [_matmul_cmd(A_d.data_ptr(), w, sa_d.data_ptr(),
+                                         bias.data_ptr() if bias is not None else None,
+                                         C.data_ptr(), M, K, N)]) == vnpu.OK
+        g = C[:, :I].contiguous()
+        u = C[:, I:].contiguous()
+        want = torch.empty((M, I), device="cuda")
+        gpu.swiglu(g.data_ptr(), u.data_ptr(), want.data_ptr(), M * I, alpha)
+        ldy = I + ldy_pad
+        Y = torch.full((M, ldy), float("nan"), device="cuda")
+        assert gpu.matmul_i8_swiglu(A_d, w, sa_d, bias, Y, M, K, N, ldy=ldy, alpha=alpha) == vnpu.OK
+        if kernel:
+            assert gpu.lib.b200_last_matmul_kernel().decode() == kernel
+        assert bits_equal(Y[:, :I].cpu().numpy(), want.cpu().numpy())
+        if ldy_pad:
+            assert torch.isnan(Y[:, I:]).all()   # nothing written past I
+        # and against the oracle on a few rows (block form: no bias here)
+        if not bias_on and M <= 512:
+            B, sb = oracle.quantize(np.random.default_rng(M * 3 + K + I).normal(0, 0.02, (K, N))
+                                    .astype(np.float32), 1)
+            rows = np.unique(np.r_[0, M // 2, M - 1])
+            Co = oracle.matmul_i8(A[rows], B, sa[rows], sb, None, 0, 0)
+            Yo = oracle.swiglu(Co[:, :I].copy(), Co[:, I:].copy(), alpha)
+            assert bits_equal(Y[rows, :I].cpu().numpy(), Yo)
+    finally:
+        gpu.unpack(w)
+
+
+def test_matmul_swiglu_host_operands(gpu, oracle):
+    """Host A / scales in and host Y out, staged through HBM."""
+    M, K, I = 384, 1024, 640
+    rng = np.random.default_rng(5)
+    w = _weights(gpu, oracle, rng, K, 2 * I)
+    try:
+        A, sa = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
+        Y = np.full((M, I), np.nan, np.float32)
+        assert gpu.matmul_i8_swiglu(A, w, sa, None, Y, M, K, 2 * I) == vnpu.OK
+        B, sb = oracle.quantize(np.random.default_rng(5).normal(0, 0.02, (K, 2 * I))
+                                .astype(np.float32), 1)
+        rows = np.arange(0, M, 41)
+        Co = oracle.matmul_i8(A[rows], B, sa[rows], sb, None, 0, 0)
+        assert bits_equal(Y[rows], oracle.swiglu(Co[:, :I].copy(), Co[:, I:].copy(), 1.0))
+    finally:
+        gpu.unpack(w)

@@ -475,6 +475,7 @@ def test_pair_and_single_cta_kernels_agree(gpu, oracle, monkeypatch, M, K, N):
     B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
     bias = rng.normal(0, 0.01, N).astype(np.float32)
     monkeypatch.setenv("VNPU_B200_NO_SPLITK", "1")
+    monkeypatch.setenv("VNPU_B200_PAIR_TN", "256")
     outs = []
     for no_pair in (False, True):
         if no_pair:
@@ -508,6 +509,7 @@ def test_splitk_pair_kernel_agrees(gpu, oracle, monkeypatch, M, K, N, epi, form,
     B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
     bias = rng.normal(0, 0.01, N).astype(np.float32) if bias_on else None
     ldc = N + pad if pad else 0
+    monkeypatch.setenv("VNPU_B200_PAIR_TN", "256")
     outs = []
     for split in (True, False):
         if split:
@@ -591,6 +593,7 @@ def test_wide_pair_kernel_agrees(gpu, oracle, monkeypatch, M, K, N, epi, form, p
     bias = rng.normal(0, 0.01, N).astype(np.float32)
     ldc = N + pad if pad else 0
     monkeypatch.setenv("VNPU_B200_NO_SPLITK", "1")
+    monkeypatch.setenv("VNPU_B200_PAIR_TN", "256")
     outs = []
     for wide in ("1", "0"):
         monkeypatch.setenv("VNPU_B200_PAIR_WIDE", wide)
@@ -605,6 +608,45 @@ def test_wide_pair_kernel_agrees(gpu, oracle, monkeypatch, M, K, N, epi, form, p
     assert bits_equal(outs[0], outs[1])
     rows = np.unique(np.r_[np.arange(0, M, 17), M - 1])
     assert bits_equal(outs[0][rows], oracle.matmul_i8(A[rows], B, sa[rows], sb, bias, epi, form))
+
+
+@pytest.mark.parametrize("M,K,N,epi,form,pad", [
+    (129, 256, 224, 3, 0, 0),      # one partial tile, exactly one 224-column tile
+    (300, 1008, 700, 2, 0, 0),     # ragged K and N
+    (257, 128, 449, 1, 1, 0),      # one k-block; N one past two 224-column tiles
+    (512, 384, 1024, 2, 2, 0),     # three k-blocks
+    (2000, 640, 2056, 2, 0, 3),    # ldc % 4 != 0: direct stores
+    (1024, 2048, 3584, 0, 0, 0),   # the 8-way shard width of 28672 (16 x 224)
+    (4096, 1024, 7168, 0, 0, 0),   # the 4-way shard width (16 x 448): several waves
+])
+def test_224_column_tiles_agree(gpu, oracle, monkeypatch, M, K, N, epi, form, pad):
+    """The 224-column tiles (256x224 pair kernel, 256x448 wide kernel: each
+    CTA loads 112 weight rows per stage) give the same bits as the 256x256
+    pair kernel and the oracle."""
+    rng = np.random.default_rng(M * 5 + K + N)
+    A, sa = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
+    B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
+    bias = rng.normal(0, 0.01, N).astype(np.float32)
+    ldc = N + pad if pad else 0
+    monkeypatch.setenv("VNPU_B200_NO_SPLITK", "1")
+    outs = []
+    for wide, tn, name in (("0", "256", "gemm_i8_tcgen05_pair_kernel"),
+                           ("0", "224", "gemm_i8_tcgen05_pair_kernel<224>"),
+                           ("1", "224", "gemm_i8_tcgen05_pair_wide_kernel<224>")):
+        monkeypatch.setenv("VNPU_B200_PAIR_WIDE", wide)
+        monkeypatch.setenv("VNPU_B200_PAIR_TN", tn)
+        Cbuf = np.full((M, ldc), np.nan, np.float32) if pad else None
+        C = run_matmul(gpu, A, B, sa, sb, bias, epi, form, ldc=ldc, Cbuf=Cbuf)
+        assert gpu.lib.b200_last_matmul_kernel().decode() == name
+        outs.append(C[:, :N].copy())
+        if pad:
+            assert np.isnan(C[:, N:]).all()   # nothing written past N
+    monkeypatch.delenv("VNPU_B200_PAIR_WIDE", raising=False)
+    monkeypatch.delenv("VNPU_B200_PAIR_TN", raising=False)
+    assert bits_equal(outs[0], outs[1])
+    assert bits_equal(outs[0], outs[2])
+    rows = np.unique(np.r_[np.arange(0, M, 17), M - 1])
+    assert bits_equal(outs[1][rows], oracle.matmul_i8(A[rows], B, sa[rows], sb, bias, epi, form))
 
 
 @pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8])
