@@ -1280,9 +1280,9 @@ cudaError_t device_setup(int &max_pairs, int &max_wide_pairs) {
             (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<16, 5, 224>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(pair_smem_bytes(16, 5, 224)))) != cudaSuccess ||
-            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<8, 6, 256, true>,
+            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<16, 5, 256, true>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(pair_smem_bytes(8, 6)))) != cudaSuccess)
+                                      static_cast<int>(pair_smem_bytes(16, 5)))) != cudaSuccess)
             return e;
         if ((e = wide_device_setup(d.max_wide_pairs)) != cudaSuccess) return e;
         d.done = true;
@@ -1515,9 +1515,11 @@ cudaError_t matmul_i8_swiglu(const LaunchCtx &ctx, const MatmulI8 &p, float *Y, 
         const uint32_t tiles = tp.tiles_m * tp.tiles_n;
         const uint32_t pairs = tiles < static_cast<uint32_t>(max_pairs) ? tiles
                                                                         : static_cast<uint32_t>(max_pairs);
-        VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, 6, 256, true>,
-                               dim3(2 * pairs), dim3(pair_threads(8)), pair_smem_bytes(8, 6), tmap_a,
-                               *p.tmap_b128, tmap_c, tp));
+        // 16 epilogue warps: the SwiGLU's exp and division per element make
+        // the epilogue latency-bound, as with the SiLU / GELU epilogues.
+        VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<16, 5, 256, true>,
+                               dim3(2 * pairs), dim3(pair_threads(16)), pair_smem_bytes(16, 5),
+                               tmap_a, *p.tmap_b128, tmap_c, tp));
         g_last_kernel.store("gemm_i8_tcgen05_pair_kernel+swiglu", std::memory_order_relaxed);
         count_launch(ctx);
         return cudaGetLastError();

@@ -19,10 +19,14 @@ namespace vnpu_b200 {
 namespace {
 
 constexpr int kQThreads = 256;
-constexpr int kQRegVec = 8;  // float4 per thread kept in registers: rows <= 8192
+// float4 per thread kept in registers: 8 (rows <= 8192, more CTAs per SM)
+// or 12 (rows <= 12288, e.g. the decoder block's 11008-wide SwiGLU output,
+// which would otherwise be read twice).
+constexpr int kQRegVecNarrow = 8;
+constexpr int kQRegVecWide = 12;
 
 // One CTA per row; vector path: cols % 4 == 0 and 16-byte aligned rows.
-template <bool kVec>
+template <bool kVec, int kQRegVec = kQRegVecNarrow>
 __global__ void __launch_bounds__(kQThreads) quantize_rows_kernel(const float *__restrict__ X,
                                                                   int8_t *__restrict__ Y,
                                                                   float *__restrict__ scales,
@@ -200,7 +204,12 @@ cudaError_t quantize_rows(const LaunchCtx &ctx, const float *X, int8_t *Y, float
     if (rows > 0x7fffffffull) return cudaErrorInvalidValue;
     const bool vec = (cols % 4 == 0) && (reinterpret_cast<uintptr_t>(X) % 16 == 0) &&
                      (reinterpret_cast<uintptr_t>(Y) % 4 == 0);
-    if (vec)
+    if (vec && cols > static_cast<uint64_t>(kQThreads) * 4 * kQRegVecNarrow &&
+        cols <= static_cast<uint64_t>(kQThreads) * 4 * kQRegVecWide)
+        VNPU_LAUNCH(launch_pdl(ctx.stream, quantize_rows_kernel<true, kQRegVecWide>,
+                               dim3(static_cast<unsigned>(rows)), dim3(kQThreads), 0, X, Y, scales,
+                               cols));
+    else if (vec)
         VNPU_LAUNCH(launch_pdl(ctx.stream, quantize_rows_kernel<true>, dim3(static_cast<unsigned>(rows)), dim3(kQThreads), 0, 
             X, Y, scales, cols));
     else
