@@ -45,7 +45,12 @@
 // 11.2 / 18.1 us with one group per CTA.  Activations staged in shared
 // memory instead of registers, four warps per CTA, or four groups per CTA
 // all measured slower; K = 11008 (88 KiB of weights per 8 columns) is
-// faster on the register-streaming GEMV.
+// faster on the register-streaming GEMV.  Landing only the first 7/8, 6/8 or
+// 5/8 of each warp's chunks before the programmatic wait (the rest read from
+// global memory after it, 64 registers, four CTAs per SM, so every CTA of
+// the next launch fits beside this one's) took 4.7 / 6.8 / 7.3 us at
+// 4096 x 4096, M = 1, against 3.63 us landing all of it: the loads after the
+// wait put a DRAM round trip on the critical path behind the previous kernel.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
