@@ -498,8 +498,49 @@ def llm_block_secondary(lib, dev, torch, prefill=512, decode=128, with_reference
         blk.close()
         return ms_prefill, ms_decode
 
+    def run_capi():
+        """The same block driven inside the library (vnpu_b200_block_*)."""
+        from llm_block import make_weights
+        w, (n1, n2) = make_weights(cfg)
+        c = vnpu.BlockConfigArgs(cfg.d, cfg.heads, cfg.inter, cfg.cap, cfg.eps, cfg.theta, 0, 0)
+        blk = vnpu.vp()
+        lib.check(lib.b200_block_create(dev.stream, C.byref(c), vnpu.ptr(w["qkv"]),
+                                        vnpu.ptr(w["o"]), vnpu.ptr(w["gate_up"]),
+                                        vnpu.ptr(w["down"]), vnpu.ptr(n1), vnpu.ptr(n2),
+                                        C.byref(blk)), "block_create")
+        del w
+        g = torch.Generator(device="cuda").manual_seed(11)
+        x = torch.empty((prefill, cfg.d), device="cuda").normal_(0, 1, generator=g)
+        y = torch.empty_like(x)
+        for _ in range(3):
+            lib.check(lib.b200_block_forward(blk, x.data_ptr(), prefill, 0, y.data_ptr()), "fwd")
+        dev.sync()
+        lib.check(lib.b200_block_reset(blk), "reset")
+        e0 = st.event()
+        lib.check(lib.b200_block_forward(blk, x.data_ptr(), prefill, 0, y.data_ptr()), "fwd")
+        e1 = st.event()
+        dev.sync()
+        e1.synchronize()
+        ms_pre = e0.elapsed_time(e1)
+        xin = torch.empty((1, cfg.d), device="cuda").normal_(0, 1, generator=g)
+        yout = torch.empty_like(xin)
+        lib.check(lib.b200_block_decode(blk, xin.data_ptr(), yout.data_ptr()), "decode")
+        dev.sync()
+        lib.check(lib.b200_block_forward(blk, x.data_ptr(), prefill, 0, y.data_ptr()), "fwd")
+        dev.sync()
+        e0 = st.event()
+        for _ in range(decode):
+            lib.check(lib.b200_block_decode(blk, xin.data_ptr(), yout.data_ptr()), "decode")
+        e1 = st.event()
+        dev.sync()
+        e1.synchronize()
+        ms_dec = e0.elapsed_time(e1)
+        lib.b200_block_destroy(blk)
+        return ms_pre, ms_dec
+
     ms_prefill, ms_decode = run(True)
     pro_prefill, pro_decode = run(False)
+    capi_prefill, capi_decode = run_capi()
     out = {"config": f"d={cfg.d} heads={cfg.heads} I={cfg.inter} prefill {prefill} + {decode} decode",
            "prefill_ms": ms_prefill, "prefill_tok_s": prefill / ms_prefill * 1e3,
            "decode_ms_per_token": ms_decode / decode, "decode_tok_s": decode / ms_decode * 1e3,
@@ -508,7 +549,12 @@ def llm_block_secondary(lib, dev, torch, prefill=512, decode=128, with_reference
            "gate_up": "MATMUL_I8_SWIGLU (SwiGLU in the gate/up GEMM's epilogue) -> QUANTIZE_I8",
            "swiglu_prologue": {"gate_up": "MATMUL_I8 (2I columns) -> SWIGLU_QUANTIZE_I8",
                                "prefill_ms": pro_prefill,
-                               "decode_ms_per_token": pro_decode / decode}}
+                               "decode_ms_per_token": pro_decode / decode},
+           "library_driver": {"api": "vnpu_b200_block_forward (prefill) / vnpu_b200_block_decode "
+                                     "(one CUDA-graph launch per token, position advanced on the "
+                                     "device)",
+                              "prefill_ms": capi_prefill,
+                              "decode_ms_per_token": capi_decode / decode}}
     if with_reference and os.path.exists(REF_LIB):
         import time as _time
         os.environ.setdefault("VNPU_FORCE_ISA", "avx2")

@@ -405,6 +405,68 @@ VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_graph_launch(vnpu_b200_graph_t *graph
 VNPU_API void VNPU_CALL vnpu_b200_graph_destroy(vnpu_b200_graph_t *graph);
 
 /*
+ * The decoder block of the reference's synthetic LLM benchmark (no reference
+ * counterpart as an API: the reference drives it from its tool,
+ * tools/llm_bench.cpp:213-326, with host vectors, and has no KV cache; its
+ * "decode" re-runs the block).  Here the block lives in the library: weights
+ * quantized per column and packed in HBM, a KV cache of `capacity` slots
+ * ([heads][capacity][head_dim] f32 each, zero, with an additive mask of -inf
+ * on the slots not yet written), activations in HBM, and every op a vnpu
+ * command on the block's stream, so a C engine can run prefill and KV-cached
+ * decode without any other runtime.  The op sequence and its bits are the
+ * reference block's: RMSNorm (eps) -> QUANTIZE_I8 -> MATMUL_I8 (QKV) -> RoPE
+ * (theta_base) on Q, K -> causal ATTENTION_F32 -> QUANTIZE_I8 -> MATMUL_I8
+ * (O) -> ADD -> RMSNorm -> QUANTIZE_I8 -> MATMUL_I8 (gate/up) -> SWIGLU_F32 ->
+ * QUANTIZE_I8 -> MATMUL_I8 (down) -> ADD, run as the B200 opcodes that give
+ * the same bits (RMSNORM_QUANTIZE_I8, QKV_ROPE_APPEND, MATMUL_I8_RESIDUAL,
+ * MATMUL_I8_SWIGLU, or SWIGLU_QUANTIZE_I8 with VNPU_B200_BLOCK_SWIGLU_PROLOGUE).
+ */
+#define VNPU_B200_BLOCK_SWIGLU_PROLOGUE  (1u << 0)
+
+typedef struct vnpu_b200_block_config_t {
+    uint32_t d_model;      /* heads * head_dim */
+    uint32_t heads;
+    uint32_t inter;        /* SwiGLU hidden width I */
+    uint32_t capacity;     /* KV-cache slots; also the largest prefill */
+    float eps;             /* RMSNorm epsilon; <= 0: 1e-5, as RMSNORM_F32 */
+    float theta_base;      /* RoPE; <= 0: 10000 */
+    uint32_t flags;        /* VNPU_B200_BLOCK_* */
+    uint32_t reserved0;
+} vnpu_b200_block_config_t;
+
+typedef struct vnpu_b200_block vnpu_b200_block_t;
+
+/* Creates the block on `stream`'s device.  Weights are f32, host or device
+ * memory, row-major: w_qkv d x 3d (columns [Q | K | V], head-contiguous),
+ * w_o d x d, w_gate_up d x 2I (columns [gate | up]), w_down I x d, norm1 and
+ * norm2 d entries.  They are quantized per column (QUANTIZE_I8) and packed;
+ * the f32 arrays are not kept.  Synchronous. */
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_block_create(
+    vnpu_stream_t *stream, const vnpu_b200_block_config_t *config, const float *w_qkv,
+    const float *w_o, const float *w_gate_up, const float *w_down, const float *norm1,
+    const float *norm2, vnpu_b200_block_t **out_block);
+
+/* T tokens x (T x d f32, device) at positions pos .. pos+T-1 -> y (T x d f32,
+ * device; may not alias x).  T > 1 is a prefill from an empty cache (pos must
+ * be 0; the tokens attend causally to each other, as the reference block
+ * does); T = 1 attends to every filled cache slot.  Sets the device-side
+ * position to pos + T.  Enqueued on the block's stream. */
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_block_forward(vnpu_b200_block_t *block, const float *x,
+                                                        uint32_t T, uint32_t pos, float *y);
+
+/* One decode token at the device-side position, which then advances by one,
+ * as one CUDA-graph launch: the first call (and any call whose x or y differs
+ * from the previous one) records the step, later calls replay it.  x and y
+ * are 1 x d f32 device memory.  Enqueued on the block's stream. */
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_block_decode(vnpu_b200_block_t *block, const float *x,
+                                                       float *y);
+
+/* Empties the cache (zero K/V, mask -inf) and sets the position to 0. */
+VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_block_reset(vnpu_b200_block_t *block);
+
+VNPU_API void VNPU_CALL vnpu_b200_block_destroy(vnpu_b200_block_t *block);
+
+/*
  * Per-tensor QUANTIZE_I8 (VNPU_QUANT_PER_TENSOR) that allocates nothing.  No
  * reference counterpart: the reference quantizes on host memory it already
  * owns.  Same bits as vnpu_quantize_i8 with axis PER_TENSOR (reference

@@ -1886,6 +1886,32 @@ cudaError_t attention(const LaunchCtx &ctx, const float *Q, const float *K, cons
     return cudaGetLastError();
 }
 
+// The decoder block's device-side position: *pos = value (set) or *pos +=
+// value (advance), one thread; and the cache mask filled with -inf.
+__global__ void block_position_kernel(int32_t *pos, int32_t value, uint32_t advance) {
+    pdl_enter();
+    if (threadIdx.x == 0) *pos = advance ? *pos + value : value;
+}
+
+__global__ void fill_neg_inf_kernel(float *p, uint64_t n) {
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+        p[i] = -INFINITY;
+}
+
+cudaError_t block_position(const LaunchCtx &ctx, int32_t *pos, int32_t value, bool advance) {
+    count_launch(ctx);
+    return launch_pdl(ctx.stream, block_position_kernel, dim3(1), dim3(32), 0, pos, value,
+                      advance ? 1u : 0u);
+}
+
+cudaError_t fill_neg_inf(const LaunchCtx &ctx, float *p, uint64_t n) {
+    if (n == 0) return cudaSuccess;
+    count_launch(ctx);
+    fill_neg_inf_kernel<<<grid_for(n, ctx.num_sms, 256), 256, 0, ctx.stream>>>(p, n);
+    return cudaGetLastError();
+}
+
 cudaError_t kv_append(const LaunchCtx &ctx, const float *K, const float *V, float *K_cache,
                       float *V_cache, float *mask, const int32_t *position, uint32_t heads,
                       uint32_t T, uint32_t head_dim, uint32_t capacity, uint32_t position_offset) {

@@ -219,6 +219,10 @@ cudaError_t rope(const LaunchCtx &ctx, float *Q, float *K, const int32_t *positi
                  uint32_t batch, uint32_t heads, uint32_t q_seq, uint32_t k_seq,
                  uint32_t head_dim, uint32_t position_offset, uint32_t interleaved,
                  float scaling, const float *inv_freq_host);
+// The decoder block driver's device-side position (set or advance) and the
+// -inf fill of its cache mask.
+cudaError_t block_position(const LaunchCtx &ctx, int32_t *pos, int32_t value, bool advance);
+cudaError_t fill_neg_inf(const LaunchCtx &ctx, float *p, uint64_t n);
 // Y[r][j] = swiglu(C[r][j], C[r][I + j]) * alpha, the SWIGLU_F32 expression.
 cudaError_t swiglu_rows(const LaunchCtx &ctx, const float *C, uint32_t ldc, float *Y, uint32_t ldy,
                         uint32_t rows, uint32_t I, float alpha);

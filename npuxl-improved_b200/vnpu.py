@@ -100,6 +100,15 @@ class ReferenceModel(C.Structure):
                 ("epilogue_forced", u32), ("epilogue_form", u32)]
 
 
+class BlockConfigArgs(C.Structure):
+    """vnpu_b200_block_config_t (include/vnpu_b200.h)."""
+    _fields_ = [("d_model", u32), ("heads", u32), ("inter", u32), ("capacity", u32),
+                ("eps", C.c_float), ("theta_base", C.c_float), ("flags", u32), ("reserved0", u32)]
+
+
+B200_BLOCK_SWIGLU_PROLOGUE = 1 << 0
+
+
 class ClusterConfig(C.Structure):
     _fields_ = [("abi_version", u32), ("num_streams", u32), ("flags", u32),
                 ("request_timeout_ms", u32), ("auth_token", C.c_char_p),
@@ -398,6 +407,13 @@ class Lib:
             self.b200_capture_end = _sig(h, "vnpu_b200_capture_end", _ST, vp, C.POINTER(vp))
             self.b200_graph_launch = _sig(h, "vnpu_b200_graph_launch", _ST, vp, vp)
             self.b200_graph_destroy = _sig(h, "vnpu_b200_graph_destroy", None, vp)
+            self.b200_block_create = _sig(h, "vnpu_b200_block_create", _ST, vp,
+                                          C.POINTER(BlockConfigArgs), vp, vp, vp, vp, vp, vp,
+                                          C.POINTER(vp))
+            self.b200_block_forward = _sig(h, "vnpu_b200_block_forward", _ST, vp, vp, u32, u32, vp)
+            self.b200_block_decode = _sig(h, "vnpu_b200_block_decode", _ST, vp, vp, vp)
+            self.b200_block_reset = _sig(h, "vnpu_b200_block_reset", _ST, vp)
+            self.b200_block_destroy = _sig(h, "vnpu_b200_block_destroy", None, vp)
 
     def check(self, rc: int, what: str):
         if rc != OK:
