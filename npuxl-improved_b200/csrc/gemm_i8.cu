@@ -236,7 +236,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // No TMA multicast anywhere: each CTA loads only its own tiles.
 // ===========================================================================
 
-template <uint32_t kNEpiWarps, uint32_t kNStages, uint32_t kTN = kPTileN, bool kSwiglu = false>
+template <uint32_t kNEpiWarps, uint32_t kNStages, uint32_t kTN = kPTileN, bool kSwiglu = false,
+          uint32_t kVar = kVarRuntime>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWarps), 1)
     gemm_i8_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                 const __grid_constant__ CUtensorMap tmap_b,
@@ -459,7 +460,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
                 if (m_first < p.M) {
 #pragma unroll
                     for (uint32_t c = 0; c < kChunks; ++c)
-                        dequant32_shfl_inplace_any(p.variant, rr[c], sa, sreg[c], breg[c]);
+                        dequant_chunk<kVar>(p.variant, rr[c], sa, sreg[c], breg[c]);
                 }
 #pragma unroll
                 for (uint32_t k = 0; k < kHalf; ++k) {
@@ -499,7 +500,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(kNEpiWa
                 const uint32_t col = col_base + c * 32u;
                 const uint32_t n0 = nb * kTN + col;
                 if (chunk0 + c >= kTileChunks || n0 >= p.N || m_first >= p.M) continue;  // warp-uniform
-                if (p.splits == 1) dequant32_shfl_inplace_any(p.variant, rr[c], sa, sreg[c], breg[c]);
+                if (p.splits == 1) dequant_chunk<kVar>(p.variant, rr[c], sa, sreg[c], breg[c]);
                 const float(&v)[32] = reinterpret_cast<const float(&)[32]>(rr[c]);
                 if (p.ndst) {
                     // Scatter: the 32x32 chunk is transposed through the staging
@@ -1282,6 +1283,12 @@ cudaError_t device_setup(int &max_pairs, int &max_wide_pairs) {
                                       static_cast<int>(pair_smem_bytes(16, 5, 224)))) != cudaSuccess ||
             (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<16, 5, 256, true>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(pair_smem_bytes(16, 5)))) != cudaSuccess ||
+            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<8, 6, 256, false, kVarPlain>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(pair_smem_bytes(8, 6)))) != cudaSuccess ||
+            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<16, 5, 256, false, kVarPlain>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(pair_smem_bytes(16, 5)))) != cudaSuccess)
             return e;
         if ((e = wide_device_setup(d.max_wide_pairs)) != cudaSuccess) return e;
@@ -1579,8 +1586,14 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         bool wide = false;
         const bool no_splitk = std::getenv("VNPU_B200_NO_SPLITK") != nullptr;
         const uint32_t kb_total = (p.K + kBK - 1) / kBK;
+        // Without a residual a split must keep >= 24 k-blocks (512x4096x4096:
+        // 17.3 us unsplit against 18.2 us in two splits of 16); the residual
+        // rides on the split-K finish kernel, so it splits from 8.
+        uint32_t kb_min = p.R ? 8u : 24u;
+        if (const char *e = std::getenv("VNPU_B200_SPLITK_MIN_KB"))   // tests pin it
+            kb_min = std::max(1, std::atoi(e));
         const bool splits_k = !no_splitk && p.N % 4u == 0u &&
-                              std::min(std::min(pp / tiles_p, 4u), kb_total / 8u) >= 2u;
+                              std::min(std::min(pp / tiles_p, 4u), kb_total / kb_min) >= 2u;
         if (!mixed && !splits_k)
             pick_pair_tile(p.M, p.N, p.K, p.epilogue, pp, wp, max_wide_pairs > 0, wide, tn);
         tp.tiles_m = tiles_m;
@@ -1601,7 +1614,7 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         if (!wide && tn == 256u && p.N % 4u == 0u && !no_splitk) {
             uint32_t sk = pp / tiles_p;
             sk = std::min(sk, 4u);
-            sk = std::min(sk, tp.num_kb / 8u);
+            sk = std::min(sk, tp.num_kb / kb_min);
             if (sk >= 2) {
                 tp.kb_per_split = (tp.num_kb + sk - 1) / sk;
                 splits = (tp.num_kb + tp.kb_per_split - 1) / tp.kb_per_split;
@@ -1643,6 +1656,11 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
             VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<16, 5, 224>,
                                    dim3(2 * pairs), dim3(pair_threads(16)),
                                    pair_smem_bytes(16, 5, 224), tmap_a, *tmap_b, tmap_c, tp));
+        else if (epi16 && use_plain_variant(tp.variant))
+            VNPU_LAUNCH(launch_pdl(ctx.stream,
+                                   gemm_i8_tcgen05_pair_kernel<16, 5, 256, false, kVarPlain>,
+                                   dim3(2 * pairs), dim3(pair_threads(16)), pair_smem_bytes(16, 5),
+                                   tmap_a, *tmap_b, tmap_c, tp));
         else if (epi16)
             VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<16, 5>, dim3(2 * pairs),
                                    dim3(pair_threads(16)), pair_smem_bytes(16, 5), tmap_a,
@@ -1651,6 +1669,11 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
             VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, 6, 224>,
                                    dim3(2 * pairs), dim3(pair_threads(8)),
                                    pair_smem_bytes(8, 6, 224), tmap_a, *tmap_b, tmap_c, tp));
+        else if (use_plain_variant(tp.variant))
+            VNPU_LAUNCH(launch_pdl(ctx.stream,
+                                   gemm_i8_tcgen05_pair_kernel<8, 6, 256, false, kVarPlain>,
+                                   dim3(2 * pairs), dim3(pair_threads(8)), pair_smem_bytes(8, 6),
+                                   tmap_a, *tmap_b, tmap_c, tp));
         else
             VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, 6>, dim3(2 * pairs),
                                    dim3(pair_threads(8)), pair_smem_bytes(8, 6), tmap_a,

@@ -7,7 +7,7 @@
 namespace vnpu_b200 {
 namespace {
 
-template <uint32_t kTN = 256>
+template <uint32_t kTN = 256, uint32_t kVar = kVarRuntime>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     gemm_i8_tcgen05_pair_wide_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                      const __grid_constant__ CUtensorMap tmap_b,
@@ -238,8 +238,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                     const uint32_t col = h * kTN + col_base + c * 32u;
                     const uint32_t n0 = nb * kTileW + col;
                     if (chunk0 + c >= kHalfChunks || n0 >= p.N || m_first >= p.M) continue;  // warp-uniform
-                    dequant32_shfl_inplace_any(p.variant, r[c], sa, sreg[h * kChunks + c],
-                                               breg[h * kChunks + c]);
+                    dequant_chunk<kVar>(p.variant, r[c], sa, sreg[h * kChunks + c],
+                                        breg[h * kChunks + c]);
                     const float(&v)[32] = reinterpret_cast<const float(&)[32]>(r[c]);
                     if (p.tma_store) {
                         if (lane == 0) bulk_wait_read0();  // previous store has read the buffer
@@ -286,6 +286,12 @@ cudaError_t wide_device_setup(int &max_wide_pairs) {
                                   static_cast<int>(kWSmemBytes))) != cudaSuccess ||
         (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_wide_kernel<224>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(wide_smem_bytes(224)))) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_wide_kernel<256, kVarPlain>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(kWSmemBytes))) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_wide_kernel<224, kVarPlain>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   static_cast<int>(wide_smem_bytes(224)))) != cudaSuccess)
         return e;
     cudaLaunchConfig_t cfg = {};
@@ -304,11 +310,16 @@ cudaError_t launch_wide_pair(cudaStream_t stream, uint32_t tn, uint32_t pairs,
                              const CUtensorMap &tmap_a, const CUtensorMap &tmap_b,
                              const CUtensorMap &tmap_c, const TcParams &tp) {
     const dim3 grid(2 * pairs), block(kPThreads);
+    const bool plain = use_plain_variant(tp.variant);
     if (tn == 224u)
-        return launch_pdl(stream, gemm_i8_tcgen05_pair_wide_kernel<224>, grid, block,
-                          wide_smem_bytes(224), tmap_a, tmap_b, tmap_c, tp);
-    return launch_pdl(stream, gemm_i8_tcgen05_pair_wide_kernel<256>, grid, block, kWSmemBytes,
-                      tmap_a, tmap_b, tmap_c, tp);
+        return plain ? launch_pdl(stream, gemm_i8_tcgen05_pair_wide_kernel<224, kVarPlain>, grid,
+                                  block, wide_smem_bytes(224), tmap_a, tmap_b, tmap_c, tp)
+                     : launch_pdl(stream, gemm_i8_tcgen05_pair_wide_kernel<224>, grid, block,
+                                  wide_smem_bytes(224), tmap_a, tmap_b, tmap_c, tp);
+    return plain ? launch_pdl(stream, gemm_i8_tcgen05_pair_wide_kernel<256, kVarPlain>, grid, block,
+                              kWSmemBytes, tmap_a, tmap_b, tmap_c, tp)
+                 : launch_pdl(stream, gemm_i8_tcgen05_pair_wide_kernel<256>, grid, block,
+                              kWSmemBytes, tmap_a, tmap_b, tmap_c, tp);
 }
 
 }  // namespace vnpu_b200

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -166,6 +167,30 @@ __device__ __forceinline__ void dequant32_shfl_inplace_any(uint32_t variant, uin
     }
 }
 
+// The dequant epilogue variant fixed at compile time (kVar), or chosen per
+// launch through the switch above (kVar == kVarRuntime).  The fixed form has
+// no indirect branch and a shorter instruction stream: at 512^3, where a
+// launch is mostly fixed cost, the runtime switch's launch stalled mostly on
+// instruction fetch (no_instruction 11.2 cycles per issued instruction).
+constexpr uint32_t kVarRuntime = 0xFFFFFFFFu;
+constexpr uint32_t kVarPlain = epi_variant(0, false, 0);   // NONE, no bias: every form alike
+
+// The launch takes the kVarPlain instance (VNPU_B200_EPI_RUNTIME=1 keeps the
+// runtime-switch instance, for comparisons).
+inline bool use_plain_variant(uint32_t variant) {
+    static const bool forced_runtime = std::getenv("VNPU_B200_EPI_RUNTIME") != nullptr;
+    return variant == kVarPlain && !forced_runtime;
+}
+
+template <uint32_t kVar>
+__device__ __forceinline__ void dequant_chunk(uint32_t variant, uint32_t (&r)[32], float sa,
+                                              float s_lane, float b_lane) {
+    if constexpr (kVar == kVarRuntime)
+        dequant32_shfl_inplace_any(variant, r, sa, s_lane, b_lane);
+    else
+        dequant32_shfl_inplace<kVar>(r, sa, s_lane, b_lane);
+}
+
 // Column scale and bias of column n for the lane that holds it (n past N: 1, 0).
 __device__ __forceinline__ void fetch_col(const TcParams &p, uint32_t n, float &s, float &b) {
     s = n < p.N ? __ldg(p.scale_b + n) : 1.0f;
@@ -234,6 +259,7 @@ cudaError_t wide_device_setup(int &max_wide_pairs);
 
 // One launch of the wide CTA-pair kernel (programmatic dependent launch):
 // accumulator width tn (256 or 224), 2 * pairs CTAs.
+// tp.variant == kVarPlain takes the instance with that variant compiled in.
 cudaError_t launch_wide_pair(cudaStream_t stream, uint32_t tn, uint32_t pairs,
                              const CUtensorMap &tmap_a, const CUtensorMap &tmap_b,
                              const CUtensorMap &tmap_c, const TcParams &tp);

@@ -511,6 +511,9 @@ def test_splitk_pair_kernel_agrees(gpu, oracle, monkeypatch, M, K, N, epi, form,
     ldc = N + pad if pad else 0
     monkeypatch.setenv("VNPU_B200_PAIR_TN", "256")
     outs = []
+    # splits of >= 8 k-blocks (the rule for MATMUL_I8_RESIDUAL; plain
+    # MATMUL_I8 splits only from 24)
+    monkeypatch.setenv("VNPU_B200_SPLITK_MIN_KB", "8")
     for split in (True, False):
         if split:
             monkeypatch.delenv("VNPU_B200_NO_SPLITK", raising=False)
@@ -529,11 +532,12 @@ def test_splitk_pair_kernel_agrees(gpu, oracle, monkeypatch, M, K, N, epi, form,
     assert bits_equal(outs[0][rows], oracle.matmul_i8(A[rows], B, sa[rows], sb, bias, epi, form))
 
 
-def test_splitk_in_cuda_graph(gpu, oracle):
+def test_splitk_in_cuda_graph(gpu, oracle, monkeypatch):
     """A split-K GEMM (stream-ordered workspace allocated and freed inside the
     command) recorded as a CUDA graph and replayed twice gives the eager bits,
     with and without the residual folded into its finish kernel."""
     import torch
+    monkeypatch.setenv("VNPU_B200_SPLITK_MIN_KB", "8")   # split the plain product too
     M, K, N = 512, 4096, 4096
     rng = np.random.default_rng(4242)
     A, sa = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
