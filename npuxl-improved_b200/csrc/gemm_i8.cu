@@ -1289,6 +1289,9 @@ cudaError_t device_setup(int &max_pairs, int &max_wide_pairs) {
                                       static_cast<int>(pair_smem_bytes(8, 6)))) != cudaSuccess ||
             (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<16, 5, 256, false, kVarPlain>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(pair_smem_bytes(16, 5)))) != cudaSuccess ||
+            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<16, 5, 256, false, kVarSilu>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(pair_smem_bytes(16, 5)))) != cudaSuccess)
             return e;
         if ((e = wide_device_setup(d.max_wide_pairs)) != cudaSuccess) return e;
@@ -1656,6 +1659,11 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
             VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<16, 5, 224>,
                                    dim3(2 * pairs), dim3(pair_threads(16)),
                                    pair_smem_bytes(16, 5, 224), tmap_a, *tmap_b, tmap_c, tp));
+        else if (epi16 && use_compiled_variant(tp.variant, kVarSilu))
+            VNPU_LAUNCH(launch_pdl(ctx.stream,
+                                   gemm_i8_tcgen05_pair_kernel<16, 5, 256, false, kVarSilu>,
+                                   dim3(2 * pairs), dim3(pair_threads(16)), pair_smem_bytes(16, 5),
+                                   tmap_a, *tmap_b, tmap_c, tp));
         else if (epi16 && use_plain_variant(tp.variant))
             VNPU_LAUNCH(launch_pdl(ctx.stream,
                                    gemm_i8_tcgen05_pair_kernel<16, 5, 256, false, kVarPlain>,

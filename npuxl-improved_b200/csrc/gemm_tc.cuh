@@ -175,12 +175,18 @@ __device__ __forceinline__ void dequant32_shfl_inplace_any(uint32_t variant, uin
 constexpr uint32_t kVarRuntime = 0xFFFFFFFFu;
 constexpr uint32_t kVarPlain = epi_variant(0, false, 0);   // NONE, no bias: every form alike
 
-// The launch takes the kVarPlain instance (VNPU_B200_EPI_RUNTIME=1 keeps the
-// runtime-switch instance, for comparisons).
-inline bool use_plain_variant(uint32_t variant) {
+// SiLU without bias in the block or stream form (the FFN GEMM of the
+// BASELINE's config 3) on the 16-epilogue-warp pair kernel.
+constexpr uint32_t kVarSilu = epi_variant(2, false, 0);
+
+// The launch takes the instance with `variant` compiled in
+// (VNPU_B200_EPI_RUNTIME=1 keeps the runtime-switch instance, for
+// comparisons).
+inline bool use_compiled_variant(uint32_t variant, uint32_t compiled) {
     static const bool forced_runtime = std::getenv("VNPU_B200_EPI_RUNTIME") != nullptr;
-    return variant == kVarPlain && !forced_runtime;
+    return variant == compiled && !forced_runtime;
 }
+inline bool use_plain_variant(uint32_t variant) { return use_compiled_variant(variant, kVarPlain); }
 
 template <uint32_t kVar>
 __device__ __forceinline__ void dequant_chunk(uint32_t variant, uint32_t (&r)[32], float sa,
