@@ -1651,8 +1651,13 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
             tmap_b = &tmap_b112;
         }
         // 16 epilogue warps: SiLU / GELU (latency-bound epilogue), or one short
-        // tile per pair (the epilogue is most of the time): 512^3 9.3 -> 8.8 us
-        const bool epi16 = p.epilogue >= 2 || (tiles <= cap && tp.num_kb <= 8u);
+        // tile per pair with the per-launch variant switch (the epilogue is
+        // most of the time: 512^3 9.3 -> 8.8 us).  With the NONE/no-bias
+        // variant compiled in, 8 warps are faster there too (512^3 7.80 ->
+        // 7.55 us, 1024^3 9.34 -> 9.02 us).
+        bool epi16 = p.epilogue >= 2 ||
+                     (tiles <= cap && tp.num_kb <= 8u && !use_plain_variant(tp.variant));
+        if (const char *e = std::getenv("VNPU_B200_EPI_WARPS")) epi16 = std::atoi(e) == 16;
         if (wide)
             VNPU_LAUNCH(launch_wide_pair(ctx.stream, tn, pairs, tmap_a, *tmap_b, tmap_c, tp));
         else if (epi16 && tn == 224u)
