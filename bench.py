@@ -924,6 +924,7 @@ def run_b200(args):
 def run_kernel_case(spec: str):
     """One small case of one kernel, launched twice (for ncu captures):
     gemm:MxKxN[:silu], gemv:MxKxN, f32:MxKxN[:nt], quantize:RxC, attention:HxSQxSKxD,
+    llm_lib:STEPS (the block inside the library: prefill 512, STEPS decode tokens),
     llm_prefill:T (the decoder block's prefill of T tokens, twice) or llm_decode:STEPS (the
     decoder block's graph-captured decode step)."""
     import torch
@@ -1008,6 +1009,29 @@ def run_kernel_case(spec: str):
             blk.replay_decode()
         torch.cuda.synchronize()
         blk.close()
+    elif kind == "llm_lib":
+        # the same block driven inside the library (vnpu_b200_block_*): prefill
+        # 512 tokens, then `steps` decode tokens (one graph launch each)
+        from llm_block import BlockConfig, make_weights
+        steps = shape[0]
+        cfg = BlockConfig(cap=640)
+        w, (n1, n2) = make_weights(cfg)
+        c = vnpu.BlockConfigArgs(cfg.d, cfg.heads, cfg.inter, cfg.cap, cfg.eps, cfg.theta, 0, 0)
+        blk = vnpu.vp()
+        lib.check(lib.b200_block_create(dev.stream, C.byref(c), vnpu.ptr(w["qkv"]),
+                                        vnpu.ptr(w["o"]), vnpu.ptr(w["gate_up"]),
+                                        vnpu.ptr(w["down"]), vnpu.ptr(n1), vnpu.ptr(n2),
+                                        C.byref(blk)), "block_create")
+        del w
+        x = torch.empty((512, cfg.d), device="cuda").normal_(0, 1, generator=g)
+        y = torch.empty_like(x)
+        lib.check(lib.b200_block_forward(blk, x.data_ptr(), 512, 0, y.data_ptr()), "forward")
+        xin = torch.empty((1, cfg.d), device="cuda").normal_(0, 1, generator=g)
+        yout = torch.empty_like(xin)
+        for _ in range(steps):
+            lib.check(lib.b200_block_decode(blk, xin.data_ptr(), yout.data_ptr()), "decode")
+        dev.sync()
+        lib.b200_block_destroy(blk)
     else:
         raise SystemExit(f"unknown kernel case {spec}")
     rc = dev.sync()
