@@ -159,7 +159,7 @@ def _join_main(rank, world, port, q, timeout_s):
 
 
 def test_rank_that_never_joins_times_out():
-    """SURVEY-listed failure case on CPU ranks: one of three ranks never joins
+    """Failure detection on CPU ranks: one of three ranks never joins
     the group.  The others get VNPU_ERR_TIMEOUT once the deadline passes
     instead of blocking; no GPU is involved."""
     import multiprocessing as mp
