@@ -837,6 +837,10 @@ def run_b200(args):
                                                                    14336, 2, False)
             secondary["gemm_512_cube"] = gemm_secondary(lib, dev, st, torch, 512, 512, 512, 0, False,
                                                         iters=200)
+            secondary["gemm_1024_cube"] = gemm_secondary(lib, dev, st, torch, 1024, 1024, 1024, 0,
+                                                         False, iters=200)
+            secondary["gemm_512x4096x4096"] = gemm_secondary(lib, dev, st, torch, 512, 4096, 4096,
+                                                             0, False, iters=100)
             for m in (1, 4, 8):
                 gv = gemv_secondary(lib, dev, st, torch, m)
                 gv["frac_of_hbm"] = gv["gbs"] / pk["hbm_gbs"]

@@ -1292,7 +1292,19 @@ cudaError_t device_setup(int &max_pairs, int &max_wide_pairs) {
                                       static_cast<int>(pair_smem_bytes(16, 5)))) != cudaSuccess ||
             (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<16, 5, 256, false, kVarSilu>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(pair_smem_bytes(16, 5)))) != cudaSuccess)
+                                      static_cast<int>(pair_smem_bytes(16, 5)))) != cudaSuccess ||
+            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<8, 6, 128>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(pair_smem_bytes(8, 6, 128)))) != cudaSuccess ||
+            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<8, 6, 128, false, kVarPlain>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(pair_smem_bytes(8, 6, 128)))) != cudaSuccess ||
+            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<8, 6, 64>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(pair_smem_bytes(8, 6, 64)))) != cudaSuccess ||
+            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<8, 6, 64, false, kVarPlain>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(pair_smem_bytes(8, 6, 64)))) != cudaSuccess)
             return e;
         if ((e = wide_device_setup(d.max_wide_pairs)) != cudaSuccess) return e;
         d.done = true;
@@ -1332,12 +1344,25 @@ static uint32_t raster_group(uint32_t tiles_m, uint32_t tile_m, uint32_t K) {
 // 339.6 / 322.0; N = 14336 683.8 / 806.8 / 651.2 / 633.7; N = 28672 wide
 // 1265-1345, wide-224 1304.  The wide kernel only takes NONE / RELU
 // epilogues (SiLU and GELU measured slower on it).
-// VNPU_B200_PAIR_WIDE=0|1 and VNPU_B200_PAIR_TN=224|256 pin the choice.
+// With allow_narrow, shapes whose 256-column tiles leave pairs idle may take
+// 256x128 or 256x64 tiles (pair kernel) when those still fit in one wave:
+// the same operand rows spread over more SMs, each with a shorter MMA chain
+// and a smaller share of the output to store.
+// VNPU_B200_PAIR_WIDE=0|1 and VNPU_B200_PAIR_TN=64|128|224|256 pin the choice.
 // Returns the chosen shape's estimated cost (0 when none qualifies);
 // wide_only limits the choice to the wide kernel.
+// Per-column rate of the narrow pair tiles relative to the 256x256 tile (a
+// narrow tile reads more operand bytes per MAC and pays the same fixed cost
+// per tile).  Measured on B200 (CUDA graph of 20 launches, us per launch,
+// 256 / 128 / 64 columns): 512^3 7.54 / 6.38 / 5.65, 1024^3 8.97 / 7.90 /
+// 7.64, 512x2048x2048 11.59 / 10.76 / 10.34, 256x4096x4096 16.87 / 16.36 /
+// 15.80, 512x4096x4096 17.20 / 17.07 / 26.7 (two waves at 64).
+constexpr double kNarrowRate128 = 0.80;
+constexpr double kNarrowRate64 = 0.55;
+
 double pick_pair_tile(uint32_t M, uint32_t N, uint32_t K, uint32_t epilogue, uint32_t pairs,
                       uint32_t wide_pairs, bool have_wide, bool &wide, uint32_t &tn,
-                      bool wide_only = false) {
+                      bool wide_only = false, bool allow_narrow = false) {
     const uint32_t tiles_m = (M + kPTileM - 1) / kPTileM;
     const double wide_rate = K >= 8192u ? 1.10 : 1.02;
     const char *fw = std::getenv("VNPU_B200_PAIR_WIDE");
@@ -1347,15 +1372,24 @@ double pick_pair_tile(uint32_t M, uint32_t N, uint32_t K, uint32_t epilogue, uin
     for (int w = wide_only ? 1 : 0; w < 2; ++w) {
         if (w && (!have_wide || (epilogue > 1u && !fw))) continue;
         if (fw && (fw[0] == '1') != (w == 1)) continue;
-        for (uint32_t t : {256u, 224u}) {
+        for (uint32_t t : {256u, 224u, 128u, 64u}) {
             if (ft && static_cast<uint32_t>(std::atoi(ft)) != t) continue;
+            const bool narrow = t < 224u;
+            if (narrow && (w || !(allow_narrow || ft))) continue;
             const uint32_t cols = w ? 2u * t : t;
             const uint32_t tiles = tiles_m * ((N + cols - 1) / cols);
             const uint32_t cap = w ? wide_pairs : pairs;
             // the wide tile needs a full wave to pay for its idle accumulator set
             if (w && tiles < cap && !fw) continue;
+            // a narrow tile only where it still fits in one wave, and with a
+            // SiLU / GELU epilogue only for short K (512x4096x4096 SiLU: 25.2 us
+            // at 256x128 with 8 epilogue warps, 24.7 us at 256x256 with 16)
+            if (narrow && !ft && (tiles > cap || (epilogue >= 2u && K > 1024u))) continue;
             const uint32_t waves = (tiles + cap - 1) / cap;
-            const double rate = (w ? wide_rate : 1.0) * (t == 224u ? (w ? 0.94 : 0.88) : 1.0);
+            const double rate = (w ? wide_rate : 1.0) *
+                                (t == 224u ? (w ? 0.94 : 0.88)
+                                           : t == 128u ? kNarrowRate128
+                                                       : t == 64u ? kNarrowRate64 : 1.0);
             const double cost = waves * static_cast<double>(cols) / rate;
             // a 224-column tile must win clearly (3%): its rates are measured
             // at M = K = 8192 only
@@ -1598,7 +1632,8 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         const bool splits_k = !no_splitk && p.N % 4u == 0u &&
                               std::min(std::min(pp / tiles_p, 4u), kb_total / kb_min) >= 2u;
         if (!mixed && !splits_k)
-            pick_pair_tile(p.M, p.N, p.K, p.epilogue, pp, wp, max_wide_pairs > 0, wide, tn);
+            pick_pair_tile(p.M, p.N, p.K, p.epilogue, pp, wp, max_wide_pairs > 0, wide, tn,
+                           false, true);
         tp.tiles_m = tiles_m;
         const uint32_t tile_cols = wide ? 2u * tn : tn;
         tp.tiles_n = (p.N + tile_cols - 1) / tile_cols;
@@ -1641,14 +1676,15 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         const uint32_t tiles = tp.tiles_m * tp.tiles_n;
         const uint32_t cap = static_cast<uint32_t>(wide ? max_wide_pairs : max_pairs);
         const uint32_t pairs = tiles < cap ? tiles : cap;
-        // 224-column tiles: each CTA loads 112 weight rows per stage (its own
-        // box height); the 128-row map serves the 256-column tiles.
-        CUtensorMap tmap_b112;
+        // 224-, 128- and 64-column tiles: each CTA loads tn / 2 weight rows
+        // per stage (its own box height); the 128-row map serves the
+        // 256-column tiles.
+        CUtensorMap tmap_bn;
         const CUtensorMap *tmap_b = p.tmap_b128;
-        if (tn == 224u) {
-            if (!encode_tmap_kmajor_i8(&tmap_b112, p.Bt, p.k_stride, p.N, p.k_stride, kBK, 112))
+        if (tn != 256u) {
+            if (!encode_tmap_kmajor_i8(&tmap_bn, p.Bt, p.k_stride, p.N, p.k_stride, kBK, tn / 2u))
                 return cudaErrorInvalidValue;
-            tmap_b = &tmap_b112;
+            tmap_b = &tmap_bn;
         }
         // 16 epilogue warps: SiLU / GELU (latency-bound epilogue), or one short
         // tile per pair with the per-launch variant switch (the epilogue is
@@ -1658,7 +1694,26 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         bool epi16 = p.epilogue >= 2 ||
                      (tiles <= cap && tp.num_kb <= 8u && !use_plain_variant(tp.variant));
         if (const char *e = std::getenv("VNPU_B200_EPI_WARPS")) epi16 = std::atoi(e) == 16;
-        if (wide)
+        // Narrow tiles: 8 epilogue warps (at most four 32-column chunks per tile).
+        if (tn == 128u && use_plain_variant(tp.variant))
+            VNPU_LAUNCH(launch_pdl(ctx.stream,
+                                   gemm_i8_tcgen05_pair_kernel<8, 6, 128, false, kVarPlain>,
+                                   dim3(2 * pairs), dim3(pair_threads(8)),
+                                   pair_smem_bytes(8, 6, 128), tmap_a, *tmap_b, tmap_c, tp));
+        else if (tn == 128u)
+            VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, 6, 128>,
+                                   dim3(2 * pairs), dim3(pair_threads(8)),
+                                   pair_smem_bytes(8, 6, 128), tmap_a, *tmap_b, tmap_c, tp));
+        else if (tn == 64u && use_plain_variant(tp.variant))
+            VNPU_LAUNCH(launch_pdl(ctx.stream,
+                                   gemm_i8_tcgen05_pair_kernel<8, 6, 64, false, kVarPlain>,
+                                   dim3(2 * pairs), dim3(pair_threads(8)),
+                                   pair_smem_bytes(8, 6, 64), tmap_a, *tmap_b, tmap_c, tp));
+        else if (tn == 64u)
+            VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, 6, 64>,
+                                   dim3(2 * pairs), dim3(pair_threads(8)),
+                                   pair_smem_bytes(8, 6, 64), tmap_a, *tmap_b, tmap_c, tp));
+        else if (wide)
             VNPU_LAUNCH(launch_wide_pair(ctx.stream, tn, pairs, tmap_a, *tmap_b, tmap_c, tp));
         else if (epi16 && tn == 224u)
             VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<16, 5, 224>,
@@ -1693,8 +1748,10 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
                                    *tmap_b, tmap_c, tp));
         g_last_kernel.store(wide ? (tn == 224u ? "gemm_i8_tcgen05_pair_wide_kernel<224>"
                                                : "gemm_i8_tcgen05_pair_wide_kernel")
-                                 : (tn == 224u ? "gemm_i8_tcgen05_pair_kernel<224>"
-                                               : "gemm_i8_tcgen05_pair_kernel"),
+                                 : tn == 224u ? "gemm_i8_tcgen05_pair_kernel<224>"
+                                 : tn == 128u ? "gemm_i8_tcgen05_pair_kernel<128>"
+                                 : tn == 64u  ? "gemm_i8_tcgen05_pair_kernel<64>"
+                                              : "gemm_i8_tcgen05_pair_kernel",
                             std::memory_order_relaxed);
         count_launch(ctx);
         return cudaGetLastError();

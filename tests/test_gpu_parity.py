@@ -653,6 +653,56 @@ def test_224_column_tiles_agree(gpu, oracle, monkeypatch, M, K, N, epi, form, pa
     assert bits_equal(outs[1][rows], oracle.matmul_i8(A[rows], B, sa[rows], sb, bias, epi, form))
 
 
+@pytest.mark.parametrize("M,K,N,epi,form,pad", [
+    (512, 512, 512, 0, 0, 0),      # configs[0]'s shape: 16 tiles of 256x64
+    (257, 128, 449, 1, 1, 0),      # one k-block; ragged M and N
+    (300, 640, 1000, 2, 2, 3),     # SiLU, stream form, ldc % 4 != 0: direct stores
+    (512, 4096, 4096, 0, 0, 0),    # the prefill projection shape
+    (600, 896, 200, 3, 0, 0),      # GELU, N below one 256-column tile
+])
+def test_narrow_column_tiles_agree(gpu, oracle, monkeypatch, M, K, N, epi, form, pad):
+    """The 128- and 64-column pair tiles (each CTA loads 64 or 32 weight rows
+    per stage) give the same bits as the 256x256 pair kernel and the oracle."""
+    rng = np.random.default_rng(M * 7 + K + N)
+    A, sa = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
+    B, sb = oracle.quantize(rng.normal(0, 0.02, (K, N)).astype(np.float32), 1)
+    bias = rng.normal(0, 0.01, N).astype(np.float32)
+    ldc = N + pad if pad else 0
+    monkeypatch.setenv("VNPU_B200_NO_SPLITK", "1")
+    monkeypatch.setenv("VNPU_B200_PAIR_WIDE", "0")
+    outs = []
+    for tn, name in (("256", "gemm_i8_tcgen05_pair_kernel"),
+                     ("128", "gemm_i8_tcgen05_pair_kernel<128>"),
+                     ("64", "gemm_i8_tcgen05_pair_kernel<64>")):
+        monkeypatch.setenv("VNPU_B200_PAIR_TN", tn)
+        Cbuf = np.full((M, ldc), np.nan, np.float32) if pad else None
+        C = run_matmul(gpu, A, B, sa, sb, bias, epi, form, ldc=ldc, Cbuf=Cbuf)
+        assert gpu.lib.b200_last_matmul_kernel().decode() == name
+        outs.append(C[:, :N].copy())
+        if pad:
+            assert np.isnan(C[:, N:]).all()   # nothing written past N
+    monkeypatch.delenv("VNPU_B200_PAIR_WIDE", raising=False)
+    monkeypatch.delenv("VNPU_B200_PAIR_TN", raising=False)
+    assert bits_equal(outs[0], outs[1])
+    assert bits_equal(outs[0], outs[2])
+    rows = np.unique(np.r_[np.arange(0, M, 17), M - 1])
+    assert bits_equal(outs[2][rows], oracle.matmul_i8(A[rows], B, sa[rows], sb, bias, epi, form))
+
+
+def test_narrow_tiles_chosen_for_underfilled_shapes(gpu, oracle, monkeypatch):
+    """Shapes whose 256-column tiles fill few CTA pairs take the narrow tiles
+    by default (512^3: 16 pairs of 256x64 instead of 4 of 256x256), and the
+    result is the oracle's."""
+    for var in ("VNPU_B200_PAIR_TN", "VNPU_B200_PAIR_WIDE", "VNPU_B200_NO_SPLITK"):
+        monkeypatch.delenv(var, raising=False)
+    rng = np.random.default_rng(5)
+    A, sa = oracle.quantize(rng.uniform(-1, 1, (512, 512)).astype(np.float32), 0)
+    B, sb = oracle.quantize(rng.normal(0, 0.02, (512, 512)).astype(np.float32), 1)
+    C = run_matmul(gpu, A, B, sa, sb, None, 0, 0)
+    assert gpu.lib.b200_last_matmul_kernel().decode().startswith("gemm_i8_tcgen05_pair_kernel<")
+    assert bits_equal(C, oracle.matmul_i8(A, B, sa, sb, None, 0, 0))
+
+
 @pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8])
 @pytest.mark.parametrize("K,N", [(4096, 4096), (11008, 4096), (4096, 11008), (100, 300),
                                  (16, 128), (1000, 1000), (130, 12288)])
