@@ -233,6 +233,26 @@ typedef struct vnpu_b200_matmul_i8_residual_args_t {
 } vnpu_b200_matmul_i8_residual_args_t;
 
 /*
+ * Position advance (a B200 command flag; no reference counterpart).  With
+ * VNPU_B200_CMD_FLAG_ADVANCE_POSITION, VNPU_B200_OP_MATMUL_I8_RESIDUAL also
+ * adds advance to the device int32 *position once the stream's earlier
+ * commands are complete: the decode step's position, which QKV_ROPE_APPEND
+ * and KV_APPEND read, moves on in the step's last command instead of a
+ * launch of its own (for one row the GEMV does it; other shapes run a
+ * one-thread kernel after the product).  The fields sit at byte
+ * VNPU_B200_ADVANCE_OFFSET of vnpu_command_t.args.raw, after the command's
+ * own arguments.  The flag is an argument error on other commands.
+ */
+#define VNPU_B200_CMD_FLAG_ADVANCE_POSITION  (1u << 14)
+#define VNPU_B200_ADVANCE_OFFSET             128u
+
+typedef struct vnpu_b200_advance_t {
+    int32_t *position;      /* device int32 */
+    int32_t advance;
+    uint32_t reserved;
+} vnpu_b200_advance_t;
+
+/*
  * The gate/up projection with its SwiGLU (no reference counterpart; the
  * reference block runs MATMUL_I8 on the [K][2I] gate/up weight, splits the
  * [T][2I] output into gate and up on the host and submits SWIGLU_F32:

@@ -65,6 +65,14 @@ vnpu_command_t b200_cmd(uint32_t opcode, const A &args, uint32_t flags = 0) {
     return c;
 }
 
+// VNPU_B200_CMD_FLAG_ADVANCE_POSITION with its fields after the command's own
+// arguments.
+void with_advance(vnpu_command_t &c, int32_t *position, int32_t advance) {
+    c.flags |= VNPU_B200_CMD_FLAG_ADVANCE_POSITION;
+    const vnpu_b200_advance_t a{position, advance, 0};
+    std::memcpy(c.args.raw + VNPU_B200_ADVANCE_OFFSET, &a, sizeof(a));
+}
+
 // Launch context for the block's own small kernels on the stream; launches
 // are counted like the commands' (into the capture while capturing).
 LaunchCtx block_ctx(vnpu_stream_t *s, uint64_t *counter) {
@@ -179,10 +187,14 @@ std::vector<vnpu_command_t> block_commands(vnpu_b200_block_t *b, const float *x,
         qf.args.quantize_i8 = vnpu_quantize_i8_args_t{b->ff, b->a8, b->sa, T, I, VNPU_QUANT_PER_ROW, 0};
         cmds.push_back(qf);
     }
-    // down projection + residual: y = x1 + ff W_down
-    cmds.push_back(b200_cmd(VNPU_B200_OP_MATMUL_I8_RESIDUAL,
-                            vnpu_b200_matmul_i8_residual_args_t{b->a8, b->w_down, b->sa, nullptr,
-                                                                b->x1, y, T, I, d, 0, 0, 0, 0, 0}));
+    // down projection + residual: y = x1 + ff W_down; a decode step also
+    // advances the device position there
+    vnpu_command_t dc = b200_cmd(VNPU_B200_OP_MATMUL_I8_RESIDUAL,
+                                 vnpu_b200_matmul_i8_residual_args_t{b->a8, b->w_down, b->sa,
+                                                                     nullptr, b->x1, y, T, I, d, 0,
+                                                                     0, 0, 0, 0});
+    if (position) with_advance(dc, b->pos, static_cast<int32_t>(T));
+    cmds.push_back(dc);
     return cmds;
 }
 
@@ -305,7 +317,6 @@ VNPU_API vnpu_status_t VNPU_CALL vnpu_b200_block_decode(vnpu_b200_block_t *block
         if (rc != VNPU_OK) return rc;
         const std::vector<vnpu_command_t> cmds = block_commands(block, x, 1, 0, block->pos, y);
         rc = vnpu_stream_submit(s, cmds.data(), cmds.size(), nullptr);
-        if (rc == VNPU_OK) rc = set_position(block, 1, true);
         vnpu_b200_graph_t *g = nullptr;
         const vnpu_status_t rc_end = vnpu_b200_capture_end(s, &g);
         if (rc == VNPU_OK) rc = rc_end;

@@ -858,10 +858,13 @@ __device__ __forceinline__ int4 load_a16(const GvParams &p, uint32_t m, uint32_t
 // so more columns per warp cut the L1 traffic of A for M > 1.
 // Epilogue variants of the streaming GEMV (the extra kernel argument).
 struct GvPlain {};
-// C = R + out (VNPU_B200_OP_MATMUL_I8_RESIDUAL).
+// C = R + out (VNPU_B200_OP_MATMUL_I8_RESIDUAL); *advance_pos += advance
+// (when not NULL) once the previous kernels of the stream are complete.
 struct GvResidual {
     const float *R;
     uint32_t ldr;
+    int32_t *advance_pos;
+    int32_t advance;
 };
 // QKV projection + RoPE + KV-cache append for one token
 // (VNPU_B200_OP_QKV_ROPE_APPEND): warp w computes rotation pair w, the
@@ -971,6 +974,8 @@ __global__ void __launch_bounds__(kThreads) gemv_i8_kernel(const GvParams p, con
                 acc[c][m] += __shfl_xor_sync(0xffffffffu, acc[c][m], o);
 
     if (!waited) pdl_wait_previous();
+    if constexpr (std::is_same<Extra, GvResidual>::value)
+        if (x.advance_pos && blockIdx.x == 0 && threadIdx.x == 0) *x.advance_pos += x.advance;
     const bool has_bias = p.bias != nullptr;
     if constexpr (kQkv) {
         // Lane 0 holds both columns of the pair: dequantize them as MATMUL_I8
@@ -1927,7 +1932,8 @@ cudaError_t matmul_i8_gemv_residual(const LaunchCtx &ctx, const MatmulI8 &p, con
     }
     const GvParams g = gv_params(p);
     const bool aligned = (reinterpret_cast<uintptr_t>(p.A) % 16u == 0u) && (p.lda % 16u == 0u);
-    const cudaError_t e = launch_gemv_m<1>(ctx, g, aligned, GvResidual{R, ldr});
+    const cudaError_t e =
+        launch_gemv_m<1>(ctx, g, aligned, GvResidual{R, ldr, p.advance_pos, p.advance});
     count_launch(ctx);
     return e;
 }

@@ -86,10 +86,21 @@ struct GsParams {
 };
 
 struct GsPlain {};
+// C = R + out; *advance_pos += advance (when not NULL) once the previous
+// kernels of the stream are complete (MATMUL_I8_RESIDUAL's
+// VNPU_B200_CMD_FLAG_ADVANCE_POSITION).
 struct GsResidual {
     const float *R;
     uint32_t ldr;
+    int32_t *advance_pos;
+    int32_t advance;
 };
+
+template <typename Extra>
+__device__ __forceinline__ void gs_advance(const Extra &x) {
+    if constexpr (std::is_same<Extra, GsResidual>::value)
+        if (x.advance_pos && blockIdx.x == 0 && threadIdx.x == 0) *x.advance_pos += x.advance;
+}
 struct GsQkv {
     float *Q, *Kout, *Vout, *Kc, *Vc, *mask;
     const int32_t *position;
@@ -180,6 +191,7 @@ __global__ void __launch_bounds__(kGsThreads) gemv_i8_stream_kernel(const GsPara
     // The stream's next kernel may start now; the activations, the scales,
     // the bias and C may belong to the previous one.
     pdl_enter();
+    gs_advance(x);
     // Lane 0 fetches the epilogue's operands now, so their latency overlaps
     // the products instead of following them.
     const bool has_bias = p.bias != nullptr;
@@ -385,6 +397,7 @@ __global__ void __launch_bounds__(kGmThreads) gemv_i8_mma_kernel(const GsParams 
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
     pdl_enter();
+    gs_advance(x);
     // This thread's output (if any): its epilogue operands now.
     const uint32_t o = threadIdx.x;
     const uint32_t oq = o / 64u, orr = o % 64u, oln = orr / 2u;
@@ -512,8 +525,9 @@ cudaError_t matmul_i8_gemv_stream(const LaunchCtx &ctx, const MatmulI8 &p, const
     if (!gemv_stream_supported(p, 1)) return cudaErrorInvalidValue;
     const GsParams g = gs_params(p);
     const uint32_t grid = (p.N + kGsWarps - 1) / kGsWarps;
+    if (p.advance_pos && !R) return cudaErrorNotSupported;
     if (R) {
-        const GsResidual x{R, ldr};
+        const GsResidual x{R, ldr, p.advance_pos, p.advance};
         return p.M == 1 ? gs_launch<1, 1>(ctx, g, grid, x) : gs_launch<2, 1>(ctx, g, grid, x);
     }
     return p.M == 1 ? gs_launch<1, 1>(ctx, g, grid, GsPlain{})
@@ -554,7 +568,8 @@ cudaError_t matmul_i8_gemv_mma(const LaunchCtx &ctx, const MatmulI8 &p, const fl
     if (!gemv_mma_supported(p)) return cudaErrorInvalidValue;
     if (groups == 0) groups = gemv_mma_small(p) ? 2u : 1u;
     const GsParams g = gs_params(p);
-    if (R) return gm_dispatch(ctx, g, groups, GsResidual{R, ldr});
+    if (p.advance_pos && !R) return cudaErrorNotSupported;
+    if (R) return gm_dispatch(ctx, g, groups, GsResidual{R, ldr, p.advance_pos, p.advance});
     return gm_dispatch(ctx, g, groups, GsPlain{});
 }
 

@@ -92,6 +92,10 @@ struct MatmulI8 {
     // matmul_i8_split_residual.
     const float *R = nullptr;
     uint32_t ldr = 0;
+    // The residual GEMVs (M = 1) only: *advance_pos += advance once the
+    // previous kernels of the stream are complete.
+    int32_t *advance_pos = nullptr;
+    int32_t advance = 0;
 };
 
 enum class MatmulKernel { kTcgen05, kGemv, kSimt };

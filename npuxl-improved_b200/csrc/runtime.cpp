@@ -350,6 +350,29 @@ static_assert(sizeof(vnpu_b200_matmul_i8_shard_args_t) <= sizeof(vnpu_command_t:
 static_assert(sizeof(vnpu_b200_matmul_i8_swiglu_args_t) <= sizeof(vnpu_command_t::args),
               "matmul + swiglu args fit the command");
 
+static_assert(VNPU_B200_ADVANCE_OFFSET + sizeof(vnpu_b200_advance_t) <=
+                  sizeof(vnpu_command_t::args),
+              "the position advance fits the command");
+static_assert(sizeof(vnpu_b200_matmul_i8_residual_args_t) <= VNPU_B200_ADVANCE_OFFSET,
+              "the position advance follows the command's own arguments");
+
+// VNPU_B200_CMD_FLAG_ADVANCE_POSITION (the command's own flag: a batch's
+// other commands' flags do not apply): the device position, staged.
+struct AdvancePosition {
+    int32_t *position = nullptr;
+    int32_t step = 0;
+
+    AdvancePosition(const vnpu_command_t &cmd, Staging &st) {
+        if (!(cmd.flags & VNPU_B200_CMD_FLAG_ADVANCE_POSITION)) return;
+        vnpu_b200_advance_t f;
+        std::memcpy(&f, cmd.args.raw + VNPU_B200_ADVANCE_OFFSET, sizeof(f));
+        if (!f.position) throw CommandError("ADVANCE_POSITION without a position",
+                                            VNPU_ERR_INVALID_ARGUMENT);
+        position = st.out(f.position, sizeof(int32_t), true);
+        step = f.advance;
+    }
+};
+
 // MATMUL_I8 of a [K][2I] gate/up weight, then SWIGLU_F32 of its halves: the
 // validation of exec_matmul_i8, the rounding forms of the 2I-wide product.
 void exec_matmul_i8_swiglu(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t flags,
@@ -386,6 +409,8 @@ void exec_matmul_i8_swiglu(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32_t
                          in.epilogue);
     p.tmap_b = w->tmap_ok ? &w->tmap : nullptr;
     p.tmap_b128 = w->tmap128_ok ? &w->tmap128 : nullptr;
+    if (cmd.flags & VNPU_B200_CMD_FLAG_ADVANCE_POSITION)
+        throw CommandError("ADVANCE_POSITION on MATMUL_I8_SWIGLU", VNPU_ERR_INVALID_ARGUMENT);
     cuda_check(matmul_i8_swiglu(ctx, p, Y, ldy, in.alpha == 0.0f ? 1.0f : in.alpha),
                "matmul_i8_swiglu launch");
     st.finish();
@@ -1013,8 +1038,15 @@ void exec_matmul_i8_residual(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32
                          a.epilogue);
     p.tmap_b = w->tmap_ok ? &w->tmap : nullptr;
     p.tmap_b128 = w->tmap128_ok ? &w->tmap128 : nullptr;
+    const AdvancePosition adv(cmd, st);
+    bool advanced = false;
     if (a.M == 1) {
-        cuda_check(matmul_i8_gemv_residual(ctx, p, R, ldr), "matmul_i8_residual launch");
+        // the GEMV advances the position itself
+        MatmulI8 f = p;
+        f.advance_pos = adv.position;
+        f.advance = adv.step;
+        cuda_check(matmul_i8_gemv_residual(ctx, f, R, ldr), "matmul_i8_residual launch");
+        advanced = true;
     } else {
         const uint64_t count = static_cast<uint64_t>(a.M) * a.N;
         const bool aliased = R < p.C + count && p.C < R + count;
@@ -1041,6 +1073,8 @@ void exec_matmul_i8_residual(vnpu_stream_t *s, const vnpu_command_t &cmd, uint32
         if (tmp) cudaFreeAsync(tmp, ctx.stream);
         cuda_check(e, "matmul_i8_residual launch");
     }
+    if (adv.position && !advanced)
+        cuda_check(block_position(ctx, adv.position, adv.step, true), "position advance");
     st.finish();
     acc.bytes_read = static_cast<uint64_t>(a.M) * a.K + static_cast<uint64_t>(a.K) * a.N +
                      static_cast<uint64_t>(a.M) * a.N * sizeof(float);

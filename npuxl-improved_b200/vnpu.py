@@ -244,6 +244,25 @@ class MatmulI8ResidualArgs(C.Structure):
                 ("epilogue", u32), ("reserved0", u32)]
 
 
+# MATMUL_I8_RESIDUAL that also advances a device int32 position: the fields
+# sit at byte ADVANCE_OFFSET of the command's argument bytes.
+CMD_FLAG_ADVANCE_POSITION = 1 << 14
+ADVANCE_OFFSET = 128
+
+
+class AdvanceArgs(C.Structure):
+    _fields_ = [("position", vp), ("advance", C.c_int32), ("reserved", u32)]
+
+
+def with_advance_position(cmd: "Command", position, advance: int) -> "Command":
+    """Ask a MATMUL_I8_RESIDUAL command to add `advance` to the device int32
+    at `position` once the stream's earlier commands are complete."""
+    cmd.flags |= CMD_FLAG_ADVANCE_POSITION
+    o = AdvanceArgs(ptr(position), advance, 0)
+    C.memmove(C.addressof(cmd.args) + ADVANCE_OFFSET, C.addressof(o), C.sizeof(o))
+    return cmd
+
+
 OP_B200_MATMUL_I8_SHARD = 0x106
 
 

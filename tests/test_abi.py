@@ -184,6 +184,9 @@ int main(void) {
     printf("res %zu\n", sizeof(vnpu_b200_matmul_i8_residual_args_t));
     F(vnpu_b200_matmul_i8_residual_args_t, R); F(vnpu_b200_matmul_i8_residual_args_t, ldr);
     F(vnpu_b200_matmul_i8_residual_args_t, epilogue);
+    printf("adv %zu\noff %u\nflags %u\n", sizeof(vnpu_b200_advance_t),
+           VNPU_B200_ADVANCE_OFFSET, VNPU_B200_CMD_FLAG_ADVANCE_POSITION);
+    F(vnpu_b200_advance_t, position); F(vnpu_b200_advance_t, advance);
     printf("ops %u %u %u %u\n", VNPU_B200_OP_RMSNORM_QUANTIZE_I8, VNPU_B200_OP_SWIGLU_QUANTIZE_I8,
            VNPU_B200_OP_QKV_ROPE_APPEND, VNPU_B200_OP_MATMUL_I8_RESIDUAL);
     return 0;
@@ -210,6 +213,13 @@ int main(void) {
     for f in ("R", "ldr", "epilogue"):
         assert int(out[f"vnpu_b200_matmul_i8_residual_args_t.{f}"]) == \
             getattr(vnpu.MatmulI8ResidualArgs, f).offset
+    assert int(out["adv"]) == C.sizeof(vnpu.AdvanceArgs)
+    assert int(out["off"]) == vnpu.ADVANCE_OFFSET
+    assert int(out["off"]) + int(out["adv"]) <= int(out["raw"])
+    assert int(out["res"]) <= vnpu.ADVANCE_OFFSET
+    assert int(out["flags"]) == vnpu.CMD_FLAG_ADVANCE_POSITION
+    for f in ("position", "advance"):
+        assert int(out[f"vnpu_b200_advance_t.{f}"]) == getattr(vnpu.AdvanceArgs, f).offset
     assert out["ops"].split() == [str(vnpu.OP_B200_RMSNORM_QUANTIZE_I8),
                                   str(vnpu.OP_B200_SWIGLU_QUANTIZE_I8),
                                   str(vnpu.OP_B200_QKV_ROPE_APPEND),

@@ -218,6 +218,81 @@ def test_residual_host_operands(gpu, oracle):
         gpu.unpack(w)
 
 
+@pytest.mark.parametrize("M,K,N,kernels", [
+    (1, 4096, 4096, 1),     # the decode O projection: mma GEMV
+    (1, 1024, 6000, 1),     # N past the mma GEMV's shapes: streaming GEMV
+    (1, 11008, 4096, 1),    # the decode down projection: register-streaming GEMV
+    (1, 1000, 333, 1),      # lda % 16 != 0
+    (3, 512, 1024, None),   # several rows: a one-thread kernel after the product
+])
+def test_residual_advances_position(gpu, oracle, torch, M, K, N, kernels):
+    """MATMUL_I8_RESIDUAL with ADVANCE_POSITION gives the residual command's
+    bits and adds to the device position; for one row the GEMV itself does it
+    (no further launch), also in a batch beside commands without the flag."""
+    rng = np.random.default_rng(M * 3 + K + N)
+    w = _weights(gpu, oracle, rng, K, N)
+    A8h, sah = oracle.quantize(rng.uniform(-1, 1, (M, K)).astype(np.float32), 0)
+    A8, sa = torch.from_numpy(A8h).cuda(), torch.from_numpy(sah).cuda()
+    R = torch.from_numpy(rng.normal(0, 1, (M, N)).astype(np.float32)).cuda()
+    try:
+        ref = torch.full((M, N), float("nan"), device="cuda")
+        out = torch.full((M, N), float("nan"), device="cuda")
+        pos = torch.tensor([5], dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        plain = vnpu.b200_command(vnpu.OP_B200_MATMUL_I8_RESIDUAL, vnpu.MatmulI8ResidualArgs(
+            A8.data_ptr(), w, sa.data_ptr(), None, R.data_ptr(), ref.data_ptr(), M, K, N, 0, 0, 0,
+            0, 0))
+        assert _submit(gpu, [plain]) == vnpu.OK
+        adv = vnpu.with_advance_position(vnpu.b200_command(
+            vnpu.OP_B200_MATMUL_I8_RESIDUAL, vnpu.MatmulI8ResidualArgs(
+                A8.data_ptr(), w, sa.data_ptr(), None, R.data_ptr(), out.data_ptr(), M, K, N, 0,
+                0, 0, 0, 0)), pos, 3)
+        launches0 = gpu.lib.b200_kernel_launches(gpu.dev)
+        assert _submit(gpu, [adv]) == vnpu.OK
+        launched = gpu.lib.b200_kernel_launches(gpu.dev) - launches0
+        assert bits_equal(out.cpu().numpy(), ref.cpu().numpy())
+        assert int(pos.item()) == 8
+        if kernels is not None:
+            assert launched == kernels, launched
+        # in one batch after a command without the flag: only the flagged one advances
+        assert _submit(gpu, [plain, adv]) == vnpu.OK
+        assert int(pos.item()) == 11
+        assert bits_equal(out.cpu().numpy(), ref.cpu().numpy())
+    finally:
+        gpu.unpack(w)
+
+
+def test_advance_position_rejects_bad_fields(b200_lib, oracle, torch):
+    """ADVANCE_POSITION without a position, or on MATMUL_I8_SWIGLU, fails the
+    command (the stream's error at the next sync) and moves nothing."""
+    rng = np.random.default_rng(2)
+    A8h, sah = oracle.quantize(rng.uniform(-1, 1, (1, 128)).astype(np.float32), 0)
+    A8, sa = torch.from_numpy(A8h).cuda(), torch.from_numpy(sah).cuda()
+    R = torch.zeros((1, 64), device="cuda")
+    out = torch.zeros((1, 64), device="cuda")
+    Y = torch.zeros((1, 32), device="cuda")
+    pos = torch.zeros(1, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    for case in ("no_position", "swiglu"):
+        with vnpu.Device(b200_lib) as d:
+            w = _weights(d, oracle, rng, 128, 64)
+            if case == "swiglu":
+                a = vnpu.MatmulI8SwigluArgs(A8.data_ptr(), w, sa.data_ptr(), None, Y.data_ptr(), 1,
+                                            128, 64, 0, 0, 0, 1.0, 0)
+                cmd = vnpu.with_advance_position(
+                    vnpu.b200_command(vnpu.OP_B200_MATMUL_I8_SWIGLU, a), pos, 1)
+            else:
+                args = vnpu.MatmulI8ResidualArgs(A8.data_ptr(), w, sa.data_ptr(), None,
+                                                 R.data_ptr(), out.data_ptr(), 1, 128, 64, 0, 0,
+                                                 0, 0, 0)
+                cmd = vnpu.with_advance_position(
+                    vnpu.b200_command(vnpu.OP_B200_MATMUL_I8_RESIDUAL, args), None, 1)
+            assert d.submit([cmd]) == vnpu.OK
+            assert d.sync() == vnpu.ERR_DEVICE_ERROR, case
+            assert int(pos.item()) == 0
+            d.unpack(w)
+
+
 # ------------------------------------------------------------------ MATMUL_I8_SWIGLU
 @pytest.mark.parametrize("M,K,I,bias_on,ldy_pad,alpha,kernel", [
     (1, 4096, 1024, False, 0, 1.0, "gemv_i8_stream_kernel+swiglu"),   # decode token
