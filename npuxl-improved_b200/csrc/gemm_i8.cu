@@ -1298,18 +1298,18 @@ cudaError_t device_setup(int &max_pairs, int &max_wide_pairs) {
             (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<16, 5, 256, false, kVarSilu>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(pair_smem_bytes(16, 5)))) != cudaSuccess ||
-            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<8, 6, 128>,
+            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<8, kNarrowStages128, 128>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(pair_smem_bytes(8, 6, 128)))) != cudaSuccess ||
-            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<8, 6, 128, false, kVarPlain>,
+                                      static_cast<int>(pair_smem_bytes(8, kNarrowStages128, 128)))) != cudaSuccess ||
+            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<8, kNarrowStages128, 128, false, kVarPlain>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(pair_smem_bytes(8, 6, 128)))) != cudaSuccess ||
-            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<8, 6, 64>,
+                                      static_cast<int>(pair_smem_bytes(8, kNarrowStages128, 128)))) != cudaSuccess ||
+            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<8, kNarrowStages64, 64>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(pair_smem_bytes(8, 6, 64)))) != cudaSuccess ||
-            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<8, 6, 64, false, kVarPlain>,
+                                      static_cast<int>(pair_smem_bytes(8, kNarrowStages64, 64)))) != cudaSuccess ||
+            (e = cudaFuncSetAttribute(gemm_i8_tcgen05_pair_kernel<8, kNarrowStages64, 64, false, kVarPlain>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(pair_smem_bytes(8, 6, 64)))) != cudaSuccess)
+                                      static_cast<int>(pair_smem_bytes(8, kNarrowStages64, 64)))) != cudaSuccess)
             return e;
         if ((e = wide_device_setup(d.max_wide_pairs)) != cudaSuccess) return e;
         d.done = true;
@@ -1702,22 +1702,22 @@ cudaError_t matmul_i8_tcgen05(const LaunchCtx &ctx, const MatmulI8 &p) {
         // Narrow tiles: 8 epilogue warps (at most four 32-column chunks per tile).
         if (tn == 128u && use_plain_variant(tp.variant))
             VNPU_LAUNCH(launch_pdl(ctx.stream,
-                                   gemm_i8_tcgen05_pair_kernel<8, 6, 128, false, kVarPlain>,
+                                   gemm_i8_tcgen05_pair_kernel<8, kNarrowStages128, 128, false, kVarPlain>,
                                    dim3(2 * pairs), dim3(pair_threads(8)),
-                                   pair_smem_bytes(8, 6, 128), tmap_a, *tmap_b, tmap_c, tp));
+                                   pair_smem_bytes(8, kNarrowStages128, 128), tmap_a, *tmap_b, tmap_c, tp));
         else if (tn == 128u)
-            VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, 6, 128>,
+            VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, kNarrowStages128, 128>,
                                    dim3(2 * pairs), dim3(pair_threads(8)),
-                                   pair_smem_bytes(8, 6, 128), tmap_a, *tmap_b, tmap_c, tp));
+                                   pair_smem_bytes(8, kNarrowStages128, 128), tmap_a, *tmap_b, tmap_c, tp));
         else if (tn == 64u && use_plain_variant(tp.variant))
             VNPU_LAUNCH(launch_pdl(ctx.stream,
-                                   gemm_i8_tcgen05_pair_kernel<8, 6, 64, false, kVarPlain>,
+                                   gemm_i8_tcgen05_pair_kernel<8, kNarrowStages64, 64, false, kVarPlain>,
                                    dim3(2 * pairs), dim3(pair_threads(8)),
-                                   pair_smem_bytes(8, 6, 64), tmap_a, *tmap_b, tmap_c, tp));
+                                   pair_smem_bytes(8, kNarrowStages64, 64), tmap_a, *tmap_b, tmap_c, tp));
         else if (tn == 64u)
-            VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, 6, 64>,
+            VNPU_LAUNCH(launch_pdl(ctx.stream, gemm_i8_tcgen05_pair_kernel<8, kNarrowStages64, 64>,
                                    dim3(2 * pairs), dim3(pair_threads(8)),
-                                   pair_smem_bytes(8, 6, 64), tmap_a, *tmap_b, tmap_c, tp));
+                                   pair_smem_bytes(8, kNarrowStages64, 64), tmap_a, *tmap_b, tmap_c, tp));
         else if (wide)
             VNPU_LAUNCH(launch_wide_pair(ctx.stream, tn, pairs, tmap_a, *tmap_b, tmap_c, tp));
         else if (epi16 && tn == 224u)

@@ -225,6 +225,13 @@ constexpr uint32_t pair_smem_bytes(uint32_t epi_warps, uint32_t stages, uint32_t
     return stages * pair_stage_bytes(tn) + epi_warps * 32 * 32 * 4 + 1024;
 }
 constexpr uint32_t kPStageOutBytes = 32 * 32 * 4;  // one 32 rows x 32 floats staging buffer
+// Ring depth of the narrow pair tiles (8 epilogue warps): as many 24 / 20 KiB
+// stages as fit beside the epilogue's staging buffers.  Where few tiles run at
+// once the main loop is bound by the copies in flight per SM (256x256 and
+// 256x128 tiles with 6 stages both took ~0.4 us per 128-deep k-block at
+// 512x4096x4096), so the deeper ring is the narrow tile's speed.
+constexpr uint32_t kNarrowStages128 = 8;
+constexpr uint32_t kNarrowStages64 = 9;
 
 
 // ===========================================================================
